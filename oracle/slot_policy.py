@@ -1,0 +1,241 @@
+"""CPU restatement of the router-split gap's slot cache (TEST INFRASTRUCTURE).
+
+Restates, in plain Python over small integer arrays, the per-layer expert slot
+cache that kfirtoledo/sluice keeps in ``src/sluice/offloader.py``:
+
+* state: ``_ExpertLayerCache`` (offloader.py:121-169) — slot owners, the
+  free list, the protected/probation SLRU segments, the expert map;
+* install: ``_install_cache`` (offloader.py:936-1007) — ``num_slots =
+  min(SLUICE_SLOTS, local_n)``, ``protected_cap = min(int(slots*frac),
+  slots-1)``, free list ``[slots-1, ..., 0]`` popped from the end;
+* pins: ``_apply_pins`` (offloader.py:1046-1083);
+* policy: ``_touch`` (2009-2021), ``_coldest_protected`` (2023-2034, LRU
+  branch), ``_acquire_slot`` (2036-2074), ``_evict_to`` (2076-2081);
+* maps: ``_write_map`` / ``_write_standing_map`` (2083-2123);
+* the gap body: ``_router_split_gap`` (2362-2467), FAST_HIT on or off.
+
+Recency is kept as a per-slot stamp from one per-layer clock instead of
+ordered dictionaries: a segment's LRU order is its slots sorted by stamp, and
+"move to end" / "insert at end" is "take a new stamp". This is the same
+representation the CUDA planner uses, so the oracle also documents it.
+
+The LFU hybrid (``SLUICE_LFU``) is not restated: it is off by default in the
+reference and outside the decode hot path this build covers.
+"""
+
+from __future__ import annotations
+
+FREE, PROBATION, PROTECTED, PINNED = 0, 1, 2, 3
+
+
+class SlotOverflow(RuntimeError):
+    """The reference raises RuntimeError here (offloader.py:2456-2460).
+
+    ``fills`` lists the acquisitions (and streams) done before the failure.
+    """
+
+    def __init__(self, msg: str, fills=()):
+        super().__init__(msg)
+        self.fills = list(fills)
+
+
+def protected_cap_for(num_slots: int, protect_frac: float) -> int:
+    """offloader.py:236-241 (frac clamp) and 937 (cap)."""
+    frac = min(max(float(protect_frac), 0.0), 0.9)
+    return max(min(int(num_slots * frac), num_slots - 1), 0)
+
+
+class SlotPolicyModel:
+    """One layer's slot cache, driven one gap call at a time."""
+
+    def __init__(self, num_slots: int, local_of: list[int], local_n: int,
+                 protect_frac: float = 0.5, fast_hit: bool = True,
+                 bytes_per_expert: int = 0, prefill_resident: bool = False):
+        self.num_slots = int(num_slots)
+        self.local_of = [int(v) for v in local_of]
+        self.global_n = len(self.local_of)
+        self.local_n = int(local_n)
+        self.protected_cap = protected_cap_for(self.num_slots, protect_frac)
+        self.fast_hit = bool(fast_hit)
+        self.bytes_per_expert = int(bytes_per_expert)
+        self.global_of_local = [-1] * self.local_n
+        for g, loc in enumerate(self.local_of):
+            if 0 <= loc < self.local_n:
+                self.global_of_local[loc] = g
+        S = self.num_slots
+        self.expert_in_slot = [-1] * S
+        self.slot_of = [-1] * self.local_n
+        self.seg = [FREE] * S
+        self.stamp = [0] * S
+        self.clock = 0
+        # popped from the end: lowest slot index first (offloader.py:944)
+        self.free_stack = list(range(S - 1, -1, -1))
+        self.expert_map = [-1] * self.global_n
+        self.map_is_standing = False
+        self.gaps = 0
+        self.fast_hits = 0
+        self.misses = 0
+        self.bytes_streamed = 0
+        if prefill_resident:
+            # offloader.py:992-1003: every local expert preloaded into slot ==
+            # local index, outside both SLRU segments; extra slots stay free.
+            for loc in range(self.local_n):
+                self.slot_of[loc] = loc
+                self.expert_in_slot[loc] = loc
+                self.seg[loc] = PINNED
+            self.free_stack = list(range(S - 1, self.local_n - 1, -1))
+
+    # -- helpers ---------------------------------------------------------
+    def _tick(self) -> int:
+        self.clock += 1
+        return self.clock
+
+    def _lru(self, seg: int) -> list[int]:
+        return sorted((s for s in range(self.num_slots) if self.seg[s] == seg),
+                      key=lambda s: self.stamp[s])
+
+    def segment_order(self, seg: int) -> list[int]:
+        """Slots of a segment, least recently used first."""
+        return self._lru(seg)
+
+    def protected_count(self) -> int:
+        return sum(1 for s in self.seg if s == PROTECTED)
+
+    # -- pins (offloader.py:1046-1083) ------------------------------------
+    def apply_pins(self, wanted: list[int]) -> list[tuple[int, int]]:
+        fills = []
+        budget = self.protected_cap
+        n = 0
+        for g in wanted:
+            if n >= budget:
+                break
+            if not (0 <= g < self.global_n):
+                continue
+            loc = self.local_of[g]
+            if loc < 0 or self.slot_of[loc] >= 0 or not self.free_stack:
+                continue
+            slot = self.free_stack.pop()
+            self.expert_in_slot[slot] = loc
+            self.slot_of[loc] = slot
+            self.seg[slot] = PINNED
+            fills.append((loc, slot))
+            n += 1
+        self.protected_cap -= n
+        return fills
+
+    # -- policy ------------------------------------------------------------
+    def _touch(self, slot: int, friendly: bool) -> None:
+        """offloader.py:2009-2021 (pinned slots are in neither segment)."""
+        if self.seg[slot] == PROTECTED:
+            self.stamp[slot] = self._tick()
+        elif self.seg[slot] == PROBATION:
+            if friendly and self.protected_cap > 0:
+                self.seg[slot] = PROTECTED
+                self.stamp[slot] = self._tick()
+                while self.protected_count() > self.protected_cap:
+                    demoted = self._lru(PROTECTED)[0]
+                    self.seg[demoted] = PROBATION
+                    self.stamp[demoted] = self._tick()
+            else:
+                self.stamp[slot] = self._tick()
+
+    def _acquire(self, loc: int, claimed: set) -> int | None:
+        """offloader.py:2036-2074 with allow_protected=True (the gap's call)."""
+        slot = None
+        if self.free_stack:
+            slot = self.free_stack.pop()
+        else:
+            for cand in self._lru(PROBATION):
+                if cand not in claimed:
+                    slot = cand
+                    break
+            if slot is None:
+                for cand in self._lru(PROTECTED):
+                    if cand not in claimed:
+                        slot = cand
+                        break
+        if slot is None:
+            return None
+        old = self.expert_in_slot[slot]                  # _evict_to 2076-2081
+        if old >= 0:
+            self.slot_of[old] = -1
+        self.expert_in_slot[slot] = loc
+        self.slot_of[loc] = slot
+        self.seg[slot] = PROBATION                       # new entries: probation
+        self.stamp[slot] = self._tick()
+        return slot
+
+    def _write_standing_map(self) -> None:
+        """offloader.py:2112-2123 via _write_map 2083-2110."""
+        m = [-1] * self.global_n
+        for slot, loc in enumerate(self.expert_in_slot):
+            if loc >= 0:
+                m[self.global_of_local[loc]] = slot
+        self.expert_map = m
+        self.map_is_standing = True
+
+    # -- the gap (offloader.py:2362-2467) -----------------------------------
+    def gap(self, ids: list[int]) -> list[tuple[int, int]]:
+        """Run one gap call over the flattened topk ids.
+
+        Returns the fills ``[(local, slot), ...]`` in streaming order. Raises
+        SlotOverflow with the state mutated up to the failed acquisition, as
+        the reference does.
+        """
+        self.gaps += 1
+        ids = [int(g) for g in ids]
+        G = self.global_n
+        if self.fast_hit and self.map_is_standing:          # 2409-2424
+            all_hit = True
+            for g in ids:
+                if 0 <= g < G:
+                    loc = self.local_of[g]
+                    if loc >= 0 and self.slot_of[loc] < 0:
+                        all_hit = False
+                        break
+            if all_hit:
+                self.fast_hits += 1
+                return []
+        missing, hit_slots = [], set()
+        for g in sorted(set(ids)):                            # 2427-2441
+            if 0 <= g < G:
+                loc = self.local_of[g]
+                if loc < 0:
+                    continue
+                slot = self.slot_of[loc]
+                if slot < 0:
+                    missing.append(loc)
+                else:
+                    hit_slots.add(slot)
+                    self._touch(slot, True)
+        fills = []
+        changed = False
+        if missing:                                           # 2442-2465
+            claimed = set(hit_slots)
+            for loc in missing:
+                slot = self._acquire(loc, claimed)
+                if slot is None:
+                    raise SlotOverflow(
+                        "working set exceeds slots on a decode-sized step",
+                        fills)
+                fills.append((loc, slot))
+                self.bytes_streamed += self.bytes_per_expert
+                claimed.add(slot)
+            self.misses += len(missing)
+            changed = True
+        if changed or not self.map_is_standing:               # 2466-2467
+            self._write_standing_map()
+        return fills
+
+    # -- views ---------------------------------------------------------------
+    def snapshot(self) -> dict:
+        return {
+            "expert_map": list(self.expert_map),
+            "expert_in_slot": list(self.expert_in_slot),
+            "protected": self._lru(PROTECTED),
+            "probation": self._lru(PROBATION),
+            "free": list(self.free_stack),
+            "map_is_standing": self.map_is_standing,
+            "gaps": self.gaps, "fast_hits": self.fast_hits,
+            "misses": self.misses,
+        }

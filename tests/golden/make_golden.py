@@ -1,0 +1,263 @@
+"""Generate the golden fixtures in this folder from the reference itself.
+
+Run in a container that has the reference checkout and vLLM installed::
+
+    SLUICE_REFERENCE=<path to kfirtoledo/sluice> python tests/golden/make_golden.py
+
+It writes:
+
+* ``slot_traces.json`` — per scenario, the flattened ``topk_ids`` of every
+  step and the state after each call of the reference's own
+  ``ExpertStreamOffloader._router_split_gap`` (``src/sluice/offloader.py``
+  2362-2467) on a CPU ``_ExpertLayerCache`` built by the reference's own
+  ``_install_cache`` (895-1044) and ``_apply_pins`` (1046-1083): the expert
+  map, slot owners, slot contents, protected / probation order and counters.
+* ``routing.npz`` — router logits and vLLM 0.22's CPU ``grouped_topk``
+  (``fused_moe/cpu_fused_moe.py`` 59-115) outputs for the V2-Lite, Qwen3 and
+  DeepSeek-V3 routing modes.
+* ``moe.npz`` — a small ``fused_experts`` case through an expert map,
+  evaluated by vLLM's ``cpu_fused_moe_torch`` (``cpu_fused_moe.py`` 428-482).
+
+Nothing at test time reads the reference; the tests read these files.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REF = os.environ.get("SLUICE_REFERENCE", "/root/reference")
+
+
+def _ref_offloader(slots: int, fast_hit: bool, frac: float, no_static_full=False):
+    os.environ["SLUICE_RS_FAST_HIT"] = "1" if fast_hit else "0"
+    os.environ["SLUICE_PROTECT_FRAC"] = str(frac)
+    os.environ["SLUICE_NO_STATIC_FULL"] = "1" if no_static_full else "0"
+    os.environ.pop("SLUICE_ROUTER_SPLIT", None)
+    from sluice.offloader import ExpertStreamOffloader
+
+    ExpertStreamOffloader._infer_device = staticmethod(lambda m: torch.device("cpu"))
+    off = ExpertStreamOffloader(slots)
+    off.pin_memory = False
+    return off
+
+
+class _FakeMoE(nn.Module):
+    """Just enough of a FusedMoE layer for the reference's _install_cache."""
+
+    def __init__(self, local_n: int, global_n: int, expert_map):
+        super().__init__()
+        self.local_num_experts = local_n
+        self.global_num_experts = global_n
+        self.quant_method = None
+        # each local expert's payload is its own local index
+        self.w = nn.Parameter(torch.arange(local_n, dtype=torch.float32).view(-1, 1),
+                              requires_grad=False)
+        self.expert_map = expert_map
+
+
+def _zipf_ids(gen, steps, T, k, E, s=1.1, locality=0.6):
+    """Top-k ids per token without replacement, Zipf popularity over a seeded
+    permutation, 60% of tokens repeating their previous-step selection."""
+    perm = torch.randperm(E, generator=gen)
+    p = 1.0 / torch.arange(1, E + 1, dtype=torch.float64) ** s
+    p = p / p.sum()
+    prev = None
+    out = []
+    for _ in range(steps):
+        rows = []
+        for t in range(T):
+            if prev is not None and torch.rand(1, generator=gen).item() < locality:
+                rows.append(prev[t])
+                continue
+            pick = torch.multinomial(p, k, replacement=False, generator=gen)
+            rows.append(perm[pick].tolist())
+        prev = rows
+        out.append([g for r in rows for g in r])
+    return out
+
+
+def _run_scenario(name, *, slots, global_n, local_n, owned_lo=0, steps_ids,
+                  fast_hit=True, frac=0.5, pins=None, no_static_full=False):
+    off = _ref_offloader(slots, fast_hit, frac, no_static_full)
+    if pins is not None:
+        off._pin_layers = {0: list(pins)}
+    if local_n == global_n:
+        emap = None
+        local_of = list(range(global_n))
+    else:
+        lo = [-1] * global_n
+        for i in range(local_n):
+            lo[owned_lo + i] = i
+        emap = torch.tensor(lo, dtype=torch.int32)
+        local_of = lo
+    mod = _FakeMoE(local_n, global_n, emap)
+    off._install_cache(mod)
+    cache = off._caches[id(mod)]
+    assert not cache.static_full, name
+    off._rs_caches.append(cache)
+    trace = []
+    overflow_step = -1
+    for i, ids in enumerate(steps_ids):
+        try:
+            off._router_split_gap(0, torch.tensor(ids, dtype=torch.int32))
+        except RuntimeError:
+            overflow_step = i
+        w = cache.gpu_cache["w"][:, 0]
+        trace.append({
+            "expert_map": cache.expert_map_buf.tolist(),
+            "expert_in_slot": [-1 if v is None else int(v) for v in cache.expert_in_slot],
+            "slot_payload": [int(w[s].item()) if cache.expert_in_slot[s] is not None
+                             else -1 for s in range(cache.num_slots)],
+            "protected": list(cache.protected),
+            "probation": list(cache.probation),
+            "map_is_standing": bool(cache.map_is_standing),
+            "gaps": off._rs_gaps, "misses": off._rs_misses,
+            "fast_hits": off._rs_fast_hits,
+        })
+        if overflow_step >= 0:
+            break
+    return {
+        "name": name, "num_slots": cache.num_slots, "global_n": global_n,
+        "local_n": local_n, "local_of": local_of, "fast_hit": fast_hit,
+        "protect_frac": frac, "protected_cap": cache.protected_cap,
+        "pins": list(pins) if pins is not None else None,
+        "pinned_slots": sorted(cache.pinned_slots),
+        "prefill_resident": bool(no_static_full and slots >= local_n),
+        "steps": steps_ids[: len(trace)], "trace": trace,
+        "overflow_step": overflow_step,
+    }
+
+
+def make_slot_traces():
+    g = torch.Generator().manual_seed(1234)
+    zipf = _zipf_ids(g, 64, 8, 6, 64)
+    uni = [torch.randint(0, 64, (48,), generator=g).tolist() for _ in range(40)]
+    qwen = _zipf_ids(g, 48, 12, 8, 128)
+    v3 = _zipf_ids(g, 40, 8, 8, 256)
+    noisy = []
+    for ids in _zipf_ids(g, 30, 8, 6, 64):
+        ids = list(ids)
+        ids[3] = -1
+        ids[7] = 64 + (len(noisy) % 5)
+        noisy.append(ids)
+    big = [torch.randperm(64, generator=g)[:48].tolist() for _ in range(12)]
+    exact = [torch.randperm(64, generator=g)[:48].tolist() for _ in range(12)]
+    sc = [
+        _run_scenario("v2lite_zipf_fasthit", slots=48, global_n=64, local_n=64,
+                      steps_ids=zipf),
+        _run_scenario("v2lite_zipf_nofasthit", slots=48, global_n=64, local_n=64,
+                      steps_ids=zipf, fast_hit=False),
+        _run_scenario("v2lite_uniform", slots=48, global_n=64, local_n=64,
+                      steps_ids=uni),
+        _run_scenario("v2lite_frac0", slots=48, global_n=64, local_n=64,
+                      steps_ids=zipf, frac=0.0),
+        _run_scenario("v2lite_frac09", slots=48, global_n=64, local_n=64,
+                      steps_ids=uni, frac=0.9),
+        _run_scenario("v2lite_pins", slots=48, global_n=64, local_n=64,
+                      steps_ids=uni, pins=[5, 9, 9, 70, 2, 11]),
+        _run_scenario("v2lite_invalid_ids", slots=40, global_n=64, local_n=64,
+                      steps_ids=noisy),
+        _run_scenario("ep_rank1_of2", slots=24, global_n=64, local_n=32,
+                      owned_lo=32, steps_ids=uni),
+        _run_scenario("qwen3_s96", slots=96, global_n=128, local_n=128,
+                      steps_ids=qwen),
+        _run_scenario("v3_ep4_rank2", slots=48, global_n=256, local_n=64,
+                      owned_lo=128, steps_ids=v3),
+        _run_scenario("overflow_s40", slots=40, global_n=64, local_n=64,
+                      steps_ids=zipf[:10] + big[:2]),
+        _run_scenario("uniques_equal_slots", slots=48, global_n=64, local_n=64,
+                      steps_ids=exact),
+        _run_scenario("prefill_resident", slots=64, global_n=64, local_n=64,
+                      steps_ids=uni[:8], no_static_full=True),
+    ]
+    with open(os.path.join(HERE, "slot_traces.json"), "w") as f:
+        json.dump({"generator": "tests/golden/make_golden.py",
+                   "scenarios": sc}, f, separators=(",", ":"))
+    for s in sc:
+        print(f"{s['name']}: steps={len(s['trace'])} misses={s['trace'][-1]['misses']} "
+              f"fast_hits={s['trace'][-1]['fast_hits']} overflow={s['overflow_step']}")
+
+
+def make_routing():
+    from vllm.model_executor.layers.fused_moe import cpu_fused_moe as cfm
+
+    g = torch.Generator().manual_seed(99)
+    out = {}
+    cases = {
+        # name: (T, H, E, topk, renorm, groups, topk_group, scoring, scale, bias)
+        "v2lite": (32, 2048, 64, 6, False, 1, 1, "softmax", 1.0, False),
+        "qwen3": (32, 2048, 128, 8, True, 1, 1, "softmax", 1.0, False),
+        "v3": (32, 7168, 256, 8, True, 8, 4, "sigmoid", 2.5, True),
+    }
+    for name, (T, H, E, k, renorm, G, TG, sf, scale, has_bias) in cases.items():
+        x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+        w = (torch.randn(E, H, generator=g) * 0.02).to(torch.bfloat16)
+        lb = 1.5 * torch.log(1.0 / (torch.randperm(E, generator=g) + 1).double()).float()
+        logits = (x.float() @ w.float().t() + lb).to(torch.bfloat16)
+        sb = (torch.rand(E, generator=g) * 0.1).float() if has_bias else None
+        tw, ti = cfm.grouped_topk(x, logits, k, renorm, G, TG, sf, scale, sb)
+        out[f"{name}_logits"] = logits.view(torch.int16).numpy()
+        out[f"{name}_ids"] = ti.numpy()
+        out[f"{name}_weights"] = tw.numpy()
+        if sb is not None:
+            out[f"{name}_score_bias"] = sb.numpy()
+        out[f"{name}_meta"] = np.array([T, H, E, k, int(renorm), G, TG,
+                                        1 if sf == "sigmoid" else 0], dtype=np.int64)
+        out[f"{name}_scale"] = np.array([scale], dtype=np.float32)
+    np.savez_compressed(os.path.join(HERE, "routing.npz"), **out)
+    print("routing:", sorted(k for k in out if k.endswith("_ids")))
+
+
+def make_moe():
+    from vllm.model_executor.layers.activation import SiluAndMul
+    from vllm.model_executor.layers.fused_moe import cpu_fused_moe as cfm
+    from vllm.model_executor.layers.fused_moe.activation import MoEActivation
+
+    cfm._CPU_MOE_ACT_FN[MoEActivation.SILU] = SiluAndMul.forward_native
+    g = torch.Generator().manual_seed(7)
+    T, H, I, S, E, k = 6, 256, 128, 4, 8, 3
+    hs = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    w13 = (torch.randn(S, 2 * I, H, generator=g) * 0.05).to(torch.bfloat16)
+    w2 = (torch.randn(S, H, I, generator=g) * 0.05).to(torch.bfloat16)
+    emap = torch.tensor([2, -1, 0, -1, 3, 1, -1, -1], dtype=torch.int32)
+    ti = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)]).to(torch.int32)
+    tw = torch.rand(T, k, generator=g).float()
+    # vLLM's CPU path has no expert map: route unmapped pairs to a zero expert
+    # (one zero expert per choice j, so no token sees the same expert twice)
+    zero_slot = S + torch.arange(k, dtype=torch.int32).expand(T, k)
+    slots = torch.where(emap[ti.long()] >= 0, emap[ti.long()], zero_slot)
+    w13z = torch.cat([w13, torch.zeros(k, 2 * I, H, dtype=w13.dtype)])
+    w2z = torch.cat([w2, torch.zeros(k, H, I, dtype=w2.dtype)])
+
+    class _L:
+        pass
+
+    layer = _L()
+    layer.gate_up_linear = [(lambda x, i=i: F.linear(x, w13z[i])) for i in range(S + k)]
+    layer.down_linear = [(lambda x, i=i: F.linear(x, w2z[i])) for i in range(S + k)]
+    cfm._CPU_MOE_LAYER_CACHE[12345] = lambda: layer
+    out = torch.empty(T, H, dtype=torch.bfloat16)
+    cfm.cpu_fused_moe_torch(12345, out, hs, tw, slots.to(torch.int32), "silu",
+                            global_num_experts=S + k)
+    np.savez_compressed(
+        os.path.join(HERE, "moe.npz"),
+        hs=hs.view(torch.int16).numpy(), w13=w13.view(torch.int16).numpy(),
+        w2=w2.view(torch.int16).numpy(), expert_map=emap.numpy(),
+        topk_ids=ti.numpy(), topk_weights=tw.numpy(),
+        out=out.view(torch.int16).numpy())
+    print("moe: out", out.float().abs().mean().item())
+
+
+if __name__ == "__main__":
+    sys.path.insert(0, os.path.join(REF, "src"))
+    make_slot_traces()
+    make_routing()
+    make_moe()
