@@ -1,0 +1,179 @@
+/*
+ * sluice_b200 — C ABI of the B200 (sm_100a) MoE expert-offload hot path.
+ *
+ * Every entry point takes plain device / host pointers and sizes, enqueues
+ * its kernels on the caller's CUDA stream and returns an int status (SL_OK on
+ * success). No call synchronises the stream, so every call can be captured in
+ * a CUDA graph. Conditions found on the device (slot overflow, a bounded wait
+ * that ran out) are written to a device status word that the caller reads
+ * outside capture (sl_slot_state_offsets / the fused-experts workspace).
+ *
+ * Tensor layouts (row-major, last dim contiguous):
+ *   hidden        bf16 [T, H]
+ *   gate_w        bf16 [E, H]
+ *   w13 slots     bf16 [num_slots, 2*I, H]   (gate rows, then up rows)
+ *   w2 slots      bf16 [num_slots, H, I]
+ *   topk_weights  f32  [T, topk];  topk_ids  i32 [T, topk]
+ *   expert_map    i32  [global_n]  (global id -> slot, -1 = not resident)
+ *
+ * Each declaration names the reference interface it replaces
+ * (kfirtoledo/sluice, paths inside that project; vLLM paths are the
+ * third-party code the reference calls, vLLM 0.22 as installed here).
+ */
+#ifndef SLUICE_B200_H
+#define SLUICE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* sl_stream_t; /* a cudaStream_t */
+
+enum {
+  SL_OK = 0,
+  SL_ERR_OVERFLOW = 1,    /* working set exceeds slots (offloader.py:2456-2460) */
+  SL_ERR_INVALID = 2,     /* bad argument */
+  SL_ERR_CUDA = 3,        /* CUDA runtime error */
+  SL_ERR_UNSUPPORTED = 4, /* shape / dtype this build does not cover */
+  SL_ERR_TIMEOUT = 5      /* a bounded device wait ran out */
+};
+
+/* Human-readable text for a status code. */
+const char* sl_status_string(int status);
+/* Library ABI version (major*100 + minor). */
+int sl_version(void);
+/* Number of SMs of the current device (used to size persistent grids). */
+int sl_device_sm_count(void);
+
+/* ------------------------------------------------------------------ router
+ * Replaces runner.gate(hs) + router.select_experts(...)
+ *   src/sluice/offloader.py:2582-2585 (router-split entry);
+ *   vLLM fused_moe/router/base_router.py:250-298 (select_experts),
+ *   router/grouped_topk_router.py:81-166 (grouped_topk),
+ *   router/fused_topk_router.py:69-118 (topk_softmax contract).
+ * logits = bf16(hidden @ gate_w^T + logit_bias); scores = softmax or sigmoid
+ * (fp32); optional score_bias (e_score_correction_bias) for selection only;
+ * num_expert_group/topk_group group mask (1/1 = no grouping); top-k with
+ * ties to the lower id; optional renormalisation; routed_scaling_factor.
+ * Outputs are ordered by selection score descending, id ascending.
+ * scoring: 0 = softmax, 1 = sigmoid. router_logits_out (bf16 [T,E]) may be
+ * NULL. Limits: E % 32 == 0, E <= 512, H % 8 == 0, topk <= 32. */
+int sl_route(const void* hidden, const void* gate_w, const float* logit_bias,
+             int T, int H, int E, int topk, int scoring, int num_expert_group,
+             int topk_group, int renormalize, float routed_scaling_factor,
+             const float* score_bias, float* topk_weights, int32_t* topk_ids,
+             void* router_logits_out, sl_stream_t stream);
+
+/* select_experts from given bf16 router logits [T, E]
+ * (vLLM router/base_router.py:250-298). Same arithmetic as sl_route. */
+int sl_select_experts(const void* router_logits, int T, int E, int topk,
+                      int scoring, int num_expert_group, int topk_group,
+                      int renormalize, float routed_scaling_factor,
+                      const float* score_bias, float* topk_weights,
+                      int32_t* topk_ids, sl_stream_t stream);
+
+/* -------------------------------------------------------------- slot state
+ * Device-resident state of one layer's slot cache: replaces the host-side
+ * _ExpertLayerCache (offloader.py:121-169) fields slot_of, expert_in_slot,
+ * free_slots, protected / probation (SLRU), protected_cap, local_of,
+ * global_of_local, map_is_standing, plus the gap counters
+ * (offloader.py:2367-2385) and the fill list of the last gap. */
+enum {
+  SL_SEG_FREE = 0, SL_SEG_PROBATION = 1, SL_SEG_PROTECTED = 2, SL_SEG_PINNED = 3
+};
+enum { SL_PLAN_FAST_HIT = 1 }; /* SLUICE_RS_FAST_HIT (offloader.py:2409-2424) */
+
+/* Field offsets (bytes) inside the state block, in this order:
+ * 0 header (int32 x 16, see SL_HDR_*), 1 counters (uint64 x 8, SL_CNT_*),
+ * 2 local_of[global_n], 3 global_of_local[local_n], 4 slot_of[local_n],
+ * 5 expert_in_slot[S], 6 seg[S] (uint8), 7 stamp[S] (uint32),
+ * 8 free_stack[S], 9 fill_local[S], 10 fill_slot[S]; offsets[11] = total. */
+enum { SL_STATE_NFIELDS = 11 };
+enum {
+  SL_HDR_NUM_SLOTS = 0, SL_HDR_GLOBAL_N, SL_HDR_LOCAL_N, SL_HDR_PROTECTED_CAP,
+  SL_HDR_FLAGS, SL_HDR_MAP_IS_STANDING, SL_HDR_FREE_TOP, SL_HDR_PROTECTED_COUNT,
+  SL_HDR_CLOCK, SL_HDR_STATUS, SL_HDR_FILL_COUNT, SL_HDR_LAST_MISSES
+};
+enum {
+  SL_CNT_GAPS = 0, SL_CNT_FAST_HITS, SL_CNT_MISSES, SL_CNT_HITS,
+  SL_CNT_OVERFLOWS, SL_CNT_FILLS
+};
+size_t sl_slot_state_bytes(int num_slots, int global_n, int local_n);
+int sl_slot_state_offsets(int num_slots, int global_n, int local_n,
+                          size_t* offsets /* [SL_STATE_NFIELDS + 1] */);
+
+/* Initialise a state block from host arrays (replaces the state set-up of
+ * _install_cache offloader.py:936-1003 and _apply_pins 1046-1083, which the
+ * host computes). expert_in_slot / seg are [S]; free_stack lists the free
+ * slots bottom first (the next slot taken is free_stack[n_free-1]). Copies
+ * are enqueued on `stream` from the host arrays, which must stay valid until
+ * the stream reaches them (the call itself copies them to a staging buffer,
+ * so they may be freed on return). */
+int sl_slot_state_init(void* state, int num_slots, int global_n, int local_n,
+                       int protected_cap, int flags, const int32_t* local_of,
+                       const int32_t* expert_in_slot, const uint8_t* seg,
+                       const int32_t* free_stack, int n_free,
+                       sl_stream_t stream);
+
+/* The gap's slot planning, on the device: replaces the body of
+ * _router_split_gap (offloader.py:2362-2467) minus the device-to-host id
+ * sync: FAST_HIT check, sorted unique selected ids, SLRU touches of hits,
+ * _acquire_slot / _evict_to for misses in ascending id order (the fill
+ * list), and the standing expert map (_write_standing_map 2112-2123) written
+ * in place into expert_map [global_n]. One CTA. Overflow sets the state's
+ * status word to SL_ERR_OVERFLOW (the map is then left as it was). */
+int sl_plan_slots(void* state, const int32_t* topk_ids, int num_ids,
+                  int32_t* expert_map, sl_stream_t stream);
+
+/* Stream the last plan's fills: replaces _stream_in (offloader.py:2709-2723)
+ * and its copy-stream events (1979-1991). For every fill (local, slot) and
+ * every parameter p, copies bytes_per_expert[p] bytes from
+ * host_src[p] + local*bytes_per_expert[p] (mapped pinned host memory) to
+ * slot_dst[p] + slot*bytes_per_expert[p], as device-side 16-byte loads.
+ * bytes_per_expert[p] % 16 == 0; num_params <= 8; num_ctas <= 0 picks a
+ * default. */
+int sl_stream_experts(const void* state, int num_params,
+                      const void* const* host_src, void* const* slot_dst,
+                      const size_t* bytes_per_expert, int num_ctas,
+                      sl_stream_t stream);
+
+/* Page-locked host memory mapped into the device address space
+ * (cudaHostAlloc Mapped|Portable): the host store of offloaded experts
+ * (replaces cpu.pin_memory(), offloader.py:965-967). */
+int sl_host_alloc_mapped(size_t bytes, void** host_ptr);
+int sl_host_free(void* host_ptr);
+
+/* ----------------------------------------------------------- fused experts
+ * Replaces torch.ops.vllm.fused_experts(h, w13, w2, tw, ti, activation=
+ * "silu", global_num_experts, expert_map) (offloader.py:2590-2599; vLLM
+ * fused_moe.py:1587-1869) plus the shared-expert MLP (offloader.py:2602) and
+ * the runner tail (vLLM runner/moe_runner.py:350-366, 663-680):
+ *   out[t] = bf16( shared(t) + bf16(scale * bf16(sum_j w[t,j] * z(t,j))) )
+ * with z(t,j) = W2[e] (silu(W1g[e] x_t) * W1u[e] x_t) through
+ * e = expert_map[topk_ids[t,j]] (a -1 entry contributes nothing) and shared
+ * experts given as n_shared experts of the same I (shared_w13 [n_shared,2I,H],
+ * shared_w2 [n_shared,H,I]; NULL/0 for none). expert_map NULL means ids are
+ * slot indices. weight_dtype 0 = bf16 (fp8 is not in this build yet).
+ * Tensor-core GEMMs (tcgen05, TMEM accumulators, TMA-fed). Limits:
+ * H % 128 == 0, I % 128 == 0, num_slots + n_shared <= 1024.
+ * workspace: device memory of at least sl_fused_experts_workspace_bytes(...),
+ * 256-byte aligned; its first int32 is the device status word. */
+size_t sl_fused_experts_workspace_bytes(int T, int topk, int H, int I,
+                                        int num_slots, int n_shared);
+int sl_fused_experts(const void* hidden, int T, int H, int I,
+                     const void* w13, const void* w2, int num_slots,
+                     int weight_dtype, const float* topk_weights,
+                     const int32_t* topk_ids, int topk,
+                     const int32_t* expert_map, int global_n,
+                     const void* shared_w13, const void* shared_w2,
+                     int n_shared, float routed_scaling_factor, void* out,
+                     void* workspace, size_t workspace_bytes,
+                     sl_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SLUICE_B200_H */

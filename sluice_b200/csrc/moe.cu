@@ -1,0 +1,569 @@
+// fused_experts on sm_100a: token grouping through the expert map, two
+// tcgen05 grouped GEMMs (gate/up with SwiGLU fused in the epilogue, then
+// down), and the weighted top-k combine with the shared experts.
+//
+// Reference semantics (kfirtoledo/sluice calls vLLM for this step):
+//   offloader.py:2590-2602  fused_experts(h, w13, w2, tw, ti, "silu",
+//                           global_num_experts, expert_map) + shared MLP
+//   vLLM fused_moe.py:1587-1869 (map lookup, -1 = skip, SiLU-and-mul,
+//   routed weight, moe_sum), runner/moe_runner.py:350-366, 663-680 (routed
+//   scaling, shared + routed).
+//
+// Data flow per call (all on the caller's stream, no host sync):
+//   align    1 CTA: slot of every (token, choice) via the map, per-slot counts,
+//            work items of BN tokens, row of every pair; gathers token rows
+//            into X (rows grouped by item) and copies the shared rows.
+//   gemm1    persistent, one CTA per SM: tile = (item, 128 intermediate
+//            columns). TMA loads a 128x64 gate tile, a 128x64 up tile and the
+//            BNx64 token tile per stage; two tcgen05.mma (M=128, N=BN, K=16
+//            x4) into two TMEM accumulators; the epilogue computes
+//            a = silu(g) * u per (column, token) and writes bf16 rows of A.
+//   gemm2    same pipeline: tile = (item, 128 hidden rows), K = I; epilogue
+//            writes bf16 z rows of Z.
+//   combine  out[t] = shared(t) + scale * sum_j w[t,j] z(t,j).
+// Warp roles in the GEMMs: warp 0 TMA producer, warp 1 MMA issuer (one
+// thread) and TMEM owner, warps 2-5 epilogue (TMEM lanes 32*(warp%4)..).
+#include <cudaTypedefs.h>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace {
+
+constexpr int BM = 128;      // weight rows per tile
+constexpr int BK = 64;       // K per stage: one 128-byte swizzle atom of bf16
+constexpr int kThreads = 192;
+constexpr int kMaxCode = 1056;  // slots + shared experts per call
+constexpr int kMaxShared = 32;
+
+// workspace header (int32 words)
+enum { WS_STATUS = 0, WS_NUM_ITEMS = 1, WS_NUM_ROWS = 2, WS_SH_BASE = 8, WS_HDR_WORDS = 64 };
+
+struct WsLayout {
+  size_t items, pair_pos, x, act, z, total;
+  int max_items, max_rows;
+};
+
+__host__ __device__ inline size_t r256(size_t v) { return (v + 255) & ~size_t(255); }
+
+inline int choose_bn(int /*T*/) { return 16; }
+
+inline WsLayout ws_layout(int T, int topk, int H, int I, int S, int n_sh, int BN) {
+  WsLayout w;
+  const long P = static_cast<long>(T) * topk;
+  const long routed = P / BN + (P < S ? P : S);
+  const long shared = static_cast<long>(n_sh) * ((T + BN - 1) / BN);
+  w.max_items = static_cast<int>(routed + shared + 1);
+  w.max_rows = w.max_items * BN;
+  size_t o = r256(WS_HDR_WORDS * 4);
+  w.items = o; o += r256(sizeof(int4) * w.max_items);
+  w.pair_pos = o; o += r256(sizeof(int32_t) * (P > 0 ? P : 1));
+  w.x = o; o += r256(sizeof(__nv_bfloat16) * size_t(w.max_rows) * H);
+  w.act = o; o += r256(sizeof(__nv_bfloat16) * size_t(w.max_rows) * I);
+  w.z = o; o += r256(sizeof(__nv_bfloat16) * size_t(w.max_rows) * H);
+  w.total = o;
+  return w;
+}
+
+// ------------------------------------------------------------------ align
+__global__ void __launch_bounds__(1024) align_kernel(
+    const int32_t* __restrict__ ids, int T, int topk, const int32_t* __restrict__ emap,
+    int G, int S, int n_sh, int BN, const __nv_bfloat16* __restrict__ hs, int H,
+    int32_t* __restrict__ ws_hdr, int4* __restrict__ items, int32_t* __restrict__ pair_pos,
+    __nv_bfloat16* __restrict__ X, int max_items) {
+  __shared__ int cnt[kMaxCode];
+  __shared__ int ibase[kMaxCode + 1];
+  __shared__ int cursor[kMaxCode];
+  __shared__ int warp_sums[32];
+  const int tid = threadIdx.x, nthr = blockDim.x;
+  const int P = T * topk;
+  const int C = S + n_sh;
+  for (int c = tid; c < C; c += nthr) {
+    cnt[c] = c < S ? 0 : T;
+    cursor[c] = 0;
+  }
+  __syncthreads();
+  for (int p = tid; p < P; p += nthr) {
+    const int g = ids[p];
+    int s = -1;
+    if (emap) {
+      if (g >= 0 && g < G) s = emap[g];
+    } else {
+      s = g;
+    }
+    if (s < 0 || s >= S) s = -1;
+    pair_pos[p] = s;
+    if (s >= 0) atomicAdd(&cnt[s], 1);
+  }
+  __syncthreads();
+  // exclusive scan of tiles per code (C <= kMaxCode; each thread two entries)
+  const int lane = tid & 31, warp = tid >> 5;
+  int a0 = 0, a1 = 0;
+  const int c0 = 2 * tid, c1 = 2 * tid + 1;
+  if (c0 < C) a0 = (cnt[c0] + BN - 1) / BN;
+  if (c1 < C) a1 = (cnt[c1] + BN - 1) / BN;
+  int v = a0 + a1;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += n;
+  }
+  if (lane == 31) warp_sums[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int ws = warp_sums[lane];
+    int wi = ws;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += n;
+    }
+    warp_sums[lane] = wi - ws;  // exclusive
+  }
+  __syncthreads();
+  const int excl = warp_sums[warp] + incl - v;
+  if (c0 < C) ibase[c0] = excl;
+  if (c1 < C) ibase[c1] = excl + a0;
+  if (tid == nthr - 1) ibase[C] = excl + v;  // total (C <= 2*nthr)
+  __syncthreads();
+  const int n_items = ibase[C];
+  if (tid == 0) {
+    ws_hdr[WS_STATUS] = (n_items > max_items) ? SL_ERR_INVALID : SL_OK;
+    ws_hdr[WS_NUM_ITEMS] = n_items <= max_items ? n_items : 0;
+    ws_hdr[WS_NUM_ROWS] = n_items * BN;
+    for (int i = 0; i < n_sh; ++i) ws_hdr[WS_SH_BASE + i] = ibase[S + i] * BN;
+  }
+  if (n_items > max_items) return;
+  for (int c = tid; c < C; c += nthr) {
+    const int nt = ibase[c + 1] - ibase[c];
+    for (int i = 0; i < nt; ++i)
+      items[ibase[c] + i] = make_int4(c, (ibase[c] + i) * BN, min(BN, cnt[c] - i * BN), 0);
+  }
+  for (int p = tid; p < P; p += nthr) {
+    const int s = pair_pos[p];
+    if (s >= 0) pair_pos[p] = ibase[s] * BN + atomicAdd(&cursor[s], 1);
+  }
+  __syncthreads();
+  // gather token rows: routed pairs, then every token once per shared expert
+  const int vrow = H >> 3;
+  const uint4* src = reinterpret_cast<const uint4*>(hs);
+  uint4* dst = reinterpret_cast<uint4*>(X);
+  for (long q = tid; q < static_cast<long>(P) * vrow; q += nthr) {
+    const int p = static_cast<int>(q / vrow), c = static_cast<int>(q % vrow);
+    const int pos = pair_pos[p];
+    if (pos >= 0) dst[static_cast<long>(pos) * vrow + c] = src[static_cast<long>(p / topk) * vrow + c];
+  }
+  for (long q = tid; q < static_cast<long>(n_sh) * T * vrow; q += nthr) {
+    const int r = static_cast<int>(q / vrow), c = static_cast<int>(q % vrow);
+    const int i = r / T, t = r % T;
+    dst[static_cast<long>(ibase[S + i] * BN + t) * vrow + c] = src[static_cast<long>(t) * vrow + c];
+  }
+}
+
+// ------------------------------------------------------------- tcgen05 GEMM
+// GATED = true: gate/up GEMM (two weight tiles per stage, SwiGLU epilogue).
+// GATED = false: down GEMM (one weight tile per stage).
+template <int BN, int STAGES, bool GATED>
+struct GemmCfg {
+  static constexpr int kATile = BM * BK;                     // elements
+  static constexpr int kBTile = BN * BK;
+  static constexpr int kNumA = GATED ? 2 : 1;
+  static constexpr int kStageBytes = (kNumA * kATile + kBTile) * 2;
+  static constexpr int kAccCols = GATED ? 2 * BN : BN;       // per accumulator
+  static constexpr int kTmemCols = (2 * kAccCols) <= 32 ? 32 : (2 * kAccCols) <= 64 ? 64
+                                   : (2 * kAccCols) <= 128 ? 128 : 256;
+  static constexpr int kSmemBytes = STAGES * kStageBytes + 1024 /*align*/ + 256 /*bars*/;
+};
+
+template <int BN, int STAGES, bool GATED>
+__global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(
+    const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_wsh,
+    const __grid_constant__ CUtensorMap tm_b, const int32_t* __restrict__ ws_hdr,
+    const int4* __restrict__ items, __nv_bfloat16* __restrict__ out, int S, int K,
+    int M_total /* rows of one expert's weight block in this GEMM's view */,
+    int out_ld, int32_t* __restrict__ status) {
+  using Cfg = GemmCfg<BN, STAGES, GATED>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  __nv_bfloat16* sA = reinterpret_cast<__nv_bfloat16*>(smem);  // [STAGES][kNumA][BM*BK]
+  __nv_bfloat16* sB = sA + STAGES * Cfg::kNumA * Cfg::kATile;  // [STAGES][BN*BK]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::kBTile);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* mma_done = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      sl::mbar_init(&full[s], 1);
+      sl::mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      sl::mbar_init(&tfull[a], 1);
+      sl::mbar_init(&tempty[a], 4);
+    }
+    sl::mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    sl::fence_barrier_init();
+    sl::tma_prefetch_desc(&tm_w);
+    sl::tma_prefetch_desc(&tm_wsh);
+    sl::tma_prefetch_desc(&tm_b);
+  }
+  if (warp == 1) sl::tmem_alloc(tmem_slot, Cfg::kTmemCols);
+  sl::tc_fence_before();
+  __syncthreads();
+  sl::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int m_tiles = M_total / BM;  // GATED: I/128 column blocks; else H/128
+  const int num_items = ws_hdr[WS_NUM_ITEMS];
+  const int num_tiles = num_items * m_tiles;
+  const int k_blocks = K / BK;
+
+  if (warp == 0) {
+    // ------------------------------------------------------ TMA producer
+    if (sl::elect_one()) {
+      const uint64_t pol_w = sl::policy_evict_first();
+      const uint64_t pol_b = sl::policy_evict_last();
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_phase_mask = 0;  // stages with a TMA in flight at exit
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int4 it = items[tile / m_tiles];
+        const int mt = tile % m_tiles;
+        const bool sh = it.x >= S;
+        const CUtensorMap* tw = sh ? &tm_wsh : &tm_w;
+        const int e = sh ? it.x - S : it.x;
+        // weight rows of this tile in the 2-D view [experts * rows, K]
+        const int row0 = GATED ? e * 2 * M_total + mt * BM : e * M_total + mt * BM;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (*abort_flag || !sl::mbar_wait(&empty[stage], phase ^ 1)) {
+            ok = false;
+            break;
+          }
+          sl::mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+          __nv_bfloat16* a0 = sA + (stage * Cfg::kNumA) * Cfg::kATile;
+          sl::tma_load_2d(a0, tw, &full[stage], kb * BK, row0, pol_w);
+          if constexpr (GATED)
+            sl::tma_load_2d(a0 + Cfg::kATile, tw, &full[stage], kb * BK, row0 + M_total, pol_w);
+          sl::tma_load_2d(sB + stage * Cfg::kBTile, &tm_b, &full[stage], kb * BK, it.y, pol_b);
+          issued_phase_mask = (issued_phase_mask & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        atomicExch(status, SL_ERR_TIMEOUT);
+        *abort_flag = 1;
+        // let every TMA issued into shared memory land before the CTA exits
+        for (int s = 0; s < STAGES; ++s)
+          (void)sl::mbar_wait(&full[s], (issued_phase_mask >> s) & 1u);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------- MMA issuer
+    if (sl::elect_one()) {
+      constexpr uint32_t idesc = sl::umma_idesc_bf16(BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        if (*abort_flag || !sl::mbar_wait(&tempty[acc], acc_phase ^ 1)) {
+          ok = false;
+          break;
+        }
+        sl::tc_fence_after();
+        const uint32_t d0 = tmem_base + acc * Cfg::kAccCols;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (*abort_flag || !sl::mbar_wait(&full[stage], phase)) {
+            ok = false;
+            break;
+          }
+          sl::tc_fence_after();
+          const uint32_t a_addr = sl::smem_u32(sA + (stage * Cfg::kNumA) * Cfg::kATile);
+          const uint32_t b_addr = sl::smem_u32(sB + stage * Cfg::kBTile);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t bd = sl::umma_desc_sw128(b_addr + k * 32);
+            const uint32_t accum = (kb | k) != 0;
+            sl::umma_bf16(d0, sl::umma_desc_sw128(a_addr + k * 32), bd, idesc, accum);
+            if constexpr (GATED)
+              sl::umma_bf16(d0 + BN, sl::umma_desc_sw128(a_addr + Cfg::kATile * 2 + k * 32), bd,
+                            idesc, accum);
+          }
+          sl::umma_commit(&empty[stage]);  // stage free once these MMAs finish
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        sl::umma_commit(&tfull[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      if (!ok) {
+        atomicExch(status, SL_ERR_TIMEOUT);
+        *abort_flag = 1;
+      }
+      // every MMA this thread issued has completed before TMEM is freed
+      sl::umma_commit(mma_done);
+      (void)sl::mbar_wait(mma_done, 0);
+    }
+  } else {
+    // --------------------------------------------------------- epilogue
+    const int q = warp & 3;
+    const int row = q * 32 + lane;  // TMEM lane = weight row within the tile
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      if (*abort_flag || !sl::mbar_wait(&tfull[acc], acc_phase)) {
+        atomicExch(status, SL_ERR_TIMEOUT);
+        *abort_flag = 1;
+        break;
+      }
+      sl::tc_fence_after();
+      const int4 it = items[tile / m_tiles];
+      const int mt = tile % m_tiles;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * Cfg::kAccCols;
+      float v0[BN];
+      float v1[BN];
+#pragma unroll
+      for (int c = 0; c < BN; c += 16) {
+        float tmp[16];
+        sl::tmem_ld16(taddr + c, tmp);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v0[c + i] = tmp[i];
+        if constexpr (GATED) {
+          sl::tmem_ld16(taddr + BN + c, tmp);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v1[c + i] = tmp[i];
+        }
+      }
+      sl::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) sl::mbar_arrive(&tempty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+      const int col = mt * BM + row;
+      __nv_bfloat16* dst = out + static_cast<size_t>(it.y) * out_ld + col;
+#pragma unroll
+      for (int n = 0; n < BN; ++n) {
+        if (n < it.z) {
+          float r;
+          if constexpr (GATED) {
+            // vLLM's torch-native chain: bf16 GEMM outputs, bf16 SiLU, bf16 mul
+            const float g = sl::bf16_round(v0[n]);
+            const float u = sl::bf16_round(v1[n]);
+            const float sg = sl::bf16_round(g / (1.0f + expf(-g)));
+            r = sg * u;
+          } else {
+            r = v0[n];
+          }
+          dst[static_cast<size_t>(n) * out_ld] = __float2bfloat16(r);
+        }
+      }
+    }
+  }
+  sl::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    sl::tc_fence_after();
+    sl::tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------- combine
+__global__ void __launch_bounds__(256) combine_kernel(
+    const int32_t* __restrict__ ws_hdr, const int32_t* __restrict__ pair_pos,
+    const float* __restrict__ tw, const __nv_bfloat16* __restrict__ Z, int T, int topk, int H,
+    int n_sh, float scale, __nv_bfloat16* __restrict__ out) {
+  const int t = blockIdx.y;
+  const int h0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (h0 >= H || ws_hdr[WS_STATUS] != SL_OK) return;
+  float r[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) r[i] = 0.f;
+  for (int j = 0; j < topk; ++j) {
+    const int pos = pair_pos[t * topk + j];
+    if (pos < 0) continue;
+    const float w = tw[t * topk + j];
+    const uint4 zv = *reinterpret_cast<const uint4*>(Z + static_cast<size_t>(pos) * H + h0);
+    const __nv_bfloat162* z2 = reinterpret_cast<const __nv_bfloat162*>(&zv);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(z2[i]);
+      r[2 * i] = __fadd_rn(r[2 * i], __fmul_rn(f.x, w));
+      r[2 * i + 1] = __fadd_rn(r[2 * i + 1], __fmul_rn(f.y, w));
+    }
+  }
+  float o[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float routed = sl::bf16_round(r[i]);
+    if (scale != 1.f) routed = sl::bf16_round(routed * scale);
+    o[i] = routed;
+  }
+  if (n_sh > 0) {
+    float s[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s[i] = 0.f;
+    for (int e = 0; e < n_sh; ++e) {
+      const int pos = ws_hdr[WS_SH_BASE + e] + t;
+      const uint4 zv = *reinterpret_cast<const uint4*>(Z + static_cast<size_t>(pos) * H + h0);
+      const __nv_bfloat162* z2 = reinterpret_cast<const __nv_bfloat162*>(&zv);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(z2[i]);
+        s[2 * i] += f.x;
+        s[2 * i + 1] += f.y;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = sl::bf16_round(s[i]) + o[i];
+  }
+  uint4 ov;
+  __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&ov);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) o2[i] = __floats2bfloat162_rn(o[2 * i], o[2 * i + 1]);
+  *reinterpret_cast<uint4*>(out + static_cast<size_t>(t) * H + h0) = ov;
+}
+
+// ------------------------------------------------------------------- host
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D bf16 view [rows, inner] (inner contiguous), box {64, box_rows}, 128B swizzle.
+bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn || (reinterpret_cast<uintptr_t>(base) & 15) || rows == 0) return false;
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {inner * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN, int STAGES, bool GATED>
+int launch_gemm(const CUtensorMap& tw, const CUtensorMap& twsh, const CUtensorMap& tb,
+                const int32_t* hdr, const int4* items, __nv_bfloat16* out, int S, int K,
+                int M_total, int out_ld, int32_t* status, int max_items, cudaStream_t st) {
+  using Cfg = GemmCfg<BN, STAGES, GATED>;
+  auto kern = moe_gemm_kernel<BN, STAGES, GATED>;
+  static int configured_dev = -1;
+  int dev = 0;
+  SL_CUDA_TRY(cudaGetDevice(&dev));
+  if (configured_dev != dev) {
+    SL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     Cfg::kSmemBytes));
+    configured_dev = dev;
+  }
+  const int max_tiles = max_items * (M_total / BM);
+  int grid = sl_device_sm_count();
+  if (grid <= 0) return SL_ERR_CUDA;
+  if (max_tiles < grid) grid = max_tiles > 0 ? max_tiles : 1;
+  kern<<<grid, kThreads, Cfg::kSmemBytes, st>>>(tw, twsh, tb, hdr, items, out, S, K, M_total,
+                                                out_ld, status);
+  SL_LAUNCH_CHECK();
+  return SL_OK;
+}
+
+}  // namespace
+
+extern "C" size_t sl_fused_experts_workspace_bytes(int T, int topk, int H, int I,
+                                                   int num_slots, int n_shared) {
+  if (T < 0 || topk <= 0 || H <= 0 || I <= 0 || num_slots <= 0 || n_shared < 0) return 0;
+  return ws_layout(T, topk, H, I, num_slots, n_shared, choose_bn(T)).total;
+}
+
+extern "C" int sl_fused_experts(const void* hidden, int T, int H, int I, const void* w13,
+                                const void* w2, int num_slots, int weight_dtype,
+                                const float* topk_weights, const int32_t* topk_ids, int topk,
+                                const int32_t* expert_map, int global_n,
+                                const void* shared_w13, const void* shared_w2, int n_shared,
+                                float routed_scaling_factor, void* out, void* workspace,
+                                size_t workspace_bytes, sl_stream_t stream) {
+  if (weight_dtype != 0) return SL_ERR_UNSUPPORTED;
+  if (T < 0 || topk <= 0 || num_slots <= 0 || n_shared < 0) return SL_ERR_INVALID;
+  if (H % BM || I % BM || H <= 0 || I <= 0) return SL_ERR_UNSUPPORTED;
+  if (num_slots + n_shared > kMaxCode || n_shared > kMaxShared) return SL_ERR_UNSUPPORTED;
+  if (T == 0) return SL_OK;
+  if (!hidden || !w13 || !w2 || !topk_weights || !topk_ids || !out || !workspace)
+    return SL_ERR_INVALID;
+  if (n_shared > 0 && (!shared_w13 || !shared_w2)) return SL_ERR_INVALID;
+  if (expert_map && global_n <= 0) return SL_ERR_INVALID;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255) ||
+      ((reinterpret_cast<uintptr_t>(hidden) | reinterpret_cast<uintptr_t>(out)) & 15))
+    return SL_ERR_INVALID;
+  const int BN = choose_bn(T);
+  const WsLayout L = ws_layout(T, topk, H, I, num_slots, n_shared, BN);
+  if (workspace_bytes < L.total) return SL_ERR_INVALID;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int32_t* hdr = reinterpret_cast<int32_t*>(ws);
+  int4* items = reinterpret_cast<int4*>(ws + L.items);
+  int32_t* pair_pos = reinterpret_cast<int32_t*>(ws + L.pair_pos);
+  __nv_bfloat16* X = reinterpret_cast<__nv_bfloat16*>(ws + L.x);
+  __nv_bfloat16* A = reinterpret_cast<__nv_bfloat16*>(ws + L.act);
+  __nv_bfloat16* Z = reinterpret_cast<__nv_bfloat16*>(ws + L.z);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+
+  CUtensorMap m_w13, m_w13sh, m_x, m_w2, m_w2sh, m_a;
+  const int nsh = n_shared > 0 ? n_shared : 0;
+  bool ok = make_map(&m_w13, w13, H, uint64_t(num_slots) * 2 * I, BM) &&
+            make_map(&m_w2, w2, I, uint64_t(num_slots) * H, BM) &&
+            make_map(&m_x, X, H, uint64_t(L.max_rows), BN) &&
+            make_map(&m_a, A, I, uint64_t(L.max_rows), BN);
+  if (ok && nsh) {
+    ok = make_map(&m_w13sh, shared_w13, H, uint64_t(nsh) * 2 * I, BM) &&
+         make_map(&m_w2sh, shared_w2, I, uint64_t(nsh) * H, BM);
+  } else {
+    m_w13sh = m_w13;
+    m_w2sh = m_w2;
+  }
+  if (!ok) return SL_ERR_INVALID;
+
+  align_kernel<<<1, 1024, 0, st>>>(topk_ids, T, topk, expert_map, global_n, num_slots, nsh, BN,
+                                   static_cast<const __nv_bfloat16*>(hidden), H, hdr, items,
+                                   pair_pos, X, L.max_items);
+  SL_LAUNCH_CHECK();
+  int rc;
+  rc = launch_gemm<16, 6, true>(m_w13, m_w13sh, m_x, hdr, items, A, num_slots, H, I, I, hdr,
+                                L.max_items, st);
+  if (rc != SL_OK) return rc;
+  rc = launch_gemm<16, 12, false>(m_w2, m_w2sh, m_a, hdr, items, Z, num_slots, I, H, H, hdr,
+                                  L.max_items, st);
+  if (rc != SL_OK) return rc;
+  dim3 cgrid((H / 8 + 255) / 256, T);
+  combine_kernel<<<cgrid, 256, 0, st>>>(hdr, pair_pos, topk_weights, Z, T, topk, H, nsh,
+                                        routed_scaling_factor, static_cast<__nv_bfloat16*>(out));
+  SL_LAUNCH_CHECK();
+  return SL_OK;
+}

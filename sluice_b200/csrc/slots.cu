@@ -1,0 +1,513 @@
+// Device-resident slot cache: state layout, planner (the router-split gap's
+// SLRU policy, no host round trip) and the GPU-initiated expert streamer.
+//
+// Reference: kfirtoledo/sluice src/sluice/offloader.py
+//   state      _ExpertLayerCache 121-169, _install_cache 936-1003
+//   gap        _router_split_gap 2362-2467 (FAST_HIT 2409-2424)
+//   policy     _touch 2009-2021, _coldest_protected 2023-2034 (LRU),
+//              _acquire_slot 2036-2074, _evict_to 2076-2081
+//   map        _write_map / _write_standing_map 2083-2123
+//   streaming  _stream_in 2709-2723
+//
+// Recency: every slot of the probation / protected segments carries a
+// 32-bit stamp from one per-layer clock; a segment's LRU order is ascending
+// stamp, and "move to end" is "take the next stamp". Stamps are renumbered
+// (order kept) before the clock could overflow.
+#include <stdlib.h>
+#include <string.h>
+
+#include "common.cuh"
+
+namespace {
+
+constexpr int kMaxSlots = 1024;
+constexpr int kMaxGlobal = 4096;
+constexpr uint32_t kClockRenorm = 0x7fff0000u;
+
+__host__ __device__ inline size_t round16(size_t v) { return (v + 15) & ~size_t(15); }
+
+__host__ __device__ inline void state_layout(int S, int G, int L, size_t* off) {
+  size_t o = 0;
+  off[0] = o; o += round16(16 * 4);           // header
+  off[1] = o; o += round16(8 * 8);            // counters
+  off[2] = o; o += round16(size_t(G) * 4);    // local_of
+  off[3] = o; o += round16(size_t(L) * 4);    // global_of_local
+  off[4] = o; o += round16(size_t(L) * 4);    // slot_of
+  off[5] = o; o += round16(size_t(S) * 4);    // expert_in_slot
+  off[6] = o; o += round16(size_t(S));        // seg
+  off[7] = o; o += round16(size_t(S) * 4);    // stamp
+  off[8] = o; o += round16(size_t(S) * 4);    // free_stack
+  off[9] = o; o += round16(size_t(S) * 4);    // fill_local
+  off[10] = o; o += round16(size_t(S) * 4);   // fill_slot
+  off[11] = o;
+}
+
+struct StateView {
+  int32_t* hdr;
+  unsigned long long* cnt;
+  int32_t* local_of;
+  int32_t* global_of_local;
+  int32_t* slot_of;
+  int32_t* eis;
+  uint8_t* seg;
+  uint32_t* stamp;
+  int32_t* free_stack;
+  int32_t* fill_local;
+  int32_t* fill_slot;
+};
+
+__device__ inline StateView view(uint8_t* base, int S, int G, int L) {
+  size_t off[12];
+  state_layout(S, G, L, off);
+  StateView v;
+  v.hdr = reinterpret_cast<int32_t*>(base + off[0]);
+  v.cnt = reinterpret_cast<unsigned long long*>(base + off[1]);
+  v.local_of = reinterpret_cast<int32_t*>(base + off[2]);
+  v.global_of_local = reinterpret_cast<int32_t*>(base + off[3]);
+  v.slot_of = reinterpret_cast<int32_t*>(base + off[4]);
+  v.eis = reinterpret_cast<int32_t*>(base + off[5]);
+  v.seg = base + off[6];
+  v.stamp = reinterpret_cast<uint32_t*>(base + off[7]);
+  v.free_stack = reinterpret_cast<int32_t*>(base + off[8]);
+  v.fill_local = reinterpret_cast<int32_t*>(base + off[9]);
+  v.fill_slot = reinterpret_cast<int32_t*>(base + off[10]);
+  return v;
+}
+
+struct PlanSmem {
+  uint32_t bitmap[kMaxGlobal / 32];
+  uint32_t word_base[kMaxGlobal / 32];
+  int32_t uniq[kMaxGlobal];
+  int32_t miss_loc[kMaxSlots + 1];
+  uint32_t stamp[kMaxSlots];
+  int32_t eis[kMaxSlots];
+  uint8_t seg[kMaxSlots];
+  uint8_t claimed[kMaxSlots];
+  int any_missing;
+  int n_uniq;
+};
+
+// Least-recently-used slot of segment `want` (optionally skipping claimed
+// slots), or -1. Whole warp; stamps of live slots are unique.
+__device__ int warp_lru(const PlanSmem& sm, int S, uint8_t want, bool skip_claimed) {
+  const int lane = threadIdx.x & 31;
+  uint32_t best = 0xffffffffu;
+  int bslot = -1;
+  for (int s = lane; s < S; s += 32) {
+    if (sm.seg[s] == want && !(skip_claimed && sm.claimed[s]) && sm.stamp[s] < best) {
+      best = sm.stamp[s];
+      bslot = s;
+    }
+  }
+  const uint32_t m = __reduce_min_sync(0xffffffffu, best);
+  const uint32_t bal = __ballot_sync(0xffffffffu, bslot >= 0 && best == m);
+  if (!bal) return -1;
+  return __shfl_sync(0xffffffffu, bslot, __ffs(bal) - 1);
+}
+
+__device__ inline StateView view_from_header(uint8_t* base, int& S, int& G, int& L) {
+  const int32_t* h = reinterpret_cast<const int32_t*>(base);
+  S = h[SL_HDR_NUM_SLOTS];
+  G = h[SL_HDR_GLOBAL_N];
+  L = h[SL_HDR_LOCAL_N];
+  return view(base, S, G, L);
+}
+
+__global__ void __launch_bounds__(256) plan_kernel(uint8_t* state,
+                                                   const int32_t* __restrict__ ids,
+                                                   int num_ids, int32_t* __restrict__ emap) {
+  __shared__ PlanSmem sm;
+  int S, G, L;
+  StateView st = view_from_header(state, S, G, L);
+  if (S <= 0 || S > kMaxSlots || G <= 0 || G > kMaxGlobal || L <= 0) return;
+  const int tid = threadIdx.x, nthr = blockDim.x;
+  const int nwords = (G + 31) >> 5;
+  for (int i = tid; i < nwords; i += nthr) sm.bitmap[i] = 0;
+  if (tid == 0) sm.any_missing = 0;
+  __syncthreads();
+  for (int p = tid; p < num_ids; p += nthr) {
+    const int g = ids[p];
+    if (g >= 0 && g < G) {
+      atomicOr(&sm.bitmap[g >> 5], 1u << (g & 31));
+      const int loc = st.local_of[g];
+      if (loc >= 0 && st.slot_of[loc] < 0) sm.any_missing = 1;
+    }
+  }
+  __syncthreads();
+  const int flags = st.hdr[SL_HDR_FLAGS];
+  const int standing = st.hdr[SL_HDR_MAP_IS_STANDING];
+  if (tid == 0) {
+    st.cnt[SL_CNT_GAPS] += 1;
+    st.hdr[SL_HDR_STATUS] = SL_OK;
+    st.hdr[SL_HDR_FILL_COUNT] = 0;
+    st.hdr[SL_HDR_LAST_MISSES] = 0;
+  }
+  if ((flags & SL_PLAN_FAST_HIT) && standing && !sm.any_missing) {
+    if (tid == 0) st.cnt[SL_CNT_FAST_HITS] += 1;
+    return;  // all-hit: no touches, no map write (offloader.py:2409-2424)
+  }
+  // sorted(set(ids)): expand the bitmap in ascending order
+  if (tid == 0) {
+    uint32_t run = 0;
+    for (int w = 0; w < nwords; ++w) {
+      sm.word_base[w] = run;
+      run += __popc(sm.bitmap[w]);
+    }
+    sm.n_uniq = static_cast<int>(run);
+  }
+  for (int s = tid; s < S; s += nthr) {
+    sm.seg[s] = st.seg[s];
+    sm.stamp[s] = st.stamp[s];
+    sm.eis[s] = st.eis[s];
+    sm.claimed[s] = 0;
+  }
+  __syncthreads();
+  for (int w = tid; w < nwords; w += nthr) {
+    uint32_t bits = sm.bitmap[w];
+    uint32_t pos = sm.word_base[w];
+    while (bits) {
+      const int b = __ffs(bits) - 1;
+      bits &= bits - 1;
+      sm.uniq[pos++] = (w << 5) + b;
+    }
+  }
+  // renumber stamps (order kept) before the clock can wrap
+  uint32_t clock0 = static_cast<uint32_t>(st.hdr[SL_HDR_CLOCK]);
+  if (clock0 > kClockRenorm) {
+    __syncthreads();
+    uint32_t newstamp[kMaxSlots / 256];
+    int nlive = 0;
+    for (int s = 0; s < S; ++s) nlive += (sm.seg[s] == SL_SEG_PROBATION || sm.seg[s] == SL_SEG_PROTECTED);
+    for (int k = 0, s = tid; s < S; s += nthr, ++k) {
+      uint32_t r = 0;
+      if (sm.seg[s] == SL_SEG_PROBATION || sm.seg[s] == SL_SEG_PROTECTED)
+        for (int q = 0; q < S; ++q)
+          r += (sm.seg[q] == SL_SEG_PROBATION || sm.seg[q] == SL_SEG_PROTECTED) &&
+               sm.stamp[q] < sm.stamp[s];
+      newstamp[k] = r + 1;
+    }
+    __syncthreads();
+    for (int k = 0, s = tid; s < S; s += nthr, ++k)
+      if (sm.seg[s] == SL_SEG_PROBATION || sm.seg[s] == SL_SEG_PROTECTED) sm.stamp[s] = newstamp[k];
+    clock0 = static_cast<uint32_t>(nlive);
+  }
+  __syncthreads();
+
+  if (tid < 32) {
+    const int lane = tid;
+    uint32_t clock = clock0;
+    int pcount = st.hdr[SL_HDR_PROTECTED_COUNT];
+    int free_top = st.hdr[SL_HDR_FREE_TOP];
+    const int cap = st.hdr[SL_HDR_PROTECTED_CAP];
+    const int U = sm.n_uniq;
+    int nmiss = 0;
+    unsigned long long hits = 0;
+    // touch hits, collect misses (offloader.py:2427-2441)
+    for (int i = 0; i < U; ++i) {
+      const int g = sm.uniq[i];
+      const int loc = st.local_of[g];
+      if (loc < 0) continue;  // owned by another rank
+      const int slot = st.slot_of[loc];
+      if (slot < 0) {
+        if (lane == 0 && nmiss <= kMaxSlots) sm.miss_loc[nmiss] = loc;
+        ++nmiss;
+        continue;
+      }
+      ++hits;
+      const uint8_t sg = sm.seg[slot];
+      if (lane == 0) sm.claimed[slot] = 1;
+      if (sg == SL_SEG_PROTECTED) {
+        ++clock;
+        if (lane == 0) sm.stamp[slot] = clock;
+      } else if (sg == SL_SEG_PROBATION) {
+        ++clock;
+        if (cap > 0) {
+          if (lane == 0) {
+            sm.seg[slot] = SL_SEG_PROTECTED;
+            sm.stamp[slot] = clock;
+          }
+          ++pcount;
+          while (pcount > cap) {
+            __syncwarp();
+            const int v = warp_lru(sm, S, SL_SEG_PROTECTED, false);
+            ++clock;
+            if (lane == 0) {
+              sm.seg[v] = SL_SEG_PROBATION;
+              sm.stamp[v] = clock;
+            }
+            --pcount;
+          }
+        } else if (lane == 0) {
+          sm.stamp[slot] = clock;
+        }
+      }
+      __syncwarp();
+    }
+    // acquire a slot per miss, ascending id order (offloader.py:2442-2465)
+    int fc = 0;
+    bool overflow = false;
+    const int nm = min(nmiss, kMaxSlots + 1);
+    for (int i = 0; i < nm; ++i) {
+      const int loc = sm.miss_loc[i];
+      int slot = -1;
+      if (free_top > 0) {
+        slot = st.free_stack[--free_top];
+      } else {
+        slot = warp_lru(sm, S, SL_SEG_PROBATION, true);
+        if (slot < 0) {
+          slot = warp_lru(sm, S, SL_SEG_PROTECTED, true);
+          if (slot >= 0) --pcount;
+        }
+      }
+      if (slot < 0) {
+        overflow = true;
+        break;
+      }
+      ++clock;
+      if (lane == 0) {
+        const int old = sm.eis[slot];
+        if (old >= 0) st.slot_of[old] = -1;
+        sm.eis[slot] = loc;
+        st.slot_of[loc] = slot;
+        sm.seg[slot] = SL_SEG_PROBATION;
+        sm.stamp[slot] = clock;
+        sm.claimed[slot] = 1;
+        st.fill_local[fc] = loc;
+        st.fill_slot[fc] = slot;
+      }
+      ++fc;
+      __syncwarp();
+    }
+    if (lane == 0) {
+      st.hdr[SL_HDR_FREE_TOP] = free_top;
+      st.hdr[SL_HDR_PROTECTED_COUNT] = pcount;
+      st.hdr[SL_HDR_CLOCK] = static_cast<int32_t>(clock);
+      st.hdr[SL_HDR_FILL_COUNT] = fc;
+      st.hdr[SL_HDR_STATUS] = overflow ? SL_ERR_OVERFLOW : SL_OK;
+      st.hdr[SL_HDR_LAST_MISSES] = overflow ? 0 : nmiss;
+      st.cnt[SL_CNT_HITS] += hits;
+      st.cnt[SL_CNT_FILLS] += fc;
+      if (overflow) st.cnt[SL_CNT_OVERFLOWS] += 1;
+      else st.cnt[SL_CNT_MISSES] += nmiss;
+      sm.any_missing = overflow ? -1 : nmiss;  // reuse: map-write decision
+    }
+  }
+  __syncthreads();
+  const int decision = sm.any_missing;
+  for (int s = tid; s < S; s += nthr) {
+    st.seg[s] = sm.seg[s];
+    st.stamp[s] = sm.stamp[s];
+    st.eis[s] = sm.eis[s];
+  }
+  if (decision >= 0 && (decision > 0 || !standing)) {
+    // standing map: every resident expert -> its slot (offloader.py:2112-2123)
+    for (int g = tid; g < G; g += nthr) emap[g] = -1;
+    __syncthreads();
+    for (int s = tid; s < S; s += nthr) {
+      const int loc = sm.eis[s];
+      if (loc >= 0) emap[st.global_of_local[loc]] = s;
+    }
+    if (tid == 0) st.hdr[SL_HDR_MAP_IS_STANDING] = 1;
+  }
+}
+
+// ---------------------------------------------------------------- streamer
+constexpr int kMaxParams = 8;
+constexpr int kChunkVec = 4096;  // 64 KiB per work unit
+constexpr int kStreamThreads = 256;
+constexpr int kStreamUnroll = 8;
+
+struct StreamArgs {
+  int n;
+  const uint4* src[kMaxParams];
+  uint4* dst[kMaxParams];
+  unsigned long long vec[kMaxParams];     // 16-byte vectors per expert
+  unsigned long long chunks[kMaxParams];  // work units per expert
+};
+
+__device__ __forceinline__ uint4 ld_host_nc(const uint4* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__global__ void __launch_bounds__(kStreamThreads) stream_kernel(const uint8_t* state,
+                                                                StreamArgs a) {
+  int S, G, L;
+  const StateView st = view_from_header(const_cast<uint8_t*>(state), S, G, L);
+  const int fc = st.hdr[SL_HDR_FILL_COUNT];
+  if (fc <= 0) return;
+  unsigned long long per_fill = 0;
+  for (int p = 0; p < a.n; ++p) per_fill += a.chunks[p];
+  const unsigned long long total = per_fill * static_cast<unsigned long long>(fc);
+  for (unsigned long long u = blockIdx.x; u < total; u += gridDim.x) {
+    const int f = static_cast<int>(u / per_fill);
+    unsigned long long r = u - static_cast<unsigned long long>(f) * per_fill;
+    int p = 0;
+    while (r >= a.chunks[p]) {
+      r -= a.chunks[p];
+      ++p;
+    }
+    const unsigned long long v0 = r * kChunkVec;
+    const unsigned long long nvec = min(static_cast<unsigned long long>(kChunkVec), a.vec[p] - v0);
+    const uint4* src = a.src[p] + static_cast<unsigned long long>(st.fill_local[f]) * a.vec[p] + v0;
+    uint4* dst = a.dst[p] + static_cast<unsigned long long>(st.fill_slot[f]) * a.vec[p] + v0;
+    for (unsigned long long base = 0; base < nvec; base += kStreamThreads * kStreamUnroll) {
+      uint4 v[kStreamUnroll];
+#pragma unroll
+      for (int k = 0; k < kStreamUnroll; ++k) {
+        const unsigned long long i = base + k * kStreamThreads + threadIdx.x;
+        if (i < nvec) v[k] = ld_host_nc(src + i);
+      }
+#pragma unroll
+      for (int k = 0; k < kStreamUnroll; ++k) {
+        const unsigned long long i = base + k * kStreamThreads + threadIdx.x;
+        if (i < nvec) dst[i] = v[k];
+      }
+    }
+  }
+}
+
+int g_default_stream_ctas = 0;
+
+}  // namespace
+
+extern "C" size_t sl_slot_state_bytes(int num_slots, int global_n, int local_n) {
+  if (num_slots <= 0 || global_n <= 0 || local_n <= 0) return 0;
+  size_t off[12];
+  state_layout(num_slots, global_n, local_n, off);
+  return off[11];
+}
+
+extern "C" int sl_slot_state_offsets(int num_slots, int global_n, int local_n,
+                                     size_t* offsets) {
+  if (num_slots <= 0 || global_n <= 0 || local_n <= 0 || !offsets) return SL_ERR_INVALID;
+  size_t off[12];
+  state_layout(num_slots, global_n, local_n, off);
+  for (int i = 0; i <= SL_STATE_NFIELDS; ++i) offsets[i] = off[i];
+  return SL_OK;
+}
+
+extern "C" int sl_slot_state_init(void* state, int num_slots, int global_n, int local_n,
+                                  int protected_cap, int flags, const int32_t* local_of,
+                                  const int32_t* expert_in_slot, const uint8_t* seg,
+                                  const int32_t* free_stack, int n_free,
+                                  sl_stream_t stream) {
+  const int S = num_slots, G = global_n, L = local_n;
+  if (!state || S <= 0 || G <= 0 || L <= 0 || S > kMaxSlots || G > kMaxGlobal)
+    return SL_ERR_INVALID;
+  if (!local_of || !expert_in_slot || !seg || n_free < 0 || n_free > S ||
+      (n_free > 0 && !free_stack) || protected_cap < 0 || protected_cap > S)
+    return SL_ERR_INVALID;
+  size_t off[12];
+  state_layout(S, G, L, off);
+  uint8_t* img = static_cast<uint8_t*>(calloc(1, off[11]));
+  if (!img) return SL_ERR_INVALID;
+  int32_t* hdr = reinterpret_cast<int32_t*>(img + off[0]);
+  int32_t* lof = reinterpret_cast<int32_t*>(img + off[2]);
+  int32_t* gol = reinterpret_cast<int32_t*>(img + off[3]);
+  int32_t* sof = reinterpret_cast<int32_t*>(img + off[4]);
+  int32_t* eis = reinterpret_cast<int32_t*>(img + off[5]);
+  uint8_t* sg = img + off[6];
+  uint32_t* stamp = reinterpret_cast<uint32_t*>(img + off[7]);
+  int32_t* fs = reinterpret_cast<int32_t*>(img + off[8]);
+  int rc = SL_OK;
+  for (int l = 0; l < L; ++l) gol[l] = -1, sof[l] = -1;
+  for (int g = 0; g < G; ++g) {
+    lof[g] = local_of[g];
+    if (lof[g] >= L) rc = SL_ERR_INVALID;
+    else if (lof[g] >= 0) gol[lof[g]] = g;
+  }
+  int pcount = 0;
+  uint32_t clock = 0;
+  for (int s = 0; s < S && rc == SL_OK; ++s) {
+    eis[s] = expert_in_slot[s];
+    sg[s] = seg[s];
+    if (sg[s] > SL_SEG_PINNED || eis[s] >= L) rc = SL_ERR_INVALID;
+    else if (eis[s] >= 0) {
+      if (sg[s] == SL_SEG_FREE || sof[eis[s]] >= 0) rc = SL_ERR_INVALID;
+      else sof[eis[s]] = s;
+    } else if (sg[s] != SL_SEG_FREE) {
+      rc = SL_ERR_INVALID;
+    }
+    if (sg[s] == SL_SEG_PROBATION || sg[s] == SL_SEG_PROTECTED) stamp[s] = ++clock;
+    if (sg[s] == SL_SEG_PROTECTED) ++pcount;
+  }
+  for (int i = 0; i < n_free && rc == SL_OK; ++i) {
+    fs[i] = free_stack[i];
+    if (fs[i] < 0 || fs[i] >= S || seg[fs[i]] != SL_SEG_FREE) rc = SL_ERR_INVALID;
+  }
+  if (rc != SL_OK) {
+    free(img);
+    return rc;
+  }
+  hdr[SL_HDR_NUM_SLOTS] = S;
+  hdr[SL_HDR_GLOBAL_N] = G;
+  hdr[SL_HDR_LOCAL_N] = L;
+  hdr[SL_HDR_PROTECTED_CAP] = protected_cap;
+  hdr[SL_HDR_FLAGS] = flags;
+  hdr[SL_HDR_MAP_IS_STANDING] = 0;
+  hdr[SL_HDR_FREE_TOP] = n_free;
+  hdr[SL_HDR_PROTECTED_COUNT] = pcount;
+  hdr[SL_HDR_CLOCK] = static_cast<int32_t>(clock);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // pageable source: the copy is staged before this call returns
+  cudaError_t e = cudaMemcpyAsync(state, img, off[11], cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  free(img);
+  return e == cudaSuccess ? SL_OK : SL_ERR_CUDA;
+}
+
+extern "C" int sl_plan_slots(void* state, const int32_t* topk_ids, int num_ids,
+                             int32_t* expert_map, sl_stream_t stream) {
+  if (!state || !expert_map || num_ids < 0 || (num_ids > 0 && !topk_ids)) return SL_ERR_INVALID;
+  plan_kernel<<<1, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<uint8_t*>(state), topk_ids, num_ids, expert_map);
+  SL_LAUNCH_CHECK();
+  return SL_OK;
+}
+
+extern "C" int sl_stream_experts(const void* state, int num_params,
+                                 const void* const* host_src, void* const* slot_dst,
+                                 const size_t* bytes_per_expert, int num_ctas,
+                                 sl_stream_t stream) {
+  if (!state || num_params <= 0 || num_params > kMaxParams || !host_src || !slot_dst ||
+      !bytes_per_expert)
+    return SL_ERR_INVALID;
+  StreamArgs a;
+  memset(&a, 0, sizeof(a));
+  a.n = num_params;
+  for (int p = 0; p < num_params; ++p) {
+    const size_t b = bytes_per_expert[p];
+    if (b == 0 || (b & 15) || !host_src[p] || !slot_dst[p] ||
+        ((reinterpret_cast<uintptr_t>(host_src[p]) | reinterpret_cast<uintptr_t>(slot_dst[p])) & 15))
+      return SL_ERR_INVALID;
+    a.src[p] = static_cast<const uint4*>(host_src[p]);
+    a.dst[p] = static_cast<uint4*>(slot_dst[p]);
+    a.vec[p] = b / 16;
+    a.chunks[p] = (a.vec[p] + kChunkVec - 1) / kChunkVec;
+  }
+  if (num_ctas <= 0) {
+    if (g_default_stream_ctas <= 0) g_default_stream_ctas = 64;
+    num_ctas = g_default_stream_ctas;
+  }
+  stream_kernel<<<num_ctas, kStreamThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(state), a);
+  SL_LAUNCH_CHECK();
+  return SL_OK;
+}
+
+extern "C" int sl_host_alloc_mapped(size_t bytes, void** host_ptr) {
+  if (!host_ptr || bytes == 0) return SL_ERR_INVALID;
+  *host_ptr = nullptr;
+  SL_CUDA_TRY(cudaHostAlloc(host_ptr, bytes, cudaHostAllocMapped | cudaHostAllocPortable));
+  return SL_OK;
+}
+
+extern "C" int sl_host_free(void* host_ptr) {
+  if (!host_ptr) return SL_OK;
+  SL_CUDA_TRY(cudaFreeHost(host_ptr));
+  return SL_OK;
+}

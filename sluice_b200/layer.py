@@ -1,0 +1,121 @@
+"""One MoE layer on the router-split path, and a decode stack of such layers.
+
+``SluiceMoELayer.forward`` is the router-split entry of the reference
+(``offloader.py:2578-2603``) plus vLLM's runner tail
+(``runner/moe_runner.py:663-680``), with every box on sm_100a kernels:
+
+    gate + select_experts      -> sl_route        (router kernels)
+    sluice_stream_gap          -> SlotCache.gap   (planner + streamer, no sync)
+    fused_experts + shared MLP -> sl_fused_experts (tcgen05 GEMMs + combine)
+      + routed scaling + add
+
+``MoEDecodeStack`` chains layers with a residual (``h = h + moe(h)``) to run
+the decode step of a MoE decoder's expert layers over the slot caches; the
+step is capturable in one CUDA graph because no kernel waits on the host.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import ops, synth
+from .configs import MoEConfig
+from .offloader import ExpertStreamOffloader, SlotCache
+
+
+class SluiceMoELayer:
+    def __init__(self, cfg: MoEConfig, router: ops.Router, cache: SlotCache,
+                 shared_w13: torch.Tensor | None, shared_w2: torch.Tensor | None,
+                 layer_idx: int = 0):
+        self.cfg = cfg
+        self.router = router
+        self.cache = cache
+        self.shared_w13 = shared_w13
+        self.shared_w2 = shared_w2
+        self.layer_idx = layer_idx
+        self.last_ids = None
+        self.last_logits = None
+
+    def forward(self, hs: torch.Tensor) -> torch.Tensor:
+        tw, ti, logits = self.router.route(hs)
+        self.last_ids, self.last_logits = ti, logits
+        self.cache.gap(ti)
+        return ops.fused_experts(hs, self.cache.w13, self.cache.w2, tw, ti,
+                                 global_num_experts=self.cfg.num_experts,
+                                 expert_map=self.cache.expert_map,
+                                 shared_w13=self.shared_w13, shared_w2=self.shared_w2,
+                                 routed_scaling_factor=self.cfg.routed_scaling_factor)
+
+    __call__ = forward
+
+
+class MoEDecodeStack:
+    """The MoE layers of a decoder, each behind its own slot cache."""
+
+    def __init__(self, cfg: MoEConfig, slots: int, seed: int = 0, device="cuda",
+                 protect_frac: float | None = None, fast_hit: bool = True,
+                 num_layers: int | None = None):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.offloader = ExpertStreamOffloader(slots, protect_frac=protect_frac,
+                                               fast_hit=fast_hit)
+        self.layers: list[SluiceMoELayer] = []
+        n = cfg.num_moe_layers if num_layers is None else num_layers
+        for li in range(n):
+            w13, w2 = synth.layer_weights(cfg, li, seed, device=self.device)
+            cache = self.offloader.install_layer(w13, w2, device=self.device)
+            del w13, w2
+            gw, lb, sb = synth.gate_params(cfg, li, seed, device=self.device)
+            router = ops.Router(cfg.routing, gw, lb, sb)
+            sh13, sh2 = synth.shared_weights(cfg, li, seed, device=self.device)
+            self.layers.append(SluiceMoELayer(cfg, router, cache, sh13, sh2, li))
+        torch.cuda.synchronize(self.device)
+        self.graph = None
+        self._static_in = None
+        self._static_out = None
+
+    def step(self, x: torch.Tensor) -> torch.Tensor:
+        h = x
+        for layer in self.layers:
+            h = h + layer(h)
+        return h
+
+    # -- CUDA graph of one decode step ------------------------------------
+    def capture(self, tokens: int) -> None:
+        self._static_in = torch.zeros(tokens, self.cfg.hidden, dtype=torch.bfloat16,
+                                      device=self.device)
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            self.step(self._static_in)  # allocator warm-up outside capture
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._static_out = self.step(self._static_in)
+        self.graph = g
+
+    def replay(self, x: torch.Tensor | None = None) -> torch.Tensor:
+        if x is not None:
+            self._static_in.copy_(x, non_blocking=True)
+        self.graph.replay()
+        return self._static_out
+
+    def decode_step(self, x_host: torch.Tensor, out_host: torch.Tensor) -> torch.Tensor:
+        """Public end-to-end call: host tokens in, host hidden states out."""
+        self._static_in.copy_(x_host, non_blocking=True)
+        self.graph.replay()
+        out_host.copy_(self._static_out, non_blocking=True)
+        return out_host
+
+    def check(self) -> None:
+        for layer in self.layers:
+            layer.cache.check()
+
+    def stats(self) -> dict:
+        tot = {}
+        for layer in self.layers:
+            for k, v in layer.cache.stats().items():
+                if isinstance(v, bool):
+                    continue
+                tot[k] = tot.get(k, 0) + v
+        return tot

@@ -1,0 +1,306 @@
+"""Per-layer expert slot cache with a device-resident SLRU policy.
+
+Mirrors the reference's offloader state and lifecycle for the router-split
+path (kfirtoledo/sluice ``src/sluice/offloader.py``):
+
+* ``ExpertStreamOffloader(expert_cache_slots)`` — ``SLUICE_SLOTS`` slots per
+  layer (``plugin.py:29-38``), ``SLUICE_PROTECT_FRAC`` (default 0.5, clamped to
+  [0, 0.9]: ``offloader.py:236-241``), FAST_HIT (``SLUICE_RS_FAST_HIT``, on by
+  default here as in the shipped configuration, ``README.md:90``).
+* ``install_layer`` — ``_install_cache`` (895-1044): ``num_slots =
+  min(slots, local_n)``, the protected cap, slot buffers ``[num_slots, ...]``
+  per expert parameter, the host store of every local expert, the int32 expert
+  map (``-1`` = not resident); full residency (``static_full``) installs the
+  identity map and never streams; pins follow ``_apply_pins`` (1046-1083).
+* ``SlotCache.gap(topk_ids)`` — the body of ``_router_split_gap``
+  (2362-2467) on the device: the planner kernel updates the SLRU state and the
+  standing expert map in place, the streamer kernel copies the misses from
+  the mapped host store into their slots. No device-to-host synchronisation.
+
+Buffers are allocated once and never reallocated (captured CUDA graphs bake
+pointers); a gap rewrites their contents only.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import weakref
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import CNT, HDR, SEG_FREE, SEG_PINNED, check, lib, ptr
+
+PROTECT_FRAC_ENV = "SLUICE_PROTECT_FRAC"
+SLOTS_ENV = "SLUICE_SLOTS"
+FAST_HIT_ENV = "SLUICE_RS_FAST_HIT"
+
+
+def protected_cap_for(num_slots: int, protect_frac: float) -> int:
+    """``min(int(slots * frac), slots - 1)`` with frac clamped to [0, 0.9]."""
+    frac = min(max(float(protect_frac), 0.0), 0.9)
+    return max(min(int(num_slots * frac), num_slots - 1), 0)
+
+
+@dataclass
+class InitialSlotState:
+    """Host-computed starting residency of one layer's slots."""
+
+    num_slots: int
+    protected_cap: int
+    expert_in_slot: list      # local id per slot, -1 free
+    seg: list                 # SEG_* per slot
+    free_stack: list          # bottom first; the next slot taken is the last
+    fills: list               # (local, slot) copies to make at install
+
+
+def initial_slot_state(num_slots: int, local_of: list, local_n: int, protect_frac: float,
+                       pins: list | None = None,
+                       prefill_resident: bool = False) -> InitialSlotState:
+    """Starting state per ``_install_cache`` (936-1003) and ``_apply_pins``
+    (1046-1083): free list ``[S-1, ..., 0]`` popped from the end; pins take
+    free slots, sit outside both SLRU segments and reduce the protected cap."""
+    S = num_slots
+    cap = protected_cap_for(S, protect_frac)
+    eis = [-1] * S
+    seg = [SEG_FREE] * S
+    free = list(range(S - 1, -1, -1))
+    fills = []
+    if prefill_resident:
+        for loc in range(local_n):
+            eis[loc] = loc
+            seg[loc] = SEG_PINNED
+            fills.append((loc, loc))
+        free = list(range(S - 1, local_n - 1, -1))
+    if pins:
+        resident = set(v for v in eis if v >= 0)
+        n = 0
+        for g in pins:
+            if n >= cap:
+                break
+            if not (0 <= g < len(local_of)):
+                continue
+            loc = local_of[g]
+            if loc < 0 or loc in resident or not free:
+                continue
+            slot = free.pop()
+            eis[slot] = loc
+            seg[slot] = SEG_PINNED
+            resident.add(loc)
+            fills.append((loc, slot))
+            n += 1
+        cap -= n
+    return InitialSlotState(S, cap, eis, seg, free, fills)
+
+
+class HostStore:
+    """Page-locked, device-mapped host buffer (``cudaHostAlloc`` Mapped|Portable)."""
+
+    def __init__(self, nbytes: int):
+        p = ctypes.c_void_p()
+        check(lib().sl_host_alloc_mapped(nbytes, ctypes.byref(p)), "sl_host_alloc_mapped")
+        self.ptr = p.value
+        self.nbytes = nbytes
+        buf = (ctypes.c_uint8 * nbytes).from_address(self.ptr)
+        self.bytes = torch.frombuffer(buf, dtype=torch.uint8)
+        self._fin = weakref.finalize(self, lib().sl_host_free, ctypes.c_void_p(self.ptr))
+
+    def view(self, dtype, shape) -> torch.Tensor:
+        return self.bytes.view(dtype).view(shape)
+
+
+class SlotCache:
+    """One MoE layer's slots, host store, expert map and device SLRU state."""
+
+    PARAMS = ("w13", "w2")
+
+    def __init__(self, num_slots: int, local_n: int, global_n: int, local_of: list,
+                 protected_cap: int, static_full: bool, device: torch.device,
+                 gpu_cache: dict, cpu_store: dict, expert_map: torch.Tensor,
+                 state: torch.Tensor | None, bytes_per_expert: int):
+        self.num_slots = num_slots
+        self.local_n = local_n
+        self.global_n = global_n
+        self.local_of = local_of
+        self.protected_cap = protected_cap
+        self.static_full = static_full
+        self.device = device
+        self.gpu_cache = gpu_cache
+        self.cpu_store = cpu_store
+        self.expert_map = expert_map
+        self.state = state
+        self.bytes_per_expert = bytes_per_expert
+        self._stream_args = None
+        if state is not None:
+            offs = (ctypes.c_size_t * (_lib.STATE_NFIELDS + 1))()
+            check(lib().sl_slot_state_offsets(num_slots, global_n, local_n, offs),
+                  "sl_slot_state_offsets")
+            self.offsets = list(offs)
+            n = len(self.PARAMS)
+            src = (ctypes.c_void_p * n)(*[cpu_store[k].data_ptr() for k in self.PARAMS])
+            dst = (ctypes.c_void_p * n)(*[gpu_cache[k].data_ptr() for k in self.PARAMS])
+            nb = (ctypes.c_size_t * n)(*[cpu_store[k][0].numel() * cpu_store[k].element_size()
+                                         for k in self.PARAMS])
+            self._stream_args = (n, src, dst, nb)
+
+    @property
+    def w13(self) -> torch.Tensor:
+        return self.gpu_cache["w13"]
+
+    @property
+    def w2(self) -> torch.Tensor:
+        return self.gpu_cache["w2"]
+
+    # -- the gap ---------------------------------------------------------
+    def gap(self, topk_ids: torch.Tensor, stream_ctas: int = 0) -> None:
+        """Plan slots for this step's ids and stream the misses (async)."""
+        if self.static_full:
+            return
+        ids = topk_ids if topk_ids.dtype == torch.int32 and topk_ids.is_contiguous() \
+            else topk_ids.contiguous().to(torch.int32)
+        s = torch.cuda.current_stream().cuda_stream
+        L = lib()
+        check(L.sl_plan_slots(ptr(self.state), ptr(ids), ids.numel(), ptr(self.expert_map), s),
+              "sl_plan_slots")
+        n, src, dst, nb = self._stream_args
+        check(L.sl_stream_experts(ptr(self.state), n, src, dst, nb, int(stream_ctas), s),
+              "sl_stream_experts")
+
+    # -- host-side views (synchronise) ----------------------------------------
+    def _field(self, i: int, dtype, count: int) -> np.ndarray:
+        b = self.state[self.offsets[i]: self.offsets[i] + count * np.dtype(dtype).itemsize]
+        return b.cpu().numpy().view(dtype)
+
+    def header(self) -> dict:
+        h = self._field(0, np.int32, 16)
+        return {k: int(h[v]) for k, v in HDR.items()}
+
+    def counters(self) -> dict:
+        c = self._field(1, np.uint64, 8)
+        return {k: int(c[v]) for k, v in CNT.items()}
+
+    def check(self) -> None:
+        """Raise the reference's overflow error if the last gap overflowed."""
+        if self.state is None:
+            return
+        st = self.header()["status"]
+        if st != _lib.SL_OK:
+            raise _lib.SluiceError("sluice_stream_gap", st)
+
+    def snapshot(self) -> dict:
+        """Expert map, slot owners, SLRU order and counters (for tests)."""
+        S = self.num_slots
+        eis = self._field(5, np.int32, S).tolist()
+        seg = self._field(6, np.uint8, S).tolist()
+        stamp = self._field(7, np.uint32, S).tolist()
+        order = lambda v: sorted((s for s in range(S) if seg[s] == v), key=lambda s: stamp[s])
+        return {
+            "expert_map": self.expert_map.cpu().tolist(),
+            "expert_in_slot": eis,
+            "protected": order(_lib.SEG_PROTECTED),
+            "probation": order(_lib.SEG_PROBATION),
+            "header": self.header(),
+            "counters": self.counters(),
+            "fills": list(zip(self._field(9, np.int32, S).tolist(),
+                              self._field(10, np.int32, S).tolist()))[: self.header()["fill_count"]],
+        }
+
+    def stats(self) -> dict:
+        if self.state is None:
+            return {"static_full": True}
+        c = self.counters()
+        c["bytes_streamed"] = c["fills"] * self.bytes_per_expert
+        return c
+
+
+class ExpertStreamOffloader:
+    """Installs slot caches for MoE layers (``SLUICE_SLOTS`` per layer)."""
+
+    def __init__(self, expert_cache_slots: int, protect_frac: float | None = None,
+                 fast_hit: bool | None = None, no_static_full: bool = False):
+        if expert_cache_slots <= 0:
+            raise ValueError("expert_cache_slots must be positive")
+        self.expert_cache_slots = int(expert_cache_slots)
+        if protect_frac is None:
+            try:
+                protect_frac = float(os.environ.get(PROTECT_FRAC_ENV, "0.5"))
+            except ValueError:
+                protect_frac = 0.5
+        self.protect_frac = min(max(protect_frac, 0.0), 0.9)
+        if fast_hit is None:
+            fast_hit = os.environ.get(FAST_HIT_ENV, "1") != "0"
+        self.fast_hit = bool(fast_hit)
+        self.no_static_full = bool(no_static_full)
+        self.caches: list[SlotCache] = []
+
+    @classmethod
+    def from_env(cls) -> "ExpertStreamOffloader | None":
+        raw = os.environ.get(SLOTS_ENV)
+        if not raw:
+            return None
+        return cls(int(raw))
+
+    def install_layer(self, w13: torch.Tensor, w2: torch.Tensor, global_n: int | None = None,
+                      local_of: list | None = None, pins: list | None = None,
+                      device: torch.device | str = "cuda") -> SlotCache:
+        """Install one layer from its local experts ``w13`` [L, 2I, H], ``w2``
+        [L, H, I] (CPU or CUDA tensors; copied into the host store)."""
+        device = torch.device(device)
+        local_n = w13.shape[0]
+        if global_n is None:
+            global_n = local_n
+        if local_of is None:
+            if global_n != local_n:
+                raise ValueError("local_of is required when global_n != local_n")
+            local_of = list(range(global_n))
+        local_of = [int(v) for v in local_of]
+        S = min(self.expert_cache_slots, local_n)
+        resident_all = S >= local_n
+        static_full = resident_all and not self.no_static_full
+        params = {"w13": w13, "w2": w2}
+        gpu_cache, cpu_store = {}, {}
+        bpe = 0
+        for name, p in params.items():
+            gpu_cache[name] = torch.empty((S, *p.shape[1:]), dtype=p.dtype, device=device)
+            bpe += p[0].numel() * p.element_size()
+            if static_full:
+                gpu_cache[name].copy_(p)
+            else:
+                store = HostStore(p.numel() * p.element_size())
+                t = store.view(p.dtype, p.shape)
+                t.copy_(p)
+                t._sluice_store = store  # keep the allocation alive with the view
+                cpu_store[name] = t
+        emap = torch.full((global_n,), -1, dtype=torch.int32, device=device)
+        if static_full:
+            lo = torch.tensor(local_of, dtype=torch.int32)
+            emap.copy_(torch.where(lo >= 0, lo, torch.full_like(lo, -1)))
+            cache = SlotCache(S, local_n, global_n, local_of, 0, True, device, gpu_cache,
+                              cpu_store, emap, None, bpe)
+            self.caches.append(cache)
+            return cache
+        init = initial_slot_state(S, local_of, local_n, self.protect_frac, pins,
+                                  prefill_resident=resident_all)
+        nbytes = lib().sl_slot_state_bytes(S, global_n, local_n)
+        state = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+        arr = lambda v, t: (t * len(v))(*v)
+        rc = lib().sl_slot_state_init(
+            ptr(state), S, global_n, local_n, init.protected_cap,
+            _lib.PLAN_FAST_HIT if self.fast_hit else 0,
+            arr(local_of, ctypes.c_int32), arr(init.expert_in_slot, ctypes.c_int32),
+            arr(init.seg, ctypes.c_uint8), arr(init.free_stack or [0], ctypes.c_int32),
+            len(init.free_stack), torch.cuda.current_stream(device).cuda_stream)
+        check(rc, "sl_slot_state_init")
+        for loc, slot in init.fills:
+            for name in params:
+                gpu_cache[name][slot].copy_(cpu_store[name][loc])
+        cache = SlotCache(S, local_n, global_n, local_of, init.protected_cap, False, device,
+                          gpu_cache, cpu_store, emap, state, bpe)
+        self.caches.append(cache)
+        return cache
+
+    def get_stats(self) -> list[dict]:
+        return [c.stats() for c in self.caches]

@@ -1,0 +1,197 @@
+"""The reference's operator surface, backed by the sm_100a library.
+
+* ``Router.select_experts(hidden_states, router_logits, *, input_ids=None)``
+  mirrors vLLM's ``BaseRouter.select_experts`` (``router/base_router.py``
+  250-298) as called at ``offloader.py:2583-2585``; ``Router.gate`` is the
+  bf16 gate linear (``offloader.py:2582``) fused with the selection.
+* ``sluice_stream_gap(hidden_states, topk_ids, layer_idx)`` mirrors the
+  custom op ``vllm::sluice_stream_gap`` (``offloader.py:2311-2331``): it runs
+  the slot planner and the expert streamer of the registered layer and
+  returns ``hidden_states.clone()`` (``mutates_args=[]``; the fake returns
+  ``empty_like``). Registered as ``torch.ops.sluice.sluice_stream_gap``.
+* ``fused_experts(hidden_states, w1, w2, topk_weights, topk_ids,
+  activation="silu", global_num_experts=-1, expert_map=None, ...)`` mirrors
+  ``torch.ops.vllm.fused_experts`` as called at ``offloader.py:2590-2599``,
+  with the shared experts and routed scaling fused into its combine.
+  Registered as ``torch.ops.sluice.fused_experts``.
+
+All calls enqueue on the current CUDA stream and never synchronise, so they
+can be captured in a CUDA graph.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import check, lib, ptr
+from .configs import RoutingConfig
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("sluice_b200 ops take CUDA tensors")
+
+
+class Router:
+    """Gate linear + expert selection for one MoE layer."""
+
+    def __init__(self, routing: RoutingConfig, gate_weight: torch.Tensor | None = None,
+                 logit_bias: torch.Tensor | None = None,
+                 score_bias: torch.Tensor | None = None):
+        self.routing = routing
+        self.gate_weight = gate_weight
+        self.logit_bias = logit_bias
+        self.score_bias = score_bias
+        if routing.has_score_bias and score_bias is None:
+            raise ValueError("this routing mode needs e_score_correction_bias")
+
+    @property
+    def num_experts(self) -> int:
+        return self.gate_weight.shape[0]
+
+    def _groups(self):
+        r = self.routing
+        if r.use_grouped_topk:
+            return r.num_expert_group, r.topk_group
+        return 1, 1
+
+    def select_experts(self, hidden_states: torch.Tensor, router_logits: torch.Tensor, *,
+                       input_ids: torch.Tensor | None = None):
+        """(topk_weights fp32 [T,k], topk_ids int32 [T,k]) from bf16 logits."""
+        _need_cuda(router_logits)
+        r = self.routing
+        T, E = router_logits.shape
+        lg = router_logits.contiguous()
+        if lg.dtype != torch.bfloat16:
+            lg = lg.to(torch.bfloat16)
+        w = torch.empty(T, r.topk, dtype=torch.float32, device=lg.device)
+        ids = torch.empty(T, r.topk, dtype=torch.int32, device=lg.device)
+        ng, tg = self._groups()
+        check(lib().sl_select_experts(ptr(lg), T, E, r.topk, r.scoring, ng, tg,
+                                      int(r.renormalize), 1.0, ptr(self.score_bias),
+                                      ptr(w), ptr(ids), _stream()), "sl_select_experts")
+        return w, ids
+
+    def route(self, hidden_states: torch.Tensor, logits_out: torch.Tensor | None = None):
+        """Fused gate GEMV + selection: (topk_weights, topk_ids, router_logits)."""
+        _need_cuda(hidden_states, self.gate_weight)
+        r = self.routing
+        hs = hidden_states.contiguous()
+        T, H = hs.shape
+        E = self.gate_weight.shape[0]
+        dev = hs.device
+        logits = logits_out if logits_out is not None else torch.empty(
+            T, E, dtype=torch.bfloat16, device=dev)
+        w = torch.empty(T, r.topk, dtype=torch.float32, device=dev)
+        ids = torch.empty(T, r.topk, dtype=torch.int32, device=dev)
+        ng, tg = self._groups()
+        check(lib().sl_route(ptr(hs), ptr(self.gate_weight), ptr(self.logit_bias), T, H, E,
+                             r.topk, r.scoring, ng, tg, int(r.renormalize), 1.0,
+                             ptr(self.score_bias), ptr(w), ptr(ids), ptr(logits),
+                             _stream()), "sl_route")
+        return w, ids, logits
+
+
+def fused_experts(hidden_states: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
+                  topk_weights: torch.Tensor, topk_ids: torch.Tensor,
+                  activation: str = "silu", global_num_experts: int = -1,
+                  expert_map: torch.Tensor | None = None,
+                  shared_w13: torch.Tensor | None = None,
+                  shared_w2: torch.Tensor | None = None,
+                  routed_scaling_factor: float = 1.0,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """Routed (+ shared) expert output [T, H] bf16.
+
+    ``w1`` is [slots, 2I, H] (gate rows then up rows), ``w2`` [slots, H, I];
+    ``expert_map`` int32 [global_num_experts] maps a global id to its slot
+    (-1: contributes nothing). Without a map, ids index ``w1`` directly.
+    """
+    if activation != "silu":
+        raise ValueError("only activation='silu' (SwiGLU) is on this path")
+    _need_cuda(hidden_states, w1, w2, topk_weights, topk_ids, expert_map)
+    hs = hidden_states.contiguous()
+    T, H = hs.shape
+    S, two_i, H1 = w1.shape
+    I = two_i // 2
+    if H1 != H or tuple(w2.shape) != (S, H, I):
+        raise ValueError(f"weight shapes {tuple(w1.shape)} / {tuple(w2.shape)} do not match H={H}")
+    if w1.dtype != torch.bfloat16 or w2.dtype != torch.bfloat16 or hs.dtype != torch.bfloat16:
+        raise ValueError("bf16 weights and activations expected")
+    k = topk_ids.shape[1]
+    n_sh = 0 if shared_w13 is None else shared_w13.shape[0]
+    G = expert_map.numel() if expert_map is not None else (
+        global_num_experts if global_num_experts > 0 else S)
+    if expert_map is not None and expert_map.dtype != torch.int32:
+        raise ValueError("expert_map must be int32")
+    L = lib()
+    nbytes = L.sl_fused_experts_workspace_bytes(T, k, H, I, S, n_sh)
+    ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=hs.device)
+    if out is None:
+        out = torch.empty(T, H, dtype=torch.bfloat16, device=hs.device)
+    tw = topk_weights.contiguous().float()
+    ti = topk_ids.contiguous().to(torch.int32)
+    check(L.sl_fused_experts(ptr(hs), T, H, I, ptr(w1), ptr(w2), S, 0, ptr(tw), ptr(ti), k,
+                             ptr(expert_map), G, ptr(shared_w13), ptr(shared_w2), n_sh,
+                             float(routed_scaling_factor), ptr(out), ptr(ws), nbytes,
+                             _stream()), "sl_fused_experts")
+    fused_experts.last_workspace = ws
+    return out
+
+
+fused_experts.last_workspace = None
+
+
+def workspace_status(ws: torch.Tensor) -> int:
+    """Device status word of a fused_experts workspace (synchronises)."""
+    return int(ws[:4].view(torch.int32)[0].item())
+
+
+# --------------------------------------------------------------- torch ops
+# The gap registry: layer_idx -> SlotCache (the reference's _rs_caches).
+_GAP_CACHES: list = []
+
+
+def register_gap_layer(cache) -> int:
+    _GAP_CACHES.append(cache)
+    return len(_GAP_CACHES) - 1
+
+
+def sluice_stream_gap(hidden_states: torch.Tensor, topk_ids: torch.Tensor,
+                      layer_idx: int) -> torch.Tensor:
+    _GAP_CACHES[int(layer_idx)].gap(topk_ids)
+    return hidden_states.clone()
+
+
+_lib_def = torch.library.Library("sluice", "DEF")
+_lib_def.define("sluice_stream_gap(Tensor hidden_states, Tensor topk_ids, int layer_idx) -> Tensor")
+_lib_def.define(
+    "fused_experts(Tensor hidden_states, Tensor w1, Tensor w2, Tensor topk_weights, "
+    "Tensor topk_ids, str activation='silu', int global_num_experts=-1, "
+    "Tensor? expert_map=None, Tensor? shared_w13=None, Tensor? shared_w2=None, "
+    "float routed_scaling_factor=1.0) -> Tensor")
+_lib_def.impl("sluice_stream_gap", sluice_stream_gap, "CUDA")
+_lib_def.impl(
+    "fused_experts",
+    lambda hs, w1, w2, tw, ti, activation="silu", global_num_experts=-1, expert_map=None,
+    shared_w13=None, shared_w2=None, routed_scaling_factor=1.0: fused_experts(
+        hs, w1, w2, tw, ti, activation, global_num_experts, expert_map, shared_w13,
+        shared_w2, routed_scaling_factor),
+    "CUDA")
+
+
+@torch.library.register_fake("sluice::sluice_stream_gap")
+def _gap_fake(hidden_states, topk_ids, layer_idx):
+    return torch.empty_like(hidden_states)
+
+
+@torch.library.register_fake("sluice::fused_experts")
+def _fe_fake(hidden_states, w1, w2, topk_weights, topk_ids, activation="silu",
+             global_num_experts=-1, expert_map=None, shared_w13=None, shared_w2=None,
+             routed_scaling_factor=1.0):
+    return torch.empty_like(hidden_states)

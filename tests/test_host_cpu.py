@@ -1,0 +1,88 @@
+"""CPU tier: the C-ABI library loads and exports its header, and the host-side
+logic (initial slot residency, state layout) matches the oracle."""
+
+import ctypes
+import json
+import os
+
+import pytest
+
+from oracle.slot_policy import PINNED, SlotPolicyModel
+from sluice_b200 import _lib
+from sluice_b200.offloader import initial_slot_state, protected_cap_for
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def test_library_exports_every_header_symbol():
+    L = _lib.lib()
+    syms = _lib.header_symbols()
+    assert len(syms) >= 12
+    missing = [s for s in syms if not hasattr(L, s)]
+    assert not missing, missing
+    assert set(_lib._SIGNATURES) == set(syms)
+
+
+def test_status_strings_and_version():
+    L = _lib.lib()
+    assert L.sl_version() >= 100
+    assert b"raise SLUICE_SLOTS" in L.sl_status_string(_lib.SL_ERR_OVERFLOW)
+    assert L.sl_status_string(_lib.SL_OK) == b"ok"
+
+
+def test_state_layout_is_aligned_and_sized():
+    L = _lib.lib()
+    for S, G, Lc in [(48, 64, 64), (96, 128, 128), (24, 64, 32), (1, 1, 1), (1024, 4096, 256)]:
+        offs = (ctypes.c_size_t * (_lib.STATE_NFIELDS + 1))()
+        assert L.sl_slot_state_offsets(S, G, Lc, offs) == 0
+        o = list(offs)
+        assert all(v % 16 == 0 for v in o)
+        assert o == sorted(o)
+        assert o[-1] == L.sl_slot_state_bytes(S, G, Lc)
+        assert o[3] - o[2] >= 4 * G and o[6] - o[5] >= 4 * S and o[7] - o[6] >= S
+
+
+def test_host_calls_reject_bad_arguments_without_a_gpu():
+    L = _lib.lib()
+    assert L.sl_slot_state_bytes(0, 4, 4) == 0
+    assert L.sl_fused_experts_workspace_bytes(8, 6, 2048, 1408, 48, 2) > 0
+    # argument checks run before any CUDA call
+    assert L.sl_route(None, None, None, 1, 100, 64, 6, 0, 1, 1, 0, 1.0, None, None, None,
+                      None, None) == _lib.SL_ERR_UNSUPPORTED
+    assert L.sl_select_experts(None, 4, 48, 6, 0, 1, 1, 0, 1.0, None, None, None,
+                               None) == _lib.SL_ERR_UNSUPPORTED  # E % 32
+    assert L.sl_fused_experts(None, 4, 2048, 1400, None, None, 8, 0, None, None, 2, None,
+                              0, None, None, 0, 1.0, None, None, 0, None) == _lib.SL_ERR_UNSUPPORTED
+    assert L.sl_fused_experts(None, 4, 2048, 1408, None, None, 8, 1, None, None, 2, None,
+                              0, None, None, 0, 1.0, None, None, 0, None) == _lib.SL_ERR_UNSUPPORTED
+    assert L.sl_plan_slots(None, None, 0, None, None) == _lib.SL_ERR_INVALID
+    assert L.sl_stream_experts(None, 0, None, None, None, 0, None) == _lib.SL_ERR_INVALID
+
+
+@pytest.mark.parametrize("S,frac", [(48, 0.5), (48, 0.0), (48, 0.95), (1, 0.5), (96, 0.9)])
+def test_protected_cap_matches_oracle(S, frac):
+    m = SlotPolicyModel(S, list(range(S + 4)), S + 4, protect_frac=frac)
+    assert protected_cap_for(S, frac) == m.protected_cap
+
+
+def _scenarios():
+    with open(os.path.join(GOLDEN, "slot_traces.json")) as f:
+        return json.load(f)["scenarios"]
+
+
+@pytest.mark.parametrize("sc", _scenarios(), ids=lambda s: s["name"])
+def test_initial_state_matches_oracle(sc):
+    init = initial_slot_state(sc["num_slots"], sc["local_of"], sc["local_n"],
+                              sc["protect_frac"], sc["pins"], sc["prefill_resident"])
+    m = SlotPolicyModel(sc["num_slots"], sc["local_of"], sc["local_n"],
+                        protect_frac=sc["protect_frac"],
+                        prefill_resident=sc["prefill_resident"])
+    if sc["pins"]:
+        m.apply_pins(sc["pins"])
+    assert init.protected_cap == m.protected_cap == sc["protected_cap"]
+    assert init.expert_in_slot == m.expert_in_slot
+    assert init.free_stack == m.free_stack
+    assert [s for s in range(m.num_slots) if init.seg[s] == PINNED] == \
+        [s for s in range(m.num_slots) if m.seg[s] == PINNED]
+    if sc["pins"]:
+        assert sorted(s for _, s in init.fills) == sc["pinned_slots"]

@@ -1,0 +1,126 @@
+"""GPU parity: fused_experts (tcgen05 grouped GEMMs + combine) vs the oracle.
+
+Tolerance (bf16): |out - ref| <= 2e-2 * max|ref| + 2e-2 * |ref| elementwise,
+the north star's 2e-2 relative, scaled by the output's magnitude so that
+near-zero entries are not judged on their own relative error.
+"""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe as omoe
+from sluice_b200 import ops
+
+pytestmark = pytest.mark.gpu
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+RTOL = 2e-2
+
+
+def assert_moe_close(out, ref, rtol=RTOL):
+    out, ref = out.float().cpu(), ref.float().cpu()
+    assert torch.isfinite(out).all()
+    scale = ref.abs().max().item()
+    err = (out - ref).abs()
+    bound = rtol * scale + rtol * ref.abs()
+    bad = (err > bound).sum().item()
+    assert bad == 0, f"{bad} elements off; max err {err.max().item():.3e} vs scale {scale:.3e}"
+    rel = (err.norm() / ref.norm()).item()
+    assert rel < rtol / 2, rel
+
+
+def test_golden_case_through_expert_map():
+    z = np.load(os.path.join(GOLDEN, "moe.npz"))
+    bf = lambda a: torch.from_numpy(a).view(torch.bfloat16)
+    hs, w13, w2 = bf(z["hs"]), bf(z["w13"]), bf(z["w2"])
+    tw, ti = torch.from_numpy(z["topk_weights"]), torch.from_numpy(z["topk_ids"])
+    emap = torch.from_numpy(z["expert_map"])
+    ref = bf(z["out"])
+    out = ops.fused_experts(hs.cuda(), w13.cuda(), w2.cuda(), tw.cuda(), ti.cuda(),
+                            global_num_experts=emap.numel(), expert_map=emap.cuda())
+    torch.cuda.synchronize()
+    assert ops.workspace_status(ops.fused_experts.last_workspace) == 0
+    assert_moe_close(out, ref)
+
+
+def _random_case(T, H, I, S, E, k, n_sh, seed, map_frac=0.8, std=0.02):
+    g = torch.Generator().manual_seed(seed)
+    hs = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    w13 = (torch.randn(S, 2 * I, H, generator=g) * std).to(torch.bfloat16)
+    w2 = (torch.randn(S, H, I, generator=g) * std).to(torch.bfloat16)
+    perm = torch.randperm(E, generator=g)
+    emap = torch.full((E,), -1, dtype=torch.int32)
+    nres = min(S, int(E * map_frac))
+    emap[perm[:nres]] = torch.randperm(S, generator=g)[:nres].to(torch.int32)
+    ti = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)]).to(torch.int32)
+    tw = torch.rand(T, k, generator=g).float()
+    sh13 = sh2 = None
+    if n_sh:
+        sh13 = (torch.randn(n_sh, 2 * I, H, generator=g) * std).to(torch.bfloat16)
+        sh2 = (torch.randn(n_sh, H, I, generator=g) * std).to(torch.bfloat16)
+    return hs, w13, w2, emap, ti, tw, sh13, sh2
+
+
+def _reference(hs, w13, w2, emap, ti, tw, sh13, sh2, scale):
+    routed = omoe.fused_experts(hs, w13, w2, tw, ti, emap)
+    shared = None
+    if sh13 is not None:
+        shared = sum(omoe.expert_mlp(hs, sh13[i], sh2[i]).float()
+                     for i in range(sh13.shape[0])).to(torch.bfloat16)
+    return omoe.layer_output(routed, shared, scale)
+
+
+@pytest.mark.parametrize("T,H,I,S,E,k,n_sh,scale", [
+    (8, 2048, 1408, 48, 64, 6, 2, 1.0),     # V2-Lite decode, c=8
+    (1, 2048, 1408, 48, 64, 6, 2, 1.0),     # c=1
+    (12, 2048, 768, 96, 128, 8, 0, 1.0),    # Qwen3 decode, c=12
+    (16, 2048, 768, 128, 128, 8, 0, 1.0),   # Qwen3 resident
+    (5, 256, 128, 6, 8, 3, 1, 2.5),         # tiny, shared + routed scaling
+    (40, 512, 256, 16, 32, 4, 0, 1.0),      # experts with > 16 tokens (several items)
+])
+def test_random_cases(T, H, I, S, E, k, n_sh, scale):
+    hs, w13, w2, emap, ti, tw, sh13, sh2 = _random_case(T, H, I, S, E, k, n_sh, seed=T * 7 + H)
+    c = lambda t: None if t is None else t.cuda()
+    out = ops.fused_experts(c(hs), c(w13), c(w2), c(tw), c(ti), global_num_experts=E,
+                            expert_map=c(emap), shared_w13=c(sh13), shared_w2=c(sh2),
+                            routed_scaling_factor=scale)
+    torch.cuda.synchronize()
+    assert ops.workspace_status(ops.fused_experts.last_workspace) == 0
+    assert_moe_close(out, _reference(hs, w13, w2, emap, ti, tw, sh13, sh2, scale))
+
+
+def test_unmapped_and_out_of_range_ids_contribute_nothing():
+    T, H, I, S, E, k = 4, 256, 128, 4, 8, 2
+    hs, w13, w2, emap, ti, tw, _, _ = _random_case(T, H, I, S, E, k, 0, seed=11)
+    emap[:] = -1
+    out = ops.fused_experts(hs.cuda(), w13.cuda(), w2.cuda(), tw.cuda(), ti.cuda(),
+                            global_num_experts=E, expert_map=emap.cuda())
+    assert torch.count_nonzero(out).item() == 0
+    ti2 = ti.clone()
+    ti2[:, 0] = -1
+    ti2[:, 1] = 1000
+    emap2 = torch.arange(E, dtype=torch.int32) % S
+    out2 = ops.fused_experts(hs.cuda(), w13.cuda(), w2.cuda(), tw.cuda(), ti2.cuda(),
+                             global_num_experts=E, expert_map=emap2.cuda())
+    assert torch.count_nonzero(out2).item() == 0
+
+
+def test_no_map_indexes_slots_directly_and_repeats_are_stable():
+    T, H, I, S, k = 8, 512, 256, 8, 2
+    hs, w13, w2, _, _, tw, _, _ = _random_case(T, H, I, S, S, k, 0, seed=3)
+    g = torch.Generator().manual_seed(4)
+    ti = torch.stack([torch.randperm(S, generator=g)[:k] for _ in range(T)]).to(torch.int32)
+    a = ops.fused_experts(hs.cuda(), w13.cuda(), w2.cuda(), tw.cuda(), ti.cuda())
+    b = ops.fused_experts(hs.cuda(), w13.cuda(), w2.cuda(), tw.cuda(), ti.cuda())
+    assert torch.equal(a, b)
+    assert_moe_close(a, omoe.fused_experts(hs, w13, w2, tw, ti))
+
+
+def test_torch_op_registration():
+    T, H, I, S, E, k = 3, 256, 128, 4, 8, 2
+    hs, w13, w2, emap, ti, tw, _, _ = _random_case(T, H, I, S, E, k, 0, seed=21)
+    out = torch.ops.sluice.fused_experts(hs.cuda(), w13.cuda(), w2.cuda(), tw.cuda(),
+                                         ti.cuda(), "silu", E, emap.cuda())
+    assert_moe_close(out, omoe.fused_experts(hs, w13, w2, tw, ti, emap))
