@@ -1,0 +1,432 @@
+"""Benchmark: offloaded MoE decode on B200 (the reference's headline path).
+
+Workload (the MoE path of a DeepSeek-V2-Lite-shaped
+decoder): 26 MoE layers, hidden 2048, 64 routed experts of SwiGLU
+intermediate 1408 (bf16, 17.3 MB each) plus 2 shared experts, softmax top-6,
+48 GPU slots per layer (16 of 64 experts per layer live only in host RAM),
+c = 8 decode tokens per step. Seeded synthetic weights and tokens (no
+checkpoints): gate logit bias 1.5*log(1/rank) for Zipf-like popularity, 60%
+of each step's tokens reuse the previous step's vector plus noise.
+
+One step = one decode step through all 26 MoE layers (router -> device slot
+planner -> GPU-initiated expert streaming -> tcgen05 fused experts with the
+shared experts -> residual), replayed as one CUDA graph.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl sluice|reference]
+
+``--impl reference`` times the reference's torch-native CPU path (the oracle
+port of routing, the slot policy and the MoE layer) on the host cores.
+Prints one JSON line on rank 0.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+METRIC = "decode tok/s"
+UNIT = "tok/s"
+
+
+def _args(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="sluice", choices=["sluice", "reference"])
+    ap.add_argument("--config", default="deepseek-v2-lite")
+    ap.add_argument("--slots", type=int, default=48)
+    ap.add_argument("--tokens", type=int, default=8)
+    ap.add_argument("--layers", type=int, default=None)
+    ap.add_argument("--prefill-steps", type=int, default=24,
+                    help="untimed steps that fill the slot caches before warm-up")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-resident", action="store_true")
+    ap.add_argument("--seed", type=int, default=0)
+    return ap.parse_args(argv)
+
+
+def _workload(cfg, slots, tokens, layers):
+    return (f"{cfg.name} MoE decode stack: {layers} MoE layers, H={cfg.hidden}, "
+            f"{cfg.num_experts} experts x I={cfg.moe_intermediate} ({slots} GPU slots, "
+            f"{cfg.num_experts - slots} per layer in host RAM), top-{cfg.routing.topk}, "
+            f"{cfg.n_shared} shared, c={tokens}")
+
+
+# ------------------------------------------------------------ clock sampling
+class ClockSampler:
+    def __init__(self, index: int):
+        self.index = index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                       "-i", str(self.index), "-lms", "200"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+        return self
+
+    def __exit__(self, *a):
+        if self.p is not None:
+            self.p.terminate()
+            try:
+                self.p.wait(timeout=5)
+            except Exception:
+                self.p.kill()
+
+    def summary(self):
+        try:
+            self.f.flush()
+            with open(self.f.name) as fh:
+                rows = [r.split(", ") for r in fh.read().strip().splitlines() if r.strip()]
+            os.unlink(self.f.name)
+        except Exception:
+            return None
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = max(float(r[2]) for r in rows)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4)
+                          if len(r) > 5 + i and r[5 + i].strip() == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# --------------------------------------------------------------- CPU port
+def cpu_layer_runner(cfg, seed, n_weight_sets=2):
+    """The reference's torch-native CPU path for one layer (oracle port):
+    gate + routing, the gap's slot policy, the MoE with shared experts."""
+    from oracle import moe as omoe
+    from oracle import routing as orouting
+    from oracle.slot_policy import SlotPolicyModel
+    from sluice_b200 import synth
+
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    sets = []
+    for li in range(n_weight_sets):
+        w13, w2 = synth.layer_weights(cfg, li, seed, device=dev)
+        sh13, sh2 = synth.shared_weights(cfg, li, seed, device=dev)
+        gw, lb, sb = synth.gate_params(cfg, li, seed, device="cpu")
+        cpu = lambda t: None if t is None else t.cpu()
+        sh = None
+        if sh13 is not None:
+            # one shared MLP of intermediate n*I, as the reference's shared_layer
+            n, I = cfg.n_shared, cfg.moe_intermediate
+            g13 = torch.cat([sh13[:, :I].reshape(n * I, -1), sh13[:, I:].reshape(n * I, -1)])
+            g2 = sh2.permute(1, 0, 2).reshape(cfg.hidden, n * I)
+            sh = (g13.cpu(), g2.cpu())
+        sets.append((w13.cpu(), w2.cpu(), gw, lb, sb, sh))
+        del w13, w2
+    rc = cfg.routing
+    policies = {}
+
+    def run_layer(li, x, slots):
+        w13, w2, gw, lb, sb, sh = sets[li % n_weight_sets]
+        logits = orouting.gate_logits(x, gw, lb)
+        tw, ti = orouting.grouped_topk(logits, rc.topk, rc.renormalize, rc.num_expert_group,
+                                       rc.topk_group, rc.scoring_func, 1.0, sb)
+        pol = policies.setdefault(li, SlotPolicyModel(slots, list(range(cfg.num_experts)),
+                                                      cfg.num_experts, 0.5, True))
+        pol.gap(ti.flatten().tolist())
+        routed = omoe.fused_experts(x, w13, w2, tw, ti)
+        shared = omoe.shared_experts(x, *sh) if sh is not None else None
+        return omoe.layer_output(routed, shared, cfg.routed_scaling_factor)
+
+    return run_layer
+
+
+def cpu_step_time(cfg, slots, tokens, layers, seed, steps, warmup, budget_s=None):
+    """Seconds per full decode step of the CPU port (all layers)."""
+    from sluice_b200 import synth
+
+    run = cpu_layer_runner(cfg, seed)
+    stream = synth.TokenStream(cfg.hidden, tokens, seed=seed)
+    times = []
+    t_start = time.perf_counter()
+    for s in range(warmup + steps):
+        x = stream.next()
+        t0 = time.perf_counter()
+        h = x
+        for li in range(layers):
+            h = h + run(li, h, slots)
+        dt = time.perf_counter() - t0
+        if s >= warmup:
+            times.append(dt)
+        if budget_s is not None and s >= warmup and time.perf_counter() - t_start > budget_s:
+            break
+    return statistics.median(times), len(times)
+
+
+# ---------------------------------------------------------------- GPU arm
+def h2d_ceiling_gbs(nbytes=1 << 30):
+    src = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    dst = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    dst.copy_(src, non_blocking=True)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    best = 0.0
+    for _ in range(3):
+        a.record()
+        dst.copy_(src, non_blocking=True)
+        b.record()
+        b.synchronize()
+        best = max(best, nbytes / (a.elapsed_time(b) * 1e-3) / 1e9)
+    del src, dst
+    return best
+
+
+def profile_layers(stack, stream_tokens, steps=6):
+    """Eager pass with CUDA events around each layer's sub-steps: returns
+    per-launch averages (ms) and algorithmic bytes of fused_experts / stream."""
+    from sluice_b200 import ops
+
+    cfg = stack.cfg
+    bpe = cfg.bytes_per_expert
+    rec = {"route": [], "gap": [], "fused": []}
+    fused_bytes, stream_bytes = [], []
+    torch.cuda.synchronize()
+    for _ in range(steps):
+        h = stream_tokens.next().cuda()
+        for layer in stack.layers:
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+            ev[0].record()
+            tw, ti, logits = layer.router.route(h)
+            ev[1].record()
+            misses0 = layer.cache.counters()["fills"] if layer.cache.state is not None else 0
+            layer.cache.gap(ti)
+            ev[2].record()
+            out = ops.fused_experts(h, layer.cache.w13, layer.cache.w2, tw, ti,
+                                    global_num_experts=cfg.num_experts,
+                                    expert_map=layer.cache.expert_map,
+                                    shared_w13=layer.shared_w13, shared_w2=layer.shared_w2,
+                                    routed_scaling_factor=cfg.routed_scaling_factor)
+            ev[3].record()
+            h = h + out
+            torch.cuda.synchronize()
+            rec["route"].append(ev[0].elapsed_time(ev[1]))
+            rec["gap"].append(ev[1].elapsed_time(ev[2]))
+            rec["fused"].append(ev[2].elapsed_time(ev[3]))
+            u = len(set(ti.flatten().tolist()))
+            fused_bytes.append((u + cfg.n_shared) * bpe)
+            misses1 = layer.cache.counters()["fills"] if layer.cache.state is not None else 0
+            stream_bytes.append((misses1 - misses0) * bpe)
+    return rec, fused_bytes, stream_bytes
+
+
+def load_traffic():
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(p) as f:
+            return json.load(f)
+    except Exception:
+        return {}
+
+
+def run_sluice(a):
+    from sluice_b200 import configs, synth
+    from sluice_b200.layer import MoEDecodeStack
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
+    cfg = configs.CONFIGS[a.config]
+    layers = a.layers or cfg.num_moe_layers
+    T = a.tokens
+    t_build = time.perf_counter()
+    stack = MoEDecodeStack(cfg, slots=a.slots, seed=a.seed + rank, num_layers=layers)
+    stack.capture(tokens=T)
+    build_s = time.perf_counter() - t_build
+    stream = synth.TokenStream(cfg.hidden, T, seed=a.seed + 100 + rank)
+    # preconditioning: fill the slot caches, then the W warm-up steps
+    for _ in range(a.prefill_steps):
+        stack.replay(stream.next().cuda())
+    torch.cuda.synchronize()
+    stats0 = stack.stats()
+    K, W = a.steps, a.warmup
+    xs = torch.stack([stream.next() for _ in range(W + K)]).cuda()
+    for i in range(W):
+        stack.replay(xs[i])
+    torch.cuda.synchronize()
+    stats_w = stack.stats()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        ev0.record()
+        for i in range(K):
+            stack.replay(xs[W + i])
+        ev1.record()
+        torch.cuda.synchronize()
+    stack.check()
+    stats_t = stack.stats()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    value = world * T * K / (ms * 1e-3)
+
+    # end to end through the public call: pinned host in, host out
+    xh = torch.stack([stream.next() for _ in range(K)]).pin_memory()
+    oh = torch.empty(K, T, cfg.hidden, dtype=torch.bfloat16).pin_memory()
+    stack.decode_step(xh[0], oh[0])
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(K):
+        stack.decode_step(xh[i], oh[i])
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    stack.check()
+
+    misses = stats_t["misses"] - stats_w["misses"]
+    fills = stats_t["fills"] - stats_w["fills"]
+    bpe = cfg.bytes_per_expert
+    # kernel roofline from an eager, event-timed pass over the same stack
+    rec, fbytes, sbytes = profile_layers(stack, stream)
+    t_fused = statistics.mean(rec["fused"])
+    t_gap = statistics.mean(rec["gap"])
+    t_route = statistics.mean(rec["route"])
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except Exception:
+        pass
+    hbm_peak = peaks.get("hbm_gbs", 6650.0)
+    fused_gbs = statistics.mean(fbytes) / (t_fused * 1e-3) / 1e9
+    traffic = load_traffic().get("fused_experts_bytes_per_launch")
+    h2d = h2d_ceiling_gbs()
+    stream_gbs = (sum(sbytes) / (sum(rec["gap"]) * 1e-3) / 1e9) if sum(sbytes) else None
+
+    # resident comparison: same kernels, every expert in HBM (slots = E)
+    resident = None
+    if not a.no_resident and world == 1:
+        del stack
+        torch.cuda.empty_cache()
+        rs = MoEDecodeStack(cfg, slots=cfg.num_experts, seed=a.seed, num_layers=layers)
+        rs.capture(tokens=T)
+        for i in range(W):
+            rs.replay(xs[i])
+        torch.cuda.synchronize()
+        r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        r0.record()
+        for i in range(K):
+            rs.replay(xs[W + i])
+        r1.record()
+        torch.cuda.synchronize()
+        resident = {"value": T * K / (r0.elapsed_time(r1) * 1e-3), "unit": UNIT,
+                    "slots": cfg.num_experts}
+        del rs
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        t_cpu, n = cpu_step_time(cfg, a.slots, T, layers, a.seed, steps=3, warmup=1,
+                                 budget_s=25.0)
+        cpu = {"value": T / t_cpu, "unit": UNIT, "cores": torch.get_num_threads(),
+               "kind": "port",
+               "sample": f"{n} full decode steps ({layers} layers, c={T}) of the torch-native "
+                         f"CPU path (oracle routing + slot policy + MoE), median"}
+
+    # per layer: gate, select, plan, stream, align, gate/up GEMM, down GEMM,
+    # combine (plan and stream are skipped on fully resident layers)
+    launches = K * layers * (8 if a.slots < cfg.num_experts else 6)
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
+        "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": _workload(cfg, a.slots, T, layers), "model": cfg.name,
+                   "tokens_per_step": T, "slots": a.slots, "layers": layers,
+                   "global_batch": T * world, "seq_len": 1,
+                   "parallelism": "replicas" if world > 1 else "single",
+                   "cache_prefill_steps": a.prefill_steps,
+                   "l2": "per-step expert weights >> 126 MB L2 (no flush needed)",
+                   "build_s": round(build_s, 1)},
+        "e2e": {"value": T * K / (e2e_ms * 1e-3), "unit": UNIT,
+                "h2d_bytes_per_step": T * cfg.hidden * 2,
+                "d2h_bytes_per_step": T * cfg.hidden * 2},
+        "roofline": {"bound": "hbm", "kernel": "fused_experts (align+gate/up+down+combine)",
+                     "achieved": fused_gbs, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": fused_gbs / hbm_peak, "traffic": traffic,
+                     "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)",
+                     "per_launch_ms": {"route": t_route, "gap": t_gap, "fused": t_fused},
+                     "fused_bytes_per_launch": statistics.mean(fbytes)},
+        "stream": {"misses_per_step": misses / K, "fills_per_step": fills / K,
+                   "streamed_gbs_in_gap": stream_gbs, "h2d_ceiling_gbs": h2d,
+                   "pcie_gen5_x16_gbs": 63.0},
+        "resident": resident,
+        "cpu_baseline": cpu,
+        "gpu_launches": launches,
+        "clocks": clk.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+def run_reference(a):
+    """The reference's CPU path (oracle port) on the host cores, rank 0 only."""
+    from sluice_b200 import configs
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    cfg = configs.CONFIGS[a.config]
+    layers = a.layers or cfg.num_moe_layers
+    T = a.tokens
+    torch.set_num_threads(os.cpu_count() or 1)
+    t_step, n = cpu_step_time(cfg, a.slots, T, layers, a.seed, steps=a.steps,
+                              warmup=max(1, min(a.warmup, 2)), budget_s=150.0)
+    v = T / t_step
+    line = {
+        "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": n,
+        "warmup": a.warmup, "ms_per_step": t_step * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "impl": "reference",
+        "config": {"workload": _workload(cfg, a.slots, T, layers), "model": cfg.name,
+                   "tokens_per_step": T, "slots": a.slots, "layers": layers},
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": torch.get_num_threads(),
+                         "kind": "port",
+                         "sample": f"{n} full decode steps ({layers} layers, c={T}), median; "
+                                   "2 distinct weight sets cycled over the layers"},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main(argv=None):
+    a = _args(argv)
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_sluice(a)
+
+
+if __name__ == "__main__":
+    main()

@@ -22,10 +22,12 @@ def _scenarios():
 
 
 def _payload_params(local_n):
-    """Tiny per-expert params whose every element is the local expert id."""
+    """Tiny per-expert params whose elements encode the local expert id
+    (exact in bf16 for ids below 256)."""
+    assert local_n <= 255
     ids = torch.arange(local_n, dtype=torch.float32)
     w13 = ids.view(-1, 1, 1).expand(local_n, 2, 8).to(torch.bfloat16).contiguous()
-    w2 = (ids + 1000).view(-1, 1, 1).expand(local_n, 8, 1).to(torch.bfloat16).contiguous()
+    w2 = (-ids - 1).view(-1, 1, 1).expand(local_n, 8, 1).to(torch.bfloat16).contiguous()
     return w13, w2
 
 
@@ -66,7 +68,7 @@ def test_planner_matches_reference_trace(sc):
         w2 = cache.w2[:, 0, 0].float().cpu().tolist()
         for s, loc in enumerate(exp["slot_payload"]):
             if loc >= 0:
-                assert w13[s] == loc and w2[s] == loc + 1000, (sc["name"], i, s)
+                assert w13[s] == loc and w2[s] == -loc - 1, (sc["name"], i, s)
 
 
 def test_planner_long_random_run_matches_oracle():
