@@ -38,7 +38,8 @@ enum {
   SL_ERR_INVALID = 2,     /* bad argument */
   SL_ERR_CUDA = 3,        /* CUDA runtime error */
   SL_ERR_UNSUPPORTED = 4, /* shape / dtype this build does not cover */
-  SL_ERR_TIMEOUT = 5      /* a bounded device wait ran out */
+  SL_ERR_TIMEOUT = 5,     /* a bounded device wait ran out */
+  SL_ERR_NO_SCRATCH = 6   /* problem too large for sl_fused_experts_noalloc */
 };
 
 /* Human-readable text for a status code. */
@@ -172,6 +173,36 @@ int sl_fused_experts(const void* hidden, int T, int H, int I,
                      int n_shared, float routed_scaling_factor, void* out,
                      void* workspace, size_t workspace_bytes,
                      sl_stream_t stream);
+
+/* sl_fused_experts without any device allocation. No counterpart in the
+ * reference: it serves callers that cannot allocate device scratch memory for
+ * a call -- a host program binding this C ABI directly (cgo, JNI, ctypes
+ * without torch) has no caching allocator to draw on, and a serving process
+ * that has handed nearly all HBM to its own pool sees cudaMalloc fail or
+ * stall the device mid-step. Same arguments and result as sl_fused_experts,
+ * minus the workspace; the scratch is one file-scope device array of 32 MiB
+ * per device, held from library load until process exit.
+ *   - Problems whose sl_fused_experts_workspace_bytes(...) exceeds 32 MiB
+ *     return SL_ERR_NO_SCRATCH and launch nothing.
+ *   - Every call on a device shares the array: calls that can overlap on the
+ *     GPU (unordered streams) race and corrupt each other.
+ *   - The array keeps the last call's contents; each call clears its status
+ *     word and work counts first and rewrites every row it reads.
+ *   - The first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress) with that device current: make it before any
+ *     stream capture.
+ *   - status_out (device int32, may be NULL) receives the device status word
+ *     (SL_OK or SL_ERR_TIMEOUT) on the same stream.
+ * Calls no cudaMalloc / cudaFree / allocating library routine. */
+int sl_fused_experts_noalloc(const void* hidden, int T, int H, int I,
+                             const void* w13, const void* w2, int num_slots,
+                             int weight_dtype, const float* topk_weights,
+                             const int32_t* topk_ids, int topk,
+                             const int32_t* expert_map, int global_n,
+                             const void* shared_w13, const void* shared_w2,
+                             int n_shared, float routed_scaling_factor,
+                             void* out, int32_t* status_out,
+                             sl_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -22,6 +22,7 @@ SL_ERR_INVALID = 2
 SL_ERR_CUDA = 3
 SL_ERR_UNSUPPORTED = 4
 SL_ERR_TIMEOUT = 5
+SL_ERR_NO_SCRATCH = 6
 
 SEG_FREE, SEG_PROBATION, SEG_PROTECTED, SEG_PINNED = 0, 1, 2, 3
 PLAN_FAST_HIT = 1
@@ -55,6 +56,8 @@ _SIGNATURES = {
     "sl_fused_experts_workspace_bytes": (_sz, [_i, _i, _i, _i, _i, _i]),
     "sl_fused_experts": (_i, [_vp, _i, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _i, _vp,
                               _i, _vp, _vp, _i, _f, _vp, _vp, _sz, _vp]),
+    "sl_fused_experts_noalloc": (_i, [_vp, _i, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _i,
+                                      _vp, _i, _vp, _vp, _i, _f, _vp, _vp, _vp]),
 }
 
 _lock = threading.Lock()

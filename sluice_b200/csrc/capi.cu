@@ -16,6 +16,9 @@ extern "C" const char* sl_status_string(int status) {
     case SL_ERR_CUDA: return "CUDA runtime error";
     case SL_ERR_UNSUPPORTED: return "shape or dtype not supported by this build";
     case SL_ERR_TIMEOUT: return "a bounded device wait ran out";
+    case SL_ERR_NO_SCRATCH:
+      return "problem needs more than the 32 MiB static scratch of sl_fused_experts_noalloc; "
+             "use sl_fused_experts with a caller workspace";
     default: return "unknown status";
   }
 }
