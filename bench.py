@@ -193,42 +193,86 @@ def h2d_ceiling_gbs(nbytes=1 << 30):
     return best
 
 
-def profile_layers(stack, stream_tokens, steps=6):
-    """Eager pass with CUDA events around each layer's sub-steps: returns
-    per-launch averages (ms) and algorithmic bytes of fused_experts / stream."""
+def _graph_time_ms(fn, reps=10):
+    """Device time per call of `fn` captured in a CUDA graph (no host gaps)."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        g.replay()
+    b.record()
+    b.synchronize()
+    del g
+    return a.elapsed_time(b) / reps
+
+
+def profile_layers(stack, x):
+    """Per-layer device time of route and fused_experts, each replayed as its
+    own CUDA graph on the inputs of one real decode step; returns the lists
+    of (ms, algorithmic bytes)."""
     from sluice_b200 import ops
 
     cfg = stack.cfg
     bpe = cfg.bytes_per_expert
-    rec = {"route": [], "gap": [], "fused": []}
-    fused_bytes, stream_bytes = [], []
+    route_ms, fused_ms, fused_bytes = [], [], []
+    h = x
+    for layer in stack.layers:
+        tw, ti, _ = layer.router.route(h)
+        layer.cache.gap(ti)
+        out = torch.empty_like(h)
+        hs = h.clone()
+        fused = lambda: ops.fused_experts(hs, layer.cache.w13, layer.cache.w2, tw, ti,
+                                          global_num_experts=cfg.num_experts,
+                                          expert_map=layer.cache.expert_map,
+                                          shared_w13=layer.shared_w13,
+                                          shared_w2=layer.shared_w2,
+                                          routed_scaling_factor=cfg.routed_scaling_factor,
+                                          out=out)
+        fused_ms.append(_graph_time_ms(fused))
+        route_ms.append(_graph_time_ms(lambda: layer.router.route(hs)))
+        u = len(set(ti.flatten().tolist()))
+        fused_bytes.append((u + cfg.n_shared) * bpe)
+        h = h + out
     torch.cuda.synchronize()
-    for _ in range(steps):
-        h = stream_tokens.next().cuda()
-        for layer in stack.layers:
-            ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
-            ev[0].record()
-            tw, ti, logits = layer.router.route(h)
-            ev[1].record()
-            misses0 = layer.cache.counters()["fills"] if layer.cache.state is not None else 0
-            layer.cache.gap(ti)
-            ev[2].record()
-            out = ops.fused_experts(h, layer.cache.w13, layer.cache.w2, tw, ti,
-                                    global_num_experts=cfg.num_experts,
-                                    expert_map=layer.cache.expert_map,
-                                    shared_w13=layer.shared_w13, shared_w2=layer.shared_w2,
-                                    routed_scaling_factor=cfg.routed_scaling_factor)
-            ev[3].record()
-            h = h + out
-            torch.cuda.synchronize()
-            rec["route"].append(ev[0].elapsed_time(ev[1]))
-            rec["gap"].append(ev[1].elapsed_time(ev[2]))
-            rec["fused"].append(ev[2].elapsed_time(ev[3]))
-            u = len(set(ti.flatten().tolist()))
-            fused_bytes.append((u + cfg.n_shared) * bpe)
-            misses1 = layer.cache.counters()["fills"] if layer.cache.state is not None else 0
-            stream_bytes.append((misses1 - misses0) * bpe)
-    return rec, fused_bytes, stream_bytes
+    return route_ms, fused_ms, fused_bytes
+
+
+def stream_probe(stack, n_miss=12, ctas=(16, 32, 64, 128, 148)):
+    """Streamer bandwidth: plan a gap that misses `n_miss` experts on layer 0,
+    then re-run the streamer over that fill list (idempotent) per CTA count."""
+    import ctypes
+    from sluice_b200._lib import check, lib, ptr
+
+    layer = stack.layers[0]
+    cache = layer.cache
+    if cache.state is None:
+        return None
+    resident = set(v for v in cache.snapshot()["expert_in_slot"] if v >= 0)
+    cold = [e for e in range(cache.local_n) if e not in resident][:n_miss]
+    if not cold:
+        return None
+    ids = torch.tensor(cold, dtype=torch.int32, device="cuda")
+    cache.gap(ids)
+    torch.cuda.synchronize()
+    fills = cache.header()["fill_count"]
+    n, src, dst, nb = cache._stream_args
+    out = {}
+    for c in ctas:
+        s = lambda: check(lib().sl_stream_experts(ptr(cache.state), n, src, dst, nb, c,
+                                                  torch.cuda.current_stream().cuda_stream),
+                          "stream")
+        ms = _graph_time_ms(s, reps=5)
+        out[c] = fills * cache.bytes_per_expert / (ms * 1e-3) / 1e9
+    return {"fills": fills, "gbs_by_ctas": out}
 
 
 def load_traffic():
@@ -240,7 +284,25 @@ def load_traffic():
         return {}
 
 
+def _step_bytes(stack, cfg):
+    """Algorithmic HBM bytes of the last step's expert GEMMs on this rank:
+    sum over layers of (distinct resident selected experts + shared) x bytes."""
+    tot = 0
+    for layer in stack.layers:
+        ids = layer.last_ids
+        if ids is None:
+            continue
+        emap = layer.cache.expert_map
+        sel = ids.flatten().long()
+        sel = sel[(sel >= 0) & (sel < emap.numel())]
+        u = torch.unique(sel[emap[sel] >= 0]).numel()
+        tot += (u + cfg.n_shared) * cfg.bytes_per_expert
+    return tot
+
+
 def run_sluice(a):
+    import datetime
+
     from sluice_b200 import configs, synth
     from sluice_b200.layer import MoEDecodeStack
 
@@ -248,22 +310,29 @@ def run_sluice(a):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local_rank)
+    dist = None
     if world > 1:
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
     cfg = configs.CONFIGS[a.config]
     layers = a.layers or cfg.num_moe_layers
     T = a.tokens
     t_build = time.perf_counter()
-    stack = MoEDecodeStack(cfg, slots=a.slots, seed=a.seed + rank, num_layers=layers)
-    stack.capture(tokens=T)
+    if world > 1:
+        from sluice_b200.ep import EPDecodeStack
+        stack = EPDecodeStack(cfg, slots=a.slots, seed=a.seed, num_layers=layers)
+        graphed = stack.capture(tokens=T)
+    else:
+        stack = MoEDecodeStack(cfg, slots=a.slots, seed=a.seed, num_layers=layers)
+        stack.capture(tokens=T)
+        graphed = True
     build_s = time.perf_counter() - t_build
     stream = synth.TokenStream(cfg.hidden, T, seed=a.seed + 100 + rank)
     # preconditioning: fill the slot caches, then the W warm-up steps
     for _ in range(a.prefill_steps):
         stack.replay(stream.next().cuda())
     torch.cuda.synchronize()
-    stats0 = stack.stats()
     K, W = a.steps, a.warmup
     xs = torch.stack([stream.next() for _ in range(W + K)]).cuda()
     for i in range(W):
@@ -271,8 +340,8 @@ def run_sluice(a):
     torch.cuda.synchronize()
     stats_w = stack.stats()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        torch.distributed.barrier()
+    if dist:
+        dist.barrier()
     torch.cuda.synchronize()
     with ClockSampler(torch.cuda.current_device()) as clk:
         ev0.record()
@@ -280,20 +349,26 @@ def run_sluice(a):
             stack.replay(xs[W + i])
         ev1.record()
         torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
     stack.check()
     stats_t = stack.stats()
     ms = ev0.elapsed_time(ev1)
-    if world > 1:
+    if dist:
         t = torch.tensor([ms], device="cuda")
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     value = world * T * K / (ms * 1e-3)
+    hbm_step = _step_bytes(stack, cfg)
 
     # end to end through the public call: pinned host in, host out
     xh = torch.stack([stream.next() for _ in range(K)]).pin_memory()
     oh = torch.empty(K, T, cfg.hidden, dtype=torch.bfloat16).pin_memory()
     stack.decode_step(xh[0], oh[0])
     torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for i in range(K):
@@ -301,16 +376,15 @@ def run_sluice(a):
     e1.record()
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
     stack.check()
 
-    misses = stats_t["misses"] - stats_w["misses"]
-    fills = stats_t["fills"] - stats_w["fills"]
+    misses = stats_t.get("misses", 0) - stats_w.get("misses", 0)
+    fills = stats_t.get("fills", 0) - stats_w.get("fills", 0)
     bpe = cfg.bytes_per_expert
-    # kernel roofline from an eager, event-timed pass over the same stack
-    rec, fbytes, sbytes = profile_layers(stack, stream)
-    t_fused = statistics.mean(rec["fused"])
-    t_gap = statistics.mean(rec["gap"])
-    t_route = statistics.mean(rec["route"])
     peaks = {}
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -318,10 +392,36 @@ def run_sluice(a):
     except Exception:
         pass
     hbm_peak = peaks.get("hbm_gbs", 6650.0)
-    fused_gbs = statistics.mean(fbytes) / (t_fused * 1e-3) / 1e9
-    traffic = load_traffic().get("fused_experts_bytes_per_launch")
     h2d = h2d_ceiling_gbs()
-    stream_gbs = (sum(sbytes) / (sum(rec["gap"]) * 1e-3) / 1e9) if sum(sbytes) else None
+    host_step = fills / K * bpe
+    t_roof = max(hbm_step / (hbm_peak * 1e9), host_step / 63.0e9) * 1e3
+    step_roof = {"t_roof_ms": t_roof, "t_ms": ms / K, "frac": t_roof / (ms / K),
+                 "hbm_bytes_per_step": hbm_step, "host_bytes_per_step": host_step,
+                 "host_peak_gbs": 63.0, "hbm_peak_gbs": hbm_peak}
+
+    roof = None
+    sprobe = None
+    if world == 1:
+        # kernel roofline: each layer's fused_experts / route replayed as a graph
+        route_ms, fused_ms, fbytes = profile_layers(stack, stream.next().cuda())
+        t_fused = statistics.mean(fused_ms)
+        fused_gbs = statistics.mean(fbytes) / (t_fused * 1e-3) / 1e9
+        roof = {"bound": "hbm", "kernel": "fused_experts (align+gate/up+down+combine)",
+                "achieved": fused_gbs, "peak": hbm_peak, "unit": "GB/s",
+                "frac": fused_gbs / hbm_peak,
+                "traffic": load_traffic().get("fused_experts_bytes_per_launch"),
+                "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)",
+                "per_launch_ms": {"route": statistics.mean(route_ms), "fused": t_fused},
+                "fused_bytes_per_launch": statistics.mean(fbytes),
+                "timing": "each layer's fused_experts replayed as its own CUDA graph, "
+                          "CUDA events, mean over layers"}
+        sprobe = stream_probe(stack)
+    else:
+        roof = {"bound": "hbm", "kernel": "expert-parallel decode step (per rank)",
+                "achieved": hbm_step / (ms / K * 1e-3) / 1e9, "peak": hbm_peak,
+                "unit": "GB/s", "frac": hbm_step / (ms / K * 1e-3) / 1e9 / hbm_peak,
+                "traffic": None, "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)",
+                "timing": "timed region, max over ranks"}
 
     # resident comparison: same kernels, every expert in HBM (slots = E)
     resident = None
@@ -342,6 +442,8 @@ def run_sluice(a):
         resident = {"value": T * K / (r0.elapsed_time(r1) * 1e-3), "unit": UNIT,
                     "slots": cfg.num_experts}
         del rs
+    elif hasattr(stack, "release"):
+        stack.release()
 
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
@@ -352,32 +454,30 @@ def run_sluice(a):
                "sample": f"{n} full decode steps ({layers} layers, c={T}) of the torch-native "
                          f"CPU path (oracle routing + slot policy + MoE), median"}
 
-    # per layer: gate, select, plan, stream, align, gate/up GEMM, down GEMM,
-    # combine (plan and stream are skipped on fully resident layers)
-    launches = K * layers * (8 if a.slots < cfg.num_experts else 6)
+    local_n = cfg.num_experts // world
+    offloaded = a.slots < local_n
+    # per layer: gate, select, [plan, stream,] align, gate/up GEMM, down GEMM, combine
+    launches = K * layers * (8 if offloaded else 6)
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": _workload(cfg, a.slots, T, layers), "model": cfg.name,
-                   "tokens_per_step": T, "slots": a.slots, "layers": layers,
-                   "global_batch": T * world, "seq_len": 1,
-                   "parallelism": "replicas" if world > 1 else "single",
+        "config": {"workload": _workload(cfg, min(a.slots, local_n), T, layers),
+                   "model": cfg.name, "tokens_per_step": T, "slots": min(a.slots, local_n),
+                   "layers": layers, "global_batch": T * world, "seq_len": 1,
+                   "parallelism": f"ep{world}" if world > 1 else "single",
+                   "local_experts": local_n, "offloaded": offloaded, "cuda_graph": graphed,
                    "cache_prefill_steps": a.prefill_steps,
                    "l2": "per-step expert weights >> 126 MB L2 (no flush needed)",
                    "build_s": round(build_s, 1)},
-        "e2e": {"value": T * K / (e2e_ms * 1e-3), "unit": UNIT,
-                "h2d_bytes_per_step": T * cfg.hidden * 2,
-                "d2h_bytes_per_step": T * cfg.hidden * 2},
-        "roofline": {"bound": "hbm", "kernel": "fused_experts (align+gate/up+down+combine)",
-                     "achieved": fused_gbs, "peak": hbm_peak, "unit": "GB/s",
-                     "frac": fused_gbs / hbm_peak, "traffic": traffic,
-                     "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)",
-                     "per_launch_ms": {"route": t_route, "gap": t_gap, "fused": t_fused},
-                     "fused_bytes_per_launch": statistics.mean(fbytes)},
+        "e2e": {"value": world * T * K / (e2e_ms * 1e-3), "unit": UNIT,
+                "h2d_bytes_per_step": world * T * cfg.hidden * 2,
+                "d2h_bytes_per_step": world * T * cfg.hidden * 2},
+        "roofline": roof,
+        "step_roofline": step_roof,
         "stream": {"misses_per_step": misses / K, "fills_per_step": fills / K,
-                   "streamed_gbs_in_gap": stream_gbs, "h2d_ceiling_gbs": h2d,
-                   "pcie_gen5_x16_gbs": 63.0},
+                   "bytes_per_step": host_step, "probe": sprobe,
+                   "h2d_ceiling_gbs": h2d, "pcie_gen5_x16_gbs": 63.0},
         "resident": resident,
         "cpu_baseline": cpu,
         "gpu_launches": launches,
@@ -385,8 +485,10 @@ def run_sluice(a):
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
-    if world > 1:
-        torch.distributed.destroy_process_group()
+    if dist:
+        dist.barrier()
+        del stack
+        dist.destroy_process_group()
 
 
 def run_reference(a):

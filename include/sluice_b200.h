@@ -174,6 +174,26 @@ int sl_fused_experts(const void* hidden, int T, int H, int I,
                      void* workspace, size_t workspace_bytes,
                      sl_stream_t stream);
 
+/* Expert-parallel half of fused_experts: this rank's experts only, fp32, no
+ * rounding, so partial outputs of all ranks can be summed (reduce-scatter)
+ * before the final bf16 rounding:
+ *   out_f32[t] = scale * sum_{j: expert_map[ids[t,j]] >= 0} w[t,j] z(t,j)
+ *              + (shared_t0 <= t < shared_t0 + shared_nt ? shared(t) : 0)
+ * Replaces the per-rank expert computation of vLLM's EP path under the
+ * reference (non-owned experts are -1 in the map: offloader.py:974-986,
+ * 2432-2435); shared experts run once per token, on the token's home rank.
+ * Same workspace as sl_fused_experts. */
+int sl_fused_experts_partial(const void* hidden, int T, int H, int I,
+                             const void* w13, const void* w2, int num_slots,
+                             int weight_dtype, const float* topk_weights,
+                             const int32_t* topk_ids, int topk,
+                             const int32_t* expert_map, int global_n,
+                             const void* shared_w13, const void* shared_w2,
+                             int n_shared, int shared_t0, int shared_nt,
+                             float routed_scaling_factor, float* out_f32,
+                             void* workspace, size_t workspace_bytes,
+                             sl_stream_t stream);
+
 /* sl_fused_experts without any device allocation. No counterpart in the
  * reference: it serves callers that cannot allocate device scratch memory for
  * a call -- a host program binding this C ABI directly (cgo, JNI, ctypes

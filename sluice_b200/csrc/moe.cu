@@ -68,7 +68,8 @@ inline WsLayout ws_layout(int T, int topk, int H, int I, int S, int n_sh, int BN
 // ------------------------------------------------------------------ align
 __global__ void __launch_bounds__(1024) align_kernel(
     const int32_t* __restrict__ ids, int T, int topk, const int32_t* __restrict__ emap,
-    int G, int S, int n_sh, int BN, const __nv_bfloat16* __restrict__ hs, int H,
+    int G, int S, int n_sh, int sh_t0, int sh_nt, int BN,
+    const __nv_bfloat16* __restrict__ hs, int H,
     int32_t* __restrict__ ws_hdr, int4* __restrict__ items, int32_t* __restrict__ pair_pos,
     __nv_bfloat16* __restrict__ X, int max_items) {
   __shared__ int cnt[kMaxCode];
@@ -79,7 +80,7 @@ __global__ void __launch_bounds__(1024) align_kernel(
   const int P = T * topk;
   const int C = S + n_sh;
   for (int c = tid; c < C; c += nthr) {
-    cnt[c] = c < S ? 0 : T;
+    cnt[c] = c < S ? 0 : sh_nt;
     cursor[c] = 0;
   }
   __syncthreads();
@@ -154,10 +155,11 @@ __global__ void __launch_bounds__(1024) align_kernel(
     const int pos = pair_pos[p];
     if (pos >= 0) dst[static_cast<long>(pos) * vrow + c] = src[static_cast<long>(p / topk) * vrow + c];
   }
-  for (long q = tid; q < static_cast<long>(n_sh) * T * vrow; q += nthr) {
+  for (long q = tid; q < static_cast<long>(n_sh) * sh_nt * vrow; q += nthr) {
     const int r = static_cast<int>(q / vrow), c = static_cast<int>(q % vrow);
-    const int i = r / T, t = r % T;
-    dst[static_cast<long>(ibase[S + i] * BN + t) * vrow + c] = src[static_cast<long>(t) * vrow + c];
+    const int i = r / sh_nt, t = r % sh_nt;
+    dst[static_cast<long>(ibase[S + i] * BN + t) * vrow + c] =
+        src[static_cast<long>(sh_t0 + t) * vrow + c];
   }
 }
 
@@ -389,10 +391,15 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(
 }
 
 // ---------------------------------------------------------------- combine
+// OUT_F32 = false: out = bf16(shared + bf16(scale * bf16(sum_j w z)))  (vLLM
+//   torch-native rounding chain, runner tail in bf16)
+// OUT_F32 = true:  out = scale * sum_j w z + shared, fp32, no rounding (the
+//   per-rank partial of expert parallelism, summed across ranks afterwards)
+template <bool OUT_F32>
 __global__ void __launch_bounds__(256) combine_kernel(
     const int32_t* __restrict__ ws_hdr, const int32_t* __restrict__ pair_pos,
     const float* __restrict__ tw, const __nv_bfloat16* __restrict__ Z, int T, int topk, int H,
-    int n_sh, float scale, __nv_bfloat16* __restrict__ out) {
+    int n_sh, int sh_t0, int sh_nt, float scale, void* __restrict__ out) {
   const int t = blockIdx.y;
   const int h0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
   if (h0 >= H || ws_hdr[WS_STATUS] != SL_OK) return;
@@ -415,33 +422,43 @@ __global__ void __launch_bounds__(256) combine_kernel(
   float o[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    float routed = sl::bf16_round(r[i]);
-    if (scale != 1.f) routed = sl::bf16_round(routed * scale);
-    o[i] = routed;
+    if constexpr (OUT_F32) {
+      o[i] = r[i] * scale;
+    } else {
+      float routed = sl::bf16_round(r[i]);
+      if (scale != 1.f) routed = sl::bf16_round(routed * scale);
+      o[i] = routed;
+    }
   }
-  if (n_sh > 0) {
-    float s[8];
+  if (n_sh > 0 && t >= sh_t0 && t < sh_t0 + sh_nt) {
+    float sv[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) s[i] = 0.f;
+    for (int i = 0; i < 8; ++i) sv[i] = 0.f;
     for (int e = 0; e < n_sh; ++e) {
-      const int pos = ws_hdr[WS_SH_BASE + e] + t;
+      const int pos = ws_hdr[WS_SH_BASE + e] + (t - sh_t0);
       const uint4 zv = *reinterpret_cast<const uint4*>(Z + static_cast<size_t>(pos) * H + h0);
       const __nv_bfloat162* z2 = reinterpret_cast<const __nv_bfloat162*>(&zv);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const float2 f = __bfloat1622float2(z2[i]);
-        s[2 * i] += f.x;
-        s[2 * i + 1] += f.y;
+        sv[2 * i] += f.x;
+        sv[2 * i + 1] += f.y;
       }
     }
 #pragma unroll
-    for (int i = 0; i < 8; ++i) o[i] = sl::bf16_round(s[i]) + o[i];
+    for (int i = 0; i < 8; ++i) o[i] = (OUT_F32 ? sv[i] : sl::bf16_round(sv[i])) + o[i];
   }
-  uint4 ov;
-  __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&ov);
+  if constexpr (OUT_F32) {
+    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(out) + static_cast<size_t>(t) * H + h0);
+    dst[0] = make_float4(o[0], o[1], o[2], o[3]);
+    dst[1] = make_float4(o[4], o[5], o[6], o[7]);
+  } else {
+    uint4 ov;
+    __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&ov);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) o2[i] = __floats2bfloat162_rn(o[2 * i], o[2 * i + 1]);
-  *reinterpret_cast<uint4*>(out + static_cast<size_t>(t) * H + h0) = ov;
+    for (int i = 0; i < 4; ++i) o2[i] = __floats2bfloat162_rn(o[2 * i], o[2 * i + 1]);
+    *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(out) + static_cast<size_t>(t) * H + h0) = ov;
+  }
 }
 
 // ------------------------------------------------------------------- host
@@ -504,13 +521,14 @@ extern "C" size_t sl_fused_experts_workspace_bytes(int T, int topk, int H, int I
   return ws_layout(T, topk, H, I, num_slots, n_shared, choose_bn(T)).total;
 }
 
-extern "C" int sl_fused_experts(const void* hidden, int T, int H, int I, const void* w13,
-                                const void* w2, int num_slots, int weight_dtype,
-                                const float* topk_weights, const int32_t* topk_ids, int topk,
-                                const int32_t* expert_map, int global_n,
-                                const void* shared_w13, const void* shared_w2, int n_shared,
-                                float routed_scaling_factor, void* out, void* workspace,
-                                size_t workspace_bytes, sl_stream_t stream) {
+namespace {
+
+int run_fused(const void* hidden, int T, int H, int I, const void* w13, const void* w2,
+              int num_slots, int weight_dtype, const float* topk_weights,
+              const int32_t* topk_ids, int topk, const int32_t* expert_map, int global_n,
+              const void* shared_w13, const void* shared_w2, int n_shared, int sh_t0,
+              int sh_nt, float routed_scaling_factor, void* out, bool out_f32,
+              void* workspace, size_t workspace_bytes, cudaStream_t st) {
   if (weight_dtype != 0) return SL_ERR_UNSUPPORTED;
   if (T < 0 || topk <= 0 || num_slots <= 0 || n_shared < 0) return SL_ERR_INVALID;
   if (H % BM || I % BM || H <= 0 || I <= 0) return SL_ERR_UNSUPPORTED;
@@ -519,6 +537,7 @@ extern "C" int sl_fused_experts(const void* hidden, int T, int H, int I, const v
   if (!hidden || !w13 || !w2 || !topk_weights || !topk_ids || !out || !workspace)
     return SL_ERR_INVALID;
   if (n_shared > 0 && (!shared_w13 || !shared_w2)) return SL_ERR_INVALID;
+  if (n_shared > 0 && (sh_t0 < 0 || sh_nt < 0 || sh_t0 + sh_nt > T)) return SL_ERR_INVALID;
   if (expert_map && global_n <= 0) return SL_ERR_INVALID;
   if ((reinterpret_cast<uintptr_t>(workspace) & 255) ||
       ((reinterpret_cast<uintptr_t>(hidden) | reinterpret_cast<uintptr_t>(out)) & 15))
@@ -533,7 +552,6 @@ extern "C" int sl_fused_experts(const void* hidden, int T, int H, int I, const v
   __nv_bfloat16* X = reinterpret_cast<__nv_bfloat16*>(ws + L.x);
   __nv_bfloat16* A = reinterpret_cast<__nv_bfloat16*>(ws + L.act);
   __nv_bfloat16* Z = reinterpret_cast<__nv_bfloat16*>(ws + L.z);
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
 
   CUtensorMap m_w13, m_w13sh, m_x, m_w2, m_w2sh, m_a;
   const int nsh = n_shared > 0 ? n_shared : 0;
@@ -550,7 +568,8 @@ extern "C" int sl_fused_experts(const void* hidden, int T, int H, int I, const v
   }
   if (!ok) return SL_ERR_INVALID;
 
-  align_kernel<<<1, 1024, 0, st>>>(topk_ids, T, topk, expert_map, global_n, num_slots, nsh, BN,
+  align_kernel<<<1, 1024, 0, st>>>(topk_ids, T, topk, expert_map, global_n, num_slots, nsh,
+                                   nsh ? sh_t0 : 0, nsh ? sh_nt : 0, BN,
                                    static_cast<const __nv_bfloat16*>(hidden), H, hdr, items,
                                    pair_pos, X, L.max_items);
   SL_LAUNCH_CHECK();
@@ -562,8 +581,43 @@ extern "C" int sl_fused_experts(const void* hidden, int T, int H, int I, const v
                                   L.max_items, st);
   if (rc != SL_OK) return rc;
   dim3 cgrid((H / 8 + 255) / 256, T);
-  combine_kernel<<<cgrid, 256, 0, st>>>(hdr, pair_pos, topk_weights, Z, T, topk, H, nsh,
-                                        routed_scaling_factor, static_cast<__nv_bfloat16*>(out));
+  if (out_f32)
+    combine_kernel<true><<<cgrid, 256, 0, st>>>(hdr, pair_pos, topk_weights, Z, T, topk, H,
+                                                nsh, sh_t0, sh_nt, routed_scaling_factor, out);
+  else
+    combine_kernel<false><<<cgrid, 256, 0, st>>>(hdr, pair_pos, topk_weights, Z, T, topk, H,
+                                                 nsh, sh_t0, sh_nt, routed_scaling_factor, out);
   SL_LAUNCH_CHECK();
   return SL_OK;
+}
+
+}  // namespace
+
+extern "C" int sl_fused_experts(const void* hidden, int T, int H, int I, const void* w13,
+                                const void* w2, int num_slots, int weight_dtype,
+                                const float* topk_weights, const int32_t* topk_ids, int topk,
+                                const int32_t* expert_map, int global_n,
+                                const void* shared_w13, const void* shared_w2, int n_shared,
+                                float routed_scaling_factor, void* out, void* workspace,
+                                size_t workspace_bytes, sl_stream_t stream) {
+  return run_fused(hidden, T, H, I, w13, w2, num_slots, weight_dtype, topk_weights, topk_ids,
+                   topk, expert_map, global_n, shared_w13, shared_w2, n_shared, 0, T,
+                   routed_scaling_factor, out, false, workspace, workspace_bytes,
+                   reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int sl_fused_experts_partial(const void* hidden, int T, int H, int I,
+                                        const void* w13, const void* w2, int num_slots,
+                                        int weight_dtype, const float* topk_weights,
+                                        const int32_t* topk_ids, int topk,
+                                        const int32_t* expert_map, int global_n,
+                                        const void* shared_w13, const void* shared_w2,
+                                        int n_shared, int shared_t0, int shared_nt,
+                                        float routed_scaling_factor, float* out_f32,
+                                        void* workspace, size_t workspace_bytes,
+                                        sl_stream_t stream) {
+  return run_fused(hidden, T, H, I, w13, w2, num_slots, weight_dtype, topk_weights, topk_ids,
+                   topk, expert_map, global_n, shared_w13, shared_w2, n_shared, shared_t0,
+                   shared_nt, routed_scaling_factor, out_f32, true, workspace,
+                   workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
 }

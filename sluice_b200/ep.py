@@ -1,0 +1,197 @@
+"""Expert parallelism for the offloaded MoE layer (one process per GPU).
+
+Experts are sharded in contiguous ranges, as vLLM's ``expert_map`` does for
+the reference (global id -> local id, -1 on other ranks; the reference honours
+it at ``offloader.py:974-986`` and skips non-owned ids in the gap,
+``2432-2435``). Every rank keeps its own host shard, slot cache and device
+planner. One decode step of a layer:
+
+1. route the rank's own tokens (gate + select_experts, replicated gate);
+2. dispatch: all-gather of every rank's (token rows, top-k weights, top-k
+   ids) — one packed NCCL all-gather; fixed size, no host sync;
+3. gap on the **post-dispatch** ids (the lesson of ``offloader.py:1192-1201``):
+   the planner sees every gathered id and plans only the ones this rank owns;
+4. ``fused_experts_partial`` over all gathered tokens: this rank's experts
+   (fp32, scaled), plus the shared experts on this rank's own token rows;
+5. combine: reduce-scatter (sum) of the fp32 partials back to each token's
+   home rank, then one bf16 rounding.
+
+This is the all-gather / reduce-scatter dispatch that vLLM uses for expert
+parallelism without an all-to-all backend, at decode token counts where
+every rank needs most tokens anyway.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from . import ops
+from .configs import MoEConfig
+
+
+def expert_shard(num_experts: int, world: int, rank: int):
+    """(first global id, local count, local_of[global]) of a contiguous shard."""
+    if num_experts % world:
+        raise ValueError(f"{num_experts} experts do not split over {world} ranks")
+    per = num_experts // world
+    lo = rank * per
+    local_of = [g - lo if lo <= g < lo + per else -1 for g in range(num_experts)]
+    return lo, per, local_of
+
+
+def pack_routing(x: torch.Tensor, tw: torch.Tensor, ti: torch.Tensor) -> torch.Tensor:
+    """One byte row per token: [hidden bf16 | topk weights f32 | topk ids i32]."""
+    T = x.shape[0]
+    return torch.cat([x.contiguous().view(torch.uint8).view(T, -1),
+                      tw.contiguous().view(torch.uint8).view(T, -1),
+                      ti.contiguous().view(torch.uint8).view(T, -1)], dim=1)
+
+
+def unpack_routing(buf: torch.Tensor, H: int, k: int):
+    n = buf.shape[0]
+    xb = 2 * H
+    x = buf[:, :xb].contiguous().view(torch.bfloat16).view(n, H)
+    tw = buf[:, xb:xb + 4 * k].contiguous().view(torch.float32).view(n, k)
+    ti = buf[:, xb + 4 * k:].contiguous().view(torch.int32).view(n, k)
+    return x, tw, ti
+
+
+def dispatch(x, tw, ti, group=None):
+    """All-gather of every rank's tokens and routing: ([N*T,H], [N*T,k], [N*T,k])."""
+    world = dist.get_world_size(group)
+    packed = pack_routing(x, tw, ti)
+    out = torch.empty((world * packed.shape[0], packed.shape[1]), dtype=torch.uint8,
+                      device=packed.device)
+    dist.all_gather_into_tensor(out, packed, group=group)
+    return unpack_routing(out, x.shape[1], tw.shape[1])
+
+
+def combine(partial: torch.Tensor, group=None) -> torch.Tensor:
+    """Sum of every rank's fp32 partial rows for this rank's tokens."""
+    world = dist.get_world_size(group)
+    out = torch.empty((partial.shape[0] // world, partial.shape[1]), dtype=partial.dtype,
+                      device=partial.device)
+    dist.reduce_scatter_tensor(out, partial, group=group)
+    return out
+
+
+class EPMoELayer:
+    """One MoE layer's expert-parallel step on this rank."""
+
+    def __init__(self, cfg: MoEConfig, router: ops.Router, cache, shared_w13, shared_w2,
+                 group=None):
+        self.cfg = cfg
+        self.router = router
+        self.cache = cache
+        self.shared_w13 = shared_w13
+        self.shared_w2 = shared_w2
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.last_ids = None
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        T = x.shape[0]
+        tw, ti, _ = self.router.route(x)
+        xg, twg, tig = dispatch(x, tw, ti, self.group)
+        self.last_ids = tig
+        self.cache.gap(tig)
+        part = ops.fused_experts_partial(
+            xg, self.cache.w13, self.cache.w2, twg, tig, self.cache.expert_map,
+            self.shared_w13, self.shared_w2, shared_t0=self.rank * T, shared_nt=T,
+            routed_scaling_factor=self.cfg.routed_scaling_factor)
+        return combine(part, self.group).to(torch.bfloat16)
+
+    __call__ = forward
+
+
+class EPDecodeStack:
+    """The MoE layers of a decoder under expert parallelism on this rank."""
+
+    def __init__(self, cfg: MoEConfig, slots: int, seed: int = 0, device="cuda",
+                 num_layers: int | None = None, group=None, protect_frac=None):
+        from . import synth
+        from .offloader import ExpertStreamOffloader
+
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.group = group
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        lo, per, local_of = expert_shard(cfg.num_experts, world, rank)
+        self.offloader = ExpertStreamOffloader(slots, protect_frac=protect_frac, fast_hit=True)
+        self.layers: list[EPMoELayer] = []
+        n = cfg.num_moe_layers if num_layers is None else num_layers
+        for li in range(n):
+            w13, w2 = synth.layer_weights(cfg, li, seed, device=self.device,
+                                          num_experts=per, expert_lo=lo)
+            cache = self.offloader.install_layer(w13, w2, global_n=cfg.num_experts,
+                                                 local_of=local_of, device=self.device)
+            del w13, w2
+            gw, lb, sb = synth.gate_params(cfg, li, seed, device=self.device)
+            sh13, sh2 = synth.shared_weights(cfg, li, seed, device=self.device)
+            self.layers.append(EPMoELayer(cfg, ops.Router(cfg.routing, gw, lb, sb), cache,
+                                          sh13, sh2, group))
+        torch.cuda.synchronize(self.device)
+        self.graph = None
+        self._static_in = None
+        self._static_out = None
+
+    def step(self, x: torch.Tensor) -> torch.Tensor:
+        h = x
+        for layer in self.layers:
+            h = h + layer(h)
+        return h
+
+    def capture(self, tokens: int) -> bool:
+        """Capture one step (NCCL collectives included) in a CUDA graph;
+        returns False (eager replay) if this stack cannot be captured."""
+        self._static_in = torch.zeros(tokens, self.cfg.hidden, dtype=torch.bfloat16,
+                                      device=self.device)
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            self.step(self._static_in)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        try:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self._static_out = self.step(self._static_in)
+            self.graph = g
+            return True
+        except Exception:
+            self.graph = None
+            torch.cuda.synchronize(self.device)
+            return False
+
+    def replay(self, x: torch.Tensor | None = None) -> torch.Tensor:
+        if x is not None:
+            self._static_in.copy_(x, non_blocking=True)
+        if self.graph is None:
+            self._static_out = self.step(self._static_in)
+        else:
+            self.graph.replay()
+        return self._static_out
+
+    def decode_step(self, x_host: torch.Tensor, out_host: torch.Tensor) -> torch.Tensor:
+        self.replay(x_host.to(self.device, non_blocking=True))
+        out_host.copy_(self._static_out, non_blocking=True)
+        return out_host
+
+    def release(self) -> None:
+        """Drop the captured graph (it holds NCCL work) before process-group teardown."""
+        self.graph = None
+
+    def check(self) -> None:
+        for layer in self.layers:
+            layer.cache.check()
+
+    def stats(self) -> dict:
+        tot = {}
+        for layer in self.layers:
+            for k, v in layer.cache.stats().items():
+                if isinstance(v, bool):
+                    continue
+                tot[k] = tot.get(k, 0) + v
+        return tot

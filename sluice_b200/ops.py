@@ -147,6 +147,41 @@ def fused_experts(hidden_states: torch.Tensor, w1: torch.Tensor, w2: torch.Tenso
 fused_experts.last_workspace = None
 
 
+def fused_experts_partial(hidden_states: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
+                          topk_weights: torch.Tensor, topk_ids: torch.Tensor,
+                          expert_map: torch.Tensor, shared_w13: torch.Tensor | None = None,
+                          shared_w2: torch.Tensor | None = None, shared_t0: int = 0,
+                          shared_nt: int = 0, routed_scaling_factor: float = 1.0,
+                          out: torch.Tensor | None = None) -> torch.Tensor:
+    """Expert-parallel partial output [T, H] fp32: this rank's experts (the
+    ones ``expert_map`` maps) scaled by ``routed_scaling_factor``, plus the
+    shared experts on rows [shared_t0, shared_t0 + shared_nt)."""
+    _need_cuda(hidden_states, w1, w2, topk_weights, topk_ids, expert_map)
+    hs = hidden_states.contiguous()
+    T, H = hs.shape
+    S, two_i, _ = w1.shape
+    I = two_i // 2
+    k = topk_ids.shape[1]
+    n_sh = 0 if shared_w13 is None else shared_w13.shape[0]
+    L = lib()
+    nbytes = L.sl_fused_experts_workspace_bytes(T, k, H, I, S, n_sh)
+    ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=hs.device)
+    if out is None:
+        out = torch.empty(T, H, dtype=torch.float32, device=hs.device)
+    tw = topk_weights.contiguous().float()
+    ti = topk_ids.contiguous().to(torch.int32)
+    check(L.sl_fused_experts_partial(ptr(hs), T, H, I, ptr(w1), ptr(w2), S, 0, ptr(tw), ptr(ti),
+                                     k, ptr(expert_map), expert_map.numel(), ptr(shared_w13),
+                                     ptr(shared_w2), n_sh, int(shared_t0), int(shared_nt),
+                                     float(routed_scaling_factor), ptr(out), ptr(ws), nbytes,
+                                     _stream()), "sl_fused_experts_partial")
+    fused_experts_partial.last_workspace = ws
+    return out
+
+
+fused_experts_partial.last_workspace = None
+
+
 def workspace_status(ws: torch.Tensor) -> int:
     """Device status word of a fused_experts workspace (synchronises)."""
     return int(ws[:4].view(torch.int32)[0].item())

@@ -1,0 +1,73 @@
+"""Expert parallelism on 2 GPUs over NCCL: each rank's layer output (its own
+tokens, experts sharded across ranks, fp32 partials reduce-scattered) must
+match the single-process oracle within the bf16 tolerance. Skipped on a box
+with fewer than 2 GPUs."""
+
+import datetime
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")]
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _rank_main(rank, world, port, out_dir):
+    import torch.distributed as dist
+
+    from oracle import moe as omoe
+    from oracle import routing as orouting
+    from sluice_b200 import configs, ep, synth
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port),
+                      NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        cfg = configs.V2_LITE
+        stack = ep.EPDecodeStack(cfg, slots=48, seed=3, num_layers=1)
+        layer = stack.layers[0]
+        w13, w2 = synth.layer_weights(cfg, 0, 3, device="cuda")
+        w13, w2 = w13.cpu(), w2.cpu()
+        sh13, sh2 = (t.cpu() for t in synth.shared_weights(cfg, 0, 3, device="cuda"))
+        tokens = synth.TokenStream(cfg.hidden, 8, seed=50 + rank)
+        errs = []
+        for _ in range(3):
+            x = tokens.next().cuda()
+            out = layer(x)
+            tw, ti, logits = layer.router.route(x)
+            torch.cuda.synchronize()
+            xc = x.cpu()
+            rc = cfg.routing
+            otw, oti = orouting.grouped_topk(logits.cpu(), rc.topk, rc.renormalize)
+            routed = omoe.fused_experts(xc, w13, w2, otw, oti)
+            shared = sum(omoe.expert_mlp(xc, sh13[i], sh2[i]).float()
+                         for i in range(cfg.n_shared)).to(torch.bfloat16)
+            ref = omoe.layer_output(routed, shared).float()
+            got = out.float().cpu()
+            errs.append(((got - ref).abs().max() / ref.abs().max()).item())
+        stack.check()
+        torch.save(torch.tensor(errs), os.path.join(out_dir, f"err{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ep2_layer_matches_oracle(tmp_path):
+    mp.start_processes(_rank_main, args=(2, _free_port(), str(tmp_path)), nprocs=2,
+                       start_method="spawn")
+    for r in range(2):
+        errs = torch.load(os.path.join(tmp_path, f"err{r}.pt"))
+        assert (errs < 2e-2).all(), errs
