@@ -57,11 +57,14 @@ def _args(argv=None):
     return ap.parse_args(argv)
 
 
-def _workload(cfg, slots, tokens, layers):
+def _workload(cfg, slots, tokens, layers, world=1):
+    local = cfg.num_experts // world
+    where = (f"{slots} GPU slots, {local - slots} per layer in host RAM" if slots < local
+             else "all resident")
+    ep = f", expert-parallel over {world} GPUs ({local} experts per rank)" if world > 1 else ""
     return (f"{cfg.name} MoE decode stack: {layers} MoE layers, H={cfg.hidden}, "
-            f"{cfg.num_experts} experts x I={cfg.moe_intermediate} ({slots} GPU slots, "
-            f"{cfg.num_experts - slots} per layer in host RAM), top-{cfg.routing.topk}, "
-            f"{cfg.n_shared} shared, c={tokens}")
+            f"{cfg.num_experts} experts x I={cfg.moe_intermediate} ({where}){ep}, "
+            f"top-{cfg.routing.topk}, {cfg.n_shared} shared, c={tokens} per GPU")
 
 
 # ------------------------------------------------------------ clock sampling
@@ -275,6 +278,16 @@ def stream_probe(stack, n_miss=12, ctas=(16, 32, 64, 128, 148)):
     return {"fills": fills, "gbs_by_ctas": out}
 
 
+def _traffic_per_launch(fbytes, cfg):
+    """DRAM bytes per fused_experts launch: the ncu-measured bytes per expert
+    (profiles/traffic.json, a smaller capture) times this run's mean experts
+    per launch (DRAM traffic grows in proportion to the experts streamed)."""
+    per = load_traffic().get("fused_experts_traffic_bytes_per_expert")
+    if not per:
+        return None
+    return per * statistics.mean(fbytes) / cfg.bytes_per_expert
+
+
 def load_traffic():
     p = os.path.join(ROOT, "profiles", "traffic.json")
     try:
@@ -313,7 +326,7 @@ def run_sluice(a):
     dist = None
     if world > 1:
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     cfg = configs.CONFIGS[a.config]
     layers = a.layers or cfg.num_moe_layers
@@ -409,7 +422,7 @@ def run_sluice(a):
         roof = {"bound": "hbm", "kernel": "fused_experts (align+gate/up+down+combine)",
                 "achieved": fused_gbs, "peak": hbm_peak, "unit": "GB/s",
                 "frac": fused_gbs / hbm_peak,
-                "traffic": load_traffic().get("fused_experts_bytes_per_launch"),
+                "traffic": _traffic_per_launch(fbytes, cfg),
                 "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)",
                 "per_launch_ms": {"route": statistics.mean(route_ms), "fused": t_fused},
                 "fused_bytes_per_launch": statistics.mean(fbytes),
@@ -462,7 +475,7 @@ def run_sluice(a):
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": _workload(cfg, min(a.slots, local_n), T, layers),
+        "config": {"workload": _workload(cfg, min(a.slots, local_n), T, layers, world),
                    "model": cfg.name, "tokens_per_step": T, "slots": min(a.slots, local_n),
                    "layers": layers, "global_batch": T * world, "seq_len": 1,
                    "parallelism": f"ep{world}" if world > 1 else "single",
