@@ -1,4 +1,6 @@
 // Library-level entry points: status strings, version, device properties.
+#include <stdlib.h>
+
 #include "common.cuh"
 
 namespace {
@@ -24,6 +26,15 @@ extern "C" const char* sl_status_string(int status) {
 }
 
 extern "C" int sl_version(void) { return 100; }
+
+// PDL on unless SLUICE_PDL=0 in the environment (read once).
+bool sl::pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("SLUICE_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
 
 extern "C" int sl_device_sm_count(void) {
   int dev = 0;

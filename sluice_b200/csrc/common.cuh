@@ -8,6 +8,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "../../include/sluice_b200.h"
 
 #define SL_CUDA_TRY(expr)                                   \
@@ -188,6 +190,39 @@ __device__ __forceinline__ uint32_t elect_one() {
       "selp.u32 %0, 1, 0, P;\n\t}"
       : "=r"(pred));
   return pred;
+}
+
+// ------------------------------------------- programmatic dependent launch
+// Every kernel of the layer chain calls pdl_wait() before it touches data an
+// earlier kernel produced, then pdl_trigger() so the next kernel in the
+// stream can be scheduled and run its own prologue. Because each kernel
+// triggers only after its wait returned, a kernel that has started knows the
+// kernel two launches back has completed (used by the down GEMM to prefetch
+// slot weights before its wait). Both are no-ops for a normal launch.
+__device__ __forceinline__ void pdl_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+bool pdl_enabled();
+
+// Launch with programmatic stream serialisation (PDL) when enabled.
+template <typename... KArgs, typename... Args>
+cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                   cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 }  // namespace sl

@@ -76,6 +76,8 @@ __global__ void __launch_bounds__(1024) align_kernel(
   __shared__ int ibase[kMaxCode + 1];
   __shared__ int cursor[kMaxCode];
   __shared__ int warp_sums[32];
+  sl::pdl_wait();
+  sl::pdl_trigger();
   const int tid = threadIdx.x, nthr = blockDim.x;
   const int P = T * topk;
   const int C = S + n_sh;
@@ -146,20 +148,38 @@ __global__ void __launch_bounds__(1024) align_kernel(
     if (s >= 0) pair_pos[p] = ibase[s] * BN + atomicAdd(&cursor[s], 1);
   }
   __syncthreads();
-  // gather token rows: routed pairs, then every token once per shared expert
+  // gather token rows: routed pairs, then every token once per shared expert;
+  // four independent 16-byte copies per thread per round
   const int vrow = H >> 3;
   const uint4* src = reinterpret_cast<const uint4*>(hs);
   uint4* dst = reinterpret_cast<uint4*>(X);
-  for (long q = tid; q < static_cast<long>(P) * vrow; q += nthr) {
-    const int p = static_cast<int>(q / vrow), c = static_cast<int>(q % vrow);
-    const int pos = pair_pos[p];
-    if (pos >= 0) dst[static_cast<long>(pos) * vrow + c] = src[static_cast<long>(p / topk) * vrow + c];
-  }
-  for (long q = tid; q < static_cast<long>(n_sh) * sh_nt * vrow; q += nthr) {
-    const int r = static_cast<int>(q / vrow), c = static_cast<int>(q % vrow);
-    const int i = r / sh_nt, t = r % sh_nt;
-    dst[static_cast<long>(ibase[S + i] * BN + t) * vrow + c] =
-        src[static_cast<long>(sh_t0 + t) * vrow + c];
+  const long n_routed = static_cast<long>(P) * vrow;
+  const long n_total = n_routed + static_cast<long>(n_sh) * sh_nt * vrow;
+  for (long q0 = tid; q0 < n_total; q0 += 4L * nthr) {
+    uint4 v[4];
+    long d[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const long q = q0 + static_cast<long>(u) * nthr;
+      d[u] = -1;
+      if (q < n_routed) {
+        const int p = static_cast<int>(q / vrow), c = static_cast<int>(q % vrow);
+        const int pos = pair_pos[p];
+        if (pos >= 0) {
+          d[u] = static_cast<long>(pos) * vrow + c;
+          v[u] = src[static_cast<long>(p / topk) * vrow + c];
+        }
+      } else if (q < n_total) {
+        const long r = (q - n_routed) / vrow;
+        const int c = static_cast<int>((q - n_routed) % vrow);
+        const int i = static_cast<int>(r / sh_nt), t = static_cast<int>(r % sh_nt);
+        d[u] = static_cast<long>(ibase[S + i] * BN + t) * vrow + c;
+        v[u] = src[static_cast<long>(sh_t0 + t) * vrow + c];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (d[u] >= 0) dst[d[u]] = v[u];
   }
 }
 
@@ -223,6 +243,14 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(
   const uint32_t tmem_base = *tmem_slot;
 
   const int m_tiles = M_total / BM;  // GATED: I/128 column blocks; else H/128
+  if constexpr (GATED) {
+    // the work items, token rows and slot weights come from the launches
+    // just before this one
+    sl::pdl_wait();
+    sl::pdl_trigger();
+  }
+  // down GEMM: items were written two launches back (align), so they may be
+  // read before the wait; its A operand (the activations) may not
   const int num_items = ws_hdr[WS_NUM_ITEMS];
   const int num_tiles = num_items * m_tiles;
   const int k_blocks = K / BK;
@@ -236,6 +264,20 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(
       uint32_t phase = 0;
       uint32_t issued_phase_mask = 0;  // stages with a TMA in flight at exit
       bool ok = true;
+      // Down GEMM under PDL: the first STAGES weight tiles are fetched before
+      // waiting on the gate/up GEMM; their activation tiles follow the wait.
+      bool waited = GATED;
+      int pend_n = 0;
+      int pend_stage[STAGES], pend_kb[STAGES], pend_row[STAGES];
+      auto flush = [&]() {
+        sl::pdl_wait();
+        sl::pdl_trigger();
+        waited = true;
+        for (int i = 0; i < pend_n; ++i)
+          sl::tma_load_2d(sB + pend_stage[i] * Cfg::kBTile, &tm_b, &full[pend_stage[i]],
+                          pend_kb[i] * BK, pend_row[i], pol_b);
+        pend_n = 0;
+      };
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         const int4 it = items[tile / m_tiles];
         const int mt = tile % m_tiles;
@@ -254,7 +296,14 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(
           sl::tma_load_2d(a0, tw, &full[stage], kb * BK, row0, pol_w);
           if constexpr (GATED)
             sl::tma_load_2d(a0 + Cfg::kATile, tw, &full[stage], kb * BK, row0 + M_total, pol_w);
-          sl::tma_load_2d(sB + stage * Cfg::kBTile, &tm_b, &full[stage], kb * BK, it.y, pol_b);
+          if (waited) {
+            sl::tma_load_2d(sB + stage * Cfg::kBTile, &tm_b, &full[stage], kb * BK, it.y, pol_b);
+          } else {
+            pend_stage[pend_n] = stage;
+            pend_kb[pend_n] = kb;
+            pend_row[pend_n] = it.y;
+            if (++pend_n == STAGES) flush();
+          }
           issued_phase_mask = (issued_phase_mask & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) {
             stage = 0;
@@ -262,6 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(
           }
         }
       }
+      if (!waited) flush();
       if (!ok) {
         atomicExch(status, SL_ERR_TIMEOUT);
         *abort_flag = 1;
@@ -400,23 +450,39 @@ __global__ void __launch_bounds__(256) combine_kernel(
     const int32_t* __restrict__ ws_hdr, const int32_t* __restrict__ pair_pos,
     const float* __restrict__ tw, const __nv_bfloat16* __restrict__ Z, int T, int topk, int H,
     int n_sh, int sh_t0, int sh_nt, float scale, void* __restrict__ out) {
+  sl::pdl_wait();
+  sl::pdl_trigger();
   const int t = blockIdx.y;
   const int h0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
   if (h0 >= H || ws_hdr[WS_STATUS] != SL_OK) return;
   float r[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) r[i] = 0.f;
-  for (int j = 0; j < topk; ++j) {
-    const int pos = pair_pos[t * topk + j];
-    if (pos < 0) continue;
-    const float w = tw[t * topk + j];
-    const uint4 zv = *reinterpret_cast<const uint4*>(Z + static_cast<size_t>(pos) * H + h0);
-    const __nv_bfloat162* z2 = reinterpret_cast<const __nv_bfloat162*>(&zv);
+  for (int j0 = 0; j0 < topk; j0 += 8) {
+    uint4 zv[8];
+    float wj[8];
+    uint32_t valid = 0;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 f = __bfloat1622float2(z2[i]);
-      r[2 * i] = __fadd_rn(r[2 * i], __fmul_rn(f.x, w));
-      r[2 * i + 1] = __fadd_rn(r[2 * i + 1], __fmul_rn(f.y, w));
+    for (int u = 0; u < 8; ++u) {
+      const int j = j0 + u;
+      const int pos = j < topk ? pair_pos[t * topk + j] : -1;
+      wj[u] = 0.f;
+      if (pos >= 0) {
+        valid |= 1u << u;
+        wj[u] = tw[t * topk + j];
+        zv[u] = *reinterpret_cast<const uint4*>(Z + static_cast<size_t>(pos) * H + h0);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      if (!((valid >> u) & 1u)) continue;
+      const __nv_bfloat162* z2 = reinterpret_cast<const __nv_bfloat162*>(&zv[u]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(z2[i]);
+        r[2 * i] = __fadd_rn(r[2 * i], __fmul_rn(f.x, wj[u]));
+        r[2 * i + 1] = __fadd_rn(r[2 * i + 1], __fmul_rn(f.y, wj[u]));
+      }
     }
   }
   float o[8];
@@ -507,9 +573,8 @@ int launch_gemm(const CUtensorMap& tw, const CUtensorMap& twsh, const CUtensorMa
   int grid = sl_device_sm_count();
   if (grid <= 0) return SL_ERR_CUDA;
   if (max_tiles < grid) grid = max_tiles > 0 ? max_tiles : 1;
-  kern<<<grid, kThreads, Cfg::kSmemBytes, st>>>(tw, twsh, tb, hdr, items, out, S, K, M_total,
-                                                out_ld, status);
-  SL_LAUNCH_CHECK();
+  SL_CUDA_TRY(sl::launch(kern, dim3(grid), dim3(kThreads), Cfg::kSmemBytes, st, tw, twsh, tb,
+                         hdr, items, out, S, K, M_total, out_ld, status));
   return SL_OK;
 }
 
@@ -568,11 +633,10 @@ int run_fused(const void* hidden, int T, int H, int I, const void* w13, const vo
   }
   if (!ok) return SL_ERR_INVALID;
 
-  align_kernel<<<1, 1024, 0, st>>>(topk_ids, T, topk, expert_map, global_n, num_slots, nsh,
-                                   nsh ? sh_t0 : 0, nsh ? sh_nt : 0, BN,
-                                   static_cast<const __nv_bfloat16*>(hidden), H, hdr, items,
-                                   pair_pos, X, L.max_items);
-  SL_LAUNCH_CHECK();
+  SL_CUDA_TRY(sl::launch(align_kernel, dim3(1), dim3(1024), 0, st, topk_ids, T, topk,
+                         expert_map, global_n, num_slots, nsh, nsh ? sh_t0 : 0,
+                         nsh ? sh_nt : 0, BN, static_cast<const __nv_bfloat16*>(hidden), H, hdr,
+                         items, pair_pos, X, L.max_items));
   int rc;
   rc = launch_gemm<16, 6, true>(m_w13, m_w13sh, m_x, hdr, items, A, num_slots, H, I, I, hdr,
                                 L.max_items, st);
@@ -581,13 +645,11 @@ int run_fused(const void* hidden, int T, int H, int I, const void* w13, const vo
                                   L.max_items, st);
   if (rc != SL_OK) return rc;
   dim3 cgrid((H / 8 + 255) / 256, T);
-  if (out_f32)
-    combine_kernel<true><<<cgrid, 256, 0, st>>>(hdr, pair_pos, topk_weights, Z, T, topk, H,
-                                                nsh, sh_t0, sh_nt, routed_scaling_factor, out);
-  else
-    combine_kernel<false><<<cgrid, 256, 0, st>>>(hdr, pair_pos, topk_weights, Z, T, topk, H,
-                                                 nsh, sh_t0, sh_nt, routed_scaling_factor, out);
-  SL_LAUNCH_CHECK();
+  SL_CUDA_TRY(sl::launch(out_f32 ? combine_kernel<true> : combine_kernel<false>, cgrid,
+                         dim3(256), 0, st, static_cast<const int32_t*>(hdr),
+                         static_cast<const int32_t*>(pair_pos), topk_weights,
+                         static_cast<const __nv_bfloat16*>(Z), T, topk, H, nsh, sh_t0, sh_nt,
+                         routed_scaling_factor, out));
   return SL_OK;
 }
 

@@ -6,10 +6,9 @@
 // called by kfirtoledo/sluice src/sluice/offloader.py:2582-2585.
 //
 // Two kernels:
-//  * gate_kernel: one warp per expert, 16 tokens per CTA row; each lane
-//    streams 16-byte chunks of the expert's weight row and dots them with
-//    every token's chunk (fp32 accumulate); logits rounded to bf16 like the
-//    bf16 gate linear.
+//  * gate_kernel: one CTA per expert and tile of 16 tokens; threads split the
+//    hidden dimension in 16-byte chunks (fp32 accumulate, CTA reduction);
+//    logits rounded to bf16 like the bf16 gate linear.
 //  * select_kernel: one warp per token; each lane owns E/32 contiguous
 //    experts; scores, group mask and top-k by warp arg-max reductions with
 //    ties to the lower expert id.
@@ -31,29 +30,41 @@ __device__ __forceinline__ void bf16x8_to_f32(const uint4& v, float (&f)[8]) {
   }
 }
 
-__global__ void __launch_bounds__(128) gate_kernel(
+// One CTA per expert (x a tile of up to kTokTile tokens): the CTA's threads
+// split the hidden dimension into 16-byte chunks, so the expert's weight row
+// is read once and every token row once per expert, with all loads of a
+// thread independent; per-token sums reduce across the CTA.
+constexpr int kGateThreads = 128;
+
+__global__ void __launch_bounds__(kGateThreads) gate_kernel(
     const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
     const float* __restrict__ logit_bias, int T, int H, int E,
     __nv_bfloat16* __restrict__ logits) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int e = blockIdx.x * 4 + warp;
+  __shared__ float part[kGateThreads / 32][kTokTile];
+  sl::pdl_wait();
+  sl::pdl_trigger();
+  const int e = blockIdx.x;
   const int t0 = blockIdx.y * kTokTile;
-  if (e >= E) return;
   const int nt = min(kTokTile, T - t0);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float acc[kTokTile];
 #pragma unroll
   for (int t = 0; t < kTokTile; ++t) acc[t] = 0.f;
   const uint4* wrow = reinterpret_cast<const uint4*>(w + static_cast<size_t>(e) * H);
+  const uint4* xb = reinterpret_cast<const uint4*>(x + static_cast<size_t>(t0) * H);
   const int nvec = H >> 3;
-  for (int v = lane; v < nvec; v += 32) {
+  for (int v = threadIdx.x; v < nvec; v += kGateThreads) {
     float wf[8];
     bf16x8_to_f32(__ldg(wrow + v), wf);
+    uint4 xv[kTokTile];
+#pragma unroll
+    for (int t = 0; t < kTokTile; ++t)
+      if (t < nt) xv[t] = __ldg(xb + static_cast<size_t>(t) * nvec + v);
 #pragma unroll
     for (int t = 0; t < kTokTile; ++t) {
       if (t < nt) {
-        const uint4* xr = reinterpret_cast<const uint4*>(x + static_cast<size_t>(t0 + t) * H);
         float xf[8];
-        bf16x8_to_f32(__ldg(xr + v), xf);
+        bf16x8_to_f32(xv[t], xf);
 #pragma unroll
         for (int i = 0; i < 8; ++i) acc[t] = fmaf(wf[i], xf[i], acc[t]);
       }
@@ -64,12 +75,15 @@ __global__ void __launch_bounds__(128) gate_kernel(
     float s = acc[t];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    acc[t] = s;
+    if (lane == 0) part[warp][t] = s;
   }
-  if (lane == 0) {
+  __syncthreads();
+  if (threadIdx.x < nt) {
+    float s = 0.f;
+#pragma unroll
+    for (int q = 0; q < kGateThreads / 32; ++q) s += part[q][threadIdx.x];
     const float b = logit_bias ? logit_bias[e] : 0.f;
-    for (int t = 0; t < nt; ++t)
-      logits[static_cast<size_t>(t0 + t) * E + e] = __float2bfloat16(acc[t] + b);
+    logits[static_cast<size_t>(t0 + threadIdx.x) * E + e] = __float2bfloat16(s + b);
   }
 }
 
@@ -92,6 +106,8 @@ __global__ void __launch_bounds__(128) select_kernel(
     const float* __restrict__ score_bias, float* __restrict__ out_w,
     int32_t* __restrict__ out_ids) {
   __shared__ float s_sel[4][kMaxE];
+  sl::pdl_wait();
+  sl::pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * 4 + warp;
   if (t >= T) return;
@@ -172,10 +188,10 @@ __global__ void __launch_bounds__(128) select_kernel(
       if (i < epl && !((gmask >> ((e0 + i) / gs)) & 1u)) sel[i] = -INFINITY;
   }
 
-  // top-k, canonical order
+  // top-k, canonical order; lane r keeps the r-th choice
   uint32_t taken = 0;
-  float wsel[32];
-  int isel[32];
+  float my_w = 0.f;
+  int my_id = 0;
   float wsum = 0.f;
   for (int r = 0; r < topk; ++r) {
     float v = -INFINITY;
@@ -202,18 +218,18 @@ __global__ void __launch_bounds__(128) select_kernel(
     }
     const int owner = (id / epl) & 31;
     wv = __shfl_sync(0xffffffffu, wv, owner);
-    wsel[r] = wv;
-    isel[r] = id;
-    wsum += wv;
-  }
-  if (lane == 0) {
-    for (int r = 0; r < topk; ++r) {
-      float wv = wsel[r];
-      if (renorm) wv = wv / wsum;
-      if (scale != 1.f) wv = wv * scale;
-      out_w[static_cast<size_t>(t) * topk + r] = wv;
-      out_ids[static_cast<size_t>(t) * topk + r] = isel[r];
+    if (lane == r) {
+      my_w = wv;
+      my_id = id;
     }
+    wsum += wv;  // ascending r: the canonical order
+  }
+  if (lane < topk) {
+    float wv = my_w;
+    if (renorm) wv = wv / wsum;
+    if (scale != 1.f) wv = wv * scale;
+    out_w[static_cast<size_t>(t) * topk + lane] = wv;
+    out_ids[static_cast<size_t>(t) * topk + lane] = my_id;
   }
 }
 
@@ -238,11 +254,11 @@ extern "C" int sl_select_experts(const void* router_logits, int T, int E, int to
   if (st != SL_OK) return st;
   if (T == 0) return SL_OK;
   if (!router_logits || !topk_weights || !topk_ids) return SL_ERR_INVALID;
-  select_kernel<<<(T + 3) / 4, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(router_logits), T, E, topk, scoring,
-      num_expert_group, topk_group, renormalize, routed_scaling_factor, score_bias,
-      topk_weights, topk_ids);
-  SL_LAUNCH_CHECK();
+  SL_CUDA_TRY(sl::launch(select_kernel, dim3((T + 3) / 4), dim3(128), 0,
+                         reinterpret_cast<cudaStream_t>(stream),
+                         static_cast<const __nv_bfloat16*>(router_logits), T, E, topk, scoring,
+                         num_expert_group, topk_group, renormalize, routed_scaling_factor,
+                         score_bias, topk_weights, topk_ids));
   return SL_OK;
 }
 
@@ -260,12 +276,11 @@ extern "C" int sl_route(const void* hidden, const void* gate_w, const float* log
   if ((reinterpret_cast<uintptr_t>(hidden) | reinterpret_cast<uintptr_t>(gate_w)) & 15)
     return SL_ERR_INVALID;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  dim3 grid((E + 3) / 4, (T + kTokTile - 1) / kTokTile);
-  gate_kernel<<<grid, 128, 0, s>>>(static_cast<const __nv_bfloat16*>(hidden),
-                                   static_cast<const __nv_bfloat16*>(gate_w),
-                                   logit_bias, T, H, E,
-                                   static_cast<__nv_bfloat16*>(router_logits_out));
-  SL_LAUNCH_CHECK();
+  dim3 grid(E, (T + kTokTile - 1) / kTokTile);
+  SL_CUDA_TRY(sl::launch(gate_kernel, grid, dim3(kGateThreads), 0, s,
+                         static_cast<const __nv_bfloat16*>(hidden),
+                         static_cast<const __nv_bfloat16*>(gate_w), logit_bias, T, H, E,
+                         static_cast<__nv_bfloat16*>(router_logits_out)));
   return sl_select_experts(router_logits_out, T, E, topk, scoring, num_expert_group,
                            topk_group, renormalize, routed_scaling_factor, score_bias,
                            topk_weights, topk_ids, stream);

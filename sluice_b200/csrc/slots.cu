@@ -74,18 +74,55 @@ __device__ inline StateView view(uint8_t* base, int S, int G, int L) {
   return v;
 }
 
+// Planner shared memory, carved at run time from the state's dimensions:
+// the id bitmap, the sorted unique ids, and copies of every state array the
+// sequential pass touches (so it never waits on global memory).
+constexpr int kPlanSmemBytes = 72 * 1024;
+
 struct PlanSmem {
-  uint32_t bitmap[kMaxGlobal / 32];
-  uint32_t word_base[kMaxGlobal / 32];
-  int32_t uniq[kMaxGlobal];
-  int32_t miss_loc[kMaxSlots + 1];
-  uint32_t stamp[kMaxSlots];
-  int32_t eis[kMaxSlots];
-  uint8_t seg[kMaxSlots];
-  uint8_t claimed[kMaxSlots];
-  int any_missing;
-  int n_uniq;
+  int* scal;          // [0] any_missing, [1] n_uniq, [2] decision
+  uint32_t* bitmap;   // [W]
+  uint32_t* word_base;
+  int32_t* uniq;      // [G]
+  int32_t* local_of;  // [G]
+  int32_t* slot_of;   // [L]
+  int32_t* miss_loc;  // [S + 1]
+  uint32_t* stamp;    // [S]
+  int32_t* eis;       // [S]
+  int32_t* free_s;    // [S]
+  uint8_t* seg;       // [S]
+  uint8_t* claimed;   // [S]
 };
+
+__host__ __device__ inline size_t plan_smem_bytes(int S, int G, int L) {
+  const size_t W = (G + 31) / 32;
+  return 16 + 8 * W + 8 * size_t(G) + 4 * size_t(L) + 4 * size_t(S + 1) + 12 * size_t(S) +
+         2 * size_t(S) + 64;
+}
+
+__device__ inline PlanSmem plan_smem(uint8_t* base, int S, int G, int L) {
+  PlanSmem m;
+  const int W = (G + 31) / 32;
+  uint8_t* p = base;
+  auto take = [&](size_t bytes) {
+    uint8_t* r = p;
+    p += (bytes + 15) & ~size_t(15);
+    return r;
+  };
+  m.scal = reinterpret_cast<int*>(take(16));
+  m.bitmap = reinterpret_cast<uint32_t*>(take(4 * W));
+  m.word_base = reinterpret_cast<uint32_t*>(take(4 * W));
+  m.uniq = reinterpret_cast<int32_t*>(take(4 * size_t(G)));
+  m.local_of = reinterpret_cast<int32_t*>(take(4 * size_t(G)));
+  m.slot_of = reinterpret_cast<int32_t*>(take(4 * size_t(L)));
+  m.miss_loc = reinterpret_cast<int32_t*>(take(4 * size_t(S + 1)));
+  m.stamp = reinterpret_cast<uint32_t*>(take(4 * size_t(S)));
+  m.eis = reinterpret_cast<int32_t*>(take(4 * size_t(S)));
+  m.free_s = reinterpret_cast<int32_t*>(take(4 * size_t(S)));
+  m.seg = take(S);
+  m.claimed = take(S);
+  return m;
+}
 
 // Least-recently-used slot of segment `want` (optionally skipping claimed
 // slots), or -1. Whole warp; stamps of live slots are unique.
@@ -116,21 +153,37 @@ __device__ inline StateView view_from_header(uint8_t* base, int& S, int& G, int&
 __global__ void __launch_bounds__(256) plan_kernel(uint8_t* state,
                                                    const int32_t* __restrict__ ids,
                                                    int num_ids, int32_t* __restrict__ emap) {
-  __shared__ PlanSmem sm;
+  extern __shared__ __align__(16) uint8_t plan_smem_raw[];
+  sl::pdl_wait();
+  sl::pdl_trigger();
   int S, G, L;
   StateView st = view_from_header(state, S, G, L);
-  if (S <= 0 || S > kMaxSlots || G <= 0 || G > kMaxGlobal || L <= 0) return;
+  if (S <= 0 || S > kMaxSlots || G <= 0 || G > kMaxGlobal || L <= 0 || L > kMaxGlobal ||
+      plan_smem_bytes(S, G, L) > kPlanSmemBytes) {
+    if (threadIdx.x == 0) st.hdr[SL_HDR_STATUS] = SL_ERR_INVALID;
+    return;
+  }
+  PlanSmem sm = plan_smem(plan_smem_raw, S, G, L);
   const int tid = threadIdx.x, nthr = blockDim.x;
   const int nwords = (G + 31) >> 5;
   for (int i = tid; i < nwords; i += nthr) sm.bitmap[i] = 0;
-  if (tid == 0) sm.any_missing = 0;
+  for (int g = tid; g < G; g += nthr) sm.local_of[g] = st.local_of[g];
+  for (int l = tid; l < L; l += nthr) sm.slot_of[l] = st.slot_of[l];
+  for (int s = tid; s < S; s += nthr) {
+    sm.seg[s] = st.seg[s];
+    sm.stamp[s] = st.stamp[s];
+    sm.eis[s] = st.eis[s];
+    sm.free_s[s] = st.free_stack[s];
+    sm.claimed[s] = 0;
+  }
+  if (tid == 0) sm.scal[0] = 0;
   __syncthreads();
   for (int p = tid; p < num_ids; p += nthr) {
     const int g = ids[p];
     if (g >= 0 && g < G) {
       atomicOr(&sm.bitmap[g >> 5], 1u << (g & 31));
-      const int loc = st.local_of[g];
-      if (loc >= 0 && st.slot_of[loc] < 0) sm.any_missing = 1;
+      const int loc = sm.local_of[g];
+      if (loc >= 0 && sm.slot_of[loc] < 0) sm.scal[0] = 1;
     }
   }
   __syncthreads();
@@ -142,24 +195,26 @@ __global__ void __launch_bounds__(256) plan_kernel(uint8_t* state,
     st.hdr[SL_HDR_FILL_COUNT] = 0;
     st.hdr[SL_HDR_LAST_MISSES] = 0;
   }
-  if ((flags & SL_PLAN_FAST_HIT) && standing && !sm.any_missing) {
+  if ((flags & SL_PLAN_FAST_HIT) && standing && !sm.scal[0]) {
     if (tid == 0) st.cnt[SL_CNT_FAST_HITS] += 1;
     return;  // all-hit: no touches, no map write (offloader.py:2409-2424)
   }
   // sorted(set(ids)): expand the bitmap in ascending order
-  if (tid == 0) {
+  if (tid < 32) {
     uint32_t run = 0;
-    for (int w = 0; w < nwords; ++w) {
-      sm.word_base[w] = run;
-      run += __popc(sm.bitmap[w]);
+    for (int w0 = 0; w0 < nwords; w0 += 32) {
+      const int w = w0 + tid;
+      const uint32_t c = w < nwords ? __popc(sm.bitmap[w]) : 0;
+      uint32_t incl = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (tid >= o) incl += n;
+      }
+      if (w < nwords) sm.word_base[w] = run + incl - c;
+      run += __shfl_sync(0xffffffffu, incl, 31);
     }
-    sm.n_uniq = static_cast<int>(run);
-  }
-  for (int s = tid; s < S; s += nthr) {
-    sm.seg[s] = st.seg[s];
-    sm.stamp[s] = st.stamp[s];
-    sm.eis[s] = st.eis[s];
-    sm.claimed[s] = 0;
+    if (tid == 0) sm.scal[1] = static_cast<int>(run);
   }
   __syncthreads();
   for (int w = tid; w < nwords; w += nthr) {
@@ -199,17 +254,17 @@ __global__ void __launch_bounds__(256) plan_kernel(uint8_t* state,
     int pcount = st.hdr[SL_HDR_PROTECTED_COUNT];
     int free_top = st.hdr[SL_HDR_FREE_TOP];
     const int cap = st.hdr[SL_HDR_PROTECTED_CAP];
-    const int U = sm.n_uniq;
+    const int U = sm.scal[1];
     int nmiss = 0;
     unsigned long long hits = 0;
     // touch hits, collect misses (offloader.py:2427-2441)
     for (int i = 0; i < U; ++i) {
       const int g = sm.uniq[i];
-      const int loc = st.local_of[g];
+      const int loc = sm.local_of[g];
       if (loc < 0) continue;  // owned by another rank
-      const int slot = st.slot_of[loc];
+      const int slot = sm.slot_of[loc];
       if (slot < 0) {
-        if (lane == 0 && nmiss <= kMaxSlots) sm.miss_loc[nmiss] = loc;
+        if (lane == 0 && nmiss <= kMaxSlots) sm.miss_loc[min(nmiss, S)] = loc;
         ++nmiss;
         continue;
       }
@@ -243,15 +298,16 @@ __global__ void __launch_bounds__(256) plan_kernel(uint8_t* state,
       }
       __syncwarp();
     }
-    // acquire a slot per miss, ascending id order (offloader.py:2442-2465)
+    // acquire a slot per miss, ascending id order (offloader.py:2442-2465);
+    // at most S misses can succeed, so S + 1 entries decide overflow
     int fc = 0;
     bool overflow = false;
-    const int nm = min(nmiss, kMaxSlots + 1);
+    const int nm = min(nmiss, S + 1);
     for (int i = 0; i < nm; ++i) {
       const int loc = sm.miss_loc[i];
       int slot = -1;
       if (free_top > 0) {
-        slot = st.free_stack[--free_top];
+        slot = sm.free_s[--free_top];
       } else {
         slot = warp_lru(sm, S, SL_SEG_PROBATION, true);
         if (slot < 0) {
@@ -266,9 +322,9 @@ __global__ void __launch_bounds__(256) plan_kernel(uint8_t* state,
       ++clock;
       if (lane == 0) {
         const int old = sm.eis[slot];
-        if (old >= 0) st.slot_of[old] = -1;
+        if (old >= 0) sm.slot_of[old] = -1;
         sm.eis[slot] = loc;
-        st.slot_of[loc] = slot;
+        sm.slot_of[loc] = slot;
         sm.seg[slot] = SL_SEG_PROBATION;
         sm.stamp[slot] = clock;
         sm.claimed[slot] = 1;
@@ -289,16 +345,17 @@ __global__ void __launch_bounds__(256) plan_kernel(uint8_t* state,
       st.cnt[SL_CNT_FILLS] += fc;
       if (overflow) st.cnt[SL_CNT_OVERFLOWS] += 1;
       else st.cnt[SL_CNT_MISSES] += nmiss;
-      sm.any_missing = overflow ? -1 : nmiss;  // reuse: map-write decision
+      sm.scal[2] = overflow ? -1 : nmiss;  // map-write decision
     }
   }
   __syncthreads();
-  const int decision = sm.any_missing;
+  const int decision = sm.scal[2];
   for (int s = tid; s < S; s += nthr) {
     st.seg[s] = sm.seg[s];
     st.stamp[s] = sm.stamp[s];
     st.eis[s] = sm.eis[s];
   }
+  for (int l = tid; l < L; l += nthr) st.slot_of[l] = sm.slot_of[l];
   if (decision >= 0 && (decision > 0 || !standing)) {
     // standing map: every resident expert -> its slot (offloader.py:2112-2123)
     for (int g = tid; g < G; g += nthr) emap[g] = -1;
@@ -335,6 +392,8 @@ __device__ __forceinline__ uint4 ld_host_nc(const uint4* p) {
 
 __global__ void __launch_bounds__(kStreamThreads) stream_kernel(const uint8_t* state,
                                                                 StreamArgs a) {
+  sl::pdl_wait();
+  sl::pdl_trigger();
   int S, G, L;
   const StateView st = view_from_header(const_cast<uint8_t*>(state), S, G, L);
   const int fc = st.hdr[SL_HDR_FILL_COUNT];
@@ -396,8 +455,10 @@ extern "C" int sl_slot_state_init(void* state, int num_slots, int global_n, int 
                                   const int32_t* free_stack, int n_free,
                                   sl_stream_t stream) {
   const int S = num_slots, G = global_n, L = local_n;
-  if (!state || S <= 0 || G <= 0 || L <= 0 || S > kMaxSlots || G > kMaxGlobal)
-    return SL_ERR_INVALID;
+  if (!state || S <= 0 || G <= 0 || L <= 0) return SL_ERR_INVALID;
+  if (S > kMaxSlots || G > kMaxGlobal || L > kMaxGlobal ||
+      plan_smem_bytes(S, G, L) > kPlanSmemBytes)
+    return SL_ERR_UNSUPPORTED;
   if (!local_of || !expert_in_slot || !seg || n_free < 0 || n_free > S ||
       (n_free > 0 && !free_stack) || protected_cap < 0 || protected_cap > S)
     return SL_ERR_INVALID;
@@ -463,9 +524,17 @@ extern "C" int sl_slot_state_init(void* state, int num_slots, int global_n, int 
 extern "C" int sl_plan_slots(void* state, const int32_t* topk_ids, int num_ids,
                              int32_t* expert_map, sl_stream_t stream) {
   if (!state || !expert_map || num_ids < 0 || (num_ids > 0 && !topk_ids)) return SL_ERR_INVALID;
-  plan_kernel<<<1, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      static_cast<uint8_t*>(state), topk_ids, num_ids, expert_map);
-  SL_LAUNCH_CHECK();
+  static int configured_dev = -1;
+  int dev = 0;
+  SL_CUDA_TRY(cudaGetDevice(&dev));
+  if (configured_dev != dev) {
+    SL_CUDA_TRY(cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kPlanSmemBytes));
+    configured_dev = dev;
+  }
+  SL_CUDA_TRY(sl::launch(plan_kernel, dim3(1), dim3(256), kPlanSmemBytes,
+                         reinterpret_cast<cudaStream_t>(stream), static_cast<uint8_t*>(state),
+                         topk_ids, num_ids, expert_map));
   return SL_OK;
 }
 
@@ -493,9 +562,9 @@ extern "C" int sl_stream_experts(const void* state, int num_params,
     if (g_default_stream_ctas <= 0) g_default_stream_ctas = 64;
     num_ctas = g_default_stream_ctas;
   }
-  stream_kernel<<<num_ctas, kStreamThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint8_t*>(state), a);
-  SL_LAUNCH_CHECK();
+  SL_CUDA_TRY(sl::launch(stream_kernel, dim3(num_ctas), dim3(kStreamThreads), 0,
+                         reinterpret_cast<cudaStream_t>(stream),
+                         static_cast<const uint8_t*>(state), a));
   return SL_OK;
 }
 
