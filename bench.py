@@ -54,6 +54,8 @@ def _args(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-resident", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="serialise the expert stream and the GEMMs (A/B)")
     return ap.parse_args(argv)
 
 
@@ -337,7 +339,8 @@ def run_sluice(a):
         stack = EPDecodeStack(cfg, slots=a.slots, seed=a.seed, num_layers=layers)
         graphed = stack.capture(tokens=T)
     else:
-        stack = MoEDecodeStack(cfg, slots=a.slots, seed=a.seed, num_layers=layers)
+        stack = MoEDecodeStack(cfg, slots=a.slots, seed=a.seed, num_layers=layers,
+                               overlap=not a.no_overlap)
         stack.capture(tokens=T)
         graphed = True
     build_s = time.perf_counter() - t_build
@@ -480,6 +483,7 @@ def run_sluice(a):
                    "layers": layers, "global_batch": T * world, "seq_len": 1,
                    "parallelism": f"ep{world}" if world > 1 else "single",
                    "local_experts": local_n, "offloaded": offloaded, "cuda_graph": graphed,
+                   "stream_overlap": offloaded and not a.no_overlap,
                    "cache_prefill_steps": a.prefill_steps,
                    "l2": "per-step expert weights >> 126 MB L2 (no flush needed)",
                    "build_s": round(build_s, 1)},

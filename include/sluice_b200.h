@@ -174,6 +174,28 @@ int sl_fused_experts(const void* hidden, int T, int H, int I,
                      void* workspace, size_t workspace_bytes,
                      sl_stream_t stream);
 
+/* sl_fused_experts in two phases, so the gap's expert stream can overlap
+ * with the experts that were already resident (the reference serialises the
+ * copy stream and the GEMM with events, offloader.py:2443-2464):
+ *   phase 0 — token grouping (items of the slots in the state's current fill
+ *             list are ordered last) and both GEMMs over the resident
+ *             experts' items;
+ *   phase 1 — both GEMMs over the streamed experts' items, then the
+ *             combine (output written here).
+ * Order sl_stream_experts (e.g. on a second stream) before phase 1 and after
+ * sl_plan_slots; phase 0 only reads slots the streamer does not write. Both
+ * calls take the same workspace. */
+int sl_fused_experts_phase(const void* hidden, int T, int H, int I,
+                           const void* w13, const void* w2, int num_slots,
+                           int weight_dtype, const float* topk_weights,
+                           const int32_t* topk_ids, int topk,
+                           const int32_t* expert_map, int global_n,
+                           const void* shared_w13, const void* shared_w2,
+                           int n_shared, float routed_scaling_factor,
+                           const void* slot_state, int phase, void* out,
+                           void* workspace, size_t workspace_bytes,
+                           sl_stream_t stream);
+
 /* Expert-parallel half of fused_experts: this rank's experts only, fp32, no
  * rounding, so partial outputs of all ranks can be summed (reduce-scatter)
  * before the final bf16 rounding:

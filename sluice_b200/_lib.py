@@ -56,6 +56,8 @@ _SIGNATURES = {
     "sl_fused_experts_workspace_bytes": (_sz, [_i, _i, _i, _i, _i, _i]),
     "sl_fused_experts": (_i, [_vp, _i, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _i, _vp,
                               _i, _vp, _vp, _i, _f, _vp, _vp, _sz, _vp]),
+    "sl_fused_experts_phase": (_i, [_vp, _i, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _i, _vp,
+                                    _i, _vp, _vp, _i, _f, _vp, _i, _vp, _vp, _sz, _vp]),
     "sl_fused_experts_partial": (_i, [_vp, _i, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _i,
                                       _vp, _i, _vp, _vp, _i, _i, _i, _f, _vp, _vp, _sz,
                                       _vp]),

@@ -27,6 +27,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "slot_state.cuh"
 
 namespace {
 
@@ -37,7 +38,10 @@ constexpr int kMaxCode = 1056;  // slots + shared experts per call
 constexpr int kMaxShared = 32;
 
 // workspace header (int32 words)
-enum { WS_STATUS = 0, WS_NUM_ITEMS = 1, WS_NUM_ROWS = 2, WS_SH_BASE = 8, WS_HDR_WORDS = 64 };
+enum {
+  WS_STATUS = 0, WS_NUM_ITEMS = 1, WS_NUM_ROWS = 2, WS_NUM_HIT_ITEMS = 3, WS_SH_BASE = 8,
+  WS_HDR_WORDS = 64
+};
 
 struct WsLayout {
   size_t items, pair_pos, x, act, z, total;
@@ -71,11 +75,14 @@ __global__ void __launch_bounds__(1024) align_kernel(
     int G, int S, int n_sh, int sh_t0, int sh_nt, int BN,
     const __nv_bfloat16* __restrict__ hs, int H,
     int32_t* __restrict__ ws_hdr, int4* __restrict__ items, int32_t* __restrict__ pair_pos,
-    __nv_bfloat16* __restrict__ X, int max_items) {
+    __nv_bfloat16* __restrict__ X, int max_items, const uint8_t* __restrict__ fill_state) {
   __shared__ int cnt[kMaxCode];
   __shared__ int ibase[kMaxCode + 1];
   __shared__ int cursor[kMaxCode];
   __shared__ int warp_sums[32];
+  __shared__ uint32_t fill_bits[kMaxCode / 32 + 1];
+  __shared__ int n_hit_items;
+  __shared__ int grp_total;
   sl::pdl_wait();
   sl::pdl_trigger();
   const int tid = threadIdx.x, nthr = blockDim.x;
@@ -99,47 +106,83 @@ __global__ void __launch_bounds__(1024) align_kernel(
     if (s >= 0) atomicAdd(&cnt[s], 1);
   }
   __syncthreads();
-  // exclusive scan of tiles per code (C <= kMaxCode; each thread two entries)
-  const int lane = tid & 31, warp = tid >> 5;
-  int a0 = 0, a1 = 0;
-  const int c0 = 2 * tid, c1 = 2 * tid + 1;
-  if (c0 < C) a0 = (cnt[c0] + BN - 1) / BN;
-  if (c1 < C) a1 = (cnt[c1] + BN - 1) / BN;
-  int v = a0 + a1;
-  int incl = v;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int n = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += n;
-  }
-  if (lane == 31) warp_sums[warp] = incl;
+  // codes whose slot is being filled by this gap's streamer go last, so the
+  // items of already-resident experts form a prefix that can run first
+  for (int w = tid; w <= kMaxCode / 32; w += nthr) fill_bits[w] = 0;
   __syncthreads();
-  if (warp == 0) {
-    int ws = warp_sums[lane];
-    int wi = ws;
+  if (fill_state != nullptr) {
+    int fS, fG, fL;
+    const StateView fv = view_from_header(const_cast<uint8_t*>(fill_state), fS, fG, fL);
+    const int nf = fv.hdr[SL_HDR_FILL_COUNT];
+    for (int f = tid; f < nf; f += nthr) {
+      const int slot = fv.fill_slot[f];
+      if (slot >= 0 && slot < S) atomicOr(&fill_bits[slot >> 5], 1u << (slot & 31));
+    }
+  }
+  __syncthreads();
+  const int lane = tid & 31, warp = tid >> 5;
+  const int c0 = 2 * tid, c1 = 2 * tid + 1;  // C <= kMaxCode <= 2 * blockDim
+  auto is_fill = [&](int c) { return ((fill_bits[c >> 5] >> (c & 31)) & 1u) != 0; };
+  auto tiles = [&](int c) { return (cnt[c] + BN - 1) / BN; };
+  // block-wide exclusive scan; `total` receives the sum over the block
+  auto block_scan = [&](int v, int& total) -> int {
+    int incl = v;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const int n = __shfl_up_sync(0xffffffffu, wi, o);
-      if (lane >= o) wi += n;
+      const int n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += n;
     }
-    warp_sums[lane] = wi - ws;  // exclusive
+    if (lane == 31) warp_sums[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      const int ws = warp_sums[lane];
+      int wi = ws;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, wi, o);
+        if (lane >= o) wi += n;
+      }
+      warp_sums[lane] = wi - ws;
+      if (lane == 31) grp_total = wi;
+    }
+    __syncthreads();
+    const int r = warp_sums[warp] + incl - v;
+    total = grp_total;
+    __syncthreads();
+    return r;
+  };
+  // group 0: resident (hit) codes; group 1: codes being filled
+  int n_hit = 0, n_fill = 0;
+  {
+    const int a0 = (c0 < C && !is_fill(c0)) ? tiles(c0) : 0;
+    const int a1 = (c1 < C && !is_fill(c1)) ? tiles(c1) : 0;
+    const int ex = block_scan(a0 + a1, n_hit);
+    if (c0 < C && !is_fill(c0)) ibase[c0] = ex;
+    if (c1 < C && !is_fill(c1)) ibase[c1] = ex + a0;
   }
-  __syncthreads();
-  const int excl = warp_sums[warp] + incl - v;
-  if (c0 < C) ibase[c0] = excl;
-  if (c1 < C) ibase[c1] = excl + a0;
-  if (tid == nthr - 1) ibase[C] = excl + v;  // total (C <= 2*nthr)
+  {
+    const int a0 = (c0 < C && is_fill(c0)) ? tiles(c0) : 0;
+    const int a1 = (c1 < C && is_fill(c1)) ? tiles(c1) : 0;
+    const int ex = block_scan(a0 + a1, n_fill);
+    if (c0 < C && is_fill(c0)) ibase[c0] = n_hit + ex;
+    if (c1 < C && is_fill(c1)) ibase[c1] = n_hit + ex + a0;
+  }
+  if (tid == 0) {
+    ibase[C] = n_hit + n_fill;
+    n_hit_items = n_hit;
+  }
   __syncthreads();
   const int n_items = ibase[C];
   if (tid == 0) {
     ws_hdr[WS_STATUS] = (n_items > max_items) ? SL_ERR_INVALID : SL_OK;
     ws_hdr[WS_NUM_ITEMS] = n_items <= max_items ? n_items : 0;
     ws_hdr[WS_NUM_ROWS] = n_items * BN;
+    ws_hdr[WS_NUM_HIT_ITEMS] = n_items <= max_items ? n_hit_items : 0;
     for (int i = 0; i < n_sh; ++i) ws_hdr[WS_SH_BASE + i] = ibase[S + i] * BN;
   }
   if (n_items > max_items) return;
   for (int c = tid; c < C; c += nthr) {
-    const int nt = ibase[c + 1] - ibase[c];
+    const int nt = (cnt[c] + BN - 1) / BN;
     for (int i = 0; i < nt; ++i)
       items[ibase[c] + i] = make_int4(c, (ibase[c] + i) * BN, min(BN, cnt[c] - i * BN), 0);
   }
@@ -204,7 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(
     const __grid_constant__ CUtensorMap tm_b, const int32_t* __restrict__ ws_hdr,
     const int4* __restrict__ items, __nv_bfloat16* __restrict__ out, int S, int K,
     int M_total /* rows of one expert's weight block in this GEMM's view */,
-    int out_ld, int32_t* __restrict__ status) {
+    int out_ld, int32_t* __restrict__ status, int phase) {
   using Cfg = GemmCfg<BN, STAGES, GATED>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -251,8 +294,13 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(
   }
   // down GEMM: items were written two launches back (align), so they may be
   // read before the wait; its A operand (the activations) may not
+  // phase -1: every item; 0: items of resident experts; 1: items of experts
+  // streamed in by this gap (they follow the resident ones)
   const int num_items = ws_hdr[WS_NUM_ITEMS];
-  const int num_tiles = num_items * m_tiles;
+  const int n_hit = ws_hdr[WS_NUM_HIT_ITEMS];
+  const int item_lo = phase == 1 ? n_hit : 0;
+  const int item_hi = phase == 0 ? n_hit : num_items;
+  const int num_tiles = (item_hi > item_lo ? item_hi - item_lo : 0) * m_tiles;
   const int k_blocks = K / BK;
 
   if (warp == 0) {
@@ -279,7 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(
         pend_n = 0;
       };
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int4 it = items[tile / m_tiles];
+        const int4 it = items[item_lo + tile / m_tiles];
         const int mt = tile % m_tiles;
         const bool sh = it.x >= S;
         const CUtensorMap* tw = sh ? &tm_wsh : &tm_w;
@@ -387,7 +435,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(
         break;
       }
       sl::tc_fence_after();
-      const int4 it = items[tile / m_tiles];
+      const int4 it = items[item_lo + tile / m_tiles];
       const int mt = tile % m_tiles;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * Cfg::kAccCols;
       float v0[BN];
@@ -558,7 +606,8 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, u
 template <int BN, int STAGES, bool GATED>
 int launch_gemm(const CUtensorMap& tw, const CUtensorMap& twsh, const CUtensorMap& tb,
                 const int32_t* hdr, const int4* items, __nv_bfloat16* out, int S, int K,
-                int M_total, int out_ld, int32_t* status, int max_items, cudaStream_t st) {
+                int M_total, int out_ld, int32_t* status, int max_items, cudaStream_t st,
+                int phase) {
   using Cfg = GemmCfg<BN, STAGES, GATED>;
   auto kern = moe_gemm_kernel<BN, STAGES, GATED>;
   static int configured_dev = -1;
@@ -574,7 +623,7 @@ int launch_gemm(const CUtensorMap& tw, const CUtensorMap& twsh, const CUtensorMa
   if (grid <= 0) return SL_ERR_CUDA;
   if (max_tiles < grid) grid = max_tiles > 0 ? max_tiles : 1;
   SL_CUDA_TRY(sl::launch(kern, dim3(grid), dim3(kThreads), Cfg::kSmemBytes, st, tw, twsh, tb,
-                         hdr, items, out, S, K, M_total, out_ld, status));
+                         hdr, items, out, S, K, M_total, out_ld, status, phase));
   return SL_OK;
 }
 
@@ -593,7 +642,8 @@ int run_fused(const void* hidden, int T, int H, int I, const void* w13, const vo
               const int32_t* topk_ids, int topk, const int32_t* expert_map, int global_n,
               const void* shared_w13, const void* shared_w2, int n_shared, int sh_t0,
               int sh_nt, float routed_scaling_factor, void* out, bool out_f32,
-              void* workspace, size_t workspace_bytes, cudaStream_t st) {
+              void* workspace, size_t workspace_bytes, cudaStream_t st,
+              const void* fill_state = nullptr, int phase = -1) {
   if (weight_dtype != 0) return SL_ERR_UNSUPPORTED;
   if (T < 0 || topk <= 0 || num_slots <= 0 || n_shared < 0) return SL_ERR_INVALID;
   if (H % BM || I % BM || H <= 0 || I <= 0) return SL_ERR_UNSUPPORTED;
@@ -633,17 +683,20 @@ int run_fused(const void* hidden, int T, int H, int I, const void* w13, const vo
   }
   if (!ok) return SL_ERR_INVALID;
 
-  SL_CUDA_TRY(sl::launch(align_kernel, dim3(1), dim3(1024), 0, st, topk_ids, T, topk,
-                         expert_map, global_n, num_slots, nsh, nsh ? sh_t0 : 0,
-                         nsh ? sh_nt : 0, BN, static_cast<const __nv_bfloat16*>(hidden), H, hdr,
-                         items, pair_pos, X, L.max_items));
+  if (phase != 1)
+    SL_CUDA_TRY(sl::launch(align_kernel, dim3(1), dim3(1024), 0, st, topk_ids, T, topk,
+                           expert_map, global_n, num_slots, nsh, nsh ? sh_t0 : 0,
+                           nsh ? sh_nt : 0, BN, static_cast<const __nv_bfloat16*>(hidden), H,
+                           hdr, items, pair_pos, X, L.max_items,
+                           static_cast<const uint8_t*>(fill_state)));
   int rc;
   rc = launch_gemm<16, 6, true>(m_w13, m_w13sh, m_x, hdr, items, A, num_slots, H, I, I, hdr,
-                                L.max_items, st);
+                                L.max_items, st, phase);
   if (rc != SL_OK) return rc;
   rc = launch_gemm<16, 12, false>(m_w2, m_w2sh, m_a, hdr, items, Z, num_slots, I, H, H, hdr,
-                                  L.max_items, st);
+                                  L.max_items, st, phase);
   if (rc != SL_OK) return rc;
+  if (phase == 0) return SL_OK;
   dim3 cgrid((H / 8 + 255) / 256, T);
   SL_CUDA_TRY(sl::launch(out_f32 ? combine_kernel<true> : combine_kernel<false>, cgrid,
                          dim3(256), 0, st, static_cast<const int32_t*>(hdr),
@@ -682,4 +735,21 @@ extern "C" int sl_fused_experts_partial(const void* hidden, int T, int H, int I,
                    topk, expert_map, global_n, shared_w13, shared_w2, n_shared, shared_t0,
                    shared_nt, routed_scaling_factor, out_f32, true, workspace,
                    workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int sl_fused_experts_phase(const void* hidden, int T, int H, int I, const void* w13,
+                                      const void* w2, int num_slots, int weight_dtype,
+                                      const float* topk_weights, const int32_t* topk_ids,
+                                      int topk, const int32_t* expert_map, int global_n,
+                                      const void* shared_w13, const void* shared_w2,
+                                      int n_shared, float routed_scaling_factor,
+                                      const void* slot_state, int phase, void* out,
+                                      void* workspace, size_t workspace_bytes,
+                                      sl_stream_t stream) {
+  if (phase != 0 && phase != 1) return SL_ERR_INVALID;
+  if (!slot_state) return SL_ERR_INVALID;
+  return run_fused(hidden, T, H, I, w13, w2, num_slots, weight_dtype, topk_weights, topk_ids,
+                   topk, expert_map, global_n, shared_w13, shared_w2, n_shared, 0, T,
+                   routed_scaling_factor, out, false, workspace, workspace_bytes,
+                   reinterpret_cast<cudaStream_t>(stream), slot_state, phase);
 }

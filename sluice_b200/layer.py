@@ -26,8 +26,12 @@ from .offloader import ExpertStreamOffloader, SlotCache
 class SluiceMoELayer:
     def __init__(self, cfg: MoEConfig, router: ops.Router, cache: SlotCache,
                  shared_w13: torch.Tensor | None, shared_w2: torch.Tensor | None,
-                 layer_idx: int = 0):
+                 layer_idx: int = 0, overlap: bool = True, stream_ctas: int = 16):
         self.cfg = cfg
+        # overlap the gap's expert stream with the resident experts' GEMMs
+        self.overlap = overlap and not cache.static_full
+        self.stream_ctas = stream_ctas
+        self._side = torch.cuda.Stream(device=cache.device) if self.overlap else None
         self.router = router
         self.cache = cache
         self.shared_w13 = shared_w13
@@ -39,12 +43,36 @@ class SluiceMoELayer:
     def forward(self, hs: torch.Tensor) -> torch.Tensor:
         tw, ti, logits = self.router.route(hs)
         self.last_ids, self.last_logits = ti, logits
+        if self.overlap:
+            return self._forward_overlapped(hs, tw, ti)
         self.cache.gap(ti)
         return ops.fused_experts(hs, self.cache.w13, self.cache.w2, tw, ti,
                                  global_num_experts=self.cfg.num_experts,
                                  expert_map=self.cache.expert_map,
                                  shared_w13=self.shared_w13, shared_w2=self.shared_w2,
                                  routed_scaling_factor=self.cfg.routed_scaling_factor)
+
+    def _forward_overlapped(self, hs, tw, ti):
+        """plan -> [stream on a side stream || resident experts' GEMMs] ->
+        streamed experts' GEMMs + combine."""
+        c, cfg = self.cache, self.cfg
+        main = torch.cuda.current_stream()
+        c.plan(ti)
+        self._side.wait_stream(main)
+        with torch.cuda.stream(self._side):
+            c.stream(self.stream_ctas)
+        hs = hs.contiguous()
+        T, H = hs.shape
+        ws = ops.fused_experts_workspace(T, ti.shape[1], H, c.w13.shape[1] // 2,
+                                         c.num_slots, 0 if self.shared_w13 is None
+                                         else self.shared_w13.shape[0], hs.device)
+        out = torch.empty_like(hs)
+        args = (hs, c.w13, c.w2, tw, ti, c.expert_map, c.state)
+        kw = dict(shared_w13=self.shared_w13, shared_w2=self.shared_w2,
+                  routed_scaling_factor=cfg.routed_scaling_factor)
+        ops.fused_experts_phase(*args, 0, ws, out, **kw)
+        main.wait_stream(self._side)
+        return ops.fused_experts_phase(*args, 1, ws, out, **kw)
 
     __call__ = forward
 
@@ -54,7 +82,7 @@ class MoEDecodeStack:
 
     def __init__(self, cfg: MoEConfig, slots: int, seed: int = 0, device="cuda",
                  protect_frac: float | None = None, fast_hit: bool = True,
-                 num_layers: int | None = None):
+                 num_layers: int | None = None, overlap: bool = True):
         self.cfg = cfg
         self.device = torch.device(device)
         self.offloader = ExpertStreamOffloader(slots, protect_frac=protect_frac,
@@ -68,7 +96,8 @@ class MoEDecodeStack:
             gw, lb, sb = synth.gate_params(cfg, li, seed, device=self.device)
             router = ops.Router(cfg.routing, gw, lb, sb)
             sh13, sh2 = synth.shared_weights(cfg, li, seed, device=self.device)
-            self.layers.append(SluiceMoELayer(cfg, router, cache, sh13, sh2, li))
+            self.layers.append(SluiceMoELayer(cfg, router, cache, sh13, sh2, li,
+                                              overlap=overlap))
         torch.cuda.synchronize(self.device)
         self.graph = None
         self._static_in = None

@@ -159,14 +159,21 @@ class SlotCache:
         """Plan slots for this step's ids and stream the misses (async)."""
         if self.static_full:
             return
+        self.plan(topk_ids)
+        self.stream(stream_ctas)
+
+    def plan(self, topk_ids: torch.Tensor) -> None:
+        """The gap's slot planning on the current stream (updates the map)."""
         ids = topk_ids if topk_ids.dtype == torch.int32 and topk_ids.is_contiguous() \
             else topk_ids.contiguous().to(torch.int32)
-        s = torch.cuda.current_stream().cuda_stream
-        L = lib()
-        check(L.sl_plan_slots(ptr(self.state), ptr(ids), ids.numel(), ptr(self.expert_map), s),
-              "sl_plan_slots")
+        check(lib().sl_plan_slots(ptr(self.state), ptr(ids), ids.numel(), ptr(self.expert_map),
+                                  torch.cuda.current_stream().cuda_stream), "sl_plan_slots")
+
+    def stream(self, stream_ctas: int = 0) -> None:
+        """Stream the last plan's fills on the current stream."""
         n, src, dst, nb = self._stream_args
-        check(L.sl_stream_experts(ptr(self.state), n, src, dst, nb, int(stream_ctas), s),
+        check(lib().sl_stream_experts(ptr(self.state), n, src, dst, nb, int(stream_ctas),
+                                      torch.cuda.current_stream().cuda_stream),
               "sl_stream_experts")
 
     # -- host-side views (synchronise) ----------------------------------------

@@ -147,6 +147,37 @@ def fused_experts(hidden_states: torch.Tensor, w1: torch.Tensor, w2: torch.Tenso
 fused_experts.last_workspace = None
 
 
+def fused_experts_phase(hidden_states: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
+                        topk_weights: torch.Tensor, topk_ids: torch.Tensor,
+                        expert_map: torch.Tensor, slot_state: torch.Tensor, phase: int,
+                        workspace: torch.Tensor, out: torch.Tensor,
+                        shared_w13: torch.Tensor | None = None,
+                        shared_w2: torch.Tensor | None = None,
+                        routed_scaling_factor: float = 1.0) -> torch.Tensor:
+    """One phase of ``fused_experts`` split around the expert stream: phase 0
+    computes the already-resident experts, phase 1 the streamed ones and the
+    combine into ``out``. Both phases take the same ``workspace``
+    (``fused_experts_workspace``)."""
+    hs = hidden_states
+    T, H = hs.shape
+    S, two_i, _ = w1.shape
+    k = topk_ids.shape[1]
+    n_sh = 0 if shared_w13 is None else shared_w13.shape[0]
+    check(lib().sl_fused_experts_phase(ptr(hs), T, H, two_i // 2, ptr(w1), ptr(w2), S, 0,
+                                       ptr(topk_weights), ptr(topk_ids), k, ptr(expert_map),
+                                       expert_map.numel(), ptr(shared_w13), ptr(shared_w2),
+                                       n_sh, float(routed_scaling_factor), ptr(slot_state),
+                                       int(phase), ptr(out), ptr(workspace), workspace.numel(),
+                                       _stream()), "sl_fused_experts_phase")
+    return out
+
+
+def fused_experts_workspace(T: int, topk: int, H: int, I: int, slots: int, n_shared: int,
+                            device) -> torch.Tensor:
+    n = lib().sl_fused_experts_workspace_bytes(T, topk, H, I, slots, n_shared)
+    return torch.empty(max(n, 256), dtype=torch.uint8, device=device)
+
+
 def fused_experts_partial(hidden_states: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
                           topk_weights: torch.Tensor, topk_ids: torch.Tensor,
                           expert_map: torch.Tensor, shared_w13: torch.Tensor | None = None,

@@ -16,16 +16,18 @@ from test_moe_gpu import assert_moe_close
 pytestmark = pytest.mark.gpu
 
 
+@pytest.mark.parametrize("overlap", [True, False], ids=["overlap", "serial"])
 @pytest.mark.parametrize("cfg,slots,T", [(configs.V2_LITE, 48, 8),
                                          (configs.QWEN3_30B_A3B, 64, 8)],
                          ids=["v2lite_s48", "qwen3_s64"])
-def test_layer_steps_with_misses_match_oracle(cfg, slots, T):
+def test_layer_steps_with_misses_match_oracle(cfg, slots, T, overlap):
     w13, w2 = synth.layer_weights(cfg, 0, seed=2, device="cuda")
     gw, lb, sb = synth.gate_params(cfg, 0, seed=2, device="cuda")
     sh13, sh2 = synth.shared_weights(cfg, 0, seed=2, device="cuda")
     off = ExpertStreamOffloader(slots, protect_frac=0.5, fast_hit=True)
     cache = off.install_layer(w13, w2, device="cuda")
-    layer = SluiceMoELayer(cfg, ops.Router(cfg.routing, gw, lb, sb), cache, sh13, sh2)
+    layer = SluiceMoELayer(cfg, ops.Router(cfg.routing, gw, lb, sb), cache, sh13, sh2,
+                           overlap=overlap)
     model = SlotPolicyModel(cache.num_slots, list(range(cfg.num_experts)), cfg.num_experts,
                             0.5, True)
     w13c, w2c = w13.cpu(), w2.cpu()
