@@ -157,7 +157,8 @@ int sl_host_free(void* host_ptr);
  * e = expert_map[topk_ids[t,j]] (a -1 entry contributes nothing) and shared
  * experts given as n_shared experts of the same I (shared_w13 [n_shared,2I,H],
  * shared_w2 [n_shared,H,I]; NULL/0 for none). expert_map NULL means ids are
- * slot indices. weight_dtype 0 = bf16 (fp8 is not in this build yet).
+ * slot indices. weight_dtype must be SL_WEIGHTS_BF16 here (fp8 block-scaled
+ * weights go through sl_fused_experts_ex).
  * Tensor-core GEMMs (tcgen05, TMEM accumulators, TMA-fed). Limits:
  * H % 128 == 0, I % 128 == 0, num_slots + n_shared <= 1024.
  * workspace: device memory of at least sl_fused_experts_workspace_bytes(...),
@@ -173,6 +174,40 @@ int sl_fused_experts(const void* hidden, int T, int H, int I,
                      int n_shared, float routed_scaling_factor, void* out,
                      void* workspace, size_t workspace_bytes,
                      sl_stream_t stream);
+
+/* Expert weights of one layer for sl_fused_experts_ex. */
+enum { SL_WEIGHTS_BF16 = 0, SL_WEIGHTS_FP8_BLOCK128 = 1 };
+typedef struct sl_expert_weights {
+  const void* w13;                /* [num_slots, 2I, H] bf16 or fp8 e4m3 */
+  const void* w2;                 /* [num_slots, H, I] */
+  const float* w13_scale;         /* fp8: [num_slots, 2I/128, H/128] */
+  const float* w2_scale;          /* fp8: [num_slots, H/128, I/128] */
+  int num_slots;
+  const void* shared_w13;         /* [n_shared, 2I, H] or NULL */
+  const void* shared_w2;          /* [n_shared, H, I] or NULL */
+  const float* shared_w13_scale;  /* fp8 */
+  const float* shared_w2_scale;   /* fp8 */
+  int n_shared;
+  int dtype;                      /* SL_WEIGHTS_* */
+} sl_expert_weights;
+
+/* The general form of fused_experts (offloader.py:2590-2602 with vLLM's
+ * block-fp8 MoE layout, fused_moe.py:1587-1632 w1_scale / w2_scale /
+ * block_shape=[128,128]): bf16 or fp8 e4m3 weights with fp32 128x128 block
+ * scales (dequantised per tile into bf16 for the tensor cores; activations
+ * stay bf16), shared experts on tokens [shared_t0, shared_t0 + shared_nt)
+ * (shared_nt < 0: every token), optional phase split around the expert
+ * stream (phase -1: whole call; 0 / 1 as sl_fused_experts_phase, slot_state
+ * required), and out_f32 != 0 for the expert-parallel fp32 partial (as
+ * sl_fused_experts_partial). */
+int sl_fused_experts_ex(const void* hidden, int T, int H, int I,
+                        const sl_expert_weights* weights,
+                        const float* topk_weights, const int32_t* topk_ids,
+                        int topk, const int32_t* expert_map, int global_n,
+                        float routed_scaling_factor, int shared_t0,
+                        int shared_nt, const void* slot_state, int phase,
+                        int out_f32, void* out, void* workspace,
+                        size_t workspace_bytes, sl_stream_t stream);
 
 /* sl_fused_experts in two phases, so the gap's expert stream can overlap
  * with the experts that were already resident (the reference serialises the

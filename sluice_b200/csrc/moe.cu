@@ -23,6 +23,8 @@
 //   combine  out[t] = shared(t) + scale * sum_j w[t,j] z(t,j).
 // Warp roles in the GEMMs: warp 0 TMA producer, warp 1 MMA issuer (one
 // thread) and TMEM owner, warps 2-5 epilogue (TMEM lanes 32*(warp%4)..).
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
 #include <cudaTypedefs.h>
 #include <mutex>
 
@@ -488,6 +490,347 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(
   }
 }
 
+// --------------------------------------------------------- fp8 weight GEMM
+// fp8 e4m3 expert weights with fp32 128x128 block scales (vLLM's block-fp8
+// MoE layout: w13_scale [E, 2I/128, H/128], w2_scale [E, H/128, I/128]).
+// TMA brings raw fp8 weight tiles (128 rows x 64 K, unswizzled) into a raw
+// ring; a converter warpgroup dequantises each tile (fp8 -> fp32 x block
+// scale -> bf16) into the 128B-swizzled bf16 layout the MMA reads; the MMA,
+// epilogue and token tiles are those of the bf16 kernel (bf16 activations,
+// fp32 accumulation in TMEM). Roles: warp 0 producer, warp 1 MMA + TMEM,
+// warps 2-5 epilogue, warps 6-9 converter.
+constexpr int kFp8Threads = 320;
+
+template <int BN, int RSTAGES, int CSTAGES, bool GATED>
+struct Fp8Cfg {
+  static constexpr int kNumA = GATED ? 2 : 1;
+  static constexpr int kRawA = BM * BK;                    // bytes (fp8)
+  static constexpr int kBTile = BN * BK;                   // bf16 elements
+  static constexpr int kCvtA = BM * BK;                    // bf16 elements
+  static constexpr int kRawBytes = kNumA * kRawA;          // per raw stage
+  static constexpr int kTxBytes = kRawBytes + kBTile * 2;  // TMA bytes per stage
+  static constexpr int kAccCols = GATED ? 2 * BN : BN;
+  static constexpr int kTmemCols = (2 * kAccCols) <= 32 ? 32 : (2 * kAccCols) <= 64 ? 64
+                                   : (2 * kAccCols) <= 128 ? 128 : 256;
+  static constexpr int kSmemBytes = CSTAGES * kNumA * kCvtA * 2 + RSTAGES * kBTile * 2 +
+                                    RSTAGES * kRawBytes + 1024 + 512;
+};
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// 16 fp8 e4m3 values -> 16 floats
+__device__ __forceinline__ void fp8x16_to_f32(const uint4& v, float (&f)[16]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const __nv_fp8x2_storage_t pair = static_cast<__nv_fp8x2_storage_t>(w[q] >> (16 * h));
+      const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(pair, __NV_E4M3);
+      const float2 ff = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+      f[4 * q + 2 * h] = ff.x;
+      f[4 * q + 2 * h + 1] = ff.y;
+    }
+  }
+}
+
+template <int BN, int RSTAGES, int CSTAGES, bool GATED>
+__global__ void __launch_bounds__(kFp8Threads, 1) moe_gemm_fp8_kernel(
+    const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_wsh,
+    const __grid_constant__ CUtensorMap tm_b, const float* __restrict__ w_scale,
+    const float* __restrict__ wsh_scale, const int32_t* __restrict__ ws_hdr,
+    const int4* __restrict__ items, __nv_bfloat16* __restrict__ out, int S, int K,
+    int M_total, int out_ld, int32_t* __restrict__ status, int phase) {
+  using Cfg = Fp8Cfg<BN, RSTAGES, CSTAGES, GATED>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  __nv_bfloat16* sC = reinterpret_cast<__nv_bfloat16*>(smem);        // [C][kNumA][BM*BK]
+  __nv_bfloat16* sB = sC + CSTAGES * Cfg::kNumA * Cfg::kCvtA;        // [R][BN*BK]
+  uint8_t* sR = reinterpret_cast<uint8_t*>(sB + RSTAGES * Cfg::kBTile);  // [R][kNumA][BM*BK]
+  uint64_t* raw_full = reinterpret_cast<uint64_t*>(sR + RSTAGES * Cfg::kRawBytes);
+  uint64_t* raw_empty = raw_full + RSTAGES;
+  uint64_t* b_empty = raw_empty + RSTAGES;
+  uint64_t* cvt_full = b_empty + RSTAGES;
+  uint64_t* cvt_empty = cvt_full + CSTAGES;
+  uint64_t* tfull = cvt_empty + CSTAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* mma_done = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < RSTAGES; ++s) {
+      sl::mbar_init(&raw_full[s], 1);
+      sl::mbar_init(&raw_empty[s], 4);
+      sl::mbar_init(&b_empty[s], 1);
+    }
+    for (int s = 0; s < CSTAGES; ++s) {
+      sl::mbar_init(&cvt_full[s], 4);
+      sl::mbar_init(&cvt_empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      sl::mbar_init(&tfull[a], 1);
+      sl::mbar_init(&tempty[a], 4);
+    }
+    sl::mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    sl::fence_barrier_init();
+    sl::tma_prefetch_desc(&tm_w);
+    sl::tma_prefetch_desc(&tm_wsh);
+    sl::tma_prefetch_desc(&tm_b);
+  }
+  if (warp == 1) sl::tmem_alloc(tmem_slot, Cfg::kTmemCols);
+  sl::tc_fence_before();
+  __syncthreads();
+  sl::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  sl::pdl_wait();
+  sl::pdl_trigger();
+
+  const int m_tiles = M_total / BM;
+  const int num_items = ws_hdr[WS_NUM_ITEMS];
+  const int n_hit = ws_hdr[WS_NUM_HIT_ITEMS];
+  const int item_lo = phase == 1 ? n_hit : 0;
+  const int item_hi = phase == 0 ? n_hit : num_items;
+  const int num_tiles = (item_hi > item_lo ? item_hi - item_lo : 0) * m_tiles;
+  const int k_blocks = K / BK;
+  const int kscale = K / 128;  // scale blocks along K
+
+  if (warp == 0) {
+    // ------------------------------------------------------ TMA producer
+    if (sl::elect_one()) {
+      const uint64_t pol_w = sl::policy_evict_first();
+      const uint64_t pol_b = sl::policy_evict_last();
+      int r = 0;
+      uint32_t rph = 0;
+      uint32_t issued_mask = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int4 it = items[item_lo + tile / m_tiles];
+        const int mt = tile % m_tiles;
+        const bool sh = it.x >= S;
+        const CUtensorMap* tw = sh ? &tm_wsh : &tm_w;
+        const int e = sh ? it.x - S : it.x;
+        const int row0 = GATED ? e * 2 * M_total + mt * BM : e * M_total + mt * BM;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (*abort_flag || !sl::mbar_wait(&raw_empty[r], rph ^ 1) ||
+              !sl::mbar_wait(&b_empty[r], rph ^ 1)) {
+            ok = false;
+            break;
+          }
+          sl::mbar_arrive_expect_tx(&raw_full[r], Cfg::kTxBytes);
+          uint8_t* a0 = sR + r * Cfg::kRawBytes;
+          sl::tma_load_2d(a0, tw, &raw_full[r], kb * BK, row0, pol_w);
+          if constexpr (GATED)
+            sl::tma_load_2d(a0 + Cfg::kRawA, tw, &raw_full[r], kb * BK, row0 + M_total, pol_w);
+          sl::tma_load_2d(sB + r * Cfg::kBTile, &tm_b, &raw_full[r], kb * BK, it.y, pol_b);
+          issued_mask = (issued_mask & ~(1u << r)) | (rph << r);
+          if (++r == RSTAGES) {
+            r = 0;
+            rph ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        atomicExch(status, SL_ERR_TIMEOUT);
+        *abort_flag = 1;
+        for (int s = 0; s < RSTAGES; ++s) (void)sl::mbar_wait(&raw_full[s], (issued_mask >> s) & 1u);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------- MMA issuer
+    if (sl::elect_one()) {
+      constexpr uint32_t idesc = sl::umma_idesc_bf16(BM, BN);
+      int r = 0, c = 0;
+      uint32_t rph = 0, cph = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        if (*abort_flag || !sl::mbar_wait(&tempty[acc], acc_phase ^ 1)) {
+          ok = false;
+          break;
+        }
+        sl::tc_fence_after();
+        const uint32_t d0 = tmem_base + acc * Cfg::kAccCols;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (*abort_flag || !sl::mbar_wait(&cvt_full[c], cph)) {
+            ok = false;
+            break;
+          }
+          sl::tc_fence_after();
+          const uint32_t a_addr = sl::smem_u32(sC + (c * Cfg::kNumA) * Cfg::kCvtA);
+          const uint32_t b_addr = sl::smem_u32(sB + r * Cfg::kBTile);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t bd = sl::umma_desc_sw128(b_addr + k * 32);
+            const uint32_t accum = (kb | k) != 0;
+            sl::umma_bf16(d0, sl::umma_desc_sw128(a_addr + k * 32), bd, idesc, accum);
+            if constexpr (GATED)
+              sl::umma_bf16(d0 + BN, sl::umma_desc_sw128(a_addr + Cfg::kCvtA * 2 + k * 32), bd,
+                            idesc, accum);
+          }
+          sl::umma_commit(&cvt_empty[c]);
+          sl::umma_commit(&b_empty[r]);
+          if (++c == CSTAGES) {
+            c = 0;
+            cph ^= 1;
+          }
+          if (++r == RSTAGES) {
+            r = 0;
+            rph ^= 1;
+          }
+        }
+        if (!ok) break;
+        sl::umma_commit(&tfull[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      if (!ok) {
+        atomicExch(status, SL_ERR_TIMEOUT);
+        *abort_flag = 1;
+      }
+      sl::umma_commit(mma_done);
+      (void)sl::mbar_wait(mma_done, 0);
+    }
+  } else if (warp >= 6) {
+    // ---------------------------------------------------------- converter
+    const int row = threadIdx.x - 6 * 32;  // 0..127: weight row within the tile
+    int r = 0, c = 0;
+    uint32_t rph = 0, cph = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      const int4 it = items[item_lo + tile / m_tiles];
+      const int mt = tile % m_tiles;
+      const bool sh = it.x >= S;
+      const int e = sh ? it.x - S : it.x;
+      const float* scale = sh ? wsh_scale : w_scale;
+      // scale rows: GATED -> [2I/128] (gate block mt, up block I/128 + mt); else [H/128]
+      const int srows = GATED ? 2 * (M_total / 128) : M_total / 128;
+      const float* srow_a = scale + (static_cast<size_t>(e) * srows + mt) * kscale;
+      const float* srow_b = GATED ? scale + (static_cast<size_t>(e) * srows + M_total / 128 + mt) * kscale
+                                  : srow_a;
+      bool ok = true;
+      for (int kb = 0; kb < k_blocks; ++kb) {
+        if (*abort_flag || !sl::mbar_wait(&raw_full[r], rph) ||
+            !sl::mbar_wait(&cvt_empty[c], cph ^ 1)) {
+          ok = false;
+          break;
+        }
+#pragma unroll
+        for (int a = 0; a < Cfg::kNumA; ++a) {
+          const float sc = (a == 0 ? srow_a : srow_b)[kb >> 1];
+          const uint4* src =
+              reinterpret_cast<const uint4*>(sR + r * Cfg::kRawBytes + a * Cfg::kRawA + row * BK);
+          uint8_t* dst_row = reinterpret_cast<uint8_t*>(sC + (c * Cfg::kNumA + a) * Cfg::kCvtA) +
+                             row * 128;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {  // 16 fp8 -> 16 bf16 = two 16-byte chunks
+            float f[16];
+            fp8x16_to_f32(src[q], f);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              uint4 o;
+              __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                o2[j] = __floats2bfloat162_rn(f[8 * h + 2 * j] * sc, f[8 * h + 2 * j + 1] * sc);
+              const int chunk = 2 * q + h;  // 16-byte chunk within the 128-byte row
+              *reinterpret_cast<uint4*>(dst_row + ((chunk ^ (row & 7)) << 4)) = o;
+            }
+          }
+        }
+        fence_proxy_async_smem();  // generic-proxy writes -> visible to tcgen05.mma
+        __syncwarp();
+        if (lane == 0) {
+          sl::mbar_arrive(&cvt_full[c]);
+          sl::mbar_arrive(&raw_empty[r]);
+        }
+        if (++r == RSTAGES) {
+          r = 0;
+          rph ^= 1;
+        }
+        if (++c == CSTAGES) {
+          c = 0;
+          cph ^= 1;
+        }
+      }
+      if (!ok) {
+        atomicExch(status, SL_ERR_TIMEOUT);
+        *abort_flag = 1;
+        break;
+      }
+    }
+  } else {
+    // --------------------------------------------------------- epilogue
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      if (*abort_flag || !sl::mbar_wait(&tfull[acc], acc_phase)) {
+        atomicExch(status, SL_ERR_TIMEOUT);
+        *abort_flag = 1;
+        break;
+      }
+      sl::tc_fence_after();
+      const int4 it = items[item_lo + tile / m_tiles];
+      const int mt = tile % m_tiles;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * Cfg::kAccCols;
+      float v0[BN];
+      float v1[BN];
+#pragma unroll
+      for (int cc = 0; cc < BN; cc += 16) {
+        float tmp[16];
+        sl::tmem_ld16(taddr + cc, tmp);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v0[cc + i] = tmp[i];
+        if constexpr (GATED) {
+          sl::tmem_ld16(taddr + BN + cc, tmp);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v1[cc + i] = tmp[i];
+        }
+      }
+      sl::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) sl::mbar_arrive(&tempty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+      const int col = mt * BM + row;
+      __nv_bfloat16* dst = out + static_cast<size_t>(it.y) * out_ld + col;
+#pragma unroll
+      for (int n = 0; n < BN; ++n) {
+        if (n < it.z) {
+          float rr;
+          if constexpr (GATED) {
+            const float g = sl::bf16_round(v0[n]);
+            const float u = sl::bf16_round(v1[n]);
+            const float sg = sl::bf16_round(g / (1.0f + expf(-g)));
+            rr = sg * u;
+          } else {
+            rr = v0[n];
+          }
+          dst[static_cast<size_t>(n) * out_ld] = __float2bfloat16(rr);
+        }
+      }
+    }
+  }
+  sl::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    sl::tc_fence_after();
+    sl::tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
 // ---------------------------------------------------------------- combine
 // OUT_F32 = false: out = bf16(shared + bf16(scale * bf16(sum_j w z)))  (vLLM
 //   torch-native rounding chain, runner tail in bf16)
@@ -591,16 +934,46 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // 2-D bf16 view [rows, inner] (inner contiguous), box {64, box_rows}, 128B swizzle.
-bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint32_t box_rows) {
+bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint32_t box_rows,
+              bool fp8 = false) {
   auto fn = encode_fn();
   if (!fn || (reinterpret_cast<uintptr_t>(base) & 15) || rows == 0) return false;
+  // bf16: 64-element (128 B) inner box, 128B swizzle (the MMA operand layout);
+  // fp8: 64-byte inner box, unswizzled (a staging tile the converter reads)
+  const uint64_t esz = fp8 ? 1 : 2;
   cuuint64_t dims[2] = {inner, rows};
-  cuuint64_t strides[1] = {inner * 2};
+  cuuint64_t strides[1] = {inner * esz};
   cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), box_rows};
   cuuint32_t estr[2] = {1, 1};
-  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
-            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+  return fn(m, fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+            const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            fp8 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN, int RSTAGES, int CSTAGES, bool GATED>
+int launch_gemm_fp8(const CUtensorMap& tw, const CUtensorMap& twsh, const CUtensorMap& tb,
+                    const float* wscale, const float* wshscale, const int32_t* hdr,
+                    const int4* items, __nv_bfloat16* out, int S, int K, int M_total, int out_ld,
+                    int32_t* status, int max_items, cudaStream_t st, int phase) {
+  using Cfg = Fp8Cfg<BN, RSTAGES, CSTAGES, GATED>;
+  auto kern = moe_gemm_fp8_kernel<BN, RSTAGES, CSTAGES, GATED>;
+  static int configured_dev = -1;
+  int dev = 0;
+  SL_CUDA_TRY(cudaGetDevice(&dev));
+  if (configured_dev != dev) {
+    SL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     Cfg::kSmemBytes));
+    configured_dev = dev;
+  }
+  const int max_tiles = max_items * (M_total / BM);
+  int grid = sl_device_sm_count();
+  if (grid <= 0) return SL_ERR_CUDA;
+  if (max_tiles < grid) grid = max_tiles > 0 ? max_tiles : 1;
+  SL_CUDA_TRY(sl::launch(kern, dim3(grid), dim3(kFp8Threads), Cfg::kSmemBytes, st, tw, twsh, tb,
+                         wscale, wshscale, hdr, items, out, S, K, M_total, out_ld, status,
+                         phase));
+  return SL_OK;
 }
 
 template <int BN, int STAGES, bool GATED>
@@ -637,21 +1010,25 @@ extern "C" size_t sl_fused_experts_workspace_bytes(int T, int topk, int H, int I
 
 namespace {
 
-int run_fused(const void* hidden, int T, int H, int I, const void* w13, const void* w2,
-              int num_slots, int weight_dtype, const float* topk_weights,
-              const int32_t* topk_ids, int topk, const int32_t* expert_map, int global_n,
-              const void* shared_w13, const void* shared_w2, int n_shared, int sh_t0,
-              int sh_nt, float routed_scaling_factor, void* out, bool out_f32,
-              void* workspace, size_t workspace_bytes, cudaStream_t st,
-              const void* fill_state = nullptr, int phase = -1) {
-  if (weight_dtype != 0) return SL_ERR_UNSUPPORTED;
+int run_fused(const void* hidden, int T, int H, int I, const sl_expert_weights& w,
+              const float* topk_weights, const int32_t* topk_ids, int topk,
+              const int32_t* expert_map, int global_n, int sh_t0, int sh_nt,
+              float routed_scaling_factor, void* out, bool out_f32, void* workspace,
+              size_t workspace_bytes, cudaStream_t st, const void* fill_state = nullptr,
+              int phase = -1) {
+  const int num_slots = w.num_slots, n_shared = w.n_shared;
+  const bool fp8 = w.dtype == SL_WEIGHTS_FP8_BLOCK128;
+  if (w.dtype != SL_WEIGHTS_BF16 && !fp8) return SL_ERR_UNSUPPORTED;
   if (T < 0 || topk <= 0 || num_slots <= 0 || n_shared < 0) return SL_ERR_INVALID;
   if (H % BM || I % BM || H <= 0 || I <= 0) return SL_ERR_UNSUPPORTED;
   if (num_slots + n_shared > kMaxCode || n_shared > kMaxShared) return SL_ERR_UNSUPPORTED;
+  if (phase < -1 || phase > 1 || (phase >= 0 && !fill_state)) return SL_ERR_INVALID;
   if (T == 0) return SL_OK;
-  if (!hidden || !w13 || !w2 || !topk_weights || !topk_ids || !out || !workspace)
+  if (!hidden || !w.w13 || !w.w2 || !topk_weights || !topk_ids || !out || !workspace)
     return SL_ERR_INVALID;
-  if (n_shared > 0 && (!shared_w13 || !shared_w2)) return SL_ERR_INVALID;
+  if (fp8 && (!w.w13_scale || !w.w2_scale)) return SL_ERR_INVALID;
+  if (n_shared > 0 && (!w.shared_w13 || !w.shared_w2)) return SL_ERR_INVALID;
+  if (fp8 && n_shared > 0 && (!w.shared_w13_scale || !w.shared_w2_scale)) return SL_ERR_INVALID;
   if (n_shared > 0 && (sh_t0 < 0 || sh_nt < 0 || sh_t0 + sh_nt > T)) return SL_ERR_INVALID;
   if (expert_map && global_n <= 0) return SL_ERR_INVALID;
   if ((reinterpret_cast<uintptr_t>(workspace) & 255) ||
@@ -670,13 +1047,13 @@ int run_fused(const void* hidden, int T, int H, int I, const void* w13, const vo
 
   CUtensorMap m_w13, m_w13sh, m_x, m_w2, m_w2sh, m_a;
   const int nsh = n_shared > 0 ? n_shared : 0;
-  bool ok = make_map(&m_w13, w13, H, uint64_t(num_slots) * 2 * I, BM) &&
-            make_map(&m_w2, w2, I, uint64_t(num_slots) * H, BM) &&
+  bool ok = make_map(&m_w13, w.w13, H, uint64_t(num_slots) * 2 * I, BM, fp8) &&
+            make_map(&m_w2, w.w2, I, uint64_t(num_slots) * H, BM, fp8) &&
             make_map(&m_x, X, H, uint64_t(L.max_rows), BN) &&
             make_map(&m_a, A, I, uint64_t(L.max_rows), BN);
   if (ok && nsh) {
-    ok = make_map(&m_w13sh, shared_w13, H, uint64_t(nsh) * 2 * I, BM) &&
-         make_map(&m_w2sh, shared_w2, I, uint64_t(nsh) * H, BM);
+    ok = make_map(&m_w13sh, w.shared_w13, H, uint64_t(nsh) * 2 * I, BM, fp8) &&
+         make_map(&m_w2sh, w.shared_w2, I, uint64_t(nsh) * H, BM, fp8);
   } else {
     m_w13sh = m_w13;
     m_w2sh = m_w2;
@@ -690,11 +1067,21 @@ int run_fused(const void* hidden, int T, int H, int I, const void* w13, const vo
                            hdr, items, pair_pos, X, L.max_items,
                            static_cast<const uint8_t*>(fill_state)));
   int rc;
-  rc = launch_gemm<16, 6, true>(m_w13, m_w13sh, m_x, hdr, items, A, num_slots, H, I, I, hdr,
-                                L.max_items, st, phase);
-  if (rc != SL_OK) return rc;
-  rc = launch_gemm<16, 12, false>(m_w2, m_w2sh, m_a, hdr, items, Z, num_slots, I, H, H, hdr,
+  if (fp8) {
+    rc = launch_gemm_fp8<16, 8, 2, true>(m_w13, m_w13sh, m_x, w.w13_scale, w.shared_w13_scale,
+                                         hdr, items, A, num_slots, H, I, I, hdr, L.max_items,
+                                         st, phase);
+    if (rc != SL_OK) return rc;
+    rc = launch_gemm_fp8<16, 12, 3, false>(m_w2, m_w2sh, m_a, w.w2_scale, w.shared_w2_scale,
+                                           hdr, items, Z, num_slots, I, H, H, hdr, L.max_items,
+                                           st, phase);
+  } else {
+    rc = launch_gemm<16, 6, true>(m_w13, m_w13sh, m_x, hdr, items, A, num_slots, H, I, I, hdr,
                                   L.max_items, st, phase);
+    if (rc != SL_OK) return rc;
+    rc = launch_gemm<16, 12, false>(m_w2, m_w2sh, m_a, hdr, items, Z, num_slots, I, H, H, hdr,
+                                    L.max_items, st, phase);
+  }
   if (rc != SL_OK) return rc;
   if (phase == 0) return SL_OK;
   dim3 cgrid((H / 8 + 255) / 256, T);
@@ -706,6 +1093,19 @@ int run_fused(const void* hidden, int T, int H, int I, const void* w13, const vo
   return SL_OK;
 }
 
+sl_expert_weights bf16_weights(const void* w13, const void* w2, int num_slots,
+                               const void* shared_w13, const void* shared_w2, int n_shared) {
+  sl_expert_weights w = {};
+  w.w13 = w13;
+  w.w2 = w2;
+  w.num_slots = num_slots;
+  w.shared_w13 = shared_w13;
+  w.shared_w2 = shared_w2;
+  w.n_shared = n_shared;
+  w.dtype = SL_WEIGHTS_BF16;
+  return w;
+}
+
 }  // namespace
 
 extern "C" int sl_fused_experts(const void* hidden, int T, int H, int I, const void* w13,
@@ -715,9 +1115,10 @@ extern "C" int sl_fused_experts(const void* hidden, int T, int H, int I, const v
                                 const void* shared_w13, const void* shared_w2, int n_shared,
                                 float routed_scaling_factor, void* out, void* workspace,
                                 size_t workspace_bytes, sl_stream_t stream) {
-  return run_fused(hidden, T, H, I, w13, w2, num_slots, weight_dtype, topk_weights, topk_ids,
-                   topk, expert_map, global_n, shared_w13, shared_w2, n_shared, 0, T,
-                   routed_scaling_factor, out, false, workspace, workspace_bytes,
+  if (weight_dtype != SL_WEIGHTS_BF16) return SL_ERR_UNSUPPORTED;
+  const sl_expert_weights w = bf16_weights(w13, w2, num_slots, shared_w13, shared_w2, n_shared);
+  return run_fused(hidden, T, H, I, w, topk_weights, topk_ids, topk, expert_map, global_n, 0,
+                   T, routed_scaling_factor, out, false, workspace, workspace_bytes,
                    reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -731,9 +1132,10 @@ extern "C" int sl_fused_experts_partial(const void* hidden, int T, int H, int I,
                                         float routed_scaling_factor, float* out_f32,
                                         void* workspace, size_t workspace_bytes,
                                         sl_stream_t stream) {
-  return run_fused(hidden, T, H, I, w13, w2, num_slots, weight_dtype, topk_weights, topk_ids,
-                   topk, expert_map, global_n, shared_w13, shared_w2, n_shared, shared_t0,
-                   shared_nt, routed_scaling_factor, out_f32, true, workspace,
+  if (weight_dtype != SL_WEIGHTS_BF16) return SL_ERR_UNSUPPORTED;
+  const sl_expert_weights w = bf16_weights(w13, w2, num_slots, shared_w13, shared_w2, n_shared);
+  return run_fused(hidden, T, H, I, w, topk_weights, topk_ids, topk, expert_map, global_n,
+                   shared_t0, shared_nt, routed_scaling_factor, out_f32, true, workspace,
                    workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -746,10 +1148,28 @@ extern "C" int sl_fused_experts_phase(const void* hidden, int T, int H, int I, c
                                       const void* slot_state, int phase, void* out,
                                       void* workspace, size_t workspace_bytes,
                                       sl_stream_t stream) {
+  if (weight_dtype != SL_WEIGHTS_BF16) return SL_ERR_UNSUPPORTED;
   if (phase != 0 && phase != 1) return SL_ERR_INVALID;
-  if (!slot_state) return SL_ERR_INVALID;
-  return run_fused(hidden, T, H, I, w13, w2, num_slots, weight_dtype, topk_weights, topk_ids,
-                   topk, expert_map, global_n, shared_w13, shared_w2, n_shared, 0, T,
-                   routed_scaling_factor, out, false, workspace, workspace_bytes,
+  const sl_expert_weights w = bf16_weights(w13, w2, num_slots, shared_w13, shared_w2, n_shared);
+  return run_fused(hidden, T, H, I, w, topk_weights, topk_ids, topk, expert_map, global_n, 0,
+                   T, routed_scaling_factor, out, false, workspace, workspace_bytes,
                    reinterpret_cast<cudaStream_t>(stream), slot_state, phase);
+}
+
+extern "C" int sl_fused_experts_ex(const void* hidden, int T, int H, int I,
+                                   const sl_expert_weights* weights, const float* topk_weights,
+                                   const int32_t* topk_ids, int topk, const int32_t* expert_map,
+                                   int global_n, float routed_scaling_factor, int shared_t0,
+                                   int shared_nt, const void* slot_state, int phase, int out_f32,
+                                   void* out, void* workspace, size_t workspace_bytes,
+                                   sl_stream_t stream) {
+  if (!weights) return SL_ERR_INVALID;
+  if (shared_nt < 0) {  // default: every token
+    shared_t0 = 0;
+    shared_nt = T;
+  }
+  return run_fused(hidden, T, H, I, *weights, topk_weights, topk_ids, topk, expert_map,
+                   global_n, shared_t0, shared_nt, routed_scaling_factor, out, out_f32 != 0,
+                   workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream),
+                   slot_state, phase);
 }
