@@ -37,6 +37,18 @@ STATE_NFIELDS = 11
 _c = ctypes
 _vp, _i, _sz, _f = _c.c_void_p, _c.c_int, _c.c_size_t, _c.c_float
 
+WEIGHTS_BF16, WEIGHTS_FP8_BLOCK128 = 0, 1
+
+
+class ExpertWeights(ctypes.Structure):
+    """``sl_expert_weights`` (include/sluice_b200.h)."""
+
+    _fields_ = [("w13", _vp), ("w2", _vp), ("w13_scale", _vp), ("w2_scale", _vp),
+                ("num_slots", _i), ("shared_w13", _vp), ("shared_w2", _vp),
+                ("shared_w13_scale", _vp), ("shared_w2_scale", _vp), ("n_shared", _i),
+                ("dtype", _i)]
+
+
 _SIGNATURES = {
     "sl_status_string": (_c.c_char_p, [_i]),
     "sl_version": (_i, []),
@@ -61,6 +73,8 @@ _SIGNATURES = {
     "sl_fused_experts_partial": (_i, [_vp, _i, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _i,
                                       _vp, _i, _vp, _vp, _i, _i, _i, _f, _vp, _vp, _sz,
                                       _vp]),
+    "sl_fused_experts_ex": (_i, [_vp, _i, _i, _i, _c.POINTER(ExpertWeights), _vp, _vp, _i,
+                                 _vp, _i, _f, _i, _i, _vp, _i, _i, _vp, _vp, _sz, _vp]),
     "sl_fused_experts_noalloc": (_i, [_vp, _i, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _i,
                                       _vp, _i, _vp, _vp, _i, _f, _vp, _vp, _vp]),
 }

@@ -26,8 +26,12 @@ from .offloader import ExpertStreamOffloader, SlotCache
 class SluiceMoELayer:
     def __init__(self, cfg: MoEConfig, router: ops.Router, cache: SlotCache,
                  shared_w13: torch.Tensor | None, shared_w2: torch.Tensor | None,
-                 layer_idx: int = 0, overlap: bool = True, stream_ctas: int = 16):
+                 layer_idx: int = 0, overlap: bool = True, stream_ctas: int = 16,
+                 shared_w13_scale: torch.Tensor | None = None,
+                 shared_w2_scale: torch.Tensor | None = None):
         self.cfg = cfg
+        self.shared_w13_scale = shared_w13_scale
+        self.shared_w2_scale = shared_w2_scale
         # overlap the gap's expert stream with the resident experts' GEMMs
         self.overlap = overlap and not cache.static_full
         self.stream_ctas = stream_ctas
@@ -46,10 +50,14 @@ class SluiceMoELayer:
         if self.overlap:
             return self._forward_overlapped(hs, tw, ti)
         self.cache.gap(ti)
-        return ops.fused_experts(hs, self.cache.w13, self.cache.w2, tw, ti,
+        c = self.cache
+        return ops.fused_experts(hs, c.w13, c.w2, tw, ti,
                                  global_num_experts=self.cfg.num_experts,
-                                 expert_map=self.cache.expert_map,
-                                 shared_w13=self.shared_w13, shared_w2=self.shared_w2,
+                                 expert_map=c.expert_map, w1_scale=c.w13_scale,
+                                 w2_scale=c.w2_scale, shared_w13=self.shared_w13,
+                                 shared_w2=self.shared_w2,
+                                 shared_w13_scale=self.shared_w13_scale,
+                                 shared_w2_scale=self.shared_w2_scale,
                                  routed_scaling_factor=self.cfg.routed_scaling_factor)
 
     def _forward_overlapped(self, hs, tw, ti):
@@ -68,7 +76,9 @@ class SluiceMoELayer:
                                          else self.shared_w13.shape[0], hs.device)
         out = torch.empty_like(hs)
         args = (hs, c.w13, c.w2, tw, ti, c.expert_map, c.state)
-        kw = dict(shared_w13=self.shared_w13, shared_w2=self.shared_w2,
+        kw = dict(w1_scale=c.w13_scale, w2_scale=c.w2_scale, shared_w13=self.shared_w13,
+                  shared_w2=self.shared_w2, shared_w13_scale=self.shared_w13_scale,
+                  shared_w2_scale=self.shared_w2_scale,
                   routed_scaling_factor=cfg.routed_scaling_factor)
         ops.fused_experts_phase(*args, 0, ws, out, **kw)
         main.wait_stream(self._side)

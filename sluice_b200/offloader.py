@@ -113,9 +113,10 @@ class HostStore:
 
 
 class SlotCache:
-    """One MoE layer's slots, host store, expert map and device SLRU state."""
+    """One MoE layer's slots, host store, expert map and device SLRU state.
 
-    PARAMS = ("w13", "w2")
+    Per-expert parameters: ``w13``, ``w2`` and, for fp8 block-scaled experts,
+    ``w13_scale``, ``w2_scale`` — every one streamed on a miss."""
 
     def __init__(self, num_slots: int, local_n: int, global_n: int, local_of: list,
                  protected_cap: int, static_full: bool, device: torch.device,
@@ -139,11 +140,12 @@ class SlotCache:
             check(lib().sl_slot_state_offsets(num_slots, global_n, local_n, offs),
                   "sl_slot_state_offsets")
             self.offsets = list(offs)
-            n = len(self.PARAMS)
-            src = (ctypes.c_void_p * n)(*[cpu_store[k].data_ptr() for k in self.PARAMS])
-            dst = (ctypes.c_void_p * n)(*[gpu_cache[k].data_ptr() for k in self.PARAMS])
+            names = list(gpu_cache)
+            n = len(names)
+            src = (ctypes.c_void_p * n)(*[cpu_store[k].data_ptr() for k in names])
+            dst = (ctypes.c_void_p * n)(*[gpu_cache[k].data_ptr() for k in names])
             nb = (ctypes.c_size_t * n)(*[cpu_store[k][0].numel() * cpu_store[k].element_size()
-                                         for k in self.PARAMS])
+                                         for k in names])
             self._stream_args = (n, src, dst, nb)
 
     @property
@@ -153,6 +155,14 @@ class SlotCache:
     @property
     def w2(self) -> torch.Tensor:
         return self.gpu_cache["w2"]
+
+    @property
+    def w13_scale(self) -> torch.Tensor | None:
+        return self.gpu_cache.get("w13_scale")
+
+    @property
+    def w2_scale(self) -> torch.Tensor | None:
+        return self.gpu_cache.get("w2_scale")
 
     # -- the gap ---------------------------------------------------------
     def gap(self, topk_ids: torch.Tensor, stream_ctas: int = 0) -> None:
@@ -252,9 +262,13 @@ class ExpertStreamOffloader:
 
     def install_layer(self, w13: torch.Tensor, w2: torch.Tensor, global_n: int | None = None,
                       local_of: list | None = None, pins: list | None = None,
-                      device: torch.device | str = "cuda") -> SlotCache:
+                      device: torch.device | str = "cuda",
+                      w13_scale: torch.Tensor | None = None,
+                      w2_scale: torch.Tensor | None = None) -> SlotCache:
         """Install one layer from its local experts ``w13`` [L, 2I, H], ``w2``
-        [L, H, I] (CPU or CUDA tensors; copied into the host store)."""
+        [L, H, I] (bf16, or fp8 e4m3 with fp32 128x128 block scales
+        ``w13_scale`` [L, 2I/128, H/128], ``w2_scale`` [L, H/128, I/128]; CPU or
+        CUDA tensors, copied into the host store)."""
         device = torch.device(device)
         local_n = w13.shape[0]
         if global_n is None:
@@ -268,6 +282,9 @@ class ExpertStreamOffloader:
         resident_all = S >= local_n
         static_full = resident_all and not self.no_static_full
         params = {"w13": w13, "w2": w2}
+        if w13_scale is not None:
+            params["w13_scale"] = w13_scale.float().contiguous()
+            params["w2_scale"] = w2_scale.float().contiguous()
         gpu_cache, cpu_store = {}, {}
         bpe = 0
         for name, p in params.items():

@@ -21,6 +21,8 @@ can be captured in a CUDA graph.
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from . import _lib
@@ -98,78 +100,24 @@ class Router:
         return w, ids, logits
 
 
-def fused_experts(hidden_states: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
-                  topk_weights: torch.Tensor, topk_ids: torch.Tensor,
-                  activation: str = "silu", global_num_experts: int = -1,
-                  expert_map: torch.Tensor | None = None,
-                  shared_w13: torch.Tensor | None = None,
-                  shared_w2: torch.Tensor | None = None,
-                  routed_scaling_factor: float = 1.0,
-                  out: torch.Tensor | None = None) -> torch.Tensor:
-    """Routed (+ shared) expert output [T, H] bf16.
-
-    ``w1`` is [slots, 2I, H] (gate rows then up rows), ``w2`` [slots, H, I];
-    ``expert_map`` int32 [global_num_experts] maps a global id to its slot
-    (-1: contributes nothing). Without a map, ids index ``w1`` directly.
-    """
-    if activation != "silu":
-        raise ValueError("only activation='silu' (SwiGLU) is on this path")
-    _need_cuda(hidden_states, w1, w2, topk_weights, topk_ids, expert_map)
-    hs = hidden_states.contiguous()
-    T, H = hs.shape
-    S, two_i, H1 = w1.shape
-    I = two_i // 2
-    if H1 != H or tuple(w2.shape) != (S, H, I):
-        raise ValueError(f"weight shapes {tuple(w1.shape)} / {tuple(w2.shape)} do not match H={H}")
-    if w1.dtype != torch.bfloat16 or w2.dtype != torch.bfloat16 or hs.dtype != torch.bfloat16:
-        raise ValueError("bf16 weights and activations expected")
-    k = topk_ids.shape[1]
+def _expert_weights(w1, w2, w1_scale, w2_scale, shared_w13, shared_w2,
+                    shared_w13_scale, shared_w2_scale) -> _lib.ExpertWeights:
+    fp8 = w1.dtype == torch.float8_e4m3fn
+    if fp8:
+        if w1_scale is None or w2_scale is None:
+            raise ValueError("fp8 expert weights need w1_scale / w2_scale (128x128 blocks)")
+        for t in (w1_scale, w2_scale, shared_w13_scale, shared_w2_scale):
+            if t is not None and (t.dtype != torch.float32 or not t.is_contiguous()):
+                raise ValueError("block scales must be contiguous fp32")
+    elif w1.dtype != torch.bfloat16:
+        raise ValueError(f"unsupported expert weight dtype {w1.dtype}")
+    if w2.dtype != w1.dtype or (shared_w13 is not None and shared_w13.dtype != w1.dtype):
+        raise ValueError("all expert weights must share one dtype")
     n_sh = 0 if shared_w13 is None else shared_w13.shape[0]
-    G = expert_map.numel() if expert_map is not None else (
-        global_num_experts if global_num_experts > 0 else S)
-    if expert_map is not None and expert_map.dtype != torch.int32:
-        raise ValueError("expert_map must be int32")
-    L = lib()
-    nbytes = L.sl_fused_experts_workspace_bytes(T, k, H, I, S, n_sh)
-    ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=hs.device)
-    if out is None:
-        out = torch.empty(T, H, dtype=torch.bfloat16, device=hs.device)
-    tw = topk_weights.contiguous().float()
-    ti = topk_ids.contiguous().to(torch.int32)
-    check(L.sl_fused_experts(ptr(hs), T, H, I, ptr(w1), ptr(w2), S, 0, ptr(tw), ptr(ti), k,
-                             ptr(expert_map), G, ptr(shared_w13), ptr(shared_w2), n_sh,
-                             float(routed_scaling_factor), ptr(out), ptr(ws), nbytes,
-                             _stream()), "sl_fused_experts")
-    fused_experts.last_workspace = ws
-    return out
-
-
-fused_experts.last_workspace = None
-
-
-def fused_experts_phase(hidden_states: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
-                        topk_weights: torch.Tensor, topk_ids: torch.Tensor,
-                        expert_map: torch.Tensor, slot_state: torch.Tensor, phase: int,
-                        workspace: torch.Tensor, out: torch.Tensor,
-                        shared_w13: torch.Tensor | None = None,
-                        shared_w2: torch.Tensor | None = None,
-                        routed_scaling_factor: float = 1.0) -> torch.Tensor:
-    """One phase of ``fused_experts`` split around the expert stream: phase 0
-    computes the already-resident experts, phase 1 the streamed ones and the
-    combine into ``out``. Both phases take the same ``workspace``
-    (``fused_experts_workspace``)."""
-    hs = hidden_states
-    T, H = hs.shape
-    S, two_i, _ = w1.shape
-    k = topk_ids.shape[1]
-    n_sh = 0 if shared_w13 is None else shared_w13.shape[0]
-    check(lib().sl_fused_experts_phase(ptr(hs), T, H, two_i // 2, ptr(w1), ptr(w2), S, 0,
-                                       ptr(topk_weights), ptr(topk_ids), k, ptr(expert_map),
-                                       expert_map.numel(), ptr(shared_w13), ptr(shared_w2),
-                                       n_sh, float(routed_scaling_factor), ptr(slot_state),
-                                       int(phase), ptr(out), ptr(workspace), workspace.numel(),
-                                       _stream()), "sl_fused_experts_phase")
-    return out
+    return _lib.ExpertWeights(ptr(w1), ptr(w2), ptr(w1_scale), ptr(w2_scale), w1.shape[0],
+                              ptr(shared_w13), ptr(shared_w2), ptr(shared_w13_scale),
+                              ptr(shared_w2_scale), n_sh,
+                              _lib.WEIGHTS_FP8_BLOCK128 if fp8 else _lib.WEIGHTS_BF16)
 
 
 def fused_experts_workspace(T: int, topk: int, H: int, I: int, slots: int, n_shared: int,
@@ -178,36 +126,108 @@ def fused_experts_workspace(T: int, topk: int, H: int, I: int, slots: int, n_sha
     return torch.empty(max(n, 256), dtype=torch.uint8, device=device)
 
 
-def fused_experts_partial(hidden_states: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
-                          topk_weights: torch.Tensor, topk_ids: torch.Tensor,
-                          expert_map: torch.Tensor, shared_w13: torch.Tensor | None = None,
-                          shared_w2: torch.Tensor | None = None, shared_t0: int = 0,
+def _fused_ex(hs, w1, w2, topk_weights, topk_ids, expert_map, global_n, *, w1_scale=None,
+              w2_scale=None, shared_w13=None, shared_w2=None, shared_w13_scale=None,
+              shared_w2_scale=None, routed_scaling_factor=1.0, shared_t0=0, shared_nt=-1,
+              slot_state=None, phase=-1, out_f32=False, out=None, workspace=None):
+    _need_cuda(hs, w1, w2, topk_weights, topk_ids, expert_map)
+    hs = hs.contiguous()
+    if hs.dtype != torch.bfloat16:
+        raise ValueError("bf16 activations expected")
+    T, H = hs.shape
+    S, two_i, H1 = w1.shape
+    I = two_i // 2
+    if H1 != H or tuple(w2.shape) != (S, H, I):
+        raise ValueError(f"weight shapes {tuple(w1.shape)} / {tuple(w2.shape)} do not match H={H}")
+    if expert_map is not None and expert_map.dtype != torch.int32:
+        raise ValueError("expert_map must be int32")
+    w = _expert_weights(w1, w2, w1_scale, w2_scale, shared_w13, shared_w2, shared_w13_scale,
+                        shared_w2_scale)
+    k = topk_ids.shape[1]
+    if workspace is None:
+        workspace = fused_experts_workspace(T, k, H, I, S, w.n_shared, hs.device)
+    if out is None:
+        out = torch.empty(T, H, dtype=torch.float32 if out_f32 else torch.bfloat16,
+                          device=hs.device)
+    tw = topk_weights if topk_weights.dtype == torch.float32 and topk_weights.is_contiguous() \
+        else topk_weights.contiguous().float()
+    ti = topk_ids if topk_ids.dtype == torch.int32 and topk_ids.is_contiguous() \
+        else topk_ids.contiguous().to(torch.int32)
+    check(lib().sl_fused_experts_ex(ptr(hs), T, H, I, ctypes.byref(w), ptr(tw), ptr(ti), k,
+                                    ptr(expert_map), global_n, float(routed_scaling_factor),
+                                    int(shared_t0), int(shared_nt), ptr(slot_state), int(phase),
+                                    int(out_f32), ptr(out), ptr(workspace), workspace.numel(),
+                                    _stream()), "sl_fused_experts_ex")
+    fused_experts.last_workspace = workspace
+    return out
+
+
+def fused_experts(hidden_states: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
+                  topk_weights: torch.Tensor, topk_ids: torch.Tensor,
+                  activation: str = "silu", global_num_experts: int = -1,
+                  expert_map: torch.Tensor | None = None,
+                  w1_scale: torch.Tensor | None = None, w2_scale: torch.Tensor | None = None,
+                  block_shape: list | None = None,
+                  shared_w13: torch.Tensor | None = None,
+                  shared_w2: torch.Tensor | None = None,
+                  shared_w13_scale: torch.Tensor | None = None,
+                  shared_w2_scale: torch.Tensor | None = None,
+                  routed_scaling_factor: float = 1.0,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """Routed (+ shared) expert output [T, H] bf16.
+
+    ``w1`` is [slots, 2I, H] (gate rows then up rows), ``w2`` [slots, H, I],
+    bf16 or fp8 e4m3 with fp32 ``w1_scale`` [slots, 2I/128, H/128] /
+    ``w2_scale`` [slots, H/128, I/128] (``block_shape`` [128, 128]);
+    ``expert_map`` int32 [global_num_experts] maps a global id to its slot
+    (-1: contributes nothing). Without a map, ids index ``w1`` directly.
+    """
+    if activation != "silu":
+        raise ValueError("only activation='silu' (SwiGLU) is on this path")
+    if block_shape is not None and list(block_shape) != [128, 128]:
+        raise ValueError("only 128x128 weight blocks are supported")
+    G = expert_map.numel() if expert_map is not None else (
+        global_num_experts if global_num_experts > 0 else w1.shape[0])
+    return _fused_ex(hidden_states, w1, w2, topk_weights, topk_ids, expert_map, G,
+                     w1_scale=w1_scale, w2_scale=w2_scale, shared_w13=shared_w13,
+                     shared_w2=shared_w2, shared_w13_scale=shared_w13_scale,
+                     shared_w2_scale=shared_w2_scale,
+                     routed_scaling_factor=routed_scaling_factor, out=out)
+
+
+fused_experts.last_workspace = None
+
+
+def fused_experts_phase(hidden_states, w1, w2, topk_weights, topk_ids, expert_map, slot_state,
+                        phase: int, workspace: torch.Tensor, out: torch.Tensor,
+                        w1_scale=None, w2_scale=None, shared_w13=None, shared_w2=None,
+                        shared_w13_scale=None, shared_w2_scale=None,
+                        routed_scaling_factor: float = 1.0) -> torch.Tensor:
+    """One phase of ``fused_experts`` split around the expert stream: phase 0
+    computes the already-resident experts, phase 1 the streamed ones and the
+    combine into ``out``. Both phases take the same ``workspace``."""
+    return _fused_ex(hidden_states, w1, w2, topk_weights, topk_ids, expert_map,
+                     expert_map.numel(), w1_scale=w1_scale, w2_scale=w2_scale,
+                     shared_w13=shared_w13, shared_w2=shared_w2,
+                     shared_w13_scale=shared_w13_scale, shared_w2_scale=shared_w2_scale,
+                     routed_scaling_factor=routed_scaling_factor, slot_state=slot_state,
+                     phase=phase, out=out, workspace=workspace)
+
+
+def fused_experts_partial(hidden_states, w1, w2, topk_weights, topk_ids, expert_map,
+                          shared_w13=None, shared_w2=None, shared_t0: int = 0,
                           shared_nt: int = 0, routed_scaling_factor: float = 1.0,
-                          out: torch.Tensor | None = None) -> torch.Tensor:
+                          out=None, w1_scale=None, w2_scale=None, shared_w13_scale=None,
+                          shared_w2_scale=None) -> torch.Tensor:
     """Expert-parallel partial output [T, H] fp32: this rank's experts (the
     ones ``expert_map`` maps) scaled by ``routed_scaling_factor``, plus the
     shared experts on rows [shared_t0, shared_t0 + shared_nt)."""
-    _need_cuda(hidden_states, w1, w2, topk_weights, topk_ids, expert_map)
-    hs = hidden_states.contiguous()
-    T, H = hs.shape
-    S, two_i, _ = w1.shape
-    I = two_i // 2
-    k = topk_ids.shape[1]
-    n_sh = 0 if shared_w13 is None else shared_w13.shape[0]
-    L = lib()
-    nbytes = L.sl_fused_experts_workspace_bytes(T, k, H, I, S, n_sh)
-    ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=hs.device)
-    if out is None:
-        out = torch.empty(T, H, dtype=torch.float32, device=hs.device)
-    tw = topk_weights.contiguous().float()
-    ti = topk_ids.contiguous().to(torch.int32)
-    check(L.sl_fused_experts_partial(ptr(hs), T, H, I, ptr(w1), ptr(w2), S, 0, ptr(tw), ptr(ti),
-                                     k, ptr(expert_map), expert_map.numel(), ptr(shared_w13),
-                                     ptr(shared_w2), n_sh, int(shared_t0), int(shared_nt),
-                                     float(routed_scaling_factor), ptr(out), ptr(ws), nbytes,
-                                     _stream()), "sl_fused_experts_partial")
-    fused_experts_partial.last_workspace = ws
-    return out
+    return _fused_ex(hidden_states, w1, w2, topk_weights, topk_ids, expert_map,
+                     expert_map.numel(), w1_scale=w1_scale, w2_scale=w2_scale,
+                     shared_w13=shared_w13, shared_w2=shared_w2,
+                     shared_w13_scale=shared_w13_scale, shared_w2_scale=shared_w2_scale,
+                     routed_scaling_factor=routed_scaling_factor, shared_t0=shared_t0,
+                     shared_nt=shared_nt, out_f32=True, out=out)
 
 
 fused_experts_partial.last_workspace = None
@@ -239,15 +259,18 @@ _lib_def.define("sluice_stream_gap(Tensor hidden_states, Tensor topk_ids, int la
 _lib_def.define(
     "fused_experts(Tensor hidden_states, Tensor w1, Tensor w2, Tensor topk_weights, "
     "Tensor topk_ids, str activation='silu', int global_num_experts=-1, "
-    "Tensor? expert_map=None, Tensor? shared_w13=None, Tensor? shared_w2=None, "
-    "float routed_scaling_factor=1.0) -> Tensor")
+    "Tensor? expert_map=None, Tensor? w1_scale=None, Tensor? w2_scale=None, "
+    "Tensor? shared_w13=None, Tensor? shared_w2=None, float routed_scaling_factor=1.0) "
+    "-> Tensor")
 _lib_def.impl("sluice_stream_gap", sluice_stream_gap, "CUDA")
 _lib_def.impl(
     "fused_experts",
     lambda hs, w1, w2, tw, ti, activation="silu", global_num_experts=-1, expert_map=None,
-    shared_w13=None, shared_w2=None, routed_scaling_factor=1.0: fused_experts(
-        hs, w1, w2, tw, ti, activation, global_num_experts, expert_map, shared_w13,
-        shared_w2, routed_scaling_factor),
+    w1_scale=None, w2_scale=None, shared_w13=None, shared_w2=None,
+    routed_scaling_factor=1.0: fused_experts(
+        hs, w1, w2, tw, ti, activation=activation, global_num_experts=global_num_experts,
+        expert_map=expert_map, w1_scale=w1_scale, w2_scale=w2_scale, shared_w13=shared_w13,
+        shared_w2=shared_w2, routed_scaling_factor=routed_scaling_factor),
     "CUDA")
 
 
@@ -258,6 +281,6 @@ def _gap_fake(hidden_states, topk_ids, layer_idx):
 
 @torch.library.register_fake("sluice::fused_experts")
 def _fe_fake(hidden_states, w1, w2, topk_weights, topk_ids, activation="silu",
-             global_num_experts=-1, expert_map=None, shared_w13=None, shared_w2=None,
-             routed_scaling_factor=1.0):
+             global_num_experts=-1, expert_map=None, w1_scale=None, w2_scale=None,
+             shared_w13=None, shared_w2=None, routed_scaling_factor=1.0):
     return torch.empty_like(hidden_states)

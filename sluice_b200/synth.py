@@ -41,6 +41,18 @@ def layer_weights(cfg: MoEConfig, layer: int, seed: int = 0, device="cuda",
     return w13, w2
 
 
+def quantize_block_fp8(w: torch.Tensor, block: int = 128):
+    """e4m3 weights and fp32 block scales (dequantised value = q * scale) for
+    [..., N, K] weights, one scale per 128x128 block (max-abs / 448)."""
+    *lead, N, K = w.shape
+    wb = w.float().reshape(*lead, N // block, block, K // block, block)
+    amax = wb.abs().amax(dim=(-3, -1), keepdim=True).clamp(min=1e-12)
+    scale = amax / 448.0
+    q = (wb / scale).clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
+    return (q.reshape(*lead, N, K),
+            scale.reshape(*lead, N // block, K // block).contiguous())
+
+
 def shared_weights(cfg: MoEConfig, layer: int, seed: int = 0, device="cuda", std=0.02):
     """Shared experts as n_shared experts of the routed I: ([n,2I,H], [n,H,I])."""
     if cfg.n_shared == 0:
@@ -101,5 +113,5 @@ def expected_unique(topk: int, tokens: int, num_experts: int) -> float:
     return num_experts * (1 - (1 - 1 / num_experts) ** n)
 
 
-__all__ = ["layer_weights", "shared_weights", "gate_params", "TokenStream", "zipf_ids",
+__all__ = ["layer_weights", "shared_weights", "quantize_block_fp8", "gate_params", "TokenStream", "zipf_ids",
            "expected_unique", "math"]

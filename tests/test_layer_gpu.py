@@ -98,3 +98,47 @@ def test_decode_step_host_round_trip():
     torch.cuda.synchronize()
     assert torch.isfinite(out.float()).all()
     assert out.shape == ref.shape
+
+
+def test_fp8_v3_routing_layer_with_streaming():
+    """DeepSeek-V3-style layer at reduced size: sigmoid + score bias, 8 groups /
+    top-4 groups, top-8, renormalised, routed scaling 2.5, fp8 e4m3 experts
+    with 128x128 block scales streamed (weights and scales) into 16 slots."""
+    from dataclasses import replace
+    cfg = replace(configs.DEEPSEEK_V3, hidden=1024, num_experts=32, moe_intermediate=512,
+                  num_moe_layers=1)
+    w13, w2 = synth.layer_weights(cfg, 0, seed=9, device="cuda")
+    q13, s13 = synth.quantize_block_fp8(w13)
+    q2, s2 = synth.quantize_block_fp8(w2)
+    gw, lb, sb = synth.gate_params(cfg, 0, seed=9, device="cuda")
+    sh13, sh2 = synth.shared_weights(cfg, 0, seed=9, device="cuda")
+    qs13, ss13 = synth.quantize_block_fp8(sh13)
+    qs2, ss2 = synth.quantize_block_fp8(sh2)
+    off = ExpertStreamOffloader(16, protect_frac=0.5, fast_hit=True)
+    cache = off.install_layer(q13, q2, device="cuda", w13_scale=s13, w2_scale=s2)
+    layer = SluiceMoELayer(cfg, ops.Router(cfg.routing, gw, lb, sb), cache, qs13, qs2,
+                           shared_w13_scale=ss13, shared_w2_scale=ss2)
+    rc = cfg.routing
+    q13c, s13c, q2c, s2c = q13.cpu(), s13.cpu(), q2.cpu(), s2.cpu()
+    stream = synth.TokenStream(cfg.hidden, 2, seed=10, reuse=0.2)
+    misses = 0
+    for step in range(5):
+        x = stream.next()
+        out = layer(x.cuda())
+        torch.cuda.synchronize()
+        cache.check()
+        misses = cache.stats()["misses"]
+        logits = layer.last_logits.cpu()
+        ow, oi = orouting.grouped_topk(logits, rc.topk, rc.renormalize, rc.num_expert_group,
+                                       rc.topk_group, rc.scoring_func, 1.0, sb.cpu())
+        ti = layer.last_ids.cpu()
+        for t in range(ti.shape[0]):
+            assert set(ti[t].tolist()) == set(oi[t].tolist()), (step, t)
+        wmap = [dict(zip(oi[t].tolist(), ow[t].tolist())) for t in range(ti.shape[0])]
+        tw = torch.tensor([[wmap[t][e] for e in ti[t].tolist()] for t in range(ti.shape[0])])
+        routed = omoe.fused_experts(x, q13c, q2c, tw, ti, None, s13c, s2c)
+        shared = omoe.shared_experts(x, qs13[0].cpu(), qs2[0].cpu(), ss13[0].cpu(),
+                                     ss2[0].cpu())
+        ref = omoe.layer_output(routed, shared, cfg.routed_scaling_factor)
+        assert_moe_close(out, ref, rtol=5e-2)
+    assert misses > 0

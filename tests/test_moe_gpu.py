@@ -124,3 +124,35 @@ def test_torch_op_registration():
     out = torch.ops.sluice.fused_experts(hs.cuda(), w13.cuda(), w2.cuda(), tw.cuda(),
                                          ti.cuda(), "silu", E, emap.cuda())
     assert_moe_close(out, omoe.fused_experts(hs, w13, w2, tw, ti, emap))
+
+
+@pytest.mark.parametrize("T,H,I,S,E,k,n_sh,scale", [
+    (8, 512, 256, 8, 16, 4, 1, 1.0),
+    (8, 7168, 2048, 16, 256, 8, 1, 2.5),    # DeepSeek-V3 expert shape, decode
+    (33, 1024, 512, 6, 12, 3, 0, 1.0),      # several items per expert
+])
+def test_fp8_block_scaled_cases(T, H, I, S, E, k, n_sh, scale):
+    """fp8 e4m3 weights with 128x128 block scales: within 5e-2 of the oracle's
+    fp32 dequantised math."""
+    from sluice_b200 import synth
+    hs, w13, w2, emap, ti, tw, sh13, sh2 = _random_case(T, H, I, S, E, k, n_sh, seed=T + H)
+    q13, s13 = synth.quantize_block_fp8(w13)
+    q2, s2 = synth.quantize_block_fp8(w2)
+    qs13 = qs2 = ss13 = ss2 = None
+    if n_sh:
+        qs13, ss13 = synth.quantize_block_fp8(sh13)
+        qs2, ss2 = synth.quantize_block_fp8(sh2)
+    c = lambda t: None if t is None else t.cuda()
+    out = ops.fused_experts(c(hs), c(q13), c(q2), c(tw), c(ti), global_num_experts=E,
+                            expert_map=c(emap), w1_scale=c(s13), w2_scale=c(s2),
+                            block_shape=[128, 128], shared_w13=c(qs13), shared_w2=c(qs2),
+                            shared_w13_scale=c(ss13), shared_w2_scale=c(ss2),
+                            routed_scaling_factor=scale)
+    torch.cuda.synchronize()
+    assert ops.workspace_status(ops.fused_experts.last_workspace) == 0
+    routed = omoe.fused_experts(hs, q13, q2, tw, ti, emap, s13, s2)
+    shared = None
+    if n_sh:
+        shared = sum(omoe.shared_experts(hs, qs13[i], qs2[i], ss13[i], ss2[i]).float()
+                     for i in range(n_sh)).to(torch.bfloat16)
+    assert_moe_close(out, omoe.layer_output(routed, shared, scale), rtol=5e-2)
