@@ -52,7 +52,15 @@ struct WsLayout {
 
 __host__ __device__ inline size_t r256(size_t v) { return (v + 255) & ~size_t(255); }
 
-inline int choose_bn(int /*T*/) { return 16; }
+// Token-tile width from the average tokens per used slot: decode steps (a few
+// tokens per expert) use 16, prefill-sized steps 64 or 128 so each weight
+// tile is reused across more tokens.
+inline int choose_bn(int T, int topk, int S) {
+  const long P = static_cast<long>(T) * topk;
+  const long used = P < S ? P : S;
+  const long avg = used > 0 ? (P + used - 1) / used : 1;
+  return avg <= 16 ? 16 : avg <= 64 ? 64 : 128;
+}
 
 inline WsLayout ws_layout(int T, int topk, int H, int I, int S, int n_sh, int BN) {
   WsLayout w;
@@ -77,7 +85,8 @@ __global__ void __launch_bounds__(1024) align_kernel(
     int G, int S, int n_sh, int sh_t0, int sh_nt, int BN,
     const __nv_bfloat16* __restrict__ hs, int H,
     int32_t* __restrict__ ws_hdr, int4* __restrict__ items, int32_t* __restrict__ pair_pos,
-    __nv_bfloat16* __restrict__ X, int max_items, const uint8_t* __restrict__ fill_state) {
+    __nv_bfloat16* __restrict__ X, int max_items, const uint8_t* __restrict__ fill_state,
+    int do_gather) {
   __shared__ int cnt[kMaxCode];
   __shared__ int ibase[kMaxCode + 1];
   __shared__ int cursor[kMaxCode];
@@ -193,6 +202,7 @@ __global__ void __launch_bounds__(1024) align_kernel(
     if (s >= 0) pair_pos[p] = ibase[s] * BN + atomicAdd(&cursor[s], 1);
   }
   __syncthreads();
+  if (!do_gather) return;  // large steps: gather_kernel copies the rows
   // gather token rows: routed pairs, then every token once per shared expert;
   // four independent 16-byte copies per thread per round
   const int vrow = H >> 3;
@@ -228,19 +238,140 @@ __global__ void __launch_bounds__(1024) align_kernel(
   }
 }
 
+// Token-row gather for large steps, spread over the whole GPU: row of pair p
+// (pair_pos) <- hidden row p / topk; shared experts' rows <- their tokens.
+__global__ void __launch_bounds__(256) gather_kernel(
+    const int32_t* __restrict__ ws_hdr, const int32_t* __restrict__ pair_pos, int P, int topk,
+    int n_sh, int sh_t0, int sh_nt, const __nv_bfloat16* __restrict__ hs, int H,
+    __nv_bfloat16* __restrict__ X) {
+  sl::pdl_wait();
+  sl::pdl_trigger();
+  const int vrow = H >> 3;
+  const uint4* src = reinterpret_cast<const uint4*>(hs);
+  uint4* dst = reinterpret_cast<uint4*>(X);
+  const long n_routed = static_cast<long>(P) * vrow;
+  const long n_total = n_routed + static_cast<long>(n_sh) * sh_nt * vrow;
+  const long stride = static_cast<long>(gridDim.x) * blockDim.x;
+  for (long q0 = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; q0 < n_total;
+       q0 += 4 * stride) {
+    uint4 v[4];
+    long d[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const long q = q0 + u * stride;
+      d[u] = -1;
+      if (q < n_routed) {
+        const int p = static_cast<int>(q / vrow), c = static_cast<int>(q % vrow);
+        const int pos = pair_pos[p];
+        if (pos >= 0) {
+          d[u] = static_cast<long>(pos) * vrow + c;
+          v[u] = src[static_cast<long>(p / topk) * vrow + c];
+        }
+      } else if (q < n_total) {
+        const long r = (q - n_routed) / vrow;
+        const int c = static_cast<int>((q - n_routed) % vrow);
+        const int i = static_cast<int>(r / sh_nt), t = static_cast<int>(r % sh_nt);
+        d[u] = static_cast<long>(ws_hdr[WS_SH_BASE + i] + t) * vrow + c;
+        v[u] = src[static_cast<long>(sh_t0 + t) * vrow + c];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (d[u] >= 0) dst[d[u]] = v[u];
+  }
+}
+
 // ------------------------------------------------------------- tcgen05 GEMM
-// GATED = true: gate/up GEMM (two weight tiles per stage, SwiGLU epilogue).
-// GATED = false: down GEMM (one weight tile per stage).
+// Weight-stationary orientation ("swap AB"): the weight rows are the MMA's M
+// dimension (128), the tokens of one work item its N dimension (BN), K runs
+// over the hidden (gate/up) or intermediate (down) dimension in 64-element
+// stages of 128-byte swizzled tiles.
+// GATED = true (gate/up GEMM): a 128-row A tile is 64 gate rows stacked on the
+//   64 up rows of the same intermediate columns, so one M=128 MMA per K step
+//   covers both; the epilogue pairs row r (gate) with row r + 64 (up) through
+//   a small shared-memory exchange and writes silu(g) * u for 64 columns.
+// GATED = false (down GEMM): 128 output rows per tile.
+// The epilogue drains TMEM 16 token columns at a time, so BN can reach 128.
+constexpr int kXchgStride = 17;  // padded fp32 row of the gate/up exchange
+
+template <int BN, bool GATED>
+struct TileShape {
+  static constexpr int kRowsOut = GATED ? 64 : 128;   // output columns per tile
+  static constexpr int kBoxRows = GATED ? 64 : 128;   // rows per weight TMA box
+  static constexpr int kAccCols = BN;                 // TMEM columns per accumulator
+  static constexpr int kTmemCols = (2 * BN) <= 32 ? 32 : (2 * BN) <= 64 ? 64
+                                   : (2 * BN) <= 128 ? 128 : 256;
+};
+
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// OR of a predicate over the four epilogue warps (named barrier 2), so they
+// leave the tile loop together and never strand one another at barrier 1.
+__device__ __forceinline__ bool epi_any(bool p) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred a, b;\n\t"
+      "setp.ne.u32 a, %1, 0;\n\t"
+      "bar.red.or.pred b, 2, 128, a;\n\t"
+      "selp.u32 %0, 1, 0, b;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(p))
+      : "memory");
+  return r != 0;
+}
+
+// Drain one accumulator (TMEM lanes = the tile's 128 weight rows, columns =
+// tokens) into bf16 output rows. Called by the four epilogue warps.
+template <int BN, bool GATED>
+__device__ __forceinline__ void epilogue_tile(uint32_t tmem_acc, int q, int lane, int4 it, int mt,
+                                              __nv_bfloat16* __restrict__ out, int out_ld,
+                                              float* xchg) {
+  using TS = TileShape<BN, GATED>;
+  const int row = q * 32 + lane;
+  const uint32_t taddr = tmem_acc + (static_cast<uint32_t>(q * 32) << 16);
+  for (int c0 = 0; c0 < BN; c0 += 16) {
+    if (c0 >= it.z) break;  // it.z is the same for the four warps
+    float v[16];
+    sl::tmem_ld16(taddr + c0, v);
+    if constexpr (GATED) {
+      if (q >= 2) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) xchg[(row - 64) * kXchgStride + i] = v[i];
+      }
+      named_bar_sync(1, 128);
+      if (q < 2) {
+        __nv_bfloat16* dst = out + static_cast<size_t>(it.y + c0) * out_ld + mt * TS::kRowsOut + row;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          if (c0 + i < it.z) {
+            // vLLM's torch-native chain: bf16 GEMM outputs, bf16 SiLU, bf16 mul
+            const float g = sl::bf16_round(v[i]);
+            const float u = sl::bf16_round(xchg[row * kXchgStride + i]);
+            const float sg = sl::bf16_round(g / (1.0f + expf(-g)));
+            dst[static_cast<size_t>(i) * out_ld] = __float2bfloat16(sg * u);
+          }
+        }
+      }
+      named_bar_sync(1, 128);  // the exchange rows are rewritten next chunk
+    } else {
+      __nv_bfloat16* dst = out + static_cast<size_t>(it.y + c0) * out_ld + mt * TS::kRowsOut + row;
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (c0 + i < it.z) dst[static_cast<size_t>(i) * out_ld] = __float2bfloat16(v[i]);
+    }
+  }
+}
+
 template <int BN, int STAGES, bool GATED>
 struct GemmCfg {
-  static constexpr int kATile = BM * BK;                     // elements
+  using TS = TileShape<BN, GATED>;
+  static constexpr int kATile = BM * BK;  // bf16 elements
   static constexpr int kBTile = BN * BK;
-  static constexpr int kNumA = GATED ? 2 : 1;
-  static constexpr int kStageBytes = (kNumA * kATile + kBTile) * 2;
-  static constexpr int kAccCols = GATED ? 2 * BN : BN;       // per accumulator
-  static constexpr int kTmemCols = (2 * kAccCols) <= 32 ? 32 : (2 * kAccCols) <= 64 ? 64
-                                   : (2 * kAccCols) <= 128 ? 128 : 256;
-  static constexpr int kSmemBytes = STAGES * kStageBytes + 1024 /*align*/ + 256 /*bars*/;
+  static constexpr int kStageBytes = (kATile + kBTile) * 2;
+  static constexpr int kSmemBytes = STAGES * kStageBytes + 1024 /*align*/ + 512 /*bars*/ +
+                                    64 * kXchgStride * 4;
 };
 
 template <int BN, int STAGES, bool GATED>
@@ -251,12 +382,14 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(
     int M_total /* rows of one expert's weight block in this GEMM's view */,
     int out_ld, int32_t* __restrict__ status, int phase) {
   using Cfg = GemmCfg<BN, STAGES, GATED>;
+  using TS = TileShape<BN, GATED>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  __nv_bfloat16* sA = reinterpret_cast<__nv_bfloat16*>(smem);  // [STAGES][kNumA][BM*BK]
-  __nv_bfloat16* sB = sA + STAGES * Cfg::kNumA * Cfg::kATile;  // [STAGES][BN*BK]
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::kBTile);
+  __nv_bfloat16* sA = reinterpret_cast<__nv_bfloat16*>(smem);  // [STAGES][BM*BK]
+  __nv_bfloat16* sB = sA + STAGES * Cfg::kATile;               // [STAGES][BN*BK]
+  float* xchg = reinterpret_cast<float*>(sB + STAGES * Cfg::kBTile);
+  uint64_t* full = reinterpret_cast<uint64_t*>(xchg + 64 * kXchgStride);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -281,13 +414,13 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(
     sl::tma_prefetch_desc(&tm_wsh);
     sl::tma_prefetch_desc(&tm_b);
   }
-  if (warp == 1) sl::tmem_alloc(tmem_slot, Cfg::kTmemCols);
+  if (warp == 1) sl::tmem_alloc(tmem_slot, TS::kTmemCols);
   sl::tc_fence_before();
   __syncthreads();
   sl::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int m_tiles = M_total / BM;  // GATED: I/128 column blocks; else H/128
+  const int m_tiles = M_total / TS::kRowsOut;
   if constexpr (GATED) {
     // the work items, token rows and slot weights come from the launches
     // just before this one
@@ -295,7 +428,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(
     sl::pdl_trigger();
   }
   // down GEMM: items were written two launches back (align), so they may be
-  // read before the wait; its A operand (the activations) may not
+  // read before the wait; its B operand (the activations) may not.
   // phase -1: every item; 0: items of resident experts; 1: items of experts
   // streamed in by this gap (they follow the resident ones)
   const int num_items = ws_hdr[WS_NUM_ITEMS];
@@ -311,7 +444,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(
       const uint64_t pol_w = sl::policy_evict_first();
       const uint64_t pol_b = sl::policy_evict_last();
       int stage = 0;
-      uint32_t phase = 0;
+      uint32_t phase_bit = 0;
       uint32_t issued_phase_mask = 0;  // stages with a TMA in flight at exit
       bool ok = true;
       // Down GEMM under PDL: the first STAGES weight tiles are fetched before
@@ -334,18 +467,18 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(
         const bool sh = it.x >= S;
         const CUtensorMap* tw = sh ? &tm_wsh : &tm_w;
         const int e = sh ? it.x - S : it.x;
-        // weight rows of this tile in the 2-D view [experts * rows, K]
-        const int row0 = GATED ? e * 2 * M_total + mt * BM : e * M_total + mt * BM;
+        // weight rows in the 2-D view [experts * rows, K]
+        const int row0 = GATED ? e * 2 * M_total + mt * 64 : e * M_total + mt * BM;
         for (int kb = 0; kb < k_blocks; ++kb) {
-          if (*abort_flag || !sl::mbar_wait(&empty[stage], phase ^ 1)) {
+          if (*abort_flag || !sl::mbar_wait(&empty[stage], phase_bit ^ 1)) {
             ok = false;
             break;
           }
           sl::mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
-          __nv_bfloat16* a0 = sA + (stage * Cfg::kNumA) * Cfg::kATile;
+          __nv_bfloat16* a0 = sA + stage * Cfg::kATile;
           sl::tma_load_2d(a0, tw, &full[stage], kb * BK, row0, pol_w);
-          if constexpr (GATED)
-            sl::tma_load_2d(a0 + Cfg::kATile, tw, &full[stage], kb * BK, row0 + M_total, pol_w);
+          if constexpr (GATED)  // up rows under the gate rows
+            sl::tma_load_2d(a0 + 64 * BK, tw, &full[stage], kb * BK, row0 + M_total, pol_w);
           if (waited) {
             sl::tma_load_2d(sB + stage * Cfg::kBTile, &tm_b, &full[stage], kb * BK, it.y, pol_b);
           } else {
@@ -354,10 +487,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(
             pend_row[pend_n] = it.y;
             if (++pend_n == STAGES) flush();
           }
-          issued_phase_mask = (issued_phase_mask & ~(1u << stage)) | (phase << stage);
+          issued_phase_mask = (issued_phase_mask & ~(1u << stage)) | (phase_bit << stage);
           if (++stage == STAGES) {
             stage = 0;
-            phase ^= 1;
+            phase_bit ^= 1;
           }
         }
       }
@@ -375,7 +508,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(
     if (sl::elect_one()) {
       constexpr uint32_t idesc = sl::umma_idesc_bf16(BM, BN);
       int stage = 0;
-      uint32_t phase = 0;
+      uint32_t phase_bit = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
@@ -385,28 +518,23 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(
           break;
         }
         sl::tc_fence_after();
-        const uint32_t d0 = tmem_base + acc * Cfg::kAccCols;
+        const uint32_t d0 = tmem_base + acc * TS::kAccCols;
         for (int kb = 0; kb < k_blocks; ++kb) {
-          if (*abort_flag || !sl::mbar_wait(&full[stage], phase)) {
+          if (*abort_flag || !sl::mbar_wait(&full[stage], phase_bit)) {
             ok = false;
             break;
           }
           sl::tc_fence_after();
-          const uint32_t a_addr = sl::smem_u32(sA + (stage * Cfg::kNumA) * Cfg::kATile);
+          const uint32_t a_addr = sl::smem_u32(sA + stage * Cfg::kATile);
           const uint32_t b_addr = sl::smem_u32(sB + stage * Cfg::kBTile);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t bd = sl::umma_desc_sw128(b_addr + k * 32);
-            const uint32_t accum = (kb | k) != 0;
-            sl::umma_bf16(d0, sl::umma_desc_sw128(a_addr + k * 32), bd, idesc, accum);
-            if constexpr (GATED)
-              sl::umma_bf16(d0 + BN, sl::umma_desc_sw128(a_addr + Cfg::kATile * 2 + k * 32), bd,
-                            idesc, accum);
-          }
+          for (int k = 0; k < BK / 16; ++k)
+            sl::umma_bf16(d0, sl::umma_desc_sw128(a_addr + k * 32),
+                          sl::umma_desc_sw128(b_addr + k * 32), idesc, (kb | k) != 0);
           sl::umma_commit(&empty[stage]);  // stage free once these MMAs finish
           if (++stage == STAGES) {
             stage = 0;
-            phase ^= 1;
+            phase_bit ^= 1;
           }
         }
         if (!ok) break;
@@ -427,57 +555,26 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(
   } else {
     // --------------------------------------------------------- epilogue
     const int q = warp & 3;
-    const int row = q * 32 + lane;  // TMEM lane = weight row within the tile
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      if (*abort_flag || !sl::mbar_wait(&tfull[acc], acc_phase)) {
+      const bool ok = !*abort_flag && sl::mbar_wait(&tfull[acc], acc_phase);
+      // the four epilogue warps must agree before the exchange barriers
+      if (epi_any(!ok)) {
         atomicExch(status, SL_ERR_TIMEOUT);
         *abort_flag = 1;
         break;
       }
       sl::tc_fence_after();
       const int4 it = items[item_lo + tile / m_tiles];
-      const int mt = tile % m_tiles;
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * Cfg::kAccCols;
-      float v0[BN];
-      float v1[BN];
-#pragma unroll
-      for (int c = 0; c < BN; c += 16) {
-        float tmp[16];
-        sl::tmem_ld16(taddr + c, tmp);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v0[c + i] = tmp[i];
-        if constexpr (GATED) {
-          sl::tmem_ld16(taddr + BN + c, tmp);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) v1[c + i] = tmp[i];
-        }
-      }
+      epilogue_tile<BN, GATED>(tmem_base + acc * TS::kAccCols, q, lane, it, tile % m_tiles,
+                               out, out_ld, xchg);
       sl::tc_fence_before();
       __syncwarp();
       if (lane == 0) sl::mbar_arrive(&tempty[acc]);
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;
-      }
-      const int col = mt * BM + row;
-      __nv_bfloat16* dst = out + static_cast<size_t>(it.y) * out_ld + col;
-#pragma unroll
-      for (int n = 0; n < BN; ++n) {
-        if (n < it.z) {
-          float r;
-          if constexpr (GATED) {
-            // vLLM's torch-native chain: bf16 GEMM outputs, bf16 SiLU, bf16 mul
-            const float g = sl::bf16_round(v0[n]);
-            const float u = sl::bf16_round(v1[n]);
-            const float sg = sl::bf16_round(g / (1.0f + expf(-g)));
-            r = sg * u;
-          } else {
-            r = v0[n];
-          }
-          dst[static_cast<size_t>(n) * out_ld] = __float2bfloat16(r);
-        }
       }
     }
   }
@@ -486,7 +583,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(
   if (warp == 1) {
     __syncwarp();
     sl::tc_fence_after();
-    sl::tmem_dealloc(tmem_base, Cfg::kTmemCols);
+    sl::tmem_dealloc(tmem_base, TS::kTmemCols);
   }
 }
 
@@ -494,26 +591,21 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(
 // fp8 e4m3 expert weights with fp32 128x128 block scales (vLLM's block-fp8
 // MoE layout: w13_scale [E, 2I/128, H/128], w2_scale [E, H/128, I/128]).
 // TMA brings raw fp8 weight tiles (128 rows x 64 K, unswizzled) into a raw
-// ring; a converter warpgroup dequantises each tile (fp8 -> fp32 x block
-// scale -> bf16) into the 128B-swizzled bf16 layout the MMA reads; the MMA,
-// epilogue and token tiles are those of the bf16 kernel (bf16 activations,
-// fp32 accumulation in TMEM). Roles: warp 0 producer, warp 1 MMA + TMEM,
-// warps 2-5 epilogue, warps 6-9 converter.
+// ring; a converter warpgroup dequantises each row (fp8 -> fp32 x block scale
+// -> bf16) into the 128B-swizzled bf16 tile the MMA reads; MMA, epilogue and
+// token tiles are those of the bf16 kernel (bf16 activations, fp32
+// accumulation in TMEM). Roles: warp 0 producer, warp 1 MMA + TMEM, warps 2-5
+// epilogue, warps 6-9 converter.
 constexpr int kFp8Threads = 320;
 
 template <int BN, int RSTAGES, int CSTAGES, bool GATED>
 struct Fp8Cfg {
-  static constexpr int kNumA = GATED ? 2 : 1;
-  static constexpr int kRawA = BM * BK;                    // bytes (fp8)
-  static constexpr int kBTile = BN * BK;                   // bf16 elements
-  static constexpr int kCvtA = BM * BK;                    // bf16 elements
-  static constexpr int kRawBytes = kNumA * kRawA;          // per raw stage
-  static constexpr int kTxBytes = kRawBytes + kBTile * 2;  // TMA bytes per stage
-  static constexpr int kAccCols = GATED ? 2 * BN : BN;
-  static constexpr int kTmemCols = (2 * kAccCols) <= 32 ? 32 : (2 * kAccCols) <= 64 ? 64
-                                   : (2 * kAccCols) <= 128 ? 128 : 256;
-  static constexpr int kSmemBytes = CSTAGES * kNumA * kCvtA * 2 + RSTAGES * kBTile * 2 +
-                                    RSTAGES * kRawBytes + 1024 + 512;
+  static constexpr int kRawA = BM * BK;          // bytes (fp8) per raw weight tile
+  static constexpr int kBTile = BN * BK;         // bf16 elements
+  static constexpr int kCvtA = BM * BK;          // bf16 elements
+  static constexpr int kTxBytes = kRawA + kBTile * 2;  // TMA bytes per raw stage
+  static constexpr int kSmemBytes = CSTAGES * kCvtA * 2 + RSTAGES * kBTile * 2 +
+                                    RSTAGES * kRawA + 64 * kXchgStride * 4 + 1024 + 512;
 };
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -544,13 +636,15 @@ __global__ void __launch_bounds__(kFp8Threads, 1) moe_gemm_fp8_kernel(
     const int4* __restrict__ items, __nv_bfloat16* __restrict__ out, int S, int K,
     int M_total, int out_ld, int32_t* __restrict__ status, int phase) {
   using Cfg = Fp8Cfg<BN, RSTAGES, CSTAGES, GATED>;
+  using TS = TileShape<BN, GATED>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  __nv_bfloat16* sC = reinterpret_cast<__nv_bfloat16*>(smem);        // [C][kNumA][BM*BK]
-  __nv_bfloat16* sB = sC + CSTAGES * Cfg::kNumA * Cfg::kCvtA;        // [R][BN*BK]
-  uint8_t* sR = reinterpret_cast<uint8_t*>(sB + RSTAGES * Cfg::kBTile);  // [R][kNumA][BM*BK]
-  uint64_t* raw_full = reinterpret_cast<uint64_t*>(sR + RSTAGES * Cfg::kRawBytes);
+  __nv_bfloat16* sC = reinterpret_cast<__nv_bfloat16*>(smem);        // [C][BM*BK]
+  __nv_bfloat16* sB = sC + CSTAGES * Cfg::kCvtA;                     // [R][BN*BK]
+  uint8_t* sR = reinterpret_cast<uint8_t*>(sB + RSTAGES * Cfg::kBTile);  // [R][BM*BK]
+  float* xchg = reinterpret_cast<float*>(sR + RSTAGES * Cfg::kRawA);
+  uint64_t* raw_full = reinterpret_cast<uint64_t*>(xchg + 64 * kXchgStride);
   uint64_t* raw_empty = raw_full + RSTAGES;
   uint64_t* b_empty = raw_empty + RSTAGES;
   uint64_t* cvt_full = b_empty + RSTAGES;
@@ -583,7 +677,7 @@ __global__ void __launch_bounds__(kFp8Threads, 1) moe_gemm_fp8_kernel(
     sl::tma_prefetch_desc(&tm_wsh);
     sl::tma_prefetch_desc(&tm_b);
   }
-  if (warp == 1) sl::tmem_alloc(tmem_slot, Cfg::kTmemCols);
+  if (warp == 1) sl::tmem_alloc(tmem_slot, TS::kTmemCols);
   sl::tc_fence_before();
   __syncthreads();
   sl::tc_fence_after();
@@ -591,7 +685,7 @@ __global__ void __launch_bounds__(kFp8Threads, 1) moe_gemm_fp8_kernel(
   sl::pdl_wait();
   sl::pdl_trigger();
 
-  const int m_tiles = M_total / BM;
+  const int m_tiles = M_total / TS::kRowsOut;
   const int num_items = ws_hdr[WS_NUM_ITEMS];
   const int n_hit = ws_hdr[WS_NUM_HIT_ITEMS];
   const int item_lo = phase == 1 ? n_hit : 0;
@@ -615,7 +709,7 @@ __global__ void __launch_bounds__(kFp8Threads, 1) moe_gemm_fp8_kernel(
         const bool sh = it.x >= S;
         const CUtensorMap* tw = sh ? &tm_wsh : &tm_w;
         const int e = sh ? it.x - S : it.x;
-        const int row0 = GATED ? e * 2 * M_total + mt * BM : e * M_total + mt * BM;
+        const int row0 = GATED ? e * 2 * M_total + mt * 64 : e * M_total + mt * BM;
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (*abort_flag || !sl::mbar_wait(&raw_empty[r], rph ^ 1) ||
               !sl::mbar_wait(&b_empty[r], rph ^ 1)) {
@@ -623,10 +717,10 @@ __global__ void __launch_bounds__(kFp8Threads, 1) moe_gemm_fp8_kernel(
             break;
           }
           sl::mbar_arrive_expect_tx(&raw_full[r], Cfg::kTxBytes);
-          uint8_t* a0 = sR + r * Cfg::kRawBytes;
+          uint8_t* a0 = sR + r * Cfg::kRawA;
           sl::tma_load_2d(a0, tw, &raw_full[r], kb * BK, row0, pol_w);
           if constexpr (GATED)
-            sl::tma_load_2d(a0 + Cfg::kRawA, tw, &raw_full[r], kb * BK, row0 + M_total, pol_w);
+            sl::tma_load_2d(a0 + 64 * BK, tw, &raw_full[r], kb * BK, row0 + M_total, pol_w);
           sl::tma_load_2d(sB + r * Cfg::kBTile, &tm_b, &raw_full[r], kb * BK, it.y, pol_b);
           issued_mask = (issued_mask & ~(1u << r)) | (rph << r);
           if (++r == RSTAGES) {
@@ -656,24 +750,19 @@ __global__ void __launch_bounds__(kFp8Threads, 1) moe_gemm_fp8_kernel(
           break;
         }
         sl::tc_fence_after();
-        const uint32_t d0 = tmem_base + acc * Cfg::kAccCols;
+        const uint32_t d0 = tmem_base + acc * TS::kAccCols;
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (*abort_flag || !sl::mbar_wait(&cvt_full[c], cph)) {
             ok = false;
             break;
           }
           sl::tc_fence_after();
-          const uint32_t a_addr = sl::smem_u32(sC + (c * Cfg::kNumA) * Cfg::kCvtA);
+          const uint32_t a_addr = sl::smem_u32(sC + c * Cfg::kCvtA);
           const uint32_t b_addr = sl::smem_u32(sB + r * Cfg::kBTile);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t bd = sl::umma_desc_sw128(b_addr + k * 32);
-            const uint32_t accum = (kb | k) != 0;
-            sl::umma_bf16(d0, sl::umma_desc_sw128(a_addr + k * 32), bd, idesc, accum);
-            if constexpr (GATED)
-              sl::umma_bf16(d0 + BN, sl::umma_desc_sw128(a_addr + Cfg::kCvtA * 2 + k * 32), bd,
-                            idesc, accum);
-          }
+          for (int k = 0; k < BK / 16; ++k)
+            sl::umma_bf16(d0, sl::umma_desc_sw128(a_addr + k * 32),
+                          sl::umma_desc_sw128(b_addr + k * 32), idesc, (kb | k) != 0);
           sl::umma_commit(&cvt_empty[c]);
           sl::umma_commit(&b_empty[r]);
           if (++c == CSTAGES) {
@@ -710,11 +799,16 @@ __global__ void __launch_bounds__(kFp8Threads, 1) moe_gemm_fp8_kernel(
       const bool sh = it.x >= S;
       const int e = sh ? it.x - S : it.x;
       const float* scale = sh ? wsh_scale : w_scale;
-      // scale rows: GATED -> [2I/128] (gate block mt, up block I/128 + mt); else [H/128]
-      const int srows = GATED ? 2 * (M_total / 128) : M_total / 128;
-      const float* srow_a = scale + (static_cast<size_t>(e) * srows + mt) * kscale;
-      const float* srow_b = GATED ? scale + (static_cast<size_t>(e) * srows + M_total / 128 + mt) * kscale
-                                  : srow_a;
+      // the 128x128 scale block of this thread's weight row
+      int sblk;
+      if constexpr (GATED) {
+        const int srows = 2 * (M_total / 128);
+        const int wrow = row < 64 ? mt * 64 + row : M_total + mt * 64 + (row - 64);
+        sblk = e * srows + wrow / 128;
+      } else {
+        sblk = e * (M_total / 128) + mt;
+      }
+      const float* srow = scale + static_cast<size_t>(sblk) * kscale;
       bool ok = true;
       for (int kb = 0; kb < k_blocks; ++kb) {
         if (*abort_flag || !sl::mbar_wait(&raw_full[r], rph) ||
@@ -722,27 +816,22 @@ __global__ void __launch_bounds__(kFp8Threads, 1) moe_gemm_fp8_kernel(
           ok = false;
           break;
         }
+        const float sc = srow[kb >> 1];
+        const uint4* src = reinterpret_cast<const uint4*>(sR + r * Cfg::kRawA + row * BK);
+        uint8_t* dst_row = reinterpret_cast<uint8_t*>(sC + c * Cfg::kCvtA) + row * 128;
 #pragma unroll
-        for (int a = 0; a < Cfg::kNumA; ++a) {
-          const float sc = (a == 0 ? srow_a : srow_b)[kb >> 1];
-          const uint4* src =
-              reinterpret_cast<const uint4*>(sR + r * Cfg::kRawBytes + a * Cfg::kRawA + row * BK);
-          uint8_t* dst_row = reinterpret_cast<uint8_t*>(sC + (c * Cfg::kNumA + a) * Cfg::kCvtA) +
-                             row * 128;
+        for (int q4 = 0; q4 < 4; ++q4) {  // 16 fp8 -> 16 bf16 = two 16-byte chunks
+          float f[16];
+          fp8x16_to_f32(src[q4], f);
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {  // 16 fp8 -> 16 bf16 = two 16-byte chunks
-            float f[16];
-            fp8x16_to_f32(src[q], f);
+          for (int h = 0; h < 2; ++h) {
+            uint4 o;
+            __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              uint4 o;
-              __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
-#pragma unroll
-              for (int j = 0; j < 4; ++j)
-                o2[j] = __floats2bfloat162_rn(f[8 * h + 2 * j] * sc, f[8 * h + 2 * j + 1] * sc);
-              const int chunk = 2 * q + h;  // 16-byte chunk within the 128-byte row
-              *reinterpret_cast<uint4*>(dst_row + ((chunk ^ (row & 7)) << 4)) = o;
-            }
+            for (int j = 0; j < 4; ++j)
+              o2[j] = __floats2bfloat162_rn(f[8 * h + 2 * j] * sc, f[8 * h + 2 * j + 1] * sc);
+            const int chunk = 2 * q4 + h;  // 16-byte chunk within the 128-byte row
+            *reinterpret_cast<uint4*>(dst_row + ((chunk ^ (row & 7)) << 4)) = o;
           }
         }
         fence_proxy_async_smem();  // generic-proxy writes -> visible to tcgen05.mma
@@ -769,56 +858,25 @@ __global__ void __launch_bounds__(kFp8Threads, 1) moe_gemm_fp8_kernel(
   } else {
     // --------------------------------------------------------- epilogue
     const int q = warp & 3;
-    const int row = q * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      if (*abort_flag || !sl::mbar_wait(&tfull[acc], acc_phase)) {
+      const bool ok = !*abort_flag && sl::mbar_wait(&tfull[acc], acc_phase);
+      if (epi_any(!ok)) {
         atomicExch(status, SL_ERR_TIMEOUT);
         *abort_flag = 1;
         break;
       }
       sl::tc_fence_after();
       const int4 it = items[item_lo + tile / m_tiles];
-      const int mt = tile % m_tiles;
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * Cfg::kAccCols;
-      float v0[BN];
-      float v1[BN];
-#pragma unroll
-      for (int cc = 0; cc < BN; cc += 16) {
-        float tmp[16];
-        sl::tmem_ld16(taddr + cc, tmp);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v0[cc + i] = tmp[i];
-        if constexpr (GATED) {
-          sl::tmem_ld16(taddr + BN + cc, tmp);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) v1[cc + i] = tmp[i];
-        }
-      }
+      epilogue_tile<BN, GATED>(tmem_base + acc * TS::kAccCols, q, lane, it, tile % m_tiles,
+                               out, out_ld, xchg);
       sl::tc_fence_before();
       __syncwarp();
       if (lane == 0) sl::mbar_arrive(&tempty[acc]);
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;
-      }
-      const int col = mt * BM + row;
-      __nv_bfloat16* dst = out + static_cast<size_t>(it.y) * out_ld + col;
-#pragma unroll
-      for (int n = 0; n < BN; ++n) {
-        if (n < it.z) {
-          float rr;
-          if constexpr (GATED) {
-            const float g = sl::bf16_round(v0[n]);
-            const float u = sl::bf16_round(v1[n]);
-            const float sg = sl::bf16_round(g / (1.0f + expf(-g)));
-            rr = sg * u;
-          } else {
-            rr = v0[n];
-          }
-          dst[static_cast<size_t>(n) * out_ld] = __float2bfloat16(rr);
-        }
       }
     }
   }
@@ -827,9 +885,10 @@ __global__ void __launch_bounds__(kFp8Threads, 1) moe_gemm_fp8_kernel(
   if (warp == 1) {
     __syncwarp();
     sl::tc_fence_after();
-    sl::tmem_dealloc(tmem_base, Cfg::kTmemCols);
+    sl::tmem_dealloc(tmem_base, TS::kTmemCols);
   }
 }
+
 
 // ---------------------------------------------------------------- combine
 // OUT_F32 = false: out = bf16(shared + bf16(scale * bf16(sum_j w z)))  (vLLM
@@ -966,7 +1025,7 @@ int launch_gemm_fp8(const CUtensorMap& tw, const CUtensorMap& twsh, const CUtens
                                      Cfg::kSmemBytes));
     configured_dev = dev;
   }
-  const int max_tiles = max_items * (M_total / BM);
+  const int max_tiles = max_items * (M_total / TileShape<BN, GATED>::kRowsOut);
   int grid = sl_device_sm_count();
   if (grid <= 0) return SL_ERR_CUDA;
   if (max_tiles < grid) grid = max_tiles > 0 ? max_tiles : 1;
@@ -991,7 +1050,7 @@ int launch_gemm(const CUtensorMap& tw, const CUtensorMap& twsh, const CUtensorMa
                                      Cfg::kSmemBytes));
     configured_dev = dev;
   }
-  const int max_tiles = max_items * (M_total / BM);
+  const int max_tiles = max_items * (M_total / TileShape<BN, GATED>::kRowsOut);
   int grid = sl_device_sm_count();
   if (grid <= 0) return SL_ERR_CUDA;
   if (max_tiles < grid) grid = max_tiles > 0 ? max_tiles : 1;
@@ -1005,7 +1064,7 @@ int launch_gemm(const CUtensorMap& tw, const CUtensorMap& twsh, const CUtensorMa
 extern "C" size_t sl_fused_experts_workspace_bytes(int T, int topk, int H, int I,
                                                    int num_slots, int n_shared) {
   if (T < 0 || topk <= 0 || H <= 0 || I <= 0 || num_slots <= 0 || n_shared < 0) return 0;
-  return ws_layout(T, topk, H, I, num_slots, n_shared, choose_bn(T)).total;
+  return ws_layout(T, topk, H, I, num_slots, n_shared, choose_bn(T, topk, num_slots)).total;
 }
 
 namespace {
@@ -1034,7 +1093,7 @@ int run_fused(const void* hidden, int T, int H, int I, const sl_expert_weights& 
   if ((reinterpret_cast<uintptr_t>(workspace) & 255) ||
       ((reinterpret_cast<uintptr_t>(hidden) | reinterpret_cast<uintptr_t>(out)) & 15))
     return SL_ERR_INVALID;
-  const int BN = choose_bn(T);
+  const int BN = choose_bn(T, topk, num_slots);
   const WsLayout L = ws_layout(T, topk, H, I, num_slots, n_shared, BN);
   if (workspace_bytes < L.total) return SL_ERR_INVALID;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
@@ -1047,12 +1106,12 @@ int run_fused(const void* hidden, int T, int H, int I, const sl_expert_weights& 
 
   CUtensorMap m_w13, m_w13sh, m_x, m_w2, m_w2sh, m_a;
   const int nsh = n_shared > 0 ? n_shared : 0;
-  bool ok = make_map(&m_w13, w.w13, H, uint64_t(num_slots) * 2 * I, BM, fp8) &&
+  bool ok = make_map(&m_w13, w.w13, H, uint64_t(num_slots) * 2 * I, 64, fp8) &&
             make_map(&m_w2, w.w2, I, uint64_t(num_slots) * H, BM, fp8) &&
             make_map(&m_x, X, H, uint64_t(L.max_rows), BN) &&
             make_map(&m_a, A, I, uint64_t(L.max_rows), BN);
   if (ok && nsh) {
-    ok = make_map(&m_w13sh, w.shared_w13, H, uint64_t(nsh) * 2 * I, BM, fp8) &&
+    ok = make_map(&m_w13sh, w.shared_w13, H, uint64_t(nsh) * 2 * I, 64, fp8) &&
          make_map(&m_w2sh, w.shared_w2, I, uint64_t(nsh) * H, BM, fp8);
   } else {
     m_w13sh = m_w13;
@@ -1060,28 +1119,45 @@ int run_fused(const void* hidden, int T, int H, int I, const sl_expert_weights& 
   }
   if (!ok) return SL_ERR_INVALID;
 
+  // one CTA gathers decode-sized steps; larger ones get a grid-wide gather
+  const bool big = static_cast<long>(T) * (topk + nsh) * H > (8L << 20);
   if (phase != 1)
     SL_CUDA_TRY(sl::launch(align_kernel, dim3(1), dim3(1024), 0, st, topk_ids, T, topk,
                            expert_map, global_n, num_slots, nsh, nsh ? sh_t0 : 0,
                            nsh ? sh_nt : 0, BN, static_cast<const __nv_bfloat16*>(hidden), H,
                            hdr, items, pair_pos, X, L.max_items,
-                           static_cast<const uint8_t*>(fill_state)));
-  int rc;
-  if (fp8) {
-    rc = launch_gemm_fp8<16, 8, 2, true>(m_w13, m_w13sh, m_x, w.w13_scale, w.shared_w13_scale,
-                                         hdr, items, A, num_slots, H, I, I, hdr, L.max_items,
-                                         st, phase);
-    if (rc != SL_OK) return rc;
-    rc = launch_gemm_fp8<16, 12, 3, false>(m_w2, m_w2sh, m_a, w.w2_scale, w.shared_w2_scale,
-                                           hdr, items, Z, num_slots, I, H, H, hdr, L.max_items,
-                                           st, phase);
-  } else {
-    rc = launch_gemm<16, 6, true>(m_w13, m_w13sh, m_x, hdr, items, A, num_slots, H, I, I, hdr,
-                                  L.max_items, st, phase);
-    if (rc != SL_OK) return rc;
-    rc = launch_gemm<16, 12, false>(m_w2, m_w2sh, m_a, hdr, items, Z, num_slots, I, H, H, hdr,
-                                    L.max_items, st, phase);
+                           static_cast<const uint8_t*>(fill_state), big ? 0 : 1));
+  if (phase != 1 && big)
+    SL_CUDA_TRY(sl::launch(gather_kernel, dim3(2 * sl_device_sm_count()), dim3(256), 0, st,
+                           static_cast<const int32_t*>(hdr),
+                           static_cast<const int32_t*>(pair_pos), T * topk, topk, nsh,
+                           nsh ? sh_t0 : 0, nsh ? sh_nt : 0,
+                           static_cast<const __nv_bfloat16*>(hidden), H, X));
+  int rc = SL_OK;
+#define SL_GEMMS(BNV, R1, C1, R2, C2, S1, S2)                                                    \
+  if (fp8) {                                                                                     \
+    rc = launch_gemm_fp8<BNV, R1, C1, true>(m_w13, m_w13sh, m_x, w.w13_scale,                   \
+                                            w.shared_w13_scale, hdr, items, A, num_slots, H, I, \
+                                            I, hdr, L.max_items, st, phase);                     \
+    if (rc == SL_OK)                                                                             \
+      rc = launch_gemm_fp8<BNV, R2, C2, false>(m_w2, m_w2sh, m_a, w.w2_scale,                   \
+                                               w.shared_w2_scale, hdr, items, Z, num_slots, I,  \
+                                               H, H, hdr, L.max_items, st, phase);               \
+  } else {                                                                                       \
+    rc = launch_gemm<BNV, S1, true>(m_w13, m_w13sh, m_x, hdr, items, A, num_slots, H, I, I, hdr, \
+                                    L.max_items, st, phase);                                     \
+    if (rc == SL_OK)                                                                             \
+      rc = launch_gemm<BNV, S2, false>(m_w2, m_w2sh, m_a, hdr, items, Z, num_slots, I, H, H,     \
+                                       hdr, L.max_items, st, phase);                             \
   }
+  if (BN == 16) {
+    SL_GEMMS(16, 12, 4, 12, 4, 12, 12)
+  } else if (BN == 64) {
+    SL_GEMMS(64, 8, 3, 8, 3, 9, 9)
+  } else {
+    SL_GEMMS(128, 6, 3, 6, 3, 6, 6)
+  }
+#undef SL_GEMMS
   if (rc != SL_OK) return rc;
   if (phase == 0) return SL_OK;
   dim3 cgrid((H / 8 + 255) / 256, T);

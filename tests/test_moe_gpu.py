@@ -156,3 +156,29 @@ def test_fp8_block_scaled_cases(T, H, I, S, E, k, n_sh, scale):
         shared = sum(omoe.shared_experts(hs, qs13[i], qs2[i], ss13[i], ss2[i]).float()
                      for i in range(n_sh)).to(torch.bfloat16)
     assert_moe_close(out, omoe.layer_output(routed, shared, scale), rtol=5e-2)
+
+
+@pytest.mark.parametrize("fp8", [False, True], ids=["bf16", "fp8"])
+@pytest.mark.parametrize("T,H,I,S,E,k", [
+    (64, 1024, 512, 16, 16, 8),      # 32 tokens per expert: 64-token tiles
+    (256, 1024, 512, 16, 16, 8),     # 128 per expert: 128-token tiles
+    (1024, 1024, 512, 16, 20, 8),    # grid-wide token gather, a few unmapped experts
+])
+def test_prefill_sized_steps(T, H, I, S, E, k, fp8):
+    """Token tiles of 64 / 128 and the grid-wide gather, bf16 and fp8."""
+    from sluice_b200 import synth
+    hs, w13, w2, emap, ti, tw, _, _ = _random_case(T, H, I, S, E, k, 0, seed=T + k,
+                                                   map_frac=1.0 if E == S else 0.8)
+    c = lambda t: None if t is None else t.cuda()
+    kw, ref_kw, rtol = {}, {}, RTOL
+    if fp8:
+        w13, s13 = synth.quantize_block_fp8(w13)
+        w2, s2 = synth.quantize_block_fp8(w2)
+        kw = dict(w1_scale=c(s13), w2_scale=c(s2))
+        ref_kw = dict(w13_scale=s13, w2_scale=s2)
+        rtol = 5e-2
+    out = ops.fused_experts(c(hs), c(w13), c(w2), c(tw), c(ti), global_num_experts=E,
+                            expert_map=c(emap), **kw)
+    torch.cuda.synchronize()
+    assert ops.workspace_status(ops.fused_experts.last_workspace) == 0
+    assert_moe_close(out, omoe.fused_experts(hs, w13, w2, tw, ti, emap, **ref_kw), rtol=rtol)
