@@ -238,6 +238,178 @@ __global__ void __launch_bounds__(1024) align_kernel(
   }
 }
 
+// Decode-sized steps (at most kSmallP pairs): the same grouping computed
+// redundantly and deterministically by every CTA of a small grid (a pair's
+// row is its rank among the earlier pairs of its slot), so each CTA can
+// gather its share of the token rows at once; CTA 0 publishes the metadata.
+constexpr int kSmallP = 1024;
+constexpr int kAlignSmallThreads = 256;
+constexpr int kAlignSmallCtas = 32;
+
+__global__ void __launch_bounds__(kAlignSmallThreads) align_small_kernel(
+    const int32_t* __restrict__ ids, int T, int topk, const int32_t* __restrict__ emap,
+    int G, int S, int n_sh, int sh_t0, int sh_nt, int BN,
+    const __nv_bfloat16* __restrict__ hs, int H,
+    int32_t* __restrict__ ws_hdr, int4* __restrict__ items, int32_t* __restrict__ pair_pos,
+    __nv_bfloat16* __restrict__ X, int max_items, const uint8_t* __restrict__ fill_state) {
+  __shared__ int cnt[kMaxCode];
+  __shared__ int ibase[kMaxCode];
+  __shared__ int sp[kSmallP];    // slot of each pair, then its row
+  __shared__ uint32_t fill_bits[kMaxCode / 32 + 1];
+  __shared__ int warp_sums[kAlignSmallThreads / 32];
+  __shared__ int grp_total;
+  sl::pdl_wait();
+  sl::pdl_trigger();
+  const int tid = threadIdx.x, nthr = blockDim.x;
+  const int lane = tid & 31, warp = tid >> 5, nwarps = nthr >> 5;
+  const int P = T * topk;
+  const int C = S + n_sh;
+  for (int c = tid; c < C; c += nthr) cnt[c] = c < S ? 0 : sh_nt;
+  for (int w = tid; w <= kMaxCode / 32; w += nthr) fill_bits[w] = 0;
+  __syncthreads();
+  for (int p = tid; p < P; p += nthr) {
+    const int g = ids[p];
+    int sl_ = -1;
+    if (emap) {
+      if (g >= 0 && g < G) sl_ = emap[g];
+    } else {
+      sl_ = g;
+    }
+    if (sl_ < 0 || sl_ >= S) sl_ = -1;
+    sp[p] = sl_;
+    if (sl_ >= 0) atomicAdd(&cnt[sl_], 1);
+  }
+  if (fill_state != nullptr) {
+    int fS, fG, fL;
+    const StateView fv = view_from_header(const_cast<uint8_t*>(fill_state), fS, fG, fL);
+    const int nf = fv.hdr[SL_HDR_FILL_COUNT];
+    for (int f = tid; f < nf; f += nthr) {
+      const int slot = fv.fill_slot[f];
+      if (slot >= 0 && slot < S) atomicOr(&fill_bits[slot >> 5], 1u << (slot & 31));
+    }
+  }
+  __syncthreads();
+  auto is_fill = [&](int c) { return ((fill_bits[c >> 5] >> (c & 31)) & 1u) != 0; };
+  auto tiles = [&](int c) { return (cnt[c] + BN - 1) / BN; };
+  auto block_scan = [&](int v, int& total) -> int {
+    int incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += n;
+    }
+    if (lane == 31) warp_sums[warp] = incl;
+    __syncthreads();
+    if (tid == 0) {
+      int run = 0;
+      for (int w = 0; w < nwarps; ++w) {
+        const int t = warp_sums[w];
+        warp_sums[w] = run;
+        run += t;
+      }
+      grp_total = run;
+    }
+    __syncthreads();
+    const int r = warp_sums[warp] + incl - v;
+    total = grp_total;
+    __syncthreads();
+    return r;
+  };
+  // each thread owns a run of consecutive codes; resident codes first
+  const int per = (C + nthr - 1) / nthr;
+  const int c_lo = min(C, tid * per), c_hi = min(C, c_lo + per);
+  int n_hit = 0, n_fill = 0;
+  for (int group = 0; group < 2; ++group) {
+    int local = 0;
+    for (int c = c_lo; c < c_hi; ++c)
+      if (is_fill(c) == (group == 1)) local += tiles(c);
+    int total = 0;
+    int run = block_scan(local, total) + (group == 1 ? n_hit : 0);
+    for (int c = c_lo; c < c_hi; ++c)
+      if (is_fill(c) == (group == 1)) {
+        ibase[c] = run;
+        run += tiles(c);
+      }
+    if (group == 0) n_hit = total;
+    else n_fill = total;
+  }
+  __syncthreads();
+  const int n_items = n_hit + n_fill;
+  const bool lead = blockIdx.x == 0;
+  if (lead && tid == 0) {
+    ws_hdr[WS_STATUS] = (n_items > max_items) ? SL_ERR_INVALID : SL_OK;
+    ws_hdr[WS_NUM_ITEMS] = n_items <= max_items ? n_items : 0;
+    ws_hdr[WS_NUM_ROWS] = n_items * BN;
+    ws_hdr[WS_NUM_HIT_ITEMS] = n_items <= max_items ? n_hit : 0;
+    for (int i = 0; i < n_sh; ++i) ws_hdr[WS_SH_BASE + i] = ibase[S + i] * BN;
+  }
+  if (n_items > max_items) return;
+  if (lead)
+    for (int c = tid; c < C; c += nthr) {
+      const int nt = tiles(c);
+      for (int i = 0; i < nt; ++i)
+        items[ibase[c] + i] = make_int4(c, (ibase[c] + i) * BN, min(BN, cnt[c] - i * BN), 0);
+    }
+  // row of each pair: rank among the earlier pairs of the same slot
+  int myrow[kSmallP / kAlignSmallThreads];
+#pragma unroll
+  for (int k = 0; k < kSmallP / kAlignSmallThreads; ++k) {
+    const int p = tid + k * nthr;
+    myrow[k] = -1;
+    if (p < P) {
+      const int s0 = sp[p];
+      if (s0 >= 0) {
+        int r = 0;
+        for (int q = 0; q < p; ++q) r += sp[q] == s0;
+        myrow[k] = ibase[s0] * BN + r;
+      }
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < kSmallP / kAlignSmallThreads; ++k) {
+    const int p = tid + k * nthr;
+    if (p < P) {
+      sp[p] = myrow[k];
+      if (lead) pair_pos[p] = myrow[k];
+    }
+  }
+  __syncthreads();
+  // this CTA's share of the rows: routed pairs, then each shared expert's tokens
+  const int vrow = H >> 3;
+  const uint4* src = reinterpret_cast<const uint4*>(hs);
+  uint4* dst = reinterpret_cast<uint4*>(X);
+  const long n_routed = static_cast<long>(P) * vrow;
+  const long n_total = n_routed + static_cast<long>(n_sh) * sh_nt * vrow;
+  const long stride = static_cast<long>(gridDim.x) * nthr;
+  for (long q0 = static_cast<long>(blockIdx.x) * nthr + tid; q0 < n_total; q0 += 4 * stride) {
+    uint4 v[4];
+    long d[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const long q = q0 + u * stride;
+      d[u] = -1;
+      if (q < n_routed) {
+        const int p = static_cast<int>(q / vrow), c = static_cast<int>(q % vrow);
+        const int pos = sp[p];
+        if (pos >= 0) {
+          d[u] = static_cast<long>(pos) * vrow + c;
+          v[u] = src[static_cast<long>(p / topk) * vrow + c];
+        }
+      } else if (q < n_total) {
+        const long r = (q - n_routed) / vrow;
+        const int c = static_cast<int>((q - n_routed) % vrow);
+        const int i = static_cast<int>(r / sh_nt), t = static_cast<int>(r % sh_nt);
+        d[u] = static_cast<long>(ibase[S + i] * BN + t) * vrow + c;
+        v[u] = src[static_cast<long>(sh_t0 + t) * vrow + c];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (d[u] >= 0) dst[d[u]] = v[u];
+  }
+}
+
 // Token-row gather for large steps, spread over the whole GPU: row of pair p
 // (pair_pos) <- hidden row p / topk; shared experts' rows <- their tokens.
 __global__ void __launch_bounds__(256) gather_kernel(
@@ -398,6 +570,32 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if constexpr (GATED) {
+    // the work items, token rows and slot weights come from the launches
+    // just before this one
+    sl::pdl_wait();
+    sl::pdl_trigger();
+  }
+  // down GEMM: items were written two launches back (align), so they may be
+  // read before the wait; its B operand (the activations) may not.
+  // phase -1: every item; 0: items of resident experts; 1: items of experts
+  // streamed in by this gap (they follow the resident ones)
+  const int m_tiles = M_total / TS::kRowsOut;
+  const int num_items = ws_hdr[WS_NUM_ITEMS];
+  const int n_hit = ws_hdr[WS_NUM_HIT_ITEMS];
+  const int item_lo = phase == 1 ? n_hit : 0;
+  const int item_hi = phase == 0 ? n_hit : num_items;
+  const int num_tiles = (item_hi > item_lo ? item_hi - item_lo : 0) * m_tiles;
+  const int k_blocks = K / BK;
+  if (static_cast<int>(blockIdx.x) >= num_tiles) {
+    // nothing for this CTA (e.g. phase 1 of a step without misses): leave
+    // before any set-up; a dependent may start only once this grid has waited
+    if constexpr (!GATED) {
+      sl::pdl_wait();
+      sl::pdl_trigger();
+    }
+    return;
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       sl::mbar_init(&full[s], 1);
@@ -419,24 +617,6 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(
   __syncthreads();
   sl::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-
-  const int m_tiles = M_total / TS::kRowsOut;
-  if constexpr (GATED) {
-    // the work items, token rows and slot weights come from the launches
-    // just before this one
-    sl::pdl_wait();
-    sl::pdl_trigger();
-  }
-  // down GEMM: items were written two launches back (align), so they may be
-  // read before the wait; its B operand (the activations) may not.
-  // phase -1: every item; 0: items of resident experts; 1: items of experts
-  // streamed in by this gap (they follow the resident ones)
-  const int num_items = ws_hdr[WS_NUM_ITEMS];
-  const int n_hit = ws_hdr[WS_NUM_HIT_ITEMS];
-  const int item_lo = phase == 1 ? n_hit : 0;
-  const int item_hi = phase == 0 ? n_hit : num_items;
-  const int num_tiles = (item_hi > item_lo ? item_hi - item_lo : 0) * m_tiles;
-  const int k_blocks = K / BK;
 
   if (warp == 0) {
     // ------------------------------------------------------ TMA producer
@@ -656,6 +836,17 @@ __global__ void __launch_bounds__(kFp8Threads, 1) moe_gemm_fp8_kernel(
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  sl::pdl_wait();
+  sl::pdl_trigger();
+  const int m_tiles = M_total / TS::kRowsOut;
+  const int num_items = ws_hdr[WS_NUM_ITEMS];
+  const int n_hit = ws_hdr[WS_NUM_HIT_ITEMS];
+  const int item_lo = phase == 1 ? n_hit : 0;
+  const int item_hi = phase == 0 ? n_hit : num_items;
+  const int num_tiles = (item_hi > item_lo ? item_hi - item_lo : 0) * m_tiles;
+  const int k_blocks = K / BK;
+  const int kscale = K / 128;  // scale blocks along K
+  if (static_cast<int>(blockIdx.x) >= num_tiles) return;  // nothing for this CTA
   if (threadIdx.x == 0) {
     for (int s = 0; s < RSTAGES; ++s) {
       sl::mbar_init(&raw_full[s], 1);
@@ -682,17 +873,6 @@ __global__ void __launch_bounds__(kFp8Threads, 1) moe_gemm_fp8_kernel(
   __syncthreads();
   sl::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  sl::pdl_wait();
-  sl::pdl_trigger();
-
-  const int m_tiles = M_total / TS::kRowsOut;
-  const int num_items = ws_hdr[WS_NUM_ITEMS];
-  const int n_hit = ws_hdr[WS_NUM_HIT_ITEMS];
-  const int item_lo = phase == 1 ? n_hit : 0;
-  const int item_hi = phase == 0 ? n_hit : num_items;
-  const int num_tiles = (item_hi > item_lo ? item_hi - item_lo : 0) * m_tiles;
-  const int k_blocks = K / BK;
-  const int kscale = K / 128;  // scale blocks along K
 
   if (warp == 0) {
     // ------------------------------------------------------ TMA producer
@@ -1119,20 +1299,30 @@ int run_fused(const void* hidden, int T, int H, int I, const sl_expert_weights& 
   }
   if (!ok) return SL_ERR_INVALID;
 
-  // one CTA gathers decode-sized steps; larger ones get a grid-wide gather
-  const bool big = static_cast<long>(T) * (topk + nsh) * H > (8L << 20);
-  if (phase != 1)
-    SL_CUDA_TRY(sl::launch(align_kernel, dim3(1), dim3(1024), 0, st, topk_ids, T, topk,
-                           expert_map, global_n, num_slots, nsh, nsh ? sh_t0 : 0,
-                           nsh ? sh_nt : 0, BN, static_cast<const __nv_bfloat16*>(hidden), H,
-                           hdr, items, pair_pos, X, L.max_items,
-                           static_cast<const uint8_t*>(fill_state), big ? 0 : 1));
-  if (phase != 1 && big)
-    SL_CUDA_TRY(sl::launch(gather_kernel, dim3(2 * sl_device_sm_count()), dim3(256), 0, st,
-                           static_cast<const int32_t*>(hdr),
-                           static_cast<const int32_t*>(pair_pos), T * topk, topk, nsh,
-                           nsh ? sh_t0 : 0, nsh ? sh_nt : 0,
-                           static_cast<const __nv_bfloat16*>(hidden), H, X));
+  // decode-sized steps: a small grid groups and gathers at once; larger ones
+  // group in one CTA and gather with a grid-wide kernel
+  const int P = T * topk;
+  const bool small = P <= kSmallP && (num_slots + nsh) <= kMaxCode;
+  if (phase != 1) {
+    if (small) {
+      SL_CUDA_TRY(sl::launch(align_small_kernel, dim3(kAlignSmallCtas), dim3(kAlignSmallThreads),
+                             0, st, topk_ids, T, topk, expert_map, global_n, num_slots, nsh,
+                             nsh ? sh_t0 : 0, nsh ? sh_nt : 0, BN,
+                             static_cast<const __nv_bfloat16*>(hidden), H, hdr, items, pair_pos,
+                             X, L.max_items, static_cast<const uint8_t*>(fill_state)));
+    } else {
+      SL_CUDA_TRY(sl::launch(align_kernel, dim3(1), dim3(1024), 0, st, topk_ids, T, topk,
+                             expert_map, global_n, num_slots, nsh, nsh ? sh_t0 : 0,
+                             nsh ? sh_nt : 0, BN, static_cast<const __nv_bfloat16*>(hidden), H,
+                             hdr, items, pair_pos, X, L.max_items,
+                             static_cast<const uint8_t*>(fill_state), 0));
+      SL_CUDA_TRY(sl::launch(gather_kernel, dim3(2 * sl_device_sm_count()), dim3(256), 0, st,
+                             static_cast<const int32_t*>(hdr),
+                             static_cast<const int32_t*>(pair_pos), P, topk, nsh,
+                             nsh ? sh_t0 : 0, nsh ? sh_nt : 0,
+                             static_cast<const __nv_bfloat16*>(hidden), H, X));
+    }
+  }
   int rc = SL_OK;
 #define SL_GEMMS(BNV, R1, C1, R2, C2, S1, S2)                                                    \
   if (fp8) {                                                                                     \
