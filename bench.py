@@ -477,7 +477,9 @@ def run_sluice(a):
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "vs_baseline": None,
+        "dtype": "bf16" if cfg.weight_dtype == "bf16" else "fp8e4m3 weights, bf16 activations",
+        "data": "synthetic",
         "config": {"workload": _workload(cfg, min(a.slots, local_n), T, layers, world),
                    "model": cfg.name, "tokens_per_step": T, "slots": min(a.slots, local_n),
                    "layers": layers, "global_batch": T * world, "seq_len": 1,

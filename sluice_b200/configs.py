@@ -44,9 +44,12 @@ class MoEConfig:
 
     @property
     def bytes_per_expert(self) -> int:
-        """w13 [2I, H] + w2 [H, I] in the weight dtype."""
-        el = 2 if self.weight_dtype == "bf16" else 1
-        return 3 * self.hidden * self.moe_intermediate * el
+        """w13 [2I, H] + w2 [H, I] in the weight dtype (+ fp32 128x128 block
+        scales for fp8)."""
+        H, I = self.hidden, self.moe_intermediate
+        if self.weight_dtype == "bf16":
+            return 6 * H * I
+        return 3 * H * I + 4 * (2 * I // 128 * (H // 128) + (H // 128) * (I // 128))
 
     @property
     def flops_per_pair(self) -> int:

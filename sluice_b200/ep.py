@@ -80,8 +80,10 @@ class EPMoELayer:
     """One MoE layer's expert-parallel step on this rank."""
 
     def __init__(self, cfg: MoEConfig, router: ops.Router, cache, shared_w13, shared_w2,
-                 group=None):
+                 group=None, shared_w13_scale=None, shared_w2_scale=None):
         self.cfg = cfg
+        self.shared_w13_scale = shared_w13_scale
+        self.shared_w2_scale = shared_w2_scale
         self.router = router
         self.cache = cache
         self.shared_w13 = shared_w13
@@ -97,10 +99,13 @@ class EPMoELayer:
         xg, twg, tig = dispatch(x, tw, ti, self.group)
         self.last_ids = tig
         self.cache.gap(tig)
+        c = self.cache
         part = ops.fused_experts_partial(
-            xg, self.cache.w13, self.cache.w2, twg, tig, self.cache.expert_map,
-            self.shared_w13, self.shared_w2, shared_t0=self.rank * T, shared_nt=T,
-            routed_scaling_factor=self.cfg.routed_scaling_factor)
+            xg, c.w13, c.w2, twg, tig, c.expert_map, self.shared_w13, self.shared_w2,
+            shared_t0=self.rank * T, shared_nt=T,
+            routed_scaling_factor=self.cfg.routed_scaling_factor, w1_scale=c.w13_scale,
+            w2_scale=c.w2_scale, shared_w13_scale=self.shared_w13_scale,
+            shared_w2_scale=self.shared_w2_scale)
         return combine(part, self.group).to(torch.bfloat16)
 
     __call__ = forward
@@ -123,15 +128,19 @@ class EPDecodeStack:
         self.layers: list[EPMoELayer] = []
         n = cfg.num_moe_layers if num_layers is None else num_layers
         for li in range(n):
-            w13, w2 = synth.layer_weights(cfg, li, seed, device=self.device,
-                                          num_experts=per, expert_lo=lo)
-            cache = self.offloader.install_layer(w13, w2, global_n=cfg.num_experts,
-                                                 local_of=local_of, device=self.device)
-            del w13, w2
+            prm = synth.layer_params(cfg, li, seed, device=self.device, num_experts=per,
+                                     expert_lo=lo)
+            cache = self.offloader.install_layer(prm["w13"], prm["w2"], global_n=cfg.num_experts,
+                                                 local_of=local_of, device=self.device,
+                                                 w13_scale=prm.get("w13_scale"),
+                                                 w2_scale=prm.get("w2_scale"))
+            del prm
             gw, lb, sb = synth.gate_params(cfg, li, seed, device=self.device)
-            sh13, sh2 = synth.shared_weights(cfg, li, seed, device=self.device)
+            sh = synth.shared_params(cfg, li, seed, device=self.device)
             self.layers.append(EPMoELayer(cfg, ops.Router(cfg.routing, gw, lb, sb), cache,
-                                          sh13, sh2, group))
+                                          sh.get("shared_w13"), sh.get("shared_w2"), group,
+                                          sh.get("shared_w13_scale"),
+                                          sh.get("shared_w2_scale")))
         torch.cuda.synchronize(self.device)
         self.graph = None
         self._static_in = None

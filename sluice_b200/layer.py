@@ -100,14 +100,18 @@ class MoEDecodeStack:
         self.layers: list[SluiceMoELayer] = []
         n = cfg.num_moe_layers if num_layers is None else num_layers
         for li in range(n):
-            w13, w2 = synth.layer_weights(cfg, li, seed, device=self.device)
-            cache = self.offloader.install_layer(w13, w2, device=self.device)
-            del w13, w2
+            prm = synth.layer_params(cfg, li, seed, device=self.device)
+            cache = self.offloader.install_layer(prm["w13"], prm["w2"], device=self.device,
+                                                 w13_scale=prm.get("w13_scale"),
+                                                 w2_scale=prm.get("w2_scale"))
+            del prm
             gw, lb, sb = synth.gate_params(cfg, li, seed, device=self.device)
             router = ops.Router(cfg.routing, gw, lb, sb)
-            sh13, sh2 = synth.shared_weights(cfg, li, seed, device=self.device)
-            self.layers.append(SluiceMoELayer(cfg, router, cache, sh13, sh2, li,
-                                              overlap=overlap))
+            sh = synth.shared_params(cfg, li, seed, device=self.device)
+            self.layers.append(SluiceMoELayer(
+                cfg, router, cache, sh.get("shared_w13"), sh.get("shared_w2"), li,
+                overlap=overlap, shared_w13_scale=sh.get("shared_w13_scale"),
+                shared_w2_scale=sh.get("shared_w2_scale")))
         torch.cuda.synchronize(self.device)
         self.graph = None
         self._static_in = None

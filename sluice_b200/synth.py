@@ -64,6 +64,33 @@ def shared_weights(cfg: MoEConfig, layer: int, seed: int = 0, device="cuda", std
     return w13, w2
 
 
+def layer_params(cfg: MoEConfig, layer: int, seed: int = 0, device="cuda",
+                 num_experts: int | None = None, expert_lo: int = 0) -> dict:
+    """Routed expert parameters in the config's weight dtype: ``w13``, ``w2``
+    and, for fp8 configs, ``w13_scale`` / ``w2_scale`` (128x128 blocks)."""
+    w13, w2 = layer_weights(cfg, layer, seed, device=device, num_experts=num_experts,
+                            expert_lo=expert_lo)
+    if cfg.weight_dtype != "fp8":
+        return {"w13": w13, "w2": w2}
+    q13, s13 = quantize_block_fp8(w13)
+    del w13
+    q2, s2 = quantize_block_fp8(w2)
+    return {"w13": q13, "w2": q2, "w13_scale": s13, "w2_scale": s2}
+
+
+def shared_params(cfg: MoEConfig, layer: int, seed: int = 0, device="cuda") -> dict:
+    """Shared experts in the config's weight dtype (empty dict if none)."""
+    sh13, sh2 = shared_weights(cfg, layer, seed, device=device)
+    if sh13 is None:
+        return {}
+    if cfg.weight_dtype != "fp8":
+        return {"shared_w13": sh13, "shared_w2": sh2}
+    q13, s13 = quantize_block_fp8(sh13)
+    q2, s2 = quantize_block_fp8(sh2)
+    return {"shared_w13": q13, "shared_w2": q2, "shared_w13_scale": s13,
+            "shared_w2_scale": s2}
+
+
 def gate_params(cfg: MoEConfig, layer: int, seed: int = 0, device="cuda", std=0.02,
                 zipf_bias: float = 1.5):
     """(gate W [E,H] bf16, logit bias [E] f32, score bias [E] f32 or None)."""
@@ -113,5 +140,6 @@ def expected_unique(topk: int, tokens: int, num_experts: int) -> float:
     return num_experts * (1 - (1 - 1 / num_experts) ** n)
 
 
-__all__ = ["layer_weights", "shared_weights", "quantize_block_fp8", "gate_params", "TokenStream", "zipf_ids",
+__all__ = ["layer_weights", "shared_weights", "quantize_block_fp8", "layer_params",
+           "shared_params", "gate_params", "TokenStream", "zipf_ids",
            "expected_unique", "math"]
