@@ -299,6 +299,27 @@ def load_traffic():
         return {}
 
 
+def _timed_c1(stack, cfg, K, W, seed):
+    """Decode at concurrency 1 on the same stack (its own CUDA graph)."""
+    from sluice_b200 import synth
+
+    stack.capture(tokens=1)
+    st = synth.TokenStream(cfg.hidden, 1, seed=seed + 777)
+    xs = torch.stack([st.next() for _ in range(W + K)]).cuda()
+    for i in range(W):
+        stack.replay(xs[i])
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(K):
+        stack.replay(xs[W + i])
+    b.record()
+    torch.cuda.synchronize()
+    stack.check()
+    ms = a.elapsed_time(b) / K
+    return {"value": 1.0 / (ms * 1e-3), "unit": UNIT, "ms_per_step": ms}
+
+
 def _step_bytes(stack, cfg):
     """Algorithmic HBM bytes of the last step's expert GEMMs on this rank:
     sum over layers of (distinct resident selected experts + shared) x bytes."""
@@ -398,6 +419,10 @@ def run_sluice(a):
         e2e_ms = float(t.item())
     stack.check()
 
+    c1 = None
+    if world == 1 and T != 1:
+        c1 = _timed_c1(stack, cfg, K, W, a.seed)
+
     misses = stats_t.get("misses", 0) - stats_w.get("misses", 0)
     fills = stats_t.get("fills", 0) - stats_w.get("fills", 0)
     bpe = cfg.bytes_per_expert
@@ -456,7 +481,7 @@ def run_sluice(a):
         r1.record()
         torch.cuda.synchronize()
         resident = {"value": T * K / (r0.elapsed_time(r1) * 1e-3), "unit": UNIT,
-                    "slots": cfg.num_experts}
+                    "slots": cfg.num_experts, "c1": _timed_c1(rs, cfg, K, W, a.seed)}
         del rs
     elif hasattr(stack, "release"):
         stack.release()
@@ -497,6 +522,7 @@ def run_sluice(a):
         "stream": {"misses_per_step": misses / K, "fills_per_step": fills / K,
                    "bytes_per_step": host_step, "probe": sprobe,
                    "h2d_ceiling_gbs": h2d, "pcie_gen5_x16_gbs": 63.0},
+        "c1": c1,
         "resident": resident,
         "cpu_baseline": cpu,
         "gpu_launches": launches,

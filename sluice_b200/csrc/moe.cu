@@ -1141,7 +1141,18 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(
   const int nit = hi > lo ? hi - lo : 0;
   const int n1 = nit * m1, n2 = nit * m2;
   const int num_tiles = n1 + n2;
-  if (static_cast<int>(blockIdx.x) >= num_tiles || ws_hdr[WS_STATUS] != SL_OK) return;
+  if (ws_hdr[WS_STATUS] != SL_OK) return;
+  if (num_items == 0 && phase != 0) {
+    // no pair maps to a resident expert and there are no shared experts
+    const size_t n = static_cast<size_t>(T) * H;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+      if constexpr (OUT_F32) static_cast<float*>(out)[i] = 0.f;
+      else static_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16(0.f);
+    }
+    return;
+  }
+  if (static_cast<int>(blockIdx.x) >= num_tiles) return;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {

@@ -113,9 +113,7 @@ class MoEDecodeStack:
                 overlap=overlap, shared_w13_scale=sh.get("shared_w13_scale"),
                 shared_w2_scale=sh.get("shared_w2_scale")))
         torch.cuda.synchronize(self.device)
-        self.graph = None
-        self._static_in = None
-        self._static_out = None
+        self.graphs: dict = {}  # tokens -> (graph, static input, static output)
 
     def step(self, x: torch.Tensor) -> torch.Tensor:
         h = x
@@ -123,31 +121,33 @@ class MoEDecodeStack:
             h = h + layer(h)
         return h
 
-    # -- CUDA graph of one decode step ------------------------------------
+    # -- CUDA graphs of one decode step (one per token count) -----------------
     def capture(self, tokens: int) -> None:
-        self._static_in = torch.zeros(tokens, self.cfg.hidden, dtype=torch.bfloat16,
-                                      device=self.device)
+        static_in = torch.zeros(tokens, self.cfg.hidden, dtype=torch.bfloat16,
+                                device=self.device)
         s = torch.cuda.Stream(self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
-            self.step(self._static_in)  # allocator warm-up outside capture
+            self.step(static_in)  # allocator warm-up outside capture
         torch.cuda.current_stream(self.device).wait_stream(s)
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
-            self._static_out = self.step(self._static_in)
-        self.graph = g
+            static_out = self.step(static_in)
+        self.graphs[tokens] = (g, static_in, static_out)
 
-    def replay(self, x: torch.Tensor | None = None) -> torch.Tensor:
-        if x is not None:
-            self._static_in.copy_(x, non_blocking=True)
-        self.graph.replay()
-        return self._static_out
+    @property
+    def graph(self):
+        return next(iter(self.graphs.values()))[0] if self.graphs else None
+
+    def replay(self, x: torch.Tensor) -> torch.Tensor:
+        g, static_in, static_out = self.graphs[x.shape[0]]
+        static_in.copy_(x, non_blocking=True)
+        g.replay()
+        return static_out
 
     def decode_step(self, x_host: torch.Tensor, out_host: torch.Tensor) -> torch.Tensor:
         """Public end-to-end call: host tokens in, host hidden states out."""
-        self._static_in.copy_(x_host, non_blocking=True)
-        self.graph.replay()
-        out_host.copy_(self._static_out, non_blocking=True)
+        out_host.copy_(self.replay(x_host), non_blocking=True)
         return out_host
 
     def check(self) -> None:
