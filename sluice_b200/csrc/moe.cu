@@ -1342,34 +1342,61 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(
       if (et == 0) *combine_flag = (atomicAdd(&done2[mt], 1) + 1 == num_items);
       named_bar_sync(1, 128);
       if (!*combine_flag) continue;
-      // last down tile of stripe mt: out[t, stripe] for every token
+      // last down tile of stripe mt: out[t, stripe] for every token, four
+      // tokens at a time with all their loads in flight together
       __threadfence();
       const int col = mt * BM + et;
-      for (int t = 0; t < T; ++t) {
-        float r = 0.f;
-        for (int j = 0; j < topk; ++j) {
-          const int pos = pair_pos[t * topk + j];
-          if (pos >= 0)
-            r = __fadd_rn(r, __fmul_rn(__bfloat162float(Z[static_cast<size_t>(pos) * H + col]),
-                                       tw[t * topk + j]));
+      for (int t0 = 0; t0 < T; t0 += 4) {
+        float zr[4][8], wr[4][8], sv[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int t = t0 + u;
+          sv[u] = 0.f;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            zr[u][j] = 0.f;
+            wr[u][j] = 0.f;
+            if (t < T && j < topk) {
+              const int pos = pair_pos[t * topk + j];
+              if (pos >= 0) {
+                zr[u][j] = __bfloat162float(Z[static_cast<size_t>(pos) * H + col]);
+                wr[u][j] = tw[t * topk + j];
+              }
+            }
+          }
+          if (t < T && n_sh > 0 && t >= sh_t0 && t < sh_t0 + sh_nt)
+            for (int i = 0; i < n_sh; ++i)
+              sv[u] += __bfloat162float(
+                  Z[static_cast<size_t>(ws_hdr[WS_SH_BASE + i] + t - sh_t0) * H + col]);
         }
-        float o;
-        if constexpr (OUT_F32) {
-          o = r * scale;
-        } else {
-          o = sl::bf16_round(r);
-          if (scale != 1.f) o = sl::bf16_round(o * scale);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int t = t0 + u;
+          if (t >= T) break;
+          float r = 0.f;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) r = __fadd_rn(r, __fmul_rn(zr[u][j], wr[u][j]));
+          for (int j = 8; j < topk; ++j) {  // top-k beyond 8: plain loop
+            const int pos = pair_pos[t * topk + j];
+            if (pos >= 0)
+              r = __fadd_rn(r, __fmul_rn(__bfloat162float(Z[static_cast<size_t>(pos) * H + col]),
+                                         tw[t * topk + j]));
+          }
+          float o;
+          if constexpr (OUT_F32) {
+            o = r * scale;
+          } else {
+            o = sl::bf16_round(r);
+            if (scale != 1.f) o = sl::bf16_round(o * scale);
+          }
+          if (n_sh > 0 && t >= sh_t0 && t < sh_t0 + sh_nt)
+            o = (OUT_F32 ? sv[u] : sl::bf16_round(sv[u])) + o;
+          if constexpr (OUT_F32)
+            static_cast<float*>(out)[static_cast<size_t>(t) * H + col] = o;
+          else
+            static_cast<__nv_bfloat16*>(out)[static_cast<size_t>(t) * H + col] =
+                __float2bfloat16(o);
         }
-        if (n_sh > 0 && t >= sh_t0 && t < sh_t0 + sh_nt) {
-          float sv = 0.f;
-          for (int i = 0; i < n_sh; ++i)
-            sv += __bfloat162float(Z[static_cast<size_t>(ws_hdr[WS_SH_BASE + i] + t - sh_t0) * H + col]);
-          o = (OUT_F32 ? sv : sl::bf16_round(sv)) + o;
-        }
-        if constexpr (OUT_F32)
-          static_cast<float*>(out)[static_cast<size_t>(t) * H + col] = o;
-        else
-          static_cast<__nv_bfloat16*>(out)[static_cast<size_t>(t) * H + col] = __float2bfloat16(o);
       }
     }
   }
