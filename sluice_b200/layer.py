@@ -44,7 +44,26 @@ class SluiceMoELayer:
         self.last_ids = None
         self.last_logits = None
 
+    @property
+    def envelope(self) -> int:
+        """Tokens per single-wave step: ``slots // topk`` (the reference's
+        router-split batch envelope, ``offloader.py:816-842``); a fully
+        resident layer has none."""
+        if self.cache.static_full:
+            return 1 << 30
+        return max(1, self.cache.num_slots // self.cfg.routing.topk)
+
     def forward(self, hs: torch.Tensor) -> torch.Tensor:
+        thr = self.envelope
+        if hs.shape[0] > thr:
+            # larger steps (prefill) run as consecutive envelope-sized chunks,
+            # as the reference's piecewise mode requires of the batch
+            # (max_num_batched_tokens = slots // topk): every chunk is a
+            # single-wave gap plus fused experts
+            return torch.cat([self._forward_step(c) for c in hs.split(thr)])
+        return self._forward_step(hs)
+
+    def _forward_step(self, hs: torch.Tensor) -> torch.Tensor:
         tw, ti, logits = self.router.route(hs)
         self.last_ids, self.last_logits = ti, logits
         if self.overlap:

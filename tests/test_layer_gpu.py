@@ -142,3 +142,35 @@ def test_fp8_v3_routing_layer_with_streaming():
         ref = omoe.layer_output(routed, shared, cfg.routed_scaling_factor)
         assert_moe_close(out, ref, rtol=5e-2)
     assert misses > 0
+
+
+def test_prefill_sized_step_runs_in_envelope_chunks():
+    """A step larger than slots // topk runs as envelope-sized chunks; the
+    slot map then equals the oracle's after the same chunked gaps."""
+    cfg = configs.V2_LITE
+    w13, w2 = synth.layer_weights(cfg, 1, seed=12, device="cuda")
+    gw, lb, sb = synth.gate_params(cfg, 1, seed=12, device="cuda")
+    sh13, sh2 = synth.shared_weights(cfg, 1, seed=12, device="cuda")
+    cache = ExpertStreamOffloader(48, protect_frac=0.5, fast_hit=True).install_layer(
+        w13, w2, device="cuda")
+    layer = SluiceMoELayer(cfg, ops.Router(cfg.routing, gw, lb, sb), cache, sh13, sh2)
+    assert layer.envelope == 8
+    g = torch.Generator().manual_seed(13)
+    x = torch.randn(29, cfg.hidden, generator=g).to(torch.bfloat16)
+    out = layer(x.cuda())
+    torch.cuda.synchronize()
+    cache.check()
+    model = SlotPolicyModel(48, list(range(cfg.num_experts)), cfg.num_experts, 0.5, True)
+    rc = cfg.routing
+    outs = []
+    for chunk in x.split(8):
+        # the kernel's own bf16 logits (same GEMV as inside the layer)
+        logits = layer.router.route(chunk.cuda())[2].cpu()
+        tw, ti = orouting.grouped_topk(logits, rc.topk, rc.renormalize)
+        model.gap(ti.flatten().tolist())
+        routed = omoe.fused_experts(chunk, w13.cpu(), w2.cpu(), tw, ti)
+        shared = sum(omoe.expert_mlp(chunk, sh13[i].cpu(), sh2[i].cpu()).float()
+                     for i in range(cfg.n_shared)).to(torch.bfloat16)
+        outs.append(omoe.layer_output(routed, shared))
+    assert cache.expert_map.cpu().tolist() == model.expert_map
+    assert_moe_close(out, torch.cat(outs))
