@@ -54,6 +54,8 @@ def _args(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-resident", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--exchange", default="nvlink", choices=["nvlink", "nccl"],
+                    help="expert-parallel dispatch/combine (N>1): peer-memory kernels or NCCL")
     ap.add_argument("--no-overlap", action="store_true",
                     help="serialise the expert stream and the GEMMs (A/B)")
     return ap.parse_args(argv)
@@ -357,7 +359,8 @@ def run_sluice(a):
     t_build = time.perf_counter()
     if world > 1:
         from sluice_b200.ep import EPDecodeStack
-        stack = EPDecodeStack(cfg, slots=a.slots, seed=a.seed, num_layers=layers)
+        stack = EPDecodeStack(cfg, slots=a.slots, seed=a.seed, num_layers=layers,
+                              exchange=a.exchange, max_tokens=T)
         graphed = stack.capture(tokens=T)
     else:
         stack = MoEDecodeStack(cfg, slots=a.slots, seed=a.seed, num_layers=layers,
@@ -498,7 +501,9 @@ def run_sluice(a):
     local_n = cfg.num_experts // world
     offloaded = a.slots < local_n
     # per layer: gate, select, [plan, stream,] align, gate/up GEMM, down GEMM, combine
-    launches = K * layers * (8 if offloaded else 6)
+    # (+ dispatch and combine kernels under the NVLink exchange)
+    per_layer = (8 if offloaded else 6) + (2 if world > 1 and a.exchange == "nvlink" else 0)
+    launches = K * layers * per_layer
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
@@ -509,6 +514,7 @@ def run_sluice(a):
                    "model": cfg.name, "tokens_per_step": T, "slots": min(a.slots, local_n),
                    "layers": layers, "global_batch": T * world, "seq_len": 1,
                    "parallelism": f"ep{world}" if world > 1 else "single",
+                   "ep_exchange": a.exchange if world > 1 else None,
                    "local_experts": local_n, "offloaded": offloaded, "cuda_graph": graphed,
                    "stream_overlap": offloaded and not a.no_overlap,
                    "cache_prefill_steps": a.prefill_steps,

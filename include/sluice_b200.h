@@ -251,6 +251,32 @@ int sl_fused_experts_partial(const void* hidden, int T, int H, int I,
                              void* workspace, size_t workspace_bytes,
                              sl_stream_t stream);
 
+/* ------------------------------------------------ expert-parallel exchange
+ * Replaces vLLM's EP dispatch / combine around the reference's per-rank
+ * experts (naive all-gather of tokens + routing and reduction of outputs,
+ * offloader.py:690-699, 1192-1201) with one kernel each over NVLink peer
+ * memory. peer_recv[q] / peer_signal[q] are rank q's receive buffer and
+ * signal words (16 x u32, zeroed before first use), mapped into every rank
+ * (symmetric memory); book is 16 bytes of this rank's device memory, zeroed
+ * once; status a device int32. T <= the T the buffers were sized for.
+ * Receive buffers hold two halves used alternately (sized by the _bytes
+ * queries). All ranks must make the same sequence of calls; every wait on a
+ * peer is bounded (SL_ERR_TIMEOUT in *status).
+ * dispatch: rows = this rank's [T, 2H + 8*topk] packed (hidden bf16 | weights
+ *   f32 | ids i32); outputs every rank's rows unpacked: x_out bf16
+ *   [world*T, H], w_out [world*T, topk], id_out [world*T, topk].
+ * combine: partial fp32 [world*T, H] (this rank's experts over every rank's
+ *   tokens); out = bf16(sum over ranks, rank order) for this rank's T tokens. */
+size_t sl_ep_dispatch_recv_bytes(int world, int T, int H, int topk);
+size_t sl_ep_combine_recv_bytes(int world, int T, int H);
+int sl_ep_dispatch(const void* rows, int T, int H, int topk, int rank, int world,
+                   void* const* peer_recv, void* const* peer_signal, void* book,
+                   void* x_out, float* w_out, int32_t* id_out, int32_t* status,
+                   sl_stream_t stream);
+int sl_ep_combine(const float* partial, int T, int H, int rank, int world,
+                  void* const* peer_recv, void* const* peer_signal, void* book,
+                  void* out, int32_t* status, sl_stream_t stream);
+
 /* sl_fused_experts without any device allocation. No counterpart in the
  * reference: it serves callers that cannot allocate device scratch memory for
  * a call -- a host program binding this C ABI directly (cgo, JNI, ctypes

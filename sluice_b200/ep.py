@@ -76,12 +76,91 @@ def combine(partial: torch.Tensor, group=None) -> torch.Tensor:
     return out
 
 
+class NvlinkExchange:
+    """Dispatch / combine kernels over NVLink peer memory (``sl_ep_dispatch``,
+    ``sl_ep_combine``). One symmetric allocation per rank
+    (``torch.distributed._symmetric_memory``), mapped into every peer:
+    [dispatch receive halves | combine receive halves | 16 signal words],
+    sized for ``max_tokens`` tokens per rank per call."""
+
+    SIGNAL_BYTES = 256
+
+    def __init__(self, max_tokens: int, hidden: int, topk: int, group=None, device="cuda"):
+        import ctypes
+
+        import torch.distributed._symmetric_memory as symm_mem
+
+        from . import _lib
+
+        self.group = group
+        self.max_tokens = max_tokens
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        L = _lib.lib()
+        nd = L.sl_ep_dispatch_recv_bytes(self.world, max_tokens, hidden, topk)
+        nc = L.sl_ep_combine_recv_bytes(self.world, max_tokens, hidden)
+        nd = (nd + 255) // 256 * 256
+        nc = (nc + 255) // 256 * 256
+        self.buf = symm_mem.empty(nd + nc + self.SIGNAL_BYTES, dtype=torch.uint8, device=device)
+        self.buf[nd + nc:].zero_()
+        grp = group if group is not None else dist.group.WORLD
+        self.handle = symm_mem.rendezvous(self.buf, grp)
+        ptrs = list(self.handle.buffer_ptrs)
+        vp = ctypes.c_void_p * self.world
+        self._recv_d = vp(*ptrs)
+        self._recv_c = vp(*[p + nd for p in ptrs])
+        self._sig = vp(*[p + nd + nc for p in ptrs])
+        self.book = torch.zeros(4, dtype=torch.int32, device=device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=device)
+        torch.cuda.synchronize(device)
+        dist.barrier(group)  # every rank's signal words are zero before any peer signals
+
+    def dispatch(self, x, tw, ti):
+        from ._lib import check, lib, ptr
+
+        T, H = x.shape
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens exceed the exchange's {self.max_tokens}")
+        k = tw.shape[1]
+        packed = pack_routing(x, tw, ti)
+        n = self.world * T
+        xg = torch.empty(n, H, dtype=torch.bfloat16, device=x.device)
+        twg = torch.empty(n, k, dtype=torch.float32, device=x.device)
+        tig = torch.empty(n, k, dtype=torch.int32, device=x.device)
+        check(lib().sl_ep_dispatch(ptr(packed), T, H, k, self.rank, self.world, self._recv_d,
+                                   self._sig, ptr(self.book), ptr(xg), ptr(twg), ptr(tig),
+                                   ptr(self.status), torch.cuda.current_stream().cuda_stream),
+              "sl_ep_dispatch")
+        return xg, twg, tig
+
+    def combine(self, partial: torch.Tensor) -> torch.Tensor:
+        from ._lib import check, lib, ptr
+
+        n, H = partial.shape
+        T = n // self.world
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens exceed the exchange's {self.max_tokens}")
+        out = torch.empty(T, H, dtype=torch.bfloat16, device=partial.device)
+        check(lib().sl_ep_combine(ptr(partial), T, H, self.rank, self.world, self._recv_c,
+                                  self._sig, ptr(self.book), ptr(out), ptr(self.status),
+                                  torch.cuda.current_stream().cuda_stream), "sl_ep_combine")
+        return out
+
+    def check(self) -> None:
+        from . import _lib
+
+        st = int(self.status.item())
+        if st != _lib.SL_OK:
+            raise _lib.SluiceError("expert-parallel exchange", st)
+
+
 class EPMoELayer:
     """One MoE layer's expert-parallel step on this rank."""
 
     def __init__(self, cfg: MoEConfig, router: ops.Router, cache, shared_w13, shared_w2,
-                 group=None, shared_w13_scale=None, shared_w2_scale=None):
+                 group=None, shared_w13_scale=None, shared_w2_scale=None,
+                 exchange: "NvlinkExchange | None" = None):
         self.cfg = cfg
+        self.exchange = exchange  # None: NCCL all-gather / reduce-scatter
         self.shared_w13_scale = shared_w13_scale
         self.shared_w2_scale = shared_w2_scale
         self.router = router
@@ -96,7 +175,10 @@ class EPMoELayer:
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         T = x.shape[0]
         tw, ti, _ = self.router.route(x)
-        xg, twg, tig = dispatch(x, tw, ti, self.group)
+        if self.exchange is not None:
+            xg, twg, tig = self.exchange.dispatch(x, tw, ti)
+        else:
+            xg, twg, tig = dispatch(x, tw, ti, self.group)
         self.last_ids = tig
         self.cache.gap(tig)
         c = self.cache
@@ -106,6 +188,8 @@ class EPMoELayer:
             routed_scaling_factor=self.cfg.routed_scaling_factor, w1_scale=c.w13_scale,
             w2_scale=c.w2_scale, shared_w13_scale=self.shared_w13_scale,
             shared_w2_scale=self.shared_w2_scale)
+        if self.exchange is not None:
+            return self.exchange.combine(part)
         return combine(part, self.group).to(torch.bfloat16)
 
     __call__ = forward
@@ -115,7 +199,8 @@ class EPDecodeStack:
     """The MoE layers of a decoder under expert parallelism on this rank."""
 
     def __init__(self, cfg: MoEConfig, slots: int, seed: int = 0, device="cuda",
-                 num_layers: int | None = None, group=None, protect_frac=None):
+                 num_layers: int | None = None, group=None, protect_frac=None,
+                 exchange: str = "nvlink", max_tokens: int = 16):
         from . import synth
         from .offloader import ExpertStreamOffloader
 
@@ -125,6 +210,8 @@ class EPDecodeStack:
         rank, world = dist.get_rank(group), dist.get_world_size(group)
         lo, per, local_of = expert_shard(cfg.num_experts, world, rank)
         self.offloader = ExpertStreamOffloader(slots, protect_frac=protect_frac, fast_hit=True)
+        self.exchange = (NvlinkExchange(max_tokens, cfg.hidden, cfg.routing.topk, group,
+                                        self.device) if exchange == "nvlink" else None)
         self.layers: list[EPMoELayer] = []
         n = cfg.num_moe_layers if num_layers is None else num_layers
         for li in range(n):
@@ -140,8 +227,9 @@ class EPDecodeStack:
             self.layers.append(EPMoELayer(cfg, ops.Router(cfg.routing, gw, lb, sb), cache,
                                           sh.get("shared_w13"), sh.get("shared_w2"), group,
                                           sh.get("shared_w13_scale"),
-                                          sh.get("shared_w2_scale")))
+                                          sh.get("shared_w2_scale"), self.exchange))
         torch.cuda.synchronize(self.device)
+        dist.barrier(group)  # ranks enter the first exchange together (peer waits are bounded)
         self.graph = None
         self._static_in = None
         self._static_out = None
@@ -195,6 +283,8 @@ class EPDecodeStack:
     def check(self) -> None:
         for layer in self.layers:
             layer.cache.check()
+        if self.exchange is not None:
+            self.exchange.check()
 
     def stats(self) -> dict:
         tot = {}

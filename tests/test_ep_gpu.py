@@ -1,7 +1,9 @@
-"""Expert parallelism on 2 GPUs over NCCL: each rank's layer output (its own
-tokens, experts sharded across ranks, fp32 partials reduce-scattered) must
-match the single-process oracle within the bf16 tolerance. Skipped on a box
-with fewer than 2 GPUs."""
+"""Expert parallelism on 2 GPUs: each rank's layer output (its own tokens,
+experts sharded across ranks, fp32 partials summed on the home rank) must
+match the single-process oracle within the bf16 tolerance, with the exchange
+done by the NVLink peer-memory kernels and by NCCL collectives; the two
+exchanges must agree bit for bit (two ranks: one fp32 addition either way),
+eager and under CUDA-graph replay. Skipped on a box with fewer than 2 GPUs."""
 
 import datetime
 import os
@@ -23,7 +25,7 @@ def _free_port():
     return p
 
 
-def _rank_main(rank, world, port, out_dir):
+def _rank_main(rank, world, port, out_dir, exchange):
     import torch.distributed as dist
 
     from oracle import moe as omoe
@@ -38,7 +40,7 @@ def _rank_main(rank, world, port, out_dir):
                             device_id=torch.device("cuda", rank))
     try:
         cfg = configs.V2_LITE
-        stack = ep.EPDecodeStack(cfg, slots=48, seed=3, num_layers=1)
+        stack = ep.EPDecodeStack(cfg, slots=48, seed=3, num_layers=1, exchange=exchange)
         layer = stack.layers[0]
         w13, w2 = synth.layer_weights(cfg, 0, 3, device="cuda")
         w13, w2 = w13.cpu(), w2.cpu()
@@ -65,9 +67,54 @@ def _rank_main(rank, world, port, out_dir):
         dist.destroy_process_group()
 
 
-def test_ep2_layer_matches_oracle(tmp_path):
-    mp.start_processes(_rank_main, args=(2, _free_port(), str(tmp_path)), nprocs=2,
+def _agree_main(rank, world, port, out_dir):
+    import torch.distributed as dist
+
+    from sluice_b200 import configs, ep, synth
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port),
+                      NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    stacks = []
+    try:
+        cfg = configs.V2_LITE
+        outs = {}
+        for exchange in ("nvlink", "nccl"):
+            stack = ep.EPDecodeStack(cfg, slots=48, seed=5, num_layers=2, exchange=exchange)
+            stacks.append(stack)
+            tokens = synth.TokenStream(cfg.hidden, 4, seed=70 + rank)
+            xs = [tokens.next().cuda() for _ in range(4)]
+            eager = [stack.step(x).clone() for x in xs[:2]]
+            graphed = stack.capture(4)
+            replay = [stack.replay(x).clone() for x in xs[2:]]
+            torch.cuda.synchronize()
+            stack.check()
+            outs[exchange] = (torch.stack(eager + replay).cpu(), graphed)
+        same = bool(torch.equal(outs["nvlink"][0], outs["nccl"][0]))
+        torch.save({"same": same, "graphed": outs["nvlink"][1]},
+                   os.path.join(out_dir, f"agree{rank}.pt"))
+    finally:
+        for s in stacks:
+            s.release()
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("exchange", ["nvlink", "nccl"])
+def test_ep2_layer_matches_oracle(tmp_path, exchange):
+    mp.start_processes(_rank_main, args=(2, _free_port(), str(tmp_path), exchange), nprocs=2,
                        start_method="spawn")
     for r in range(2):
         errs = torch.load(os.path.join(tmp_path, f"err{r}.pt"))
         assert (errs < 2e-2).all(), errs
+
+
+def test_ep2_nvlink_exchange_equals_nccl(tmp_path):
+    mp.start_processes(_agree_main, args=(2, _free_port(), str(tmp_path)), nprocs=2,
+                       start_method="spawn")
+    for r in range(2):
+        res = torch.load(os.path.join(tmp_path, f"agree{r}.pt"))
+        assert res["graphed"], "the NVLink exchange must capture in a CUDA graph"
+        assert res["same"]
