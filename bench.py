@@ -58,6 +58,12 @@ def _args(argv=None):
                     help="expert-parallel dispatch/combine (N>1): peer-memory kernels or NCCL")
     ap.add_argument("--no-overlap", action="store_true",
                     help="serialise the expert stream and the GEMMs (A/B)")
+    ap.add_argument("--workload", default="decode", choices=["decode", "grouped-gemm"],
+                    help="grouped-gemm: the fp8 grouped-GEMM microbench (one JSON line per T)")
+    ap.add_argument("--gemm-tokens", default="8,64,512,4096",
+                    help="token counts of the grouped-GEMM microbench")
+    ap.add_argument("--gemm-experts", type=int, default=256,
+                    help="experts of the grouped-GEMM microbench (a smaller profiling case)")
     return ap.parse_args(argv)
 
 
@@ -541,6 +547,150 @@ def run_sluice(a):
         del stack
         dist.destroy_process_group()
 
+# ------------------------------------------------- grouped-GEMM microbench
+def fp8_peak_tflops(n=8192, reps=10):
+    """Burst fp8 e4m3 GEMM throughput of this GPU (cuBLASLt through
+    ``torch._scaled_mm``, n^3, best of ``reps``): the fp8 tensor denominator."""
+    a = torch.randn(n, n, device="cuda").to(torch.float8_e4m3fn)
+    b = torch.randn(n, n, device="cuda").to(torch.float8_e4m3fn).t()
+    one = torch.ones((), device="cuda")
+    for _ in range(3):
+        torch._scaled_mm(a, b, one, one, out_dtype=torch.bfloat16)
+    best = float("inf")
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        e0.record()
+        torch._scaled_mm(a, b, one, one, out_dtype=torch.bfloat16)
+        e1.record()
+        torch.cuda.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    return 2 * n ** 3 / (best * 1e-3) / 1e12
+
+
+def run_grouped_gemm(a):
+    """fp8 grouped expert GEMM at DeepSeek-V3 expert shapes (E=256, H=7168,
+    I=2048, 128x128 block scales): experts 0..127 resident in slots, 128..255
+    streamed from mapped pinned host RAM on every call; T tokens, top-8 ids
+    Zipf(1.1) over a seeded expert permutation, renormalised fp32 weights.
+    Per T: the all-resident GEMM alone, the stream alone, and the overlapped
+    call (plan -> stream on a side stream || resident experts' GEMMs ->
+    streamed experts' GEMMs), each against its roofline."""
+    from sluice_b200 import configs, ops, synth
+    from sluice_b200.offloader import ExpertStreamOffloader
+
+    cfg = configs.DEEPSEEK_V3
+    E, H, I, k = a.gemm_experts, cfg.hidden, cfg.moe_intermediate, 8
+    half = E // 2
+    dev = torch.device("cuda")
+    with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+        peaks = json.load(f)
+    hbm_peak, bf16_peak = peaks["hbm_gbs"], peaks["bf16_tflops"]
+    fp8_peak = fp8_peak_tflops()
+    # weights, generated and quantised 32 experts at a time
+    w13 = torch.empty(E, 2 * I, H, dtype=torch.float8_e4m3fn, device=dev)
+    w2 = torch.empty(E, H, I, dtype=torch.float8_e4m3fn, device=dev)
+    s13 = torch.empty(E, 2 * I // 128, H // 128, dtype=torch.float32, device=dev)
+    s2 = torch.empty(E, H // 128, I // 128, dtype=torch.float32, device=dev)
+    for lo in range(0, E, 32):
+        n = min(32, E - lo)
+        prm = synth.layer_params(cfg, 0, a.seed, device=dev, num_experts=n, expert_lo=lo)
+        w13[lo:lo + n].copy_(prm["w13"])
+        w2[lo:lo + n].copy_(prm["w2"])
+        s13[lo:lo + n].copy_(prm["w13_scale"])
+        s2[lo:lo + n].copy_(prm["w2_scale"])
+        del prm
+    off = ExpertStreamOffloader(E, protect_frac=0.5, fast_hit=True, no_static_full=True)
+    cache = off.install_layer(w13, w2, pins=list(range(half)), prefill_resident=False,
+                              device=dev, w13_scale=s13, w2_scale=s2)
+    del w13, w2, s13, s2
+    torch.cuda.empty_cache()
+    state0, map0 = cache.state.clone(), cache.expert_map.clone()
+    bpe = cfg.bytes_per_expert
+    side = torch.cuda.Stream()
+    g = torch.Generator().manual_seed(a.seed + 7)
+    perm = torch.randperm(E, generator=g)
+    reps = max(3, min(a.steps, 10))
+
+    def restore():
+        cache.state.copy_(state0)
+        cache.expert_map.copy_(map0)
+
+    for T in [int(t) for t in a.gemm_tokens.split(",")]:
+        ids = synth.zipf_ids(T, k, E, gen=g, perm=perm)
+        tw = torch.rand(T, k, generator=g)
+        tw = (tw / tw.sum(1, keepdim=True)).float()
+        x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+        ti, tw, x = ids.to(dev), tw.to(dev), x.to(dev)
+        uniq = torch.unique(ids)
+        U, Us = int(uniq.numel()), int((uniq >= half).sum())
+        ws = ops.fused_experts_workspace(T, k, H, I, E, 0, dev)
+        out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+        kw = dict(w1_scale=cache.w13_scale, w2_scale=cache.w2_scale)
+
+        def overlapped():
+            main = torch.cuda.current_stream()
+            cache.plan(ti)
+            side.wait_stream(main)
+            with torch.cuda.stream(side):
+                cache.stream()
+            args = (x, cache.w13, cache.w2, tw, ti, cache.expert_map, cache.state)
+            ops.fused_experts_phase(*args, 0, ws, out, **kw)
+            main.wait_stream(side)
+            ops.fused_experts_phase(*args, 1, ws, out, **kw)
+
+        def timed(fn, pre=None):
+            ts = []
+            for _ in range(reps + 2):
+                if pre is not None:
+                    pre()
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+                e0.record()
+                fn()
+                e1.record()
+                torch.cuda.synchronize()
+                ts.append(e0.elapsed_time(e1))
+            return statistics.median(ts[2:])
+
+        t_over = timed(overlapped, restore)
+        cache.check()
+        # every used expert is now resident: the GEMM alone over the same pairs
+        t_gemm = timed(lambda: ops.fused_experts(x, cache.w13, cache.w2, tw, ti,
+                                                 expert_map=cache.expert_map, out=out, **kw))
+
+        def plan_only():
+            restore()
+            cache.plan(ti)
+
+        t_stream = timed(lambda: cache.stream(), plan_only)
+        flops = T * k * cfg.flops_per_pair
+        hbm = U * bpe
+        host = Us * bpe
+        t_roof_gemm = max(hbm / (hbm_peak * 1e9), flops / (bf16_peak * 1e12)) * 1e3
+        t_roof = max(t_roof_gemm, host / 63.0e9 * 1e3)
+        line = {
+            "metric": "grouped GEMM microbench", "workload": "fp8 grouped expert GEMM, "
+            f"E={E} H={H} I={I}, 128x128 block scales, experts 0..{half - 1} resident, "
+            f"{half}..{E - 1} streamed from mapped pinned host per call, top-{k} Zipf(1.1)",
+            "tokens": T, "pairs": T * k, "unique_experts": U, "streamed_experts": Us,
+            "dtype": "fp8 e4m3 weights, bf16 activations, bf16 tensor cores, fp32 accumulate",
+            "gemm": {"ms": t_gemm, "tflops": flops / (t_gemm * 1e-3) / 1e12,
+                     "frac_bf16_peak": flops / (t_gemm * 1e-3) / 1e12 / bf16_peak,
+                     "frac_fp8_peak": flops / (t_gemm * 1e-3) / 1e12 / fp8_peak,
+                     "hbm_gbs": hbm / (t_gemm * 1e-3) / 1e9,
+                     "frac_hbm_peak": hbm / (t_gemm * 1e-3) / 1e9 / hbm_peak,
+                     "roofline_ms": t_roof_gemm, "frac_roofline": t_roof_gemm / t_gemm},
+            "stream": {"ms": t_stream, "bytes": host,
+                       "gbs": host / (t_stream * 1e-3) / 1e9 if Us else None,
+                       "frac_pcie_gen5_x16": host / (t_stream * 1e-3) / 1e9 / 63.0 if Us else None},
+            "overlapped": {"ms": t_over, "roofline_ms": t_roof, "frac_roofline": t_roof / t_over,
+                           "serial_ms": t_gemm + t_stream},
+            "peaks": {"hbm_gbs": hbm_peak, "bf16_tflops": bf16_peak, "fp8_tflops": fp8_peak,
+                      "fp8_source": "measured here: torch._scaled_mm 8192^3, best of 10",
+                      "host_link_gbs": 63.0},
+        }
+        print(json.dumps(line), flush=True)
+
 
 def run_reference(a):
     """The reference's CPU path (oracle port) on the host cores, rank 0 only."""
@@ -577,6 +727,8 @@ def main(argv=None):
     a = _args(argv)
     if a.impl == "reference":
         run_reference(a)
+    elif a.workload == "grouped-gemm":
+        run_grouped_gemm(a)
     else:
         run_sluice(a)
 

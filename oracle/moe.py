@@ -20,8 +20,14 @@ here follow vLLM 0.22:
   token, and vLLM's tail (``runner/moe_runner.py:350-366``, ``663-680``)
   scales the routed output by ``routed_scaling_factor`` in bf16 and adds the
   shared output in bf16;
-* fp8: e4m3 weights times fp32 128x128 block scales, dequantised to fp32,
-  then the same math with fp32 weights.
+* fp8 (vLLM's ``use_fp8_w8a8`` with ``block_shape=[128, 128]``,
+  ``fused_moe.py:1587-1632``): e4m3 weights times fp32 128x128 block scales;
+  the activations entering each GEMM (the token rows, then the SwiGLU
+  output) are quantised per token and 128-column group the way
+  ``per_token_group_quant_fp8`` does ([vLLM] ``quantization/utils/fp8_utils.py``
+  ``_per_token_group_quant_fp8``, 95-150: scale = max(amax, 1e-10) * (1/448),
+  ``q = clamp(x / scale, -448, 448)`` to e4m3); products of the dequantised
+  operands accumulate in fp32, each GEMM output rounds to bf16.
 """
 
 from __future__ import annotations
@@ -35,13 +41,31 @@ def silu_and_mul(x: torch.Tensor) -> torch.Tensor:
     return F.silu(x[..., :d]) * x[..., d:]
 
 
-def expert_mlp(x: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor) -> torch.Tensor:
-    """One expert's SwiGLU MLP in the dtype of its operands."""
+FP8_MAX = 448.0
+
+
+def quant_dequant_group_fp8(x: torch.Tensor, group: int = 128) -> torch.Tensor:
+    """Activations through vLLM's per-token-group e4m3 quantisation, returned
+    dequantised in fp32 (q * scale)."""
+    *lead, K = x.shape
+    g = x.float().reshape(*lead, K // group, group)
+    amax = g.abs().amax(dim=-1, keepdim=True).clamp(min=1e-10)
+    scale = amax * (1.0 / FP8_MAX)
+    q = (g / scale).clamp(-FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn)
+    return (q.float() * scale).reshape(*lead, K)
+
+
+def expert_mlp(x: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor,
+               act_quant: bool = False) -> torch.Tensor:
+    """One expert's SwiGLU MLP in the dtype of its operands. ``act_quant``:
+    quantise each GEMM's activations per 128-column group (fp8 w8a8)."""
     if w13.dtype != x.dtype:
         # dequantised fp32 weights: compute in fp32, round like a bf16 kernel
-        gu = F.linear(x.float(), w13.float()).to(x.dtype)
+        xa = quant_dequant_group_fp8(x) if act_quant else x.float()
+        gu = F.linear(xa, w13.float()).to(x.dtype)
         a = silu_and_mul(gu)
-        return F.linear(a.float(), w2.float()).to(x.dtype)
+        aa = quant_dequant_group_fp8(a) if act_quant else a.float()
+        return F.linear(aa, w2.float()).to(x.dtype)
     gu = F.linear(x, w13)
     return F.linear(silu_and_mul(gu), w2)
 
@@ -86,7 +110,7 @@ def fused_experts(hs: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor,
         if w13_scale is not None:
             a = dequant_block_fp8(a, w13_scale[s], block_shape)
             b = dequant_block_fp8(b, w2_scale[s], block_shape)
-        z[sel[:, 0], sel[:, 1]] = expert_mlp(hs[tok], a, b)
+        z[sel[:, 0], sel[:, 1]] = expert_mlp(hs[tok], a, b, act_quant=w13_scale is not None)
     return (z.float() * topk_weights.float().unsqueeze(-1)).sum(dim=1).to(hs.dtype)
 
 
@@ -97,7 +121,7 @@ def shared_experts(hs: torch.Tensor, w13_sh: torch.Tensor, w2_sh: torch.Tensor,
     if w13_scale is not None:
         a = dequant_block_fp8(a, w13_scale, block_shape)
         b = dequant_block_fp8(b, w2_scale, block_shape)
-    return expert_mlp(hs, a, b)
+    return expert_mlp(hs, a, b, act_quant=w13_scale is not None)
 
 
 def layer_output(routed: torch.Tensor, shared: torch.Tensor | None,

@@ -392,6 +392,7 @@ __global__ void __launch_bounds__(kAlignSmallThreads) align_small_kernel(
     }
   }
   __syncthreads();
+  if (X == nullptr) return;  // fp8 weights: a quantising gather follows
   // this CTA's share of the rows: routed pairs, then each shared expert's tokens
   const int vrow = H >> 3;
   const uint4* src = reinterpret_cast<const uint4*>(hs);
@@ -784,99 +785,161 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(
   }
 }
 
-// --------------------------------------------------------- fp8 weight GEMM
-// fp8 e4m3 expert weights with fp32 128x128 block scales (vLLM's block-fp8
-// MoE layout: w13_scale [E, 2I/128, H/128], w2_scale [E, H/128, I/128]).
-// TMA brings raw fp8 weight tiles (128 rows x 64 K, unswizzled) into a raw
-// ring; a converter warpgroup dequantises each row (fp8 -> fp32 x block scale
-// -> bf16) into the 128B-swizzled bf16 tile the MMA reads; MMA, epilogue and
-// token tiles are those of the bf16 kernel (bf16 activations, fp32
-// accumulation in TMEM). Roles: warp 0 producer, warp 1 MMA + TMEM, warps 2-5
-// epilogue, warps 6-9 converter.
-constexpr int kFp8Threads = 320;
+// ------------------------------------------------------ fp8 (w8a8) GEMM
+// vLLM's block-fp8 MoE arithmetic (fused_experts with use_fp8_w8a8 and
+// block_shape [128, 128]): the activations are quantised per row and
+// 128-column group to e4m3 with an fp32 scale (amax / 448), the weights are
+// e4m3 with fp32 128x128 block scales. Each 128-wide K block is one tcgen05
+// kind::f8f6f4 accumulation (4 MMAs of K = 32) into a TMEM buffer, which the
+// promotion warps scale by (weight block scale x the token's group scale)
+// and add into fp32 registers.
+// GATED (gate/up GEMM): a tile is 128 gate rows and the 128 up rows of the
+//   same intermediate columns (two M=128 MMAs per K step into two TMEM
+//   column ranges), so SwiGLU is thread-local and one tile covers one
+//   128-column group of the intermediate: the epilogue quantises it per
+//   token for the down GEMM (group amax across the four lane quadrants).
+// !GATED (down GEMM): 128 output rows per tile, bf16 out per (pair, row).
+// Roles: warp 0 TMA producer, warp 1 MMA issuer + TMEM owner, warps 2.. the
+// promotion / epilogue warps (4, or 8 for 128-token tiles: two groups of
+// token columns).
+constexpr int F8_BK = 128;  // K per stage: one scale block, one 128-byte swizzle row
 
-template <int BN, int RSTAGES, int CSTAGES, bool GATED>
-struct Fp8Cfg {
-  static constexpr int kRawA = BM * BK;          // bytes (fp8) per raw weight tile
-  static constexpr int kBTile = BN * BK;         // bf16 elements
-  static constexpr int kCvtA = BM * BK;          // bf16 elements
-  static constexpr int kTxBytes = kRawA + kBTile * 2;  // TMA bytes per raw stage
-  static constexpr int kSmemBytes = CSTAGES * kCvtA * 2 + RSTAGES * kBTile * 2 +
-                                    RSTAGES * kRawA + 64 * kXchgStride * 4 + 1024 + 512;
+template <int BN, bool GATED>
+struct F8Cfg {
+  static constexpr int kNP = BN == 128 ? 8 : 4;         // promotion warps
+  static constexpr int kThreads = 64 + 32 * kNP;
+  static constexpr int kCW = BN / (kNP / 4);             // token columns per promotion warp
+  static constexpr int kATiles = GATED ? 2 : 1;          // 128-row weight tiles per stage
+  static constexpr int kABytes = kATiles * 128 * F8_BK;
+  static constexpr int kBBytes = BN * F8_BK;
+  static constexpr int kStageBytes = kABytes + kBBytes;   // multiple of 1024
+  static constexpr int kTxBytes = kStageBytes + BN * 4;   // + the tokens' group scales
+  static constexpr int kAccCols = kATiles * BN;          // TMEM columns per buffer
+  static constexpr int kNB = kAccCols * 4 <= 512 ? 4 : 2;
+  static constexpr int kTmemUsed = kNB * kAccCols;
+  static constexpr int kTmemCols = kTmemUsed <= 32 ? 32 : kTmemUsed <= 64 ? 64
+                                   : kTmemUsed <= 128 ? 128 : kTmemUsed <= 256 ? 256 : 512;
+  static constexpr int kFixed = 1024 /*align*/ + 4 * BN * 4 /*amax*/ + 1024 /*barriers*/;
+  static constexpr int kStagesRaw = (220 * 1024 - kFixed) / (kStageBytes + BN * 4);
+  static constexpr int kStages = kStagesRaw > 12 ? 12 : kStagesRaw;
+  static constexpr int kSmemBytes = kStages * (kStageBytes + BN * 4) + kFixed;
 };
 
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+__device__ __forceinline__ uint32_t e4m3x4(float a, float b, float c, float d) {
+  const __nv_fp8x2_storage_t lo =
+      __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
+  const __nv_fp8x2_storage_t hi =
+      __nv_cvt_float2_to_fp8x2(make_float2(c, d), __NV_SATFINITE, __NV_E4M3);
+  return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
 }
 
-// 16 fp8 e4m3 values -> 16 floats
-__device__ __forceinline__ void fp8x16_to_f32(const uint4& v, float (&f)[16]) {
-  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const __nv_fp8x2_storage_t pair = static_cast<__nv_fp8x2_storage_t>(w[q] >> (16 * h));
-      const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(pair, __NV_E4M3);
-      const float2 ff = __half22float2(*reinterpret_cast<const __half2*>(&hr));
-      f[4 * q + 2 * h] = ff.x;
-      f[4 * q + 2 * h + 1] = ff.y;
+// vLLM's per_token_group_quant_fp8 (fp8_utils.py, _per_token_group_quant_fp8):
+// scale = max(amax, 1e-10) * (1 / 448), q = clamp(x / scale, -448, 448) ->
+// e4m3 (round to nearest even).
+constexpr float kF8Max = 448.0f;
+__device__ __forceinline__ float group_scale(float amax) {
+  return fmaxf(amax, 1e-10f) * (1.0f / kF8Max);
+}
+__device__ __forceinline__ float q_clamp(float x, float scale) {
+  return fminf(fmaxf(__fdiv_rn(x, scale), -kF8Max), kF8Max);
+}
+
+// Token rows for the fp8 GEMMs: row pair_pos[p] <- hidden row p / topk (and
+// the shared experts' rows <- their tokens), quantised per 128-column group:
+// Xq [max_rows, H] e4m3, Xs [H/128, max_rows] fp32. One warp per (row, group).
+__global__ void __launch_bounds__(256) gather_quant_kernel(
+    const int32_t* __restrict__ ws_hdr, const int32_t* __restrict__ pair_pos, int P, int topk,
+    int n_sh, int sh_t0, int sh_nt, const __nv_bfloat16* __restrict__ hs, int H,
+    uint8_t* __restrict__ Xq, float* __restrict__ Xs, int max_rows) {
+  sl::pdl_wait();
+  sl::pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int G = H / 128;
+  const long n_units = static_cast<long>(P + n_sh * sh_nt) * G;
+  const long nwarps = static_cast<long>(gridDim.x) * (blockDim.x >> 5);
+  for (long u = static_cast<long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+       u < n_units; u += nwarps) {
+    const int r = static_cast<int>(u / G), kb = static_cast<int>(u % G);
+    int pos, tok;
+    if (r < P) {
+      pos = pair_pos[r];
+      tok = r / topk;
+    } else {
+      const int rr = r - P, i = rr / sh_nt, t = rr % sh_nt;
+      pos = ws_hdr[WS_SH_BASE + i] + t;
+      tok = sh_t0 + t;
     }
+    if (pos < 0) continue;  // the same for the whole warp
+    const uint2 raw = *reinterpret_cast<const uint2*>(hs + static_cast<size_t>(tok) * H +
+                                                      kb * 128 + lane * 4);
+    const float2 f01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+    const float2 f23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+    float m = fmaxf(fmaxf(fabsf(f01.x), fabsf(f01.y)), fmaxf(fabsf(f23.x), fabsf(f23.y)));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float sc = group_scale(m);
+    *reinterpret_cast<uint32_t*>(Xq + static_cast<size_t>(pos) * H + kb * 128 + lane * 4) =
+        e4m3x4(q_clamp(f01.x, sc), q_clamp(f01.y, sc), q_clamp(f23.x, sc), q_clamp(f23.y, sc));
+    if (lane == 0) Xs[static_cast<size_t>(kb) * max_rows + pos] = sc;
   }
 }
 
-template <int BN, int RSTAGES, int CSTAGES, bool GATED>
-__global__ void __launch_bounds__(kFp8Threads, 1) moe_gemm_fp8_kernel(
+template <int BN, bool GATED>
+__global__ void __launch_bounds__(F8Cfg<BN, GATED>::kThreads, 1) moe_gemm_f8_kernel(
     const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_wsh,
-    const __grid_constant__ CUtensorMap tm_b, const float* __restrict__ w_scale,
-    const float* __restrict__ wsh_scale, const int32_t* __restrict__ ws_hdr,
-    const int4* __restrict__ items, __nv_bfloat16* __restrict__ out, int S, int K,
-    int M_total, int out_ld, int32_t* __restrict__ status, int phase) {
-  using Cfg = Fp8Cfg<BN, RSTAGES, CSTAGES, GATED>;
-  using TS = TileShape<BN, GATED>;
+    const __grid_constant__ CUtensorMap tm_b, const float* __restrict__ b_scale,
+    const float* __restrict__ w_scale, const float* __restrict__ wsh_scale,
+    const int32_t* __restrict__ ws_hdr, const int4* __restrict__ items,
+    uint8_t* __restrict__ out_q, float* __restrict__ out_s, __nv_bfloat16* __restrict__ out_z,
+    int S, int K, int M_total, int max_rows, int32_t* __restrict__ status, int phase) {
+  using Cfg = F8Cfg<BN, GATED>;
+  constexpr int ST = Cfg::kStages;
+  constexpr int NB = Cfg::kNB;
+  constexpr int CW = Cfg::kCW;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  __nv_bfloat16* sC = reinterpret_cast<__nv_bfloat16*>(smem);        // [C][BM*BK]
-  __nv_bfloat16* sB = sC + CSTAGES * Cfg::kCvtA;                     // [R][BN*BK]
-  uint8_t* sR = reinterpret_cast<uint8_t*>(sB + RSTAGES * Cfg::kBTile);  // [R][BM*BK]
-  float* xchg = reinterpret_cast<float*>(sR + RSTAGES * Cfg::kRawA);
-  uint64_t* raw_full = reinterpret_cast<uint64_t*>(xchg + 64 * kXchgStride);
-  uint64_t* raw_empty = raw_full + RSTAGES;
-  uint64_t* b_empty = raw_empty + RSTAGES;
-  uint64_t* cvt_full = b_empty + RSTAGES;
-  uint64_t* cvt_empty = cvt_full + CSTAGES;
-  uint64_t* tfull = cvt_empty + CSTAGES;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* mma_done = tempty + 2;
+  uint8_t* sAB = smem;                                                  // [ST][A | B]
+  float* sS = reinterpret_cast<float*>(sAB + ST * Cfg::kStageBytes);    // [ST][BN]
+  float* red = sS + ST * BN;                                            // [4][BN]
+  uint64_t* full = reinterpret_cast<uint64_t*>(red + 4 * BN);
+  uint64_t* empty = full + ST;
+  uint64_t* tfull = empty + ST;
+  uint64_t* tempty = tfull + NB;
+  uint64_t* mma_done = tempty + NB;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  sl::pdl_wait();
-  sl::pdl_trigger();
-  const int m_tiles = M_total / TS::kRowsOut;
+  if constexpr (GATED) {
+    sl::pdl_wait();
+    sl::pdl_trigger();
+  }
+  // down GEMM: the items were written two launches back, so they may be read
+  // before the wait; its B operand (the quantised activations) may not
+  const int m_tiles = M_total / 128;
   const int num_items = ws_hdr[WS_NUM_ITEMS];
   const int n_hit = ws_hdr[WS_NUM_HIT_ITEMS];
   const int item_lo = phase == 1 ? n_hit : 0;
   const int item_hi = phase == 0 ? n_hit : num_items;
   const int num_tiles = (item_hi > item_lo ? item_hi - item_lo : 0) * m_tiles;
-  const int k_blocks = K / BK;
-  const int kscale = K / 128;  // scale blocks along K
-  if (static_cast<int>(blockIdx.x) >= num_tiles) return;  // nothing for this CTA
+  const int k_blocks = K / F8_BK;
+  const int kscale = K / 128;
+  if (static_cast<int>(blockIdx.x) >= num_tiles) {
+    if constexpr (!GATED) {
+      sl::pdl_wait();
+      sl::pdl_trigger();
+    }
+    return;
+  }
   if (threadIdx.x == 0) {
-    for (int s = 0; s < RSTAGES; ++s) {
-      sl::mbar_init(&raw_full[s], 1);
-      sl::mbar_init(&raw_empty[s], 4);
-      sl::mbar_init(&b_empty[s], 1);
+    for (int s = 0; s < ST; ++s) {
+      sl::mbar_init(&full[s], 1);
+      sl::mbar_init(&empty[s], 1 + Cfg::kNP);  // the MMAs' commit + every promotion warp
     }
-    for (int s = 0; s < CSTAGES; ++s) {
-      sl::mbar_init(&cvt_full[s], 4);
-      sl::mbar_init(&cvt_empty[s], 1);
-    }
-    for (int a = 0; a < 2; ++a) {
-      sl::mbar_init(&tfull[a], 1);
-      sl::mbar_init(&tempty[a], 4);
+    for (int b = 0; b < NB; ++b) {
+      sl::mbar_init(&tfull[b], 1);
+      sl::mbar_init(&tempty[b], Cfg::kNP);
     }
     sl::mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -885,7 +948,7 @@ __global__ void __launch_bounds__(kFp8Threads, 1) moe_gemm_fp8_kernel(
     sl::tma_prefetch_desc(&tm_wsh);
     sl::tma_prefetch_desc(&tm_b);
   }
-  if (warp == 1) sl::tmem_alloc(tmem_slot, TS::kTmemCols);
+  if (warp == 1) sl::tmem_alloc(tmem_slot, Cfg::kTmemCols);
   sl::tc_fence_before();
   __syncthreads();
   sl::tc_fence_after();
@@ -896,86 +959,104 @@ __global__ void __launch_bounds__(kFp8Threads, 1) moe_gemm_fp8_kernel(
     if (sl::elect_one()) {
       const uint64_t pol_w = sl::policy_evict_first();
       const uint64_t pol_b = sl::policy_evict_last();
-      int r = 0;
-      uint32_t rph = 0;
+      int s = 0;
+      uint32_t ph = 0;
       uint32_t issued_mask = 0;
       bool ok = true;
+      bool waited = GATED;
+      int pend_n = 0;
+      int pend_s[ST], pend_kb[ST], pend_row[ST];
+      auto load_b = [&](int st, int kb, int row) {
+        sl::tma_load_2d(sAB + st * Cfg::kStageBytes + Cfg::kABytes, &tm_b, &full[st],
+                        kb * F8_BK, row, pol_b);
+        sl::bulk_load(sS + st * BN, b_scale + static_cast<size_t>(kb) * max_rows + row, BN * 4,
+                      &full[st]);
+      };
+      auto flush = [&]() {
+        sl::pdl_wait();
+        sl::pdl_trigger();
+        waited = true;
+        for (int i = 0; i < pend_n; ++i) load_b(pend_s[i], pend_kb[i], pend_row[i]);
+        pend_n = 0;
+      };
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         const int4 it = items[item_lo + tile / m_tiles];
         const int mt = tile % m_tiles;
         const bool sh = it.x >= S;
         const CUtensorMap* tw = sh ? &tm_wsh : &tm_w;
         const int e = sh ? it.x - S : it.x;
-        const int row0 = GATED ? e * 2 * M_total + mt * 64 : e * M_total + mt * BM;
+        // weight rows in the 2-D view [experts * rows, K]
+        const int row0 = GATED ? e * 2 * M_total + mt * 128 : e * M_total + mt * 128;
         for (int kb = 0; kb < k_blocks; ++kb) {
-          if (*abort_flag || !sl::mbar_wait(&raw_empty[r], rph ^ 1) ||
-              !sl::mbar_wait(&b_empty[r], rph ^ 1)) {
+          if (*abort_flag || !sl::mbar_wait(&empty[s], ph ^ 1)) {
             ok = false;
             break;
           }
-          sl::mbar_arrive_expect_tx(&raw_full[r], Cfg::kTxBytes);
-          uint8_t* a0 = sR + r * Cfg::kRawA;
-          sl::tma_load_2d(a0, tw, &raw_full[r], kb * BK, row0, pol_w);
-          if constexpr (GATED)
-            sl::tma_load_2d(a0 + 64 * BK, tw, &raw_full[r], kb * BK, row0 + M_total, pol_w);
-          sl::tma_load_2d(sB + r * Cfg::kBTile, &tm_b, &raw_full[r], kb * BK, it.y, pol_b);
-          issued_mask = (issued_mask & ~(1u << r)) | (rph << r);
-          if (++r == RSTAGES) {
-            r = 0;
-            rph ^= 1;
+          sl::mbar_arrive_expect_tx(&full[s], Cfg::kTxBytes);
+          uint8_t* a0 = sAB + s * Cfg::kStageBytes;
+          sl::tma_load_2d(a0, tw, &full[s], kb * F8_BK, row0, pol_w);
+          if constexpr (GATED)  // the up rows of the same intermediate columns
+            sl::tma_load_2d(a0 + 128 * F8_BK, tw, &full[s], kb * F8_BK, row0 + M_total, pol_w);
+          if (waited) {
+            load_b(s, kb, it.y);
+          } else {
+            pend_s[pend_n] = s;
+            pend_kb[pend_n] = kb;
+            pend_row[pend_n] = it.y;
+            if (++pend_n == ST) flush();
+          }
+          issued_mask = (issued_mask & ~(1u << s)) | (ph << s);
+          if (++s == ST) {
+            s = 0;
+            ph ^= 1;
           }
         }
       }
+      if (!waited) flush();
       if (!ok) {
         atomicExch(status, SL_ERR_TIMEOUT);
         *abort_flag = 1;
-        for (int s = 0; s < RSTAGES; ++s) (void)sl::mbar_wait(&raw_full[s], (issued_mask >> s) & 1u);
+        for (int i = 0; i < ST; ++i) (void)sl::mbar_wait(&full[i], (issued_mask >> i) & 1u);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------- MMA issuer
     if (sl::elect_one()) {
-      constexpr uint32_t idesc = sl::umma_idesc_bf16(BM, BN);
-      int r = 0, c = 0;
-      uint32_t rph = 0, cph = 0;
-      int acc = 0;
-      uint32_t acc_phase = 0;
+      constexpr uint32_t idesc = sl::umma_idesc_e4m3(128, BN);
+      int s = 0, b = 0;
+      uint32_t ph = 0, bph = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        if (*abort_flag || !sl::mbar_wait(&tempty[acc], acc_phase ^ 1)) {
-          ok = false;
-          break;
-        }
-        sl::tc_fence_after();
-        const uint32_t d0 = tmem_base + acc * TS::kAccCols;
         for (int kb = 0; kb < k_blocks; ++kb) {
-          if (*abort_flag || !sl::mbar_wait(&cvt_full[c], cph)) {
+          if (*abort_flag || !sl::mbar_wait(&tempty[b], bph ^ 1) ||
+              !sl::mbar_wait(&full[s], ph)) {
             ok = false;
             break;
           }
           sl::tc_fence_after();
-          const uint32_t a_addr = sl::smem_u32(sC + c * Cfg::kCvtA);
-          const uint32_t b_addr = sl::smem_u32(sB + r * Cfg::kBTile);
+          const uint32_t d0 = tmem_base + b * Cfg::kAccCols;
+          const uint32_t a_addr = sl::smem_u32(sAB + s * Cfg::kStageBytes);
+          const uint32_t b_addr = a_addr + Cfg::kABytes;
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
-            sl::umma_bf16(d0, sl::umma_desc_sw128(a_addr + k * 32),
-                          sl::umma_desc_sw128(b_addr + k * 32), idesc, (kb | k) != 0);
-          sl::umma_commit(&cvt_empty[c]);
-          sl::umma_commit(&b_empty[r]);
-          if (++c == CSTAGES) {
-            c = 0;
-            cph ^= 1;
+          for (int k = 0; k < F8_BK / 32; ++k)
+            sl::umma_e4m3(d0, sl::umma_desc_sw128(a_addr + k * 32),
+                          sl::umma_desc_sw128(b_addr + k * 32), idesc, k != 0);
+          if constexpr (GATED) {
+#pragma unroll
+            for (int k = 0; k < F8_BK / 32; ++k)
+              sl::umma_e4m3(d0 + BN, sl::umma_desc_sw128(a_addr + 128 * F8_BK + k * 32),
+                            sl::umma_desc_sw128(b_addr + k * 32), idesc, k != 0);
           }
-          if (++r == RSTAGES) {
-            r = 0;
-            rph ^= 1;
+          sl::umma_commit(&empty[s]);
+          sl::umma_commit(&tfull[b]);
+          if (++s == ST) {
+            s = 0;
+            ph ^= 1;
           }
-        }
-        if (!ok) break;
-        sl::umma_commit(&tfull[acc]);
-        if (++acc == 2) {
-          acc = 0;
-          acc_phase ^= 1;
+          if (++b == NB) {
+            b = 0;
+            bph ^= 1;
+          }
         }
       }
       if (!ok) {
@@ -985,95 +1066,117 @@ __global__ void __launch_bounds__(kFp8Threads, 1) moe_gemm_fp8_kernel(
       sl::umma_commit(mma_done);
       (void)sl::mbar_wait(mma_done, 0);
     }
-  } else if (warp >= 6) {
-    // ---------------------------------------------------------- converter
-    const int row = threadIdx.x - 6 * 32;  // 0..127: weight row within the tile
-    int r = 0, c = 0;
-    uint32_t rph = 0, cph = 0;
+  } else {
+    // ------------------------------------------- promotion and epilogue
+    const int pw = warp - 2;
+    const int q = warp & 3;           // TMEM lane quadrant of this warp
+    const int cg = pw >> 2;           // token-column group
+    const int c0 = cg * CW;
+    const int row = q * 32 + lane;    // weight row within the 128-row tile
+    int s = 0, b = 0;
+    uint32_t ph = 0, bph = 0;
+    bool ok = true;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       const int4 it = items[item_lo + tile / m_tiles];
       const int mt = tile % m_tiles;
       const bool sh = it.x >= S;
       const int e = sh ? it.x - S : it.x;
       const float* scale = sh ? wsh_scale : w_scale;
-      // the 128x128 scale block of this thread's weight row
-      int sblk;
+      // this tile's weight block-scale rows (block row mt; up rows at I/128 + mt)
+      const int srows = GATED ? 2 * (M_total / 128) : M_total / 128;
+      const float* sc_g = scale + (static_cast<size_t>(e) * srows + mt) * kscale;
+      const float* sc_u = GATED ? sc_g + static_cast<size_t>(M_total / 128) * kscale : sc_g;
+      float acc_g[CW], acc_u[GATED ? CW : 1];
+#pragma unroll
+      for (int i = 0; i < CW; ++i) acc_g[i] = 0.f;
       if constexpr (GATED) {
-        const int srows = 2 * (M_total / 128);
-        const int wrow = row < 64 ? mt * 64 + row : M_total + mt * 64 + (row - 64);
-        sblk = e * srows + wrow / 128;
-      } else {
-        sblk = e * (M_total / 128) + mt;
+#pragma unroll
+        for (int i = 0; i < CW; ++i) acc_u[i] = 0.f;
       }
-      const float* srow = scale + static_cast<size_t>(sblk) * kscale;
-      bool ok = true;
       for (int kb = 0; kb < k_blocks; ++kb) {
-        if (*abort_flag || !sl::mbar_wait(&raw_full[r], rph) ||
-            !sl::mbar_wait(&cvt_empty[c], cph ^ 1)) {
-          ok = false;
-          break;
-        }
-        const float sc = srow[kb >> 1];
-        const uint4* src = reinterpret_cast<const uint4*>(sR + r * Cfg::kRawA + row * BK);
-        uint8_t* dst_row = reinterpret_cast<uint8_t*>(sC + c * Cfg::kCvtA) + row * 128;
+        const float swg = __ldg(sc_g + kb);
+        const float swu = GATED ? __ldg(sc_u + kb) : 0.f;
+        // the accumulator of this K block, then the stage's token scales
+        // (landed with the stage; its full phase stays complete until this
+        // warp releases the stage)
+        ok = ok && !*abort_flag && sl::mbar_wait(&tfull[b], bph) && sl::mbar_wait(&full[s], ph);
+        if (ok) {
+          sl::tc_fence_after();
+          const uint32_t taddr = tmem_base + b * Cfg::kAccCols +
+                                 (static_cast<uint32_t>(q * 32) << 16) + c0;
+          const float* sa = sS + s * BN + c0;
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {  // 16 fp8 -> 16 bf16 = two 16-byte chunks
-          float f[16];
-          fp8x16_to_f32(src[q4], f);
+          for (int cc = 0; cc < CW; cc += 16) {
+            uint32_t vg[16], vu[16];
+            sl::tmem_ld16_nowait(taddr + cc, vg);
+            if constexpr (GATED) sl::tmem_ld16_nowait(taddr + BN + cc, vu);
+            sl::tmem_wait_ld(vg);
+            if constexpr (GATED) sl::tmem_wait_ld(vu);
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            uint4 o;
-            __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              o2[j] = __floats2bfloat162_rn(f[8 * h + 2 * j] * sc, f[8 * h + 2 * j + 1] * sc);
-            const int chunk = 2 * q4 + h;  // 16-byte chunk within the 128-byte row
-            *reinterpret_cast<uint4*>(dst_row + ((chunk ^ (row & 7)) << 4)) = o;
+            for (int i = 0; i < 16; ++i) {
+              const float a_s = sa[cc + i];
+              acc_g[cc + i] = fmaf(__uint_as_float(vg[i]), swg * a_s, acc_g[cc + i]);
+              if constexpr (GATED)
+                acc_u[cc + i] = fmaf(__uint_as_float(vu[i]), swu * a_s, acc_u[cc + i]);
+            }
           }
+          sl::tc_fence_before();
         }
-        fence_proxy_async_smem();  // generic-proxy writes -> visible to tcgen05.mma
         __syncwarp();
-        if (lane == 0) {
-          sl::mbar_arrive(&cvt_full[c]);
-          sl::mbar_arrive(&raw_empty[r]);
+        if (ok && lane == 0) {
+          sl::mbar_arrive(&tempty[b]);
+          sl::mbar_arrive(&empty[s]);
         }
-        if (++r == RSTAGES) {
-          r = 0;
-          rph ^= 1;
+        if (++s == ST) {
+          s = 0;
+          ph ^= 1;
         }
-        if (++c == CSTAGES) {
-          c = 0;
-          cph ^= 1;
+        if (++b == NB) {
+          b = 0;
+          bph ^= 1;
         }
       }
       if (!ok) {
         atomicExch(status, SL_ERR_TIMEOUT);
         *abort_flag = 1;
-        break;
       }
-    }
-  } else {
-    // --------------------------------------------------------- epilogue
-    const int q = warp & 3;
-    int acc = 0;
-    uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      const bool ok = !*abort_flag && sl::mbar_wait(&tfull[acc], acc_phase);
-      if (epi_any(!ok)) {
-        atomicExch(status, SL_ERR_TIMEOUT);
-        *abort_flag = 1;
-        break;
-      }
-      sl::tc_fence_after();
-      const int4 it = items[item_lo + tile / m_tiles];
-      epilogue_tile<BN, GATED>(tmem_base + acc * TS::kAccCols, q, lane, it, tile % m_tiles,
-                               out, out_ld, xchg);
-      sl::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) sl::mbar_arrive(&tempty[acc]);
-      if (++acc == 2) {
-        acc = 0;
-        acc_phase ^= 1;
+      if constexpr (GATED) {
+        // every warp of this column group runs the same tiles and barriers
+        // (a failed wait above only skips work), so the barriers cannot strand
+        // one of them
+        const int f = mt * 128 + row;  // intermediate column of this thread
+#pragma unroll
+        for (int i = 0; i < CW; ++i) {
+          // vLLM's chain: bf16 GEMM outputs, bf16 SiLU, bf16 product
+          const float g = sl::bf16_round(acc_g[i]);
+          const float u = sl::bf16_round(acc_u[i]);
+          const float sg = sl::bf16_round(g / (1.0f + expf(-g)));
+          acc_g[i] = sl::bf16_round(sg * u);
+          float m = fabsf(acc_g[i]);
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+          if (lane == 0) red[q * BN + c0 + i] = m;
+        }
+        named_bar_sync(1 + cg, 128);
+#pragma unroll
+        for (int i = 0; i < CW; ++i) {
+          const int c = c0 + i;
+          const float m = fmaxf(fmaxf(red[c], red[BN + c]), fmaxf(red[2 * BN + c], red[3 * BN + c]));
+          const float sc = group_scale(m);
+          if (ok && c < it.z) {
+            const __nv_fp8_storage_t v = __nv_cvt_float_to_fp8(q_clamp(acc_g[i], sc),
+                                                               __NV_SATFINITE, __NV_E4M3);
+            out_q[static_cast<size_t>(it.y + c) * M_total + f] = v;
+            if (row == 0) out_s[static_cast<size_t>(mt) * max_rows + it.y + c] = sc;
+          }
+        }
+        named_bar_sync(1 + cg, 128);  // red is rewritten by the next tile
+      } else {
+        const int h = mt * 128 + row;
+#pragma unroll
+        for (int i = 0; i < CW; ++i)
+          if (ok && c0 + i < it.z)
+            out_z[static_cast<size_t>(it.y + c0 + i) * M_total + h] = __float2bfloat16(acc_g[i]);
       }
     }
   }
@@ -1082,7 +1185,7 @@ __global__ void __launch_bounds__(kFp8Threads, 1) moe_gemm_fp8_kernel(
   if (warp == 1) {
     __syncwarp();
     sl::tc_fence_after();
-    sl::tmem_dealloc(tmem_base, TS::kTmemCols);
+    sl::tmem_dealloc(tmem_base, Cfg::kTmemCols);
   }
 }
 
@@ -1513,31 +1616,32 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// 2-D bf16 view [rows, inner] (inner contiguous), box {64, box_rows}, 128B swizzle.
+// 2-D view [rows, inner] (inner contiguous), 128B swizzle (the MMA operand
+// layout): bf16 with a 64-element box, or e4m3 (fp8) with a 128-byte box,
+// box_rows rows.
 bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint32_t box_rows,
               bool fp8 = false) {
   auto fn = encode_fn();
   if (!fn || (reinterpret_cast<uintptr_t>(base) & 15) || rows == 0) return false;
-  // bf16: 64-element (128 B) inner box, 128B swizzle (the MMA operand layout);
-  // fp8: 64-byte inner box, unswizzled (a staging tile the converter reads)
   const uint64_t esz = fp8 ? 1 : 2;
   cuuint64_t dims[2] = {inner, rows};
   cuuint64_t strides[1] = {inner * esz};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), box_rows};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(fp8 ? F8_BK : BK), box_rows};
   cuuint32_t estr[2] = {1, 1};
   return fn(m, fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
             const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-            fp8 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, int RSTAGES, int CSTAGES, bool GATED>
-int launch_gemm_fp8(const CUtensorMap& tw, const CUtensorMap& twsh, const CUtensorMap& tb,
-                    const float* wscale, const float* wshscale, const int32_t* hdr,
-                    const int4* items, __nv_bfloat16* out, int S, int K, int M_total, int out_ld,
-                    int32_t* status, int max_items, cudaStream_t st, int phase) {
-  using Cfg = Fp8Cfg<BN, RSTAGES, CSTAGES, GATED>;
-  auto kern = moe_gemm_fp8_kernel<BN, RSTAGES, CSTAGES, GATED>;
+template <int BN, bool GATED>
+int launch_gemm_f8(const CUtensorMap& tw, const CUtensorMap& twsh, const CUtensorMap& tb,
+                   const float* bscale, const float* wscale, const float* wshscale,
+                   const int32_t* hdr, const int4* items, uint8_t* out_q, float* out_s,
+                   __nv_bfloat16* out_z, int S, int K, int M_total, int max_rows,
+                   int32_t* status, int max_items, cudaStream_t st, int phase) {
+  using Cfg = F8Cfg<BN, GATED>;
+  auto kern = moe_gemm_f8_kernel<BN, GATED>;
   static int configured_dev = -1;
   int dev = 0;
   SL_CUDA_TRY(cudaGetDevice(&dev));
@@ -1546,13 +1650,13 @@ int launch_gemm_fp8(const CUtensorMap& tw, const CUtensorMap& twsh, const CUtens
                                      Cfg::kSmemBytes));
     configured_dev = dev;
   }
-  const int max_tiles = max_items * (M_total / TileShape<BN, GATED>::kRowsOut);
+  const int max_tiles = max_items * (M_total / 128);
   int grid = sl_device_sm_count();
   if (grid <= 0) return SL_ERR_CUDA;
   if (max_tiles < grid) grid = max_tiles > 0 ? max_tiles : 1;
-  SL_CUDA_TRY(sl::launch(kern, dim3(grid), dim3(kFp8Threads), Cfg::kSmemBytes, st, tw, twsh, tb,
-                         wscale, wshscale, hdr, items, out, S, K, M_total, out_ld, status,
-                         phase));
+  SL_CUDA_TRY(sl::launch(kern, dim3(grid), dim3(Cfg::kThreads), Cfg::kSmemBytes, st, tw, twsh,
+                         tb, bscale, wscale, wshscale, hdr, items, out_q, out_s, out_z, S, K,
+                         M_total, max_rows, status, phase));
   return SL_OK;
 }
 
@@ -1664,14 +1768,24 @@ int run_fused(const void* hidden, int T, int H, int I, const sl_expert_weights& 
   __nv_bfloat16* A = reinterpret_cast<__nv_bfloat16*>(ws + L.act);
   __nv_bfloat16* Z = reinterpret_cast<__nv_bfloat16*>(ws + L.z);
 
+  // fp8: the gathered rows and the gate/up output are quantised per
+  // 128-column group: e4m3 rows [max_rows, H or I] followed by fp32 scales
+  // [H/128 or I/128, max_rows], inside the bf16 regions
+  uint8_t* Xq = ws + L.x;
+  float* Xs = reinterpret_cast<float*>(ws + L.x + r256(size_t(L.max_rows) * H));
+  uint8_t* Aq = ws + L.act;
+  float* As = reinterpret_cast<float*>(ws + L.act + r256(size_t(L.max_rows) * I));
+
   CUtensorMap m_w13, m_w13sh, m_x, m_w2, m_w2sh, m_a;
   const int nsh = n_shared > 0 ? n_shared : 0;
-  bool ok = make_map(&m_w13, w.w13, H, uint64_t(num_slots) * 2 * I, 64, fp8) &&
+  // bf16 gate/up weight boxes are 64 gate + 64 up rows; fp8 ones 128 + 128
+  const uint32_t w13_box = fp8 ? 128 : 64;
+  bool ok = make_map(&m_w13, w.w13, H, uint64_t(num_slots) * 2 * I, w13_box, fp8) &&
             make_map(&m_w2, w.w2, I, uint64_t(num_slots) * H, BM, fp8) &&
-            make_map(&m_x, X, H, uint64_t(L.max_rows), BN) &&
-            make_map(&m_a, A, I, uint64_t(L.max_rows), BN);
+            make_map(&m_x, fp8 ? static_cast<void*>(Xq) : X, H, uint64_t(L.max_rows), BN, fp8) &&
+            make_map(&m_a, fp8 ? static_cast<void*>(Aq) : A, I, uint64_t(L.max_rows), BN, fp8);
   if (ok && nsh) {
-    ok = make_map(&m_w13sh, w.shared_w13, H, uint64_t(nsh) * 2 * I, 64, fp8) &&
+    ok = make_map(&m_w13sh, w.shared_w13, H, uint64_t(nsh) * 2 * I, w13_box, fp8) &&
          make_map(&m_w2sh, w.shared_w2, I, uint64_t(nsh) * H, BM, fp8);
   } else {
     m_w13sh = m_w13;
@@ -1693,7 +1807,8 @@ int run_fused(const void* hidden, int T, int H, int I, const sl_expert_weights& 
                              0, st, topk_ids, T, topk, expert_map, global_n, num_slots, nsh,
                              nsh ? sh_t0 : 0, nsh ? sh_nt : 0, BN,
                              static_cast<const __nv_bfloat16*>(hidden), H, hdr, items, pair_pos,
-                             X, L.max_items, static_cast<const uint8_t*>(fill_state),
+                             fp8 ? nullptr : X, L.max_items,
+                             static_cast<const uint8_t*>(fill_state),
                              fused ? counters : nullptr, n_counters));
     } else {
       SL_CUDA_TRY(sl::launch(align_kernel, dim3(1), dim3(1024), 0, st, topk_ids, T, topk,
@@ -1701,11 +1816,24 @@ int run_fused(const void* hidden, int T, int H, int I, const sl_expert_weights& 
                              nsh ? sh_nt : 0, BN, static_cast<const __nv_bfloat16*>(hidden), H,
                              hdr, items, pair_pos, X, L.max_items,
                              static_cast<const uint8_t*>(fill_state), 0));
-      SL_CUDA_TRY(sl::launch(gather_kernel, dim3(2 * sl_device_sm_count()), dim3(256), 0, st,
-                             static_cast<const int32_t*>(hdr),
+      if (!fp8)
+        SL_CUDA_TRY(sl::launch(gather_kernel, dim3(2 * sl_device_sm_count()), dim3(256), 0, st,
+                               static_cast<const int32_t*>(hdr),
+                               static_cast<const int32_t*>(pair_pos), P, topk, nsh,
+                               nsh ? sh_t0 : 0, nsh ? sh_nt : 0,
+                               static_cast<const __nv_bfloat16*>(hidden), H, X));
+    }
+    if (fp8) {
+      const long units = static_cast<long>(P + nsh * (nsh ? sh_nt : 0)) * (H / 128);
+      long ctas = (units + 7) / 8;  // 8 warps per CTA, one (row, group) each
+      const long cap = 4L * sl_device_sm_count();
+      if (ctas > cap) ctas = cap;
+      if (ctas < 1) ctas = 1;
+      SL_CUDA_TRY(sl::launch(gather_quant_kernel, dim3(static_cast<unsigned>(ctas)), dim3(256),
+                             0, st, static_cast<const int32_t*>(hdr),
                              static_cast<const int32_t*>(pair_pos), P, topk, nsh,
                              nsh ? sh_t0 : 0, nsh ? sh_nt : 0,
-                             static_cast<const __nv_bfloat16*>(hidden), H, X));
+                             static_cast<const __nv_bfloat16*>(hidden), H, Xq, Xs, L.max_rows));
     }
   }
   if (fused) {
@@ -1727,15 +1855,15 @@ int run_fused(const void* hidden, int T, int H, int I, const sl_expert_weights& 
 #undef SL_FUSED
   }
   int rc = SL_OK;
-#define SL_GEMMS(BNV, R1, C1, R2, C2, S1, S2)                                                    \
+#define SL_GEMMS(BNV, S1, S2)                                                                    \
   if (fp8) {                                                                                     \
-    rc = launch_gemm_fp8<BNV, R1, C1, true>(m_w13, m_w13sh, m_x, w.w13_scale,                   \
-                                            w.shared_w13_scale, hdr, items, A, num_slots, H, I, \
-                                            I, hdr, L.max_items, st, phase);                     \
+    rc = launch_gemm_f8<BNV, true>(m_w13, m_w13sh, m_x, Xs, w.w13_scale, w.shared_w13_scale, hdr, \
+                                   items, Aq, As, nullptr, num_slots, H, I, L.max_rows, hdr,    \
+                                   L.max_items, st, phase);                                      \
     if (rc == SL_OK)                                                                             \
-      rc = launch_gemm_fp8<BNV, R2, C2, false>(m_w2, m_w2sh, m_a, w.w2_scale,                   \
-                                               w.shared_w2_scale, hdr, items, Z, num_slots, I,  \
-                                               H, H, hdr, L.max_items, st, phase);               \
+      rc = launch_gemm_f8<BNV, false>(m_w2, m_w2sh, m_a, As, w.w2_scale, w.shared_w2_scale, hdr, \
+                                      items, nullptr, nullptr, Z, num_slots, I, H, L.max_rows,  \
+                                      hdr, L.max_items, st, phase);                              \
   } else {                                                                                       \
     rc = launch_gemm<BNV, S1, true>(m_w13, m_w13sh, m_x, hdr, items, A, num_slots, H, I, I, hdr, \
                                     L.max_items, st, phase);                                     \
@@ -1744,11 +1872,11 @@ int run_fused(const void* hidden, int T, int H, int I, const sl_expert_weights& 
                                        hdr, L.max_items, st, phase);                             \
   }
   if (BN == 16) {
-    SL_GEMMS(16, 12, 4, 12, 4, 12, 12)
+    SL_GEMMS(16, 12, 12)
   } else if (BN == 64) {
-    SL_GEMMS(64, 8, 3, 8, 3, 9, 9)
+    SL_GEMMS(64, 9, 9)
   } else {
-    SL_GEMMS(128, 6, 3, 6, 3, 6, 6)
+    SL_GEMMS(128, 6, 6)
   }
 #undef SL_GEMMS
   if (rc != SL_OK) return rc;

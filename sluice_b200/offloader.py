@@ -264,11 +264,14 @@ class ExpertStreamOffloader:
                       local_of: list | None = None, pins: list | None = None,
                       device: torch.device | str = "cuda",
                       w13_scale: torch.Tensor | None = None,
-                      w2_scale: torch.Tensor | None = None) -> SlotCache:
+                      w2_scale: torch.Tensor | None = None,
+                      prefill_resident: bool | None = None) -> SlotCache:
         """Install one layer from its local experts ``w13`` [L, 2I, H], ``w2``
         [L, H, I] (bf16, or fp8 e4m3 with fp32 128x128 block scales
         ``w13_scale`` [L, 2I/128, H/128], ``w2_scale`` [L, H/128, I/128]; CPU or
-        CUDA tensors, copied into the host store)."""
+        CUDA tensors, copied into the host store). ``prefill_resident=False``
+        starts a cache with room for every expert (``no_static_full``) holding
+        only the pins, so the rest stream in on first use."""
         device = torch.device(device)
         local_n = w13.shape[0]
         if global_n is None:
@@ -307,7 +310,8 @@ class ExpertStreamOffloader:
             self.caches.append(cache)
             return cache
         init = initial_slot_state(S, local_of, local_n, self.protect_frac, pins,
-                                  prefill_resident=resident_all)
+                                  prefill_resident=resident_all if prefill_resident is None
+                                  else prefill_resident)
         nbytes = lib().sl_slot_state_bytes(S, global_n, local_n)
         state = torch.zeros(nbytes, dtype=torch.uint8, device=device)
         arr = lambda v, t: (t * len(v))(*v)
