@@ -56,11 +56,13 @@ __host__ __device__ inline size_t r256(size_t v) { return (v + 255) & ~size_t(25
 // Token-tile width from the average tokens per used slot: decode steps (a few
 // tokens per expert) use 16, prefill-sized steps 64 or 128 so each weight
 // tile is reused across more tokens.
-inline int choose_bn(int T, int topk, int S) {
+// fp8 stops at 64: its gate/up accumulators (128 token columns x gate and up)
+// would not fit the promotion warps' registers.
+inline int choose_bn(int T, int topk, int S, bool fp8 = false) {
   const long P = static_cast<long>(T) * topk;
   const long used = P < S ? P : S;
   const long avg = used > 0 ? (P + used - 1) / used : 1;
-  return avg <= 16 ? 16 : avg <= 64 ? 64 : 128;
+  return avg <= 16 ? 16 : (avg <= 64 || fp8) ? 64 : 128;
 }
 
 // SLUICE_FUSED=1 runs bf16 decode steps through the single persistent kernel
@@ -487,7 +489,6 @@ constexpr int kXchgStride = 17;  // padded fp32 row of the gate/up exchange
 template <int BN, bool GATED>
 struct TileShape {
   static constexpr int kRowsOut = GATED ? 64 : 128;   // output columns per tile
-  static constexpr int kBoxRows = GATED ? 64 : 128;   // rows per weight TMA box
   static constexpr int kAccCols = BN;                 // TMEM columns per accumulator
   static constexpr int kTmemCols = (2 * BN) <= 32 ? 32 : (2 * BN) <= 64 ? 64
                                    : (2 * BN) <= 128 ? 128 : 256;
@@ -803,10 +804,11 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(
 // promotion / epilogue warps (4, or 8 for 128-token tiles: two groups of
 // token columns).
 constexpr int F8_BK = 128;  // K per stage: one scale block, one 128-byte swizzle row
+constexpr int kF8MaxKBlocks = 64;  // K <= 8192: a tile's weight scales fit in shared memory
 
 template <int BN, bool GATED>
 struct F8Cfg {
-  static constexpr int kNP = BN == 128 ? 8 : 4;         // promotion warps
+  static constexpr int kNP = BN >= 64 ? 8 : 4;          // promotion warps
   static constexpr int kThreads = 64 + 32 * kNP;
   static constexpr int kCW = BN / (kNP / 4);             // token columns per promotion warp
   static constexpr int kATiles = GATED ? 2 : 1;          // 128-row weight tiles per stage
@@ -819,7 +821,10 @@ struct F8Cfg {
   static constexpr int kTmemUsed = kNB * kAccCols;
   static constexpr int kTmemCols = kTmemUsed <= 32 ? 32 : kTmemUsed <= 64 ? 64
                                    : kTmemUsed <= 128 ? 128 : kTmemUsed <= 256 ? 256 : 512;
-  static constexpr int kFixed = 1024 /*align*/ + 4 * BN * 4 /*amax*/ + 1024 /*barriers*/;
+  // + amax exchange [4][BN], combined scales [2 parities][gate, up][BN],
+  // the tile's weight block scales [2 column groups][gate, up][64 K blocks]
+  static constexpr int kFixed = 1024 /*align*/ + 4 * BN * 4 + 4 * BN * 4 + 256 * 4 +
+                                1024 /*barriers*/;
   static constexpr int kStagesRaw = (220 * 1024 - kFixed) / (kStageBytes + BN * 4);
   static constexpr int kStages = kStagesRaw > 12 ? 12 : kStagesRaw;
   static constexpr int kSmemBytes = kStages * (kStageBytes + BN * 4) + kFixed;
@@ -846,7 +851,10 @@ __device__ __forceinline__ float q_clamp(float x, float scale) {
 
 // Token rows for the fp8 GEMMs: row pair_pos[p] <- hidden row p / topk (and
 // the shared experts' rows <- their tokens), quantised per 128-column group:
-// Xq [max_rows, H] e4m3, Xs [H/128, max_rows] fp32. One warp per (row, group).
+// Xq [max_rows, H] e4m3, Xs [H/128, max_rows] fp32. A warp takes four groups
+// of one row at a time (four independent 8-byte loads per lane in flight).
+constexpr int kQuantGroups = 4;
+
 __global__ void __launch_bounds__(256) gather_quant_kernel(
     const int32_t* __restrict__ ws_hdr, const int32_t* __restrict__ pair_pos, int P, int topk,
     int n_sh, int sh_t0, int sh_nt, const __nv_bfloat16* __restrict__ hs, int H,
@@ -855,11 +863,12 @@ __global__ void __launch_bounds__(256) gather_quant_kernel(
   sl::pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int G = H / 128;
-  const long n_units = static_cast<long>(P + n_sh * sh_nt) * G;
+  const int GU = (G + kQuantGroups - 1) / kQuantGroups;  // units per row
+  const long n_units = static_cast<long>(P + n_sh * sh_nt) * GU;
   const long nwarps = static_cast<long>(gridDim.x) * (blockDim.x >> 5);
   for (long u = static_cast<long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
        u < n_units; u += nwarps) {
-    const int r = static_cast<int>(u / G), kb = static_cast<int>(u % G);
+    const int r = static_cast<int>(u / GU), kb0 = static_cast<int>(u % GU) * kQuantGroups;
     int pos, tok;
     if (r < P) {
       pos = pair_pos[r];
@@ -870,17 +879,27 @@ __global__ void __launch_bounds__(256) gather_quant_kernel(
       tok = sh_t0 + t;
     }
     if (pos < 0) continue;  // the same for the whole warp
-    const uint2 raw = *reinterpret_cast<const uint2*>(hs + static_cast<size_t>(tok) * H +
-                                                      kb * 128 + lane * 4);
-    const float2 f01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
-    const float2 f23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
-    float m = fmaxf(fmaxf(fabsf(f01.x), fabsf(f01.y)), fmaxf(fabsf(f23.x), fabsf(f23.y)));
+    uint2 raw[kQuantGroups];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    const float sc = group_scale(m);
-    *reinterpret_cast<uint32_t*>(Xq + static_cast<size_t>(pos) * H + kb * 128 + lane * 4) =
-        e4m3x4(q_clamp(f01.x, sc), q_clamp(f01.y, sc), q_clamp(f23.x, sc), q_clamp(f23.y, sc));
-    if (lane == 0) Xs[static_cast<size_t>(kb) * max_rows + pos] = sc;
+    for (int g = 0; g < kQuantGroups; ++g)
+      if (kb0 + g < G)
+        raw[g] = *reinterpret_cast<const uint2*>(hs + static_cast<size_t>(tok) * H +
+                                                 (kb0 + g) * 128 + lane * 4);
+#pragma unroll
+    for (int g = 0; g < kQuantGroups; ++g) {
+      const int kb = kb0 + g;
+      if (kb >= G) break;
+      const float2 f01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw[g].x));
+      const float2 f23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw[g].y));
+      float m = fmaxf(fmaxf(fabsf(f01.x), fabsf(f01.y)), fmaxf(fabsf(f23.x), fabsf(f23.y)));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      const float sc = group_scale(m);
+      *reinterpret_cast<uint32_t*>(Xq + static_cast<size_t>(pos) * H + kb * 128 + lane * 4) =
+          e4m3x4(q_clamp(f01.x, sc), q_clamp(f01.y, sc), q_clamp(f23.x, sc),
+                 q_clamp(f23.y, sc));
+      if (lane == 0) Xs[static_cast<size_t>(kb) * max_rows + pos] = sc;
+    }
   }
 }
 
@@ -902,7 +921,9 @@ __global__ void __launch_bounds__(F8Cfg<BN, GATED>::kThreads, 1) moe_gemm_f8_ker
   uint8_t* sAB = smem;                                                  // [ST][A | B]
   float* sS = reinterpret_cast<float*>(sAB + ST * Cfg::kStageBytes);    // [ST][BN]
   float* red = sS + ST * BN;                                            // [4][BN]
-  uint64_t* full = reinterpret_cast<uint64_t*>(red + 4 * BN);
+  float* cbuf = red + 4 * BN;                                           // [2][2][BN]
+  float* wsc = cbuf + 4 * BN;                                           // [2][2][64]
+  uint64_t* full = reinterpret_cast<uint64_t*>(wsc + 256);
   uint64_t* empty = full + ST;
   uint64_t* tfull = empty + ST;
   uint64_t* tempty = tfull + NB;
@@ -1086,6 +1107,14 @@ __global__ void __launch_bounds__(F8Cfg<BN, GATED>::kThreads, 1) moe_gemm_f8_ker
       const int srows = GATED ? 2 * (M_total / 128) : M_total / 128;
       const float* sc_g = scale + (static_cast<size_t>(e) * srows + mt) * kscale;
       const float* sc_u = GATED ? sc_g + static_cast<size_t>(M_total / 128) * kscale : sc_g;
+      const int gt = (pw & 3) * 32 + lane;  // thread index within the column group
+      // the tile's weight block scales into shared memory, once per tile
+      float* my_wsc = wsc + cg * 128;        // [gate, up][64]
+      if (gt < kscale) {
+        my_wsc[gt] = __ldg(sc_g + gt);
+        if constexpr (GATED) my_wsc[64 + gt] = __ldg(sc_u + gt);
+      }
+      named_bar_sync(1 + cg, 128);
       float acc_g[CW], acc_u[GATED ? CW : 1];
 #pragma unroll
       for (int i = 0; i < CW; ++i) acc_g[i] = 0.f;
@@ -1094,30 +1123,55 @@ __global__ void __launch_bounds__(F8Cfg<BN, GATED>::kThreads, 1) moe_gemm_f8_ker
         for (int i = 0; i < CW; ++i) acc_u[i] = 0.f;
       }
       for (int kb = 0; kb < k_blocks; ++kb) {
-        const float swg = __ldg(sc_g + kb);
-        const float swu = GATED ? __ldg(sc_u + kb) : 0.f;
         // the accumulator of this K block, then the stage's token scales
         // (landed with the stage; its full phase stays complete until this
         // warp releases the stage)
         ok = ok && !*abort_flag && sl::mbar_wait(&tfull[b], bph) && sl::mbar_wait(&full[s], ph);
+        // combined scales of this column group for this K block:
+        // c[j] = weight block scale x token j's group scale
+        float* cb = cbuf + (kb & 1) * 2 * BN;
+        uint32_t vg[CW], vu[GATED ? CW : 1];
         if (ok) {
           sl::tc_fence_after();
           const uint32_t taddr = tmem_base + b * Cfg::kAccCols +
                                  (static_cast<uint32_t>(q * 32) << 16) + c0;
-          const float* sa = sS + s * BN + c0;
+          // every TMEM load of the stage in flight before the scales are made
 #pragma unroll
-          for (int cc = 0; cc < CW; cc += 16) {
-            uint32_t vg[16], vu[16];
-            sl::tmem_ld16_nowait(taddr + cc, vg);
-            if constexpr (GATED) sl::tmem_ld16_nowait(taddr + BN + cc, vu);
-            sl::tmem_wait_ld(vg);
-            if constexpr (GATED) sl::tmem_wait_ld(vu);
+          for (int cc = 0; cc < CW; cc += 16)
+            sl::tmem_ld16_nowait(taddr + cc, *reinterpret_cast<uint32_t(*)[16]>(vg + cc));
+          if constexpr (GATED) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const float a_s = sa[cc + i];
-              acc_g[cc + i] = fmaf(__uint_as_float(vg[i]), swg * a_s, acc_g[cc + i]);
-              if constexpr (GATED)
-                acc_u[cc + i] = fmaf(__uint_as_float(vu[i]), swu * a_s, acc_u[cc + i]);
+            for (int cc = 0; cc < CW; cc += 16)
+              sl::tmem_ld16_nowait(taddr + BN + cc, *reinterpret_cast<uint32_t(*)[16]>(vu + cc));
+          }
+          for (int v = gt; v < (GATED ? 2 : 1) * CW; v += 128) {
+            const int which = v >= CW, j = c0 + (v - which * CW);
+            cb[which * BN + j] = my_wsc[which * 64 + kb] * sS[s * BN + j];
+          }
+        }
+        named_bar_sync(1 + cg, 128);  // every warp of the group, ok or not
+        if (ok) {
+#pragma unroll
+          for (int cc = 0; cc < CW; cc += 16)
+            sl::tmem_wait_ld(*reinterpret_cast<uint32_t(*)[16]>(vg + cc));
+          if constexpr (GATED) {
+#pragma unroll
+            for (int cc = 0; cc < CW; cc += 16)
+              sl::tmem_wait_ld(*reinterpret_cast<uint32_t(*)[16]>(vu + cc));
+          }
+#pragma unroll
+          for (int i = 0; i < CW; i += 4) {
+            const float4 c4 = *reinterpret_cast<const float4*>(cb + c0 + i);
+            acc_g[i] = fmaf(__uint_as_float(vg[i]), c4.x, acc_g[i]);
+            acc_g[i + 1] = fmaf(__uint_as_float(vg[i + 1]), c4.y, acc_g[i + 1]);
+            acc_g[i + 2] = fmaf(__uint_as_float(vg[i + 2]), c4.z, acc_g[i + 2]);
+            acc_g[i + 3] = fmaf(__uint_as_float(vg[i + 3]), c4.w, acc_g[i + 3]);
+            if constexpr (GATED) {
+              const float4 u4 = *reinterpret_cast<const float4*>(cb + BN + c0 + i);
+              acc_u[i] = fmaf(__uint_as_float(vu[i]), u4.x, acc_u[i]);
+              acc_u[i + 1] = fmaf(__uint_as_float(vu[i + 1]), u4.y, acc_u[i + 1]);
+              acc_u[i + 2] = fmaf(__uint_as_float(vu[i + 2]), u4.z, acc_u[i + 2]);
+              acc_u[i + 3] = fmaf(__uint_as_float(vu[i + 3]), u4.w, acc_u[i + 3]);
             }
           }
           sl::tc_fence_before();
@@ -1728,7 +1782,11 @@ int launch_gemm(const CUtensorMap& tw, const CUtensorMap& twsh, const CUtensorMa
 extern "C" size_t sl_fused_experts_workspace_bytes(int T, int topk, int H, int I,
                                                    int num_slots, int n_shared) {
   if (T < 0 || topk <= 0 || H <= 0 || I <= 0 || num_slots <= 0 || n_shared < 0) return 0;
-  return ws_layout(T, topk, H, I, num_slots, n_shared, choose_bn(T, topk, num_slots)).total;
+  // large enough for either weight dtype's token tiles
+  const size_t a = ws_layout(T, topk, H, I, num_slots, n_shared, choose_bn(T, topk, num_slots)).total;
+  const size_t b = ws_layout(T, topk, H, I, num_slots, n_shared,
+                             choose_bn(T, topk, num_slots, true)).total;
+  return a > b ? a : b;
 }
 
 namespace {
@@ -1757,7 +1815,8 @@ int run_fused(const void* hidden, int T, int H, int I, const sl_expert_weights& 
   if ((reinterpret_cast<uintptr_t>(workspace) & 255) ||
       ((reinterpret_cast<uintptr_t>(hidden) | reinterpret_cast<uintptr_t>(out)) & 15))
     return SL_ERR_INVALID;
-  const int BN = choose_bn(T, topk, num_slots);
+  if (fp8 && (H / 128 > kF8MaxKBlocks || I / 128 > kF8MaxKBlocks)) return SL_ERR_UNSUPPORTED;
+  const int BN = choose_bn(T, topk, num_slots, fp8);
   const WsLayout L = ws_layout(T, topk, H, I, num_slots, n_shared, BN);
   if (workspace_bytes < L.total) return SL_ERR_INVALID;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
@@ -1824,9 +1883,10 @@ int run_fused(const void* hidden, int T, int H, int I, const sl_expert_weights& 
                                static_cast<const __nv_bfloat16*>(hidden), H, X));
     }
     if (fp8) {
-      const long units = static_cast<long>(P + nsh * (nsh ? sh_nt : 0)) * (H / 128);
-      long ctas = (units + 7) / 8;  // 8 warps per CTA, one (row, group) each
-      const long cap = 4L * sl_device_sm_count();
+      const long units = static_cast<long>(P + nsh * (nsh ? sh_nt : 0)) *
+                         ((H / 128 + kQuantGroups - 1) / kQuantGroups);
+      long ctas = (units + 7) / 8;  // 8 warps per CTA, one unit each
+      const long cap = 8L * sl_device_sm_count();
       if (ctas > cap) ctas = cap;
       if (ctas < 1) ctas = 1;
       SL_CUDA_TRY(sl::launch(gather_quant_kernel, dim3(static_cast<unsigned>(ctas)), dim3(256),
@@ -1855,30 +1915,35 @@ int run_fused(const void* hidden, int T, int H, int I, const sl_expert_weights& 
 #undef SL_FUSED
   }
   int rc = SL_OK;
-#define SL_GEMMS(BNV, S1, S2)                                                                    \
-  if (fp8) {                                                                                     \
-    rc = launch_gemm_f8<BNV, true>(m_w13, m_w13sh, m_x, Xs, w.w13_scale, w.shared_w13_scale, hdr, \
-                                   items, Aq, As, nullptr, num_slots, H, I, L.max_rows, hdr,    \
-                                   L.max_items, st, phase);                                      \
-    if (rc == SL_OK)                                                                             \
-      rc = launch_gemm_f8<BNV, false>(m_w2, m_w2sh, m_a, As, w.w2_scale, w.shared_w2_scale, hdr, \
-                                      items, nullptr, nullptr, Z, num_slots, I, H, L.max_rows,  \
-                                      hdr, L.max_items, st, phase);                              \
-  } else {                                                                                       \
-    rc = launch_gemm<BNV, S1, true>(m_w13, m_w13sh, m_x, hdr, items, A, num_slots, H, I, I, hdr, \
-                                    L.max_items, st, phase);                                     \
-    if (rc == SL_OK)                                                                             \
-      rc = launch_gemm<BNV, S2, false>(m_w2, m_w2sh, m_a, hdr, items, Z, num_slots, I, H, H,     \
-                                       hdr, L.max_items, st, phase);                             \
-  }
-  if (BN == 16) {
-    SL_GEMMS(16, 12, 12)
+#define SL_GEMMS_BF16(BNV, S1, S2)                                                              \
+  rc = launch_gemm<BNV, S1, true>(m_w13, m_w13sh, m_x, hdr, items, A, num_slots, H, I, I, hdr,   \
+                                  L.max_items, st, phase);                                       \
+  if (rc == SL_OK)                                                                               \
+    rc = launch_gemm<BNV, S2, false>(m_w2, m_w2sh, m_a, hdr, items, Z, num_slots, I, H, H, hdr,  \
+                                     L.max_items, st, phase);
+#define SL_GEMMS_F8(BNV)                                                                         \
+  rc = launch_gemm_f8<BNV, true>(m_w13, m_w13sh, m_x, Xs, w.w13_scale, w.shared_w13_scale, hdr,  \
+                                 items, Aq, As, nullptr, num_slots, H, I, L.max_rows, hdr,      \
+                                 L.max_items, st, phase);                                        \
+  if (rc == SL_OK)                                                                               \
+    rc = launch_gemm_f8<BNV, false>(m_w2, m_w2sh, m_a, As, w.w2_scale, w.shared_w2_scale, hdr,   \
+                                    items, nullptr, nullptr, Z, num_slots, I, H, L.max_rows,    \
+                                    hdr, L.max_items, st, phase);
+  if (fp8) {
+    if (BN == 16) {
+      SL_GEMMS_F8(16)
+    } else {
+      SL_GEMMS_F8(64)
+    }
+  } else if (BN == 16) {
+    SL_GEMMS_BF16(16, 12, 12)
   } else if (BN == 64) {
-    SL_GEMMS(64, 9, 9)
+    SL_GEMMS_BF16(64, 9, 9)
   } else {
-    SL_GEMMS(128, 6, 6)
+    SL_GEMMS_BF16(128, 6, 6)
   }
-#undef SL_GEMMS
+#undef SL_GEMMS_BF16
+#undef SL_GEMMS_F8
   if (rc != SL_OK) return rc;
   if (phase == 0) return SL_OK;
   dim3 cgrid((H / 8 + 255) / 256, T);
