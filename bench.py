@@ -78,33 +78,93 @@ def _workload(cfg, slots, tokens, layers, world=1):
 
 
 # ------------------------------------------------------------ clock sampling
+_REASON_BITS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40,
+                "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4}
+
+
 class ClockSampler:
+    """SM clock, power and throttle reasons of this process's GPU, sampled
+    every 10 ms through NVML on a thread while the timed region runs (so even
+    a region of tens of milliseconds gets samples); ``nvidia-smi -lms 200`` if
+    NVML is unavailable. Read-only: no setting of the GPU is changed."""
+
     def __init__(self, index: int):
         self.index = index
-        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
-        self.p = None
+        self.rows = []
+        self._stop = None
+        self._thread = None
+        self._smi = None
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        try:
+            uuid = str(torch.cuda.get_device_properties(self.index).uuid)
+            if not uuid.startswith("GPU-"):
+                uuid = "GPU-" + uuid
+            return pynvml.nvmlDeviceGetHandleByUUID(uuid)
+        except Exception:
+            return pynvml.nvmlDeviceGetHandleByIndex(self.index)
 
     def __enter__(self):
+        import threading
+        try:
+            import pynvml
+            h = self._nvml_handle()
+            mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            self._stop = threading.Event()
+
+            def run():
+                while not self._stop.is_set():
+                    try:
+                        sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                        pw = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
+                        rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                        self.rows.append((sm, mx, pw, rs))
+                    except Exception:
+                        pass
+                    self._stop.wait(0.01)
+
+            self._thread = threading.Thread(target=run, daemon=True)
+            self._thread.start()
+        except Exception:
+            self._start_smi()
+        return self
+
+    def _start_smi(self):
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         try:
-            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
-                                       "-i", str(self.index), "-lms", "200"],
-                                      stdout=self.f, stderr=subprocess.DEVNULL)
+            self._smi = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-i",
+                                          str(self.index), "-lms", "200"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:
-            self.p = None
-        return self
+            self._smi = None
 
     def __exit__(self, *a):
-        if self.p is not None:
-            self.p.terminate()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
+        if self._smi is not None:
+            self._smi.terminate()
             try:
-                self.p.wait(timeout=5)
+                self._smi.wait(timeout=5)
             except Exception:
-                self.p.kill()
+                self._smi.kill()
 
     def summary(self):
+        if self._thread is not None:
+            if not self.rows:
+                return None
+            sm = [r[0] for r in self.rows]
+            reasons = sorted({n for r in self.rows for n, bit in _REASON_BITS.items()
+                              if r[3] & bit})
+            return {"sm_mhz": statistics.median(sm), "sm_max_mhz": self.rows[0][1],
+                    "power_w_max": max(r[2] for r in self.rows), "reasons": reasons,
+                    "samples": len(self.rows), "source": "nvml, 10 ms"}
         try:
             self.f.flush()
             with open(self.f.name) as fh:
@@ -120,7 +180,7 @@ class ClockSampler:
         reasons = sorted({names[i] for r in rows for i in range(4)
                           if len(r) > 5 + i and r[5 + i].strip() == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(rows), "source": "nvidia-smi, 200 ms"}
 
 
 # --------------------------------------------------------------- CPU port
