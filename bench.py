@@ -426,7 +426,7 @@ def run_sluice(a):
     if world > 1:
         from sluice_b200.ep import EPDecodeStack
         stack = EPDecodeStack(cfg, slots=a.slots, seed=a.seed, num_layers=layers,
-                              exchange=a.exchange, max_tokens=T)
+                              exchange=a.exchange, max_tokens=T, overlap=not a.no_overlap)
         graphed = stack.capture(tokens=T)
     else:
         stack = MoEDecodeStack(cfg, slots=a.slots, seed=a.seed, num_layers=layers,

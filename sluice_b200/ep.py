@@ -158,7 +158,8 @@ class EPMoELayer:
 
     def __init__(self, cfg: MoEConfig, router: ops.Router, cache, shared_w13, shared_w2,
                  group=None, shared_w13_scale=None, shared_w2_scale=None,
-                 exchange: "NvlinkExchange | None" = None):
+                 exchange: "NvlinkExchange | None" = None, overlap: bool = True,
+                 stream_ctas: int = 16):
         self.cfg = cfg
         self.exchange = exchange  # None: NCCL all-gather / reduce-scatter
         self.shared_w13_scale = shared_w13_scale
@@ -171,6 +172,10 @@ class EPMoELayer:
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         self.last_ids = None
+        # overlap the gap's expert stream with the resident experts' GEMMs
+        self.overlap = overlap and not cache.static_full
+        self.stream_ctas = stream_ctas
+        self._side = torch.cuda.Stream(device=cache.device) if self.overlap else None
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         T = x.shape[0]
@@ -180,14 +185,31 @@ class EPMoELayer:
         else:
             xg, twg, tig = dispatch(x, tw, ti, self.group)
         self.last_ids = tig
-        self.cache.gap(tig)
         c = self.cache
-        part = ops.fused_experts_partial(
-            xg, c.w13, c.w2, twg, tig, c.expert_map, self.shared_w13, self.shared_w2,
-            shared_t0=self.rank * T, shared_nt=T,
-            routed_scaling_factor=self.cfg.routed_scaling_factor, w1_scale=c.w13_scale,
-            w2_scale=c.w2_scale, shared_w13_scale=self.shared_w13_scale,
-            shared_w2_scale=self.shared_w2_scale)
+        kw = dict(shared_t0=self.rank * T, shared_nt=T,
+                  routed_scaling_factor=self.cfg.routed_scaling_factor, w1_scale=c.w13_scale,
+                  w2_scale=c.w2_scale, shared_w13_scale=self.shared_w13_scale,
+                  shared_w2_scale=self.shared_w2_scale)
+        args = (xg, c.w13, c.w2, twg, tig, c.expert_map, self.shared_w13, self.shared_w2)
+        if self.overlap:
+            # plan -> [stream on a side stream || resident experts] -> streamed experts
+            main = torch.cuda.current_stream()
+            c.plan(tig)
+            self._side.wait_stream(main)
+            with torch.cuda.stream(self._side):
+                c.stream(self.stream_ctas)
+            n_sh = 0 if self.shared_w13 is None else self.shared_w13.shape[0]
+            ws = ops.fused_experts_workspace(xg.shape[0], tig.shape[1], xg.shape[1],
+                                             c.w13.shape[1] // 2, c.num_slots, n_sh, xg.device)
+            part = torch.empty(xg.shape, dtype=torch.float32, device=xg.device)
+            ops.fused_experts_partial(*args, out=part, slot_state=c.state, phase=0,
+                                      workspace=ws, **kw)
+            main.wait_stream(self._side)
+            ops.fused_experts_partial(*args, out=part, slot_state=c.state, phase=1,
+                                      workspace=ws, **kw)
+        else:
+            c.gap(tig)
+            part = ops.fused_experts_partial(*args, **kw)
         if self.exchange is not None:
             return self.exchange.combine(part)
         return combine(part, self.group).to(torch.bfloat16)
@@ -200,7 +222,7 @@ class EPDecodeStack:
 
     def __init__(self, cfg: MoEConfig, slots: int, seed: int = 0, device="cuda",
                  num_layers: int | None = None, group=None, protect_frac=None,
-                 exchange: str = "nvlink", max_tokens: int = 16):
+                 exchange: str = "nvlink", max_tokens: int = 16, overlap: bool = True):
         from . import synth
         from .offloader import ExpertStreamOffloader
 
@@ -227,7 +249,8 @@ class EPDecodeStack:
             self.layers.append(EPMoELayer(cfg, ops.Router(cfg.routing, gw, lb, sb), cache,
                                           sh.get("shared_w13"), sh.get("shared_w2"), group,
                                           sh.get("shared_w13_scale"),
-                                          sh.get("shared_w2_scale"), self.exchange))
+                                          sh.get("shared_w2_scale"), self.exchange,
+                                          overlap=overlap))
         torch.cuda.synchronize(self.device)
         dist.barrier(group)  # ranks enter the first exchange together (peer waits are bounded)
         self.graph = None

@@ -218,16 +218,20 @@ def fused_experts_partial(hidden_states, w1, w2, topk_weights, topk_ids, expert_
                           shared_w13=None, shared_w2=None, shared_t0: int = 0,
                           shared_nt: int = 0, routed_scaling_factor: float = 1.0,
                           out=None, w1_scale=None, w2_scale=None, shared_w13_scale=None,
-                          shared_w2_scale=None) -> torch.Tensor:
+                          shared_w2_scale=None, slot_state=None, phase: int = -1,
+                          workspace=None) -> torch.Tensor:
     """Expert-parallel partial output [T, H] fp32: this rank's experts (the
     ones ``expert_map`` maps) scaled by ``routed_scaling_factor``, plus the
-    shared experts on rows [shared_t0, shared_t0 + shared_nt)."""
+    shared experts on rows [shared_t0, shared_t0 + shared_nt). ``phase`` 0 / 1
+    split the call around the gap's expert stream as ``fused_experts_phase``
+    does (both phases: the same ``slot_state``, ``workspace`` and ``out``)."""
     return _fused_ex(hidden_states, w1, w2, topk_weights, topk_ids, expert_map,
                      expert_map.numel(), w1_scale=w1_scale, w2_scale=w2_scale,
                      shared_w13=shared_w13, shared_w2=shared_w2,
                      shared_w13_scale=shared_w13_scale, shared_w2_scale=shared_w2_scale,
                      routed_scaling_factor=routed_scaling_factor, shared_t0=shared_t0,
-                     shared_nt=shared_nt, out_f32=True, out=out)
+                     shared_nt=shared_nt, out_f32=True, out=out, slot_state=slot_state,
+                     phase=phase, workspace=workspace)
 
 
 fused_experts_partial.last_workspace = None

@@ -25,7 +25,7 @@ def _free_port():
     return p
 
 
-def _rank_main(rank, world, port, out_dir, exchange):
+def _rank_main(rank, world, port, out_dir, exchange, slots=48):
     import torch.distributed as dist
 
     from oracle import moe as omoe
@@ -40,7 +40,7 @@ def _rank_main(rank, world, port, out_dir, exchange):
                             device_id=torch.device("cuda", rank))
     try:
         cfg = configs.V2_LITE
-        stack = ep.EPDecodeStack(cfg, slots=48, seed=3, num_layers=1, exchange=exchange)
+        stack = ep.EPDecodeStack(cfg, slots=slots, seed=3, num_layers=1, exchange=exchange)
         layer = stack.layers[0]
         w13, w2 = synth.layer_weights(cfg, 0, 3, device="cuda")
         w13, w2 = w13.cpu(), w2.cpu()
@@ -102,10 +102,13 @@ def _agree_main(rank, world, port, out_dir):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("exchange", ["nvlink", "nccl"])
-def test_ep2_layer_matches_oracle(tmp_path, exchange):
-    mp.start_processes(_rank_main, args=(2, _free_port(), str(tmp_path), exchange), nprocs=2,
-                       start_method="spawn")
+@pytest.mark.parametrize("exchange,slots", [("nvlink", 48), ("nccl", 48), ("nvlink", 24)],
+                         ids=["nvlink-resident", "nccl-resident", "nvlink-offloaded"])
+def test_ep2_layer_matches_oracle(tmp_path, exchange, slots):
+    """slots 48 >= 32 local experts: every expert resident; slots 24: the
+    gap streams misses on a side stream while the resident experts run."""
+    mp.start_processes(_rank_main, args=(2, _free_port(), str(tmp_path), exchange, slots),
+                       nprocs=2, start_method="spawn")
     for r in range(2):
         errs = torch.load(os.path.join(tmp_path, f"err{r}.pt"))
         assert (errs < 2e-2).all(), errs
