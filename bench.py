@@ -54,6 +54,8 @@ def _args(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-resident", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--lfu", action="store_true",
+                    help="SLUICE_LFU=1: popularity-ordered protected victims (opt-in policy)")
     ap.add_argument("--exchange", default="nvlink", choices=["nvlink", "nccl"],
                     help="expert-parallel dispatch/combine (N>1): peer-memory kernels or NCCL")
     ap.add_argument("--no-overlap", action="store_true",
@@ -407,6 +409,9 @@ def _step_bytes(stack, cfg):
 def run_sluice(a):
     import datetime
 
+    if a.lfu:
+        os.environ["SLUICE_LFU"] = "1"
+
     from sluice_b200 import configs, synth
     from sluice_b200.layer import MoEDecodeStack
 
@@ -580,6 +585,7 @@ def run_sluice(a):
                    "model": cfg.name, "tokens_per_step": T, "slots": min(a.slots, local_n),
                    "layers": layers, "global_batch": T * world, "seq_len": 1,
                    "parallelism": f"ep{world}" if world > 1 else "single",
+                   "slot_policy": "slru+lfu" if a.lfu else "slru",
                    "ep_exchange": a.exchange if world > 1 else None,
                    "local_experts": local_n, "offloaded": offloaded, "cuda_graph": graphed,
                    "stream_overlap": offloaded and not a.no_overlap,

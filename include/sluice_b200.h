@@ -85,18 +85,25 @@ int sl_select_experts(const void* router_logits, int T, int E, int topk,
 enum {
   SL_SEG_FREE = 0, SL_SEG_PROBATION = 1, SL_SEG_PROTECTED = 2, SL_SEG_PINNED = 3
 };
-enum { SL_PLAN_FAST_HIT = 1 }; /* SLUICE_RS_FAST_HIT (offloader.py:2409-2424) */
+enum {
+  SL_PLAN_FAST_HIT = 1, /* SLUICE_RS_FAST_HIT (offloader.py:2409-2424) */
+  SL_PLAN_LFU = 2       /* SLUICE_LFU: popularity counts (_bump_freq 1993-2007,
+                           halved every 256 calls) order the protected victims
+                           (_coldest_protected 2023-2034, _acquire_slot 2056-2066) */
+};
 
 /* Field offsets (bytes) inside the state block, in this order:
  * 0 header (int32 x 16, see SL_HDR_*), 1 counters (uint64 x 8, SL_CNT_*),
  * 2 local_of[global_n], 3 global_of_local[local_n], 4 slot_of[local_n],
  * 5 expert_in_slot[S], 6 seg[S] (uint8), 7 stamp[S] (uint32),
- * 8 free_stack[S], 9 fill_local[S], 10 fill_slot[S]; offsets[11] = total. */
-enum { SL_STATE_NFIELDS = 11 };
+ * 8 free_stack[S], 9 fill_local[S], 10 fill_slot[S], 11 freq[local_n]
+ * (uint32 popularity counts, SL_PLAN_LFU); offsets[12] = total. */
+enum { SL_STATE_NFIELDS = 12 };
 enum {
   SL_HDR_NUM_SLOTS = 0, SL_HDR_GLOBAL_N, SL_HDR_LOCAL_N, SL_HDR_PROTECTED_CAP,
   SL_HDR_FLAGS, SL_HDR_MAP_IS_STANDING, SL_HDR_FREE_TOP, SL_HDR_PROTECTED_COUNT,
-  SL_HDR_CLOCK, SL_HDR_STATUS, SL_HDR_FILL_COUNT, SL_HDR_LAST_MISSES
+  SL_HDR_CLOCK, SL_HDR_STATUS, SL_HDR_FILL_COUNT, SL_HDR_LAST_MISSES,
+  SL_HDR_LFU_STEPS /* calls since the counts were last halved */
 };
 enum {
   SL_CNT_GAPS = 0, SL_CNT_FAST_HITS, SL_CNT_MISSES, SL_CNT_HITS,

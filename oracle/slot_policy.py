@@ -9,8 +9,12 @@ cache that kfirtoledo/sluice keeps in ``src/sluice/offloader.py``:
   min(SLUICE_SLOTS, local_n)``, ``protected_cap = min(int(slots*frac),
   slots-1)``, free list ``[slots-1, ..., 0]`` popped from the end;
 * pins: ``_apply_pins`` (offloader.py:1046-1083);
-* policy: ``_touch`` (2009-2021), ``_coldest_protected`` (2023-2034, LRU
-  branch), ``_acquire_slot`` (2036-2074), ``_evict_to`` (2076-2081);
+* policy: ``_touch`` (2009-2021), ``_coldest_protected`` (2023-2034),
+  ``_acquire_slot`` (2036-2074), ``_evict_to`` (2076-2081);
+* the LFU hybrid (``SLUICE_LFU=1``): ``_bump_freq`` (1993-2007: +1 per
+  selected owned expert per step, counts halved every ``LFU_AGE_STEPS`` =
+  256 steps, offloader.py:118) and the frequency-ordered protected victims of
+  ``_coldest_protected`` / ``_acquire_slot`` (ties in LRU order);
 * maps: ``_write_map`` / ``_write_standing_map`` (2083-2123);
 * the gap body: ``_router_split_gap`` (2362-2467), FAST_HIT on or off.
 
@@ -19,13 +23,15 @@ ordered dictionaries: a segment's LRU order is its slots sorted by stamp, and
 "move to end" / "insert at end" is "take a new stamp". This is the same
 representation the CUDA planner uses, so the oracle also documents it.
 
-The LFU hybrid (``SLUICE_LFU``) is not restated: it is off by default in the
-reference and outside the decode hot path this build covers.
+Under LFU the counts are bumped once per gap call, before the FAST_HIT check
+(the reference bumps them in its hook for every real step, then runs the
+gap's policy with them).
 """
 
 from __future__ import annotations
 
 FREE, PROBATION, PROTECTED, PINNED = 0, 1, 2, 3
+LFU_AGE_STEPS = 256  # offloader.py:118
 
 
 class SlotOverflow(RuntimeError):
@@ -50,13 +56,17 @@ class SlotPolicyModel:
 
     def __init__(self, num_slots: int, local_of: list[int], local_n: int,
                  protect_frac: float = 0.5, fast_hit: bool = True,
-                 bytes_per_expert: int = 0, prefill_resident: bool = False):
+                 bytes_per_expert: int = 0, prefill_resident: bool = False,
+                 lfu: bool = False):
         self.num_slots = int(num_slots)
         self.local_of = [int(v) for v in local_of]
         self.global_n = len(self.local_of)
         self.local_n = int(local_n)
         self.protected_cap = protected_cap_for(self.num_slots, protect_frac)
         self.fast_hit = bool(fast_hit)
+        self.lfu = bool(lfu)
+        self.freq = [0] * int(local_n)
+        self.lfu_steps = 0
         self.bytes_per_expert = int(bytes_per_expert)
         self.global_of_local = [-1] * self.local_n
         for g, loc in enumerate(self.local_of):
@@ -133,11 +143,29 @@ class SlotPolicyModel:
                 self.seg[slot] = PROTECTED
                 self.stamp[slot] = self._tick()
                 while self.protected_count() > self.protected_cap:
-                    demoted = self._lru(PROTECTED)[0]
+                    demoted = self._coldest_protected()
                     self.seg[demoted] = PROBATION
                     self.stamp[demoted] = self._tick()
             else:
                 self.stamp[slot] = self._tick()
+
+    def _coldest_protected(self) -> int:
+        """offloader.py:2023-2034: least frequently used under LFU (ties in
+        LRU order), else least recently used."""
+        order = self._lru(PROTECTED)
+        if self.lfu:
+            return min(order, key=lambda s: self.freq[self.expert_in_slot[s]])
+        return order[0]
+
+    def bump_freq(self, ids: list[int]) -> None:
+        """offloader.py:1993-2007 over this step's selected owned experts."""
+        for g in sorted(set(int(v) for v in ids)):
+            if 0 <= g < self.global_n and self.local_of[g] >= 0:
+                self.freq[self.local_of[g]] += 1
+        self.lfu_steps += 1
+        if self.lfu_steps >= LFU_AGE_STEPS:
+            self.lfu_steps = 0
+            self.freq = [f >> 1 for f in self.freq]
 
     def _acquire(self, loc: int, claimed: set) -> int | None:
         """offloader.py:2036-2074 with allow_protected=True (the gap's call)."""
@@ -150,7 +178,10 @@ class SlotPolicyModel:
                     slot = cand
                     break
             if slot is None:
-                for cand in self._lru(PROTECTED):
+                order = self._lru(PROTECTED)
+                if self.lfu:  # coldest first, LRU order among equals
+                    order = sorted(order, key=lambda s: self.freq[self.expert_in_slot[s]])
+                for cand in order:
                     if cand not in claimed:
                         slot = cand
                         break
@@ -185,6 +216,8 @@ class SlotPolicyModel:
         self.gaps += 1
         ids = [int(g) for g in ids]
         G = self.global_n
+        if self.lfu:
+            self.bump_freq(ids)
         if self.fast_hit and self.map_is_standing:          # 2409-2424
             all_hit = True
             for g in ids:
@@ -237,5 +270,5 @@ class SlotPolicyModel:
             "free": list(self.free_stack),
             "map_is_standing": self.map_is_standing,
             "gaps": self.gaps, "fast_hits": self.fast_hits,
-            "misses": self.misses,
+            "misses": self.misses, "freq": list(self.freq),
         }

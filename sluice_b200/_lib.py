@@ -26,13 +26,14 @@ SL_ERR_NO_SCRATCH = 6
 
 SEG_FREE, SEG_PROBATION, SEG_PROTECTED, SEG_PINNED = 0, 1, 2, 3
 PLAN_FAST_HIT = 1
+PLAN_LFU = 2
 
 # state header words / counters (include/sluice_b200.h)
 HDR = dict(num_slots=0, global_n=1, local_n=2, protected_cap=3, flags=4,
            map_is_standing=5, free_top=6, protected_count=7, clock=8, status=9,
-           fill_count=10, last_misses=11)
+           fill_count=10, last_misses=11, lfu_steps=12)
 CNT = dict(gaps=0, fast_hits=1, misses=2, hits=3, overflows=4, fills=5)
-STATE_NFIELDS = 11
+STATE_NFIELDS = 12
 
 _c = ctypes
 _vp, _i, _sz, _f = _c.c_void_p, _c.c_int, _c.c_size_t, _c.c_float

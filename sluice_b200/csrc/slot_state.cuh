@@ -25,7 +25,8 @@ __host__ __device__ inline void state_layout(int S, int G, int L, size_t* off) {
   off[8] = o; o += round16(size_t(S) * 4);    // free_stack
   off[9] = o; o += round16(size_t(S) * 4);    // fill_local
   off[10] = o; o += round16(size_t(S) * 4);   // fill_slot
-  off[11] = o;
+  off[11] = o; o += round16(size_t(L) * 4);   // freq (LFU counts)
+  off[12] = o;
 }
 
 struct StateView {
@@ -40,10 +41,11 @@ struct StateView {
   int32_t* free_stack;
   int32_t* fill_local;
   int32_t* fill_slot;
+  uint32_t* freq;
 };
 
 __device__ inline StateView view(uint8_t* base, int S, int G, int L) {
-  size_t off[12];
+  size_t off[13];
   state_layout(S, G, L, off);
   StateView v;
   v.hdr = reinterpret_cast<int32_t*>(base + off[0]);
@@ -57,6 +59,7 @@ __device__ inline StateView view(uint8_t* base, int S, int G, int L) {
   v.free_stack = reinterpret_cast<int32_t*>(base + off[8]);
   v.fill_local = reinterpret_cast<int32_t*>(base + off[9]);
   v.fill_slot = reinterpret_cast<int32_t*>(base + off[10]);
+  v.freq = reinterpret_cast<uint32_t*>(base + off[11]);
   return v;
 }
 

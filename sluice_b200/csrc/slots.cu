@@ -4,8 +4,9 @@
 // Reference: kfirtoledo/sluice src/sluice/offloader.py
 //   state      _ExpertLayerCache 121-169, _install_cache 936-1003
 //   gap        _router_split_gap 2362-2467 (FAST_HIT 2409-2424)
-//   policy     _touch 2009-2021, _coldest_protected 2023-2034 (LRU),
+//   policy     _touch 2009-2021, _coldest_protected 2023-2034,
 //              _acquire_slot 2036-2074, _evict_to 2076-2081
+//   LFU        _bump_freq 1993-2007 (SLUICE_LFU; LFU_AGE_STEPS = 256, line 118)
 //   map        _write_map / _write_standing_map 2083-2123
 //   streaming  _stream_in 2709-2723
 //
@@ -24,6 +25,7 @@ namespace {
 constexpr int kMaxSlots = 1024;
 constexpr int kMaxGlobal = 4096;
 constexpr uint32_t kClockRenorm = 0x7fff0000u;
+constexpr int kLfuAgeSteps = 256;  // offloader.py:118
 
 // Planner shared memory, carved at run time from the state's dimensions:
 // the id bitmap, the sorted unique ids, and copies of every state array the
@@ -43,12 +45,13 @@ struct PlanSmem {
   int32_t* free_s;    // [S]
   uint8_t* seg;       // [S]
   uint8_t* claimed;   // [S]
+  uint32_t* sfreq;    // [S] LFU count of each slot's expert
 };
 
 __host__ __device__ inline size_t plan_smem_bytes(int S, int G, int L) {
   const size_t W = (G + 31) / 32;
-  return 16 + 8 * W + 8 * size_t(G) + 4 * size_t(L) + 4 * size_t(S + 1) + 12 * size_t(S) +
-         2 * size_t(S) + 64;
+  return 16 + 8 * W + 8 * size_t(G) + 4 * size_t(L) + 4 * size_t(S + 1) + 16 * size_t(S) +
+         2 * size_t(S) + 80;
 }
 
 __device__ inline PlanSmem plan_smem(uint8_t* base, int S, int G, int L) {
@@ -72,6 +75,7 @@ __device__ inline PlanSmem plan_smem(uint8_t* base, int S, int G, int L) {
   m.free_s = reinterpret_cast<int32_t*>(take(4 * size_t(S)));
   m.seg = take(S);
   m.claimed = take(S);
+  m.sfreq = reinterpret_cast<uint32_t*>(take(4 * size_t(S)));
   return m;
 }
 
@@ -88,6 +92,32 @@ __device__ int warp_lru(const PlanSmem& sm, int S, uint8_t want, bool skip_claim
     }
   }
   const uint32_t m = __reduce_min_sync(0xffffffffu, best);
+  const uint32_t bal = __ballot_sync(0xffffffffu, bslot >= 0 && best == m);
+  if (!bal) return -1;
+  return __shfl_sync(0xffffffffu, bslot, __ffs(bal) - 1);
+}
+
+// Least-frequently-used slot of segment `want`, least recently used among
+// equal counts (the LFU order of offloader.py:2023-2034 / 2056-2066), or -1.
+// Whole warp; the key (count, stamp) is unique among live slots.
+__device__ int warp_lfu(const PlanSmem& sm, int S, uint8_t want, bool skip_claimed) {
+  const int lane = threadIdx.x & 31;
+  unsigned long long best = ~0ull;
+  int bslot = -1;
+  for (int s = lane; s < S; s += 32) {
+    const unsigned long long key =
+        (static_cast<unsigned long long>(sm.sfreq[s]) << 32) | sm.stamp[s];
+    if (sm.seg[s] == want && !(skip_claimed && sm.claimed[s]) && key < best) {
+      best = key;
+      bslot = s;
+    }
+  }
+  unsigned long long m = best;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long v = __shfl_xor_sync(0xffffffffu, m, o);
+    m = v < m ? v : m;
+  }
   const uint32_t bal = __ballot_sync(0xffffffffu, bslot >= 0 && best == m);
   if (!bal) return -1;
   return __shfl_sync(0xffffffffu, bslot, __ffs(bal) - 1);
@@ -132,6 +162,28 @@ __global__ void __launch_bounds__(256) plan_kernel(uint8_t* state,
   __syncthreads();
   const int flags = st.hdr[SL_HDR_FLAGS];
   const int standing = st.hdr[SL_HDR_MAP_IS_STANDING];
+  const bool lfu = (flags & SL_PLAN_LFU) != 0;
+  if (lfu) {
+    // _bump_freq: +1 per selected owned expert (each set bit once), then the
+    // periodic halving; before the FAST_HIT check, like the reference's hook
+    for (int w = tid; w < nwords; w += nthr) {
+      uint32_t bits = sm.bitmap[w];
+      while (bits) {
+        const int g = (w << 5) + __ffs(bits) - 1;
+        bits &= bits - 1;
+        const int loc = sm.local_of[g];
+        if (loc >= 0) st.freq[loc] += 1;
+      }
+    }
+    __syncthreads();
+    const int steps = st.hdr[SL_HDR_LFU_STEPS] + 1;
+    const bool age = steps >= kLfuAgeSteps;
+    if (age)
+      for (int l = tid; l < L; l += nthr) st.freq[l] >>= 1;
+    __syncthreads();
+    if (tid == 0) st.hdr[SL_HDR_LFU_STEPS] = age ? 0 : steps;
+    for (int s = tid; s < S; s += nthr) sm.sfreq[s] = sm.eis[s] >= 0 ? st.freq[sm.eis[s]] : 0;
+  }
   if (tid == 0) {
     st.cnt[SL_CNT_GAPS] += 1;
     st.hdr[SL_HDR_STATUS] = SL_OK;
@@ -227,7 +279,8 @@ __global__ void __launch_bounds__(256) plan_kernel(uint8_t* state,
           ++pcount;
           while (pcount > cap) {
             __syncwarp();
-            const int v = warp_lru(sm, S, SL_SEG_PROTECTED, false);
+            const int v = lfu ? warp_lfu(sm, S, SL_SEG_PROTECTED, false)
+                              : warp_lru(sm, S, SL_SEG_PROTECTED, false);
             ++clock;
             if (lane == 0) {
               sm.seg[v] = SL_SEG_PROBATION;
@@ -254,7 +307,8 @@ __global__ void __launch_bounds__(256) plan_kernel(uint8_t* state,
       } else {
         slot = warp_lru(sm, S, SL_SEG_PROBATION, true);
         if (slot < 0) {
-          slot = warp_lru(sm, S, SL_SEG_PROTECTED, true);
+          slot = lfu ? warp_lfu(sm, S, SL_SEG_PROTECTED, true)
+                     : warp_lru(sm, S, SL_SEG_PROTECTED, true);
           if (slot >= 0) --pcount;
         }
       }
@@ -271,6 +325,7 @@ __global__ void __launch_bounds__(256) plan_kernel(uint8_t* state,
         sm.seg[slot] = SL_SEG_PROBATION;
         sm.stamp[slot] = clock;
         sm.claimed[slot] = 1;
+        if (lfu) sm.sfreq[slot] = st.freq[loc];
         st.fill_local[fc] = loc;
         st.fill_slot[fc] = slot;
       }
@@ -378,15 +433,15 @@ int g_default_stream_ctas = 0;
 
 extern "C" size_t sl_slot_state_bytes(int num_slots, int global_n, int local_n) {
   if (num_slots <= 0 || global_n <= 0 || local_n <= 0) return 0;
-  size_t off[12];
+  size_t off[13];
   state_layout(num_slots, global_n, local_n, off);
-  return off[11];
+  return off[12];
 }
 
 extern "C" int sl_slot_state_offsets(int num_slots, int global_n, int local_n,
                                      size_t* offsets) {
   if (num_slots <= 0 || global_n <= 0 || local_n <= 0 || !offsets) return SL_ERR_INVALID;
-  size_t off[12];
+  size_t off[13];
   state_layout(num_slots, global_n, local_n, off);
   for (int i = 0; i <= SL_STATE_NFIELDS; ++i) offsets[i] = off[i];
   return SL_OK;
@@ -405,9 +460,9 @@ extern "C" int sl_slot_state_init(void* state, int num_slots, int global_n, int 
   if (!local_of || !expert_in_slot || !seg || n_free < 0 || n_free > S ||
       (n_free > 0 && !free_stack) || protected_cap < 0 || protected_cap > S)
     return SL_ERR_INVALID;
-  size_t off[12];
+  size_t off[13];
   state_layout(S, G, L, off);
-  uint8_t* img = static_cast<uint8_t*>(calloc(1, off[11]));
+  uint8_t* img = static_cast<uint8_t*>(calloc(1, off[12]));
   if (!img) return SL_ERR_INVALID;
   int32_t* hdr = reinterpret_cast<int32_t*>(img + off[0]);
   int32_t* lof = reinterpret_cast<int32_t*>(img + off[2]);
@@ -458,7 +513,7 @@ extern "C" int sl_slot_state_init(void* state, int num_slots, int global_n, int 
   hdr[SL_HDR_CLOCK] = static_cast<int32_t>(clock);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   // pageable source: the copy is staged before this call returns
-  cudaError_t e = cudaMemcpyAsync(state, img, off[11], cudaMemcpyHostToDevice, s);
+  cudaError_t e = cudaMemcpyAsync(state, img, off[12], cudaMemcpyHostToDevice, s);
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);
   free(img);
   return e == cudaSuccess ? SL_OK : SL_ERR_CUDA;

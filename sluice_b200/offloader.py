@@ -24,6 +24,7 @@ pointers); a gap rewrites their contents only.
 from __future__ import annotations
 
 import ctypes
+import json
 import os
 import weakref
 from dataclasses import dataclass
@@ -37,6 +38,18 @@ from ._lib import CNT, HDR, SEG_FREE, SEG_PINNED, check, lib, ptr
 PROTECT_FRAC_ENV = "SLUICE_PROTECT_FRAC"
 SLOTS_ENV = "SLUICE_SLOTS"
 FAST_HIT_ENV = "SLUICE_RS_FAST_HIT"
+LFU_ENV = "SLUICE_LFU"
+PIN_FILE_ENV = "SLUICE_PIN_FILE"
+
+
+def load_pin_file(path: str) -> dict:
+    """The static hot-expert pin file (offloader.py:466-483):
+    ``{"layers": {"<MoE layer install ordinal>": [global ids, ...]}}`` (or the
+    bare ``layers`` mapping). Unreadable or malformed files raise."""
+    with open(path) as f:
+        raw = json.load(f)
+    layers = raw.get("layers", raw)
+    return {int(k): [int(g) for g in v] for k, v in layers.items()}
 
 
 def protected_cap_for(num_slots: int, protect_frac: float) -> int:
@@ -221,6 +234,7 @@ class SlotCache:
             "probation": order(_lib.SEG_PROBATION),
             "header": self.header(),
             "counters": self.counters(),
+            "freq": self._field(11, np.uint32, self.local_n).tolist(),
             "fills": list(zip(self._field(9, np.int32, S).tolist(),
                               self._field(10, np.int32, S).tolist()))[: self.header()["fill_count"]],
         }
@@ -237,7 +251,8 @@ class ExpertStreamOffloader:
     """Installs slot caches for MoE layers (``SLUICE_SLOTS`` per layer)."""
 
     def __init__(self, expert_cache_slots: int, protect_frac: float | None = None,
-                 fast_hit: bool | None = None, no_static_full: bool = False):
+                 fast_hit: bool | None = None, no_static_full: bool = False,
+                 lfu: bool | None = None, pin_file: str | None = None):
         if expert_cache_slots <= 0:
             raise ValueError("expert_cache_slots must be positive")
         self.expert_cache_slots = int(expert_cache_slots)
@@ -250,6 +265,14 @@ class ExpertStreamOffloader:
         if fast_hit is None:
             fast_hit = os.environ.get(FAST_HIT_ENV, "1") != "0"
         self.fast_hit = bool(fast_hit)
+        # SLUICE_LFU=1 (offloader.py:242-247): popularity-ordered protected victims
+        if lfu is None:
+            lfu = os.environ.get(LFU_ENV, "0") == "1"
+        self.lfu = bool(lfu)
+        # SLUICE_PIN_FILE: per-layer static pins, applied in install order
+        if pin_file is None:
+            pin_file = os.environ.get(PIN_FILE_ENV) or None
+        self.pin_layers = load_pin_file(pin_file) if pin_file else None
         self.no_static_full = bool(no_static_full)
         self.caches: list[SlotCache] = []
 
@@ -309,6 +332,10 @@ class ExpertStreamOffloader:
                               cpu_store, emap, None, bpe)
             self.caches.append(cache)
             return cache
+        if pins is None and self.pin_layers is not None:
+            # the reference applies the file's list for this install ordinal
+            # to every layer that is not static_full (offloader.py:1025-1026)
+            pins = self.pin_layers.get(len(self.caches), [])
         init = initial_slot_state(S, local_of, local_n, self.protect_frac, pins,
                                   prefill_resident=resident_all if prefill_resident is None
                                   else prefill_resident)
@@ -317,7 +344,7 @@ class ExpertStreamOffloader:
         arr = lambda v, t: (t * len(v))(*v)
         rc = lib().sl_slot_state_init(
             ptr(state), S, global_n, local_n, init.protected_cap,
-            _lib.PLAN_FAST_HIT if self.fast_hit else 0,
+            (_lib.PLAN_FAST_HIT if self.fast_hit else 0) | (_lib.PLAN_LFU if self.lfu else 0),
             arr(local_of, ctypes.c_int32), arr(init.expert_in_slot, ctypes.c_int32),
             arr(init.seg, ctypes.c_uint8), arr(init.free_stack or [0], ctypes.c_int32),
             len(init.free_stack), torch.cuda.current_stream(device).cuda_stream)

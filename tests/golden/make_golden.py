@@ -36,8 +36,10 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 REF = os.environ.get("SLUICE_REFERENCE", "/root/reference")
 
 
-def _ref_offloader(slots: int, fast_hit: bool, frac: float, no_static_full=False):
+def _ref_offloader(slots: int, fast_hit: bool, frac: float, no_static_full=False,
+                   lfu=False):
     os.environ["SLUICE_RS_FAST_HIT"] = "1" if fast_hit else "0"
+    os.environ["SLUICE_LFU"] = "1" if lfu else "0"
     os.environ["SLUICE_PROTECT_FRAC"] = str(frac)
     os.environ["SLUICE_NO_STATIC_FULL"] = "1" if no_static_full else "0"
     os.environ.pop("SLUICE_ROUTER_SPLIT", None)
@@ -85,8 +87,8 @@ def _zipf_ids(gen, steps, T, k, E, s=1.1, locality=0.6):
 
 
 def _run_scenario(name, *, slots, global_n, local_n, owned_lo=0, steps_ids,
-                  fast_hit=True, frac=0.5, pins=None, no_static_full=False):
-    off = _ref_offloader(slots, fast_hit, frac, no_static_full)
+                  fast_hit=True, frac=0.5, pins=None, no_static_full=False, lfu=False):
+    off = _ref_offloader(slots, fast_hit, frac, no_static_full, lfu)
     if pins is not None:
         off._pin_layers = {0: list(pins)}
     if local_n == global_n:
@@ -106,6 +108,13 @@ def _run_scenario(name, *, slots, global_n, local_n, owned_lo=0, steps_ids,
     trace = []
     overflow_step = -1
     for i, ids in enumerate(steps_ids):
+        if lfu:
+            # the popularity counts the reference's hook keeps for every real
+            # step (_bump_freq over the step's selected owned experts), then
+            # the gap's policy reads them
+            pairs = [(g, local_of[g], True) for g in sorted(set(ids))
+                     if 0 <= g < global_n and local_of[g] >= 0]
+            off._bump_freq(cache, pairs)
         try:
             off._router_split_gap(0, torch.tensor(ids, dtype=torch.int32))
         except RuntimeError:
@@ -121,12 +130,13 @@ def _run_scenario(name, *, slots, global_n, local_n, owned_lo=0, steps_ids,
             "map_is_standing": bool(cache.map_is_standing),
             "gaps": off._rs_gaps, "misses": off._rs_misses,
             "fast_hits": off._rs_fast_hits,
+            "freq": [int(cache.freq.get(loc, 0)) for loc in range(local_n)],
         })
         if overflow_step >= 0:
             break
     return {
         "name": name, "num_slots": cache.num_slots, "global_n": global_n,
-        "local_n": local_n, "local_of": local_of, "fast_hit": fast_hit,
+        "local_n": local_n, "local_of": local_of, "fast_hit": fast_hit, "lfu": lfu,
         "protect_frac": frac, "protected_cap": cache.protected_cap,
         "pins": list(pins) if pins is not None else None,
         "pinned_slots": sorted(cache.pinned_slots),
@@ -149,6 +159,7 @@ def make_slot_traces():
         ids[7] = 64 + (len(noisy) % 5)
         noisy.append(ids)
     big = [torch.randperm(64, generator=g)[:48].tolist() for _ in range(12)]
+    lfu_long = _zipf_ids(torch.Generator().manual_seed(4321), 300, 8, 6, 64, locality=0.3)
     exact = [torch.randperm(64, generator=g)[:48].tolist() for _ in range(12)]
     sc = [
         _run_scenario("v2lite_zipf_fasthit", slots=48, global_n=64, local_n=64,
@@ -177,6 +188,16 @@ def make_slot_traces():
                       steps_ids=exact),
         _run_scenario("prefill_resident", slots=64, global_n=64, local_n=64,
                       steps_ids=uni[:8], no_static_full=True),
+        # LFU hybrid: frequency-ordered protected victims; 300 steps cross one
+        # halving of the counts (every 256 steps)
+        _run_scenario("v2lite_lfu_aging", slots=48, global_n=64, local_n=64,
+                      steps_ids=lfu_long, lfu=True),
+        _run_scenario("v2lite_lfu_uniform_frac09", slots=48, global_n=64, local_n=64,
+                      steps_ids=uni, frac=0.9, lfu=True),
+        _run_scenario("v2lite_lfu_pins_nofasthit", slots=40, global_n=64, local_n=64,
+                      steps_ids=zipf, pins=[3, 17, 40], fast_hit=False, lfu=True),
+        _run_scenario("v3_ep4_rank2_lfu", slots=48, global_n=256, local_n=64,
+                      owned_lo=128, steps_ids=v3, lfu=True),
     ]
     with open(os.path.join(HERE, "slot_traces.json"), "w") as f:
         json.dump({"generator": "tests/golden/make_golden.py",

@@ -86,3 +86,38 @@ def test_initial_state_matches_oracle(sc):
         [s for s in range(m.num_slots) if m.seg[s] == PINNED]
     if sc["pins"]:
         assert sorted(s for _, s in init.fills) == sc["pinned_slots"]
+
+
+def test_pin_file_formats(tmp_path):
+    """SLUICE_PIN_FILE: {"layers": {ordinal: ids}} or the bare mapping;
+    malformed files fail loudly (the reference refuses a silent empty pin)."""
+    import json
+
+    import pytest as _pytest
+
+    from sluice_b200.offloader import load_pin_file
+
+    a = tmp_path / "a.json"
+    a.write_text(json.dumps({"layers": {"0": [3, 5], "2": ["7"]}}))
+    assert load_pin_file(str(a)) == {0: [3, 5], 2: [7]}
+    b = tmp_path / "b.json"
+    b.write_text(json.dumps({"1": [9]}))
+    assert load_pin_file(str(b)) == {1: [9]}
+    c = tmp_path / "c.json"
+    c.write_text("{not json")
+    with _pytest.raises(ValueError):
+        load_pin_file(str(c))
+    with _pytest.raises(OSError):
+        load_pin_file(str(tmp_path / "missing.json"))
+
+
+def test_lfu_changes_victims_only_when_counts_differ():
+    """Oracle: with every count equal the LFU order is the LRU order, so an
+    LFU cache fed one expert per step behaves exactly like the plain SLRU."""
+    from oracle.slot_policy import SlotPolicyModel
+
+    lru = SlotPolicyModel(4, list(range(16)), 16)
+    lfu = SlotPolicyModel(4, list(range(16)), 16, lfu=True)
+    for g in [0, 1, 2, 3, 4, 5, 6, 7, 8, 9]:
+        assert lru.gap([g]) == lfu.gap([g])
+        assert lru.snapshot()["expert_in_slot"] == lfu.snapshot()["expert_in_slot"]

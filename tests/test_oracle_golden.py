@@ -28,7 +28,7 @@ def _scenarios():
 def model_for(sc) -> SlotPolicyModel:
     m = SlotPolicyModel(sc["num_slots"], sc["local_of"], sc["local_n"],
                         protect_frac=sc["protect_frac"], fast_hit=sc["fast_hit"],
-                        prefill_resident=sc["prefill_resident"])
+                        prefill_resident=sc["prefill_resident"], lfu=sc.get("lfu", False))
     if sc["pins"]:
         m.apply_pins(sc["pins"])
     return m
@@ -61,6 +61,8 @@ def test_slot_policy_matches_reference_trace(sc):
         live = [payload[s] if m.expert_in_slot[s] >= 0 else -1
                 for s in range(m.num_slots)]
         assert live == exp["slot_payload"], (sc["name"], i)
+        if sc.get("lfu"):
+            assert m.freq == exp["freq"], (sc["name"], i)
 
 
 def test_golden_covers_edge_cases():
@@ -68,6 +70,8 @@ def test_golden_covers_edge_cases():
     assert names["overflow_s40"]["overflow_step"] >= 1
     assert names["prefill_resident"]["prefill_resident"]
     assert names["v2lite_pins"]["pinned_slots"]
+    aging = names["v2lite_lfu_aging"]
+    assert aging["lfu"] and len(aging["trace"]) > 256  # crosses one halving
     assert any(g < 0 or g >= 64 for st in names["v2lite_invalid_ids"]["steps"] for g in st)
     assert names["ep_rank1_of2"]["local_n"] < names["ep_rank1_of2"]["global_n"]
 

@@ -31,18 +31,34 @@ def _payload_params(local_n):
     return w13, w2
 
 
-def _install(sc):
+def _install(sc, pin_file=None):
     off = ExpertStreamOffloader(sc["num_slots"], protect_frac=sc["protect_frac"],
                                 fast_hit=sc["fast_hit"],
-                                no_static_full=sc["prefill_resident"])
+                                no_static_full=sc["prefill_resident"],
+                                lfu=sc.get("lfu", False), pin_file=pin_file)
     w13, w2 = _payload_params(sc["local_n"])
     return off.install_layer(w13, w2, global_n=sc["global_n"], local_of=sc["local_of"],
-                             pins=sc["pins"], device="cuda")
+                             pins=None if pin_file else sc["pins"], device="cuda")
+
+
+def _pin_file_cases():
+    """Scenarios with pins, replayed with the pins given as a SLUICE_PIN_FILE."""
+    return [s for s in _scenarios() if s["pins"]]
 
 
 @pytest.mark.parametrize("sc", _scenarios(), ids=lambda s: s["name"])
 def test_planner_matches_reference_trace(sc):
-    cache = _install(sc)
+    _check_trace(sc, _install(sc))
+
+
+@pytest.mark.parametrize("sc", _pin_file_cases(), ids=lambda s: s["name"])
+def test_pin_file_matches_reference_trace(sc, tmp_path):
+    path = tmp_path / "pins.json"
+    path.write_text(json.dumps({"layers": {"0": sc["pins"]}}))
+    _check_trace(sc, _install(sc, pin_file=str(path)))
+
+
+def _check_trace(sc, cache):
     assert cache.protected_cap == sc["protected_cap"]
     for i, (ids, exp) in enumerate(zip(sc["steps"], sc["trace"])):
         t = torch.tensor(ids, dtype=torch.int32, device="cuda")
@@ -69,6 +85,8 @@ def test_planner_matches_reference_trace(sc):
         for s, loc in enumerate(exp["slot_payload"]):
             if loc >= 0:
                 assert w13[s] == loc and w2[s] == -loc - 1, (sc["name"], i, s)
+        if sc.get("lfu"):
+            assert snap["freq"] == exp["freq"], (sc["name"], i)
 
 
 def test_planner_long_random_run_matches_oracle():
