@@ -571,9 +571,13 @@ def run_sluice(a):
 
     local_n = cfg.num_experts // world
     offloaded = a.slots < local_n
-    # per layer: gate, select, [plan, stream,] align, gate/up GEMM, down GEMM, combine
-    # (+ dispatch and combine kernels under the NVLink exchange)
-    per_layer = (8 if offloaded else 6) + (2 if world > 1 and a.exchange == "nvlink" else 0)
+    # per layer: gate, select, [plan, stream,] align, gate/up GEMM, down GEMM,
+    # combine; the overlapped gap runs both GEMMs twice (resident experts, then
+    # the streamed ones); + dispatch and combine kernels under the NVLink exchange
+    # fp8 weights add the quantising token gather
+    per_layer = (6 if not offloaded else 10 if not a.no_overlap else 8) + \
+        (2 if world > 1 and a.exchange == "nvlink" else 0) + \
+        (1 if cfg.weight_dtype == "fp8" else 0)
     launches = K * layers * per_layer
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,

@@ -57,12 +57,16 @@ __host__ __device__ inline size_t r256(size_t v) { return (v + 255) & ~size_t(25
 // tokens per expert) use 16, prefill-sized steps 64 or 128 so each weight
 // tile is reused across more tokens.
 // fp8 stops at 64: its gate/up accumulators (128 token columns x gate and up)
-// would not fit the promotion warps' registers.
+// would not fit the promotion warps' registers. fp8 keeps 16-token tiles up
+// to 32 tokens per expert on average: a 64-token tile would promote (and
+// multiply) four times the columns it uses, while a second 16-token item of
+// the same expert re-reads its weights mostly from L2.
 inline int choose_bn(int T, int topk, int S, bool fp8 = false) {
   const long P = static_cast<long>(T) * topk;
   const long used = P < S ? P : S;
   const long avg = used > 0 ? (P + used - 1) / used : 1;
-  return avg <= 16 ? 16 : (avg <= 64 || fp8) ? 64 : 128;
+  if (fp8) return avg <= 32 ? 16 : 64;
+  return avg <= 16 ? 16 : avg <= 64 ? 64 : 128;
 }
 
 // SLUICE_FUSED=1 runs bf16 decode steps through the single persistent kernel
