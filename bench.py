@@ -772,7 +772,8 @@ def run_reference(a):
         return
     cfg = configs.CONFIGS[a.config]
     layers = a.layers or cfg.num_moe_layers
-    T = a.tokens
+    # the same global batch as the GPU arm: c tokens per GPU on N GPUs
+    T = a.tokens * world
     torch.set_num_threads(os.cpu_count() or 1)
     t_step, n = cpu_step_time(cfg, a.slots, T, layers, a.seed, steps=a.steps,
                               warmup=max(1, min(a.warmup, 2)), budget_s=150.0)
