@@ -210,3 +210,27 @@ print("ok")
     r = subprocess.run([sys.executable, "-c", code.format(root=root, tests=os.path.dirname(
         os.path.abspath(__file__)))], env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
+
+
+def test_empty_step_and_oversized_slot_count():
+    """T = 0 returns an empty output without launching work; more slots plus
+    shared experts than the grouping step handles (1056) is refused with an
+    error instead of running."""
+    from sluice_b200 import _lib
+    H, I = 256, 128
+    w13 = torch.zeros(4, 2 * I, H, dtype=torch.bfloat16, device="cuda")
+    w2 = torch.zeros(4, H, I, dtype=torch.bfloat16, device="cuda")
+    hs = torch.empty(0, H, dtype=torch.bfloat16, device="cuda")
+    tw = torch.empty(0, 2, dtype=torch.float32, device="cuda")
+    ti = torch.empty(0, 2, dtype=torch.int32, device="cuda")
+    out = ops.fused_experts(hs, w13, w2, tw, ti, global_num_experts=4)
+    assert out.shape == (0, H)
+    S = 1100
+    w13b = torch.zeros(S, 2 * I, H, dtype=torch.bfloat16, device="cuda")
+    w2b = torch.zeros(S, H, I, dtype=torch.bfloat16, device="cuda")
+    hs = torch.randn(2, H, device="cuda").to(torch.bfloat16)
+    tw = torch.ones(2, 2, device="cuda")
+    ti = torch.zeros(2, 2, dtype=torch.int32, device="cuda")
+    with pytest.raises(_lib.SluiceError) as ei:
+        ops.fused_experts(hs, w13b, w2b, tw, ti, global_num_experts=S)
+    assert ei.value.status == _lib.SL_ERR_UNSUPPORTED

@@ -154,3 +154,20 @@ def test_gap_op_is_registered_and_returns_a_clone():
     assert torch.equal(out, hs) and out.data_ptr() != hs.data_ptr()
     m = cache.expert_map.cpu().tolist()
     assert m[1] >= 0 and m[2] >= 0 and m[3] >= 0 and sum(v >= 0 for v in m) == 3
+
+
+def test_empty_step_changes_nothing_but_the_gap_count():
+    """A gap over zero ids (an empty decode batch) touches no slot."""
+    sc = {"num_slots": 8, "protect_frac": 0.5, "fast_hit": True, "prefill_resident": False,
+          "local_n": 16, "global_n": 16, "local_of": list(range(16)), "pins": None}
+    cache = _install(sc)
+    m = SlotPolicyModel(8, list(range(16)), 16, 0.5, True)
+    for ids in ([1, 2, 3], [], [4, 1], [], []):
+        cache.gap(torch.tensor(ids, dtype=torch.int32, device="cuda"))
+        m.gap(ids)
+        snap = cache.snapshot()
+        assert snap["expert_map"] == m.expert_map
+        assert snap["protected"] == m.segment_order(PROTECTED)
+        assert snap["probation"] == m.segment_order(PROBATION)
+        c = snap["counters"]
+        assert (c["gaps"], c["misses"], c["fast_hits"]) == (m.gaps, m.misses, m.fast_hits)
