@@ -269,20 +269,24 @@ int sl_fused_experts_partial(const void* hidden, int T, int H, int I,
  * Receive buffers hold two halves used alternately (sized by the _bytes
  * queries). All ranks must make the same sequence of calls; every wait on a
  * peer is bounded (SL_ERR_TIMEOUT in *status).
- * dispatch: rows = this rank's [T, 2H + 8*topk] packed (hidden bf16 | weights
- *   f32 | ids i32); outputs every rank's rows unpacked: x_out bf16
+ * dispatch: this rank's hidden bf16 [T, H] (16-byte aligned), top-k weights
+ *   f32 [T, topk] and ids i32 [T, topk] (topk even) travel packed as rows of
+ *   2H + 8*topk bytes; outputs every rank's rows, unpacked: x_out bf16
  *   [world*T, H], w_out [world*T, topk], id_out [world*T, topk].
  * combine: partial fp32 [world*T, H] (this rank's experts over every rank's
- *   tokens); out = bf16(sum over ranks, rank order) for this rank's T tokens. */
+ *   tokens); out = bf16(sum over ranks, rank order) for this rank's T tokens,
+ *   or bf16(residual + that) when residual (bf16 [T, H]) is not NULL: the
+ *   decoder's residual add folded in. */
 size_t sl_ep_dispatch_recv_bytes(int world, int T, int H, int topk);
 size_t sl_ep_combine_recv_bytes(int world, int T, int H);
-int sl_ep_dispatch(const void* rows, int T, int H, int topk, int rank, int world,
+int sl_ep_dispatch(const void* hidden, const float* topk_weights, const int32_t* topk_ids,
+                   int T, int H, int topk, int rank, int world,
                    void* const* peer_recv, void* const* peer_signal, void* book,
                    void* x_out, float* w_out, int32_t* id_out, int32_t* status,
                    sl_stream_t stream);
 int sl_ep_combine(const float* partial, int T, int H, int rank, int world,
                   void* const* peer_recv, void* const* peer_signal, void* book,
-                  void* out, int32_t* status, sl_stream_t stream);
+                  const void* residual, void* out, int32_t* status, sl_stream_t stream);
 
 /* sl_fused_experts without any device allocation. No counterpart in the
  * reference: it serves callers that cannot allocate device scratch memory for

@@ -84,8 +84,29 @@ __device__ void wait_peers(const uint32_t* my_signal, int channel, uint32_t epoc
   if (timed_out && threadIdx.x == 0) atomicExch(status, SL_ERR_TIMEOUT);
 }
 
+// One 16-byte vector of this rank's packed row r (hidden bf16 | top-k weights
+// f32 | top-k ids i32), read from the three inputs: the hidden part is whole
+// vectors; the weight / id tail is assembled word by word (4*topk need not be
+// a multiple of 16).
+__device__ __forceinline__ uint4 packed_vec(const __nv_bfloat16* __restrict__ x,
+                                            const float* __restrict__ tw,
+                                            const int32_t* __restrict__ ti, int r, int c,
+                                            int H, int topk) {
+  const int vec_x = H / 8;
+  if (c < vec_x) return reinterpret_cast<const uint4*>(x + static_cast<size_t>(r) * H)[c];
+  uint32_t w[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int word = (c - vec_x) * 4 + j;  // 4-byte word within the tail
+    w[j] = word < topk ? __float_as_uint(tw[static_cast<size_t>(r) * topk + word])
+                       : static_cast<uint32_t>(ti[static_cast<size_t>(r) * topk + word - topk]);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
 __global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(
-    const uint8_t* __restrict__ rows, int T, int row_bytes, EpPeers peers,
+    const __nv_bfloat16* __restrict__ x, const float* __restrict__ tw,
+    const int32_t* __restrict__ ti, int T, int row_bytes, EpPeers peers,
     const uint32_t* my_signal, const uint8_t* my_recv,  // written by peers: no .nc loads
     uint32_t* __restrict__ book, int rank, int world, __nv_bfloat16* __restrict__ x_out,
     float* __restrict__ w_out, int32_t* __restrict__ id_out, int H, int topk,
@@ -94,17 +115,17 @@ __global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(
   const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(&book[EP_DONE_DISPATCH]) / kEpCtas + 1;
   const size_t half = static_cast<size_t>(world) * T * row_bytes;
   const size_t base = (epoch & 1u) * half + static_cast<size_t>(rank) * T * row_bytes;
-  const int nvec = T * row_bytes / 16;
-  const uint4* src = reinterpret_cast<const uint4*>(rows);
-  for (int q = 0; q < world; ++q) {
-    if (q == rank) continue;  // own rows are read from `rows`
-    uint4* dst = reinterpret_cast<uint4*>(peers.recv[q] + base);
-    for (int v = blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += gridDim.x * blockDim.x)
-      dst[v] = src[v];
+  const int rvec = row_bytes / 16;
+  const int nvec = T * rvec;
+  // pack this rank's rows straight into every peer's receive half
+  for (int v = blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += gridDim.x * blockDim.x) {
+    const uint4 val = packed_vec(x, tw, ti, v / rvec, v % rvec, H, topk);
+    for (int q = 0; q < world; ++q)
+      if (q != rank) reinterpret_cast<uint4*>(peers.recv[q] + base)[v] = val;
   }
   signal_peers(peers, book, EP_DONE_DISPATCH, 0, epoch, rank, world);
   wait_peers(my_signal, 0, epoch, rank, world, status);
-  // own rows were pushed by every CTA of this grid: read them from `rows`
+  // every rank's rows, this rank's own straight from its inputs
   const uint8_t* half_base = my_recv + (epoch & 1u) * half;
   const int xb = 2 * H, wb = 4 * topk;
   const int n_rows = world * T;
@@ -113,18 +134,23 @@ __global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(
        i += gridDim.x * blockDim.x) {
     const int r = i / vec_x, c = i % vec_x;
     const int src_rank = r / T;
-    const uint8_t* row = src_rank == rank ? rows + static_cast<size_t>(r % T) * row_bytes
-                                          : half_base + static_cast<size_t>(r) * row_bytes;
-    reinterpret_cast<uint4*>(x_out)[i] = reinterpret_cast<const uint4*>(row)[c];
+    reinterpret_cast<uint4*>(x_out)[i] =
+        src_rank == rank
+            ? reinterpret_cast<const uint4*>(x + static_cast<size_t>(r % T) * H)[c]
+            : reinterpret_cast<const uint4*>(half_base + static_cast<size_t>(r) * row_bytes)[c];
   }
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_rows * topk;
        i += gridDim.x * blockDim.x) {
     const int r = i / topk, j = i % topk;
     const int src_rank = r / T;
-    const uint8_t* row = src_rank == rank ? rows + static_cast<size_t>(r % T) * row_bytes
-                                          : half_base + static_cast<size_t>(r) * row_bytes;
-    w_out[i] = reinterpret_cast<const float*>(row + xb)[j];
-    id_out[i] = reinterpret_cast<const int32_t*>(row + xb + wb)[j];
+    if (src_rank == rank) {
+      w_out[i] = tw[static_cast<size_t>(r % T) * topk + j];
+      id_out[i] = ti[static_cast<size_t>(r % T) * topk + j];
+    } else {
+      const uint8_t* row = half_base + static_cast<size_t>(r) * row_bytes;
+      w_out[i] = reinterpret_cast<const float*>(row + xb)[j];
+      id_out[i] = reinterpret_cast<const int32_t*>(row + xb + wb)[j];
+    }
   }
   sl::pdl_trigger();
 }
@@ -132,7 +158,8 @@ __global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(
 __global__ void __launch_bounds__(kEpThreads) ep_combine_kernel(
     const float* __restrict__ partial, int T, int H, EpPeers peers,
     const uint32_t* my_signal, const uint8_t* my_recv,  // written by peers: no .nc loads
-    uint32_t* __restrict__ book, int rank, int world, __nv_bfloat16* __restrict__ out,
+    uint32_t* __restrict__ book, int rank, int world,
+    const __nv_bfloat16* __restrict__ residual, __nv_bfloat16* __restrict__ out,
     int32_t* __restrict__ status) {
   sl::pdl_wait();
   const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(&book[EP_DONE_COMBINE]) / kEpCtas + 1;
@@ -162,8 +189,18 @@ __global__ void __launch_bounds__(kEpThreads) ep_combine_kernel(
       acc.w += v.w;
     }
     __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(out) + 2 * i;
-    o[0] = __floats2bfloat162_rn(acc.x, acc.y);
-    o[1] = __floats2bfloat162_rn(acc.z, acc.w);
+    __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y);
+    __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z, acc.w);
+    if (residual != nullptr) {
+      // the decoder's residual add: bf16(h + bf16(moe)), as a bf16 tensor add
+      const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(residual) + 2 * i;
+      const float2 a = __bfloat1622float2(lo), b = __bfloat1622float2(hi);
+      const float2 ra = __bfloat1622float2(r2[0]), rb = __bfloat1622float2(r2[1]);
+      lo = __floats2bfloat162_rn(ra.x + a.x, ra.y + a.y);
+      hi = __floats2bfloat162_rn(rb.x + b.x, rb.y + b.y);
+    }
+    o[0] = lo;
+    o[1] = hi;
   }
   sl::pdl_trigger();
 }
@@ -190,21 +227,24 @@ extern "C" size_t sl_ep_combine_recv_bytes(int world, int T, int H) {
   return 2ull * world * T * H * 4ull;
 }
 
-extern "C" int sl_ep_dispatch(const void* rows, int T, int H, int topk, int rank, int world,
-                              void* const* peer_recv, void* const* peer_signal,
+extern "C" int sl_ep_dispatch(const void* hidden, const float* topk_weights,
+                              const int32_t* topk_ids, int T, int H, int topk, int rank,
+                              int world, void* const* peer_recv, void* const* peer_signal,
                               void* book, void* x_out, float* w_out, int32_t* id_out,
                               int32_t* status, sl_stream_t stream) {
   EpPeers peers;
   int rc = fill_peers(&peers, world, peer_recv, peer_signal);
   if (rc != SL_OK) return rc;
-  if (!rows || !book || !x_out || !w_out || !id_out || !status || rank < 0 || rank >= world ||
-      T <= 0 || H % 8 || topk <= 0)
+  if (!hidden || !topk_weights || !topk_ids || !book || !x_out || !w_out || !id_out ||
+      !status || rank < 0 || rank >= world || T <= 0 || H % 8 || topk <= 0 ||
+      ((reinterpret_cast<uintptr_t>(hidden) | reinterpret_cast<uintptr_t>(x_out)) & 15))
     return SL_ERR_INVALID;
   const int row_bytes = 2 * H + 8 * topk;
   if (row_bytes % 16) return SL_ERR_UNSUPPORTED;
   SL_CUDA_TRY(sl::launch(ep_dispatch_kernel, dim3(kEpCtas), dim3(kEpThreads), 0,
                          reinterpret_cast<cudaStream_t>(stream),
-                         static_cast<const uint8_t*>(rows), T, row_bytes, peers,
+                         static_cast<const __nv_bfloat16*>(hidden), topk_weights, topk_ids, T,
+                         row_bytes, peers,
                          static_cast<const uint32_t*>(peer_signal[rank]),
                          static_cast<const uint8_t*>(peer_recv[rank]),
                          static_cast<uint32_t*>(book), rank, world,
@@ -214,7 +254,8 @@ extern "C" int sl_ep_dispatch(const void* rows, int T, int H, int topk, int rank
 
 extern "C" int sl_ep_combine(const float* partial, int T, int H, int rank, int world,
                              void* const* peer_recv, void* const* peer_signal, void* book,
-                             void* out, int32_t* status, sl_stream_t stream) {
+                             const void* residual, void* out, int32_t* status,
+                             sl_stream_t stream) {
   EpPeers peers;
   int rc = fill_peers(&peers, world, peer_recv, peer_signal);
   if (rc != SL_OK) return rc;
@@ -225,6 +266,7 @@ extern "C" int sl_ep_combine(const float* partial, int T, int H, int rank, int w
                          static_cast<const uint32_t*>(peer_signal[rank]),
                          static_cast<const uint8_t*>(peer_recv[rank]),
                          static_cast<uint32_t*>(book), rank, world,
+                         static_cast<const __nv_bfloat16*>(residual),
                          static_cast<__nv_bfloat16*>(out), status));
   return SL_OK;
 }

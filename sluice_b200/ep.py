@@ -121,18 +121,23 @@ class NvlinkExchange:
         if T > self.max_tokens:
             raise ValueError(f"{T} tokens exceed the exchange's {self.max_tokens}")
         k = tw.shape[1]
-        packed = pack_routing(x, tw, ti)
+        x = x.contiguous()
+        tw = tw.contiguous().float()
+        ti = ti.contiguous().to(torch.int32)
         n = self.world * T
         xg = torch.empty(n, H, dtype=torch.bfloat16, device=x.device)
         twg = torch.empty(n, k, dtype=torch.float32, device=x.device)
         tig = torch.empty(n, k, dtype=torch.int32, device=x.device)
-        check(lib().sl_ep_dispatch(ptr(packed), T, H, k, self.rank, self.world, self._recv_d,
-                                   self._sig, ptr(self.book), ptr(xg), ptr(twg), ptr(tig),
-                                   ptr(self.status), torch.cuda.current_stream().cuda_stream),
-              "sl_ep_dispatch")
+        # the kernel packs (hidden | weights | ids) rows itself while pushing
+        check(lib().sl_ep_dispatch(ptr(x), ptr(tw), ptr(ti), T, H, k, self.rank, self.world,
+                                   self._recv_d, self._sig, ptr(self.book), ptr(xg), ptr(twg),
+                                   ptr(tig), ptr(self.status),
+                                   torch.cuda.current_stream().cuda_stream), "sl_ep_dispatch")
         return xg, twg, tig
 
-    def combine(self, partial: torch.Tensor) -> torch.Tensor:
+    def combine(self, partial: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
+        """This rank's rows of the summed partials in bf16; with ``residual``
+        (bf16 [T, H]) the result is ``residual + that``, as a bf16 add."""
         from ._lib import check, lib, ptr
 
         n, H = partial.shape
@@ -140,9 +145,12 @@ class NvlinkExchange:
         if T > self.max_tokens:
             raise ValueError(f"{T} tokens exceed the exchange's {self.max_tokens}")
         out = torch.empty(T, H, dtype=torch.bfloat16, device=partial.device)
+        if residual is not None:
+            residual = residual.contiguous()
         check(lib().sl_ep_combine(ptr(partial), T, H, self.rank, self.world, self._recv_c,
-                                  self._sig, ptr(self.book), ptr(out), ptr(self.status),
-                                  torch.cuda.current_stream().cuda_stream), "sl_ep_combine")
+                                  self._sig, ptr(self.book), ptr(residual), ptr(out),
+                                  ptr(self.status), torch.cuda.current_stream().cuda_stream),
+              "sl_ep_combine")
         return out
 
     def check(self) -> None:
@@ -177,7 +185,10 @@ class EPMoELayer:
         self.stream_ctas = stream_ctas
         self._side = torch.cuda.Stream(device=cache.device) if self.overlap else None
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, add_residual: bool = False) -> torch.Tensor:
+        """This rank's MoE output for its tokens ``x``; ``add_residual``
+        returns ``x + output`` (the decoder's residual add; folded into the
+        combine kernel under the NVLink exchange)."""
         T = x.shape[0]
         tw, ti, _ = self.router.route(x)
         if self.exchange is not None:
@@ -211,8 +222,9 @@ class EPMoELayer:
             c.gap(tig)
             part = ops.fused_experts_partial(*args, **kw)
         if self.exchange is not None:
-            return self.exchange.combine(part)
-        return combine(part, self.group).to(torch.bfloat16)
+            return self.exchange.combine(part, x if add_residual else None)
+        out = combine(part, self.group).to(torch.bfloat16)
+        return x + out if add_residual else out
 
     __call__ = forward
 
@@ -260,7 +272,7 @@ class EPDecodeStack:
     def step(self, x: torch.Tensor) -> torch.Tensor:
         h = x
         for layer in self.layers:
-            h = h + layer(h)
+            h = layer(h, add_residual=True)  # h + moe(h)
         return h
 
     def capture(self, tokens: int) -> bool:

@@ -56,10 +56,11 @@ def test_dispatch_pushes_signals_and_unpacks():
         xo = torch.empty(2 * T, H, dtype=torch.bfloat16, device="cuda")
         wo = torch.empty(2 * T, K, dtype=torch.float32, device="cuda")
         io = torch.empty(2 * T, K, dtype=torch.int32, device="cuda")
-        packed = pack_routing(x0, tw0, ti0)
-        _lib.check(L.sl_ep_dispatch(packed.data_ptr(), T, H, K, 0, 2, recv, sig,
-                                    book.data_ptr(), xo.data_ptr(), wo.data_ptr(),
-                                    io.data_ptr(), status.data_ptr(), stream), "dispatch")
+        packed = pack_routing(x0, tw0, ti0)  # what the kernel must push
+        _lib.check(L.sl_ep_dispatch(x0.data_ptr(), tw0.data_ptr(), ti0.data_ptr(), T, H, K, 0,
+                                    2, recv, sig, book.data_ptr(), xo.data_ptr(),
+                                    wo.data_ptr(), io.data_ptr(), status.data_ptr(), stream),
+                   "dispatch")
         torch.cuda.synchronize()
         assert status.item() == _lib.SL_OK
         assert torch.equal(xo, torch.cat([x0, x1]))
@@ -83,18 +84,22 @@ def test_combine_sums_in_rank_order():
     slot = T * H * 4
     stream = torch.cuda.current_stream().cuda_stream
     g = torch.Generator().manual_seed(5)
-    for epoch in (1, 2):
+    for epoch in (1, 2, 3):
         part = torch.randn(2 * T, H, generator=g).cuda()
         from_peer = torch.randn(T, H, generator=g).cuda()
         h = (epoch & 1) * 2 * slot
         mine[h + slot:h + 2 * slot] = from_peer.view(torch.uint8).view(-1)
         my_sig[1 * 8 + 1] = epoch
         out = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+        # the third call folds in the decoder's residual add
+        res = torch.randn(T, H, generator=g).to(torch.bfloat16).cuda() if epoch == 3 else None
         _lib.check(L.sl_ep_combine(part.data_ptr(), T, H, 0, 2, recv, sig, book.data_ptr(),
-                                   out.data_ptr(), status.data_ptr(), stream), "combine")
+                                   None if res is None else res.data_ptr(), out.data_ptr(),
+                                   status.data_ptr(), stream), "combine")
         torch.cuda.synchronize()
         assert status.item() == _lib.SL_OK
-        assert torch.equal(out, (part[:T] + from_peer).to(torch.bfloat16))
+        moe = (part[:T] + from_peer).to(torch.bfloat16)
+        assert torch.equal(out, moe if res is None else res + moe)
         assert torch.equal(peer[h:h + slot], part[T:].contiguous().view(torch.uint8).view(-1))
         assert peer_sig[8].item() == epoch
         assert book[1].item() == 8 * epoch
@@ -111,8 +116,7 @@ def test_wait_on_silent_peer_times_out():
     xo = torch.empty(2 * T, H, dtype=torch.bfloat16, device="cuda")
     wo = torch.empty(2 * T, K, dtype=torch.float32, device="cuda")
     io = torch.empty(2 * T, K, dtype=torch.int32, device="cuda")
-    packed = pack_routing(x0, tw0, ti0)
-    _lib.check(L.sl_ep_dispatch(packed.data_ptr(), T, H, K, 0, 2,
+    _lib.check(L.sl_ep_dispatch(x0.data_ptr(), tw0.data_ptr(), ti0.data_ptr(), T, H, K, 0, 2,
                                 _vp(mine.data_ptr(), peer.data_ptr()),
                                 _vp(my_sig.data_ptr(), peer_sig.data_ptr()), book.data_ptr(),
                                 xo.data_ptr(), wo.data_ptr(), io.data_ptr(), status.data_ptr(),
@@ -130,8 +134,13 @@ def test_exchange_rejects_bad_arguments():
     p = z.data_ptr()
     s = torch.cuda.current_stream().cuda_stream
     recv = _vp(p, p)
-    assert L.sl_ep_dispatch(p, T, H, K, 2, 2, recv, recv, p, p, p, p, p, s) == _lib.SL_ERR_INVALID
-    assert L.sl_ep_dispatch(p, T, H, K, 0, 9, recv, recv, p, p, p, p, p, s) == _lib.SL_ERR_INVALID
-    assert L.sl_ep_dispatch(p, T, 100, 3, 0, 2, recv, recv, p, p, p, p, p, s) \
+    d = lambda *a: L.sl_ep_dispatch(p, p, p, *a)
+    assert d(T, H, K, 2, 2, recv, recv, p, p, p, p, p, s) == _lib.SL_ERR_INVALID
+    assert d(T, H, K, 0, 9, recv, recv, p, p, p, p, p, s) == _lib.SL_ERR_INVALID
+    assert d(T, 100, 3, 0, 2, recv, recv, p, p, p, p, p, s) \
         in (_lib.SL_ERR_INVALID, _lib.SL_ERR_UNSUPPORTED)
-    assert L.sl_ep_combine(p, T, H, 0, 2, _vp(p, None), recv, p, p, p, s) == _lib.SL_ERR_INVALID
+    assert d(T, H, 3, 0, 2, recv, recv, p, p, p, p, p, s) == _lib.SL_ERR_UNSUPPORTED  # odd topk
+    assert L.sl_ep_dispatch(p + 4, p, p, T, H, K, 0, 2, recv, recv, p, p, p, p, p, s) \
+        == _lib.SL_ERR_INVALID  # hidden rows not 16-byte aligned
+    assert L.sl_ep_combine(p, T, H, 0, 2, _vp(p, None), recv, p, None, p, p, s) \
+        == _lib.SL_ERR_INVALID
