@@ -8,6 +8,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <utility>
 
 #include "../../include/sluice_b200.h"
@@ -251,6 +252,21 @@ __device__ __forceinline__ void pdl_trigger() {
 }
 
 bool pdl_enabled();
+
+// Raise a kernel's dynamic shared-memory limit once per device (the bit of
+// each device that has it set lives in `done`, one per kernel instance);
+// safe when threads on different devices launch at the same time.
+template <typename Kernel>
+cudaError_t ensure_smem_limit(Kernel kernel, int bytes, std::atomic<uint64_t>& done) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = dev < 64 ? (1ull << dev) : 0;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_acq_rel);
+  return e;
+}
 
 // Launch with programmatic stream serialisation (PDL) when enabled.
 template <typename... KArgs, typename... Args>

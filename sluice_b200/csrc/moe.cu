@@ -1700,14 +1700,8 @@ int launch_gemm_f8(const CUtensorMap& tw, const CUtensorMap& twsh, const CUtenso
                    int32_t* status, int max_items, cudaStream_t st, int phase) {
   using Cfg = F8Cfg<BN, GATED>;
   auto kern = moe_gemm_f8_kernel<BN, GATED>;
-  static int configured_dev = -1;
-  int dev = 0;
-  SL_CUDA_TRY(cudaGetDevice(&dev));
-  if (configured_dev != dev) {
-    SL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     Cfg::kSmemBytes));
-    configured_dev = dev;
-  }
+  static std::atomic<uint64_t> smem_set{0};
+  SL_CUDA_TRY(sl::ensure_smem_limit(kern, Cfg::kSmemBytes, smem_set));
   const int max_tiles = max_items * (M_total / 128);
   int grid = sl_device_sm_count();
   if (grid <= 0) return SL_ERR_CUDA;
@@ -1728,14 +1722,8 @@ int launch_fused(const CUtensorMap& w13, const CUtensorMap& w13sh, const CUtenso
                  cudaStream_t st) {
   using Cfg = GemmCfg<BN, STAGES, true>;
   auto kern = moe_fused_kernel<BN, STAGES, OUT_F32>;
-  static int configured_dev = -1;
-  int dev = 0;
-  SL_CUDA_TRY(cudaGetDevice(&dev));
-  if (configured_dev != dev) {
-    SL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     Cfg::kSmemBytes));
-    configured_dev = dev;
-  }
+  static std::atomic<uint64_t> smem_set{0};
+  SL_CUDA_TRY(sl::ensure_smem_limit(kern, Cfg::kSmemBytes, smem_set));
   const long max_tiles = static_cast<long>(max_items) * (I / 64 + H / 128);
   int grid = sl_device_sm_count();
   if (grid <= 0) return SL_ERR_CUDA;
@@ -1764,14 +1752,8 @@ int launch_gemm(const CUtensorMap& tw, const CUtensorMap& twsh, const CUtensorMa
                 int phase) {
   using Cfg = GemmCfg<BN, STAGES, GATED>;
   auto kern = moe_gemm_kernel<BN, STAGES, GATED>;
-  static int configured_dev = -1;
-  int dev = 0;
-  SL_CUDA_TRY(cudaGetDevice(&dev));
-  if (configured_dev != dev) {
-    SL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     Cfg::kSmemBytes));
-    configured_dev = dev;
-  }
+  static std::atomic<uint64_t> smem_set{0};
+  SL_CUDA_TRY(sl::ensure_smem_limit(kern, Cfg::kSmemBytes, smem_set));
   const int max_tiles = max_items * (M_total / TileShape<BN, GATED>::kRowsOut);
   int grid = sl_device_sm_count();
   if (grid <= 0) return SL_ERR_CUDA;

@@ -522,14 +522,8 @@ extern "C" int sl_slot_state_init(void* state, int num_slots, int global_n, int 
 extern "C" int sl_plan_slots(void* state, const int32_t* topk_ids, int num_ids,
                              int32_t* expert_map, sl_stream_t stream) {
   if (!state || !expert_map || num_ids < 0 || (num_ids > 0 && !topk_ids)) return SL_ERR_INVALID;
-  static int configured_dev = -1;
-  int dev = 0;
-  SL_CUDA_TRY(cudaGetDevice(&dev));
-  if (configured_dev != dev) {
-    SL_CUDA_TRY(cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     kPlanSmemBytes));
-    configured_dev = dev;
-  }
+  static std::atomic<uint64_t> smem_set{0};
+  SL_CUDA_TRY(sl::ensure_smem_limit(plan_kernel, kPlanSmemBytes, smem_set));
   SL_CUDA_TRY(sl::launch(plan_kernel, dim3(1), dim3(256), kPlanSmemBytes,
                          reinterpret_cast<cudaStream_t>(stream), static_cast<uint8_t*>(state),
                          topk_ids, num_ids, expert_map));
