@@ -26,7 +26,10 @@ here follow vLLM 0.22:
   output) are quantised per token and 128-column group the way
   ``per_token_group_quant_fp8`` does ([vLLM] ``quantization/utils/fp8_utils.py``
   ``_per_token_group_quant_fp8``, 95-150: scale = max(amax, 1e-10) * (1/448),
-  ``q = clamp(x / scale, -448, 448)`` to e4m3); products of the dequantised
+  ``q = clamp(x / scale, -448, 448)`` to e4m3; vLLM's compiled CUDA op and
+  its torch-native ``QuantFP8._quantize_group_native`` compute the same
+  scale as ``amax / 448``, which can differ from this one in the last bit);
+  products of the dequantised
   operands accumulate in fp32, each GEMM output rounds to bf16.
 """
 
