@@ -47,15 +47,24 @@ def silu_and_mul(x: torch.Tensor) -> torch.Tensor:
 FP8_MAX = 448.0
 
 
-def quant_dequant_group_fp8(x: torch.Tensor, group: int = 128) -> torch.Tensor:
-    """Activations through vLLM's per-token-group e4m3 quantisation, returned
-    dequantised in fp32 (q * scale)."""
+def quant_group_fp8(x: torch.Tensor, group: int = 128):
+    """vLLM's per-token-group e4m3 quantisation: (q e4m3 [..., K], scale fp32
+    [..., K/group])."""
     *lead, K = x.shape
     g = x.float().reshape(*lead, K // group, group)
     amax = g.abs().amax(dim=-1, keepdim=True).clamp(min=1e-10)
     scale = amax * (1.0 / FP8_MAX)
     q = (g / scale).clamp(-FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn)
-    return (q.float() * scale).reshape(*lead, K)
+    return q.reshape(*lead, K), scale.reshape(*lead, K // group)
+
+
+def quant_dequant_group_fp8(x: torch.Tensor, group: int = 128) -> torch.Tensor:
+    """Activations through vLLM's per-token-group e4m3 quantisation, returned
+    dequantised in fp32 (q * scale)."""
+    *lead, K = x.shape
+    q, scale = quant_group_fp8(x, group)
+    g = q.float().reshape(*lead, K // group, group) * scale.unsqueeze(-1)
+    return g.reshape(*lead, K)
 
 
 def expert_mlp(x: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor,

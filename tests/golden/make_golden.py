@@ -17,6 +17,8 @@ It writes:
   DeepSeek-V3 routing modes.
 * ``moe.npz`` — a small ``fused_experts`` case through an expert map,
   evaluated by vLLM's ``cpu_fused_moe_torch`` (``cpu_fused_moe.py`` 428-482).
+* ``fp8_quant.npz`` — bf16 activations through vLLM's torch-native
+  per-token-group fp8 quantisation (``QuantFP8._quantize_group_native``).
 
 Nothing at test time reads the reference; the tests read these files.
 """
@@ -237,6 +239,25 @@ def make_routing():
     print("routing:", sorted(k for k in out if k.endswith("_ids")))
 
 
+def make_fp8_quant():
+    """``fp8_quant.npz``: activations through vLLM's torch-native per-token
+    group quantisation (``QuantFP8._quantize_group_native``,
+    ``layers/quantization/input_quant_fp8.py``; group 128, dynamic scales),
+    the CPU-runnable twin of the CUDA op its fp8 MoE path calls."""
+    import types
+
+    from vllm.model_executor.layers.quantization.input_quant_fp8 import QuantFP8
+
+    self_ = types.SimpleNamespace(group_size=128, use_ue8m0=False, column_major_scales=False)
+    g = torch.Generator().manual_seed(2468)
+    x = (torch.randn(96, 2048, generator=g) * torch.rand(96, 1, generator=g) * 4
+         ).to(torch.bfloat16)
+    xq, s = QuantFP8._quantize_group_native(self_, x)
+    np.savez_compressed(os.path.join(HERE, "fp8_quant.npz"),
+                        x=x.float().numpy(), q=xq.view(torch.uint8).numpy(),
+                        scale=s.float().numpy())
+
+
 def make_moe():
     from vllm.model_executor.layers.activation import SiluAndMul
     from vllm.model_executor.layers.fused_moe import cpu_fused_moe as cfm
@@ -282,3 +303,4 @@ if __name__ == "__main__":
     make_slot_traces()
     make_routing()
     make_moe()
+    make_fp8_quant()

@@ -154,3 +154,23 @@ def test_fp8_dequant_block_scale():
     d = omoe.dequant_block_fp8(w, s)
     assert torch.equal(d[:128, :128], w[:128, :128].float() * s[0, 0])
     assert torch.equal(d[128:, 256:], w[128:, 256:].float() * s[1, 2])
+
+
+def test_fp8_group_quant_matches_vllm():
+    """The oracle's per-token-group e4m3 quantisation against vLLM's own
+    (torch-native twin of its CUDA op): scales agree to one fp32 ulp (vLLM
+    divides amax by 448, the Triton path and this oracle multiply by 1/448),
+    and the e4m3 codes agree except where that ulp moves a value across a
+    rounding boundary."""
+    z = np.load(os.path.join(GOLDEN, "fp8_quant.npz"))
+    x = torch.from_numpy(z["x"]).to(torch.bfloat16)
+    q, scale = omoe.quant_group_fp8(x)
+    ref_s = torch.from_numpy(z["scale"])
+    assert ((scale - ref_s).abs() / ref_s).max().item() <= 2.4e-7
+    ref_q = torch.from_numpy(z["q"]).view(torch.float8_e4m3fn).float()
+    flips = (q.float() != ref_q)
+    assert flips.float().mean().item() < 5e-3
+    # a flip is one e4m3 step: at most 1/8 relative to the larger neighbour
+    d = (q.float() - ref_q).abs()[flips]
+    m = torch.maximum(q.float().abs(), ref_q.abs())[flips]
+    assert (d <= m / 8 + 1e-6).all()
