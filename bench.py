@@ -310,6 +310,10 @@ def profile_layers(stack, x):
                                           expert_map=layer.cache.expert_map,
                                           shared_w13=layer.shared_w13,
                                           shared_w2=layer.shared_w2,
+                                          w1_scale=layer.cache.w13_scale,
+                                          w2_scale=layer.cache.w2_scale,
+                                          shared_w13_scale=layer.shared_w13_scale,
+                                          shared_w2_scale=layer.shared_w2_scale,
                                           routed_scaling_factor=cfg.routed_scaling_factor,
                                           out=out)
         fused_ms.append(_graph_time_ms(fused))
@@ -540,7 +544,11 @@ def run_sluice(a):
 
     # resident comparison: same kernels, every expert in HBM (slots = E)
     resident = None
-    if not a.no_resident and world == 1:
+    resident_bytes = layers * (cfg.num_experts + cfg.n_shared) * cfg.bytes_per_expert
+    fits = resident_bytes < 0.8 * torch.cuda.mem_get_info()[1]
+    if not a.no_resident and world == 1 and not fits:
+        resident = {"skipped": f"{resident_bytes / 1e9:.0f} GB of experts do not fit one GPU"}
+    if not a.no_resident and world == 1 and fits:
         del stack
         torch.cuda.empty_cache()
         rs = MoEDecodeStack(cfg, slots=cfg.num_experts, seed=a.seed, num_layers=layers)
