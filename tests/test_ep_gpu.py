@@ -67,6 +67,77 @@ def _rank_main(rank, world, port, out_dir, exchange, slots=48):
         dist.destroy_process_group()
 
 
+def _v3_mini():
+    """A DeepSeek-V3-style layer at test size: fp8 e4m3 experts with 128x128
+    block scales, sigmoid scoring with score bias, 8 groups / top-4 groups,
+    top-8 with renormalisation, routed scaling 2.5, one shared expert."""
+    from sluice_b200 import configs
+    return configs.MoEConfig(
+        name="v3-mini", hidden=1024, num_experts=64, moe_intermediate=256, n_shared=1,
+        num_moe_layers=1, routed_scaling_factor=2.5, weight_dtype="fp8",
+        routing=configs.RoutingConfig(topk=8, renormalize=True, scoring_func="sigmoid",
+                                      num_expert_group=8, topk_group=4,
+                                      use_grouped_topk=True, has_score_bias=True))
+
+
+def _rank_main_fp8(rank, world, port, out_dir):
+    import torch.distributed as dist
+
+    from oracle import moe as omoe
+    from oracle import routing as orouting
+    from sluice_b200 import ep, synth
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port),
+                      NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    stack = None
+    try:
+        cfg = _v3_mini()
+        stack = ep.EPDecodeStack(cfg, slots=48, seed=4, num_layers=1)
+        layer = stack.layers[0]
+        prm = {k: v.cpu() for k, v in synth.layer_params(cfg, 0, 4, device="cuda").items()}
+        sh = {k: v.cpu() for k, v in synth.shared_params(cfg, 0, 4, device="cuda").items()}
+        _, _, sb = synth.gate_params(cfg, 0, 4, device="cpu")
+        tokens = synth.TokenStream(cfg.hidden, 8, seed=60 + rank)
+        rc = cfg.routing
+        errs = []
+        for _ in range(3):
+            x = tokens.next().cuda()
+            out = layer(x)
+            tw, ti, logits = layer.router.route(x)
+            torch.cuda.synchronize()
+            xc = x.cpu()
+            otw, oti = orouting.grouped_topk(logits.cpu(), rc.topk, rc.renormalize,
+                                             rc.num_expert_group, rc.topk_group,
+                                             rc.scoring_func, 1.0, sb)
+            routed = omoe.fused_experts(xc, prm["w13"], prm["w2"], otw, oti, None,
+                                        prm["w13_scale"], prm["w2_scale"])
+            shared = omoe.shared_experts(xc, sh["shared_w13"][0], sh["shared_w2"][0],
+                                         sh["shared_w13_scale"][0], sh["shared_w2_scale"][0])
+            ref = omoe.layer_output(routed, shared, cfg.routed_scaling_factor).float()
+            got = out.float().cpu()
+            errs.append(((got - ref).abs().max() / ref.abs().max()).item())
+        stack.check()
+        torch.save(torch.tensor(errs), os.path.join(out_dir, f"errf{rank}.pt"))
+    finally:
+        if stack is not None:
+            stack.release()
+        dist.destroy_process_group()
+
+
+def test_ep2_fp8_v3_style_layer_matches_oracle(tmp_path):
+    """fp8 block-scaled experts, sigmoid grouped routing and routed scaling
+    under expert parallelism (NVLink exchange): within the fp8 tolerance."""
+    mp.start_processes(_rank_main_fp8, args=(2, _free_port(), str(tmp_path)), nprocs=2,
+                       start_method="spawn")
+    for r in range(2):
+        errs = torch.load(os.path.join(tmp_path, f"errf{r}.pt"))
+        assert (errs < 5e-2).all(), errs
+
+
 def _agree_main(rank, world, port, out_dir):
     import torch.distributed as dist
 
