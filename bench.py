@@ -343,12 +343,12 @@ def stream_probe(stack, n_miss=12, ctas=(16, 32, 64, 128, 148)):
     cache.gap(ids)
     torch.cuda.synchronize()
     fills = cache.header()["fill_count"]
-    n, src, dst, nb = cache._stream_args
+    n, src, dst, nb, hs = cache._stream_args
     out = {}
     for c in ctas:
-        s = lambda: check(lib().sl_stream_experts(ptr(cache.state), n, src, dst, nb, c,
-                                                  torch.cuda.current_stream().cuda_stream),
-                          "stream")
+        s = lambda: check(lib().sl_stream_experts_strided(
+            ptr(cache.state), n, src, dst, nb, hs, c, torch.cuda.current_stream().cuda_stream),
+            "stream")
         ms = _graph_time_ms(s, reps=5)
         out[c] = fills * cache.bytes_per_expert / (ms * 1e-3) / 1e9
     return {"fills": fills, "gbs_by_ctas": out}

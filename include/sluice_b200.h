@@ -148,6 +148,18 @@ int sl_stream_experts(const void* state, int num_params,
                       const size_t* bytes_per_expert, int num_ctas,
                       sl_stream_t stream);
 
+/* The same for a host store whose experts are not packed per parameter:
+ * expert `local` of parameter p starts at host_src[p] + local *
+ * host_stride_bytes[p] (a multiple of 16, >= bytes_per_expert[p]). With one
+ * packed record per expert ([w13 | w2 | scales], record-sized strides) every
+ * fill reads one contiguous host range: the layout a checkpoint loader can
+ * fill directly. */
+int sl_stream_experts_strided(const void* state, int num_params,
+                              const void* const* host_src, void* const* slot_dst,
+                              const size_t* bytes_per_expert,
+                              const size_t* host_stride_bytes, int num_ctas,
+                              sl_stream_t stream);
+
 /* Page-locked host memory mapped into the device address space
  * (cudaHostAlloc Mapped|Portable): the host store of offloaded experts
  * (replaces cpu.pin_memory(), offloader.py:965-967). */

@@ -64,6 +64,7 @@ _SIGNATURES = {
                                 _vp]),
     "sl_plan_slots": (_i, [_vp, _vp, _i, _vp, _vp]),
     "sl_stream_experts": (_i, [_vp, _i, _vp, _vp, _vp, _i, _vp]),
+    "sl_stream_experts_strided": (_i, [_vp, _i, _vp, _vp, _vp, _vp, _i, _vp]),
     "sl_host_alloc_mapped": (_i, [_sz, _c.POINTER(_vp)]),
     "sl_host_free": (_i, [_vp]),
     "sl_fused_experts_workspace_bytes": (_sz, [_i, _i, _i, _i, _i, _i]),

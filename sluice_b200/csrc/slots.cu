@@ -378,6 +378,7 @@ struct StreamArgs {
   uint4* dst[kMaxParams];
   unsigned long long vec[kMaxParams];     // 16-byte vectors per expert
   unsigned long long chunks[kMaxParams];  // work units per expert
+  unsigned long long src_stride[kMaxParams];  // vectors between experts in the host store
 };
 
 __device__ __forceinline__ uint4 ld_host_nc(const uint4* p) {
@@ -409,7 +410,8 @@ __global__ void __launch_bounds__(kStreamThreads) stream_kernel(const uint8_t* s
     }
     const unsigned long long v0 = r * kChunkVec;
     const unsigned long long nvec = min(static_cast<unsigned long long>(kChunkVec), a.vec[p] - v0);
-    const uint4* src = a.src[p] + static_cast<unsigned long long>(st.fill_local[f]) * a.vec[p] + v0;
+    const uint4* src =
+        a.src[p] + static_cast<unsigned long long>(st.fill_local[f]) * a.src_stride[p] + v0;
     uint4* dst = a.dst[p] + static_cast<unsigned long long>(st.fill_slot[f]) * a.vec[p] + v0;
     for (unsigned long long base = 0; base < nvec; base += kStreamThreads * kStreamUnroll) {
       uint4 v[kStreamUnroll];
@@ -530,10 +532,11 @@ extern "C" int sl_plan_slots(void* state, const int32_t* topk_ids, int num_ids,
   return SL_OK;
 }
 
-extern "C" int sl_stream_experts(const void* state, int num_params,
-                                 const void* const* host_src, void* const* slot_dst,
-                                 const size_t* bytes_per_expert, int num_ctas,
-                                 sl_stream_t stream) {
+extern "C" int sl_stream_experts_strided(const void* state, int num_params,
+                                         const void* const* host_src, void* const* slot_dst,
+                                         const size_t* bytes_per_expert,
+                                         const size_t* host_stride_bytes, int num_ctas,
+                                         sl_stream_t stream) {
   if (!state || num_params <= 0 || num_params > kMaxParams || !host_src || !slot_dst ||
       !bytes_per_expert)
     return SL_ERR_INVALID;
@@ -549,6 +552,9 @@ extern "C" int sl_stream_experts(const void* state, int num_params,
     a.dst[p] = static_cast<uint4*>(slot_dst[p]);
     a.vec[p] = b / 16;
     a.chunks[p] = (a.vec[p] + kChunkVec - 1) / kChunkVec;
+    const size_t stride = host_stride_bytes ? host_stride_bytes[p] : b;
+    if (stride < b || (stride & 15)) return SL_ERR_INVALID;
+    a.src_stride[p] = stride / 16;
   }
   if (num_ctas <= 0) {
     if (g_default_stream_ctas <= 0) g_default_stream_ctas = 64;
@@ -558,6 +564,14 @@ extern "C" int sl_stream_experts(const void* state, int num_params,
                          reinterpret_cast<cudaStream_t>(stream),
                          static_cast<const uint8_t*>(state), a));
   return SL_OK;
+}
+
+extern "C" int sl_stream_experts(const void* state, int num_params,
+                                 const void* const* host_src, void* const* slot_dst,
+                                 const size_t* bytes_per_expert, int num_ctas,
+                                 sl_stream_t stream) {
+  return sl_stream_experts_strided(state, num_params, host_src, slot_dst, bytes_per_expert,
+                                   nullptr, num_ctas, stream);
 }
 
 extern "C" int sl_host_alloc_mapped(size_t bytes, void** host_ptr) {

@@ -159,7 +159,11 @@ class SlotCache:
             dst = (ctypes.c_void_p * n)(*[gpu_cache[k].data_ptr() for k in names])
             nb = (ctypes.c_size_t * n)(*[cpu_store[k][0].numel() * cpu_store[k].element_size()
                                          for k in names])
-            self._stream_args = (n, src, dst, nb)
+            # bytes between consecutive experts of each parameter in the host
+            # store: the parameter's size, or the record size of a packed store
+            hs = (ctypes.c_size_t * n)(*[cpu_store[k].stride(0) * cpu_store[k].element_size()
+                                         for k in names])
+            self._stream_args = (n, src, dst, nb, hs)
 
     @property
     def w13(self) -> torch.Tensor:
@@ -194,10 +198,11 @@ class SlotCache:
 
     def stream(self, stream_ctas: int = 0) -> None:
         """Stream the last plan's fills on the current stream."""
-        n, src, dst, nb = self._stream_args
-        check(lib().sl_stream_experts(ptr(self.state), n, src, dst, nb, int(stream_ctas),
-                                      torch.cuda.current_stream().cuda_stream),
-              "sl_stream_experts")
+        n, src, dst, nb, hs = self._stream_args
+        check(lib().sl_stream_experts_strided(ptr(self.state), n, src, dst, nb, hs,
+                                              int(stream_ctas),
+                                              torch.cuda.current_stream().cuda_stream),
+              "sl_stream_experts_strided")
 
     # -- host-side views (synchronise) ----------------------------------------
     def _field(self, i: int, dtype, count: int) -> np.ndarray:
@@ -252,7 +257,8 @@ class ExpertStreamOffloader:
 
     def __init__(self, expert_cache_slots: int, protect_frac: float | None = None,
                  fast_hit: bool | None = None, no_static_full: bool = False,
-                 lfu: bool | None = None, pin_file: str | None = None):
+                 lfu: bool | None = None, pin_file: str | None = None,
+                 packed_host_store: bool = False):
         if expert_cache_slots <= 0:
             raise ValueError("expert_cache_slots must be positive")
         self.expert_cache_slots = int(expert_cache_slots)
@@ -274,6 +280,9 @@ class ExpertStreamOffloader:
             pin_file = os.environ.get(PIN_FILE_ENV) or None
         self.pin_layers = load_pin_file(pin_file) if pin_file else None
         self.no_static_full = bool(no_static_full)
+        # one host record per expert ([w13 | w2 | scales]) instead of one
+        # host array per parameter: each fill reads one contiguous range
+        self.packed_host_store = bool(packed_host_store)
         self.caches: list[SlotCache] = []
 
     @classmethod
@@ -313,11 +322,27 @@ class ExpertStreamOffloader:
             params["w2_scale"] = w2_scale.float().contiguous()
         gpu_cache, cpu_store = {}, {}
         bpe = 0
+        sizes = {name: p[0].numel() * p.element_size() for name, p in params.items()}
+        packed = (self.packed_host_store and not static_full and
+                  all(b % 16 == 0 for b in sizes.values()))
+        record = sum(sizes.values())
+        pstore = HostStore(local_n * record) if packed else None
+        offset = 0
         for name, p in params.items():
             gpu_cache[name] = torch.empty((S, *p.shape[1:]), dtype=p.dtype, device=device)
-            bpe += p[0].numel() * p.element_size()
+            bpe += sizes[name]
             if static_full:
                 gpu_cache[name].copy_(p)
+            elif packed:
+                # parameter `name` of expert l at byte l * record + offset
+                es = p.element_size()
+                inner = torch.empty(p.shape[1:], dtype=p.dtype, device="meta").stride()
+                t = torch.as_strided(pstore.bytes.view(p.dtype), (local_n, *p.shape[1:]),
+                                     (record // es, *inner), offset // es)
+                t.copy_(p)
+                t._sluice_store = pstore  # keep the allocation alive with the view
+                cpu_store[name] = t
+                offset += sizes[name]
             else:
                 store = HostStore(p.numel() * p.element_size())
                 t = store.view(p.dtype, p.shape)

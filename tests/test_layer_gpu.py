@@ -100,7 +100,8 @@ def test_decode_step_host_round_trip():
     assert out.shape == ref.shape
 
 
-def test_fp8_v3_routing_layer_with_streaming():
+@pytest.mark.parametrize("packed", [False, True], ids=["per-param-store", "packed-store"])
+def test_fp8_v3_routing_layer_with_streaming(packed):
     """DeepSeek-V3-style layer at reduced size: sigmoid + score bias, 8 groups /
     top-4 groups, top-8, renormalised, routed scaling 2.5, fp8 e4m3 experts
     with 128x128 block scales streamed (weights and scales) into 16 slots."""
@@ -114,7 +115,7 @@ def test_fp8_v3_routing_layer_with_streaming():
     sh13, sh2 = synth.shared_weights(cfg, 0, seed=9, device="cuda")
     qs13, ss13 = synth.quantize_block_fp8(sh13)
     qs2, ss2 = synth.quantize_block_fp8(sh2)
-    off = ExpertStreamOffloader(16, protect_frac=0.5, fast_hit=True)
+    off = ExpertStreamOffloader(16, protect_frac=0.5, fast_hit=True, packed_host_store=packed)
     cache = off.install_layer(q13, q2, device="cuda", w13_scale=s13, w2_scale=s2)
     layer = SluiceMoELayer(cfg, ops.Router(cfg.routing, gw, lb, sb), cache, qs13, qs2,
                            shared_w13_scale=ss13, shared_w2_scale=ss2)

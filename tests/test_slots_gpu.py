@@ -31,11 +31,12 @@ def _payload_params(local_n):
     return w13, w2
 
 
-def _install(sc, pin_file=None):
+def _install(sc, pin_file=None, packed=False):
     off = ExpertStreamOffloader(sc["num_slots"], protect_frac=sc["protect_frac"],
                                 fast_hit=sc["fast_hit"],
                                 no_static_full=sc["prefill_resident"],
-                                lfu=sc.get("lfu", False), pin_file=pin_file)
+                                lfu=sc.get("lfu", False), pin_file=pin_file,
+                                packed_host_store=packed)
     w13, w2 = _payload_params(sc["local_n"])
     return off.install_layer(w13, w2, global_n=sc["global_n"], local_of=sc["local_of"],
                              pins=None if pin_file else sc["pins"], device="cuda")
@@ -56,6 +57,14 @@ def test_pin_file_matches_reference_trace(sc, tmp_path):
     path = tmp_path / "pins.json"
     path.write_text(json.dumps({"layers": {"0": sc["pins"]}}))
     _check_trace(sc, _install(sc, pin_file=str(path)))
+
+
+@pytest.mark.parametrize("name", ["v2lite_zipf_fasthit", "v3_ep4_rank2"])
+def test_packed_host_store_streams_the_same_contents(name):
+    """One host record per expert ([w13 | w2]) instead of one host array per
+    parameter: same plan, same slot contents after every streamed fill."""
+    sc = next(s for s in _scenarios() if s["name"] == name)
+    _check_trace(sc, _install(sc, packed=True))
 
 
 def _check_trace(sc, cache):
