@@ -185,10 +185,28 @@ class EPMoELayer:
         self.stream_ctas = stream_ctas
         self._side = torch.cuda.Stream(device=cache.device) if self.overlap else None
 
+    @property
+    def envelope(self) -> int:
+        """This rank's tokens per single-wave step: the gap plans over every
+        rank's gathered tokens, so the reference's ``slots // topk`` envelope
+        (``offloader.py:816-842``) is split across the world; a fully
+        resident shard has none."""
+        if self.cache.static_full:
+            return 1 << 30
+        return max(1, self.cache.num_slots // self.cfg.routing.topk // self.world)
+
     def forward(self, x: torch.Tensor, add_residual: bool = False) -> torch.Tensor:
         """This rank's MoE output for its tokens ``x``; ``add_residual``
         returns ``x + output`` (the decoder's residual add; folded into the
-        combine kernel under the NVLink exchange)."""
+        combine kernel under the NVLink exchange). Steps larger than the
+        envelope run as envelope-sized chunks (every rank the same number:
+        every rank steps the same token count)."""
+        thr = self.envelope
+        if x.shape[0] > thr:
+            return torch.cat([self._forward_step(c, add_residual) for c in x.split(thr)])
+        return self._forward_step(x, add_residual)
+
+    def _forward_step(self, x: torch.Tensor, add_residual: bool) -> torch.Tensor:
         T = x.shape[0]
         tw, ti, _ = self.router.route(x)
         if self.exchange is not None:
