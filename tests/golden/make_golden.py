@@ -35,7 +35,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("SLUICE_REFERENCE", "/root/reference")
+REF = os.environ.get("SLUICE_REFERENCE", "")
 
 
 def _ref_offloader(slots: int, fast_hit: bool, frac: float, no_static_full=False,
@@ -299,6 +299,8 @@ def make_moe():
 
 
 if __name__ == "__main__":
+    if not REF:
+        raise SystemExit("set SLUICE_REFERENCE to a checkout of kfirtoledo/sluice")
     sys.path.insert(0, os.path.join(REF, "src"))
     make_slot_traces()
     make_routing()

@@ -2,7 +2,7 @@
 
 Tolerance (bf16): |out - ref| <= 2e-2 * max|ref| + 2e-2 * |ref| elementwise,
 the north star's 2e-2 relative, scaled by the output's magnitude so that
-near-zero entries are not judged on their own relative error.
+near-zero entries are not held to their own relative error.
 """
 
 import os
