@@ -214,6 +214,11 @@ def cpu_layer_runner(cfg, seed, n_weight_sets=2):
     policies = {}
 
     def run_layer(li, x, slots):
+        # steps beyond the envelope (slots // topk tokens) run as chunks, as
+        # the GPU layer does
+        env = max(1, min(slots, cfg.num_experts) // rc.topk)
+        if slots < cfg.num_experts and x.shape[0] > env:
+            return torch.cat([run_layer(li, c, slots) for c in x.split(env)])
         w13, w2, gw, lb, sb, sh = sets[li % n_weight_sets]
         logits = orouting.gate_logits(x, gw, lb)
         tw, ti = orouting.grouped_topk(logits, rc.topk, rc.renormalize, rc.num_expert_group,
