@@ -121,3 +121,23 @@ def test_lfu_changes_victims_only_when_counts_differ():
     for g in [0, 1, 2, 3, 4, 5, 6, 7, 8, 9]:
         assert lru.gap([g]) == lfu.gap([g])
         assert lru.snapshot()["expert_in_slot"] == lfu.snapshot()["expert_in_slot"]
+
+
+def test_reference_arm_runs_the_global_batch(monkeypatch, capsys):
+    """`bench.py --impl reference` under torchrun at N=2: rank 0 times the CPU
+    port on the GPU arm's global batch (c x N tokens, beyond the slot
+    envelope, so in envelope-sized chunks) and prints one JSON line."""
+    import json
+    import os
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, root)
+    import bench
+
+    monkeypatch.setenv("RANK", "0")
+    monkeypatch.setenv("WORLD_SIZE", "2")
+    bench.main(["--impl", "reference", "--steps", "1", "--warmup", "1", "--layers", "2"])
+    line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and line["n_gpus"] == 2
+    assert line["config"]["tokens_per_step"] == 16 and line["value"] > 0
