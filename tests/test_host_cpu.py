@@ -57,6 +57,23 @@ def test_host_calls_reject_bad_arguments_without_a_gpu():
                               0, None, None, 0, 1.0, None, None, 0, None) == _lib.SL_ERR_UNSUPPORTED
     assert L.sl_plan_slots(None, None, 0, None, None) == _lib.SL_ERR_INVALID
     assert L.sl_stream_experts(None, 0, None, None, None, 0, None) == _lib.SL_ERR_INVALID
+    assert L.sl_stream_experts_strided(None, 0, None, None, None, None, 0,
+                                       None) == _lib.SL_ERR_INVALID
+    # expert-parallel exchange: sizes, and world / rank / shape checks
+    assert L.sl_ep_dispatch_recv_bytes(2, 8, 2048, 6) == 2 * 2 * 8 * (2 * 2048 + 8 * 6)
+    assert L.sl_ep_combine_recv_bytes(2, 8, 2048) == 2 * 2 * 8 * 2048 * 4
+    assert L.sl_ep_dispatch_recv_bytes(0, 8, 2048, 6) == 0
+    assert L.sl_ep_dispatch(None, None, None, 8, 2048, 6, 0, 9, None, None, None, None,
+                            None, None, None, None) == _lib.SL_ERR_INVALID
+    assert L.sl_ep_combine(None, 8, 2048, 0, 0, None, None, None, None, None, None,
+                           None) == _lib.SL_ERR_INVALID
+    # fp8 through the general entry without weights or block scales: refused
+    # before anything is dereferenced
+    w = _lib.ExpertWeights()
+    w.num_slots, w.dtype = 8, 1  # SL_WEIGHTS_FP8_BLOCK128
+    assert L.sl_fused_experts_ex(None, 4, 2048, 1408, ctypes.byref(w), None, None, 2, None, 0,
+                                 1.0, 0, -1, None, -1, 0, None, None, 0, None) \
+        == _lib.SL_ERR_INVALID
 
 
 @pytest.mark.parametrize("S,frac", [(48, 0.5), (48, 0.0), (48, 0.95), (1, 0.5), (96, 0.9)])
