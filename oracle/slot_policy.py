@@ -16,7 +16,13 @@ cache that kfirtoledo/sluice keeps in ``src/sluice/offloader.py``:
   256 steps, offloader.py:118) and the frequency-ordered protected victims of
   ``_coldest_protected`` / ``_acquire_slot`` (ties in LRU order);
 * maps: ``_write_map`` / ``_write_standing_map`` (2083-2123);
-* the gap body: ``_router_split_gap`` (2362-2467), FAST_HIT on or off.
+* the gap body: ``_router_split_gap`` (2362-2467), FAST_HIT on or off;
+* steps beyond the envelope: the classic hook's planning, ``run_moe``
+  (1452-1764: decode / scan classification, touches, wave 0) and
+  ``_run_waves`` (1846-1933: the remaining misses rotate through the
+  probation slots in ping-pong groups, one expert wave per group), with the
+  reference's default switches (hook-lite, prefill blocks, lazy modes and the
+  non-MLA classifier off).
 
 Recency is kept as a per-slot stamp from one per-layer clock instead of
 ordered dictionaries: a segment's LRU order is its slots sorted by stamp, and
@@ -86,6 +92,10 @@ class SlotPolicyModel:
         self.fast_hits = 0
         self.misses = 0
         self.bytes_streamed = 0
+        self.scan_steps = 0     # classic-hook steps (run_moe) and their waves
+        self.scan_hits = 0
+        self.scan_misses = 0
+        self.scan_waves = 0
         if prefill_resident:
             # offloader.py:992-1003: every local expert preloaded into slot ==
             # local index, outside both SLRU segments; extra slots stay free.
@@ -167,8 +177,9 @@ class SlotPolicyModel:
             self.lfu_steps = 0
             self.freq = [f >> 1 for f in self.freq]
 
-    def _acquire(self, loc: int, claimed: set) -> int | None:
-        """offloader.py:2036-2074 with allow_protected=True (the gap's call)."""
+    def _acquire(self, loc: int, claimed: set, allow_protected: bool = True) -> int | None:
+        """offloader.py:2036-2074 (the gap calls it with allow_protected=True;
+        the classic hook passes the miss's decode class)."""
         slot = None
         if self.free_stack:
             slot = self.free_stack.pop()
@@ -177,7 +188,7 @@ class SlotPolicyModel:
                 if cand not in claimed:
                     slot = cand
                     break
-            if slot is None:
+            if slot is None and allow_protected:
                 order = self._lru(PROTECTED)
                 if self.lfu:  # coldest first, LRU order among equals
                     order = sorted(order, key=lambda s: self.freq[self.expert_in_slot[s]])
@@ -187,14 +198,19 @@ class SlotPolicyModel:
                         break
         if slot is None:
             return None
-        old = self.expert_in_slot[slot]                  # _evict_to 2076-2081
+        self._evict_to(slot, loc)
+        self.seg[slot] = PROBATION                       # new entries: probation
+        self.stamp[slot] = self._tick()
+        return slot
+
+    def _evict_to(self, slot: int, loc: int) -> None:
+        """offloader.py:2076-2081: the slot's owner changes; its segment and
+        recency do not."""
+        old = self.expert_in_slot[slot]
         if old >= 0:
             self.slot_of[old] = -1
         self.expert_in_slot[slot] = loc
         self.slot_of[loc] = slot
-        self.seg[slot] = PROBATION                       # new entries: probation
-        self.stamp[slot] = self._tick()
-        return slot
 
     def _write_standing_map(self) -> None:
         """offloader.py:2112-2123 via _write_map 2083-2110."""
@@ -259,6 +275,117 @@ class SlotPolicyModel:
         if changed or not self.map_is_standing:               # 2466-2467
             self._write_standing_map()
         return fills
+
+    # -- steps beyond the envelope (offloader.py:1452-1764, 1846-1933) --------
+    def run_moe(self, ids: list[int], topk: int, decode_rows: int = 0) -> list[dict]:
+        """Plan one step through the classic hook over the flattened topk ids
+        of ``len(ids) // topk`` tokens, on a real step.
+
+        ``decode_rows`` is the step's decode signal (``_split_signal``): ``d > 0``
+        — rows [0, d) are single-token decodes (vLLM's ``num_decode_tokens``
+        equal to ``num_decodes``, decode rows first); ``0`` — no per-token
+        signal (a pure prefill, or a backend without a decode count), so the
+        working-set heuristic classifies the step; ``-1`` — short prefills
+        folded into the decode count, so every expert is scan-class.
+
+        Returns the waves in execution order, each ``{"map": [(global, slot)],
+        "fills": [(local, slot)]}``: a wave's fills are streamed before its
+        GEMM, its map routes exactly its experts, and the step's output is the
+        sum of the waves' outputs. The expert map is left holding the last
+        wave's map, not a standing one (``_write_map`` 2083-2110).
+        """
+        ids = [int(g) for g in ids]
+        T = len(ids) // max(int(topk), 1)
+        G = self.global_n
+        selected = sorted(set(ids))                           # 1561
+        decode_ids = None
+        forced_scan = decode_rows < 0                         # 1628 (nd > ndec)
+        if 0 < decode_rows <= T:                              # 1578-1583
+            decode_ids = (set(selected) if decode_rows == T
+                          else set(ids[: decode_rows * topk]))
+        pairs = []                                            # 1613-1621
+        for g in selected:
+            if 0 <= g < G and self.local_of[g] >= 0:
+                pairs.append((g, self.local_of[g], decode_ids is not None and g in decode_ids))
+        ws = len(pairs)
+        if decode_ids is None and not forced_scan:            # 1629-1639
+            n_pinned = sum(1 for v in self.seg if v == PINNED)
+            if ws <= max(self.protected_cap + n_pinned, 1):
+                pairs = [(g, loc, True) for g, loc, _ in pairs]
+        if ws == 0:                                           # 1643-1645
+            self.expert_map = [-1] * G
+            self.map_is_standing = False
+            return [{"map": [], "fills": []}]
+        self.scan_steps += 1
+        if self.lfu:                                          # 1662-1663
+            self.bump_freq([g for g, _, _ in pairs])
+        hits, missing = [], []                                # 1672-1681
+        for g, loc, dcls in pairs:
+            slot = self.slot_of[loc]
+            if slot < 0:
+                missing.append((g, loc, dcls))
+            else:
+                self._touch(slot, dcls)
+                hits.append((g, slot))
+        self.scan_hits += len(hits)
+        self.scan_misses += len(missing)
+        missing.sort(key=lambda m: not m[2])                  # 1689: decode class first
+        claimed = {slot for _, slot in hits}
+        wave0 = {"map": list(hits), "fills": []}
+        taken = len(missing)
+        for i, (g, loc, dcls) in enumerate(missing):          # 1701-1708
+            slot = self._acquire(loc, claimed, allow_protected=dcls)
+            if slot is None:
+                taken = i
+                break
+            wave0["fills"].append((loc, slot))
+            wave0["map"].append((g, slot))
+            claimed.add(slot)
+        waves = [wave0]
+        leftover = [(g, loc) for g, loc, _ in missing[taken:]]
+        if leftover:                                          # _run_waves
+            rot = self._lru(PROBATION)                        # 1856-1862
+            if not rot:
+                rot = [s for s in range(self.num_slots)
+                       if self.seg[s] != PINNED][-max(1, self.num_slots // 4):]
+            half = (len(rot) + 1) // 2
+            groups = (rot[:half], rot[half:] or rot[:half])
+            i = 0
+            while i < len(leftover):                          # 1874-1886
+                group = groups[(len(waves) - 1) % 2]
+                wave = {"map": [], "fills": []}
+                for (g, loc), slot in zip(leftover[i: i + len(group)], group):
+                    self._evict_to(slot, loc)
+                    wave["fills"].append((loc, slot))
+                    wave["map"].append((g, slot))
+                i += len(wave["fills"])
+                waves.append(wave)
+        self.scan_waves += len(waves)
+        self.bytes_streamed += self.bytes_per_expert * sum(len(w["fills"]) for w in waves)
+        last = [-1] * G
+        for g, slot in waves[-1]["map"]:
+            last[g] = slot
+        self.expert_map = last
+        self.map_is_standing = False
+        return waves
+
+    @staticmethod
+    def waves_pipelined(num_slots: int, protected_cap: int, n_pinned: int) -> bool:
+        """Whether every wave step of this cache rotates two non-empty
+        groups: the probation segment holds at least ``num_slots - n_pinned -
+        protected_cap`` slots whenever a miss finds no slot, so two or more
+        make both ping-pong groups non-empty (``_run_waves`` 1863-1866)."""
+        return num_slots - n_pinned - protected_cap >= 2
+
+    @staticmethod
+    def max_waves(num_slots: int, local_n: int, protected_cap: int, n_pinned: int) -> int:
+        """An upper bound on the waves of one step: wave 0 holds at least the
+        probation segment (``r = num_slots - n_pinned - protected_cap`` slots
+        or more), and each later wave takes a group of at least ``r // 2``."""
+        r = max(num_slots - n_pinned - protected_cap, 1)
+        left = max(local_n - r, 0)
+        g = max(r // 2, 1)
+        return 1 + (left + g - 1) // g
 
     # -- views ---------------------------------------------------------------
     def snapshot(self) -> dict:

@@ -19,6 +19,14 @@ It writes:
   evaluated by vLLM's ``cpu_fused_moe_torch`` (``cpu_fused_moe.py`` 428-482).
 * ``fp8_quant.npz`` — bf16 activations through vLLM's torch-native
   per-token-group fp8 quantisation (``QuantFP8._quantize_group_native``).
+* ``wave_traces.json`` — steps beyond the envelope through the reference's
+  classic hook ``ExpertStreamOffloader.run_moe`` (1452-1764) and
+  ``_run_waves`` (1846-1933), some scenarios interleaved with router-split gap
+  calls: per step the waves (each wave's expert map entries and the fills
+  streamed before it, read off ``_write_map`` / ``_stream_in``) and the
+  state after the step. CUDA events and the current stream are replaced by
+  no-op stand-ins (there is no copy stream on a CPU cache, so every copy is
+  made in place), and ``_split_signal`` returns the step's decode signal.
 
 Nothing at test time reads the reference; the tests read these files.
 """
@@ -298,11 +306,175 @@ def make_moe():
     print("moe: out", out.float().abs().mean().item())
 
 
+class _NoEvent:
+    def record(self, *a):
+        pass
+
+    def synchronize(self):
+        pass
+
+
+def _split_signal_for(decode_rows: int):
+    """``_split_signal`` of a real MLA step: rows [0, d) decode (d > 0), a
+    pure prefill (0), or short prefills folded into the decode count (-1)."""
+    if decode_rows > 0:
+        return (decode_rows, decode_rows, True)
+    if decode_rows == 0:
+        return (0, 0, True)
+    return (2, 1, True)
+
+
+def _run_wave_scenario(name, *, slots, global_n, local_n, owned_lo=0, steps, frac=0.5,
+                       pins=None, lfu=False, fast_hit=True):
+    """``steps``: [("gap", ids) | ("moe", ids, topk, decode_rows)]."""
+    torch.cuda.Event = _NoEvent
+    torch.cuda.current_stream = lambda *a: None
+    off = _ref_offloader(slots, fast_hit, frac, False, lfu)
+    if pins is not None:
+        off._pin_layers = {0: list(pins)}
+    if local_n == global_n:
+        emap, local_of = None, list(range(global_n))
+    else:
+        lo = [-1] * global_n
+        for i in range(local_n):
+            lo[owned_lo + i] = i
+        emap, local_of = torch.tensor(lo, dtype=torch.int32), lo
+    mod = _FakeMoE(local_n, global_n, emap)
+    off._install_cache(mod)
+    cache = off._caches[id(mod)]
+    assert not cache.static_full, name
+    off._rs_caches.append(cache)
+    log = []
+    wm, si = off._write_map, off._stream_in
+    off._write_map = lambda c, wave, pinned: (log.append(("map", [list(x) for x in wave])),
+                                              wm(c, wave, pinned))[1]
+    off._stream_in = lambda c, local, slot, cs, on_stream=False: (
+        log.append(("fill", [int(local), int(slot)])), si(c, local, slot, cs, on_stream))[1]
+    signal = [(0, 0, True)]
+    off._split_signal = lambda: signal[0]
+    trace = []
+    for st in steps:
+        log.clear()
+        rec = {"kind": st[0], "ids": list(st[1])}
+        if st[0] == "gap":
+            if lfu:
+                pairs = [(g, local_of[g], True) for g in sorted(set(st[1]))
+                         if 0 <= g < global_n and local_of[g] >= 0]
+                off._bump_freq(cache, pairs)
+            try:
+                off._router_split_gap(0, torch.tensor(st[1], dtype=torch.int32))
+                rec["overflow"] = False
+            except RuntimeError:
+                rec["overflow"] = True
+        else:
+            _, ids, topk, d = st
+            rec["topk"], rec["decode_rows"] = topk, d
+            signal[0] = _split_signal_for(d)
+            t = torch.tensor(ids, dtype=torch.int32).view(-1, topk)
+            out = off.run_moe(lambda *a, **k: torch.ones(1), (), {}, mod, t)
+            waves, pending = [], []
+            for kind, v in log:
+                if kind == "fill":
+                    pending.append(v)
+                else:
+                    waves.append({"map": v, "fills": pending})
+                    pending = []
+            assert not pending and int(out.item()) == len(waves), name
+            rec["waves"] = waves
+        w = cache.gpu_cache["w"][:, 0]
+        stats = off._stats
+        rec.update({
+            "expert_map": cache.expert_map_buf.tolist(),
+            "expert_in_slot": [-1 if v is None else int(v) for v in cache.expert_in_slot],
+            "slot_payload": [int(w[s].item()) if cache.expert_in_slot[s] is not None
+                             else -1 for s in range(cache.num_slots)],
+            "protected": list(cache.protected),
+            "probation": list(cache.probation),
+            "map_is_standing": bool(cache.map_is_standing),
+            "gaps": off._rs_gaps, "misses": off._rs_misses, "fast_hits": off._rs_fast_hits,
+            "scan_steps": stats["small"].steps + stats["scan"].steps,
+            "scan_hits": stats["small"].hits + stats["scan"].hits,
+            "scan_misses": stats["small"].misses + stats["scan"].misses,
+            "scan_waves": stats["small"].waves + stats["scan"].waves,
+            "freq": [int(cache.freq.get(loc, 0)) for loc in range(local_n)],
+        })
+        trace.append(rec)
+        if rec.get("overflow"):
+            break
+    return {
+        "name": name, "num_slots": cache.num_slots, "global_n": global_n,
+        "local_n": local_n, "local_of": local_of, "fast_hit": fast_hit, "lfu": lfu,
+        "protect_frac": frac, "protected_cap": cache.protected_cap,
+        "pins": list(pins) if pins is not None else None,
+        "pinned_slots": sorted(cache.pinned_slots), "trace": trace,
+    }
+
+
+def make_wave_traces():
+    g = torch.Generator().manual_seed(2468)
+
+    def prefill(T, k, E, d=0):
+        # each token's k distinct ids, uniform
+        ids = [i for _ in range(T) for i in torch.randperm(E, generator=g)[:k].tolist()]
+        return ("moe", ids, k, d)
+
+    def decode(T, k, E, s=1.1):
+        return ("gap", _zipf_ids(g, 1, T, k, E, s=s)[0])
+
+    def mixed(n, Tp, Td, k, E, every=4, d=0):
+        out = []
+        for i in range(n):
+            out.append(prefill(Tp, k, E, d) if i % every == 0 else decode(Td, k, E))
+        return out
+
+    sc = [
+        _run_wave_scenario("v2lite_prefill_scan", slots=48, global_n=64, local_n=64,
+                           steps=[prefill(64, 6, 64) for _ in range(6)]),
+        _run_wave_scenario("v2lite_mixed", slots=48, global_n=64, local_n=64,
+                           steps=mixed(24, 40, 8, 6, 64)),
+        _run_wave_scenario("v2lite_mixed_decode_rows", slots=48, global_n=64, local_n=64,
+                           steps=mixed(16, 24, 8, 6, 64, every=3, d=4)
+                           + [prefill(16, 6, 64, 16), prefill(30, 6, 64, -1)]),
+        _run_wave_scenario("v2lite_frac09_small_groups", slots=48, global_n=64, local_n=64,
+                           frac=0.9, steps=mixed(12, 64, 8, 6, 64, every=2)),
+        _run_wave_scenario("s8_frac09_one_slot_rotation", slots=8, global_n=32, local_n=32,
+                           frac=0.9, steps=[decode(1, 6, 32), prefill(12, 6, 32),
+                                            decode(1, 6, 32), prefill(20, 6, 32)]),
+        _run_wave_scenario("v2lite_pins_prefill", slots=40, global_n=64, local_n=64,
+                           pins=[5, 9, 11, 2], steps=mixed(12, 48, 6, 6, 64, every=3)),
+        _run_wave_scenario("v2lite_friendly_small_prefill", slots=48, global_n=64, local_n=64,
+                           steps=[prefill(3, 6, 64), prefill(5, 6, 64), prefill(12, 6, 64),
+                                  prefill(3, 6, 64)]),
+        _run_wave_scenario("ep_rank1_of2_prefill", slots=24, global_n=64, local_n=32,
+                           owned_lo=32, steps=mixed(12, 32, 4, 6, 64, every=2)),
+        _run_wave_scenario("qwen3_s64_mixed", slots=64, global_n=128, local_n=128,
+                           steps=mixed(12, 48, 8, 8, 128, every=3)),
+        _run_wave_scenario("v2lite_lfu_mixed", slots=48, global_n=64, local_n=64, lfu=True,
+                           steps=mixed(30, 32, 8, 6, 64, every=5)),
+        _run_wave_scenario("no_owned_ids", slots=24, global_n=64, local_n=32, owned_lo=0,
+                           steps=[("moe", [40, 41, 63, -1, 50, 33] * 8, 6, 0),
+                                  decode(4, 6, 64)]),
+    ]
+    with open(os.path.join(HERE, "wave_traces.json"), "w") as f:
+        json.dump({"generator": "tests/golden/make_golden.py", "scenarios": sc}, f,
+                  separators=(",", ":"))
+    for s in sc:
+        nw = [len(r["waves"]) for r in s["trace"] if r["kind"] == "moe"]
+        print(f"{s['name']}: steps={len(s['trace'])} waves per moe step={nw}")
+
+
 if __name__ == "__main__":
     if not REF:
         raise SystemExit("set SLUICE_REFERENCE to a checkout of kfirtoledo/sluice")
     sys.path.insert(0, os.path.join(REF, "src"))
-    make_slot_traces()
-    make_routing()
-    make_moe()
-    make_fp8_quant()
+    wanted = set(sys.argv[1:]) or {"slots", "routing", "moe", "fp8", "waves"}
+    if "slots" in wanted:
+        make_slot_traces()
+    if "routing" in wanted:
+        make_routing()
+    if "moe" in wanted:
+        make_moe()
+    if "fp8" in wanted:
+        make_fp8_quant()
+    if "waves" in wanted:
+        make_wave_traces()

@@ -76,6 +76,71 @@ def test_golden_covers_edge_cases():
     assert names["ep_rank1_of2"]["local_n"] < names["ep_rank1_of2"]["global_n"]
 
 
+def _wave_scenarios():
+    with open(os.path.join(GOLDEN, "wave_traces.json")) as f:
+        return json.load(f)["scenarios"]
+
+
+def replay_wave_step(m: SlotPolicyModel, step: dict):
+    """One step of a wave trace through the oracle: the gap, or the classic
+    hook's wave planning. Returns the waves (gap steps: None)."""
+    if step["kind"] == "gap":
+        try:
+            m.gap(step["ids"])
+        except SlotOverflow:
+            pass
+        return None
+    return m.run_moe(step["ids"], step["topk"], step["decode_rows"])
+
+
+@pytest.mark.parametrize("sc", _wave_scenarios(), ids=lambda s: s["name"])
+def test_wave_planning_matches_reference_run_moe(sc):
+    """Steps beyond the envelope: the oracle's run_moe / _run_waves restatement
+    against the reference's own classic hook (waves, fills, final state)."""
+    sc = dict(sc, prefill_resident=False)
+    m = model_for(sc)
+    assert m.protected_cap == sc["protected_cap"]
+    n_pinned = len(sc["pinned_slots"])
+    bound = SlotPolicyModel.max_waves(m.num_slots, m.local_n, m.protected_cap, n_pinned)
+    pipelined = SlotPolicyModel.waves_pipelined(m.num_slots, m.protected_cap, n_pinned)
+    for i, exp in enumerate(sc["trace"]):
+        waves = replay_wave_step(m, exp)
+        where = (sc["name"], i)
+        if waves is not None:
+            got = [{"map": [list(x) for x in w["map"]], "fills": [list(x) for x in w["fills"]]}
+                   for w in waves]
+            assert got == exp["waves"], where
+            assert len(waves) <= bound, where
+            if len(waves) > 2 and pipelined:
+                # ping-pong: consecutive waves use disjoint slots
+                for a, b in zip(waves[1:], waves[2:]):
+                    assert not {s for _, s in a["fills"]} & {s for _, s in b["fills"]}, where
+        assert m.expert_map == exp["expert_map"], where
+        assert m.expert_in_slot == exp["expert_in_slot"], where
+        assert m.segment_order(PROTECTED) == exp["protected"], where
+        assert m.segment_order(PROBATION) == exp["probation"], where
+        assert m.map_is_standing == exp["map_is_standing"], where
+        assert (m.gaps, m.misses, m.fast_hits) == (exp["gaps"], exp["misses"],
+                                                    exp["fast_hits"]), where
+        assert (m.scan_steps, m.scan_hits, m.scan_misses, m.scan_waves) == (
+            exp["scan_steps"], exp["scan_hits"], exp["scan_misses"], exp["scan_waves"]), where
+        if sc["lfu"]:
+            assert m.freq == exp["freq"], where
+
+
+def test_wave_golden_covers_edge_cases():
+    names = {s["name"]: s for s in _wave_scenarios()}
+    nw = lambda n: [len(r["waves"]) for r in names[n]["trace"] if r["kind"] == "moe"]
+    assert max(nw("s8_frac09_one_slot_rotation")) > 8        # one-slot groups, not ping-pong
+    assert not SlotPolicyModel.waves_pipelined(8, names["s8_frac09_one_slot_rotation"]
+                                               ["protected_cap"], 0)
+    assert max(nw("v2lite_mixed")) >= 3 and max(nw("qwen3_s64_mixed")) >= 5
+    assert nw("no_owned_ids") == [1]
+    assert names["v2lite_pins_prefill"]["pinned_slots"] and names["v2lite_lfu_mixed"]["lfu"]
+    assert {r.get("decode_rows") for r in names["v2lite_mixed_decode_rows"]["trace"]} >= {
+        4, 16, -1}
+
+
 def _routing_case(z, name):
     meta = z[f"{name}_meta"]
     T, H, E, k, renorm, G, TG, sig = (int(v) for v in meta)
