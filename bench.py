@@ -60,8 +60,11 @@ def _args(argv=None):
                     help="expert-parallel dispatch/combine (N>1): peer-memory kernels or NCCL")
     ap.add_argument("--no-overlap", action="store_true",
                     help="serialise the expert stream and the GEMMs (A/B)")
-    ap.add_argument("--workload", default="decode", choices=["decode", "grouped-gemm"],
-                    help="grouped-gemm: the fp8 grouped-GEMM microbench (one JSON line per T)")
+    ap.add_argument("--workload", default="decode", choices=["decode", "grouped-gemm", "prefill"],
+                    help="grouped-gemm: the fp8 grouped-GEMM microbench (one JSON line per T); "
+                         "prefill: steps beyond the envelope, expert waves and token chunks")
+    ap.add_argument("--prefill-tokens", type=int, default=512,
+                    help="tokens per step of the prefill workload")
     ap.add_argument("--gemm-tokens", default="8,64,512,4096",
                     help="token counts of the grouped-GEMM microbench")
     ap.add_argument("--gemm-experts", type=int, default=256,
@@ -775,6 +778,76 @@ def run_grouped_gemm(a):
         print(json.dumps(line), flush=True)
 
 
+def run_prefill(a):
+    """Steps beyond the envelope (prefill-sized batches of --prefill-tokens
+    tokens) through the same MoE stack twice: in expert waves (the
+    reference's classic-hook route for such steps) and in envelope-sized
+    token chunks through the gap. One JSON line per mode: tok/s, the experts
+    streamed per step and the roofline max(HBM bytes / copy peak, host bytes /
+    PCIe Gen5 x16, FLOPs / bf16 peak). Fresh random tokens every step."""
+    import gc
+
+    from sluice_b200 import configs
+    from sluice_b200.layer import MoEDecodeStack
+
+    cfg = configs.CONFIGS[a.config]
+    layers = a.layers or 4
+    T, K, W = a.prefill_tokens, a.steps, a.warmup
+    with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+        peaks = json.load(f)
+    hbm_peak, bf16_peak, host_peak = peaks["hbm_gbs"], peaks["bf16_tflops"], 63.0
+    bpe, k = cfg.bytes_per_expert, cfg.routing.topk
+    for mode in ("waves", "chunks"):
+        stack = MoEDecodeStack(cfg, slots=a.slots, seed=a.seed, num_layers=layers)
+        for layer in stack.layers:
+            layer.beyond_envelope = mode
+        g = torch.Generator().manual_seed(a.seed + 11)
+        xs = [torch.randn(T, cfg.hidden, generator=g).to(torch.bfloat16).cuda()
+              for _ in range(W + K)]
+        for i in range(W):
+            stack.step(xs[i])
+        torch.cuda.synchronize()
+        s0 = stack.stats()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(torch.cuda.current_device()) as clk:
+            ev0.record()
+            for i in range(K):
+                stack.step(xs[W + i])
+            ev1.record()
+            torch.cuda.synchronize()
+        ms = ev0.elapsed_time(ev1) / K
+        stack.check()
+        s1 = stack.stats()
+        # experts the last step selected, per layer (every one is read once)
+        uniq = sum(int(torch.unique(layer.last_ids).numel()) for layer in stack.layers)
+        fills = (s1["fills"] - s0["fills"]) / K
+        host = fills * bpe
+        hbm = uniq * bpe + layers * cfg.n_shared * bpe
+        flops = layers * T * (k + cfg.n_shared) * cfg.flops_per_pair
+        t_roof = max(hbm / (hbm_peak * 1e9), host / (host_peak * 1e9),
+                     flops / (bf16_peak * 1e12)) * 1e3
+        line = {
+            "metric": "prefill MoE tok/s", "value": T / (ms * 1e-3), "unit": "tok/s",
+            "mode": mode, "n_gpus": 1, "steps": K, "warmup": W, "ms_per_step": ms,
+            "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"{cfg.name} MoE stack, {layers} layers, {a.slots} slots "
+                       f"of {cfg.num_experts} experts, {T}-token steps beyond the envelope "
+                       f"({a.slots // k} tokens), fresh random tokens per step"},
+            "experts_streamed_per_step": fills,
+            "waves_per_step": (s1["waves"] - s0["waves"]) / K,
+            "host_gbs": host / (ms * 1e-3) / 1e9,
+            "roofline": {"ms": t_roof, "frac": t_roof / ms, "host_bytes": host,
+                         "hbm_bytes": hbm, "flops": flops,
+                         "peaks": {"hbm_gbs": hbm_peak, "bf16_tflops": bf16_peak,
+                                   "host_link_gbs": host_peak}},
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+        del stack, xs
+        gc.collect()
+        torch.cuda.empty_cache()
+
+
 def run_reference(a):
     """The reference's CPU path (oracle port) on the host cores, rank 0 only."""
     from sluice_b200 import configs
@@ -813,6 +886,8 @@ def main(argv=None):
         run_reference(a)
     elif a.workload == "grouped-gemm":
         run_grouped_gemm(a)
+    elif a.workload == "prefill":
+        run_prefill(a)
     else:
         run_sluice(a)
 

@@ -93,7 +93,7 @@ enum {
 };
 
 /* Field offsets (bytes) inside the state block, in this order:
- * 0 header (int32 x 16, see SL_HDR_*), 1 counters (uint64 x 8, SL_CNT_*),
+ * 0 header (int32 x 16, see SL_HDR_*), 1 counters (uint64 x 16, SL_CNT_*),
  * 2 local_of[global_n], 3 global_of_local[local_n], 4 slot_of[local_n],
  * 5 expert_in_slot[S], 6 seg[S] (uint8), 7 stamp[S] (uint32),
  * 8 free_stack[S], 9 fill_local[S], 10 fill_slot[S], 11 freq[local_n]
@@ -107,7 +107,10 @@ enum {
 };
 enum {
   SL_CNT_GAPS = 0, SL_CNT_FAST_HITS, SL_CNT_MISSES, SL_CNT_HITS,
-  SL_CNT_OVERFLOWS, SL_CNT_FILLS
+  SL_CNT_OVERFLOWS, SL_CNT_FILLS /* every expert streamed, gaps and waves */,
+  /* steps planned by sl_plan_waves (the classic hook's _StepStats steps,
+   * hits, misses and waves, offloader.py:172-183) */
+  SL_CNT_SCAN_STEPS, SL_CNT_SCAN_HITS, SL_CNT_SCAN_MISSES, SL_CNT_WAVES
 };
 size_t sl_slot_state_bytes(int num_slots, int global_n, int local_n);
 int sl_slot_state_offsets(int num_slots, int global_n, int local_n,
@@ -135,6 +138,62 @@ int sl_slot_state_init(void* state, int num_slots, int global_n, int local_n,
  * status word to SL_ERR_OVERFLOW (the map is then left as it was). */
 int sl_plan_slots(void* state, const int32_t* topk_ids, int num_ids,
                   int32_t* expert_map, sl_stream_t stream);
+
+/* ---------------------------------------------- steps beyond the envelope
+ * A step whose working set can exceed the slots (a prefill, or a mixed
+ * prefill + decode batch) runs in expert waves, as the reference's classic
+ * hook does for prefill-sized steps under router-split: run_moe
+ * (offloader.py:1452-1764) classifies the step, touches the hits and fills
+ * what it can (wave 0), and _run_waves (1846-1933) rotates the remaining
+ * misses through the probation slots in two ping-pong groups, one wave per
+ * group; the step's output is the sum of the waves' outputs.
+ *
+ * Wave plan buffer (int32 words; field offsets from sl_wave_plan_offsets):
+ * 0 header (SL_WAVE_HDR_*), 1 fill_count[max_waves], 2 fill_local
+ * [max_waves][S], 3 fill_slot [max_waves][S], 4 map [max_waves][global_n]
+ * (wave k's expert map: its experts -> their slots, -1 elsewhere). */
+enum { SL_WAVE_NFIELDS = 5 };
+enum {
+  SL_WAVE_HDR_NUM_WAVES = 0, SL_WAVE_HDR_STATUS, SL_WAVE_HDR_MAX_WAVES,
+  SL_WAVE_HDR_GLOBAL_N, SL_WAVE_HDR_NUM_SLOTS,
+  SL_WAVE_HDR_LEFTOVER,   /* misses of the last plan past wave 0 */
+  SL_WAVE_HDR_ROTATION    /* slots in the last plan's rotation groups */
+};
+size_t sl_wave_plan_bytes(int num_slots, int global_n, int max_waves);
+int sl_wave_plan_offsets(int num_slots, int global_n, int max_waves,
+                         size_t* offsets /* [SL_WAVE_NFIELDS + 1], bytes */);
+/* Write the buffer's header (dimensions) and empty waves; synchronises
+ * `stream`. */
+int sl_wave_plan_init(void* waves, int num_slots, int global_n, int max_waves,
+                      sl_stream_t stream);
+
+/* Plan one step of num_tokens x topk ids in waves, on the device (one CTA):
+ * decode_rows is the step's decode signal (_split_signal 1767-1800): > 0 —
+ * rows [0, decode_rows) are single-token decodes (decode-class experts may
+ * promote into / evict from the protected segment); 0 — no per-token signal,
+ * so the step is decode-class as a whole when its owned working set fits
+ * protected_cap + pinned slots (1629-1639); < 0 — every expert scan-class.
+ * Wave 0 = hits + the misses that found a slot (decode-class misses first,
+ * _acquire_slot 2036-2074); its fills are also the state's fill list, so
+ * sl_fused_experts_phase can split wave 0 around its stream. The expert map
+ * is left holding the last wave's map and the map stops being standing (the
+ * next sl_plan_slots touches its hits and rewrites it), as _write_map
+ * 2083-2110 leaves them. More waves than the buffer holds set
+ * SL_ERR_OVERFLOW in both status words. */
+int sl_plan_waves(void* state, const int32_t* topk_ids, int num_tokens, int topk,
+                  int decode_rows, int32_t* expert_map, void* waves,
+                  sl_stream_t stream);
+
+/* Stream wave `wave`'s fills of the last sl_plan_waves (nothing for a wave
+ * past its count), as sl_stream_experts_strided does for a gap. Order it
+ * after the GEMMs that last read the wave's slots: wave k >= 1 reuses the
+ * slots of wave k - 2 (ping-pong) or, with a single rotation group, of wave
+ * k - 1; waves 1 and 2 also reuse slots wave 0 reads. */
+int sl_stream_wave(const void* waves, int wave, int num_params,
+                   const void* const* host_src, void* const* slot_dst,
+                   const size_t* bytes_per_expert,
+                   const size_t* host_stride_bytes, int num_ctas,
+                   sl_stream_t stream);
 
 /* Stream the last plan's fills: replaces _stream_in (offloader.py:2709-2723)
  * and its copy-stream events (1979-1991). For every fill (local, slot) and
@@ -217,8 +276,9 @@ typedef struct sl_expert_weights {
  * stay bf16), shared experts on tokens [shared_t0, shared_t0 + shared_nt)
  * (shared_nt < 0: every token), optional phase split around the expert
  * stream (phase -1: whole call; 0 / 1 as sl_fused_experts_phase, slot_state
- * required), and out_f32 != 0 for the expert-parallel fp32 partial (as
- * sl_fused_experts_partial). */
+ * required), and out_f32 = 1 for the expert-parallel fp32 partial (as
+ * sl_fused_experts_partial), 2 for the same partial added to the fp32 `out`
+ * (the expert waves of one step, sl_plan_waves). */
 int sl_fused_experts_ex(const void* hidden, int T, int H, int I,
                         const sl_expert_weights* weights,
                         const float* topk_weights, const int32_t* topk_ids,

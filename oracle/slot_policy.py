@@ -369,24 +369,6 @@ class SlotPolicyModel:
         self.map_is_standing = False
         return waves
 
-    @staticmethod
-    def waves_pipelined(num_slots: int, protected_cap: int, n_pinned: int) -> bool:
-        """Whether every wave step of this cache rotates two non-empty
-        groups: the probation segment holds at least ``num_slots - n_pinned -
-        protected_cap`` slots whenever a miss finds no slot, so two or more
-        make both ping-pong groups non-empty (``_run_waves`` 1863-1866)."""
-        return num_slots - n_pinned - protected_cap >= 2
-
-    @staticmethod
-    def max_waves(num_slots: int, local_n: int, protected_cap: int, n_pinned: int) -> int:
-        """An upper bound on the waves of one step: wave 0 holds at least the
-        probation segment (``r = num_slots - n_pinned - protected_cap`` slots
-        or more), and each later wave takes a group of at least ``r // 2``."""
-        r = max(num_slots - n_pinned - protected_cap, 1)
-        left = max(local_n - r, 0)
-        g = max(r // 2, 1)
-        return 1 + (left + g - 1) // g
-
     # -- views ---------------------------------------------------------------
     def snapshot(self) -> dict:
         return {

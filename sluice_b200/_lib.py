@@ -32,8 +32,15 @@ PLAN_LFU = 2
 HDR = dict(num_slots=0, global_n=1, local_n=2, protected_cap=3, flags=4,
            map_is_standing=5, free_top=6, protected_count=7, clock=8, status=9,
            fill_count=10, last_misses=11, lfu_steps=12)
-CNT = dict(gaps=0, fast_hits=1, misses=2, hits=3, overflows=4, fills=5)
+CNT = dict(gaps=0, fast_hits=1, misses=2, hits=3, overflows=4, fills=5, scan_steps=6,
+           scan_hits=7, scan_misses=8, waves=9)
 STATE_NFIELDS = 12
+NUM_COUNTERS = 16
+
+# wave plan header words (sl_plan_waves)
+WAVE_HDR = dict(num_waves=0, status=1, max_waves=2, global_n=3, num_slots=4, leftover=5,
+                rotation=6)
+WAVE_NFIELDS = 5
 
 _c = ctypes
 _vp, _i, _sz, _f = _c.c_void_p, _c.c_int, _c.c_size_t, _c.c_float
@@ -65,6 +72,11 @@ _SIGNATURES = {
     "sl_plan_slots": (_i, [_vp, _vp, _i, _vp, _vp]),
     "sl_stream_experts": (_i, [_vp, _i, _vp, _vp, _vp, _i, _vp]),
     "sl_stream_experts_strided": (_i, [_vp, _i, _vp, _vp, _vp, _vp, _i, _vp]),
+    "sl_wave_plan_bytes": (_sz, [_i, _i, _i]),
+    "sl_wave_plan_offsets": (_i, [_i, _i, _i, _vp]),
+    "sl_wave_plan_init": (_i, [_vp, _i, _i, _i, _vp]),
+    "sl_plan_waves": (_i, [_vp, _vp, _i, _i, _i, _vp, _vp, _vp]),
+    "sl_stream_wave": (_i, [_vp, _i, _i, _vp, _vp, _vp, _vp, _i, _vp]),
     "sl_host_alloc_mapped": (_i, [_sz, _c.POINTER(_vp)]),
     "sl_host_free": (_i, [_vp]),
     "sl_fused_experts_workspace_bytes": (_sz, [_i, _i, _i, _i, _i, _i]),

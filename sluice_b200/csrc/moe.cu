@@ -1576,8 +1576,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(
 // OUT_F32 = false: out = bf16(shared + bf16(scale * bf16(sum_j w z)))  (vLLM
 //   torch-native rounding chain, runner tail in bf16)
 // OUT_F32 = true:  out = scale * sum_j w z + shared, fp32, no rounding (the
-//   per-rank partial of expert parallelism, summed across ranks afterwards)
-template <bool OUT_F32>
+//   per-rank partial of expert parallelism, summed across ranks afterwards);
+//   ACCUMULATE adds it to what `out` holds (the expert waves of one step)
+template <bool OUT_F32, bool ACCUMULATE = false>
 __global__ void __launch_bounds__(256) combine_kernel(
     const int32_t* __restrict__ ws_hdr, const int32_t* __restrict__ pair_pos,
     const float* __restrict__ tw, const __nv_bfloat16* __restrict__ Z, int T, int topk, int H,
@@ -1648,6 +1649,11 @@ __global__ void __launch_bounds__(256) combine_kernel(
   }
   if constexpr (OUT_F32) {
     float4* dst = reinterpret_cast<float4*>(static_cast<float*>(out) + static_cast<size_t>(t) * H + h0);
+    if constexpr (ACCUMULATE) {
+      const float4 a = dst[0], b = dst[1];
+      o[0] += a.x, o[1] += a.y, o[2] += a.z, o[3] += a.w;
+      o[4] += b.x, o[5] += b.y, o[6] += b.z, o[7] += b.w;
+    }
     dst[0] = make_float4(o[0], o[1], o[2], o[3]);
     dst[1] = make_float4(o[4], o[5], o[6], o[7]);
   } else {
@@ -1780,9 +1786,12 @@ namespace {
 int run_fused(const void* hidden, int T, int H, int I, const sl_expert_weights& w,
               const float* topk_weights, const int32_t* topk_ids, int topk,
               const int32_t* expert_map, int global_n, int sh_t0, int sh_nt,
-              float routed_scaling_factor, void* out, bool out_f32, void* workspace,
+              float routed_scaling_factor, void* out, int out_mode, void* workspace,
               size_t workspace_bytes, cudaStream_t st, const void* fill_state = nullptr,
               int phase = -1) {
+  // out_mode: 0 bf16 out; 1 fp32 partial written; 2 fp32 partial added to out
+  const bool out_f32 = out_mode != 0, accumulate = out_mode == 2;
+  if (out_mode < 0 || out_mode > 2) return SL_ERR_INVALID;
   const int num_slots = w.num_slots, n_shared = w.n_shared;
   const bool fp8 = w.dtype == SL_WEIGHTS_FP8_BLOCK128;
   if (w.dtype != SL_WEIGHTS_BF16 && !fp8) return SL_ERR_UNSUPPORTED;
@@ -1845,7 +1854,8 @@ int run_fused(const void* hidden, int T, int H, int I, const sl_expert_weights& 
   int* counters = reinterpret_cast<int*>(ws + L.counters);
   const int n_counters = L.max_items + H / 128 + 1;
   // bf16 decode-sized steps: one persistent kernel for both GEMMs + combine
-  const bool fused = small && !fp8 && fused_enabled();
+  // (which writes its output; an accumulating call runs the separate kernels)
+  const bool fused = small && !fp8 && !accumulate && fused_enabled();
   if (phase != 1) {
     if (small) {
       SL_CUDA_TRY(sl::launch(align_small_kernel, dim3(kAlignSmallCtas), dim3(kAlignSmallThreads),
@@ -1933,8 +1943,10 @@ int run_fused(const void* hidden, int T, int H, int I, const sl_expert_weights& 
   if (rc != SL_OK) return rc;
   if (phase == 0) return SL_OK;
   dim3 cgrid((H / 8 + 255) / 256, T);
-  SL_CUDA_TRY(sl::launch(out_f32 ? combine_kernel<true> : combine_kernel<false>, cgrid,
-                         dim3(256), 0, st, static_cast<const int32_t*>(hdr),
+  SL_CUDA_TRY(sl::launch(accumulate ? combine_kernel<true, true>
+                         : out_f32  ? combine_kernel<true>
+                                    : combine_kernel<false>,
+                         cgrid, dim3(256), 0, st, static_cast<const int32_t*>(hdr),
                          static_cast<const int32_t*>(pair_pos), topk_weights,
                          static_cast<const __nv_bfloat16*>(Z), T, topk, H, nsh, sh_t0, sh_nt,
                          routed_scaling_factor, out));
@@ -1966,7 +1978,7 @@ extern "C" int sl_fused_experts(const void* hidden, int T, int H, int I, const v
   if (weight_dtype != SL_WEIGHTS_BF16) return SL_ERR_UNSUPPORTED;
   const sl_expert_weights w = bf16_weights(w13, w2, num_slots, shared_w13, shared_w2, n_shared);
   return run_fused(hidden, T, H, I, w, topk_weights, topk_ids, topk, expert_map, global_n, 0,
-                   T, routed_scaling_factor, out, false, workspace, workspace_bytes,
+                   T, routed_scaling_factor, out, 0, workspace, workspace_bytes,
                    reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -1983,7 +1995,7 @@ extern "C" int sl_fused_experts_partial(const void* hidden, int T, int H, int I,
   if (weight_dtype != SL_WEIGHTS_BF16) return SL_ERR_UNSUPPORTED;
   const sl_expert_weights w = bf16_weights(w13, w2, num_slots, shared_w13, shared_w2, n_shared);
   return run_fused(hidden, T, H, I, w, topk_weights, topk_ids, topk, expert_map, global_n,
-                   shared_t0, shared_nt, routed_scaling_factor, out_f32, true, workspace,
+                   shared_t0, shared_nt, routed_scaling_factor, out_f32, 1, workspace,
                    workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -2000,7 +2012,7 @@ extern "C" int sl_fused_experts_phase(const void* hidden, int T, int H, int I, c
   if (phase != 0 && phase != 1) return SL_ERR_INVALID;
   const sl_expert_weights w = bf16_weights(w13, w2, num_slots, shared_w13, shared_w2, n_shared);
   return run_fused(hidden, T, H, I, w, topk_weights, topk_ids, topk, expert_map, global_n, 0,
-                   T, routed_scaling_factor, out, false, workspace, workspace_bytes,
+                   T, routed_scaling_factor, out, 0, workspace, workspace_bytes,
                    reinterpret_cast<cudaStream_t>(stream), slot_state, phase);
 }
 
@@ -2017,7 +2029,7 @@ extern "C" int sl_fused_experts_ex(const void* hidden, int T, int H, int I,
     shared_nt = T;
   }
   return run_fused(hidden, T, H, I, *weights, topk_weights, topk_ids, topk, expert_map,
-                   global_n, shared_t0, shared_nt, routed_scaling_factor, out, out_f32 != 0,
+                   global_n, shared_t0, shared_nt, routed_scaling_factor, out, out_f32,
                    workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream),
                    slot_state, phase);
 }

@@ -15,7 +15,7 @@ __host__ __device__ inline size_t round16(size_t v) { return (v + 15) & ~size_t(
 __host__ __device__ inline void state_layout(int S, int G, int L, size_t* off) {
   size_t o = 0;
   off[0] = o; o += round16(16 * 4);           // header
-  off[1] = o; o += round16(8 * 8);            // counters
+  off[1] = o; o += round16(16 * 8);           // counters
   off[2] = o; o += round16(size_t(G) * 4);    // local_of
   off[3] = o; o += round16(size_t(L) * 4);    // global_of_local
   off[4] = o; o += round16(size_t(L) * 4);    // slot_of
@@ -71,5 +71,32 @@ __device__ inline StateView view_from_header(uint8_t* base, int& S, int& G, int&
   return view(base, S, G, L);
 }
 
+// Wave plan of a step beyond the envelope (sl_plan_waves), in int32 words:
+// header, fill count per wave, fill lists per wave ([max_waves][S] locals and
+// slots), one expert map per wave ([max_waves][G]). Fields start on 16 bytes.
+__host__ __device__ inline void wave_layout(int S, int G, int MW, size_t* off) {
+  const size_t r = ~size_t(3);
+  size_t o = 0;
+  off[0] = o; o += 16;                              // header (SL_WAVE_HDR_*)
+  off[1] = o; o += (size_t(MW) + 3) & r;            // fill_count
+  off[2] = o; o += (size_t(MW) * S + 3) & r;        // fill_local
+  off[3] = o; o += (size_t(MW) * S + 3) & r;        // fill_slot
+  off[4] = o; o += (size_t(MW) * G + 3) & r;        // map
+  off[5] = o;
+}
+
+struct WaveView {
+  int32_t* hdr;
+  int32_t* count;
+  int32_t* loc;   // wave k at loc + k * S
+  int32_t* slot;
+  int32_t* map;   // wave k at map + k * G
+};
+
+__host__ __device__ inline WaveView wave_view(int32_t* base, int S, int G, int MW) {
+  size_t off[6];
+  wave_layout(S, G, MW, off);
+  return WaveView{base + off[0], base + off[1], base + off[2], base + off[3], base + off[4]};
+}
 
 }  // namespace

@@ -9,6 +9,12 @@
     fused_experts + shared MLP -> sl_fused_experts (tcgen05 GEMMs + combine)
       + routed scaling + add
 
+Steps beyond the envelope (``slots // topk`` tokens: prefills, mixed
+batches) take the route the reference gives them under router-split, its
+classic hook (``run_moe`` 1452-1764 and ``_run_waves`` 1846-1933): the
+device plans expert waves, and each wave's fills stream on a side stream
+while the previous wave computes; the waves' fp32 outputs add up to the step.
+
 ``MoEDecodeStack`` chains layers with a residual (``h = h + moe(h)``) to run
 the decode step of a MoE decoder's expert layers over the slot caches; the
 step is capturable in one CUDA graph because no kernel waits on the host.
@@ -28,14 +34,21 @@ class SluiceMoELayer:
                  shared_w13: torch.Tensor | None, shared_w2: torch.Tensor | None,
                  layer_idx: int = 0, overlap: bool = True, stream_ctas: int = 16,
                  shared_w13_scale: torch.Tensor | None = None,
-                 shared_w2_scale: torch.Tensor | None = None):
+                 shared_w2_scale: torch.Tensor | None = None,
+                 beyond_envelope: str = "waves"):
+        if beyond_envelope not in ("waves", "chunks"):
+            raise ValueError("beyond_envelope is 'waves' or 'chunks'")
         self.cfg = cfg
+        # steps larger than the envelope: expert waves (the reference's
+        # classic hook), or envelope-sized token chunks through the gap
+        self.beyond_envelope = beyond_envelope
         self.shared_w13_scale = shared_w13_scale
         self.shared_w2_scale = shared_w2_scale
         # overlap the gap's expert stream with the resident experts' GEMMs
         self.overlap = overlap and not cache.static_full
         self.stream_ctas = stream_ctas
-        self._side = torch.cuda.Stream(device=cache.device) if self.overlap else None
+        self._side = torch.cuda.Stream(device=cache.device) \
+            if not cache.static_full else None
         self.router = router
         self.cache = cache
         self.shared_w13 = shared_w13
@@ -53,15 +66,74 @@ class SluiceMoELayer:
             return 1 << 30
         return max(1, self.cache.num_slots // self.cfg.routing.topk)
 
-    def forward(self, hs: torch.Tensor) -> torch.Tensor:
+    def forward(self, hs: torch.Tensor, decode_rows: int = 0) -> torch.Tensor:
+        """One step of ``hs`` [T, H]. ``decode_rows`` only matters beyond the
+        envelope: rows [0, decode_rows) are single-token decodes (the
+        reference's ``num_decode_tokens``, decode rows first), 0 leaves the
+        step's class to the working-set heuristic, < 0 makes it a scan."""
         thr = self.envelope
         if hs.shape[0] > thr:
-            # larger steps (prefill) run as consecutive envelope-sized chunks,
-            # as the reference's piecewise mode requires of the batch
-            # (max_num_batched_tokens = slots // topk): every chunk is a
-            # single-wave gap plus fused experts
+            if self.beyond_envelope == "waves":
+                return self._forward_waves(hs, decode_rows)
+            # consecutive envelope-sized chunks, as the reference's piecewise
+            # mode requires of the batch (max_num_batched_tokens = slots //
+            # topk): every chunk is a single-wave gap plus fused experts
             return torch.cat([self._forward_step(c) for c in hs.split(thr)])
         return self._forward_step(hs)
+
+    def _forward_waves(self, hs: torch.Tensor, decode_rows: int) -> torch.Tensor:
+        """plan waves -> wave 0 (resident experts || its fills, then the
+        filled ones, the shared experts) -> waves 1.. (each after its fills,
+        which stream while the previous wave computes) -> bf16."""
+        c, cfg = self.cache, self.cfg
+        hs = hs.contiguous()
+        T, H = hs.shape
+        tw, ti, logits = self.router.route(hs)
+        self.last_ids, self.last_logits = ti, logits
+        main, side = torch.cuda.current_stream(), self._side
+        c.plan_waves(ti, decode_rows)
+        n_sh = 0 if self.shared_w13 is None else self.shared_w13.shape[0]
+        ws = ops.fused_experts_workspace(T, ti.shape[1], H, c.w13.shape[1] // 2, c.num_slots,
+                                         n_sh, hs.device)
+        acc = torch.empty(T, H, dtype=torch.float32, device=hs.device)
+        MW = c.max_waves
+        filled = [torch.cuda.Event() for _ in range(MW)]
+        computed = [torch.cuda.Event() for _ in range(MW)]
+
+        def stream(k: int) -> None:
+            with torch.cuda.stream(side):
+                c.stream_wave(k, self.stream_ctas)
+                filled[k].record(side)
+
+        side.wait_stream(main)
+        stream(0)
+        scale = cfg.routed_scaling_factor
+        args = (hs, c.w13, c.w2, tw, ti, c.wave_map(0))
+        kw = dict(shared_w13=self.shared_w13, shared_w2=self.shared_w2, shared_t0=0,
+                  shared_nt=T, routed_scaling_factor=scale, out=acc, w1_scale=c.w13_scale,
+                  w2_scale=c.w2_scale, shared_w13_scale=self.shared_w13_scale,
+                  shared_w2_scale=self.shared_w2_scale, slot_state=c.state, workspace=ws)
+        ops.fused_experts_partial(*args, phase=0, **kw)
+        main.wait_event(filled[0])
+        ops.fused_experts_partial(*args, phase=1, **kw)
+        computed[0].record(main)
+        # wave k refills the slots wave k - 2 read (ping-pong) or, with a
+        # single rotation group, wave k - 1's; waves 1 and 2 follow wave 0
+        lag = 2 if c.waves_pingpong else 1
+        for k in range(1, min(1 + lag, MW)):
+            side.wait_event(computed[0])
+            stream(k)
+        for k in range(1, MW):
+            main.wait_event(filled[k])
+            ops.fused_experts_accumulate(hs, c.w13, c.w2, tw, ti, c.wave_map(k), acc, ws,
+                                         routed_scaling_factor=scale, w1_scale=c.w13_scale,
+                                         w2_scale=c.w2_scale)
+            computed[k].record(main)
+            if k + lag < MW:
+                side.wait_event(computed[k])
+                stream(k + lag)
+        main.wait_stream(side)
+        return acc.to(torch.bfloat16)
 
     def _forward_step(self, hs: torch.Tensor) -> torch.Tensor:
         tw, ti, logits = self.router.route(hs)

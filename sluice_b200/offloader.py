@@ -16,6 +16,10 @@ path (kfirtoledo/sluice ``src/sluice/offloader.py``):
   (2362-2467) on the device: the planner kernel updates the SLRU state and the
   standing expert map in place, the streamer kernel copies the misses from
   the mapped host store into their slots. No device-to-host synchronisation.
+* ``SlotCache.plan_waves`` / ``stream_wave`` / ``wave_map`` — steps beyond
+  the envelope, which the reference sends through its classic hook
+  (``run_moe`` 1452-1764, ``_run_waves`` 1846-1933): the same state planned
+  in expert waves on the device, each wave with its own fills and map.
 
 Buffers are allocated once and never reallocated (captured CUDA graphs bake
 pointers); a gap rewrites their contents only.
@@ -56,6 +60,26 @@ def protected_cap_for(num_slots: int, protect_frac: float) -> int:
     """``min(int(slots * frac), slots - 1)`` with frac clamped to [0, 0.9]."""
     frac = min(max(float(protect_frac), 0.0), 0.9)
     return max(min(int(num_slots * frac), num_slots - 1), 0)
+
+
+def max_waves_for(num_slots: int, local_n: int, protected_cap: int, n_pinned: int) -> int:
+    """An upper bound on the expert waves of one step (sl_plan_waves).
+
+    When a miss finds no slot the free list is empty and the protected
+    segment holds at most ``protected_cap`` slots, so the probation segment
+    (the rotation) holds ``r >= num_slots - n_pinned - protected_cap``; wave 0
+    claimed all of it, and every later wave takes a rotation group of at
+    least ``r // 2`` slots (``_run_waves``, offloader.py:1856-1886)."""
+    r = max(num_slots - n_pinned - protected_cap, 1)
+    left = max(local_n - r, 0)
+    g = max(r // 2, 1)
+    return 1 + (left + g - 1) // g
+
+
+def waves_pingpong(num_slots: int, protected_cap: int, n_pinned: int) -> bool:
+    """Whether every wave step rotates two non-empty groups (so wave k's fills
+    only wait for wave k - 2's GEMMs): a rotation of two or more slots."""
+    return num_slots - n_pinned - protected_cap >= 2
 
 
 @dataclass
@@ -134,7 +158,7 @@ class SlotCache:
     def __init__(self, num_slots: int, local_n: int, global_n: int, local_of: list,
                  protected_cap: int, static_full: bool, device: torch.device,
                  gpu_cache: dict, cpu_store: dict, expert_map: torch.Tensor,
-                 state: torch.Tensor | None, bytes_per_expert: int):
+                 state: torch.Tensor | None, bytes_per_expert: int, n_pinned: int = 0):
         self.num_slots = num_slots
         self.local_n = local_n
         self.global_n = global_n
@@ -164,6 +188,21 @@ class SlotCache:
             hs = (ctypes.c_size_t * n)(*[cpu_store[k].stride(0) * cpu_store[k].element_size()
                                          for k in names])
             self._stream_args = (n, src, dst, nb, hs)
+            # the wave plan of steps beyond the envelope (sl_plan_waves)
+            self.max_waves = max_waves_for(num_slots, local_n, protected_cap, n_pinned)
+            self.waves_pingpong = waves_pingpong(num_slots, protected_cap, n_pinned)
+            nbytes = lib().sl_wave_plan_bytes(num_slots, global_n, self.max_waves)
+            self.waves = torch.empty(nbytes, dtype=torch.uint8, device=device)
+            check(lib().sl_wave_plan_init(ptr(self.waves), num_slots, global_n, self.max_waves,
+                                          torch.cuda.current_stream(device).cuda_stream),
+                  "sl_wave_plan_init")
+            woff = (ctypes.c_size_t * (_lib.WAVE_NFIELDS + 1))()
+            check(lib().sl_wave_plan_offsets(num_slots, global_n, self.max_waves, woff),
+                  "sl_wave_plan_offsets")
+            self.wave_offsets = list(woff)
+            words = self.waves.view(torch.int32)
+            self.wave_maps = words[woff[4] // 4: woff[4] // 4 + self.max_waves * global_n] \
+                .view(self.max_waves, global_n)
 
     @property
     def w13(self) -> torch.Tensor:
@@ -204,6 +243,52 @@ class SlotCache:
                                               torch.cuda.current_stream().cuda_stream),
               "sl_stream_experts_strided")
 
+    # -- steps beyond the envelope: expert waves -----------------------------
+    def plan_waves(self, topk_ids: torch.Tensor, decode_rows: int = 0) -> None:
+        """Plan this step's expert waves on the current stream (run_moe and
+        _run_waves, offloader.py:1452-1764, 1846-1933): ``topk_ids`` [T, k];
+        ``decode_rows`` > 0 marks rows [0, decode_rows) as decodes, 0 leaves
+        the class to the working-set heuristic, < 0 makes every expert
+        scan-class."""
+        ids = topk_ids if topk_ids.dtype == torch.int32 and topk_ids.is_contiguous() \
+            else topk_ids.contiguous().to(torch.int32)
+        T, k = ids.shape
+        check(lib().sl_plan_waves(ptr(self.state), ptr(ids), T, k, int(decode_rows),
+                                  ptr(self.expert_map), ptr(self.waves),
+                                  torch.cuda.current_stream().cuda_stream), "sl_plan_waves")
+
+    def stream_wave(self, wave: int, stream_ctas: int = 0) -> None:
+        """Stream wave ``wave``'s fills of the last wave plan (current stream)."""
+        n, src, dst, nb, hs = self._stream_args
+        check(lib().sl_stream_wave(ptr(self.waves), int(wave), n, src, dst, nb, hs,
+                                   int(stream_ctas), torch.cuda.current_stream().cuda_stream),
+              "sl_stream_wave")
+
+    def wave_map(self, wave: int) -> torch.Tensor:
+        """Wave ``wave``'s expert map (int32 [global_n], a view of the plan)."""
+        return self.wave_maps[wave]
+
+    def wave_plan(self) -> list[dict]:
+        """The last wave plan as ``[{"map": [(global, slot)], "fills":
+        [(local, slot)]}]`` (synchronises; for tests)."""
+        words = self.waves.view(torch.int32).cpu().numpy()
+        o = [v // 4 for v in self.wave_offsets]
+        S, G = self.num_slots, self.global_n
+        nw = int(words[_lib.WAVE_HDR["num_waves"]])
+        out = []
+        for k in range(nw):
+            c = int(words[o[1] + k])
+            loc = words[o[2] + k * S: o[2] + k * S + c].tolist()
+            slot = words[o[3] + k * S: o[3] + k * S + c].tolist()
+            m = words[o[4] + k * G: o[4] + (k + 1) * G]
+            out.append({"map": [(g, int(m[g])) for g in range(G) if m[g] >= 0],
+                        "fills": list(zip(loc, slot))})
+        return out
+
+    def wave_header(self) -> dict:
+        h = self.waves[:64].view(torch.int32).cpu().tolist()
+        return {k: int(h[v]) for k, v in _lib.WAVE_HDR.items()}
+
     # -- host-side views (synchronise) ----------------------------------------
     def _field(self, i: int, dtype, count: int) -> np.ndarray:
         b = self.state[self.offsets[i]: self.offsets[i] + count * np.dtype(dtype).itemsize]
@@ -214,7 +299,7 @@ class SlotCache:
         return {k: int(h[v]) for k, v in HDR.items()}
 
     def counters(self) -> dict:
-        c = self._field(1, np.uint64, 8)
+        c = self._field(1, np.uint64, _lib.NUM_COUNTERS)
         return {k: int(c[v]) for k, v in CNT.items()}
 
     def check(self) -> None:
@@ -378,7 +463,8 @@ class ExpertStreamOffloader:
             for name in params:
                 gpu_cache[name][slot].copy_(cpu_store[name][loc])
         cache = SlotCache(S, local_n, global_n, local_of, init.protected_cap, False, device,
-                          gpu_cache, cpu_store, emap, state, bpe)
+                          gpu_cache, cpu_store, emap, state, bpe,
+                          n_pinned=sum(1 for v in init.seg if v == SEG_PINNED))
         self.caches.append(cache)
         return cache
 

@@ -129,7 +129,7 @@ def fused_experts_workspace(T: int, topk: int, H: int, I: int, slots: int, n_sha
 def _fused_ex(hs, w1, w2, topk_weights, topk_ids, expert_map, global_n, *, w1_scale=None,
               w2_scale=None, shared_w13=None, shared_w2=None, shared_w13_scale=None,
               shared_w2_scale=None, routed_scaling_factor=1.0, shared_t0=0, shared_nt=-1,
-              slot_state=None, phase=-1, out_f32=False, out=None, workspace=None):
+              slot_state=None, phase=-1, out_f32=0, out=None, workspace=None):
     _need_cuda(hs, w1, w2, topk_weights, topk_ids, expert_map)
     hs = hs.contiguous()
     if hs.dtype != torch.bfloat16:
@@ -230,11 +230,27 @@ def fused_experts_partial(hidden_states, w1, w2, topk_weights, topk_ids, expert_
                      shared_w13=shared_w13, shared_w2=shared_w2,
                      shared_w13_scale=shared_w13_scale, shared_w2_scale=shared_w2_scale,
                      routed_scaling_factor=routed_scaling_factor, shared_t0=shared_t0,
-                     shared_nt=shared_nt, out_f32=True, out=out, slot_state=slot_state,
+                     shared_nt=shared_nt, out_f32=1, out=out, slot_state=slot_state,
                      phase=phase, workspace=workspace)
 
 
 fused_experts_partial.last_workspace = None
+
+
+def fused_experts_accumulate(hidden_states, w1, w2, topk_weights, topk_ids, expert_map,
+                             out: torch.Tensor, workspace: torch.Tensor,
+                             routed_scaling_factor: float = 1.0, w1_scale=None,
+                             w2_scale=None) -> torch.Tensor:
+    """``out`` [T, H] fp32 += the routed experts ``expert_map`` maps, scaled
+    by ``routed_scaling_factor`` (no shared experts): one expert wave of a
+    step beyond the envelope, whose waves sum to the step's output
+    (``_run_waves``, offloader.py:1920-1933)."""
+    if out.dtype != torch.float32:
+        raise ValueError("the wave accumulator is fp32")
+    return _fused_ex(hidden_states, w1, w2, topk_weights, topk_ids, expert_map,
+                     expert_map.numel(), w1_scale=w1_scale, w2_scale=w2_scale,
+                     routed_scaling_factor=routed_scaling_factor, out_f32=2, out=out,
+                     workspace=workspace)
 
 
 def workspace_status(ws: torch.Tensor) -> int:

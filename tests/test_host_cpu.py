@@ -67,6 +67,18 @@ def test_host_calls_reject_bad_arguments_without_a_gpu():
                             None, None, None, None) == _lib.SL_ERR_INVALID
     assert L.sl_ep_combine(None, 8, 2048, 0, 0, None, None, None, None, None, None,
                            None) == _lib.SL_ERR_INVALID
+    # expert waves: layout and argument checks
+    offs = (ctypes.c_size_t * (_lib.WAVE_NFIELDS + 1))()
+    assert L.sl_wave_plan_offsets(48, 64, 7, offs) == 0
+    assert list(offs) == [0, 64, 96, 96 + 7 * 48 * 4, 96 + 2 * 7 * 48 * 4,
+                          96 + 2 * 7 * 48 * 4 + 7 * 64 * 4]
+    assert L.sl_wave_plan_bytes(48, 64, 7) == offs[_lib.WAVE_NFIELDS]
+    assert all(v % 16 == 0 for v in offs)
+    assert L.sl_wave_plan_bytes(0, 64, 7) == 0 and L.sl_wave_plan_bytes(48, 64, 0) == 0
+    assert L.sl_wave_plan_offsets(48, 64, 0, offs) == _lib.SL_ERR_INVALID
+    assert L.sl_wave_plan_init(None, 48, 64, 7, None) == _lib.SL_ERR_INVALID
+    assert L.sl_plan_waves(None, None, 8, 6, 0, None, None, None) == _lib.SL_ERR_INVALID
+    assert L.sl_stream_wave(None, 0, 2, None, None, None, None, 0, None) == _lib.SL_ERR_INVALID
     # fp8 through the general entry without weights or block scales: refused
     # before anything is dereferenced
     w = _lib.ExpertWeights()

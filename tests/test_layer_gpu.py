@@ -146,15 +146,17 @@ def test_fp8_v3_routing_layer_with_streaming(packed):
 
 
 def test_prefill_sized_step_runs_in_envelope_chunks():
-    """A step larger than slots // topk runs as envelope-sized chunks; the
-    slot map then equals the oracle's after the same chunked gaps."""
+    """With beyond_envelope="chunks", a step larger than slots // topk runs as
+    envelope-sized chunks; the slot map then equals the oracle's after the
+    same chunked gaps."""
     cfg = configs.V2_LITE
     w13, w2 = synth.layer_weights(cfg, 1, seed=12, device="cuda")
     gw, lb, sb = synth.gate_params(cfg, 1, seed=12, device="cuda")
     sh13, sh2 = synth.shared_weights(cfg, 1, seed=12, device="cuda")
     cache = ExpertStreamOffloader(48, protect_frac=0.5, fast_hit=True).install_layer(
         w13, w2, device="cuda")
-    layer = SluiceMoELayer(cfg, ops.Router(cfg.routing, gw, lb, sb), cache, sh13, sh2)
+    layer = SluiceMoELayer(cfg, ops.Router(cfg.routing, gw, lb, sb), cache, sh13, sh2,
+                           beyond_envelope="chunks")
     assert layer.envelope == 8
     g = torch.Generator().manual_seed(13)
     x = torch.randn(29, cfg.hidden, generator=g).to(torch.bfloat16)

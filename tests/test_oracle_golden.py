@@ -16,6 +16,7 @@ import torch
 from oracle import moe as omoe
 from oracle import routing as orouting
 from oracle.slot_policy import PROBATION, PROTECTED, SlotOverflow, SlotPolicyModel
+from sluice_b200.offloader import max_waves_for, waves_pingpong
 
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
 
@@ -101,8 +102,10 @@ def test_wave_planning_matches_reference_run_moe(sc):
     m = model_for(sc)
     assert m.protected_cap == sc["protected_cap"]
     n_pinned = len(sc["pinned_slots"])
-    bound = SlotPolicyModel.max_waves(m.num_slots, m.local_n, m.protected_cap, n_pinned)
-    pipelined = SlotPolicyModel.waves_pipelined(m.num_slots, m.protected_cap, n_pinned)
+    # the product's wave-buffer bound and ping-pong claim hold on the
+    # reference's own plans
+    bound = max_waves_for(m.num_slots, m.local_n, m.protected_cap, n_pinned)
+    pipelined = waves_pingpong(m.num_slots, m.protected_cap, n_pinned)
     for i, exp in enumerate(sc["trace"]):
         waves = replay_wave_step(m, exp)
         where = (sc["name"], i)
@@ -132,8 +135,7 @@ def test_wave_golden_covers_edge_cases():
     names = {s["name"]: s for s in _wave_scenarios()}
     nw = lambda n: [len(r["waves"]) for r in names[n]["trace"] if r["kind"] == "moe"]
     assert max(nw("s8_frac09_one_slot_rotation")) > 8        # one-slot groups, not ping-pong
-    assert not SlotPolicyModel.waves_pipelined(8, names["s8_frac09_one_slot_rotation"]
-                                               ["protected_cap"], 0)
+    assert not waves_pingpong(8, names["s8_frac09_one_slot_rotation"]["protected_cap"], 0)
     assert max(nw("v2lite_mixed")) >= 3 and max(nw("qwen3_s64_mixed")) >= 5
     assert nw("no_owned_ids") == [1]
     assert names["v2lite_pins_prefill"]["pinned_slots"] and names["v2lite_lfu_mixed"]["lfu"]
