@@ -78,7 +78,13 @@ class SluiceMoELayer:
             # consecutive envelope-sized chunks, as the reference's piecewise
             # mode requires of the batch (max_num_batched_tokens = slots //
             # topk): every chunk is a single-wave gap plus fused experts
-            return torch.cat([self._forward_step(c) for c in hs.split(thr)])
+            outs, ids, logits = [], [], []
+            for c in hs.split(thr):
+                outs.append(self._forward_step(c))
+                ids.append(self.last_ids)
+                logits.append(self.last_logits)
+            self.last_ids, self.last_logits = torch.cat(ids), torch.cat(logits)
+            return torch.cat(outs)
         return self._forward_step(hs)
 
     def _forward_waves(self, hs: torch.Tensor, decode_rows: int) -> torch.Tensor:

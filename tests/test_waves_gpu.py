@@ -89,9 +89,11 @@ def test_wave_planner_matches_reference_run_moe(sc):
             assert snap["freq"] == exp["freq"], where
 
 
-def _layer(cfg, slots, seed, fp8=False, beyond="waves"):
+def _layer(cfg, slots, seed, fp8=False, beyond="waves", zipf_bias=0.0):
+    """A layer whose router has no popularity skew by default, so prefill
+    working sets exceed the slots and steps spill into several waves."""
     w13, w2 = synth.layer_weights(cfg, 0, seed=seed, device="cuda")
-    gw, lb, sb = synth.gate_params(cfg, 0, seed=seed, device="cuda")
+    gw, lb, sb = synth.gate_params(cfg, 0, seed=seed, device="cuda", zipf_bias=zipf_bias)
     sh13, sh2 = synth.shared_weights(cfg, 0, seed=seed, device="cuda")
     off = ExpertStreamOffloader(slots, protect_frac=0.5, fast_hit=True)
     kw, host = {}, {"w13": w13.cpu(), "w2": w2.cpu(), "sh13": sh13, "sh2": sh2}
@@ -201,7 +203,7 @@ def test_waves_and_chunks_agree():
     assert a.cache.wave_header()["num_waves"] >= 2
     assert_moe_close(oa, ob)
     # waves stream each missing expert once; chunks re-stream across chunks
-    assert a.cache.stats()["fills"] <= b.cache.stats()["fills"]
+    assert a.cache.stats()["fills"] < b.cache.stats()["fills"]
 
 
 def test_wave_step_graph_replay_equals_eager():
