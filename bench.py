@@ -418,6 +418,32 @@ def _step_bytes(stack, cfg):
     return tot
 
 
+def layer_launches(cfg, tokens, world, slots, exchange="nvlink", no_overlap=False) -> int:
+    """This build's kernel launches per MoE layer and step, following the
+    launch rules of the host code: gate + select; a fused-experts call is its
+    token grouping (one kernel for up to 1024 bf16 pairs, else grouping +
+    gather; fp8: grouping + quantising gather), the gate/up and down GEMMs and
+    the combine (a phase-0 call stops before the combine; its phase 1 runs
+    the GEMMs again and the combine); an offloaded gap adds plan + stream; a
+    step beyond the envelope runs max_waves waves (one plan, a stream per
+    wave, wave 0 split in two phases, the rest whole calls); the NVLink
+    exchange adds dispatch + combine."""
+    from sluice_b200.offloader import max_waves_for, protected_cap_for
+
+    local_n = cfg.num_experts // world
+    k = cfg.routing.topk
+    fp8 = cfg.weight_dtype == "fp8"
+    align = 2 if fp8 or tokens * world * k > 1024 else 1
+    ex = 2 if world > 1 and exchange == "nvlink" else 0
+    if slots >= local_n:
+        return 2 + align + 3 + ex
+    S = min(slots, local_n)
+    if tokens > max(1, S // k // world):
+        mw = max_waves_for(S, min(local_n, tokens * world * k), protected_cap_for(S, 0.5), 0)
+        return 2 + 1 + mw + (align + 5) + (mw - 1) * (align + 3) + ex
+    return 2 + 2 + (align + 3 if no_overlap else align + 5) + ex
+
+
 def run_sluice(a):
     import datetime
 
@@ -585,16 +611,7 @@ def run_sluice(a):
                "sample": f"{n} full decode steps ({layers} layers, c={T}) of the torch-native "
                          f"CPU path (oracle routing + slot policy + MoE), median"}
 
-    local_n = cfg.num_experts // world
-    offloaded = a.slots < local_n
-    # per layer: gate, select, [plan, stream,] align, gate/up GEMM, down GEMM,
-    # combine; the overlapped gap runs both GEMMs twice (resident experts, then
-    # the streamed ones); + dispatch and combine kernels under the NVLink exchange
-    # fp8 weights add the quantising token gather
-    per_layer = (6 if not offloaded else 10 if not a.no_overlap else 8) + \
-        (2 if world > 1 and a.exchange == "nvlink" else 0) + \
-        (1 if cfg.weight_dtype == "fp8" else 0)
-    launches = K * layers * per_layer
+    launches = K * layers * layer_launches(cfg, T, world, a.slots, a.exchange, a.no_overlap)
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",

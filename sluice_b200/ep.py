@@ -27,6 +27,7 @@ import torch
 import torch.distributed as dist
 
 from . import ops
+from .layer import expert_waves
 from .configs import MoEConfig
 
 
@@ -167,8 +168,13 @@ class EPMoELayer:
     def __init__(self, cfg: MoEConfig, router: ops.Router, cache, shared_w13, shared_w2,
                  group=None, shared_w13_scale=None, shared_w2_scale=None,
                  exchange: "NvlinkExchange | None" = None, overlap: bool = True,
-                 stream_ctas: int = 16):
+                 stream_ctas: int = 16, beyond_envelope: str = "waves"):
+        if beyond_envelope not in ("waves", "chunks"):
+            raise ValueError("beyond_envelope is 'waves' or 'chunks'")
         self.cfg = cfg
+        # steps whose gathered rows exceed the envelope: expert waves over
+        # the gathered rows, or envelope-sized token chunks through the gap
+        self.beyond_envelope = beyond_envelope
         self.exchange = exchange  # None: NCCL all-gather / reduce-scatter
         self.shared_w13_scale = shared_w13_scale
         self.shared_w2_scale = shared_w2_scale
@@ -183,7 +189,8 @@ class EPMoELayer:
         # overlap the gap's expert stream with the resident experts' GEMMs
         self.overlap = overlap and not cache.static_full
         self.stream_ctas = stream_ctas
-        self._side = torch.cuda.Stream(device=cache.device) if self.overlap else None
+        self._side = torch.cuda.Stream(device=cache.device) \
+            if not cache.static_full else None
 
     @property
     def envelope(self) -> int:
@@ -195,18 +202,31 @@ class EPMoELayer:
             return 1 << 30
         return max(1, self.cache.num_slots // self.cfg.routing.topk // self.world)
 
-    def forward(self, x: torch.Tensor, add_residual: bool = False) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, add_residual: bool = False,
+                decode: bool = True) -> torch.Tensor:
         """This rank's MoE output for its tokens ``x``; ``add_residual``
         returns ``x + output`` (the decoder's residual add; folded into the
-        combine kernel under the NVLink exchange). Steps larger than the
-        envelope run as envelope-sized chunks (every rank the same number:
-        every rank steps the same token count)."""
+        combine kernel under the NVLink exchange). Every rank steps the same
+        token count. A step whose rows exceed the envelope runs in expert
+        waves over the gathered rows (decode steps decode-class; ``decode=False``
+        plans a scan, as the reference's data-parallel mode classifies every
+        step it plans in its hook); it is split only where it exceeds the
+        exchange's capacity. With ``beyond_envelope="chunks"`` such steps run
+        as envelope-sized chunks through the gap instead."""
         thr = self.envelope
-        if x.shape[0] > thr:
-            return torch.cat([self._forward_step(c, add_residual) for c in x.split(thr)])
-        return self._forward_step(x, add_residual)
+        if self.beyond_envelope == "chunks" or self.cache.static_full:
+            if x.shape[0] > thr:
+                return torch.cat([self._forward_step(c, add_residual, decode)
+                                  for c in x.split(thr)])
+            return self._forward_step(x, add_residual, decode)
+        cap = self.exchange.max_tokens if self.exchange is not None else x.shape[0]
+        if x.shape[0] > cap:
+            return torch.cat([self._forward_step(c, add_residual, decode)
+                              for c in x.split(cap)])
+        return self._forward_step(x, add_residual, decode)
 
-    def _forward_step(self, x: torch.Tensor, add_residual: bool) -> torch.Tensor:
+    def _forward_step(self, x: torch.Tensor, add_residual: bool,
+                      decode: bool = True) -> torch.Tensor:
         T = x.shape[0]
         tw, ti, _ = self.router.route(x)
         if self.exchange is not None:
@@ -220,7 +240,13 @@ class EPMoELayer:
                   w2_scale=c.w2_scale, shared_w13_scale=self.shared_w13_scale,
                   shared_w2_scale=self.shared_w2_scale)
         args = (xg, c.w13, c.w2, twg, tig, c.expert_map, self.shared_w13, self.shared_w2)
-        if self.overlap:
+        if T > self.envelope:
+            # the gathered rows' working set can exceed the slots: waves
+            part = expert_waves(c, self._side, xg, twg, tig, tig.shape[0] if decode else -1,
+                                self.shared_w13, self.shared_w2, self.rank * T, T,
+                                self.cfg.routed_scaling_factor, self.shared_w13_scale,
+                                self.shared_w2_scale, self.stream_ctas)
+        elif self.overlap:
             # plan -> [stream on a side stream || resident experts] -> streamed experts
             main = torch.cuda.current_stream()
             c.plan(tig)

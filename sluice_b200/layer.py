@@ -29,6 +29,67 @@ from .configs import MoEConfig
 from .offloader import ExpertStreamOffloader, SlotCache
 
 
+def expert_waves(c: SlotCache, side: torch.cuda.Stream, hs: torch.Tensor, tw: torch.Tensor,
+                 ti: torch.Tensor, decode_rows: int, shared_w13, shared_w2, shared_t0: int,
+                 shared_nt: int, scale: float, shared_w13_scale=None, shared_w2_scale=None,
+                 stream_ctas: int = 16) -> torch.Tensor:
+    """One step of ``hs`` [T, H] (routed as ``tw`` / ``ti``) in expert waves
+    over the cache ``c``; returns the fp32 output [T, H]: the routed experts
+    scaled by ``scale`` plus the shared experts on rows [shared_t0, shared_t0
+    + shared_nt).
+
+    plan waves -> wave 0 (resident experts || its fills, then the filled
+    ones and the shared experts) -> waves 1.. (each after its fills, which
+    stream on ``side`` while the previous wave computes). A fixed number of
+    waves is issued for the step's size (``c.waves_for``; waves past the
+    plan's count do no work), so the step captures in a CUDA graph.
+    """
+    main = torch.cuda.current_stream()
+    T, H = hs.shape
+    c.plan_waves(ti, decode_rows)
+    n_sh = 0 if shared_w13 is None else shared_w13.shape[0]
+    ws = ops.fused_experts_workspace(T, ti.shape[1], H, c.w13.shape[1] // 2, c.num_slots,
+                                     n_sh, hs.device)
+    acc = torch.empty(T, H, dtype=torch.float32, device=hs.device)
+    MW = c.waves_for(ti.numel())
+    filled = [torch.cuda.Event() for _ in range(MW)]
+    computed = [torch.cuda.Event() for _ in range(MW)]
+
+    def stream(k: int) -> None:
+        with torch.cuda.stream(side):
+            c.stream_wave(k, stream_ctas)
+            filled[k].record(side)
+
+    side.wait_stream(main)
+    stream(0)
+    args = (hs, c.w13, c.w2, tw, ti, c.wave_map(0))
+    kw = dict(shared_w13=shared_w13, shared_w2=shared_w2, shared_t0=shared_t0,
+              shared_nt=shared_nt, routed_scaling_factor=scale, out=acc, w1_scale=c.w13_scale,
+              w2_scale=c.w2_scale, shared_w13_scale=shared_w13_scale,
+              shared_w2_scale=shared_w2_scale, slot_state=c.state, workspace=ws)
+    ops.fused_experts_partial(*args, phase=0, **kw)
+    main.wait_event(filled[0])
+    ops.fused_experts_partial(*args, phase=1, **kw)
+    computed[0].record(main)
+    # wave k refills the slots wave k - 2 read (ping-pong) or, with a single
+    # rotation group, wave k - 1's; waves 1 and 2 follow wave 0
+    lag = 2 if c.waves_pingpong else 1
+    for k in range(1, min(1 + lag, MW)):
+        side.wait_event(computed[0])
+        stream(k)
+    for k in range(1, MW):
+        main.wait_event(filled[k])
+        ops.fused_experts_accumulate(hs, c.w13, c.w2, tw, ti, c.wave_map(k), acc, ws,
+                                     routed_scaling_factor=scale, w1_scale=c.w13_scale,
+                                     w2_scale=c.w2_scale)
+        computed[k].record(main)
+        if k + lag < MW:
+            side.wait_event(computed[k])
+            stream(k + lag)
+    main.wait_stream(side)
+    return acc
+
+
 class SluiceMoELayer:
     def __init__(self, cfg: MoEConfig, router: ops.Router, cache: SlotCache,
                  shared_w13: torch.Tensor | None, shared_w2: torch.Tensor | None,
@@ -88,57 +149,13 @@ class SluiceMoELayer:
         return self._forward_step(hs)
 
     def _forward_waves(self, hs: torch.Tensor, decode_rows: int) -> torch.Tensor:
-        """plan waves -> wave 0 (resident experts || its fills, then the
-        filled ones, the shared experts) -> waves 1.. (each after its fills,
-        which stream while the previous wave computes) -> bf16."""
-        c, cfg = self.cache, self.cfg
         hs = hs.contiguous()
-        T, H = hs.shape
         tw, ti, logits = self.router.route(hs)
         self.last_ids, self.last_logits = ti, logits
-        main, side = torch.cuda.current_stream(), self._side
-        c.plan_waves(ti, decode_rows)
-        n_sh = 0 if self.shared_w13 is None else self.shared_w13.shape[0]
-        ws = ops.fused_experts_workspace(T, ti.shape[1], H, c.w13.shape[1] // 2, c.num_slots,
-                                         n_sh, hs.device)
-        acc = torch.empty(T, H, dtype=torch.float32, device=hs.device)
-        MW = c.max_waves
-        filled = [torch.cuda.Event() for _ in range(MW)]
-        computed = [torch.cuda.Event() for _ in range(MW)]
-
-        def stream(k: int) -> None:
-            with torch.cuda.stream(side):
-                c.stream_wave(k, self.stream_ctas)
-                filled[k].record(side)
-
-        side.wait_stream(main)
-        stream(0)
-        scale = cfg.routed_scaling_factor
-        args = (hs, c.w13, c.w2, tw, ti, c.wave_map(0))
-        kw = dict(shared_w13=self.shared_w13, shared_w2=self.shared_w2, shared_t0=0,
-                  shared_nt=T, routed_scaling_factor=scale, out=acc, w1_scale=c.w13_scale,
-                  w2_scale=c.w2_scale, shared_w13_scale=self.shared_w13_scale,
-                  shared_w2_scale=self.shared_w2_scale, slot_state=c.state, workspace=ws)
-        ops.fused_experts_partial(*args, phase=0, **kw)
-        main.wait_event(filled[0])
-        ops.fused_experts_partial(*args, phase=1, **kw)
-        computed[0].record(main)
-        # wave k refills the slots wave k - 2 read (ping-pong) or, with a
-        # single rotation group, wave k - 1's; waves 1 and 2 follow wave 0
-        lag = 2 if c.waves_pingpong else 1
-        for k in range(1, min(1 + lag, MW)):
-            side.wait_event(computed[0])
-            stream(k)
-        for k in range(1, MW):
-            main.wait_event(filled[k])
-            ops.fused_experts_accumulate(hs, c.w13, c.w2, tw, ti, c.wave_map(k), acc, ws,
-                                         routed_scaling_factor=scale, w1_scale=c.w13_scale,
-                                         w2_scale=c.w2_scale)
-            computed[k].record(main)
-            if k + lag < MW:
-                side.wait_event(computed[k])
-                stream(k + lag)
-        main.wait_stream(side)
+        acc = expert_waves(self.cache, self._side, hs, tw, ti, decode_rows,
+                           self.shared_w13, self.shared_w2, 0, hs.shape[0],
+                           self.cfg.routed_scaling_factor, self.shared_w13_scale,
+                           self.shared_w2_scale, self.stream_ctas)
         return acc.to(torch.bfloat16)
 
     def _forward_step(self, hs: torch.Tensor) -> torch.Tensor:

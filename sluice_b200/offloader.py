@@ -63,7 +63,8 @@ def protected_cap_for(num_slots: int, protect_frac: float) -> int:
 
 
 def max_waves_for(num_slots: int, local_n: int, protected_cap: int, n_pinned: int) -> int:
-    """An upper bound on the expert waves of one step (sl_plan_waves).
+    """An upper bound on the expert waves of one step (sl_plan_waves) that
+    selects at most ``local_n`` of this rank's experts.
 
     When a miss finds no slot the free list is empty and the protected
     segment holds at most ``protected_cap`` slots, so the probation segment
@@ -189,6 +190,7 @@ class SlotCache:
                                          for k in names])
             self._stream_args = (n, src, dst, nb, hs)
             # the wave plan of steps beyond the envelope (sl_plan_waves)
+            self.n_pinned = n_pinned
             self.max_waves = max_waves_for(num_slots, local_n, protected_cap, n_pinned)
             self.waves_pingpong = waves_pingpong(num_slots, protected_cap, n_pinned)
             nbytes = lib().sl_wave_plan_bytes(num_slots, global_n, self.max_waves)
@@ -256,6 +258,12 @@ class SlotCache:
         check(lib().sl_plan_waves(ptr(self.state), ptr(ids), T, k, int(decode_rows),
                                   ptr(self.expert_map), ptr(self.waves),
                                   torch.cuda.current_stream().cuda_stream), "sl_plan_waves")
+
+    def waves_for(self, pairs: int) -> int:
+        """The waves a step of ``pairs`` (token, expert) pairs can need: it
+        selects at most ``min(local_n, pairs)`` experts."""
+        return min(self.max_waves, max_waves_for(self.num_slots, min(self.local_n, pairs),
+                                                 self.protected_cap, self.n_pinned))
 
     def stream_wave(self, wave: int, stream_ctas: int = 0) -> None:
         """Stream wave ``wave``'s fills of the last wave plan (current stream)."""

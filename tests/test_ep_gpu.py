@@ -80,7 +80,7 @@ def _v3_mini():
                                       use_grouped_topk=True, has_score_bias=True))
 
 
-def _rank_main_fp8(rank, world, port, out_dir):
+def _rank_main_fp8(rank, world, port, out_dir, slots=48):
     import torch.distributed as dist
 
     from oracle import moe as omoe
@@ -96,7 +96,7 @@ def _rank_main_fp8(rank, world, port, out_dir):
     stack = None
     try:
         cfg = _v3_mini()
-        stack = ep.EPDecodeStack(cfg, slots=48, seed=4, num_layers=1)
+        stack = ep.EPDecodeStack(cfg, slots=slots, seed=4, num_layers=1)
         layer = stack.layers[0]
         prm = {k: v.cpu() for k, v in synth.layer_params(cfg, 0, 4, device="cuda").items()}
         sh = {k: v.cpu() for k, v in synth.shared_params(cfg, 0, 4, device="cuda").items()}
@@ -128,17 +128,20 @@ def _rank_main_fp8(rank, world, port, out_dir):
         dist.destroy_process_group()
 
 
-def test_ep2_fp8_v3_style_layer_matches_oracle(tmp_path):
+@pytest.mark.parametrize("slots", [48, 16], ids=["resident", "offloaded-waves"])
+def test_ep2_fp8_v3_style_layer_matches_oracle(tmp_path, slots):
     """fp8 block-scaled experts, sigmoid grouped routing and routed scaling
-    under expert parallelism (NVLink exchange): within the fp8 tolerance."""
-    mp.start_processes(_rank_main_fp8, args=(2, _free_port(), str(tmp_path)), nprocs=2,
-                       start_method="spawn")
+    under expert parallelism (NVLink exchange): within the fp8 tolerance.
+    16 slots of 32 local experts: 8 tokens per rank exceed the envelope, so
+    the gathered rows run in expert waves (weights and scales streamed)."""
+    mp.start_processes(_rank_main_fp8, args=(2, _free_port(), str(tmp_path), slots),
+                       nprocs=2, start_method="spawn")
     for r in range(2):
         errs = torch.load(os.path.join(tmp_path, f"errf{r}.pt"))
         assert (errs < 5e-2).all(), errs
 
 
-def _agree_main(rank, world, port, out_dir):
+def _agree_main(rank, world, port, out_dir, slots=48):
     import torch.distributed as dist
 
     from sluice_b200 import configs, ep, synth
@@ -154,7 +157,7 @@ def _agree_main(rank, world, port, out_dir):
         cfg = configs.V2_LITE
         outs = {}
         for exchange in ("nvlink", "nccl"):
-            stack = ep.EPDecodeStack(cfg, slots=48, seed=5, num_layers=2, exchange=exchange)
+            stack = ep.EPDecodeStack(cfg, slots=slots, seed=5, num_layers=2, exchange=exchange)
             stacks.append(stack)
             tokens = synth.TokenStream(cfg.hidden, 4, seed=70 + rank)
             xs = [tokens.next().cuda() for _ in range(4)]
@@ -185,8 +188,11 @@ def test_ep2_layer_matches_oracle(tmp_path, exchange, slots):
         assert (errs < 2e-2).all(), errs
 
 
-def test_ep2_nvlink_exchange_equals_nccl(tmp_path):
-    mp.start_processes(_agree_main, args=(2, _free_port(), str(tmp_path)), nprocs=2,
+@pytest.mark.parametrize("slots", [48, 16], ids=["resident", "offloaded-waves"])
+def test_ep2_nvlink_exchange_equals_nccl(tmp_path, slots):
+    """Both exchanges, eager and graph-replayed; 16 slots: steps of 4 tokens
+    per rank exceed the envelope (16 // 6 // 2 = 1) and run in waves."""
+    mp.start_processes(_agree_main, args=(2, _free_port(), str(tmp_path), slots), nprocs=2,
                        start_method="spawn")
     for r in range(2):
         res = torch.load(os.path.join(tmp_path, f"agree{r}.pt"))
