@@ -611,6 +611,8 @@ def run_sluice(a):
                "sample": f"{n} full decode steps ({layers} layers, c={T}) of the torch-native "
                          f"CPU path (oracle routing + slot policy + MoE), median"}
 
+    local_n = cfg.num_experts // world
+    offloaded = a.slots < local_n
     launches = K * layers * layer_launches(cfg, T, world, a.slots, a.exchange, a.no_overlap)
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
