@@ -535,7 +535,8 @@ def run_sluice(a):
     if world == 1 and T != 1:
         c1 = _timed_c1(stack, cfg, K, W, a.seed)
 
-    misses = stats_t.get("misses", 0) - stats_w.get("misses", 0)
+    # gap misses plus the misses of steps planned in expert waves
+    misses = sum(stats_t.get(k, 0) - stats_w.get(k, 0) for k in ("misses", "scan_misses"))
     fills = stats_t.get("fills", 0) - stats_w.get("fills", 0)
     bpe = cfg.bytes_per_expert
     peaks = {}
