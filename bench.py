@@ -65,6 +65,8 @@ def _args(argv=None):
                          "prefill: steps beyond the envelope, expert waves and token chunks")
     ap.add_argument("--prefill-tokens", type=int, default=512,
                     help="tokens per step of the prefill workload")
+    ap.add_argument("--prefill-modes", default="waves,chunks",
+                    help="prefill workload modes to run, in order (waves, chunks)")
     ap.add_argument("--gemm-tokens", default="8,64,512,4096",
                     help="token counts of the grouped-GEMM microbench")
     ap.add_argument("--gemm-experts", type=int, default=256,
@@ -817,7 +819,9 @@ def run_prefill(a):
         peaks = json.load(f)
     hbm_peak, bf16_peak, host_peak = peaks["hbm_gbs"], peaks["bf16_tflops"], 63.0
     bpe, k = cfg.bytes_per_expert, cfg.routing.topk
-    for mode in ("waves", "chunks"):
+    for mode in a.prefill_modes.split(","):
+        if mode not in ("waves", "chunks"):
+            raise ValueError(f"unknown prefill mode {mode!r}")
         stack = MoEDecodeStack(cfg, slots=a.slots, seed=a.seed, num_layers=layers)
         for layer in stack.layers:
             layer.beyond_envelope = mode
