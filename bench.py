@@ -218,32 +218,37 @@ def cpu_layer_runner(cfg, seed, n_weight_sets=2):
     rc = cfg.routing
     policies = {}
 
-    def run_layer(li, x, slots):
-        # steps beyond the envelope (slots // topk tokens) run as chunks, as
-        # the GPU layer does
-        env = max(1, min(slots, cfg.num_experts) // rc.topk)
-        if slots < cfg.num_experts and x.shape[0] > env:
-            return torch.cat([run_layer(li, c, slots) for c in x.split(env)])
+    def run_layer(li, x, slots, decode=True):
         w13, w2, gw, lb, sb, sh = sets[li % n_weight_sets]
         logits = orouting.gate_logits(x, gw, lb)
         tw, ti = orouting.grouped_topk(logits, rc.topk, rc.renormalize, rc.num_expert_group,
                                        rc.topk_group, rc.scoring_func, 1.0, sb)
         pol = policies.setdefault(li, SlotPolicyModel(slots, list(range(cfg.num_experts)),
                                                       cfg.num_experts, 0.5, True))
-        pol.gap(ti.flatten().tolist())
+        env = max(1, min(slots, cfg.num_experts) // rc.topk)
+        if slots < cfg.num_experts and x.shape[0] > env:
+            # beyond the envelope: the classic hook's expert waves (decode
+            # steps decode-class, others by the working-set heuristic); the
+            # waves' outputs add up to the MoE over every pair, computed once
+            pol.run_moe(ti.flatten().tolist(), rc.topk, x.shape[0] if decode else 0)
+        else:
+            pol.gap(ti.flatten().tolist())
         routed = omoe.fused_experts(x, w13, w2, tw, ti)
         shared = omoe.shared_experts(x, *sh) if sh is not None else None
         return omoe.layer_output(routed, shared, cfg.routed_scaling_factor)
 
+    run_layer.policies = policies
     return run_layer
 
 
-def cpu_step_time(cfg, slots, tokens, layers, seed, steps, warmup, budget_s=None):
-    """Seconds per full decode step of the CPU port (all layers)."""
+def cpu_step_time(cfg, slots, tokens, layers, seed, steps, warmup, budget_s=None,
+                  decode=True):
+    """Seconds per full step of the CPU port (all layers): a decode step, or
+    with ``decode=False`` a prefill-sized one (fresh random tokens)."""
     from sluice_b200 import synth
 
     run = cpu_layer_runner(cfg, seed)
-    stream = synth.TokenStream(cfg.hidden, tokens, seed=seed)
+    stream = synth.TokenStream(cfg.hidden, tokens, seed=seed, reuse=0.6 if decode else 0.0)
     times = []
     t_start = time.perf_counter()
     for s in range(warmup + steps):
@@ -251,7 +256,7 @@ def cpu_step_time(cfg, slots, tokens, layers, seed, steps, warmup, budget_s=None
         t0 = time.perf_counter()
         h = x
         for li in range(layers):
-            h = h + run(li, h, slots)
+            h = h + run(li, h, slots, decode)
         dt = time.perf_counter() - t0
         if s >= warmup:
             times.append(dt)
@@ -819,6 +824,16 @@ def run_prefill(a):
         peaks = json.load(f)
     hbm_peak, bf16_peak, host_peak = peaks["hbm_gbs"], peaks["bf16_tflops"], 63.0
     bpe, k = cfg.bytes_per_expert, cfg.routing.topk
+    cpu = None
+    if not a.no_cpu_baseline:
+        # the CPU port (oracle routing, the classic hook's wave plan, MoE in
+        # torch) on one layer of the same step size, scaled to the stack
+        t_layer, n = cpu_step_time(cfg, a.slots, T, 1, a.seed, steps=1, warmup=1,
+                                   decode=False)
+        cpu = {"value": T / (t_layer * layers), "unit": "tok/s",
+               "cores": torch.get_num_threads(), "kind": "port",
+               "sample": f"{n} {T}-token step of 1 of the {layers} layers (after 1 warm-up), "
+                         f"scaled by {layers}: torch-native routing + wave plan + MoE"}
     for mode in a.prefill_modes.split(","):
         if mode not in ("waves", "chunks"):
             raise ValueError(f"unknown prefill mode {mode!r}")
@@ -844,6 +859,17 @@ def run_prefill(a):
         s1 = stack.stats()
         # experts the last step selected, per layer (every one is read once)
         uniq = sum(int(torch.unique(layer.last_ids).numel()) for layer in stack.layers)
+        # end to end: the step's tokens from pinned host memory, its output
+        # read back, inside the timed region
+        xh = [x.cpu().pin_memory() for x in xs[W:]]
+        oh = torch.empty(T, cfg.hidden, dtype=torch.bfloat16).pin_memory()
+        torch.cuda.synchronize()
+        ev0.record()
+        for i in range(K):
+            oh.copy_(stack.step(xh[i].to("cuda", non_blocking=True)), non_blocking=True)
+        ev1.record()
+        torch.cuda.synchronize()
+        e2e_ms = ev0.elapsed_time(ev1) / K
         fills = (s1["fills"] - s0["fills"]) / K
         host = fills * bpe
         hbm = uniq * bpe + layers * cfg.n_shared * bpe
@@ -864,8 +890,15 @@ def run_prefill(a):
                          "hbm_bytes": hbm, "flops": flops,
                          "peaks": {"hbm_gbs": hbm_peak, "bf16_tflops": bf16_peak,
                                    "host_link_gbs": host_peak}},
+            "e2e": {"value": T / (e2e_ms * 1e-3), "unit": "tok/s",
+                    "h2d_bytes_per_step": T * cfg.hidden * 2,
+                    "d2h_bytes_per_step": T * cfg.hidden * 2},
+            "gpu_launches": K * layers * layer_launches(cfg, T, 1, a.slots)
+            if mode == "waves" else None,
             "clocks": clk.summary(),
         }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
         del stack, xs
         gc.collect()

@@ -170,3 +170,54 @@ def test_reference_arm_runs_the_global_batch(monkeypatch, capsys):
     line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     assert line["impl"] == "reference" and line["n_gpus"] == 2
     assert line["config"]["tokens_per_step"] == 16 and line["value"] > 0
+
+
+def test_cpu_port_plans_steps_beyond_the_envelope_in_waves():
+    """The CPU port (the reference arm and the CPU baselines) runs a step of
+    more than slots // topk tokens as the reference's classic hook does:
+    one wave plan over the whole step, no chunking."""
+    import os
+    import sys
+
+    import torch
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, root)
+    import bench
+    from sluice_b200 import configs
+
+    cfg = configs.V2_LITE
+    run = bench.cpu_layer_runner(cfg, seed=0, n_weight_sets=1)
+    x = torch.randn(24, cfg.hidden, generator=torch.Generator().manual_seed(1))
+    out = run(0, x.to(torch.bfloat16), 48, False)
+    pol = run.policies[0]
+    assert out.shape == (24, cfg.hidden) and torch.isfinite(out.float()).all()
+    assert pol.scan_steps == 1 and pol.gaps == 0 and pol.scan_waves >= 1
+    run(0, x[:8].to(torch.bfloat16), 48)          # within the envelope: the gap
+    assert pol.gaps == 1 and pol.scan_steps == 1
+
+
+def test_bench_launch_count_rule():
+    """gpu_launches per layer: resident 6 (gate, select, grouping, 2 GEMMs,
+    combine), offloaded 10 (+ plan, stream, both GEMMs again), serial gap 8,
+    +1 quantising gather for fp8, +2 exchange kernels; a step beyond the
+    envelope: plan + one stream per wave + wave 0 in two phases + later
+    waves as whole calls."""
+    import os
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, root)
+    import bench
+    from sluice_b200 import configs
+    from sluice_b200.offloader import max_waves_for
+
+    V2, V3 = configs.V2_LITE, configs.DEEPSEEK_V3
+    assert bench.layer_launches(V2, 8, 1, 64) == 6
+    assert bench.layer_launches(V2, 8, 1, 48) == 10
+    assert bench.layer_launches(V2, 8, 1, 48, no_overlap=True) == 8
+    assert bench.layer_launches(V2, 8, 2, 48) == 8
+    assert bench.layer_launches(V2, 8, 2, 48, exchange="nccl") == 6
+    assert bench.layer_launches(V3, 8, 8, 128) == 9
+    mw = max_waves_for(48, 64, 24, 0)
+    assert bench.layer_launches(V2, 512, 1, 48) == 2 + 1 + mw + 7 + (mw - 1) * 5 == 35
