@@ -277,7 +277,7 @@ class SlotPolicyModel:
         return fills
 
     # -- steps beyond the envelope (offloader.py:1452-1764, 1846-1933) --------
-    def run_moe(self, ids: list[int], topk: int, decode_rows: int = 0) -> list[dict]:
+    def run_moe(self, ids: list[int], topk: int, decode_rows=0) -> list[dict]:
         """Plan one step through the classic hook over the flattened topk ids
         of ``len(ids) // topk`` tokens, on a real step.
 
@@ -286,7 +286,11 @@ class SlotPolicyModel:
         equal to ``num_decodes``, decode rows first); ``0`` — no per-token
         signal (a pure prefill, or a backend without a decode count), so the
         working-set heuristic classifies the step; ``-1`` — short prefills
-        folded into the decode count, so every expert is scan-class.
+        folded into the decode count, so every expert is scan-class. A list of
+        row indices is the opt-in non-MLA classifier's signal
+        (``_non_mla_decode_rows`` 1802-1844, 1595-1611): those rows are the
+        decodes, wherever they sit; an empty list is a pure prefill, every
+        expert scan-class.
 
         Returns the waves in execution order, each ``{"map": [(global, slot)],
         "fills": [(local, slot)]}``: a wave's fills are streamed before its
@@ -299,10 +303,16 @@ class SlotPolicyModel:
         G = self.global_n
         selected = sorted(set(ids))                           # 1561
         decode_ids = None
-        forced_scan = decode_rows < 0                         # 1628 (nd > ndec)
-        if 0 < decode_rows <= T:                              # 1578-1583
-            decode_ids = (set(selected) if decode_rows == T
-                          else set(ids[: decode_rows * topk]))
+        if not isinstance(decode_rows, int):                  # 1595-1611
+            rows = [int(r) for r in decode_rows]
+            forced_scan = False
+            decode_ids = (set(selected) if len(rows) == T else
+                          {ids[r * topk + j] for r in rows for j in range(topk)})
+        else:
+            forced_scan = decode_rows < 0                     # 1628 (nd > ndec)
+            if 0 < decode_rows <= T:                          # 1578-1583
+                decode_ids = (set(selected) if decode_rows == T
+                              else set(ids[: decode_rows * topk]))
         pairs = []                                            # 1613-1621
         for g in selected:
             if 0 <= g < G and self.local_of[g] >= 0:

@@ -29,8 +29,30 @@ from .configs import MoEConfig
 from .offloader import ExpertStreamOffloader, SlotCache
 
 
+def decode_rows_from_query_start_loc(query_start_loc, num_tokens: int, max_query_len: int,
+                                     num_actual_tokens: int | None = None):
+    """The decode rows of a batch from a non-MLA attention backend's metadata
+    (the reference's opt-in ``_non_mla_decode_rows``, offloader.py:1802-1844):
+    a request whose query is one token is a decode, and its row is its query
+    start. Returns the row indices (every row when ``max_query_len`` is 1, an
+    empty tensor for a pure prefill), or None when the metadata does not
+    describe this batch (the caller then passes 0: the working-set heuristic).
+    Pass the result as ``decode_rows``."""
+    if query_start_loc is None or max_query_len is None:
+        return None
+    if num_actual_tokens is not None and int(num_actual_tokens) != num_tokens:
+        return None
+    if int(max_query_len) == 1:
+        return torch.arange(num_tokens)
+    qsl = torch.as_tensor(query_start_loc).cpu()
+    if qsl.ndim != 1 or qsl.numel() < 2 or int(qsl[-1]) != num_tokens:
+        return None
+    starts = qsl[:-1]
+    return starts[(qsl[1:] - starts) == 1].long()
+
+
 def expert_waves(c: SlotCache, side: torch.cuda.Stream, hs: torch.Tensor, tw: torch.Tensor,
-                 ti: torch.Tensor, decode_rows: int, shared_w13, shared_w2, shared_t0: int,
+                 ti: torch.Tensor, decode_rows, shared_w13, shared_w2, shared_t0: int,
                  shared_nt: int, scale: float, shared_w13_scale=None, shared_w2_scale=None,
                  stream_ctas: int = 16) -> torch.Tensor:
     """One step of ``hs`` [T, H] (routed as ``tw`` / ``ti``) in expert waves
@@ -127,11 +149,13 @@ class SluiceMoELayer:
             return 1 << 30
         return max(1, self.cache.num_slots // self.cfg.routing.topk)
 
-    def forward(self, hs: torch.Tensor, decode_rows: int = 0) -> torch.Tensor:
+    def forward(self, hs: torch.Tensor, decode_rows=0) -> torch.Tensor:
         """One step of ``hs`` [T, H]. ``decode_rows`` only matters beyond the
         envelope: rows [0, decode_rows) are single-token decodes (the
         reference's ``num_decode_tokens``, decode rows first), 0 leaves the
-        step's class to the working-set heuristic, < 0 makes it a scan."""
+        step's class to the working-set heuristic, < 0 makes it a scan; or
+        the indices of the decode rows wherever they sit (the opt-in non-MLA
+        classifier's signal, ``decode_rows_from_query_start_loc``)."""
         thr = self.envelope
         if hs.shape[0] > thr:
             if self.beyond_envelope == "waves":
@@ -148,7 +172,7 @@ class SluiceMoELayer:
             return torch.cat(outs)
         return self._forward_step(hs)
 
-    def _forward_waves(self, hs: torch.Tensor, decode_rows: int) -> torch.Tensor:
+    def _forward_waves(self, hs: torch.Tensor, decode_rows) -> torch.Tensor:
         hs = hs.contiguous()
         tw, ti, logits = self.router.route(hs)
         self.last_ids, self.last_logits = ti, logits

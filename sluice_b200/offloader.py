@@ -83,6 +83,32 @@ def waves_pingpong(num_slots: int, protected_cap: int, n_pinned: int) -> bool:
     return num_slots - n_pinned - protected_cap >= 2
 
 
+def plan_ids_for(topk_ids: torch.Tensor, decode_rows) -> tuple[torch.Tensor, int]:
+    """The ids ``sl_plan_waves`` plans a step from, and its decode signal.
+
+    ``decode_rows`` is an int (rows [0, d) are decodes, 0 the working-set
+    heuristic, < 0 a scan) or the indices of the decode rows wherever they
+    sit — the opt-in non-MLA classifier's signal (``_non_mla_decode_rows``,
+    offloader.py:1802-1844, used at 1595-1611). A wave plan depends only on
+    the set of selected ids and on which of them decode rows select, not on
+    row order, so the planner is given the decode rows first and their count;
+    all rows decode is the whole step, no rows a scan (a pure prefill)."""
+    ids = topk_ids if topk_ids.dtype == torch.int32 and topk_ids.is_contiguous() \
+        else topk_ids.contiguous().to(torch.int32)
+    if isinstance(decode_rows, int):
+        return ids, decode_rows
+    T = ids.shape[0]
+    rows = torch.unique(torch.as_tensor(decode_rows, dtype=torch.long).flatten().cpu())
+    if rows.numel() == 0:
+        return ids, -1
+    if rows.numel() == T:
+        return ids, T
+    mask = torch.zeros(T, dtype=torch.bool)
+    mask[rows] = True
+    order = torch.cat([rows, torch.nonzero(~mask).flatten()])
+    return ids.index_select(0, order.to(ids.device)).contiguous(), int(rows.numel())
+
+
 @dataclass
 class InitialSlotState:
     """Host-computed starting residency of one layer's slots."""
@@ -246,16 +272,16 @@ class SlotCache:
               "sl_stream_experts_strided")
 
     # -- steps beyond the envelope: expert waves -----------------------------
-    def plan_waves(self, topk_ids: torch.Tensor, decode_rows: int = 0) -> None:
+    def plan_waves(self, topk_ids: torch.Tensor, decode_rows=0) -> None:
         """Plan this step's expert waves on the current stream (run_moe and
         _run_waves, offloader.py:1452-1764, 1846-1933): ``topk_ids`` [T, k];
         ``decode_rows`` > 0 marks rows [0, decode_rows) as decodes, 0 leaves
         the class to the working-set heuristic, < 0 makes every expert
-        scan-class."""
-        ids = topk_ids if topk_ids.dtype == torch.int32 and topk_ids.is_contiguous() \
-            else topk_ids.contiguous().to(torch.int32)
+        scan-class; a sequence / tensor of row indices marks those rows
+        (``plan_ids_for``)."""
+        ids, d = plan_ids_for(topk_ids, decode_rows)
         T, k = ids.shape
-        check(lib().sl_plan_waves(ptr(self.state), ptr(ids), T, k, int(decode_rows),
+        check(lib().sl_plan_waves(ptr(self.state), ptr(ids), T, k, int(d),
                                   ptr(self.expert_map), ptr(self.waves),
                                   torch.cuda.current_stream().cuda_stream), "sl_plan_waves")
 

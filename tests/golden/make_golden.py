@@ -19,6 +19,9 @@ It writes:
   evaluated by vLLM's ``cpu_fused_moe_torch`` (``cpu_fused_moe.py`` 428-482).
 * ``fp8_quant.npz`` — bf16 activations through vLLM's torch-native
   per-token-group fp8 quantisation (``QuantFP8._quantize_group_native``).
+* ``nonmla_rows.json`` — the reference's opt-in non-MLA decode-row
+  classifier ``ExpertStreamOffloader._non_mla_decode_rows`` (1802-1844) on
+  synthetic attention metadata (vLLM's forward context replaced for the call).
 * ``wave_traces.json`` — steps beyond the envelope through the reference's
   classic hook ``ExpertStreamOffloader.run_moe`` (1452-1764) and
   ``_run_waves`` (1846-1933), some scenarios interleaved with router-split gap
@@ -326,7 +329,10 @@ def _split_signal_for(decode_rows: int):
 
 def _run_wave_scenario(name, *, slots, global_n, local_n, owned_lo=0, steps, frac=0.5,
                        pins=None, lfu=False, fast_hit=True):
-    """``steps``: [("gap", ids) | ("moe", ids, topk, decode_rows)]."""
+    """``steps``: [("gap", ids) | ("moe", ids, topk, signal)]: an int signal is
+    an MLA decode count (``_split_signal_for``); a list of row indices (or
+    None: metadata that does not describe the batch) is what the opt-in
+    non-MLA classifier ``_non_mla_decode_rows`` returns for the step."""
     torch.cuda.Event = _NoEvent
     torch.cuda.current_stream = lambda *a: None
     off = _ref_offloader(slots, fast_hit, frac, False, lfu)
@@ -352,6 +358,9 @@ def _run_wave_scenario(name, *, slots, global_n, local_n, owned_lo=0, steps, fra
         log.append(("fill", [int(local), int(slot)])), si(c, local, slot, cs, on_stream))[1]
     signal = [(0, 0, True)]
     off._split_signal = lambda: signal[0]
+    rows_now = [None]
+    off._non_mla_decode_rows = lambda n: (None if rows_now[0] is None
+                                          else torch.tensor(rows_now[0], dtype=torch.long))
     trace = []
     for st in steps:
         log.clear()
@@ -368,8 +377,17 @@ def _run_wave_scenario(name, *, slots, global_n, local_n, owned_lo=0, steps, fra
                 rec["overflow"] = True
         else:
             _, ids, topk, d = st
-            rec["topk"], rec["decode_rows"] = topk, d
-            signal[0] = _split_signal_for(d)
+            rec["topk"] = topk
+            if isinstance(d, int):
+                rec["decode_rows"] = d
+                off.nonmla_classifier = False
+                signal[0] = _split_signal_for(d)
+            else:
+                # a non-MLA backend: no decode count, rows from query_start_loc
+                rec["decode_row_index"] = d
+                off.nonmla_classifier = True
+                signal[0] = (None, None, True)
+                rows_now[0] = d
             t = torch.tensor(ids, dtype=torch.int32).view(-1, topk)
             out = off.run_moe(lambda *a, **k: torch.ones(1), (), {}, mod, t)
             waves, pending = [], []
@@ -455,19 +473,72 @@ def make_wave_traces():
                            steps=[("moe", [40, 41, 63, -1, 50, 33] * 8, 6, 0),
                                   decode(4, 6, 64)]),
     ]
+    # the opt-in non-MLA classifier: decode rows anywhere in the batch
+    rng = torch.Generator().manual_seed(97531)
+
+    def rows_step(T, k, E, n_dec):
+        rows = sorted(torch.randperm(T, generator=rng)[:n_dec].tolist())
+        ids = [i for _ in range(T) for i in torch.randperm(E, generator=rng)[:k].tolist()]
+        return ("moe", ids, k, rows)
+
+    sc += [
+        _run_wave_scenario("nonmla_scattered_decode_rows", slots=48, global_n=64, local_n=64,
+                           steps=[decode(8, 6, 64), rows_step(40, 6, 64, 5), decode(8, 6, 64),
+                                  rows_step(24, 6, 64, 24), rows_step(32, 6, 64, 0),
+                                  ("moe", prefill(20, 6, 64)[1], 6, None),
+                                  rows_step(48, 6, 64, 9), decode(8, 6, 64)]),
+        _run_wave_scenario("nonmla_qwen3_lfu", slots=64, global_n=128, local_n=128, lfu=True,
+                           steps=[rows_step(24, 8, 128, 6), decode(8, 8, 128),
+                                  rows_step(40, 8, 128, 12), rows_step(16, 8, 128, 1),
+                                  decode(8, 8, 128)]),
+    ]
     with open(os.path.join(HERE, "wave_traces.json"), "w") as f:
         json.dump({"generator": "tests/golden/make_golden.py", "scenarios": sc}, f,
                   separators=(",", ":"))
     for s in sc:
         nw = [len(r["waves"]) for r in s["trace"] if r["kind"] == "moe"]
         print(f"{s['name']}: steps={len(s['trace'])} waves per moe step={nw}")
+    return sc
+
+
+def make_nonmla_rows():
+    import types
+
+    import vllm.forward_context as fc
+    from sluice.offloader import ExpertStreamOffloader
+
+    cases = [  # (query_start_loc, num_tokens, max_query_len, num_actual_tokens)
+        ([0, 1, 2, 3, 4], 4, 1, 4),                 # pure decode
+        ([0, 1, 5, 6, 10], 10, 4, 10),              # decodes at rows 0 and 5
+        ([0, 4, 10], 10, 6, None),                  # pure prefill
+        ([0, 3, 4, 5, 9, 10, 11], 11, 4, 11),       # decodes at 3, 4, 9, 10
+        ([0, 2, 7], 8, 5, 8),                       # query lengths do not cover the batch
+        ([0, 1, 2], 2, 1, 3),                       # a padded batch
+        ([[0, 1], [1, 2]], 2, 2, 2),                # not a 1-D query_start_loc
+        ([0], 0, 2, 0),                             # no requests
+    ]
+    out = []
+    orig = fc.get_forward_context
+    try:
+        for qsl, T, mql, nat in cases:
+            md = types.SimpleNamespace(max_query_len=mql, query_start_loc=torch.tensor(qsl),
+                                       num_actual_tokens=nat)
+            fc.get_forward_context = lambda md=md: types.SimpleNamespace(attn_metadata=md)
+            r = ExpertStreamOffloader._non_mla_decode_rows(T)
+            out.append({"query_start_loc": qsl, "num_tokens": T, "max_query_len": mql,
+                        "num_actual_tokens": nat, "rows": None if r is None else r.tolist()})
+    finally:
+        fc.get_forward_context = orig
+    with open(os.path.join(HERE, "nonmla_rows.json"), "w") as f:
+        json.dump({"generator": "tests/golden/make_golden.py", "cases": out}, f, indent=1)
+    print("nonmla rows:", [c["rows"] for c in out])
 
 
 if __name__ == "__main__":
     if not REF:
         raise SystemExit("set SLUICE_REFERENCE to a checkout of kfirtoledo/sluice")
     sys.path.insert(0, os.path.join(REF, "src"))
-    wanted = set(sys.argv[1:]) or {"slots", "routing", "moe", "fp8", "waves"}
+    wanted = set(sys.argv[1:]) or {"slots", "routing", "moe", "fp8", "waves", "nonmla"}
     if "slots" in wanted:
         make_slot_traces()
     if "routing" in wanted:
@@ -478,3 +549,5 @@ if __name__ == "__main__":
         make_fp8_quant()
     if "waves" in wanted:
         make_wave_traces()
+    if "nonmla" in wanted:
+        make_nonmla_rows()

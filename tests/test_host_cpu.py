@@ -221,3 +221,35 @@ def test_bench_launch_count_rule():
     assert bench.layer_launches(V3, 8, 8, 128) == 9
     mw = max_waves_for(48, 64, 24, 0)
     assert bench.layer_launches(V2, 512, 1, 48) == 2 + 1 + mw + 7 + (mw - 1) * 5 == 35
+
+
+def test_decode_rows_from_query_start_loc_matches_the_reference():
+    """The host helper that turns a non-MLA backend's attention metadata into
+    decode rows, against the reference's own ``_non_mla_decode_rows`` on the
+    same metadata (tests/golden/nonmla_rows.json)."""
+    import torch
+
+    from sluice_b200.layer import decode_rows_from_query_start_loc
+
+    with open(os.path.join(GOLDEN, "nonmla_rows.json")) as f:
+        cases = json.load(f)["cases"]
+    assert any(c["rows"] is None for c in cases) and any(c["rows"] == [] for c in cases)
+    for c in cases:
+        got = decode_rows_from_query_start_loc(torch.tensor(c["query_start_loc"]),
+                                               c["num_tokens"], c["max_query_len"],
+                                               c["num_actual_tokens"])
+        assert (None if got is None else got.tolist()) == c["rows"], c
+
+
+def test_plan_ids_for_orders_decode_rows_first():
+    import torch
+
+    from sluice_b200.offloader import plan_ids_for
+
+    ids = torch.arange(12, dtype=torch.int32).view(6, 2)
+    same, d = plan_ids_for(ids, 3)
+    assert d == 3 and torch.equal(same, ids)
+    got, d = plan_ids_for(ids, torch.tensor([4, 1, 4]))
+    assert d == 2 and got[:, 0].tolist() == [2, 8, 0, 4, 6, 10]
+    assert plan_ids_for(ids, [])[1] == -1             # a pure prefill: scan
+    assert plan_ids_for(ids, list(range(6)))[1] == 6  # every row a decode

@@ -16,7 +16,7 @@ import torch
 from oracle import moe as omoe
 from oracle import routing as orouting
 from oracle.slot_policy import PROBATION, PROTECTED, SlotOverflow, SlotPolicyModel
-from sluice_b200.offloader import max_waves_for, waves_pingpong
+from sluice_b200.offloader import max_waves_for, plan_ids_for, waves_pingpong
 
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
 
@@ -91,7 +91,16 @@ def replay_wave_step(m: SlotPolicyModel, step: dict):
         except SlotOverflow:
             pass
         return None
-    return m.run_moe(step["ids"], step["topk"], step["decode_rows"])
+    return m.run_moe(step["ids"], step["topk"], step_signal(step))
+
+
+def step_signal(step: dict):
+    """An MLA decode count, or the non-MLA classifier's decode rows (None:
+    metadata that does not describe the batch, i.e. the heuristic)."""
+    if "decode_rows" in step:
+        return step["decode_rows"]
+    rows = step["decode_row_index"]
+    return 0 if rows is None else rows
 
 
 @pytest.mark.parametrize("sc", _wave_scenarios(), ids=lambda s: s["name"])
@@ -135,6 +144,33 @@ def test_wave_planning_matches_reference_run_moe(sc):
             assert m.freq == exp["freq"], where
 
 
+@pytest.mark.parametrize("sc", [s for s in _wave_scenarios() if s["name"].startswith("nonmla")],
+                         ids=lambda s: s["name"])
+def test_decode_rows_anywhere_plan_as_a_prefix(sc):
+    """The product plans the non-MLA classifier's scattered decode rows by
+    handing the planner the ids with those rows first and their count
+    (``plan_ids_for``); through the prefix semantics the device planner
+    implements, that reproduces the reference's row-index classification."""
+    sc = dict(sc, prefill_resident=False)
+    m = model_for(sc)
+    for i, step in enumerate(sc["trace"]):
+        if step["kind"] == "gap":
+            replay_wave_step(m, step)
+        else:
+            k = step["topk"]
+            t = torch.tensor(step["ids"], dtype=torch.int32).view(-1, k)
+            sig = step_signal(step)
+            ids, d = plan_ids_for(t, sig if isinstance(sig, int) else torch.tensor(sig))
+            assert isinstance(d, int)
+            waves = m.run_moe(ids.flatten().tolist(), k, d)
+            got = [{"map": [list(x) for x in w["map"]], "fills": [list(x) for x in w["fills"]]}
+                   for w in waves]
+            assert got == step["waves"], (sc["name"], i)
+        assert m.expert_map == step["expert_map"], (sc["name"], i)
+        assert m.segment_order(PROTECTED) == step["protected"], (sc["name"], i)
+        assert m.segment_order(PROBATION) == step["probation"], (sc["name"], i)
+
+
 def test_wave_golden_covers_edge_cases():
     names = {s["name"]: s for s in _wave_scenarios()}
     nw = lambda n: [len(r["waves"]) for r in names[n]["trace"] if r["kind"] == "moe"]
@@ -145,6 +181,11 @@ def test_wave_golden_covers_edge_cases():
     assert names["v2lite_pins_prefill"]["pinned_slots"] and names["v2lite_lfu_mixed"]["lfu"]
     assert {r.get("decode_rows") for r in names["v2lite_mixed_decode_rows"]["trace"]} >= {
         4, 16, -1}
+    rows = [r["decode_row_index"] for r in names["nonmla_scattered_decode_rows"]["trace"]
+            if "decode_row_index" in r]
+    # a None step, a pure prefill, and decode rows that are not a prefix
+    assert None in rows and [] in rows
+    assert any(r and r != list(range(len(r))) for r in rows if r is not None)
 
 
 def _routing_case(z, name):

@@ -53,7 +53,12 @@ def test_wave_planner_matches_reference_run_moe(sc):
             cache.gap(ids)
             torch.cuda.synchronize()
         else:
-            cache.plan_waves(ids.view(-1, exp["topk"]), exp["decode_rows"])
+            if "decode_rows" in exp:
+                signal = exp["decode_rows"]
+            else:  # the non-MLA classifier's decode rows (None: heuristic)
+                rows = exp["decode_row_index"]
+                signal = 0 if rows is None else torch.tensor(rows, dtype=torch.long)
+            cache.plan_waves(ids.view(-1, exp["topk"]), signal)
             torch.cuda.synchronize()
             assert cache.wave_header()["status"] == _lib.SL_OK, where
             plan = cache.wave_plan()
