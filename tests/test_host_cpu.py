@@ -253,3 +253,45 @@ def test_plan_ids_for_orders_decode_rows_first():
     assert d == 2 and got[:, 0].tolist() == [2, 8, 0, 4, 6, 10]
     assert plan_ids_for(ids, [])[1] == -1             # a pure prefill: scan
     assert plan_ids_for(ids, list(range(6)))[1] == 6  # every row a decode
+
+
+def _header_enum(prefix: str) -> dict:
+    """Values of the header's ``prefix*`` enumerators (sequential enums with
+    an explicit first value, as include/sluice_b200.h writes them)."""
+    import re
+
+    with open(_lib.HEADER_PATH) as f:
+        text = re.sub(r"/\*.*?\*/", "", f.read(), flags=re.S)
+    out = {}
+    for body in re.findall(r"enum\s*\{(.*?)\}", text, flags=re.S):
+        nxt = 0
+        for item in [x.strip() for x in body.split(",") if x.strip()]:
+            name, _, val = item.partition("=")
+            name = name.strip()
+            nxt = int(val.strip(), 0) if val.strip() else nxt
+            if name.startswith(prefix):
+                out[name[len(prefix):].lower()] = nxt
+            nxt += 1
+    return out
+
+
+def test_binding_tables_match_the_header():
+    """The ctypes binding's state-header, counter, wave-plan and status
+    tables against the header's enums (a drift would misread device state)."""
+    assert _header_enum("SL_HDR_") == _lib.HDR
+    assert _header_enum("SL_CNT_") == _lib.CNT
+    assert _header_enum("SL_WAVE_HDR_") == _lib.WAVE_HDR
+    assert _header_enum("SL_STATE_NFIELDS")[""] == _lib.STATE_NFIELDS
+    assert _header_enum("SL_WAVE_NFIELDS")[""] == _lib.WAVE_NFIELDS
+    plan = _header_enum("SL_PLAN_")
+    assert plan == {"fast_hit": _lib.PLAN_FAST_HIT, "lfu": _lib.PLAN_LFU}
+    err = _header_enum("SL_ERR_")
+    assert err == {"overflow": _lib.SL_ERR_OVERFLOW, "invalid": _lib.SL_ERR_INVALID,
+                   "cuda": _lib.SL_ERR_CUDA, "unsupported": _lib.SL_ERR_UNSUPPORTED,
+                   "timeout": _lib.SL_ERR_TIMEOUT, "no_scratch": _lib.SL_ERR_NO_SCRATCH}
+    assert len(_lib.CNT) <= _lib.NUM_COUNTERS
+    assert _header_enum("SL_SEG_") == {"free": _lib.SEG_FREE, "probation": _lib.SEG_PROBATION,
+                                       "protected": _lib.SEG_PROTECTED,
+                                       "pinned": _lib.SEG_PINNED}
+    assert _header_enum("SL_WEIGHTS_") == {"bf16": _lib.WEIGHTS_BF16,
+                                           "fp8_block128": _lib.WEIGHTS_FP8_BLOCK128}
