@@ -425,7 +425,8 @@ def _step_bytes(stack, cfg):
     return tot
 
 
-def layer_launches(cfg, tokens, world, slots, exchange="nvlink", no_overlap=False) -> int:
+def layer_launches(cfg, tokens, world, slots, exchange="nvlink", no_overlap=False,
+                   decode=True) -> int:
     """This build's kernel launches per MoE layer and step, following the
     launch rules of the host code: gate + select; a fused-experts call is its
     token grouping (one kernel for up to 1024 bf16 pairs, else grouping +
@@ -433,7 +434,8 @@ def layer_launches(cfg, tokens, world, slots, exchange="nvlink", no_overlap=Fals
     the combine (a phase-0 call stops before the combine; its phase 1 runs
     the GEMMs again and the combine); an offloaded gap adds plan + stream; a
     step beyond the envelope runs max_waves waves (one plan, a stream per
-    wave, wave 0 split in two phases, the rest whole calls); the NVLink
+    wave, wave 0 split in two phases, the rest whole calls; decode steps,
+    every expert decode-class, take the tighter wave count); the NVLink
     exchange adds dispatch + combine."""
     from sluice_b200.offloader import max_waves_for, protected_cap_for
 
@@ -446,7 +448,8 @@ def layer_launches(cfg, tokens, world, slots, exchange="nvlink", no_overlap=Fals
         return 2 + align + 3 + ex
     S = min(slots, local_n)
     if tokens > max(1, S // k // world):
-        mw = max_waves_for(S, min(local_n, tokens * world * k), protected_cap_for(S, 0.5), 0)
+        mw = max_waves_for(S, min(local_n, tokens * world * k), protected_cap_for(S, 0.5), 0,
+                           all_decode=decode)
         return 2 + 1 + mw + (align + 5) + (mw - 1) * (align + 3) + ex
     return 2 + 2 + (align + 3 if no_overlap else align + 5) + ex
 
@@ -843,15 +846,16 @@ def run_prefill(a):
         g = torch.Generator().manual_seed(a.seed + 11)
         xs = [torch.randn(T, cfg.hidden, generator=g).to(torch.bfloat16).cuda()
               for _ in range(W + K)]
+        # prefill steps: no decode rows (the working-set heuristic classifies)
         for i in range(W):
-            stack.step(xs[i])
+            stack.step(xs[i], decode_rows=0)
         torch.cuda.synchronize()
         s0 = stack.stats()
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with ClockSampler(torch.cuda.current_device()) as clk:
             ev0.record()
             for i in range(K):
-                stack.step(xs[W + i])
+                stack.step(xs[W + i], decode_rows=0)
             ev1.record()
             torch.cuda.synchronize()
         ms = ev0.elapsed_time(ev1) / K
@@ -866,7 +870,8 @@ def run_prefill(a):
         torch.cuda.synchronize()
         ev0.record()
         for i in range(K):
-            oh.copy_(stack.step(xh[i].to("cuda", non_blocking=True)), non_blocking=True)
+            oh.copy_(stack.step(xh[i].to("cuda", non_blocking=True), decode_rows=0),
+                     non_blocking=True)
         ev1.record()
         torch.cuda.synchronize()
         e2e_ms = ev0.elapsed_time(ev1) / K
@@ -893,7 +898,7 @@ def run_prefill(a):
             "e2e": {"value": T / (e2e_ms * 1e-3), "unit": "tok/s",
                     "h2d_bytes_per_step": T * cfg.hidden * 2,
                     "d2h_bytes_per_step": T * cfg.hidden * 2},
-            "gpu_launches": K * layers * layer_launches(cfg, T, 1, a.slots)
+            "gpu_launches": K * layers * layer_launches(cfg, T, 1, a.slots, decode=False)
             if mode == "waves" else None,
             "clocks": clk.summary(),
         }

@@ -73,7 +73,10 @@ def expert_waves(c: SlotCache, side: torch.cuda.Stream, hs: torch.Tensor, tw: to
     ws = ops.fused_experts_workspace(T, ti.shape[1], H, c.w13.shape[1] // 2, c.num_slots,
                                      n_sh, hs.device)
     acc = torch.empty(T, H, dtype=torch.float32, device=hs.device)
-    MW = c.waves_for(ti.numel())
+    # every row a decode: every expert decode-class (a tighter wave count);
+    # the planner reads a count above T as no per-token signal
+    all_decode = isinstance(decode_rows, int) and decode_rows == T
+    MW = c.waves_for(ti.numel(), all_decode)
     filled = [torch.cuda.Event() for _ in range(MW)]
     computed = [torch.cuda.Event() for _ in range(MW)]
 
@@ -253,10 +256,15 @@ class MoEDecodeStack:
         torch.cuda.synchronize(self.device)
         self.graphs: dict = {}  # tokens -> (graph, static input, static output)
 
-    def step(self, x: torch.Tensor) -> torch.Tensor:
+    def step(self, x: torch.Tensor, decode_rows=None) -> torch.Tensor:
+        """One step through every layer. By default a decode step: every row
+        is a decode (decode-class experts when the step exceeds the envelope
+        and runs in waves); ``decode_rows`` as ``SluiceMoELayer.forward``
+        otherwise (0 for a prefill: the working-set heuristic)."""
+        d = x.shape[0] if decode_rows is None else decode_rows
         h = x
         for layer in self.layers:
-            h = h + layer(h)
+            h = h + layer(h, decode_rows=d)
         return h
 
     # -- CUDA graphs of one decode step (one per token count) -----------------

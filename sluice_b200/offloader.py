@@ -62,7 +62,8 @@ def protected_cap_for(num_slots: int, protect_frac: float) -> int:
     return max(min(int(num_slots * frac), num_slots - 1), 0)
 
 
-def max_waves_for(num_slots: int, local_n: int, protected_cap: int, n_pinned: int) -> int:
+def max_waves_for(num_slots: int, local_n: int, protected_cap: int, n_pinned: int,
+                  all_decode: bool = False) -> int:
     """An upper bound on the expert waves of one step (sl_plan_waves) that
     selects at most ``local_n`` of this rank's experts.
 
@@ -70,9 +71,12 @@ def max_waves_for(num_slots: int, local_n: int, protected_cap: int, n_pinned: in
     segment holds at most ``protected_cap`` slots, so the probation segment
     (the rotation) holds ``r >= num_slots - n_pinned - protected_cap``; wave 0
     claimed all of it, and every later wave takes a rotation group of at
-    least ``r // 2`` slots (``_run_waves``, offloader.py:1856-1886)."""
+    least ``r // 2`` slots (``_run_waves``, offloader.py:1856-1886). When every
+    expert of the step is decode-class (``all_decode``), a miss may also take
+    an unclaimed protected slot, so wave 0 claimed every unpinned slot."""
     r = max(num_slots - n_pinned - protected_cap, 1)
-    left = max(local_n - r, 0)
+    wave0 = max(num_slots - n_pinned, r) if all_decode else r
+    left = max(local_n - wave0, 0)
     g = max(r // 2, 1)
     return 1 + (left + g - 1) // g
 
@@ -285,11 +289,13 @@ class SlotCache:
                                   ptr(self.expert_map), ptr(self.waves),
                                   torch.cuda.current_stream().cuda_stream), "sl_plan_waves")
 
-    def waves_for(self, pairs: int) -> int:
+    def waves_for(self, pairs: int, all_decode: bool = False) -> int:
         """The waves a step of ``pairs`` (token, expert) pairs can need: it
-        selects at most ``min(local_n, pairs)`` experts."""
+        selects at most ``min(local_n, pairs)`` experts; ``all_decode``: every
+        one of them decode-class."""
         return min(self.max_waves, max_waves_for(self.num_slots, min(self.local_n, pairs),
-                                                 self.protected_cap, self.n_pinned))
+                                                 self.protected_cap, self.n_pinned,
+                                                 all_decode))
 
     def stream_wave(self, wave: int, stream_ctas: int = 0) -> None:
         """Stream wave ``wave``'s fills of the last wave plan (current stream)."""

@@ -220,7 +220,12 @@ def test_bench_launch_count_rule():
     assert bench.layer_launches(V2, 8, 2, 48, exchange="nccl") == 6
     assert bench.layer_launches(V3, 8, 8, 128) == 9
     mw = max_waves_for(48, 64, 24, 0)
-    assert bench.layer_launches(V2, 512, 1, 48) == 2 + 1 + mw + 7 + (mw - 1) * 5 == 35
+    assert bench.layer_launches(V2, 512, 1, 48, decode=False) == 2 + 1 + mw + 7 + \
+        (mw - 1) * 5 == 35
+    # decode steps beyond the envelope: every expert decode-class, fewer waves
+    mwd = max_waves_for(96, 128, 48, 0, all_decode=True)
+    assert mwd == 3 < max_waves_for(96, 128, 48, 0) == 5
+    assert bench.layer_launches(V3, 8, 2, 96) == 2 + 1 + mwd + 7 + (mwd - 1) * 5 + 2
 
 
 def test_decode_rows_from_query_start_loc_matches_the_reference():

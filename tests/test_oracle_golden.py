@@ -124,8 +124,10 @@ def test_wave_planning_matches_reference_run_moe(sc):
             assert got == exp["waves"], where
             assert len(waves) <= bound, where
             # the per-step bound the host issues: at most min(L, pairs) experts
+            T = len(exp["ids"]) // exp["topk"]
             step_bound = max_waves_for(m.num_slots, min(m.local_n, len(exp["ids"])),
-                                       m.protected_cap, n_pinned)
+                                       m.protected_cap, n_pinned,
+                                       all_decode=exp.get("decode_rows") == T)
             assert len(waves) <= step_bound <= bound, where
             if len(waves) > 2 and pipelined:
                 # ping-pong: consecutive waves use disjoint slots

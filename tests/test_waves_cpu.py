@@ -68,7 +68,7 @@ def test_wave_plans_partition_and_fit_the_bound(seed):
                 continue
             T = rng.randint(1, 64)
             ids = _ids(rng, T, k, G, lo, hi)
-            d = rng.choice([-1, 0, 0, rng.randint(1, T)])
+            d = rng.choice([-1, 0, 0, rng.randint(1, T), T, T])
             waves = m.run_moe(ids, k, d)
             owned = {g for g in ids if 0 <= g < G and m.local_of[g] >= 0}
             # partition: every owned selected expert in exactly one wave
@@ -81,9 +81,10 @@ def test_wave_plans_partition_and_fit_the_bound(seed):
                 assert sorted(g for g, _ in w["map"]) == sorted(
                     m.global_of_local[loc] for loc, _ in w["fills"])
                 assert all(s for s in w["fills"])
-            # the host's per-step wave count covers the plan
+            # the host's per-step wave count covers the plan (tighter when
+            # every row is a decode: every expert decode-class)
             bound = max_waves_for(m.num_slots, min(m.local_n, len(ids)), m.protected_cap,
-                                  n_pinned)
+                                  n_pinned, all_decode=(d == T))
             assert len(waves) <= bound <= max_waves_for(m.num_slots, m.local_n,
                                                         m.protected_cap, n_pinned)
             # stream ordering: wave k's fills avoid wave k - 1's slots
@@ -98,6 +99,29 @@ def test_wave_plans_partition_and_fit_the_bound(seed):
             assert not m.map_is_standing
             last = waves[-1]["map"]
             assert m.expert_map == [dict(last).get(g, -1) for g in range(G)]
+
+
+@pytest.mark.parametrize("seed", range(6))
+def test_all_decode_wave_bound_is_tight_enough(seed):
+    """Decode steps beyond the envelope (every row a decode), the expert-
+    parallel decode case: many random warm caches, the decode-aware bound
+    never short, and reached by some step."""
+    rng = random.Random(5000 + seed)
+    reached = 0
+    for _case in range(40):
+        m, G = _random_cache(rng)
+        n_pinned = sum(1 for v in m.seg if v == PINNED)
+        for _step in range(rng.randint(3, 10)):
+            k = rng.randint(1, 8)
+            T = rng.randint(1, 48)
+            lo, hi = (0, G) if rng.random() < 0.5 else (0, max(k, G // 2))
+            ids = _ids(rng, T, k, G, lo, hi)
+            waves = m.run_moe(ids, k, T)
+            bound = max_waves_for(m.num_slots, min(m.local_n, len(ids)), m.protected_cap,
+                                  n_pinned, all_decode=True)
+            assert len(waves) <= bound
+            reached += len(waves) == bound and bound > 1
+    assert reached > 0
 
 
 def test_single_rotation_group_is_not_pingpong():

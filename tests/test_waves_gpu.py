@@ -154,7 +154,10 @@ def test_v2lite_layer_in_waves_matches_oracle():
     layer, cache, host, sb = _layer(cfg, 48, seed=21)
     model = SlotPolicyModel(48, list(range(cfg.num_experts)), cfg.num_experts, 0.5, True)
     g = torch.Generator().manual_seed(22)
-    plan = [(64, 0), (8, None), (40, 4), (8, None), (8, None), (29, -1), (96, 0), (8, None)]
+    # (tokens, decode signal): heuristic, decode steps, decode-row prefix,
+    # forced scan, and all-decode steps (the tighter wave count)
+    plan = [(64, 0), (8, None), (40, 4), (8, None), (8, None), (29, -1), (96, 0), (8, None),
+            (48, 48), (8, None), (64, 64)]
     nwaves = []
     for step, (T, d) in enumerate(plan):
         x = torch.randn(T, cfg.hidden, generator=g).to(torch.bfloat16)
