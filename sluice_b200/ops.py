@@ -130,6 +130,8 @@ def _fused_ex(hs, w1, w2, topk_weights, topk_ids, expert_map, global_n, *, w1_sc
               w2_scale=None, shared_w13=None, shared_w2=None, shared_w13_scale=None,
               shared_w2_scale=None, routed_scaling_factor=1.0, shared_t0=0, shared_nt=-1,
               slot_state=None, phase=-1, out_f32=0, out=None, workspace=None):
+    # out_f32: 0 bf16 output; 1 fp32 partial written to `out`; 2 fp32 partial
+    # added to `out` (sl_fused_experts_ex)
     _need_cuda(hs, w1, w2, topk_weights, topk_ids, expert_map)
     hs = hs.contiguous()
     if hs.dtype != torch.bfloat16:
