@@ -300,3 +300,28 @@ def test_binding_tables_match_the_header():
                                        "pinned": _lib.SEG_PINNED}
     assert _header_enum("SL_WEIGHTS_") == {"bf16": _lib.WEIGHTS_BF16,
                                            "fp8_block128": _lib.WEIGHTS_FP8_BLOCK128}
+
+
+def test_state_init_rejects_bad_maps_before_any_cuda_call():
+    """sl_slot_state_init validates the host arrays first: two global ids
+    mapped to one local expert, a local id out of range, an expert in two
+    slots, or a free slot in a segment are refused (no device is touched)."""
+    L = _lib.lib()
+    S, G, Ln = 4, 8, 6
+    arr = lambda v, t: (t * len(v))(*v)
+    dummy = ctypes.create_string_buffer(L.sl_slot_state_bytes(S, G, Ln))
+    ok_lof = [0, 1, 2, 3, 4, 5, -1, -1]
+    eis = [-1] * S
+    seg = [0] * S
+    free = [3, 2, 1, 0]
+
+    def init(lof, eis=eis, seg=seg):
+        return L.sl_slot_state_init(ctypes.addressof(dummy), S, G, Ln, 1, 0,
+                                    arr(lof, ctypes.c_int32), arr(eis, ctypes.c_int32),
+                                    arr(seg, ctypes.c_uint8), arr(free, ctypes.c_int32),
+                                    len(free), None)
+
+    assert init([0, 1, 2, 3, 4, 0, -1, -1]) == _lib.SL_ERR_INVALID   # not injective
+    assert init([0, 1, 2, 3, 4, 6, -1, -1]) == _lib.SL_ERR_INVALID   # local id >= L
+    assert init(ok_lof, eis=[2, 2, -1, -1], seg=[1, 1, 0, 0]) == _lib.SL_ERR_INVALID
+    assert init(ok_lof, eis=[-1, -1, -1, -1], seg=[1, 0, 0, 0]) == _lib.SL_ERR_INVALID
