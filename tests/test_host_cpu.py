@@ -325,3 +325,21 @@ def test_state_init_rejects_bad_maps_before_any_cuda_call():
     assert init([0, 1, 2, 3, 4, 6, -1, -1]) == _lib.SL_ERR_INVALID   # local id >= L
     assert init(ok_lof, eis=[2, 2, -1, -1], seg=[1, 1, 0, 0]) == _lib.SL_ERR_INVALID
     assert init(ok_lof, eis=[-1, -1, -1, -1], seg=[1, 0, 0, 0]) == _lib.SL_ERR_INVALID
+
+
+def test_header_compiles_as_c99_and_cxx17(tmp_path):
+    """The boundary is a C ABI: a C host (cgo, a plain C loader) includes the
+    header as C99, a C++ host as C++17, both warning-free."""
+    import shutil
+    import subprocess
+
+    src = tmp_path / "use_header.c"
+    src.write_text(f'#include "{_lib.HEADER_PATH}"\n'
+                   "int main(void) { sl_expert_weights w; w.num_slots = SL_WAVE_NFIELDS;\n"
+                   "  return w.num_slots + SL_CNT_WAVES + SL_ERR_NO_SCRATCH; }\n")
+    for cc, args in (("gcc", ["-std=c99", "-pedantic"]), ("g++", ["-std=c++17", "-x", "c++"])):
+        if shutil.which(cc) is None:
+            pytest.skip(f"{cc} not available")
+        r = subprocess.run([cc, *args, "-Wall", "-Wextra", "-Werror", "-fsyntax-only",
+                            str(src)], capture_output=True, text=True)
+        assert r.returncode == 0, r.stderr
