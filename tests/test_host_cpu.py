@@ -343,3 +343,26 @@ def test_header_compiles_as_c99_and_cxx17(tmp_path):
         r = subprocess.run([cc, *args, "-Wall", "-Wextra", "-Werror", "-fsyntax-only",
                             str(src)], capture_output=True, text=True)
         assert r.returncode == 0, r.stderr
+
+
+def test_c_host_links_and_calls_the_library(tmp_path):
+    """tests/c_host/abi_check.c — a C99 program linked against
+    libsluice_sm100.so, as a non-Python host would be — runs the calls that
+    need no GPU and exits 0."""
+    import shutil
+    import subprocess
+
+    if shutil.which("gcc") is None:
+        pytest.skip("gcc not available")
+    here = os.path.dirname(os.path.abspath(__file__))
+    libdir = os.path.dirname(_lib.LIB_PATH)
+    exe = tmp_path / "abi_check"
+    r = subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-Werror",
+                        "-I", os.path.dirname(_lib.HEADER_PATH),
+                        os.path.join(here, "c_host", "abi_check.c"), "-o", str(exe),
+                        "-L", libdir, "-lsluice_sm100", f"-Wl,-rpath,{libdir}"],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0, r.stderr
+    assert "c host ok" in r.stdout
