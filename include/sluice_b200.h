@@ -378,7 +378,12 @@ int sl_ep_combine(const float* partial, int T, int H, int rank, int world,
  *     (cudaGetSymbolAddress) with that device current: make it before any
  *     stream capture.
  *   - status_out (device int32, may be NULL) receives the device status word
- *     (SL_OK or SL_ERR_TIMEOUT) on the same stream.
+ *     (SL_OK or SL_ERR_TIMEOUT) on the same stream, and only when the call
+ *     returns SL_OK. Every argument is checked before anything is enqueued:
+ *     any other return leaves the stream, the scratch and status_out
+ *     untouched (SL_ERR_CUDA from a failed launch excepted).
+ *   - bf16 weights only (weight_dtype SL_WEIGHTS_BF16; others return
+ *     SL_ERR_UNSUPPORTED).
  * Calls no cudaMalloc / cudaFree / allocating library routine. */
 int sl_fused_experts_noalloc(const void* hidden, int T, int H, int I,
                              const void* w13, const void* w2, int num_slots,

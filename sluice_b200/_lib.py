@@ -144,7 +144,8 @@ def status_text(status: int) -> str:
         return lib().sl_status_string(int(status)).decode()
     except Exception:  # library not loadable: plain text
         return {0: "ok", 1: "overflow", 2: "invalid argument", 3: "CUDA error",
-                4: "unsupported", 5: "timeout"}.get(int(status), "unknown")
+                4: "unsupported", 5: "timeout",
+                6: "problem too large for the no-alloc scratch"}.get(int(status), "unknown")
 
 
 def check(rc: int, what: str) -> None:

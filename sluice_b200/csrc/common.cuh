@@ -29,6 +29,16 @@
 
 namespace sl {
 
+// The argument checks of run_fused (moe.cu), made before anything is enqueued:
+// SL_OK when a fused-experts call with these arguments (out_mode 0 bf16 out,
+// 1 fp32 partial, 2 fp32 partial added; phase -1 / 0 / 1) would launch its
+// kernels, else the status the call returns. Host only.
+int fused_experts_check(const void* hidden, int T, int H, int I, const sl_expert_weights& w,
+                        const float* topk_weights, const int32_t* topk_ids, int topk,
+                        const int32_t* expert_map, int global_n, int sh_t0, int sh_nt,
+                        const void* out, int out_mode, const void* workspace,
+                        size_t workspace_bytes, const void* fill_state, int phase);
+
 // Bounded waits give up after this many nanoseconds of %globaltimer.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 

@@ -47,7 +47,7 @@ enum {
 };
 
 struct WsLayout {
-  size_t items, pair_pos, x, act, z, counters, total;
+  size_t items, pair_pos, x, act, z, total;
   int max_items, max_rows;
 };
 
@@ -69,17 +69,6 @@ inline int choose_bn(int T, int topk, int S, bool fp8 = false) {
   return avg <= 16 ? 16 : avg <= 64 ? 64 : 128;
 }
 
-// SLUICE_FUSED=1 runs bf16 decode steps through the single persistent kernel
-// (moe_fused_kernel). Off by default: measured slower than the separate
-// PDL-chained GEMM + combine kernels (66-71 us vs 59 us per V2-Lite layer).
-inline bool fused_enabled() {
-  static const bool on = [] {
-    const char* v = getenv("SLUICE_FUSED");
-    return v && v[0] == '1';
-  }();
-  return on;
-}
-
 inline WsLayout ws_layout(int T, int topk, int H, int I, int S, int n_sh, int BN) {
   WsLayout w;
   const long P = static_cast<long>(T) * topk;
@@ -93,8 +82,6 @@ inline WsLayout ws_layout(int T, int topk, int H, int I, int S, int n_sh, int BN
   w.x = o; o += r256(sizeof(__nv_bfloat16) * size_t(w.max_rows) * H);
   w.act = o; o += r256(sizeof(__nv_bfloat16) * size_t(w.max_rows) * I);
   w.z = o; o += r256(sizeof(__nv_bfloat16) * size_t(w.max_rows) * H);
-  // fused kernel: tiles done per item (gate/up) and per 128-row stripe (down)
-  w.counters = o; o += r256(sizeof(int) * (size_t(w.max_items) + H / 128 + 1));
   w.total = o;
   return w;
 }
@@ -271,8 +258,7 @@ __global__ void __launch_bounds__(kAlignSmallThreads) align_small_kernel(
     int G, int S, int n_sh, int sh_t0, int sh_nt, int BN,
     const __nv_bfloat16* __restrict__ hs, int H,
     int32_t* __restrict__ ws_hdr, int4* __restrict__ items, int32_t* __restrict__ pair_pos,
-    __nv_bfloat16* __restrict__ X, int max_items, const uint8_t* __restrict__ fill_state,
-    int* __restrict__ counters, int n_counters) {
+    __nv_bfloat16* __restrict__ X, int max_items, const uint8_t* __restrict__ fill_state) {
   __shared__ int cnt[kMaxCode];
   __shared__ int ibase[kMaxCode];
   __shared__ int sp[kSmallP];    // slot of each pair, then its row
@@ -357,8 +343,6 @@ __global__ void __launch_bounds__(kAlignSmallThreads) align_small_kernel(
   __syncthreads();
   const int n_items = n_hit + n_fill;
   const bool lead = blockIdx.x == 0;
-  if (lead && counters != nullptr)
-    for (int i = tid; i < n_counters; i += nthr) counters[i] = 0;
   if (lead && tid == 0) {
     ws_hdr[WS_STATUS] = (n_items > max_items) ? SL_ERR_INVALID : SL_OK;
     ws_hdr[WS_NUM_ITEMS] = n_items <= max_items ? n_items : 0;
@@ -1248,330 +1232,6 @@ __global__ void __launch_bounds__(F8Cfg<BN, GATED>::kThreads, 1) moe_gemm_f8_ker
 }
 
 
-// ------------------------------------------------ fused persistent kernel
-// Decode-sized steps, bf16 weights: the gate/up GEMM, the down GEMM and the
-// weighted combine in ONE cooperative launch (one CTA per SM), so weight
-// tiles stream from HBM without a kernel boundary between the two GEMMs.
-// Tiles: gate/up tiles of the phase's items first, then down tiles, item by
-// item. Cross-CTA order comes from device counters in the workspace (zeroed
-// by the grouping kernel): done1[item] counts finished gate/up tiles — a
-// down tile's producer fetches its weight stages at once but its activation
-// stages only after done1[item] == gate/up tiles per item; done2[stripe]
-// counts finished down tiles of a 128-row output stripe — the CTA that
-// completes a stripe sums it for every token (fixed pair order). All waits
-// are bounded.
-__device__ __forceinline__ int ld_acquire(const int* p) {
-  int v;
-  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void fence_proxy_async_global() {
-  asm volatile("fence.proxy.async.global;" ::: "memory");
-}
-
-template <int BN, int STAGES, bool OUT_F32>
-__global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(
-    const __grid_constant__ CUtensorMap tm_w13, const __grid_constant__ CUtensorMap tm_w13sh,
-    const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w2,
-    const __grid_constant__ CUtensorMap tm_w2sh, const __grid_constant__ CUtensorMap tm_a,
-    const int32_t* __restrict__ ws_hdr, const int4* __restrict__ items,
-    const int32_t* __restrict__ pair_pos, const float* __restrict__ tw,
-    __nv_bfloat16* __restrict__ A, __nv_bfloat16* __restrict__ Z, void* __restrict__ out,
-    int* __restrict__ done1, int* __restrict__ done2, int S, int H, int I, int T, int topk,
-    int n_sh, int sh_t0, int sh_nt, float scale, int phase, int32_t* __restrict__ status) {
-  using Cfg = GemmCfg<BN, STAGES, true>;  // stage layout is the same for both GEMMs
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
-  __nv_bfloat16* sA = reinterpret_cast<__nv_bfloat16*>(smem);
-  __nv_bfloat16* sB = sA + STAGES * Cfg::kATile;
-  float* xchg = reinterpret_cast<float*>(sB + STAGES * Cfg::kBTile);
-  uint64_t* full = reinterpret_cast<uint64_t*>(xchg + 64 * kXchgStride);
-  uint64_t* empty = full + STAGES;
-  uint64_t* tfull = empty + STAGES;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* mma_done = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  volatile int* combine_flag = abort_flag + 1;
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m1 = I / 64, m2 = H / 128;
-  const int num_items = ws_hdr[WS_NUM_ITEMS];
-  const int n_hit = ws_hdr[WS_NUM_HIT_ITEMS];
-  const int lo = phase == 1 ? n_hit : 0;
-  const int hi = phase == 0 ? n_hit : num_items;
-  const int nit = hi > lo ? hi - lo : 0;
-  const int n1 = nit * m1, n2 = nit * m2;
-  const int num_tiles = n1 + n2;
-  if (ws_hdr[WS_STATUS] != SL_OK) return;
-  if (num_items == 0 && phase != 0) {
-    // no pair maps to a resident expert and there are no shared experts
-    const size_t n = static_cast<size_t>(T) * H;
-    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
-         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-      if constexpr (OUT_F32) static_cast<float*>(out)[i] = 0.f;
-      else static_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16(0.f);
-    }
-    return;
-  }
-  if (static_cast<int>(blockIdx.x) >= num_tiles) return;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      sl::mbar_init(&full[s], 1);
-      sl::mbar_init(&empty[s], 1);
-    }
-    for (int a = 0; a < 2; ++a) {
-      sl::mbar_init(&tfull[a], 1);
-      sl::mbar_init(&tempty[a], 4);
-    }
-    sl::mbar_init(mma_done, 1);
-    *abort_flag = 0;
-    sl::fence_barrier_init();
-    sl::tma_prefetch_desc(&tm_w13);
-    sl::tma_prefetch_desc(&tm_w13sh);
-    sl::tma_prefetch_desc(&tm_x);
-    sl::tma_prefetch_desc(&tm_w2);
-    sl::tma_prefetch_desc(&tm_w2sh);
-    sl::tma_prefetch_desc(&tm_a);
-  }
-  if (warp == 1) sl::tmem_alloc(tmem_slot, TileShape<BN, true>::kTmemCols);
-  sl::tc_fence_before();
-  __syncthreads();
-  sl::tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
-
-  if (warp == 0) {
-    // ------------------------------------------------------ TMA producer
-    if (sl::elect_one()) {
-      const uint64_t pol_w = sl::policy_evict_first();
-      const uint64_t pol_b = sl::policy_evict_last();
-      int stage = 0;
-      uint32_t phase_bit = 0;
-      uint32_t issued_phase_mask = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const bool g1 = tile < n1;
-        const int tt = g1 ? tile : tile - n1;
-        const int item = lo + tt / (g1 ? m1 : m2);
-        const int mt = tt % (g1 ? m1 : m2);
-        const int4 it = items[item];
-        const bool sh = it.x >= S;
-        const int e = sh ? it.x - S : it.x;
-        const CUtensorMap* tw_ = g1 ? (sh ? &tm_w13sh : &tm_w13) : (sh ? &tm_w2sh : &tm_w2);
-        const CUtensorMap* tb = g1 ? &tm_x : &tm_a;
-        const int row0 = g1 ? e * 2 * I + mt * 64 : e * H + mt * BM;
-        const int k_blocks = (g1 ? H : I) / BK;
-        // a down tile's activations exist once every gate/up tile of its item is done
-        bool dep_ok = g1;
-        int pend_n = 0;
-        int pend_stage[STAGES], pend_kb[STAGES];
-        auto flush = [&](bool block) -> bool {
-          if (!dep_ok) {
-            if (ld_acquire(&done1[item]) < m1) {
-              if (!block) return true;
-              const uint64_t t0 = sl::globaltimer();
-              while (ld_acquire(&done1[item]) < m1) {
-                if (*abort_flag || sl::globaltimer() - t0 > sl::kWaitLimitNs) return false;
-              }
-            }
-            fence_proxy_async_global();  // generic-proxy stores -> TMA reads
-            dep_ok = true;
-          }
-          for (int i = 0; i < pend_n; ++i)
-            sl::tma_load_2d(sB + pend_stage[i] * Cfg::kBTile, tb, &full[pend_stage[i]],
-                            pend_kb[i] * BK, it.y, pol_b);
-          pend_n = 0;
-          return true;
-        };
-        for (int kb = 0; kb < k_blocks; ++kb) {
-          if (*abort_flag || !sl::mbar_wait(&empty[stage], phase_bit ^ 1)) {
-            ok = false;
-            break;
-          }
-          sl::mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
-          __nv_bfloat16* a0 = sA + stage * Cfg::kATile;
-          sl::tma_load_2d(a0, tw_, &full[stage], kb * BK, row0, pol_w);
-          if (g1) sl::tma_load_2d(a0 + 64 * BK, tw_, &full[stage], kb * BK, row0 + I, pol_w);
-          pend_stage[pend_n] = stage;
-          pend_kb[pend_n] = kb;
-          ++pend_n;
-          if (!flush(pend_n == STAGES)) {
-            ok = false;
-            break;
-          }
-          issued_phase_mask = (issued_phase_mask & ~(1u << stage)) | (phase_bit << stage);
-          if (++stage == STAGES) {
-            stage = 0;
-            phase_bit ^= 1;
-          }
-        }
-        if (ok && pend_n && !flush(true)) ok = false;
-      }
-      if (!ok) {
-        atomicExch(status, SL_ERR_TIMEOUT);
-        *abort_flag = 1;
-        for (int s = 0; s < STAGES; ++s)
-          (void)sl::mbar_wait(&full[s], (issued_phase_mask >> s) & 1u);
-      }
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------- MMA issuer
-    if (sl::elect_one()) {
-      constexpr uint32_t idesc = sl::umma_idesc_bf16(BM, BN);
-      int stage = 0;
-      uint32_t phase_bit = 0;
-      int acc = 0;
-      uint32_t acc_phase = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        if (*abort_flag || !sl::mbar_wait(&tempty[acc], acc_phase ^ 1)) {
-          ok = false;
-          break;
-        }
-        sl::tc_fence_after();
-        const uint32_t d0 = tmem_base + acc * BN;
-        const int k_blocks = (tile < n1 ? H : I) / BK;
-        for (int kb = 0; kb < k_blocks; ++kb) {
-          if (*abort_flag || !sl::mbar_wait(&full[stage], phase_bit)) {
-            ok = false;
-            break;
-          }
-          sl::tc_fence_after();
-          const uint32_t a_addr = sl::smem_u32(sA + stage * Cfg::kATile);
-          const uint32_t b_addr = sl::smem_u32(sB + stage * Cfg::kBTile);
-#pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
-            sl::umma_bf16(d0, sl::umma_desc_sw128(a_addr + k * 32),
-                          sl::umma_desc_sw128(b_addr + k * 32), idesc, (kb | k) != 0);
-          sl::umma_commit(&empty[stage]);
-          if (++stage == STAGES) {
-            stage = 0;
-            phase_bit ^= 1;
-          }
-        }
-        if (!ok) break;
-        sl::umma_commit(&tfull[acc]);
-        if (++acc == 2) {
-          acc = 0;
-          acc_phase ^= 1;
-        }
-      }
-      if (!ok) {
-        atomicExch(status, SL_ERR_TIMEOUT);
-        *abort_flag = 1;
-      }
-      sl::umma_commit(mma_done);
-      (void)sl::mbar_wait(mma_done, 0);
-    }
-  } else {
-    // --------------------------------------------------------- epilogue
-    const int q = warp & 3;
-    const int et = threadIdx.x - 64;  // 0..127 across the four epilogue warps
-    int acc = 0;
-    uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      const bool ok = !*abort_flag && sl::mbar_wait(&tfull[acc], acc_phase);
-      if (epi_any(!ok)) {
-        atomicExch(status, SL_ERR_TIMEOUT);
-        *abort_flag = 1;
-        break;
-      }
-      sl::tc_fence_after();
-      const bool g1 = tile < n1;
-      const int tt = g1 ? tile : tile - n1;
-      const int item = lo + tt / (g1 ? m1 : m2);
-      const int mt = tt % (g1 ? m1 : m2);
-      const int4 it = items[item];
-      if (g1)
-        epilogue_tile<BN, true>(tmem_base + acc * BN, q, lane, it, mt, A, I, xchg);
-      else
-        epilogue_tile<BN, false>(tmem_base + acc * BN, q, lane, it, mt, Z, H, xchg);
-      sl::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) sl::mbar_arrive(&tempty[acc]);
-      if (++acc == 2) {
-        acc = 0;
-        acc_phase ^= 1;
-      }
-      // publish this tile: stores, then one counter increment (release)
-      __threadfence();
-      named_bar_sync(1, 128);
-      if (g1) {
-        if (et == 0) atomicAdd(&done1[item], 1);
-        continue;
-      }
-      if (et == 0) *combine_flag = (atomicAdd(&done2[mt], 1) + 1 == num_items);
-      named_bar_sync(1, 128);
-      if (!*combine_flag) continue;
-      // last down tile of stripe mt: out[t, stripe] for every token, four
-      // tokens at a time with all their loads in flight together
-      __threadfence();
-      const int col = mt * BM + et;
-      for (int t0 = 0; t0 < T; t0 += 4) {
-        float zr[4][8], wr[4][8], sv[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int t = t0 + u;
-          sv[u] = 0.f;
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            zr[u][j] = 0.f;
-            wr[u][j] = 0.f;
-            if (t < T && j < topk) {
-              const int pos = pair_pos[t * topk + j];
-              if (pos >= 0) {
-                zr[u][j] = __bfloat162float(Z[static_cast<size_t>(pos) * H + col]);
-                wr[u][j] = tw[t * topk + j];
-              }
-            }
-          }
-          if (t < T && n_sh > 0 && t >= sh_t0 && t < sh_t0 + sh_nt)
-            for (int i = 0; i < n_sh; ++i)
-              sv[u] += __bfloat162float(
-                  Z[static_cast<size_t>(ws_hdr[WS_SH_BASE + i] + t - sh_t0) * H + col]);
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int t = t0 + u;
-          if (t >= T) break;
-          float r = 0.f;
-#pragma unroll
-          for (int j = 0; j < 8; ++j) r = __fadd_rn(r, __fmul_rn(zr[u][j], wr[u][j]));
-          for (int j = 8; j < topk; ++j) {  // top-k beyond 8: plain loop
-            const int pos = pair_pos[t * topk + j];
-            if (pos >= 0)
-              r = __fadd_rn(r, __fmul_rn(__bfloat162float(Z[static_cast<size_t>(pos) * H + col]),
-                                         tw[t * topk + j]));
-          }
-          float o;
-          if constexpr (OUT_F32) {
-            o = r * scale;
-          } else {
-            o = sl::bf16_round(r);
-            if (scale != 1.f) o = sl::bf16_round(o * scale);
-          }
-          if (n_sh > 0 && t >= sh_t0 && t < sh_t0 + sh_nt)
-            o = (OUT_F32 ? sv[u] : sl::bf16_round(sv[u])) + o;
-          if constexpr (OUT_F32)
-            static_cast<float*>(out)[static_cast<size_t>(t) * H + col] = o;
-          else
-            static_cast<__nv_bfloat16*>(out)[static_cast<size_t>(t) * H + col] =
-                __float2bfloat16(o);
-        }
-      }
-    }
-  }
-  sl::tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    __syncwarp();
-    sl::tc_fence_after();
-    sl::tmem_dealloc(tmem_base, TileShape<BN, true>::kTmemCols);
-  }
-}
-
 // ---------------------------------------------------------------- combine
 // OUT_F32 = false: out = bf16(shared + bf16(scale * bf16(sum_j w z)))  (vLLM
 //   torch-native rounding chain, runner tail in bf16)
@@ -1718,39 +1378,6 @@ int launch_gemm_f8(const CUtensorMap& tw, const CUtensorMap& twsh, const CUtenso
   return SL_OK;
 }
 
-template <int BN, int STAGES, bool OUT_F32>
-int launch_fused(const CUtensorMap& w13, const CUtensorMap& w13sh, const CUtensorMap& x,
-                 const CUtensorMap& w2, const CUtensorMap& w2sh, const CUtensorMap& a,
-                 const int32_t* hdr, const int4* items, const int32_t* pair_pos,
-                 const float* tw, __nv_bfloat16* A, __nv_bfloat16* Z, void* out, int* done1,
-                 int* done2, int S, int H, int I, int T, int topk, int n_sh, int sh_t0,
-                 int sh_nt, float scale, int phase, int32_t* status, int max_items,
-                 cudaStream_t st) {
-  using Cfg = GemmCfg<BN, STAGES, true>;
-  auto kern = moe_fused_kernel<BN, STAGES, OUT_F32>;
-  static std::atomic<uint64_t> smem_set{0};
-  SL_CUDA_TRY(sl::ensure_smem_limit(kern, Cfg::kSmemBytes, smem_set));
-  const long max_tiles = static_cast<long>(max_items) * (I / 64 + H / 128);
-  int grid = sl_device_sm_count();
-  if (grid <= 0) return SL_ERR_CUDA;
-  if (max_tiles < grid) grid = static_cast<int>(max_tiles > 0 ? max_tiles : 1);
-  // co-residency of every CTA is required by the cross-CTA counters
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  SL_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, w13, w13sh, x, w2, w2sh, a, hdr, items, pair_pos,
-                                 tw, A, Z, out, done1, done2, S, H, I, T, topk, n_sh, sh_t0,
-                                 sh_nt, scale, phase, status));
-  return SL_OK;
-}
-
 template <int BN, int STAGES, bool GATED>
 int launch_gemm(const CUtensorMap& tw, const CUtensorMap& twsh, const CUtensorMap& tb,
                 const int32_t* hdr, const int4* items, __nv_bfloat16* out, int S, int K,
@@ -1781,16 +1408,13 @@ extern "C" size_t sl_fused_experts_workspace_bytes(int T, int topk, int H, int I
   return a > b ? a : b;
 }
 
-namespace {
-
-int run_fused(const void* hidden, int T, int H, int I, const sl_expert_weights& w,
-              const float* topk_weights, const int32_t* topk_ids, int topk,
-              const int32_t* expert_map, int global_n, int sh_t0, int sh_nt,
-              float routed_scaling_factor, void* out, int out_mode, void* workspace,
-              size_t workspace_bytes, cudaStream_t st, const void* fill_state = nullptr,
-              int phase = -1) {
-  // out_mode: 0 bf16 out; 1 fp32 partial written; 2 fp32 partial added to out
-  const bool out_f32 = out_mode != 0, accumulate = out_mode == 2;
+// Argument checks of every fused-experts entry point, made before anything is
+// enqueued (see common.cuh).
+int sl::fused_experts_check(const void* hidden, int T, int H, int I, const sl_expert_weights& w,
+                            const float* topk_weights, const int32_t* topk_ids, int topk,
+                            const int32_t* expert_map, int global_n, int sh_t0, int sh_nt,
+                            const void* out, int out_mode, const void* workspace,
+                            size_t workspace_bytes, const void* fill_state, int phase) {
   if (out_mode < 0 || out_mode > 2) return SL_ERR_INVALID;
   const int num_slots = w.num_slots, n_shared = w.n_shared;
   const bool fp8 = w.dtype == SL_WEIGHTS_FP8_BLOCK128;
@@ -1812,8 +1436,29 @@ int run_fused(const void* hidden, int T, int H, int I, const sl_expert_weights& 
     return SL_ERR_INVALID;
   if (fp8 && (H / 128 > kF8MaxKBlocks || I / 128 > kF8MaxKBlocks)) return SL_ERR_UNSUPPORTED;
   const int BN = choose_bn(T, topk, num_slots, fp8);
+  if (workspace_bytes < ws_layout(T, topk, H, I, num_slots, n_shared, BN).total)
+    return SL_ERR_INVALID;
+  return SL_OK;
+}
+
+namespace {
+
+int run_fused(const void* hidden, int T, int H, int I, const sl_expert_weights& w,
+              const float* topk_weights, const int32_t* topk_ids, int topk,
+              const int32_t* expert_map, int global_n, int sh_t0, int sh_nt,
+              float routed_scaling_factor, void* out, int out_mode, void* workspace,
+              size_t workspace_bytes, cudaStream_t st, const void* fill_state = nullptr,
+              int phase = -1) {
+  // out_mode: 0 bf16 out; 1 fp32 partial written; 2 fp32 partial added to out
+  const int rc0 = sl::fused_experts_check(hidden, T, H, I, w, topk_weights, topk_ids, topk,
+                                          expert_map, global_n, sh_t0, sh_nt, out, out_mode,
+                                          workspace, workspace_bytes, fill_state, phase);
+  if (rc0 != SL_OK || T == 0) return rc0;
+  const bool out_f32 = out_mode != 0, accumulate = out_mode == 2;
+  const int num_slots = w.num_slots, n_shared = w.n_shared;
+  const bool fp8 = w.dtype == SL_WEIGHTS_FP8_BLOCK128;
+  const int BN = choose_bn(T, topk, num_slots, fp8);
   const WsLayout L = ws_layout(T, topk, H, I, num_slots, n_shared, BN);
-  if (workspace_bytes < L.total) return SL_ERR_INVALID;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   int32_t* hdr = reinterpret_cast<int32_t*>(ws);
   int4* items = reinterpret_cast<int4*>(ws + L.items);
@@ -1851,11 +1496,6 @@ int run_fused(const void* hidden, int T, int H, int I, const sl_expert_weights& 
   // group in one CTA and gather with a grid-wide kernel
   const int P = T * topk;
   const bool small = P <= kSmallP && (num_slots + nsh) <= kMaxCode;
-  int* counters = reinterpret_cast<int*>(ws + L.counters);
-  const int n_counters = L.max_items + H / 128 + 1;
-  // bf16 decode-sized steps: one persistent kernel for both GEMMs + combine
-  // (which writes its output; an accumulating call runs the separate kernels)
-  const bool fused = small && !fp8 && !accumulate && fused_enabled();
   if (phase != 1) {
     if (small) {
       SL_CUDA_TRY(sl::launch(align_small_kernel, dim3(kAlignSmallCtas), dim3(kAlignSmallThreads),
@@ -1863,8 +1503,7 @@ int run_fused(const void* hidden, int T, int H, int I, const sl_expert_weights& 
                              nsh ? sh_t0 : 0, nsh ? sh_nt : 0, BN,
                              static_cast<const __nv_bfloat16*>(hidden), H, hdr, items, pair_pos,
                              fp8 ? nullptr : X, L.max_items,
-                             static_cast<const uint8_t*>(fill_state),
-                             fused ? counters : nullptr, n_counters));
+                             static_cast<const uint8_t*>(fill_state)));
     } else {
       SL_CUDA_TRY(sl::launch(align_kernel, dim3(1), dim3(1024), 0, st, topk_ids, T, topk,
                              expert_map, global_n, num_slots, nsh, nsh ? sh_t0 : 0,
@@ -1891,24 +1530,6 @@ int run_fused(const void* hidden, int T, int H, int I, const sl_expert_weights& 
                              nsh ? sh_t0 : 0, nsh ? sh_nt : 0,
                              static_cast<const __nv_bfloat16*>(hidden), H, Xq, Xs, L.max_rows));
     }
-  }
-  if (fused) {
-    int* done1 = counters;
-    int* done2 = counters + L.max_items;
-#define SL_FUSED(BNV, STV)                                                                      \
-    (out_f32 ? launch_fused<BNV, STV, true>(m_w13, m_w13sh, m_x, m_w2, m_w2sh, m_a, hdr, items, \
-                                            pair_pos, topk_weights, A, Z, out, done1, done2,   \
-                                            num_slots, H, I, T, topk, nsh, sh_t0, sh_nt,       \
-                                            routed_scaling_factor, phase, hdr, L.max_items, st) \
-             : launch_fused<BNV, STV, false>(m_w13, m_w13sh, m_x, m_w2, m_w2sh, m_a, hdr,      \
-                                             items, pair_pos, topk_weights, A, Z, out, done1,  \
-                                             done2, num_slots, H, I, T, topk, nsh, sh_t0,      \
-                                             sh_nt, routed_scaling_factor, phase, hdr,         \
-                                             L.max_items, st))
-    if (BN == 16) return SL_FUSED(16, 12);
-    if (BN == 64) return SL_FUSED(64, 9);
-    return SL_FUSED(128, 6);
-#undef SL_FUSED
   }
   int rc = SL_OK;
 #define SL_GEMMS_BF16(BNV, S1, S2)                                                              \

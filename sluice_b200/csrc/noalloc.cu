@@ -75,6 +75,9 @@ extern "C" int sl_fused_experts_noalloc(const void* hidden, int T, int H, int I,
                                         const void* shared_w13, const void* shared_w2,
                                         int n_shared, float routed_scaling_factor, void* out,
                                         int32_t* status_out, sl_stream_t stream) {
+  // Every argument is checked before anything is enqueued, so an error return
+  // leaves the stream, the scratch and status_out untouched.
+  if (weight_dtype != SL_WEIGHTS_BF16) return SL_ERR_UNSUPPORTED;
   const size_t need =
       sl_fused_experts_workspace_bytes(T, topk, H, I, num_slots, n_shared);
   if (need == 0) return SL_ERR_INVALID;
@@ -82,7 +85,26 @@ extern "C" int sl_fused_experts_noalloc(const void* hidden, int T, int H, int I,
   void* scratch = nullptr;
   int rc = scratch_for_current_device(&scratch);
   if (rc != SL_OK) return rc;
+  sl_expert_weights w = {};
+  w.w13 = w13;
+  w.w2 = w2;
+  w.num_slots = num_slots;
+  w.shared_w13 = shared_w13;
+  w.shared_w2 = shared_w2;
+  w.n_shared = n_shared;
+  w.dtype = SL_WEIGHTS_BF16;
+  rc = sl::fused_experts_check(hidden, T, H, I, w, topk_weights, topk_ids, topk, expert_map,
+                               global_n, 0, T, out, 0, scratch, kNoAllocScratchBytes, nullptr,
+                               -1);
+  if (rc != SL_OK) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (T == 0) {  // nothing to compute: report success
+    if (status_out != nullptr && cudaMemsetAsync(status_out, 0, sizeof(int32_t), st) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return SL_ERR_CUDA;
+    }
+    return SL_OK;
+  }
   if (cudaMemsetAsync(scratch, 0, 256, st) != cudaSuccess) {
     (void)cudaGetLastError();
     return SL_ERR_CUDA;

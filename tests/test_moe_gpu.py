@@ -184,34 +184,6 @@ def test_prefill_sized_steps(T, H, I, S, E, k, fp8):
     assert_moe_close(out, omoe.fused_experts(hs, w13, w2, tw, ti, emap, **ref_kw), rtol=rtol)
 
 
-def test_persistent_fused_kernel_path_in_a_subprocess():
-    """The opt-in single-kernel path (SLUICE_FUSED=1, read once per process)
-    must match the oracle like the default path."""
-    import subprocess
-    import sys
-    code = r"""
-import sys, torch
-sys.path.insert(0, {root!r}); sys.path.insert(0, {tests!r})
-from test_moe_gpu import _random_case, _reference, assert_moe_close
-from sluice_b200 import ops
-for (T, H, I, S, E, k, n_sh, scale) in [(8, 2048, 1408, 48, 64, 6, 2, 1.0),
-                                       (5, 256, 128, 6, 8, 3, 1, 2.5)]:
-    hs, w13, w2, emap, ti, tw, sh13, sh2 = _random_case(T, H, I, S, E, k, n_sh, seed=T)
-    c = lambda t: None if t is None else t.cuda()
-    out = ops.fused_experts(c(hs), c(w13), c(w2), c(tw), c(ti), global_num_experts=E,
-                            expert_map=c(emap), shared_w13=c(sh13), shared_w2=c(sh2),
-                            routed_scaling_factor=scale)
-    torch.cuda.synchronize()
-    assert_moe_close(out, _reference(hs, w13, w2, emap, ti, tw, sh13, sh2, scale))
-print("ok")
-"""
-    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    env = dict(os.environ, SLUICE_FUSED="1")
-    r = subprocess.run([sys.executable, "-c", code.format(root=root, tests=os.path.dirname(
-        os.path.abspath(__file__)))], env=env, capture_output=True, text=True, timeout=600)
-    assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
-
-
 def test_empty_step_and_oversized_slot_count():
     """T = 0 returns an empty output without launching work; more slots plus
     shared experts than the grouping step handles (1056) is refused with an
