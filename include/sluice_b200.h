@@ -68,6 +68,14 @@ int sl_route(const void* hidden, const void* gate_w, const float* logit_bias,
              const float* score_bias, float* topk_weights, int32_t* topk_ids,
              void* router_logits_out, sl_stream_t stream);
 
+/* The gate linear alone: router_logits_out (bf16 [T, E]) = bf16(hidden @
+ * gate_w^T + logit_bias), the same logits sl_route computes. Replaces
+ * `rl, _ = gate(hs)` of the router-split entry (offloader.py:2582; vLLM's
+ * bf16 ReplicatedLinear gate). logit_bias may be NULL. Limits: H % 8 == 0,
+ * 16-byte aligned hidden / gate_w. */
+int sl_gate(const void* hidden, const void* gate_w, const float* logit_bias,
+            int T, int H, int E, void* router_logits_out, sl_stream_t stream);
+
 /* select_experts from given bf16 router logits [T, E]
  * (vLLM router/base_router.py:250-298). Same arithmetic as sl_route. */
 int sl_select_experts(const void* router_logits, int T, int E, int topk,

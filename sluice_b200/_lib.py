@@ -63,6 +63,7 @@ _SIGNATURES = {
     "sl_device_sm_count": (_i, []),
     "sl_route": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp, _vp,
                       _vp, _vp, _vp]),
+    "sl_gate": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp]),
     "sl_select_experts": (_i, [_vp, _i, _i, _i, _i, _i, _i, _i, _f, _vp, _vp, _vp,
                                _vp]),
     "sl_slot_state_bytes": (_sz, [_i, _i, _i]),

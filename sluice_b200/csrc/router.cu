@@ -262,6 +262,23 @@ extern "C" int sl_select_experts(const void* router_logits, int T, int E, int to
   return SL_OK;
 }
 
+extern "C" int sl_gate(const void* hidden, const void* gate_w, const float* logit_bias, int T,
+                       int H, int E, void* router_logits_out, sl_stream_t stream) {
+  if (T < 0 || E <= 0 || E > 65535) return SL_ERR_INVALID;
+  if (H <= 0 || H % 8) return SL_ERR_UNSUPPORTED;
+  if (T == 0) return SL_OK;
+  if (!hidden || !gate_w || !router_logits_out) return SL_ERR_INVALID;
+  if ((reinterpret_cast<uintptr_t>(hidden) | reinterpret_cast<uintptr_t>(gate_w)) & 15)
+    return SL_ERR_INVALID;
+  dim3 grid(E, (T + kTokTile - 1) / kTokTile);
+  SL_CUDA_TRY(sl::launch(gate_kernel, grid, dim3(kGateThreads), 0,
+                         reinterpret_cast<cudaStream_t>(stream),
+                         static_cast<const __nv_bfloat16*>(hidden),
+                         static_cast<const __nv_bfloat16*>(gate_w), logit_bias, T, H, E,
+                         static_cast<__nv_bfloat16*>(router_logits_out)));
+  return SL_OK;
+}
+
 extern "C" int sl_route(const void* hidden, const void* gate_w, const float* logit_bias,
                         int T, int H, int E, int topk, int scoring,
                         int num_expert_group, int topk_group, int renormalize,

@@ -3,7 +3,8 @@
 * ``Router.select_experts(hidden_states, router_logits, *, input_ids=None)``
   mirrors vLLM's ``BaseRouter.select_experts`` (``router/base_router.py``
   250-298) as called at ``offloader.py:2583-2585``; ``Router.gate`` is the
-  bf16 gate linear (``offloader.py:2582``) fused with the selection.
+  bf16 gate linear (``offloader.py:2582``) and ``Router.route`` the gate
+  fused with the selection.
 * ``sluice_stream_gap(hidden_states, topk_ids, layer_idx)`` mirrors the
   custom op ``vllm::sluice_stream_gap`` (``offloader.py:2311-2331``): it runs
   the slot planner and the expert streamer of the registered layer and
@@ -14,6 +15,9 @@
   ``torch.ops.vllm.fused_experts`` as called at ``offloader.py:2590-2599``,
   with the shared experts and routed scaling fused into its combine.
   Registered as ``torch.ops.sluice.fused_experts``.
+* ``register_reference_names()`` registers the same ops under the names the
+  reference's router-split entry calls, ``torch.ops.vllm.sluice_stream_gap``
+  and ``torch.ops.vllm.fused_experts``, so that entry runs unedited.
 
 All calls enqueue on the current CUDA stream and never synchronise, so they
 can be captured in a CUDA graph.
@@ -79,6 +83,19 @@ class Router:
                                       int(r.renormalize), 1.0, ptr(self.score_bias),
                                       ptr(w), ptr(ids), _stream()), "sl_select_experts")
         return w, ids
+
+    def gate(self, hidden_states: torch.Tensor):
+        """The gate linear: ``(router_logits bf16 [T, E], None)``, the
+        ``(output, bias)`` pair of vLLM's gate module that the router-split
+        entry unpacks as ``rl, _ = gate(hs)`` (offloader.py:2582)."""
+        _need_cuda(hidden_states, self.gate_weight)
+        hs = hidden_states.contiguous()
+        T, H = hs.shape
+        E = self.gate_weight.shape[0]
+        logits = torch.empty(T, E, dtype=torch.bfloat16, device=hs.device)
+        check(lib().sl_gate(ptr(hs), ptr(self.gate_weight), ptr(self.logit_bias), T, H, E,
+                            ptr(logits), _stream()), "sl_gate")
+        return logits, None
 
     def route(self, hidden_states: torch.Tensor, logits_out: torch.Tensor | None = None):
         """Fused gate GEMV + selection: (topk_weights, topk_ids, router_logits)."""
@@ -306,3 +323,66 @@ def _fe_fake(hidden_states, w1, w2, topk_weights, topk_ids, activation="silu",
              global_num_experts=-1, expert_map=None, w1_scale=None, w2_scale=None,
              shared_w13=None, shared_w2=None, routed_scaling_factor=1.0):
     return torch.empty_like(hidden_states)
+
+
+# ------------------------------------------- the reference's own op names
+# The reference's router-split entry (offloader.py:2578-2603) calls
+# torch.ops.vllm.sluice_stream_gap, which the reference registers itself
+# (_register_stream_gap_op, offloader.py:2296-2331), and
+# torch.ops.vllm.fused_experts, vLLM's fused-MoE op. Registering this build's
+# ops under those names lets that entry run unedited on the sm_100a path.
+_VLLM_LIB = None
+
+
+def _vllm_op_exists(name: str) -> bool:
+    try:
+        getattr(torch.ops.vllm, name)
+        return True
+    except (AttributeError, RuntimeError):
+        return False
+
+
+def register_reference_names() -> list[str]:
+    """Register ``vllm::sluice_stream_gap`` (the reference's schema:
+    ``(Tensor hidden_states, Tensor topk_ids, int layer_idx) -> Tensor``,
+    ``mutates_args=[]``, a fake returning ``empty_like``) and, where no
+    ``vllm::fused_experts`` is loaded, ``vllm::fused_experts(hidden_states,
+    w1, w2, topk_weights, topk_ids, activation='silu', global_num_experts=-1,
+    expert_map=None, w1_scale=None, w2_scale=None)`` — the routed experts
+    only, as the reference's entry expects (its caller adds the shared
+    experts). Names already defined (the reference plugin's own gap op, or a
+    vLLM build that has ``fused_experts``) are left alone. Returns the names
+    this call registered; calling it again registers nothing."""
+    global _VLLM_LIB
+    done = []
+    want = [n for n in ("sluice_stream_gap", "fused_experts") if not _vllm_op_exists(n)]
+    if not want:
+        return done
+    if _VLLM_LIB is None:
+        _VLLM_LIB = torch.library.Library("vllm", "FRAGMENT")
+    lib_ = _VLLM_LIB
+    if "sluice_stream_gap" in want:
+        lib_.define("sluice_stream_gap(Tensor hidden_states, Tensor topk_ids, int layer_idx) "
+                    "-> Tensor")
+        lib_.impl("sluice_stream_gap", sluice_stream_gap, "CUDA")
+        lib_._register_fake("sluice_stream_gap", _gap_fake)
+        done.append("vllm::sluice_stream_gap")
+    if "fused_experts" in want:
+        lib_.define(
+            "fused_experts(Tensor hidden_states, Tensor w1, Tensor w2, Tensor topk_weights, "
+            "Tensor topk_ids, str activation='silu', int global_num_experts=-1, "
+            "Tensor? expert_map=None, Tensor? w1_scale=None, Tensor? w2_scale=None) -> Tensor")
+        lib_.impl(
+            "fused_experts",
+            lambda hs, w1, w2, tw, ti, activation="silu", global_num_experts=-1,
+            expert_map=None, w1_scale=None, w2_scale=None: fused_experts(
+                hs, w1, w2, tw, ti, activation=activation,
+                global_num_experts=global_num_experts, expert_map=expert_map,
+                w1_scale=w1_scale, w2_scale=w2_scale),
+            "CUDA")
+        lib_._register_fake(
+            "fused_experts",
+            lambda hs, w1, w2, tw, ti, activation="silu", global_num_experts=-1,
+            expert_map=None, w1_scale=None, w2_scale=None: torch.empty_like(hs))
+        done.append("vllm::fused_experts")
+    return done

@@ -366,3 +366,37 @@ def test_c_host_links_and_calls_the_library(tmp_path):
     r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
     assert r.returncode == 0, r.stderr
     assert "c host ok" in r.stdout
+
+
+def test_reference_op_names_registered_with_the_reference_schema():
+    """The router-split entry of the reference calls
+    torch.ops.vllm.sluice_stream_gap(hs, ti, idx) (its own op, offloader.py
+    2296-2331) and torch.ops.vllm.fused_experts(h, w13, w2, tw, ti,
+    activation=, global_num_experts=, expert_map=) (2590-2599): both names
+    resolve after register_reference_names(), with those argument names, and
+    their fakes give the output's shape without running anything."""
+    import torch
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    from sluice_b200 import ops
+
+    ops.register_reference_names()
+    assert ops.register_reference_names() == []  # idempotent
+    gap = torch.ops.vllm.sluice_stream_gap.default._schema
+    assert [a.name for a in gap.arguments] == ["hidden_states", "topk_ids", "layer_idx"]
+    assert not any(a.alias_info for a in gap.arguments)  # mutates_args=[]
+    fe = torch.ops.vllm.fused_experts.default._schema
+    names = [a.name for a in fe.arguments]
+    assert names[:8] == ["hidden_states", "w1", "w2", "topk_weights", "topk_ids",
+                         "activation", "global_num_experts", "expert_map"]
+    with FakeTensorMode():
+        hs = torch.empty(8, 2048, dtype=torch.bfloat16)
+        ti = torch.empty(8, 6, dtype=torch.int32)
+        tw = torch.empty(8, 6)
+        w13 = torch.empty(48, 2816, 2048, dtype=torch.bfloat16)
+        w2 = torch.empty(48, 2048, 1408, dtype=torch.bfloat16)
+        emap = torch.empty(64, dtype=torch.int32)
+        assert torch.ops.vllm.sluice_stream_gap(hs, ti, 0).shape == hs.shape
+        out = torch.ops.vllm.fused_experts(hs, w13, w2, tw, ti, activation="silu",
+                                           global_num_experts=64, expert_map=emap)
+        assert out.shape == hs.shape and out.dtype == torch.bfloat16
