@@ -37,6 +37,8 @@ import torch  # noqa: E402
 
 METRIC = "decode tok/s"
 UNIT = "tok/s"
+# PCIe Gen5 x16 host link: 32 GT/s x 16 lanes x 128/130 encoding / 8 bits
+PCIE_GEN5_X16_GBS = 63.0
 
 
 def _args(argv=None):
@@ -46,7 +48,13 @@ def _args(argv=None):
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="sluice", choices=["sluice", "reference"])
     ap.add_argument("--config", default="deepseek-v2-lite")
-    ap.add_argument("--slots", type=int, default=48)
+    ap.add_argument("--slots", type=int, default=None,
+                    help="GPU slots per layer and rank (default: --slots-frac of the local experts)")
+    ap.add_argument("--slots-frac", type=float, default=0.75,
+                    help="slots per layer as a fraction of each rank's local experts")
+    ap.add_argument("--sweep", default="32,40,56",
+                    help="slot counts of the one-GPU slots sweep (besides --slots and resident)")
+    ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--tokens", type=int, default=8)
     ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--prefill-steps", type=int, default=24,
@@ -72,6 +80,27 @@ def _args(argv=None):
     ap.add_argument("--gemm-experts", type=int, default=256,
                     help="experts of the grouped-GEMM microbench (a smaller profiling case)")
     return ap.parse_args(argv)
+
+
+def _slots_for(a, cfg, world=1) -> int:
+    """GPU slots per layer on each rank: --slots, else --slots-frac of the
+    rank's local experts (never more than them)."""
+    local_n = cfg.num_experts // world
+    s = a.slots if a.slots is not None else max(1, round(a.slots_frac * local_n))
+    return min(s, local_n)
+
+
+def _config(a, cfg, slots, T, layers, world):
+    """The workload's config, identical in the GPU arm and the reference arm
+    for the same arguments (facts about one arm's run go elsewhere)."""
+    local_n = cfg.num_experts // world
+    return {"workload": _workload(cfg, slots, T, layers, world), "model": cfg.name,
+            "tokens_per_step": T, "slots": slots, "slots_frac": slots / local_n,
+            "layers": layers, "global_batch": T * world, "seq_len": 1,
+            "parallelism": f"ep{world}" if world > 1 else "single",
+            "slot_policy": "slru+lfu" if a.lfu else "slru", "local_experts": local_n,
+            "offloaded": slots < local_n, "cache_prefill_steps": a.prefill_steps,
+            "l2": "per-step expert weights >> 126 MB L2 (no flush needed)"}
 
 
 def _workload(cfg, slots, tokens, layers, world=1):
@@ -191,7 +220,7 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------- CPU port
-def cpu_layer_runner(cfg, seed, n_weight_sets=2):
+def cpu_layer_runner(cfg, seed, n_weight_sets=1):
     """The reference's torch-native CPU path for one layer (oracle port):
     gate + routing, the gap's slot policy, the MoE with shared experts."""
     from oracle import moe as omoe
@@ -247,7 +276,7 @@ def cpu_step_time(cfg, slots, tokens, layers, seed, steps, warmup, budget_s=None
     with ``decode=False`` a prefill-sized one (fresh random tokens)."""
     from sluice_b200 import synth
 
-    run = cpu_layer_runner(cfg, seed)
+    run = cpu_layer_runner(cfg, seed, n_weight_sets=layers)
     stream = synth.TokenStream(cfg.hidden, tokens, seed=seed, reuse=0.6 if decode else 0.0)
     times = []
     t_start = time.perf_counter()
@@ -454,6 +483,152 @@ def layer_launches(cfg, tokens, world, slots, exchange="nvlink", no_overlap=Fals
     return 2 + 2 + (align + 3 if no_overlap else align + 5) + ex
 
 
+def _stack_save(stack):
+    """Device copies of every offloaded layer's planner state, map and slots,
+    or None when they would not fit in 80% of free HBM."""
+    need = sum(sum(t.numel() * t.element_size() for t in layer.cache.gpu_cache.values())
+               for layer in stack.layers if not layer.cache.static_full)
+    if need > 0.8 * torch.cuda.mem_get_info()[0]:
+        return None
+    return [None if layer.cache.static_full else layer.cache.save() for layer in stack.layers]
+
+
+def _stack_restore(stack, snap) -> None:
+    for layer, sv in zip(stack.layers, snap):
+        if sv is not None:
+            layer.cache.restore(sv)
+    torch.cuda.synchronize()
+
+
+def _misses(s0, s1):
+    """Experts missed (gap misses + misses of wave-planned steps) and streamed."""
+    m = sum(s1.get(k, 0) - s0.get(k, 0) for k in ("misses", "scan_misses"))
+    return m, s1.get("fills", 0) - s0.get("fills", 0)
+
+
+def _max_over_ranks(v, dist):
+    if not dist:
+        return v
+    t = torch.tensor([v], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _sum_over_ranks(vals, dist):
+    if not dist:
+        return vals
+    t = torch.tensor(vals, device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return t.tolist()
+
+
+def _timed_replays(stack, xs, W, K, dist, clocks=True):
+    """ms for K graph replays on xs[W:W+K] (barrier + synchronize on both
+    sides, CUDA events on the replaying stream, max over ranks), with the
+    slot-cache counters before and after and the SM clocks sampled meanwhile."""
+    s0 = stack.stats()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clk = ClockSampler(torch.cuda.current_device()) if clocks else None
+    if clk:
+        clk.__enter__()
+    ev0.record()
+    for i in range(K):
+        stack.replay(xs[W + i])
+    ev1.record()
+    torch.cuda.synchronize()
+    if clk:
+        clk.__exit__()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    stack.check()
+    ms = _max_over_ranks(ev0.elapsed_time(ev1), dist)
+    return ms, s0, stack.stats(), (clk.summary() if clk else None)
+
+
+def _stream_launch_window(stack, xs, W, K, bpe):
+    """Every expert-stream launch of K steps replayed on xs[W:W+K], each step
+    synchronised so that its launches' CUDA events (recorded on the stream
+    the streamer runs on, inside the captured graph) and fill counts can be
+    read: [(ms, bytes)] per launch."""
+    rows = []
+    for i in range(K):
+        stack.replay(xs[W + i])
+        torch.cuda.synchronize()
+        for layer in stack.layers:
+            if layer.stream_timer is None or layer.cache.static_full:
+                continue
+            la = layer.stream_timer.launches()
+            waves = any(w >= 0 for _, w in la)
+            counts = layer.cache.last_fill_counts(wave_steps=waves)
+            for ms, w in la:
+                rows.append((ms, (counts[w] if w >= 0 else counts[0]) * bpe))
+    return rows
+
+
+def _step_roofline(hbm_step, host_step, t_ms, hbm_peak):
+    t_roof = max(hbm_step / (hbm_peak * 1e9), host_step / PCIE_GEN5_X16_GBS / 1e9) * 1e3
+    return {"t_roof_ms": t_roof, "t_ms": t_ms, "frac": t_roof / t_ms,
+            "hbm_bytes_per_step": hbm_step, "host_bytes_per_step": host_step,
+            "host_peak_gbs": PCIE_GEN5_X16_GBS, "hbm_peak_gbs": hbm_peak,
+            "bound": "host link" if host_step / PCIE_GEN5_X16_GBS > hbm_step / hbm_peak
+            else "hbm"}
+
+
+def _build_stack(cfg, slots, layers, T, a, world, timers=False):
+    from sluice_b200.layer import MoEDecodeStack, StreamTimer
+
+    if world > 1:
+        from sluice_b200.ep import EPDecodeStack
+        stack = EPDecodeStack(cfg, slots=slots, seed=a.seed, num_layers=layers,
+                              exchange=a.exchange, max_tokens=T, overlap=not a.no_overlap)
+    else:
+        stack = MoEDecodeStack(cfg, slots=slots, seed=a.seed, num_layers=layers,
+                               overlap=not a.no_overlap)
+    if timers:
+        for layer in stack.layers:
+            layer.stream_timer = StreamTimer()
+    graphed = stack.capture(tokens=T)
+    return stack, (True if graphed is None else bool(graphed))
+
+
+def _sweep_point(a, cfg, slots, layers, K, W, hbm_peak):
+    """One point of decode tok/s against the slot count (one GPU): c=T and
+    c=1 on fresh caches, with misses per step and the step roofline."""
+    from sluice_b200 import synth
+
+    out = {"slots": slots, "slots_frac": slots / cfg.num_experts}
+    for T in (a.tokens, 1):
+        stack, _ = _build_stack(cfg, slots, layers, T, a, 1)
+        stream = synth.TokenStream(cfg.hidden, T, seed=a.seed + 100)
+        for _ in range(a.prefill_steps):
+            stack.replay(stream.next().cuda())
+        xs = torch.stack([stream.next() for _ in range(W + K)]).cuda()
+        for i in range(W):
+            stack.replay(xs[i])
+        torch.cuda.synchronize()
+        ms, s0, s1, clk = _timed_replays(stack, xs, W, K, None)
+        m, f = _misses(s0, s1)
+        roof = _step_roofline(_step_bytes(stack, cfg), f / K * cfg.bytes_per_expert, ms / K,
+                              hbm_peak)
+        out[f"c{T}"] = {"value": T * K / (ms * 1e-3), "unit": UNIT, "ms_per_step": ms / K,
+                        "misses_per_step": m / K, "step_roofline_frac": roof["frac"],
+                        "clocks": clk}
+        del stack, xs
+        _free()
+    return out
+
+
+def _free():
+    import gc
+
+    gc.collect()
+    torch.cuda.empty_cache()
+
+
 def run_sluice(a):
     import datetime
 
@@ -461,7 +636,6 @@ def run_sluice(a):
         os.environ["SLUICE_LFU"] = "1"
 
     from sluice_b200 import configs, synth
-    from sluice_b200.layer import MoEDecodeStack
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -475,17 +649,20 @@ def run_sluice(a):
     cfg = configs.CONFIGS[a.config]
     layers = a.layers or cfg.num_moe_layers
     T = a.tokens
+    local_n = cfg.num_experts // world
+    slots = _slots_for(a, cfg, world)
+    offloaded = slots < local_n
+    bpe = cfg.bytes_per_expert
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except Exception:
+        pass
+    hbm_peak = peaks.get("hbm_gbs", 6650.0)
+
     t_build = time.perf_counter()
-    if world > 1:
-        from sluice_b200.ep import EPDecodeStack
-        stack = EPDecodeStack(cfg, slots=a.slots, seed=a.seed, num_layers=layers,
-                              exchange=a.exchange, max_tokens=T, overlap=not a.no_overlap)
-        graphed = stack.capture(tokens=T)
-    else:
-        stack = MoEDecodeStack(cfg, slots=a.slots, seed=a.seed, num_layers=layers,
-                               overlap=not a.no_overlap)
-        stack.capture(tokens=T)
-        graphed = True
+    stack, graphed = _build_stack(cfg, slots, layers, T, a, world, timers=offloaded)
     build_s = time.perf_counter() - t_build
     stream = synth.TokenStream(cfg.hidden, T, seed=a.seed + 100 + rank)
     # preconditioning: fill the slot caches, then the W warm-up steps
@@ -497,170 +674,188 @@ def run_sluice(a):
     for i in range(W):
         stack.replay(xs[i])
     torch.cuda.synchronize()
-    stats_w = stack.stats()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
-    with ClockSampler(torch.cuda.current_device()) as clk:
-        ev0.record()
-        for i in range(K):
-            stack.replay(xs[W + i])
-        ev1.record()
-        torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
-    stack.check()
-    stats_t = stack.stats()
-    ms = ev0.elapsed_time(ev1)
-    if dist:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    # the e2e and stream-timing windows replay the timed window's inputs from
+    # the same cache state (planner state, maps and slot contents restored)
+    snap = _stack_save(stack)
+    restored = _max_over_ranks(0.0 if snap is not None else 1.0, dist) == 0.0
+    ms, s0, s1, clocks = _timed_replays(stack, xs, W, K, dist)
     value = world * T * K / (ms * 1e-3)
+    misses, fills = _misses(s0, s1)
+    misses, fills = _sum_over_ranks([misses, fills], dist)
     hbm_step = _step_bytes(stack, cfg)
 
     # end to end through the public call: pinned host in, host out
-    xh = torch.stack([stream.next() for _ in range(K)]).pin_memory()
+    if restored:
+        _stack_restore(stack, snap)
+    xh = xs[W:W + K].cpu().pin_memory()
     oh = torch.empty(K, T, cfg.hidden, dtype=torch.bfloat16).pin_memory()
-    stack.decode_step(xh[0], oh[0])
-    torch.cuda.synchronize()
+    se0 = stack.stats()
     if dist:
         dist.barrier()
+    torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for i in range(K):
         stack.decode_step(xh[i], oh[i])
     e1.record()
     torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
-    if dist:
-        t = torch.tensor([e2e_ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    e2e_ms = _max_over_ranks(e0.elapsed_time(e1), dist)
     stack.check()
+    e2e_misses, _ = _misses(se0, stack.stats())
+    e2e_misses = _sum_over_ranks([e2e_misses], dist)[0]
+
+    # the dominant kernel of an offloaded step: the expert streamer, each
+    # launch timed by CUDA events on its own (side) stream inside the graph
+    stream_rows = []
+    if offloaded:
+        if restored:
+            _stack_restore(stack, snap)
+        stream_rows = _stream_launch_window(stack, xs, W, K, bpe)
+    del snap
+    st_bytes, st_ms, st_n = _sum_over_ranks(
+        [float(sum(b for _, b in stream_rows)), float(sum(t for t, _ in stream_rows)),
+         float(len(stream_rows))], dist)
+    h2d = h2d_ceiling_gbs()
+    host_step = fills / K * bpe / world   # per rank: each streams over its own link
+    step_roof = _step_roofline(hbm_step, host_step, ms / K, hbm_peak)
+    traffic = load_traffic()
+
+    roof_stream = None
+    if st_n and st_ms > 0:
+        gbs = st_bytes / (st_ms * 1e-3) / 1e9
+        per_launch = st_bytes / st_n
+        ratio = traffic.get("stream_kernel_dram_bytes_per_streamed_byte")
+        pcie = traffic.get("stream_kernel_pcie_read_bytes_per_streamed_byte")
+        roof_stream = {
+            "bound": "host link", "kernel": "stream_kernel (expert streamer, side stream)",
+            "achieved": gbs, "peak": PCIE_GEN5_X16_GBS, "unit": "GB/s",
+            "frac": gbs / PCIE_GEN5_X16_GBS,
+            "traffic": per_launch * ratio if ratio else None,
+            "traffic_pcie_read": per_launch * pcie if pcie else None,
+            "peak_source": "PCIe Gen5 x16, 32 GT/s x 16 x 128/130 / 8 (host link; "
+                           "MEASURED_PEAKS.json has no host-link figure)",
+            "copy_engine_ceiling_gbs": h2d, "frac_of_copy_engine_ceiling": gbs / h2d,
+            "launches": int(st_n), "bytes_per_launch": per_launch,
+            "avg_launch_ms": st_ms / st_n,
+            "timing": "CUDA events recorded on the streamer's side stream around every "
+                      "launch inside the captured step graph; the timed window's K steps "
+                      "replayed on the same inputs from the same restored cache state"
+                      + (", summed over ranks" if world > 1 else "")}
+
+    roof_fused = None
+    sprobe = None
+    if world == 1:
+        # fused_experts: each layer's call replayed as its own CUDA graph
+        route_ms, fused_ms, fbytes = profile_layers(stack, stream.next().cuda())
+        t_fused = statistics.mean(fused_ms)
+        fused_gbs = statistics.mean(fbytes) / (t_fused * 1e-3) / 1e9
+        roof_fused = {"bound": "hbm", "kernel": "fused_experts (align+gate/up+down+combine)",
+                      "achieved": fused_gbs, "peak": hbm_peak, "unit": "GB/s",
+                      "frac": fused_gbs / hbm_peak,
+                      "traffic": _traffic_per_launch(fbytes, cfg),
+                      "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)",
+                      "per_launch_ms": {"route": statistics.mean(route_ms), "fused": t_fused},
+                      "fused_bytes_per_launch": statistics.mean(fbytes),
+                      "timing": "each layer's fused_experts replayed as its own CUDA graph, "
+                                "CUDA events, mean over layers"}
+        if offloaded:
+            sprobe = stream_probe(stack)
+    else:
+        roof_fused = {"bound": "hbm", "kernel": "expert-parallel decode step (per rank)",
+                      "achieved": hbm_step / (ms / K * 1e-3) / 1e9, "peak": hbm_peak,
+                      "unit": "GB/s", "frac": hbm_step / (ms / K * 1e-3) / 1e9 / hbm_peak,
+                      "traffic": None,
+                      "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)",
+                      "timing": "timed region, max over ranks"}
+    roof = roof_stream if roof_stream is not None else roof_fused
 
     c1 = None
     if world == 1 and T != 1:
         c1 = _timed_c1(stack, cfg, K, W, a.seed)
-
-    # gap misses plus the misses of steps planned in expert waves
-    misses = sum(stats_t.get(k, 0) - stats_w.get(k, 0) for k in ("misses", "scan_misses"))
-    fills = stats_t.get("fills", 0) - stats_w.get("fills", 0)
-    bpe = cfg.bytes_per_expert
-    peaks = {}
-    try:
-        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-            peaks = json.load(f)
-    except Exception:
-        pass
-    hbm_peak = peaks.get("hbm_gbs", 6650.0)
-    h2d = h2d_ceiling_gbs()
-    host_step = fills / K * bpe
-    t_roof = max(hbm_step / (hbm_peak * 1e9), host_step / 63.0e9) * 1e3
-    step_roof = {"t_roof_ms": t_roof, "t_ms": ms / K, "frac": t_roof / (ms / K),
-                 "hbm_bytes_per_step": hbm_step, "host_bytes_per_step": host_step,
-                 "host_peak_gbs": 63.0, "hbm_peak_gbs": hbm_peak}
-
-    roof = None
-    sprobe = None
-    if world == 1:
-        # kernel roofline: each layer's fused_experts / route replayed as a graph
-        route_ms, fused_ms, fbytes = profile_layers(stack, stream.next().cuda())
-        t_fused = statistics.mean(fused_ms)
-        fused_gbs = statistics.mean(fbytes) / (t_fused * 1e-3) / 1e9
-        roof = {"bound": "hbm", "kernel": "fused_experts (align+gate/up+down+combine)",
-                "achieved": fused_gbs, "peak": hbm_peak, "unit": "GB/s",
-                "frac": fused_gbs / hbm_peak,
-                "traffic": _traffic_per_launch(fbytes, cfg),
-                "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)",
-                "per_launch_ms": {"route": statistics.mean(route_ms), "fused": t_fused},
-                "fused_bytes_per_launch": statistics.mean(fbytes),
-                "timing": "each layer's fused_experts replayed as its own CUDA graph, "
-                          "CUDA events, mean over layers"}
-        sprobe = stream_probe(stack)
-    else:
-        roof = {"bound": "hbm", "kernel": "expert-parallel decode step (per rank)",
-                "achieved": hbm_step / (ms / K * 1e-3) / 1e9, "peak": hbm_peak,
-                "unit": "GB/s", "frac": hbm_step / (ms / K * 1e-3) / 1e9 / hbm_peak,
-                "traffic": None, "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)",
-                "timing": "timed region, max over ranks"}
-
-    # resident comparison: same kernels, every expert in HBM (slots = E)
-    resident = None
-    resident_bytes = layers * (cfg.num_experts + cfg.n_shared) * cfg.bytes_per_expert
-    fits = resident_bytes < 0.8 * torch.cuda.mem_get_info()[1]
-    if not a.no_resident and world == 1 and not fits:
-        resident = {"skipped": f"{resident_bytes / 1e9:.0f} GB of experts do not fit one GPU"}
-    if not a.no_resident and world == 1 and fits:
-        del stack
-        torch.cuda.empty_cache()
-        rs = MoEDecodeStack(cfg, slots=cfg.num_experts, seed=a.seed, num_layers=layers)
-        rs.capture(tokens=T)
-        for i in range(W):
-            rs.replay(xs[i])
-        torch.cuda.synchronize()
-        r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        r0.record()
-        for i in range(K):
-            rs.replay(xs[W + i])
-        r1.record()
-        torch.cuda.synchronize()
-        resident = {"value": T * K / (r0.elapsed_time(r1) * 1e-3), "unit": UNIT,
-                    "slots": cfg.num_experts, "c1": _timed_c1(rs, cfg, K, W, a.seed)}
-        del rs
-    elif hasattr(stack, "release"):
+    if hasattr(stack, "release"):
         stack.release()
+    del stack, xs
+    _free()
+
+    # decode tok/s against the slot count (one GPU): the metric's second axis
+    sweep = None
+    if world == 1 and offloaded and not a.no_sweep:
+        sweep = []
+        for sv in [int(v) for v in a.sweep.split(",") if v]:
+            if sv == slots or sv >= local_n:
+                continue
+            sweep.append(_sweep_point(a, cfg, sv, layers, K, W, hbm_peak))
+
+    # resident comparison: same kernels, every local expert in HBM
+    resident = None
+    resident_bytes = layers * (local_n + cfg.n_shared) * bpe
+    fits = resident_bytes < 0.8 * torch.cuda.mem_get_info()[1]
+    if not a.no_resident and offloaded and not fits:
+        resident = {"skipped": f"{resident_bytes / 1e9:.0f} GB of experts do not fit one GPU"}
+    elif not a.no_resident and offloaded:
+        rs, _ = _build_stack(cfg, local_n, layers, T, a, world)
+        rstream = synth.TokenStream(cfg.hidden, T, seed=a.seed + 100 + rank)
+        rx = torch.stack([rstream.next() for _ in range(W + K)]).cuda()
+        for i in range(W):
+            rs.replay(rx[i])
+        torch.cuda.synchronize()
+        rms, _, _, rclk = _timed_replays(rs, rx, W, K, dist, clocks=False)
+        resident = {"value": world * T * K / (rms * 1e-3), "unit": UNIT,
+                    "slots": local_n, "ms_per_step": rms / K}
+        if world == 1:
+            resident["c1"] = _timed_c1(rs, cfg, K, W, a.seed)
+        if hasattr(rs, "release"):
+            rs.release()
+        del rs, rx
+        _free()
 
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        t_cpu, n = cpu_step_time(cfg, a.slots, T, layers, a.seed, steps=3, warmup=1,
-                                 budget_s=25.0)
+        torch.set_num_threads(os.cpu_count() or 1)
+        t_cpu, n = cpu_step_time(cfg, slots, T, layers, a.seed, steps=K,
+                                 warmup=max(1, min(W, 2)), budget_s=150.0)
         cpu = {"value": T / t_cpu, "unit": UNIT, "cores": torch.get_num_threads(),
                "kind": "port",
-               "sample": f"{n} full decode steps ({layers} layers, c={T}) of the torch-native "
-                         f"CPU path (oracle routing + slot policy + MoE), median"}
+               "sample": f"{n} full decode steps ({layers} layers, c={T}, each layer its own "
+                         f"weights) of the torch-native CPU path (oracle routing + slot policy "
+                         f"+ MoE), median; the same sampling as the reference arm"}
 
-    local_n = cfg.num_experts // world
-    offloaded = a.slots < local_n
-    launches = K * layers * layer_launches(cfg, T, world, a.slots, a.exchange, a.no_overlap)
+    launches = K * layers * layer_launches(cfg, T, world, slots, a.exchange, a.no_overlap)
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None,
         "dtype": "bf16" if cfg.weight_dtype == "bf16" else "fp8e4m3 weights, bf16 activations",
         "data": "synthetic",
-        "config": {"workload": _workload(cfg, min(a.slots, local_n), T, layers, world),
-                   "model": cfg.name, "tokens_per_step": T, "slots": min(a.slots, local_n),
-                   "layers": layers, "global_batch": T * world, "seq_len": 1,
-                   "parallelism": f"ep{world}" if world > 1 else "single",
-                   "slot_policy": "slru+lfu" if a.lfu else "slru",
-                   "ep_exchange": a.exchange if world > 1 else None,
-                   "local_experts": local_n, "offloaded": offloaded, "cuda_graph": graphed,
-                   "stream_overlap": offloaded and not a.no_overlap,
-                   "cache_prefill_steps": a.prefill_steps,
-                   "l2": "per-step expert weights >> 126 MB L2 (no flush needed)",
-                   "build_s": round(build_s, 1)},
+        "config": _config(a, cfg, slots, T, layers, world),
+        "run": {"cuda_graph": graphed, "stream_overlap": offloaded and not a.no_overlap,
+                "ep_exchange": a.exchange if world > 1 else None,
+                "build_s": round(build_s, 1)},
         "e2e": {"value": world * T * K / (e2e_ms * 1e-3), "unit": UNIT,
                 "h2d_bytes_per_step": world * T * cfg.hidden * 2,
-                "d2h_bytes_per_step": world * T * cfg.hidden * 2},
+                "d2h_bytes_per_step": world * T * cfg.hidden * 2,
+                "misses_per_step": e2e_misses / K,
+                "window": "the timed window's inputs"
+                          + (" from its restored cache state (planner state, expert maps "
+                             "and slot contents)" if restored else
+                             ", continuing from the cache state the timed window left")},
         "roofline": roof,
+        "roofline_fused_experts": roof_fused,
         "step_roofline": step_roof,
         "stream": {"misses_per_step": misses / K, "fills_per_step": fills / K,
-                   "bytes_per_step": host_step, "probe": sprobe,
-                   "h2d_ceiling_gbs": h2d, "pcie_gen5_x16_gbs": 63.0},
+                   "bytes_per_step": fills / K * bpe, "probe": sprobe,
+                   "h2d_ceiling_gbs": h2d, "pcie_gen5_x16_gbs": PCIE_GEN5_X16_GBS},
         "c1": c1,
+        "slots_sweep": sweep,
         "resident": resident,
         "cpu_baseline": cpu,
         "gpu_launches": launches,
-        "clocks": clk.summary(),
+        "clocks": clocks,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
     if dist:
         dist.barrier()
-        del stack
         dist.destroy_process_group()
 
 # ------------------------------------------------- grouped-GEMM microbench
@@ -824,6 +1019,7 @@ def run_prefill(a):
 
     cfg = configs.CONFIGS[a.config]
     layers = a.layers or 4
+    slots = _slots_for(a, cfg)
     T, K, W = a.prefill_tokens, a.steps, a.warmup
     with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
         peaks = json.load(f)
@@ -833,7 +1029,7 @@ def run_prefill(a):
     if not a.no_cpu_baseline:
         # the CPU port (oracle routing, the classic hook's wave plan, MoE in
         # torch) on one layer of the same step size, scaled to the stack
-        t_layer, n = cpu_step_time(cfg, a.slots, T, 1, a.seed, steps=1, warmup=1,
+        t_layer, n = cpu_step_time(cfg, slots, T, 1, a.seed, steps=1, warmup=1,
                                    decode=False)
         cpu = {"value": T / (t_layer * layers), "unit": "tok/s",
                "cores": torch.get_num_threads(), "kind": "port",
@@ -842,7 +1038,7 @@ def run_prefill(a):
     for mode in a.prefill_modes.split(","):
         if mode not in ("waves", "chunks"):
             raise ValueError(f"unknown prefill mode {mode!r}")
-        stack = MoEDecodeStack(cfg, slots=a.slots, seed=a.seed, num_layers=layers)
+        stack = MoEDecodeStack(cfg, slots=slots, seed=a.seed, num_layers=layers)
         for layer in stack.layers:
             layer.beyond_envelope = mode
         g = torch.Generator().manual_seed(a.seed + 11)
@@ -887,9 +1083,9 @@ def run_prefill(a):
             "metric": "prefill MoE tok/s", "value": T / (ms * 1e-3), "unit": "tok/s",
             "mode": mode, "n_gpus": 1, "steps": K, "warmup": W, "ms_per_step": ms,
             "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": f"{cfg.name} MoE stack, {layers} layers, {a.slots} slots "
+            "config": {"workload": f"{cfg.name} MoE stack, {layers} layers, {slots} slots "
                        f"of {cfg.num_experts} experts, {T}-token steps beyond the envelope "
-                       f"({a.slots // k} tokens), fresh random tokens per step"},
+                       f"({slots // k} tokens), fresh random tokens per step"},
             "experts_streamed_per_step": fills,
             "waves_per_step": (s1["waves"] - s0["waves"]) / K,
             "host_gbs": host / (ms * 1e-3) / 1e9,
@@ -900,7 +1096,7 @@ def run_prefill(a):
             "e2e": {"value": T / (e2e_ms * 1e-3), "unit": "tok/s",
                     "h2d_bytes_per_step": T * cfg.hidden * 2,
                     "d2h_bytes_per_step": T * cfg.hidden * 2},
-            "gpu_launches": K * layers * layer_launches(cfg, T, 1, a.slots, decode=False)
+            "gpu_launches": K * layers * layer_launches(cfg, T, 1, slots, decode=False)
             if mode == "waves" else None,
             "clocks": clk.summary(),
         }
@@ -922,10 +1118,12 @@ def run_reference(a):
         return
     cfg = configs.CONFIGS[a.config]
     layers = a.layers or cfg.num_moe_layers
-    # the same global batch as the GPU arm: c tokens per GPU on N GPUs
+    slots = _slots_for(a, cfg)
+    # the same global batch as the GPU arm: c tokens per GPU on N GPUs; the
+    # port runs every expert of the model with --slots-frac of them in slots
     T = a.tokens * world
     torch.set_num_threads(os.cpu_count() or 1)
-    t_step, n = cpu_step_time(cfg, a.slots, T, layers, a.seed, steps=a.steps,
+    t_step, n = cpu_step_time(cfg, slots, T, layers, a.seed, steps=a.steps,
                               warmup=max(1, min(a.warmup, 2)), budget_s=150.0)
     v = T / t_step
     line = {
@@ -933,12 +1131,12 @@ def run_reference(a):
         "warmup": a.warmup, "ms_per_step": t_step * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "impl": "reference",
-        "config": {"workload": _workload(cfg, a.slots, T, layers), "model": cfg.name,
-                   "tokens_per_step": T, "slots": a.slots, "layers": layers},
+        "config": _config(a, cfg, _slots_for(a, cfg, world), a.tokens, layers, world),
         "cpu_baseline": {"value": v, "unit": UNIT, "cores": torch.get_num_threads(),
                          "kind": "port",
-                         "sample": f"{n} full decode steps ({layers} layers, c={T}), median; "
-                                   "2 distinct weight sets cycled over the layers"},
+                         "sample": f"{n} full decode steps ({layers} layers, each its own "
+                                   f"weights, c={T}, {slots} of {cfg.num_experts} experts in "
+                                   "slots), median"},
         "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

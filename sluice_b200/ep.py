@@ -27,7 +27,7 @@ import torch
 import torch.distributed as dist
 
 from . import ops
-from .layer import expert_waves
+from .layer import StreamTimer, _timed, expert_waves
 from .configs import MoEConfig
 
 
@@ -191,6 +191,8 @@ class EPMoELayer:
         self.stream_ctas = stream_ctas
         self._side = torch.cuda.Stream(device=cache.device) \
             if not cache.static_full else None
+        # set to a StreamTimer to time every expert-stream launch
+        self.stream_timer: StreamTimer | None = None
 
     @property
     def envelope(self) -> int:
@@ -214,6 +216,8 @@ class EPMoELayer:
         exchange's capacity. With ``beyond_envelope="chunks"`` such steps run
         as envelope-sized chunks through the gap instead."""
         thr = self.envelope
+        if self.stream_timer is not None:
+            self.stream_timer.reset()
         if self.beyond_envelope == "chunks" or self.cache.static_full:
             if x.shape[0] > thr:
                 return torch.cat([self._forward_step(c, add_residual, decode)
@@ -245,14 +249,14 @@ class EPMoELayer:
             part = expert_waves(c, self._side, xg, twg, tig, tig.shape[0] if decode else -1,
                                 self.shared_w13, self.shared_w2, self.rank * T, T,
                                 self.cfg.routed_scaling_factor, self.shared_w13_scale,
-                                self.shared_w2_scale, self.stream_ctas)
+                                self.shared_w2_scale, self.stream_ctas, self.stream_timer)
         elif self.overlap:
             # plan -> [stream on a side stream || resident experts] -> streamed experts
             main = torch.cuda.current_stream()
             c.plan(tig)
             self._side.wait_stream(main)
             with torch.cuda.stream(self._side):
-                c.stream(self.stream_ctas)
+                _timed(self.stream_timer, self._side, lambda: c.stream(self.stream_ctas))
             n_sh = 0 if self.shared_w13 is None else self.shared_w13.shape[0]
             ws = ops.fused_experts_workspace(xg.shape[0], tig.shape[1], xg.shape[1],
                                              c.w13.shape[1] // 2, c.num_slots, n_sh, xg.device)

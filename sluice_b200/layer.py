@@ -51,10 +51,44 @@ def decode_rows_from_query_start_loc(query_start_loc, num_tokens: int, max_query
     return starts[(qsl[1:] - starts) == 1].long()
 
 
+class StreamTimer:
+    """Optional CUDA-event timing of a layer's expert-stream launches.
+
+    Each launch is bracketed by two timing events recorded on the stream the
+    streamer runs on; the events are external, so inside a CUDA-graph capture
+    they become event-record nodes that every replay rewrites. ``launches()``
+    (after the step has completed) gives each launch's device time with its
+    wave (-1 for a gap's single stream)."""
+
+    def __init__(self):
+        self.pairs: list = []
+
+    def reset(self) -> None:
+        self.pairs = []
+
+    def around(self, stream: torch.cuda.Stream, fn, wave: int = -1) -> None:
+        a = torch.cuda.Event(enable_timing=True, external=True)
+        b = torch.cuda.Event(enable_timing=True, external=True)
+        a.record(stream)
+        fn()
+        b.record(stream)
+        self.pairs.append((a, b, wave))
+
+    def launches(self) -> list[tuple[float, int]]:
+        return [(a.elapsed_time(b), w) for a, b, w in self.pairs]
+
+
+def _timed(timer: "StreamTimer | None", stream: torch.cuda.Stream, fn, wave: int = -1) -> None:
+    if timer is None:
+        fn()
+    else:
+        timer.around(stream, fn, wave)
+
+
 def expert_waves(c: SlotCache, side: torch.cuda.Stream, hs: torch.Tensor, tw: torch.Tensor,
                  ti: torch.Tensor, decode_rows, shared_w13, shared_w2, shared_t0: int,
                  shared_nt: int, scale: float, shared_w13_scale=None, shared_w2_scale=None,
-                 stream_ctas: int = 16) -> torch.Tensor:
+                 stream_ctas: int = 16, timer: StreamTimer | None = None) -> torch.Tensor:
     """One step of ``hs`` [T, H] (routed as ``tw`` / ``ti``) in expert waves
     over the cache ``c``; returns the fp32 output [T, H]: the routed experts
     scaled by ``scale`` plus the shared experts on rows [shared_t0, shared_t0
@@ -82,7 +116,7 @@ def expert_waves(c: SlotCache, side: torch.cuda.Stream, hs: torch.Tensor, tw: to
 
     def stream(k: int) -> None:
         with torch.cuda.stream(side):
-            c.stream_wave(k, stream_ctas)
+            _timed(timer, side, lambda: c.stream_wave(k, stream_ctas), k)
             filled[k].record(side)
 
     side.wait_stream(main)
@@ -142,6 +176,8 @@ class SluiceMoELayer:
         self.layer_idx = layer_idx
         self.last_ids = None
         self.last_logits = None
+        # set to a StreamTimer to time every expert-stream launch
+        self.stream_timer: StreamTimer | None = None
 
     @property
     def envelope(self) -> int:
@@ -160,6 +196,8 @@ class SluiceMoELayer:
         the indices of the decode rows wherever they sit (the opt-in non-MLA
         classifier's signal, ``decode_rows_from_query_start_loc``)."""
         thr = self.envelope
+        if self.stream_timer is not None:
+            self.stream_timer.reset()
         if hs.shape[0] > thr:
             if self.beyond_envelope == "waves":
                 return self._forward_waves(hs, decode_rows)
@@ -182,7 +220,7 @@ class SluiceMoELayer:
         acc = expert_waves(self.cache, self._side, hs, tw, ti, decode_rows,
                            self.shared_w13, self.shared_w2, 0, hs.shape[0],
                            self.cfg.routed_scaling_factor, self.shared_w13_scale,
-                           self.shared_w2_scale, self.stream_ctas)
+                           self.shared_w2_scale, self.stream_ctas, self.stream_timer)
         return acc.to(torch.bfloat16)
 
     def _forward_step(self, hs: torch.Tensor) -> torch.Tensor:
@@ -209,7 +247,7 @@ class SluiceMoELayer:
         c.plan(ti)
         self._side.wait_stream(main)
         with torch.cuda.stream(self._side):
-            c.stream(self.stream_ctas)
+            _timed(self.stream_timer, self._side, lambda: c.stream(self.stream_ctas))
         hs = hs.contiguous()
         T, H = hs.shape
         ws = ops.fused_experts_workspace(T, ti.shape[1], H, c.w13.shape[1] // 2,

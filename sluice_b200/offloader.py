@@ -329,6 +329,37 @@ class SlotCache:
         h = self.waves[:64].view(torch.int32).cpu().tolist()
         return {k: int(h[v]) for k, v in _lib.WAVE_HDR.items()}
 
+    # -- saving and restoring the cache (benchmarks, tests) -------------------
+    def save(self) -> dict:
+        """A device copy of everything a gap reads or writes: the planner
+        state, the expert map and the slot buffers (allocates their size)."""
+        return {"state": None if self.state is None else self.state.clone(),
+                "expert_map": self.expert_map.clone(),
+                "slots": {k: t.clone() for k, t in self.gpu_cache.items()}}
+
+    def restore(self, saved: dict) -> None:
+        """Put back a ``save()``: the next gap plans exactly as it would have
+        then (copies on the current stream; buffers keep their addresses)."""
+        if self.state is not None:
+            self.state.copy_(saved["state"])
+        self.expert_map.copy_(saved["expert_map"])
+        for k, t in self.gpu_cache.items():
+            t.copy_(saved["slots"][k])
+
+    def last_fill_counts(self, wave_steps: bool = False) -> list[int]:
+        """Experts streamed by the last gap (one entry) or, with
+        ``wave_steps``, by each wave of the last wave plan (synchronises)."""
+        if self.state is None:
+            return []
+        if not wave_steps:
+            return [self.header()["fill_count"]]
+        words = self.waves.view(torch.int32)
+        o = self.wave_offsets[1] // 4
+        nw = int(words[_lib.WAVE_HDR["num_waves"]].item())
+        counts = words[o: o + self.max_waves].cpu().tolist()
+        # waves past the plan's count stream nothing (their entries are stale)
+        return [c if k < nw else 0 for k, c in enumerate(counts)]
+
     # -- host-side views (synchronise) ----------------------------------------
     def _field(self, i: int, dtype, count: int) -> np.ndarray:
         b = self.state[self.offsets[i]: self.offsets[i] + count * np.dtype(dtype).itemsize]

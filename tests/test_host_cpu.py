@@ -166,10 +166,19 @@ def test_reference_arm_runs_the_global_batch(monkeypatch, capsys):
 
     monkeypatch.setenv("RANK", "0")
     monkeypatch.setenv("WORLD_SIZE", "2")
-    bench.main(["--impl", "reference", "--steps", "1", "--warmup", "1", "--layers", "2"])
+    argv = ["--impl", "reference", "--steps", "1", "--warmup", "1", "--layers", "2"]
+    bench.main(argv)
     line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     assert line["impl"] == "reference" and line["n_gpus"] == 2
-    assert line["config"]["tokens_per_step"] == 16 and line["value"] > 0
+    assert line["config"]["global_batch"] == 16 and line["value"] > 0
+    assert "c=16" in line["cpu_baseline"]["sample"]
+    # the same config dict the GPU arm prints for these arguments at N=2
+    # (24 of 32 local experts in slots per rank)
+    from sluice_b200 import configs
+    a = bench._args(argv[2:])
+    cfg = configs.CONFIGS[a.config]
+    assert line["config"] == bench._config(a, cfg, bench._slots_for(a, cfg, 2), 8, 2, 2)
+    assert line["config"]["slots"] == 24 and line["config"]["slots_frac"] == 0.75
 
 
 def test_cpu_port_plans_steps_beyond_the_envelope_in_waves():
