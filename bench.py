@@ -534,6 +534,7 @@ def _timed_replays(stack, xs, W, K, dist, clocks=True):
     clk = ClockSampler(torch.cuda.current_device()) if clocks else None
     if clk:
         clk.__enter__()
+        time.sleep(0.05)  # the sampling thread reaches its steady state first
     ev0.record()
     for i in range(K):
         stack.replay(xs[W + i])
