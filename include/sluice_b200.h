@@ -340,31 +340,42 @@ int sl_fused_experts_partial(const void* hidden, int T, int H, int I,
 
 /* ------------------------------------------------ expert-parallel exchange
  * Replaces vLLM's EP dispatch / combine around the reference's per-rank
- * experts (naive all-gather of tokens + routing and reduction of outputs,
- * offloader.py:690-699, 1192-1201) with one kernel each over NVLink peer
- * memory. peer_recv[q] / peer_signal[q] are rank q's receive buffer and
- * signal words (16 x u32, zeroed before first use), mapped into every rank
- * (symmetric memory); book is 16 bytes of this rank's device memory, zeroed
- * once; status a device int32. T <= the T the buffers were sized for.
- * Receive buffers hold two halves used alternately (sized by the _bytes
- * queries). All ranks must make the same sequence of calls; every wait on a
- * peer is bounded (SL_ERR_TIMEOUT in *status).
+ * experts (offloader.py:690-699, 1192-1201: every rank plans the ids it owns
+ * after the dispatch) with one routed kernel each over NVLink peer memory:
+ * a token travels only to the ranks that own one of its top-k experts, and
+ * only those ranks' partial outputs come back. Experts are sharded in
+ * contiguous ranges (rank q owns global ids [q*G/world, (q+1)*G/world),
+ * global_n % world == 0). peer_recv[q] / peer_signal[q] are rank q's receive
+ * buffer (16-byte aligned) and signal words (16 x u32, zeroed before first
+ * use), mapped into every rank (symmetric memory); book is 16 bytes of this
+ * rank's device memory, zeroed once; status a device int32. T <= the T the
+ * buffers were sized for, T <= 1024. Receive buffers hold two halves used
+ * alternately (sized by the _bytes queries). All ranks must make the same
+ * sequence of calls; every wait on a peer is bounded (SL_ERR_TIMEOUT in
+ * *status).
  * dispatch: this rank's hidden bf16 [T, H] (16-byte aligned), top-k weights
- *   f32 [T, topk] and ids i32 [T, topk] (topk even) travel packed as rows of
- *   2H + 8*topk bytes; outputs every rank's rows, unpacked: x_out bf16
- *   [world*T, H], w_out [world*T, topk], id_out [world*T, topk].
- * combine: partial fp32 [world*T, H] (this rank's experts over every rank's
- *   tokens); out = bf16(sum over ranks, rank order) for this rank's T tokens,
- *   or bf16(residual + that) when residual (bf16 [T, H]) is not NULL: the
+ *   f32 [T, topk] and ids i32 [T, topk]. Outputs world*T rows: rows [0, T)
+ *   are this rank's tokens, then the rows each peer sent (peers in rank
+ *   order, each peer's tokens in token order); the remaining rows carry id
+ *   -1 and weight 0 (no expert) and an unwritten hidden row. x_out bf16
+ *   [world*T, H], w_out [world*T, topk], id_out [world*T, topk], src_out
+ *   i32 [world*T]: (home rank << 16) | token index of each row, -1 for an
+ *   empty row.
+ * combine: partial fp32 [world*T, H] (this rank's experts over the rows the
+ *   dispatch produced, in its order), the dispatch's src_out, and this rank's
+ *   own topk_ids [T, topk]; out = bf16(sum over the ranks each token was
+ *   sent to, and this rank, in rank order) for this rank's T tokens, or
+ *   bf16(residual + that) when residual (bf16 [T, H]) is not NULL: the
  *   decoder's residual add folded in. */
 size_t sl_ep_dispatch_recv_bytes(int world, int T, int H, int topk);
 size_t sl_ep_combine_recv_bytes(int world, int T, int H);
 int sl_ep_dispatch(const void* hidden, const float* topk_weights, const int32_t* topk_ids,
-                   int T, int H, int topk, int rank, int world,
+                   int T, int H, int topk, int global_n, int rank, int world,
                    void* const* peer_recv, void* const* peer_signal, void* book,
-                   void* x_out, float* w_out, int32_t* id_out, int32_t* status,
-                   sl_stream_t stream);
-int sl_ep_combine(const float* partial, int T, int H, int rank, int world,
+                   void* x_out, float* w_out, int32_t* id_out, int32_t* src_out,
+                   int32_t* status, sl_stream_t stream);
+int sl_ep_combine(const float* partial, const int32_t* src, const int32_t* topk_ids,
+                  int T, int H, int topk, int global_n, int rank, int world,
                   void* const* peer_recv, void* const* peer_signal, void* book,
                   const void* residual, void* out, int32_t* status, sl_stream_t stream);
 

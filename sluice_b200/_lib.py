@@ -92,9 +92,10 @@ _SIGNATURES = {
                                  _vp, _i, _f, _i, _i, _vp, _i, _i, _vp, _vp, _sz, _vp]),
     "sl_ep_dispatch_recv_bytes": (_sz, [_i, _i, _i, _i]),
     "sl_ep_combine_recv_bytes": (_sz, [_i, _i, _i]),
-    "sl_ep_dispatch": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp,
-                            _vp, _vp]),
-    "sl_ep_combine": (_i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "sl_ep_dispatch": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp,
+                            _vp, _vp, _vp, _vp]),
+    "sl_ep_combine": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp,
+                           _vp, _vp]),
     "sl_fused_experts_noalloc": (_i, [_vp, _i, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _i,
                                       _vp, _i, _vp, _vp, _i, _f, _vp, _vp, _vp]),
 }

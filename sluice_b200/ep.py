@@ -7,18 +7,21 @@ it at ``offloader.py:974-986`` and skips non-owned ids in the gap,
 planner. One decode step of a layer:
 
 1. route the rank's own tokens (gate + select_experts, replicated gate);
-2. dispatch: all-gather of every rank's (token rows, top-k weights, top-k
-   ids) — one packed NCCL all-gather; fixed size, no host sync;
+2. dispatch: each token travels only to the ranks owning one of its top-k
+   experts (``NvlinkExchange``: one routed push kernel over NVLink peer
+   memory); every rank ends up with its own tokens first, then the tokens its
+   peers sent it;
 3. gap on the **post-dispatch** ids (the lesson of ``offloader.py:1192-1201``):
-   the planner sees every gathered id and plans only the ones this rank owns;
-4. ``fused_experts_partial`` over all gathered tokens: this rank's experts
+   the planner sees every received id and plans only the ones this rank owns;
+4. ``fused_experts_partial`` over the received rows: this rank's experts
    (fp32, scaled), plus the shared experts on this rank's own token rows;
-5. combine: reduce-scatter (sum) of the fp32 partials back to each token's
-   home rank, then one bf16 rounding.
+5. combine: each received row's fp32 partial goes back to its home rank,
+   which sums its own and its peers' partials per token and rounds once to
+   bf16.
 
-This is the all-gather / reduce-scatter dispatch that vLLM uses for expert
-parallelism without an all-to-all backend, at decode token counts where
-every rank needs most tokens anyway.
+``exchange="nccl"`` keeps the collective form for comparison: an NCCL
+all-gather of every rank's rows (every rank receives every token) and a
+reduce-scatter of the partials.
 """
 
 from __future__ import annotations
@@ -115,7 +118,11 @@ class NvlinkExchange:
         torch.cuda.synchronize(device)
         dist.barrier(group)  # every rank's signal words are zero before any peer signals
 
-    def dispatch(self, x, tw, ti):
+    def dispatch(self, x, tw, ti, global_n: int):
+        """Routed dispatch of this rank's tokens: returns ``(xg, twg, tig,
+        src)`` over ``world * T`` rows — this rank's tokens first, then the
+        rows peers sent (rank order), then empty rows (id -1, weight 0);
+        ``src`` [world * T] int32 is ``(home rank << 16) | token`` (-1 empty)."""
         from ._lib import check, lib, ptr
 
         T, H = x.shape
@@ -129,16 +136,20 @@ class NvlinkExchange:
         xg = torch.empty(n, H, dtype=torch.bfloat16, device=x.device)
         twg = torch.empty(n, k, dtype=torch.float32, device=x.device)
         tig = torch.empty(n, k, dtype=torch.int32, device=x.device)
-        # the kernel packs (hidden | weights | ids) rows itself while pushing
-        check(lib().sl_ep_dispatch(ptr(x), ptr(tw), ptr(ti), T, H, k, self.rank, self.world,
-                                   self._recv_d, self._sig, ptr(self.book), ptr(xg), ptr(twg),
-                                   ptr(tig), ptr(self.status),
+        src = torch.empty(n, dtype=torch.int32, device=x.device)
+        # the kernel packs (hidden | weights | ids | token) rows while pushing
+        check(lib().sl_ep_dispatch(ptr(x), ptr(tw), ptr(ti), T, H, k, int(global_n), self.rank,
+                                   self.world, self._recv_d, self._sig, ptr(self.book),
+                                   ptr(xg), ptr(twg), ptr(tig), ptr(src), ptr(self.status),
                                    torch.cuda.current_stream().cuda_stream), "sl_ep_dispatch")
-        return xg, twg, tig
+        return xg, twg, tig, src
 
-    def combine(self, partial: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
-        """This rank's rows of the summed partials in bf16; with ``residual``
-        (bf16 [T, H]) the result is ``residual + that``, as a bf16 add."""
+    def combine(self, partial: torch.Tensor, src: torch.Tensor, ti: torch.Tensor,
+                global_n: int, residual: torch.Tensor | None = None) -> torch.Tensor:
+        """This rank's tokens' summed partials in bf16 (``partial`` and
+        ``src`` as the dispatch produced them, ``ti`` this rank's own top-k
+        ids); with ``residual`` (bf16 [T, H]) the result is ``residual +
+        that``, as a bf16 add."""
         from ._lib import check, lib, ptr
 
         n, H = partial.shape
@@ -148,10 +159,11 @@ class NvlinkExchange:
         out = torch.empty(T, H, dtype=torch.bfloat16, device=partial.device)
         if residual is not None:
             residual = residual.contiguous()
-        check(lib().sl_ep_combine(ptr(partial), T, H, self.rank, self.world, self._recv_c,
-                                  self._sig, ptr(self.book), ptr(residual), ptr(out),
-                                  ptr(self.status), torch.cuda.current_stream().cuda_stream),
-              "sl_ep_combine")
+        ti = ti.contiguous().to(torch.int32)
+        check(lib().sl_ep_combine(ptr(partial), ptr(src), ptr(ti), T, H, ti.shape[1],
+                                  int(global_n), self.rank, self.world, self._recv_c, self._sig,
+                                  ptr(self.book), ptr(residual), ptr(out), ptr(self.status),
+                                  torch.cuda.current_stream().cuda_stream), "sl_ep_combine")
         return out
 
     def check(self) -> None:
@@ -232,14 +244,19 @@ class EPMoELayer:
     def _forward_step(self, x: torch.Tensor, add_residual: bool,
                       decode: bool = True) -> torch.Tensor:
         T = x.shape[0]
+        G = self.cfg.num_experts
         tw, ti, _ = self.router.route(x)
         if self.exchange is not None:
-            xg, twg, tig = self.exchange.dispatch(x, tw, ti)
+            # routed: this rank's own tokens are rows [0, T)
+            xg, twg, tig, src = self.exchange.dispatch(x, tw, ti, G)
+            own0 = 0
         else:
+            # all-gather: rank r's tokens are rows [r*T, (r+1)*T)
             xg, twg, tig = dispatch(x, tw, ti, self.group)
+            own0 = self.rank * T
         self.last_ids = tig
         c = self.cache
-        kw = dict(shared_t0=self.rank * T, shared_nt=T,
+        kw = dict(shared_t0=own0, shared_nt=T,
                   routed_scaling_factor=self.cfg.routed_scaling_factor, w1_scale=c.w13_scale,
                   w2_scale=c.w2_scale, shared_w13_scale=self.shared_w13_scale,
                   shared_w2_scale=self.shared_w2_scale)
@@ -247,7 +264,7 @@ class EPMoELayer:
         if T > self.envelope:
             # the gathered rows' working set can exceed the slots: waves
             part = expert_waves(c, self._side, xg, twg, tig, tig.shape[0] if decode else -1,
-                                self.shared_w13, self.shared_w2, self.rank * T, T,
+                                self.shared_w13, self.shared_w2, own0, T,
                                 self.cfg.routed_scaling_factor, self.shared_w13_scale,
                                 self.shared_w2_scale, self.stream_ctas, self.stream_timer)
         elif self.overlap:
@@ -270,7 +287,7 @@ class EPMoELayer:
             c.gap(tig)
             part = ops.fused_experts_partial(*args, **kw)
         if self.exchange is not None:
-            return self.exchange.combine(part, x if add_residual else None)
+            return self.exchange.combine(part, src, ti, G, x if add_residual else None)
         out = combine(part, self.group).to(torch.bfloat16)
         return x + out if add_residual else out
 
