@@ -66,11 +66,22 @@ def _args(argv=None):
                     help="SLUICE_LFU=1: popularity-ordered protected victims (opt-in policy)")
     ap.add_argument("--exchange", default="nvlink", choices=["nvlink", "nccl"],
                     help="expert-parallel dispatch/combine (N>1): peer-memory kernels or NCCL")
+    ap.add_argument("--prefetch", type=int, default=0,
+                    help="opt-in cross-layer prefetch: experts per layer predicted from the "
+                         "previous layer's input and streamed ahead (one GPU; 0 = off)")
     ap.add_argument("--no-overlap", action="store_true",
                     help="serialise the expert stream and the GEMMs (A/B)")
-    ap.add_argument("--workload", default="decode", choices=["decode", "grouped-gemm", "prefill"],
-                    help="grouped-gemm: the fp8 grouped-GEMM microbench (one JSON line per T); "
-                         "prefill: steps beyond the envelope, expert waves and token chunks")
+    ap.add_argument("--workload", default="decoder",
+                    choices=["decoder", "moe-stack", "grouped-gemm", "prefill"],
+                    help="decoder: the DeepSeek-V2-Lite-shaped decoder (MoE layers on this "
+                         "build's kernels, attention / dense layer / head in PyTorch); "
+                         "moe-stack: the MoE layers alone; grouped-gemm: the fp8 grouped-GEMM "
+                         "microbench (one JSON line per T); prefill: steps beyond the "
+                         "envelope, expert waves and token chunks")
+    ap.add_argument("--prompt-len", type=int, default=128,
+                    help="decoder: prompt tokens per sequence (fed before warm-up)")
+    ap.add_argument("--gen-len", type=int, default=256,
+                    help="decoder: generated tokens per sequence (cache length budget)")
     ap.add_argument("--prefill-tokens", type=int, default=512,
                     help="tokens per step of the prefill workload")
     ap.add_argument("--prefill-modes", default="waves,chunks",
@@ -94,13 +105,34 @@ def _config(a, cfg, slots, T, layers, world):
     """The workload's config, identical in the GPU arm and the reference arm
     for the same arguments (facts about one arm's run go elsewhere)."""
     local_n = cfg.num_experts // world
-    return {"workload": _workload(cfg, slots, T, layers, world), "model": cfg.name,
+    return {"workload": _workload_for(a, cfg, slots, T, layers, world), "model": cfg.name,
             "tokens_per_step": T, "slots": slots, "slots_frac": slots / local_n,
             "layers": layers, "global_batch": T * world, "seq_len": 1,
             "parallelism": f"ep{world}" if world > 1 else "single",
-            "slot_policy": "slru+lfu" if a.lfu else "slru", "local_experts": local_n,
-            "offloaded": slots < local_n, "cache_prefill_steps": a.prefill_steps,
+            "slot_policy": ("slru+lfu" if a.lfu else "slru")
+                           + (f"+prefetch{a.prefetch}" if a.prefetch and world == 1 else ""),
+            "local_experts": local_n,
+            "offloaded": slots < local_n,
+            "decoder": a.workload == "decoder",
+            "cache_prefill": (f"{a.prompt_len}-token prompts" if a.workload == "decoder"
+                              else f"{a.prefill_steps} steps"),
             "l2": "per-step expert weights >> 126 MB L2 (no flush needed)"}
+
+
+def _workload_for(a, cfg, slots, tokens, layers, world=1):
+    if a.workload != "decoder":
+        return _workload(cfg, slots, tokens, layers, world)
+    d = _decoder_cfg(a)
+    local = cfg.num_experts // world
+    where = (f"{slots} GPU slots, {local - slots} per layer in host RAM" if slots < local
+             else "all resident")
+    ep = f", expert-parallel over {world} GPUs ({local} experts per rank)" if world > 1 else ""
+    return (f"{cfg.name} decoder: {d.num_layers} layers (dense FFN I={d.dense_intermediate} in "
+            f"layer 0, {d.num_moe_layers} MoE layers of {cfg.num_experts} experts x "
+            f"I={cfg.moe_intermediate} ({where}), top-{cfg.routing.topk}, {cfg.n_shared} "
+            f"shared), MLA attention {d.num_heads} heads kv_lora {d.kv_lora_rank}, vocab "
+            f"{d.vocab}, H={cfg.hidden}{ep}; {a.prompt_len}-token random prompts, greedy "
+            f"decode, c={tokens} per GPU")
 
 
 def _workload(cfg, slots, tokens, layers, world=1):
@@ -294,6 +326,42 @@ def cpu_step_time(cfg, slots, tokens, layers, seed, steps, warmup, budget_s=None
     return statistics.median(times), len(times)
 
 
+def cpu_decoder_step_time(a, cfg, slots, T, layers, seed, steps, warmup, budget_s=None):
+    """Seconds per decode step of the CPU port of the decoder workload: the
+    same PyTorch decoder harness on the host, its MoE layers through the
+    oracle's routing, slot policy and torch-native MoE (each layer its own
+    weights); the prompts are fed first, untimed."""
+    from sluice_b200.harness import DecoderHarness
+
+    dcfg = _decoder_cfg(a)
+    run = cpu_layer_runner(cfg, seed, n_weight_sets=layers)
+    h = DecoderHarness(dcfg, lambda li, x: run(li, x, slots), T,
+                       a.prompt_len + warmup + steps + 1, seed, device="cpu")
+    g = torch.Generator().manual_seed(seed + 31)
+    prompt = torch.randint(0, dcfg.vocab, (a.prompt_len, T), generator=g)
+    ids = None
+    for p in range(a.prompt_len):
+        ids = h.step(prompt[p])
+    times = []
+    t_start = time.perf_counter()
+    for s_ in range(warmup + steps):
+        t0 = time.perf_counter()
+        ids = h.step(ids)
+        dt = time.perf_counter() - t0
+        if s_ >= warmup:
+            times.append(dt)
+        if budget_s is not None and s_ >= warmup and time.perf_counter() - t_start > budget_s:
+            break
+    return statistics.median(times), len(times)
+
+
+def _cpu_time(a, cfg, slots, T, layers, seed, steps, warmup, budget_s):
+    if a.workload == "decoder":
+        return cpu_decoder_step_time(a, cfg, slots, T, layers, seed, steps, warmup, budget_s)
+    return cpu_step_time(cfg, slots, T, layers, seed, steps=steps, warmup=warmup,
+                         budget_s=budget_s)
+
+
 # ---------------------------------------------------------------- GPU arm
 def h2d_ceiling_gbs(nbytes=1 << 30):
     src = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
@@ -417,24 +485,34 @@ def load_traffic():
         return {}
 
 
-def _timed_c1(stack, cfg, K, W, seed):
-    """Decode at concurrency 1 on the same stack (its own CUDA graph)."""
+def _timed_c1(stack, cfg, K, W, seed, a=None):
+    """Decode at concurrency 1 on the same MoE layers (its own CUDA graph;
+    the decoder workload: a one-sequence decoder around them, after its own
+    prompt)."""
     from sluice_b200 import synth
 
-    stack.capture(tokens=1)
-    st = synth.TokenStream(cfg.hidden, 1, seed=seed + 777)
-    xs = torch.stack([st.next() for _ in range(W + K)]).cuda()
+    if a is not None and a.workload == "decoder":
+        from sluice_b200.harness import OffloadedDecoder
+        eng = OffloadedDecoder(_decoder_cfg(a), stack.stack, 1, a.prompt_len + a.gen_len, seed)
+        eng.capture()
+        _precondition(a, eng, cfg, 1, 0)
+        xs = [None] * (W + K)
+    else:
+        eng = stack
+        eng.capture(tokens=1)
+        st = synth.TokenStream(cfg.hidden, 1, seed=seed + 777)
+        xs = torch.stack([st.next() for _ in range(W + K)]).cuda()
     for i in range(W):
-        stack.replay(xs[i])
+        eng.replay(xs[i])
     torch.cuda.synchronize()
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
     for i in range(K):
-        stack.replay(xs[W + i])
-    b.record()
+        eng.replay(xs[W + i])
+    e1.record()
     torch.cuda.synchronize()
-    stack.check()
-    ms = a.elapsed_time(b) / K
+    eng.check()
+    ms = e0.elapsed_time(e1) / K
     return {"value": 1.0 / (ms * 1e-3), "unit": UNIT, "ms_per_step": ms}
 
 
@@ -490,13 +568,18 @@ def _stack_save(stack):
                for layer in stack.layers if not layer.cache.static_full)
     if need > 0.8 * torch.cuda.mem_get_info()[0]:
         return None
-    return [None if layer.cache.static_full else layer.cache.save() for layer in stack.layers]
+    snap = [None if layer.cache.static_full else layer.cache.save() for layer in stack.layers]
+    own = stack.save() if hasattr(stack, "save") else None   # the decoder's sequences
+    return snap, own
 
 
 def _stack_restore(stack, snap) -> None:
-    for layer, sv in zip(stack.layers, snap):
+    caches, own = snap
+    for layer, sv in zip(stack.layers, caches):
         if sv is not None:
             layer.cache.restore(sv)
+    if own is not None:
+        stack.restore(own)
     torch.cuda.synchronize()
 
 
@@ -580,45 +663,101 @@ def _step_roofline(hbm_step, host_step, t_ms, hbm_peak):
 
 
 def _build_stack(cfg, slots, layers, T, a, world, timers=False):
+    """The measured engine, captured for T tokens per GPU: the MoE decode
+    stack (``--workload moe-stack``) or the V2-Lite-shaped decoder around it
+    (``--workload decoder``: attention, dense layer, head in PyTorch)."""
     from sluice_b200.layer import MoEDecodeStack, StreamTimer
 
+    decoder = a.workload == "decoder"
     if world > 1:
         from sluice_b200.ep import EPDecodeStack
         stack = EPDecodeStack(cfg, slots=slots, seed=a.seed, num_layers=layers,
                               exchange=a.exchange, max_tokens=T, overlap=not a.no_overlap)
     else:
         stack = MoEDecodeStack(cfg, slots=slots, seed=a.seed, num_layers=layers,
-                               overlap=not a.no_overlap)
+                               overlap=not a.no_overlap, prefetch=a.prefetch)
     if timers:
         for layer in stack.layers:
             layer.stream_timer = StreamTimer()
+    if decoder:
+        from sluice_b200.harness import OffloadedDecoder
+        eng = OffloadedDecoder(_decoder_cfg(a), stack, T, a.prompt_len + a.gen_len, a.seed)
+        return eng, eng.capture()
     graphed = stack.capture(tokens=T)
     return stack, (True if graphed is None else bool(graphed))
+
+
+def _decoder_cfg(a):
+    """The V2-Lite-shaped decoder (--layers: its MoE layers, default 26)."""
+    from dataclasses import replace
+
+    from sluice_b200 import harness
+
+    if a.config != "deepseek-v2-lite":
+        raise ValueError("the decoder workload has the DeepSeek-V2-Lite shape")
+    d = harness.V2_LITE_DECODER
+    return replace(d, num_layers=d.first_dense + a.layers) if a.layers else d
+
+
+def _precondition(a, eng, cfg, T, rank):
+    """Fill the slot caches before warm-up: the moe-stack replays
+    --prefill-steps synthetic decode steps; the decoder feeds each sequence's
+    prompt of --prompt-len uniform random token ids, one position per step."""
+    from sluice_b200 import synth
+
+    if a.workload == "decoder":
+        g = torch.Generator().manual_seed(a.seed + 31 + rank)
+        prompt = torch.randint(0, _decoder_cfg(a).vocab, (a.prompt_len, T), generator=g).cuda()
+        for p in range(a.prompt_len):
+            eng.replay(prompt[p])
+    else:
+        stream = synth.TokenStream(cfg.hidden, T, seed=a.seed + 100 + rank)
+        for _ in range(a.prefill_steps):
+            eng.replay(stream.next().cuda())
+    torch.cuda.synchronize()
+
+
+def _step_inputs(a, cfg, T, n, rank, seed_off=0):
+    """Inputs of n steps: synthetic hidden states (moe-stack), or None for
+    the decoder (each step feeds back its own greedy ids)."""
+    from sluice_b200 import synth
+
+    if a.workload == "decoder":
+        return [None] * n
+    stream = synth.TokenStream(cfg.hidden, T, seed=a.seed + 100 + rank + seed_off)
+    # continue the preconditioning stream (same seed) past its steps
+    if seed_off == 0:
+        for _ in range(a.prefill_steps):
+            stream.next()
+    return torch.stack([stream.next() for _ in range(n)]).cuda()
+
+
+def _io_bytes(a, cfg, T):
+    """Host bytes in and out per step and GPU for the e2e window."""
+    return T * 8 if a.workload == "decoder" else T * cfg.hidden * 2
 
 
 def _sweep_point(a, cfg, slots, layers, K, W, hbm_peak):
     """One point of decode tok/s against the slot count (one GPU): c=T and
     c=1 on fresh caches, with misses per step and the step roofline."""
-    from sluice_b200 import synth
-
     out = {"slots": slots, "slots_frac": slots / cfg.num_experts}
     for T in (a.tokens, 1):
-        stack, _ = _build_stack(cfg, slots, layers, T, a, 1)
-        stream = synth.TokenStream(cfg.hidden, T, seed=a.seed + 100)
-        for _ in range(a.prefill_steps):
-            stack.replay(stream.next().cuda())
-        xs = torch.stack([stream.next() for _ in range(W + K)]).cuda()
+        eng, _ = _build_stack(cfg, slots, layers, T, a, 1)
+        _precondition(a, eng, cfg, T, 0)
+        xs = _step_inputs(a, cfg, T, W + K, 0)
         for i in range(W):
-            stack.replay(xs[i])
+            eng.replay(xs[i])
         torch.cuda.synchronize()
-        ms, s0, s1, clk = _timed_replays(stack, xs, W, K, None)
+        ms, s0, s1, clk = _timed_replays(eng, xs, W, K, None)
         m, f = _misses(s0, s1)
-        roof = _step_roofline(_step_bytes(stack, cfg), f / K * cfg.bytes_per_expert, ms / K,
+        roof = _step_roofline(_step_bytes(eng, cfg), f / K * cfg.bytes_per_expert, ms / K,
                               hbm_peak)
         out[f"c{T}"] = {"value": T * K / (ms * 1e-3), "unit": UNIT, "ms_per_step": ms / K,
                         "misses_per_step": m / K, "step_roofline_frac": roof["frac"],
                         "clocks": clk}
-        del stack, xs
+        if hasattr(eng, "release"):
+            eng.release()
+        del eng, xs
         _free()
     return out
 
@@ -665,13 +804,11 @@ def run_sluice(a):
     t_build = time.perf_counter()
     stack, graphed = _build_stack(cfg, slots, layers, T, a, world, timers=offloaded)
     build_s = time.perf_counter() - t_build
-    stream = synth.TokenStream(cfg.hidden, T, seed=a.seed + 100 + rank)
-    # preconditioning: fill the slot caches, then the W warm-up steps
-    for _ in range(a.prefill_steps):
-        stack.replay(stream.next().cuda())
-    torch.cuda.synchronize()
+    # preconditioning (fill the slot caches; the decoder's prompts), then the
+    # W warm-up steps
+    _precondition(a, stack, cfg, T, rank)
     K, W = a.steps, a.warmup
-    xs = torch.stack([stream.next() for _ in range(W + K)]).cuda()
+    xs = _step_inputs(a, cfg, T, W + K, rank)
     for i in range(W):
         stack.replay(xs[i])
     torch.cuda.synchronize()
@@ -688,8 +825,15 @@ def run_sluice(a):
     # end to end through the public call: pinned host in, host out
     if restored:
         _stack_restore(stack, snap)
-    xh = xs[W:W + K].cpu().pin_memory()
-    oh = torch.empty(K, T, cfg.hidden, dtype=torch.bfloat16).pin_memory()
+    decoder = a.workload == "decoder"
+    if decoder:
+        # the serving loop: each step's ids go to the host and come back in
+        oh = torch.empty(K + 1, T, dtype=torch.long).pin_memory()
+        oh[0].copy_(stack._ids)
+        xh = oh[:-1]
+    else:
+        xh = xs[W:W + K].cpu().pin_memory()
+        oh = torch.empty(K, T, cfg.hidden, dtype=torch.bfloat16).pin_memory()
     se0 = stack.stats()
     if dist:
         dist.barrier()
@@ -697,7 +841,7 @@ def run_sluice(a):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for i in range(K):
-        stack.decode_step(xh[i], oh[i])
+        stack.decode_step(xh[i], oh[i + 1] if decoder else oh[i])
     e1.record()
     torch.cuda.synchronize()
     e2e_ms = _max_over_ranks(e0.elapsed_time(e1), dist)
@@ -747,7 +891,8 @@ def run_sluice(a):
     sprobe = None
     if world == 1:
         # fused_experts: each layer's call replayed as its own CUDA graph
-        route_ms, fused_ms, fbytes = profile_layers(stack, stream.next().cuda())
+        hx = synth.TokenStream(cfg.hidden, T, seed=a.seed + 555).next().cuda()
+        route_ms, fused_ms, fbytes = profile_layers(stack, hx)
         t_fused = statistics.mean(fused_ms)
         fused_gbs = statistics.mean(fbytes) / (t_fused * 1e-3) / 1e9
         roof_fused = {"bound": "hbm", "kernel": "fused_experts (align+gate/up+down+combine)",
@@ -772,7 +917,7 @@ def run_sluice(a):
 
     c1 = None
     if world == 1 and T != 1:
-        c1 = _timed_c1(stack, cfg, K, W, a.seed)
+        c1 = _timed_c1(stack, cfg, K, W, a.seed, a)
     if hasattr(stack, "release"):
         stack.release()
     del stack, xs
@@ -795,8 +940,8 @@ def run_sluice(a):
         resident = {"skipped": f"{resident_bytes / 1e9:.0f} GB of experts do not fit one GPU"}
     elif not a.no_resident and offloaded:
         rs, _ = _build_stack(cfg, local_n, layers, T, a, world)
-        rstream = synth.TokenStream(cfg.hidden, T, seed=a.seed + 100 + rank)
-        rx = torch.stack([rstream.next() for _ in range(W + K)]).cuda()
+        _precondition(a, rs, cfg, T, rank)
+        rx = _step_inputs(a, cfg, T, W + K, rank)
         for i in range(W):
             rs.replay(rx[i])
         torch.cuda.synchronize()
@@ -804,7 +949,7 @@ def run_sluice(a):
         resident = {"value": world * T * K / (rms * 1e-3), "unit": UNIT,
                     "slots": local_n, "ms_per_step": rms / K}
         if world == 1:
-            resident["c1"] = _timed_c1(rs, cfg, K, W, a.seed)
+            resident["c1"] = _timed_c1(rs, cfg, K, W, a.seed, a)
         if hasattr(rs, "release"):
             rs.release()
         del rs, rx
@@ -813,15 +958,19 @@ def run_sluice(a):
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         torch.set_num_threads(os.cpu_count() or 1)
-        t_cpu, n = cpu_step_time(cfg, slots, T, layers, a.seed, steps=K,
-                                 warmup=max(1, min(W, 2)), budget_s=150.0)
+        t_cpu, n = _cpu_time(a, cfg, slots, T, layers, a.seed, K, max(1, min(W, 2)), 150.0)
         cpu = {"value": T / t_cpu, "unit": UNIT, "cores": torch.get_num_threads(),
                "kind": "port",
-               "sample": f"{n} full decode steps ({layers} layers, c={T}, each layer its own "
-                         f"weights) of the torch-native CPU path (oracle routing + slot policy "
-                         f"+ MoE), median; the same sampling as the reference arm"}
+               "sample": f"{n} full decode steps ({a.workload}, {layers} MoE layers, c={T}, "
+                         f"each layer its own weights) of the torch-native CPU path (oracle "
+                         f"routing + slot policy + MoE), median; the same sampling as the "
+                         f"reference arm"}
 
     launches = K * layers * layer_launches(cfg, T, world, slots, a.exchange, a.no_overlap)
+    if a.prefetch and offloaded and world == 1 and not a.no_overlap:
+        # each layer but the last: the next router (gate + select), the
+        # prefetch planner and its stream
+        launches += K * (layers - 1) * 4
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
@@ -833,8 +982,8 @@ def run_sluice(a):
                 "ep_exchange": a.exchange if world > 1 else None,
                 "build_s": round(build_s, 1)},
         "e2e": {"value": world * T * K / (e2e_ms * 1e-3), "unit": UNIT,
-                "h2d_bytes_per_step": world * T * cfg.hidden * 2,
-                "d2h_bytes_per_step": world * T * cfg.hidden * 2,
+                "h2d_bytes_per_step": world * _io_bytes(a, cfg, T),
+                "d2h_bytes_per_step": world * _io_bytes(a, cfg, T),
                 "misses_per_step": e2e_misses / K,
                 "window": "the timed window's inputs"
                           + (" from its restored cache state (planner state, expert maps "
@@ -1124,8 +1273,8 @@ def run_reference(a):
     # port runs every expert of the model with --slots-frac of them in slots
     T = a.tokens * world
     torch.set_num_threads(os.cpu_count() or 1)
-    t_step, n = cpu_step_time(cfg, slots, T, layers, a.seed, steps=a.steps,
-                              warmup=max(1, min(a.warmup, 2)), budget_s=150.0)
+    t_step, n = _cpu_time(a, cfg, slots, T, layers, a.seed, a.steps,
+                          max(1, min(a.warmup, 2)), 150.0)
     v = T / t_step
     line = {
         "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": n,
@@ -1135,9 +1284,9 @@ def run_reference(a):
         "config": _config(a, cfg, _slots_for(a, cfg, world), a.tokens, layers, world),
         "cpu_baseline": {"value": v, "unit": UNIT, "cores": torch.get_num_threads(),
                          "kind": "port",
-                         "sample": f"{n} full decode steps ({layers} layers, each its own "
-                                   f"weights, c={T}, {slots} of {cfg.num_experts} experts in "
-                                   "slots), median"},
+                         "sample": f"{n} full decode steps ({a.workload}, {layers} MoE "
+                                   f"layers, each its own weights, c={T}, {slots} of "
+                                   f"{cfg.num_experts} experts in slots), median"},
         "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -1152,7 +1301,7 @@ def main(argv=None):
     elif a.workload == "prefill":
         run_prefill(a)
     else:
-        run_sluice(a)
+        run_sluice(a)   # decoder or moe-stack
 
 
 if __name__ == "__main__":

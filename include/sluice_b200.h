@@ -118,7 +118,8 @@ enum {
   SL_CNT_OVERFLOWS, SL_CNT_FILLS /* every expert streamed, gaps and waves */,
   /* steps planned by sl_plan_waves (the classic hook's _StepStats steps,
    * hits, misses and waves, offloader.py:172-183) */
-  SL_CNT_SCAN_STEPS, SL_CNT_SCAN_HITS, SL_CNT_SCAN_MISSES, SL_CNT_WAVES
+  SL_CNT_SCAN_STEPS, SL_CNT_SCAN_HITS, SL_CNT_SCAN_MISSES, SL_CNT_WAVES,
+  SL_CNT_PREFETCHES /* experts filled by sl_prefetch_slots */
 };
 size_t sl_slot_state_bytes(int num_slots, int global_n, int local_n);
 int sl_slot_state_offsets(int num_slots, int global_n, int local_n,
@@ -146,6 +147,21 @@ int sl_slot_state_init(void* state, int num_slots, int global_n, int local_n,
  * status word to SL_ERR_OVERFLOW (the map is then left as it was). */
 int sl_plan_slots(void* state, const int32_t* topk_ids, int num_ids,
                   int32_t* expert_map, sl_stream_t stream);
+
+/* Opt-in cross-layer prefetch, no counterpart in the reference (which
+ * measured its gate-ahead prefetch neutral on H100 and removed it,
+ * docs/EVALUATION.md:94-97): fill this layer's slots with experts predicted
+ * for its next step (e.g. the layer's router run on the previous layer's
+ * input) while the previous layer still computes. Predicted owned experts
+ * that are not resident, ascending id, at most max_fills, each into the free
+ * list's next slot or the least recently used probation slot (never a
+ * protected or pinned slot), as a new probation entry; no touches. The fills
+ * become the state's fill list: stream them with sl_stream_experts, and order
+ * the layer's next sl_plan_slots and its GEMMs after that stream. The
+ * standing map, if standing, is rewritten. Changes the slot trajectory
+ * relative to the reference's policy, so it is off unless called. */
+int sl_prefetch_slots(void* state, const int32_t* topk_ids, int num_ids,
+                      int max_fills, int32_t* expert_map, sl_stream_t stream);
 
 /* ---------------------------------------------- steps beyond the envelope
  * A step whose working set can exceed the slots (a prefill, or a mixed

@@ -96,6 +96,7 @@ class SlotPolicyModel:
         self.scan_hits = 0
         self.scan_misses = 0
         self.scan_waves = 0
+        self.prefetches = 0     # opt-in cross-layer prefetch fills
         if prefill_resident:
             # offloader.py:992-1003: every local expert preloaded into slot ==
             # local index, outside both SLRU segments; extra slots stay free.
@@ -273,6 +274,46 @@ class SlotPolicyModel:
             self.misses += len(missing)
             changed = True
         if changed or not self.map_is_standing:               # 2466-2467
+            self._write_standing_map()
+        return fills
+
+    # -- opt-in cross-layer prefetch (no counterpart in the reference) -------
+    def prefetch(self, ids: list[int], max_fills: int) -> list[tuple[int, int]]:
+        """Fill predicted experts ahead of this layer's gap (this build's
+        opt-in prefetch; the reference measured its gate-ahead prefetch
+        neutral and removed it, docs/EVALUATION.md:94-97, so there is no
+        reference code to follow).
+
+        Predicted owned experts that are not resident, in ascending id order,
+        at most ``max_fills``: each takes the free list's next slot, else the
+        least recently used probation slot not taken by this call (never a
+        protected or pinned slot), and becomes a new probation entry. No
+        touches, no LFU bump, no gap counters; the standing map is rewritten
+        when it was standing and something was filled."""
+        fills = []
+        claimed = set()
+        for g in sorted(set(int(v) for v in ids)):
+            if len(fills) >= max_fills:
+                break
+            if not (0 <= g < self.global_n):
+                continue
+            loc = self.local_of[g]
+            if loc < 0 or self.slot_of[loc] >= 0:
+                continue
+            if self.free_stack:
+                slot = self.free_stack.pop()
+            else:
+                slot = next((c for c in self._lru(PROBATION) if c not in claimed), None)
+                if slot is None:
+                    break
+            self._evict_to(slot, loc)
+            self.seg[slot] = PROBATION
+            self.stamp[slot] = self._tick()
+            claimed.add(slot)
+            fills.append((loc, slot))
+        self.prefetches = getattr(self, "prefetches", 0) + len(fills)
+        self.bytes_streamed += len(fills) * self.bytes_per_expert
+        if fills and self.map_is_standing:
             self._write_standing_map()
         return fills
 

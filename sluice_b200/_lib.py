@@ -33,7 +33,7 @@ HDR = dict(num_slots=0, global_n=1, local_n=2, protected_cap=3, flags=4,
            map_is_standing=5, free_top=6, protected_count=7, clock=8, status=9,
            fill_count=10, last_misses=11, lfu_steps=12)
 CNT = dict(gaps=0, fast_hits=1, misses=2, hits=3, overflows=4, fills=5, scan_steps=6,
-           scan_hits=7, scan_misses=8, waves=9)
+           scan_hits=7, scan_misses=8, waves=9, prefetches=10)
 STATE_NFIELDS = 12
 NUM_COUNTERS = 16
 
@@ -71,6 +71,7 @@ _SIGNATURES = {
     "sl_slot_state_init": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _i,
                                 _vp]),
     "sl_plan_slots": (_i, [_vp, _vp, _i, _vp, _vp]),
+    "sl_prefetch_slots": (_i, [_vp, _vp, _i, _i, _vp, _vp]),
     "sl_stream_experts": (_i, [_vp, _i, _vp, _vp, _vp, _i, _vp]),
     "sl_stream_experts_strided": (_i, [_vp, _i, _vp, _vp, _vp, _vp, _i, _vp]),
     "sl_wave_plan_bytes": (_sz, [_i, _i, _i]),

@@ -789,16 +789,23 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(
 //   token for the down GEMM (group amax across the four lane quadrants).
 // !GATED (down GEMM): 128 output rows per tile, bf16 out per (pair, row).
 // Roles: warp 0 TMA producer, warp 1 MMA issuer + TMEM owner, warps 2.. the
-// promotion / epilogue warps (4, or 8 for 128-token tiles: two groups of
-// token columns).
+// promotion / epilogue warps: four per group of 16 token columns (4 for
+// 16-token tiles, 16 for 64-token tiles). Each promotion warp reads its K
+// block's accumulator columns from TMEM and scales them with its own
+// products of weight block scale and token group scale, so no barrier is
+// taken inside the K loop.
 constexpr int F8_BK = 128;  // K per stage: one scale block, one 128-byte swizzle row
 constexpr int kF8MaxKBlocks = 64;  // K <= 8192: a tile's weight scales fit in shared memory
 
 template <int BN, bool GATED>
 struct F8Cfg {
-  static constexpr int kNP = BN >= 64 ? 8 : 4;          // promotion warps
+  // promotion warps: four per column group of 16 tokens (one per TMEM lane
+  // quadrant), so a warp's accumulators stay at 16 (down) or 32 (gate/up)
+  // registers and the warps of a K block work without waiting on each other
+  static constexpr int kNP = 4 * (BN / 16);
+  static constexpr int kGroups = kNP / 4;                // token-column groups
   static constexpr int kThreads = 64 + 32 * kNP;
-  static constexpr int kCW = BN / (kNP / 4);             // token columns per promotion warp
+  static constexpr int kCW = BN / kGroups;               // token columns per promotion warp
   static constexpr int kATiles = GATED ? 2 : 1;          // 128-row weight tiles per stage
   static constexpr int kABytes = kATiles * 128 * F8_BK;
   static constexpr int kBBytes = BN * F8_BK;
@@ -809,9 +816,9 @@ struct F8Cfg {
   static constexpr int kTmemUsed = kNB * kAccCols;
   static constexpr int kTmemCols = kTmemUsed <= 32 ? 32 : kTmemUsed <= 64 ? 64
                                    : kTmemUsed <= 128 ? 128 : kTmemUsed <= 256 ? 256 : 512;
-  // + amax exchange [4][BN], combined scales [2 parities][gate, up][BN],
-  // the tile's weight block scales [2 column groups][gate, up][64 K blocks]
-  static constexpr int kFixed = 1024 /*align*/ + 4 * BN * 4 + 4 * BN * 4 + 256 * 4 +
+  // + amax exchange [4][BN], the tile's weight block scales
+  // [column groups][gate, up][64 K blocks]
+  static constexpr int kFixed = 1024 /*align*/ + 4 * BN * 4 + kGroups * 128 * 4 +
                                 1024 /*barriers*/;
   static constexpr int kStagesRaw = (220 * 1024 - kFixed) / (kStageBytes + BN * 4);
   static constexpr int kStages = kStagesRaw > 12 ? 12 : kStagesRaw;
@@ -909,9 +916,8 @@ __global__ void __launch_bounds__(F8Cfg<BN, GATED>::kThreads, 1) moe_gemm_f8_ker
   uint8_t* sAB = smem;                                                  // [ST][A | B]
   float* sS = reinterpret_cast<float*>(sAB + ST * Cfg::kStageBytes);    // [ST][BN]
   float* red = sS + ST * BN;                                            // [4][BN]
-  float* cbuf = red + 4 * BN;                                           // [2][2][BN]
-  float* wsc = cbuf + 4 * BN;                                           // [2][2][64]
-  uint64_t* full = reinterpret_cast<uint64_t*>(wsc + 256);
+  float* wsc = red + 4 * BN;                                            // [groups][2][64]
+  uint64_t* full = reinterpret_cast<uint64_t*>(wsc + Cfg::kGroups * 128);
   uint64_t* empty = full + ST;
   uint64_t* tfull = empty + ST;
   uint64_t* tempty = tfull + NB;
@@ -1115,15 +1121,11 @@ __global__ void __launch_bounds__(F8Cfg<BN, GATED>::kThreads, 1) moe_gemm_f8_ker
         // (landed with the stage; its full phase stays complete until this
         // warp releases the stage)
         ok = ok && !*abort_flag && sl::mbar_wait(&tfull[b], bph) && sl::mbar_wait(&full[s], ph);
-        // combined scales of this column group for this K block:
-        // c[j] = weight block scale x token j's group scale
-        float* cb = cbuf + (kb & 1) * 2 * BN;
-        uint32_t vg[CW], vu[GATED ? CW : 1];
         if (ok) {
           sl::tc_fence_after();
           const uint32_t taddr = tmem_base + b * Cfg::kAccCols +
                                  (static_cast<uint32_t>(q * 32) << 16) + c0;
-          // every TMEM load of the stage in flight before the scales are made
+          uint32_t vg[CW], vu[GATED ? CW : 1];
 #pragma unroll
           for (int cc = 0; cc < CW; cc += 16)
             sl::tmem_ld16_nowait(taddr + cc, *reinterpret_cast<uint32_t(*)[16]>(vg + cc));
@@ -1132,13 +1134,19 @@ __global__ void __launch_bounds__(F8Cfg<BN, GATED>::kThreads, 1) moe_gemm_f8_ker
             for (int cc = 0; cc < CW; cc += 16)
               sl::tmem_ld16_nowait(taddr + BN + cc, *reinterpret_cast<uint32_t(*)[16]>(vu + cc));
           }
-          for (int v = gt; v < (GATED ? 2 : 1) * CW; v += 128) {
-            const int which = v >= CW, j = c0 + (v - which * CW);
-            cb[which * BN + j] = my_wsc[which * 64 + kb] * sS[s * BN + j];
+          // while the loads are in flight: this K block's weight block scale
+          // and the stage's token group scales of this warp's columns
+          const float wg = my_wsc[kb];
+          const float wu = GATED ? my_wsc[64 + kb] : 0.f;
+          float ts[CW];
+#pragma unroll
+          for (int i = 0; i < CW; i += 4) {
+            const float4 t4 = *reinterpret_cast<const float4*>(sS + s * BN + c0 + i);
+            ts[i] = t4.x;
+            ts[i + 1] = t4.y;
+            ts[i + 2] = t4.z;
+            ts[i + 3] = t4.w;
           }
-        }
-        named_bar_sync(1 + cg, 128);  // every warp of the group, ok or not
-        if (ok) {
 #pragma unroll
           for (int cc = 0; cc < CW; cc += 16)
             sl::tmem_wait_ld(*reinterpret_cast<uint32_t(*)[16]>(vg + cc));
@@ -1148,19 +1156,9 @@ __global__ void __launch_bounds__(F8Cfg<BN, GATED>::kThreads, 1) moe_gemm_f8_ker
               sl::tmem_wait_ld(*reinterpret_cast<uint32_t(*)[16]>(vu + cc));
           }
 #pragma unroll
-          for (int i = 0; i < CW; i += 4) {
-            const float4 c4 = *reinterpret_cast<const float4*>(cb + c0 + i);
-            acc_g[i] = fmaf(__uint_as_float(vg[i]), c4.x, acc_g[i]);
-            acc_g[i + 1] = fmaf(__uint_as_float(vg[i + 1]), c4.y, acc_g[i + 1]);
-            acc_g[i + 2] = fmaf(__uint_as_float(vg[i + 2]), c4.z, acc_g[i + 2]);
-            acc_g[i + 3] = fmaf(__uint_as_float(vg[i + 3]), c4.w, acc_g[i + 3]);
-            if constexpr (GATED) {
-              const float4 u4 = *reinterpret_cast<const float4*>(cb + BN + c0 + i);
-              acc_u[i] = fmaf(__uint_as_float(vu[i]), u4.x, acc_u[i]);
-              acc_u[i + 1] = fmaf(__uint_as_float(vu[i + 1]), u4.y, acc_u[i + 1]);
-              acc_u[i + 2] = fmaf(__uint_as_float(vu[i + 2]), u4.z, acc_u[i + 2]);
-              acc_u[i + 3] = fmaf(__uint_as_float(vu[i + 3]), u4.w, acc_u[i + 3]);
-            }
+          for (int i = 0; i < CW; ++i) {
+            acc_g[i] = fmaf(__uint_as_float(vg[i]), wg * ts[i], acc_g[i]);
+            if constexpr (GATED) acc_u[i] = fmaf(__uint_as_float(vu[i]), wu * ts[i], acc_u[i]);
           }
           sl::tc_fence_before();
         }

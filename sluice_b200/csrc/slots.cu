@@ -448,6 +448,88 @@ __global__ void __launch_bounds__(256) plan_kernel(uint8_t* state,
   }
 }
 
+// Opt-in cross-layer prefetch (no counterpart in the reference): predicted
+// owned experts that are not resident, ascending id, at most max_fills, each
+// into the free list's next slot or the least recently used probation slot
+// not taken by this call (never protected or pinned), as a new probation
+// entry. No touches, no LFU bump, no gap counters. The fills become the
+// state's fill list (stream them with sl_stream_experts); the standing map,
+// if standing, is rewritten.
+__global__ void __launch_bounds__(256) prefetch_kernel(uint8_t* state,
+                                                       const int32_t* __restrict__ ids,
+                                                       int num_ids, int max_fills,
+                                                       int32_t* __restrict__ emap) {
+  extern __shared__ __align__(16) uint8_t plan_smem_raw[];
+  sl::pdl_wait();
+  sl::pdl_trigger();
+  int S, G, L;
+  StateView st = view_from_header(state, S, G, L);
+  if (!plan_dims_ok(S, G, L)) {
+    if (threadIdx.x == 0) st.hdr[SL_HDR_STATUS] = SL_ERR_INVALID;
+    return;
+  }
+  PlanSmem sm = plan_smem(plan_smem_raw, S, G, L);
+  const int tid = threadIdx.x, nthr = blockDim.x;
+  load_plan_state(st, sm, S, G, L);
+  __syncthreads();
+  // only predicted owned experts that are not resident matter
+  for (int p = tid; p < num_ids; p += nthr) {
+    const int g = ids[p];
+    if (g >= 0 && g < G) {
+      const int loc = sm.local_of[g];
+      if (loc >= 0 && sm.slot_of[loc] < 0) atomicOr(&sm.bitmap[g >> 5], 1u << (g & 31));
+    }
+  }
+  if (tid == 0) {
+    st.hdr[SL_HDR_STATUS] = SL_OK;
+    st.hdr[SL_HDR_FILL_COUNT] = 0;
+  }
+  __syncthreads();
+  expand_uniques(sm, G);
+  const uint32_t clock0 = renorm_stamps(st, sm, S);
+  if (tid < 32) {
+    const int lane = tid;
+    uint32_t clock = clock0;
+    int free_top = st.hdr[SL_HDR_FREE_TOP];
+    const int U = sm.scal[1];
+    int fc = 0;
+    for (int i = 0; i < U && fc < max_fills; ++i) {
+      const int loc = sm.local_of[sm.uniq[i]];
+      int slot = free_top > 0 ? sm.free_s[--free_top] : -1;
+      if (slot < 0) slot = warp_lru(sm, S, SL_SEG_PROBATION, true);
+      if (slot < 0) break;
+      ++clock;
+      if (lane == 0) {
+        place_fill(st, sm, slot, loc, clock, false);
+        st.fill_local[fc] = loc;
+        st.fill_slot[fc] = slot;
+      }
+      ++fc;
+      __syncwarp();
+    }
+    if (lane == 0) {
+      st.hdr[SL_HDR_FREE_TOP] = free_top;
+      st.hdr[SL_HDR_CLOCK] = static_cast<int32_t>(clock);
+      st.hdr[SL_HDR_FILL_COUNT] = fc;
+      st.cnt[SL_CNT_PREFETCHES] += fc;
+      st.cnt[SL_CNT_FILLS] += fc;
+      sm.scal[2] = fc;
+    }
+  }
+  __syncthreads();
+  const int filled = sm.scal[2];
+  store_plan_state(st, sm, S, L);
+  if (filled > 0 && st.hdr[SL_HDR_MAP_IS_STANDING]) {
+    __syncthreads();
+    for (int g = tid; g < G; g += nthr) emap[g] = -1;
+    __syncthreads();
+    for (int s = tid; s < S; s += nthr) {
+      const int loc = sm.eis[s];
+      if (loc >= 0) emap[st.global_of_local[loc]] = s;
+    }
+  }
+}
+
 // One step beyond the envelope, planned in expert waves: the classic hook's
 // run_moe (offloader.py:1452-1764) and _run_waves (1846-1933) with the
 // reference's default switches, on a real step, no host round trip.
@@ -965,6 +1047,18 @@ extern "C" int sl_plan_waves(void* state, const int32_t* topk_ids, int num_token
                          reinterpret_cast<cudaStream_t>(stream), static_cast<uint8_t*>(state),
                          topk_ids, num_tokens, topk, decode_rows, expert_map,
                          static_cast<int32_t*>(waves)));
+  return SL_OK;
+}
+
+extern "C" int sl_prefetch_slots(void* state, const int32_t* topk_ids, int num_ids,
+                                 int max_fills, int32_t* expert_map, sl_stream_t stream) {
+  if (!state || !expert_map || num_ids < 0 || (num_ids > 0 && !topk_ids) || max_fills < 0)
+    return SL_ERR_INVALID;
+  static std::atomic<uint64_t> smem_set{0};
+  SL_CUDA_TRY(sl::ensure_smem_limit(prefetch_kernel, kPlanSmemBytes, smem_set));
+  SL_CUDA_TRY(sl::launch(prefetch_kernel, dim3(1), dim3(256), kPlanSmemBytes,
+                         reinterpret_cast<cudaStream_t>(stream), static_cast<uint8_t*>(state),
+                         topk_ids, num_ids, max_fills, expert_map));
   return SL_OK;
 }
 

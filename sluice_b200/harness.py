@@ -1,0 +1,263 @@
+"""A DeepSeek-V2-Lite-shaped decoder around the offloaded MoE layers.
+
+The reference's headline numbers are whole-model decode tok/s inside vLLM;
+this harness gives the MoE hot path the same surroundings at the shapes the
+workload names (random-init bf16, no checkpoint): token embedding, 27
+decoder layers of [RMSNorm -> multi-head latent attention -> residual ->
+RMSNorm -> FFN -> residual] with a dense SwiGLU FFN in layer 0 and an MoE
+layer elsewhere, final RMSNorm, the vocabulary head and greedy sampling.
+
+Only the MoE layers are this package's kernels (``SluiceMoELayer``: router,
+device slot planner, expert streamer, tcgen05 fused experts). Everything
+else is plain PyTorch (cuBLAS GEMMs): it is the harness around the hot path,
+not part of it. The same module runs on the host for the CPU baseline, with
+the MoE layers replaced by the oracle's torch-native MoE and slot policy.
+
+Attention is decode-only MLA in its absorbed form over a compressed cache
+(kv_lora_rank 512 latent + 64 rotary dims per token and layer): per token
+``q`` (16 heads x (128 nope + 64 rope)), the latent ``c_kv`` (RMSNormed) and
+``k_pe`` (rotary) are written at the sequence's position; scores are
+``q_nope W_uk . c_kv + q_pe . k_pe`` over every cached position (fixed
+shapes, masked beyond the sequence's length, so a step captures in one CUDA
+graph); the output is ``softmax . c_kv`` projected through ``W_uv`` and the
+output projection. Prompt tokens are fed through the same decode step, one
+position per step. Rotary embedding: plain RoPE (theta 10000).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+
+from .configs import V2_LITE, MoEConfig
+
+
+@dataclass(frozen=True)
+class DecoderConfig:
+    moe: MoEConfig
+    num_layers: int
+    first_dense: int          # leading layers with a dense FFN
+    dense_intermediate: int
+    num_heads: int
+    kv_lora_rank: int
+    qk_nope: int
+    qk_rope: int
+    v_head: int
+    vocab: int
+    rms_eps: float = 1e-6
+    rope_theta: float = 10000.0
+
+    @property
+    def hidden(self) -> int:
+        return self.moe.hidden
+
+    @property
+    def num_moe_layers(self) -> int:
+        return self.num_layers - self.first_dense
+
+
+V2_LITE_DECODER = DecoderConfig(
+    moe=V2_LITE, num_layers=27, first_dense=1, dense_intermediate=10944, num_heads=16,
+    kv_lora_rank=512, qk_nope=128, qk_rope=64, v_head=128, vocab=102400)
+
+
+def _rms(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    xf = x.float()
+    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)).to(x.dtype) * w
+
+
+def _rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """Rotate-half RoPE on the last dim of x [B, ..., R] with cos/sin [B, R/2]."""
+    shape = [cos.shape[0]] + [1] * (x.dim() - 2) + [cos.shape[1]]
+    c, s = cos.view(shape), sin.view(shape)
+    x1, x2 = x.float().chunk(2, dim=-1)
+    return torch.cat([x1 * c - x2 * s, x2 * c + x1 * s], dim=-1).to(x.dtype)
+
+
+class DecoderHarness:
+    """Greedy decode of ``batch`` sequences through the decoder; ``moe(li,
+    x)`` computes MoE layer ``li`` (0-based over the MoE layers) of normed
+    hidden states ``x`` [batch, H]."""
+
+    def __init__(self, cfg: DecoderConfig, moe, batch: int, max_len: int, seed: int = 0,
+                 device="cuda", std: float = 0.02):
+        self.cfg = cfg
+        self.moe = moe
+        self.batch = batch
+        self.max_len = max_len
+        self.device = torch.device(device)
+        dev, bf = self.device, torch.bfloat16
+        g = torch.Generator(device="cpu")
+        g.manual_seed(seed * 7919 + 17)
+        H, nh = cfg.hidden, cfg.num_heads
+        dq = cfg.qk_nope + cfg.qk_rope
+
+        def w(*shape):
+            return (torch.randn(*shape, generator=g) * std).to(bf).to(dev)
+
+        self.embed = w(cfg.vocab, H)
+        self.head = w(cfg.vocab, H)
+        self.final_norm = torch.ones(H, dtype=bf, device=dev)
+        self.layers = []
+        for li in range(cfg.num_layers):
+            lw = {
+                "in_norm": torch.ones(H, dtype=bf, device=dev),
+                "post_norm": torch.ones(H, dtype=bf, device=dev),
+                "kv_norm": torch.ones(cfg.kv_lora_rank, dtype=bf, device=dev),
+                "wq": w(nh * dq, H),
+                "wkva": w(cfg.kv_lora_rank + cfg.qk_rope, H),
+                # kv_b_proj [nh * (nope + v), rank] split per head into the
+                # absorbed key (W_uk) and value (W_uv) maps
+                "w_uk": w(nh, cfg.qk_nope, cfg.kv_lora_rank),
+                "w_uv": w(nh, cfg.v_head, cfg.kv_lora_rank),
+                "wo": w(H, nh * cfg.v_head),
+            }
+            if li < cfg.first_dense:
+                lw["w13"] = w(2 * cfg.dense_intermediate, H)
+                lw["w2"] = w(H, cfg.dense_intermediate)
+            self.layers.append(lw)
+        L = cfg.num_layers
+        self.cache_c = torch.zeros(L, batch, max_len, cfg.kv_lora_rank, dtype=bf, device=dev)
+        self.cache_pe = torch.zeros(L, batch, max_len, cfg.qk_rope, dtype=bf, device=dev)
+        inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, cfg.qk_rope, 2).float() / cfg.qk_rope))
+        ang = torch.arange(max_len).float()[:, None] * inv[None, :]
+        self.rope_cos = ang.cos().to(dev)
+        self.rope_sin = ang.sin().to(dev)
+        self.pos = torch.zeros(batch, dtype=torch.long, device=dev)
+        self.scale = 1.0 / math.sqrt(dq)
+        self._ar = torch.arange(max_len, device=dev)
+        self._rows = torch.arange(batch, device=dev)
+
+    def reset(self) -> None:
+        self.pos.zero_()
+
+    def _attention(self, li: int, x: torch.Tensor) -> torch.Tensor:
+        cfg, lw = self.cfg, self.layers[li]
+        B, nh = x.shape[0], cfg.num_heads
+        q = F.linear(x, lw["wq"]).view(B, nh, cfg.qk_nope + cfg.qk_rope)
+        q_nope, q_pe = q[..., :cfg.qk_nope], q[..., cfg.qk_nope:]
+        kv = F.linear(x, lw["wkva"])
+        c = _rms(kv[:, :cfg.kv_lora_rank], lw["kv_norm"], cfg.rms_eps)
+        cos, sin = self.rope_cos[self.pos], self.rope_sin[self.pos]
+        k_pe = _rope(kv[:, cfg.kv_lora_rank:], cos, sin)
+        q_pe = _rope(q_pe, cos, sin)
+        self.cache_c[li, self._rows, self.pos] = c
+        self.cache_pe[li, self._rows, self.pos] = k_pe
+        cc, cp = self.cache_c[li], self.cache_pe[li]
+        q_lat = torch.einsum("bhd,hdc->bhc", q_nope, lw["w_uk"])
+        s = torch.einsum("bhc,blc->bhl", q_lat, cc).float() + \
+            torch.einsum("bhr,blr->bhl", q_pe, cp).float()
+        s = s * self.scale
+        s = s.masked_fill((self._ar[None, :] > self.pos[:, None])[:, None, :], float("-inf"))
+        p = torch.softmax(s, dim=-1).to(x.dtype)
+        o_lat = torch.einsum("bhl,blc->bhc", p, cc)
+        o = torch.einsum("bhc,hdc->bhd", o_lat, lw["w_uv"]).reshape(B, nh * cfg.v_head)
+        return F.linear(o, lw["wo"])
+
+    def _dense_ffn(self, li: int, x: torch.Tensor) -> torch.Tensor:
+        lw = self.layers[li]
+        g, u = F.linear(x, lw["w13"]).chunk(2, dim=-1)
+        return F.linear(F.silu(g) * u, lw["w2"])
+
+    def step(self, ids: torch.Tensor) -> torch.Tensor:
+        """One decode step: token ids [batch] at the sequences' positions ->
+        the greedy next ids [batch]; the positions advance by one."""
+        cfg = self.cfg
+        h = self.embed[ids]
+        for li in range(cfg.num_layers):
+            lw = self.layers[li]
+            h = h + self._attention(li, _rms(h, lw["in_norm"], cfg.rms_eps))
+            x = _rms(h, lw["post_norm"], cfg.rms_eps)
+            if li < cfg.first_dense:
+                h = h + self._dense_ffn(li, x)
+            else:
+                h = h + self.moe(li - cfg.first_dense, x)
+        logits = F.linear(_rms(h, self.final_norm, cfg.rms_eps), self.head)
+        self.pos.add_(1)
+        return logits.argmax(dim=-1)
+
+
+class OffloadedDecoder:
+    """The decoder on this GPU with its MoE layers behind slot caches: the
+    layers of a ``MoEDecodeStack`` (one GPU) or an ``EPDecodeStack``
+    (expert parallelism: every rank decodes its own sequences, the MoE
+    layers exchange tokens with the other ranks). A decode step replays as
+    one CUDA graph that also feeds its greedy ids back as the next input."""
+
+    def __init__(self, cfg: DecoderConfig, stack, batch: int, max_len: int, seed: int = 0):
+        self.cfg = cfg
+        self.stack = stack
+        self.device = stack.device
+        layers = stack.layers
+        if len(layers) != cfg.num_moe_layers:
+            raise ValueError(f"{len(layers)} MoE layers for a decoder with {cfg.num_moe_layers}")
+        self.layers = layers          # the MoE layers (slot caches, stream timers)
+        self.model = DecoderHarness(cfg, lambda li, x: layers[li](x), batch, max_len, seed,
+                                    self.device)
+        self.graph = None
+        self._ids = torch.zeros(batch, dtype=torch.long, device=self.device)
+        self._out = None
+
+    def _step(self) -> torch.Tensor:
+        out = self.model.step(self._ids)
+        self._ids.copy_(out)
+        return out
+
+    def capture(self, tokens: int | None = None) -> bool:
+        """Capture one decode step (after one eager warm-up step, whose
+        position is then rewound)."""
+        ids0 = self._ids.clone()
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            self._step()
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        self.model.pos.sub_(1)
+        self._ids.copy_(ids0)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._out = self._step()
+        self.graph = g
+        return True
+
+    def replay(self, ids: torch.Tensor | None = None) -> torch.Tensor:
+        """One decode step; ``ids`` [batch] (device) are the input tokens, or
+        None to continue from the last step's greedy ids. Returns the next
+        ids [batch] (a static buffer)."""
+        if ids is not None:
+            self._ids.copy_(ids, non_blocking=True)
+        self.graph.replay()
+        return self._out
+
+    def decode_step(self, ids_host: torch.Tensor, out_host: torch.Tensor) -> torch.Tensor:
+        """Public end-to-end call: host token ids in, host next ids out."""
+        out_host.copy_(self.replay(ids_host.to(self.device, non_blocking=True)),
+                       non_blocking=True)
+        return out_host
+
+    def save(self) -> dict:
+        """The sequences' state (KV caches, positions, next input ids)."""
+        m = self.model
+        return {"c": m.cache_c.clone(), "pe": m.cache_pe.clone(), "pos": m.pos.clone(),
+                "ids": self._ids.clone()}
+
+    def restore(self, saved: dict) -> None:
+        m = self.model
+        m.cache_c.copy_(saved["c"])
+        m.cache_pe.copy_(saved["pe"])
+        m.pos.copy_(saved["pos"])
+        self._ids.copy_(saved["ids"])
+
+    def check(self) -> None:
+        self.stack.check()
+
+    def stats(self) -> dict:
+        return self.stack.stats()
+
+    def release(self) -> None:
+        self.graph = None
+        if hasattr(self.stack, "release"):
+            self.stack.release()

@@ -178,6 +178,12 @@ class SluiceMoELayer:
         self.last_logits = None
         # set to a StreamTimer to time every expert-stream launch
         self.stream_timer: StreamTimer | None = None
+        # opt-in cross-layer prefetch: the next layer (whose experts this
+        # layer predicts and streams after its own stream) and the event the
+        # next layer's planner waits for
+        self.prefetch_next: "SluiceMoELayer | None" = None
+        self.prefetch_max_fills = 0
+        self._prefetched: torch.cuda.Event | None = None
 
     @property
     def envelope(self) -> int:
@@ -198,6 +204,11 @@ class SluiceMoELayer:
         thr = self.envelope
         if self.stream_timer is not None:
             self.stream_timer.reset()
+        if self._prefetched is not None:
+            # the previous layer's prefetch into this cache wrote its state,
+            # fill list and slots: plan and compute after it
+            torch.cuda.current_stream().wait_event(self._prefetched)
+            self._prefetched = None
         if hs.shape[0] > thr:
             if self.beyond_envelope == "waves":
                 return self._forward_waves(hs, decode_rows)
@@ -241,13 +252,17 @@ class SluiceMoELayer:
 
     def _forward_overlapped(self, hs, tw, ti):
         """plan -> [stream on a side stream || resident experts' GEMMs] ->
-        streamed experts' GEMMs + combine."""
+        streamed experts' GEMMs + combine. With prefetch on, the side stream
+        then plans and streams the next layer's predicted experts (its router
+        on this layer's input) while this layer finishes."""
         c, cfg = self.cache, self.cfg
         main = torch.cuda.current_stream()
         c.plan(ti)
         self._side.wait_stream(main)
+        streamed = torch.cuda.Event()
         with torch.cuda.stream(self._side):
             _timed(self.stream_timer, self._side, lambda: c.stream(self.stream_ctas))
+            streamed.record(self._side)
         hs = hs.contiguous()
         T, H = hs.shape
         ws = ops.fused_experts_workspace(T, ti.shape[1], H, c.w13.shape[1] // 2,
@@ -260,7 +275,21 @@ class SluiceMoELayer:
                   shared_w2_scale=self.shared_w2_scale,
                   routed_scaling_factor=cfg.routed_scaling_factor)
         ops.fused_experts_phase(*args, 0, ws, out, **kw)
-        main.wait_stream(self._side)
+        nxt = self.prefetch_next
+        if nxt is not None and not nxt.cache.static_full and self.prefetch_max_fills > 0:
+            # predict the next layer's experts from this layer's input
+            _, ti_next, _ = nxt.router.route(hs)
+            predicted = torch.cuda.Event()
+            predicted.record(main)
+            nc = nxt.cache
+            with torch.cuda.stream(self._side):
+                self._side.wait_event(predicted)
+                nc.prefetch(ti_next, self.prefetch_max_fills)
+                _timed(self.stream_timer, self._side, lambda: nc.stream(self.stream_ctas))
+                done = torch.cuda.Event()
+                done.record(self._side)
+            nxt._prefetched = done
+        main.wait_event(streamed)
         return ops.fused_experts_phase(*args, 1, ws, out, **kw)
 
     __call__ = forward
@@ -271,7 +300,12 @@ class MoEDecodeStack:
 
     def __init__(self, cfg: MoEConfig, slots: int, seed: int = 0, device="cuda",
                  protect_frac: float | None = None, fast_hit: bool = True,
-                 num_layers: int | None = None, overlap: bool = True):
+                 num_layers: int | None = None, overlap: bool = True, prefetch: int = 0):
+        """``prefetch`` > 0 turns on the opt-in cross-layer prefetch: each
+        offloaded layer predicts the next layer's experts (the next router on
+        its own input) and streams up to ``prefetch`` of them into free or
+        probation slots after its own stream (``SlotCache.prefetch``). Off by
+        default: the slot maps then follow the reference's policy exactly."""
         self.cfg = cfg
         self.device = torch.device(device)
         self.offloader = ExpertStreamOffloader(slots, protect_frac=protect_frac,
@@ -291,6 +325,10 @@ class MoEDecodeStack:
                 cfg, router, cache, sh.get("shared_w13"), sh.get("shared_w2"), li,
                 overlap=overlap, shared_w13_scale=sh.get("shared_w13_scale"),
                 shared_w2_scale=sh.get("shared_w2_scale")))
+        if prefetch > 0 and overlap:
+            for cur, nxt in zip(self.layers, self.layers[1:]):
+                cur.prefetch_next = nxt
+                cur.prefetch_max_fills = int(prefetch)
         torch.cuda.synchronize(self.device)
         self.graphs: dict = {}  # tokens -> (graph, static input, static output)
 

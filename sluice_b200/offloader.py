@@ -267,6 +267,19 @@ class SlotCache:
         check(lib().sl_plan_slots(ptr(self.state), ptr(ids), ids.numel(), ptr(self.expert_map),
                                   torch.cuda.current_stream().cuda_stream), "sl_plan_slots")
 
+    def prefetch(self, topk_ids: torch.Tensor, max_fills: int) -> None:
+        """Opt-in cross-layer prefetch on the current stream
+        (``sl_prefetch_slots``): up to ``max_fills`` predicted experts that are
+        not resident take free or least recently used probation slots; call
+        ``stream()`` after it, and order this layer's next ``plan()`` after
+        that stream."""
+        ids = topk_ids if topk_ids.dtype == torch.int32 and topk_ids.is_contiguous() \
+            else topk_ids.contiguous().to(torch.int32)
+        check(lib().sl_prefetch_slots(ptr(self.state), ptr(ids), ids.numel(), int(max_fills),
+                                      ptr(self.expert_map),
+                                      torch.cuda.current_stream().cuda_stream),
+              "sl_prefetch_slots")
+
     def stream(self, stream_ctas: int = 0) -> None:
         """Stream the last plan's fills on the current stream."""
         n, src, dst, nb, hs = self._stream_args

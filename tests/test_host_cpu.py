@@ -409,3 +409,33 @@ def test_reference_op_names_registered_with_the_reference_schema():
         out = torch.ops.vllm.fused_experts(hs, w13, w2, tw, ti, activation="silu",
                                            global_num_experts=64, expert_map=emap)
         assert out.shape == hs.shape and out.dtype == torch.bfloat16
+
+
+def test_oracle_prefetch_policy():
+    """The oracle's restatement of the opt-in prefetch: an empty prediction
+    changes nothing; predicted residents are skipped; fills take the free
+    list first, then probation slots in LRU order, never protected or pinned
+    ones; at most max_fills; the standing map follows."""
+    import copy
+
+    from oracle.slot_policy import PROBATION, PROTECTED, SlotPolicyModel
+
+    m = SlotPolicyModel(6, list(range(16)), 16, 0.5, True)
+    m.gap([0, 1, 2, 3])                      # 4 slots taken, 2 free
+    m.gap([0, 1])                            # 0 and 1 promoted to protected
+    before = copy.deepcopy(m.__dict__)
+    assert m.prefetch([], 4) == [] and m.__dict__ == before
+    assert m.prefetch([0, 1, 2], 4) == []    # all resident
+    fills = m.prefetch([9, 8, 7, 6, 5], 3)   # ascending: 5, 6, 7
+    assert [l for l, _ in fills] == [5, 6, 7]
+    assert [s for _, s in fills][:2] == [4, 5]          # the two free slots first
+    prot = set(m.segment_order(PROTECTED))
+    assert all(s not in prot for _, s in fills)
+    assert m.segment_order(PROBATION)[-3:] == [s for _, s in fills]
+    assert all(m.expert_map[g] >= 0 for g in (5, 6, 7)) and m.prefetches == 3
+    # no probation slot left to take: nothing more is filled
+    m2 = SlotPolicyModel(2, list(range(8)), 8, 0.5, False)   # no FAST_HIT: hits touch
+    m2.gap([0, 1])
+    m2.gap([0])                              # slot of 0 promoted to protected (cap 1)
+    assert m2.prefetch([5, 6], 4) == [(5, m2.slot_of[5])]
+    assert m2.slot_of[1] < 0 and m2.slot_of[0] >= 0
