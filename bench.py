@@ -408,7 +408,7 @@ def profile_layers(stack, x):
     of (ms, algorithmic bytes)."""
     from sluice_b200 import ops
 
-    cfg = stack.cfg
+    cfg = stack.layers[0].cfg   # the MoE layers' config (also under the decoder)
     bpe = cfg.bytes_per_expert
     route_ms, fused_ms, fused_bytes = [], [], []
     h = x
@@ -646,10 +646,14 @@ def _stream_launch_window(stack, xs, W, K, bpe):
             if layer.stream_timer is None or layer.cache.static_full:
                 continue
             la = layer.stream_timer.launches()
-            waves = any(w >= 0 for _, w in la)
+            waves = any(w >= 0 for _, w, _ in la)
             counts = layer.cache.last_fill_counts(wave_steps=waves)
-            for ms, w in la:
-                rows.append((ms, (counts[w] if w >= 0 else counts[0]) * bpe))
+            for ms, w, other in la:
+                if other is not None:   # a prefetch into the next layer's cache
+                    n = other.header()["prefetch_fills"]
+                else:
+                    n = counts[w] if w >= 0 else counts[0]
+                rows.append((ms, n * bpe))
     return rows
 
 

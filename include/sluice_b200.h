@@ -111,7 +111,8 @@ enum {
   SL_HDR_NUM_SLOTS = 0, SL_HDR_GLOBAL_N, SL_HDR_LOCAL_N, SL_HDR_PROTECTED_CAP,
   SL_HDR_FLAGS, SL_HDR_MAP_IS_STANDING, SL_HDR_FREE_TOP, SL_HDR_PROTECTED_COUNT,
   SL_HDR_CLOCK, SL_HDR_STATUS, SL_HDR_FILL_COUNT, SL_HDR_LAST_MISSES,
-  SL_HDR_LFU_STEPS /* calls since the counts were last halved */
+  SL_HDR_LFU_STEPS, /* calls since the counts were last halved */
+  SL_HDR_PREFETCH_FILLS /* experts filled by the last sl_prefetch_slots */
 };
 enum {
   SL_CNT_GAPS = 0, SL_CNT_FAST_HITS, SL_CNT_MISSES, SL_CNT_HITS,

@@ -286,17 +286,19 @@ class SlotPolicyModel:
 
         Predicted owned experts that are not resident, in ascending id order,
         at most ``max_fills``: each takes the free list's next slot, else the
-        least recently used probation slot not taken by this call (never a
-        protected or pinned slot), and becomes a new probation entry. No
+        least recently used probation slot that neither holds a predicted
+        expert nor was taken by this call (never a protected or pinned slot),
+        and becomes a new probation entry. No
         touches, no LFU bump, no gap counters; the standing map is rewritten
         when it was standing and something was filled."""
         fills = []
-        claimed = set()
-        for g in sorted(set(int(v) for v in ids)):
+        wanted = sorted(set(int(v) for v in ids if 0 <= int(v) < self.global_n))
+        # predicted residents keep their slots
+        claimed = {self.slot_of[self.local_of[g]] for g in wanted
+                   if self.local_of[g] >= 0 and self.slot_of[self.local_of[g]] >= 0}
+        for g in wanted:
             if len(fills) >= max_fills:
                 break
-            if not (0 <= g < self.global_n):
-                continue
             loc = self.local_of[g]
             if loc < 0 or self.slot_of[loc] >= 0:
                 continue

@@ -31,7 +31,7 @@ PLAN_LFU = 2
 # state header words / counters (include/sluice_b200.h)
 HDR = dict(num_slots=0, global_n=1, local_n=2, protected_cap=3, flags=4,
            map_is_standing=5, free_top=6, protected_count=7, clock=8, status=9,
-           fill_count=10, last_misses=11, lfu_steps=12)
+           fill_count=10, last_misses=11, lfu_steps=12, prefetch_fills=13)
 CNT = dict(gaps=0, fast_hits=1, misses=2, hits=3, overflows=4, fills=5, scan_steps=6,
            scan_hits=7, scan_misses=8, waves=9, prefetches=10)
 STATE_NFIELDS = 12

@@ -1109,12 +1109,14 @@ __global__ void __launch_bounds__(F8Cfg<BN, GATED>::kThreads, 1) moe_gemm_f8_ker
         if constexpr (GATED) my_wsc[64 + gt] = __ldg(sc_u + gt);
       }
       named_bar_sync(1 + cg, 128);
-      float acc_g[CW], acc_u[GATED ? CW : 1];
+      // accumulators as column pairs: the K-block update is packed fp32x2
+      // arithmetic (two columns per instruction, each lane an IEEE fma)
+      float2 acc_g2[CW / 2], acc_u2[GATED ? CW / 2 : 1];
 #pragma unroll
-      for (int i = 0; i < CW; ++i) acc_g[i] = 0.f;
+      for (int i = 0; i < CW / 2; ++i) acc_g2[i] = make_float2(0.f, 0.f);
       if constexpr (GATED) {
 #pragma unroll
-        for (int i = 0; i < CW; ++i) acc_u[i] = 0.f;
+        for (int i = 0; i < CW / 2; ++i) acc_u2[i] = make_float2(0.f, 0.f);
       }
       for (int kb = 0; kb < k_blocks; ++kb) {
         // the accumulator of this K block, then the stage's token scales
@@ -1138,14 +1140,18 @@ __global__ void __launch_bounds__(F8Cfg<BN, GATED>::kThreads, 1) moe_gemm_f8_ker
           // and the stage's token group scales of this warp's columns
           const float wg = my_wsc[kb];
           const float wu = GATED ? my_wsc[64 + kb] : 0.f;
-          float ts[CW];
+          // combined scales of this warp's column pairs: weight block scale x
+          // token group scale
+          float2 cg2[CW / 2], cu2[GATED ? CW / 2 : 1];
 #pragma unroll
-          for (int i = 0; i < CW; i += 4) {
-            const float4 t4 = *reinterpret_cast<const float4*>(sS + s * BN + c0 + i);
-            ts[i] = t4.x;
-            ts[i + 1] = t4.y;
-            ts[i + 2] = t4.z;
-            ts[i + 3] = t4.w;
+          for (int i = 0; i < CW / 2; i += 2) {
+            const float4 t4 = *reinterpret_cast<const float4*>(sS + s * BN + c0 + 2 * i);
+            cg2[i] = __fmul2_rn(make_float2(wg, wg), make_float2(t4.x, t4.y));
+            cg2[i + 1] = __fmul2_rn(make_float2(wg, wg), make_float2(t4.z, t4.w));
+            if constexpr (GATED) {
+              cu2[i] = __fmul2_rn(make_float2(wu, wu), make_float2(t4.x, t4.y));
+              cu2[i + 1] = __fmul2_rn(make_float2(wu, wu), make_float2(t4.z, t4.w));
+            }
           }
 #pragma unroll
           for (int cc = 0; cc < CW; cc += 16)
@@ -1156,9 +1162,14 @@ __global__ void __launch_bounds__(F8Cfg<BN, GATED>::kThreads, 1) moe_gemm_f8_ker
               sl::tmem_wait_ld(*reinterpret_cast<uint32_t(*)[16]>(vu + cc));
           }
 #pragma unroll
-          for (int i = 0; i < CW; ++i) {
-            acc_g[i] = fmaf(__uint_as_float(vg[i]), wg * ts[i], acc_g[i]);
-            if constexpr (GATED) acc_u[i] = fmaf(__uint_as_float(vu[i]), wu * ts[i], acc_u[i]);
+          for (int i = 0; i < CW / 2; ++i) {
+            acc_g2[i] = __ffma2_rn(
+                make_float2(__uint_as_float(vg[2 * i]), __uint_as_float(vg[2 * i + 1])), cg2[i],
+                acc_g2[i]);
+            if constexpr (GATED)
+              acc_u2[i] = __ffma2_rn(
+                  make_float2(__uint_as_float(vu[2 * i]), __uint_as_float(vu[2 * i + 1])),
+                  cu2[i], acc_u2[i]);
           }
           sl::tc_fence_before();
         }
@@ -1179,6 +1190,16 @@ __global__ void __launch_bounds__(F8Cfg<BN, GATED>::kThreads, 1) moe_gemm_f8_ker
       if (!ok) {
         atomicExch(status, SL_ERR_TIMEOUT);
         *abort_flag = 1;
+      }
+      float acc_g[CW], acc_u[GATED ? CW : 1];
+#pragma unroll
+      for (int i = 0; i < CW / 2; ++i) {
+        acc_g[2 * i] = acc_g2[i].x;
+        acc_g[2 * i + 1] = acc_g2[i].y;
+        if constexpr (GATED) {
+          acc_u[2 * i] = acc_u2[i].x;
+          acc_u[2 * i + 1] = acc_u2[i].y;
+        }
       }
       if constexpr (GATED) {
         // every warp of this column group runs the same tiles and barriers

@@ -451,8 +451,8 @@ __global__ void __launch_bounds__(256) plan_kernel(uint8_t* state,
 // Opt-in cross-layer prefetch (no counterpart in the reference): predicted
 // owned experts that are not resident, ascending id, at most max_fills, each
 // into the free list's next slot or the least recently used probation slot
-// not taken by this call (never protected or pinned), as a new probation
-// entry. No touches, no LFU bump, no gap counters. The fills become the
+// neither holding a predicted expert nor taken by this call (never protected
+// or pinned), as a new probation entry. No touches, no LFU bump, no gap counters. The fills become the
 // state's fill list (stream them with sl_stream_experts); the standing map,
 // if standing, is rewritten.
 __global__ void __launch_bounds__(256) prefetch_kernel(uint8_t* state,
@@ -472,12 +472,16 @@ __global__ void __launch_bounds__(256) prefetch_kernel(uint8_t* state,
   const int tid = threadIdx.x, nthr = blockDim.x;
   load_plan_state(st, sm, S, G, L);
   __syncthreads();
-  // only predicted owned experts that are not resident matter
+  // predicted owned experts: residents keep their slots (claimed), the
+  // others are the candidates
   for (int p = tid; p < num_ids; p += nthr) {
     const int g = ids[p];
     if (g >= 0 && g < G) {
       const int loc = sm.local_of[g];
-      if (loc >= 0 && sm.slot_of[loc] < 0) atomicOr(&sm.bitmap[g >> 5], 1u << (g & 31));
+      if (loc < 0) continue;
+      const int slot = sm.slot_of[loc];
+      if (slot < 0) atomicOr(&sm.bitmap[g >> 5], 1u << (g & 31));
+      else sm.claimed[slot] = 1;
     }
   }
   if (tid == 0) {
@@ -511,6 +515,7 @@ __global__ void __launch_bounds__(256) prefetch_kernel(uint8_t* state,
       st.hdr[SL_HDR_FREE_TOP] = free_top;
       st.hdr[SL_HDR_CLOCK] = static_cast<int32_t>(clock);
       st.hdr[SL_HDR_FILL_COUNT] = fc;
+      st.hdr[SL_HDR_PREFETCH_FILLS] = fc;
       st.cnt[SL_CNT_PREFETCHES] += fc;
       st.cnt[SL_CNT_FILLS] += fc;
       sm.scal[2] = fc;

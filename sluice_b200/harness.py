@@ -90,13 +90,15 @@ class DecoderHarness:
         self.max_len = max_len
         self.device = torch.device(device)
         dev, bf = self.device, torch.bfloat16
-        g = torch.Generator(device="cpu")
+        # seeded on the device that holds the weights (the host port draws
+        # its own values: it is timed, not compared)
+        g = torch.Generator(device=dev)
         g.manual_seed(seed * 7919 + 17)
         H, nh = cfg.hidden, cfg.num_heads
         dq = cfg.qk_nope + cfg.qk_rope
 
         def w(*shape):
-            return (torch.randn(*shape, generator=g) * std).to(bf).to(dev)
+            return (torch.randn(*shape, generator=g, device=dev) * std).to(bf)
 
         self.embed = w(cfg.vocab, H)
         self.head = w(cfg.vocab, H)

@@ -58,7 +58,8 @@ class StreamTimer:
     streamer runs on; the events are external, so inside a CUDA-graph capture
     they become event-record nodes that every replay rewrites. ``launches()``
     (after the step has completed) gives each launch's device time with its
-    wave (-1 for a gap's single stream)."""
+    wave (-1 for a gap's single stream) and, for a prefetch launch, the cache
+    it filled."""
 
     def __init__(self):
         self.pairs: list = []
@@ -66,23 +67,26 @@ class StreamTimer:
     def reset(self) -> None:
         self.pairs = []
 
-    def around(self, stream: torch.cuda.Stream, fn, wave: int = -1) -> None:
+    def around(self, stream: torch.cuda.Stream, fn, wave: int = -1, other=None) -> None:
         a = torch.cuda.Event(enable_timing=True, external=True)
         b = torch.cuda.Event(enable_timing=True, external=True)
         a.record(stream)
         fn()
         b.record(stream)
-        self.pairs.append((a, b, wave))
+        self.pairs.append((a, b, wave, other))
 
-    def launches(self) -> list[tuple[float, int]]:
-        return [(a.elapsed_time(b), w) for a, b, w in self.pairs]
+    def launches(self) -> list[tuple[float, int, object]]:
+        """(ms, wave, other cache) per launch; ``other`` is the cache a
+        prefetch launch filled (the next layer's), else None."""
+        return [(a.elapsed_time(b), w, o) for a, b, w, o in self.pairs]
 
 
-def _timed(timer: "StreamTimer | None", stream: torch.cuda.Stream, fn, wave: int = -1) -> None:
+def _timed(timer: "StreamTimer | None", stream: torch.cuda.Stream, fn, wave: int = -1,
+           other=None) -> None:
     if timer is None:
         fn()
     else:
-        timer.around(stream, fn, wave)
+        timer.around(stream, fn, wave, other)
 
 
 def expert_waves(c: SlotCache, side: torch.cuda.Stream, hs: torch.Tensor, tw: torch.Tensor,
@@ -285,7 +289,8 @@ class SluiceMoELayer:
             with torch.cuda.stream(self._side):
                 self._side.wait_event(predicted)
                 nc.prefetch(ti_next, self.prefetch_max_fills)
-                _timed(self.stream_timer, self._side, lambda: nc.stream(self.stream_ctas))
+                _timed(self.stream_timer, self._side, lambda: nc.stream(self.stream_ctas),
+                       other=nc)
                 done = torch.cuda.Event()
                 done.record(self._side)
             nxt._prefetched = done
