@@ -41,6 +41,8 @@ int fused_experts_check(const void* hidden, int T, int H, int I, const sl_expert
 
 // Bounded waits give up after this many nanoseconds of %globaltimer.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+// Longest a single mbarrier try_wait may park its warp (a hint).
+constexpr uint32_t kTryWaitSuspendNs = 1000000u;  // 1 ms
 
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
@@ -75,13 +77,16 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
                : "memory");
 }
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  // the suspend-time hint lets the hardware park the waiting warp until the
+  // phase completes (or the hint's time passes) instead of spinning, so
+  // waiting warps do not take issue slots from the producer / MMA warps
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kTryWaitSuspendNs)
       : "memory");
   return ok != 0;
 }
@@ -91,7 +96,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   const uint64_t t0 = globaltimer();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 0 && globaltimer() - t0 > kWaitLimitNs) return false;
+    if ((i & 15u) == 0 && globaltimer() - t0 > kWaitLimitNs) return false;
   }
 }
 

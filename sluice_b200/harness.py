@@ -21,7 +21,8 @@ Attention is decode-only MLA in its absorbed form over a compressed cache
 shapes, masked beyond the sequence's length, so a step captures in one CUDA
 graph); the output is ``softmax . c_kv`` projected through ``W_uv`` and the
 output projection. Prompt tokens are fed through the same decode step, one
-position per step. Rotary embedding: plain RoPE (theta 10000).
+position per step. Rotary embedding: RoPE (theta 10000) on adjacent dim
+pairs. The causal mask is an additive bias folded into the score GEMM.
 """
 
 from __future__ import annotations
@@ -65,16 +66,15 @@ V2_LITE_DECODER = DecoderConfig(
 
 
 def _rms(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
-    xf = x.float()
-    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)).to(x.dtype) * w
+    return F.rms_norm(x, (x.shape[-1],), w, eps)
 
 
-def _rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
-    """Rotate-half RoPE on the last dim of x [B, ..., R] with cos/sin [B, R/2]."""
-    shape = [cos.shape[0]] + [1] * (x.dim() - 2) + [cos.shape[1]]
-    c, s = cos.view(shape), sin.view(shape)
-    x1, x2 = x.float().chunk(2, dim=-1)
-    return torch.cat([x1 * c - x2 * s, x2 * c + x1 * s], dim=-1).to(x.dtype)
+def _rope(x: torch.Tensor, freqs: torch.Tensor) -> torch.Tensor:
+    """RoPE on the last dim of x [B, ..., R] (pairs of adjacent dims rotated
+    as complex numbers) by freqs [B, R/2] (complex64)."""
+    shape = [freqs.shape[0]] + [1] * (x.dim() - 2) + [freqs.shape[1]]
+    xc = torch.view_as_complex(x.float().reshape(*x.shape[:-1], -1, 2))
+    return torch.view_as_real(xc * freqs.view(shape)).flatten(-2).to(x.dtype)
 
 
 class DecoderHarness:
@@ -109,8 +109,8 @@ class DecoderHarness:
                 "in_norm": torch.ones(H, dtype=bf, device=dev),
                 "post_norm": torch.ones(H, dtype=bf, device=dev),
                 "kv_norm": torch.ones(cfg.kv_lora_rank, dtype=bf, device=dev),
-                "wq": w(nh * dq, H),
-                "wkva": w(cfg.kv_lora_rank + cfg.qk_rope, H),
+                # q_proj [nh * dq, H] and kv_a_proj [rank + rope, H] as one GEMM
+                "wqkv": w(nh * dq + cfg.kv_lora_rank + cfg.qk_rope, H),
                 # kv_b_proj [nh * (nope + v), rank] split per head into the
                 # absorbed key (W_uk) and value (W_uv) maps
                 "w_uk": w(nh, cfg.qk_nope, cfg.kv_lora_rank),
@@ -122,42 +122,44 @@ class DecoderHarness:
                 lw["w2"] = w(H, cfg.dense_intermediate)
             self.layers.append(lw)
         L = cfg.num_layers
-        self.cache_c = torch.zeros(L, batch, max_len, cfg.kv_lora_rank, dtype=bf, device=dev)
-        self.cache_pe = torch.zeros(L, batch, max_len, cfg.qk_rope, dtype=bf, device=dev)
+        # compressed cache per layer and position: [c_kv (rank) | k_pe (rope)]
+        self.cache = torch.zeros(L, batch, max_len, cfg.kv_lora_rank + cfg.qk_rope, dtype=bf,
+                                 device=dev)
         inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, cfg.qk_rope, 2).float() / cfg.qk_rope))
         ang = torch.arange(max_len).float()[:, None] * inv[None, :]
-        self.rope_cos = ang.cos().to(dev)
-        self.rope_sin = ang.sin().to(dev)
+        self.freqs = torch.polar(torch.ones_like(ang), ang).to(dev)   # complex64
         self.pos = torch.zeros(batch, dtype=torch.long, device=dev)
         self.scale = 1.0 / math.sqrt(dq)
         self._ar = torch.arange(max_len, device=dev)
         self._rows = torch.arange(batch, device=dev)
+        # w_uk / w_uv per head, laid out for batched GEMMs over heads
+        for lw in self.layers:
+            lw["w_uk_t"] = lw["w_uk"].contiguous()                  # [nh, nope, rank]
+            lw["w_uv_t"] = lw["w_uv"].transpose(1, 2).contiguous()  # [nh, rank, v]
 
     def reset(self) -> None:
         self.pos.zero_()
 
-    def _attention(self, li: int, x: torch.Tensor) -> torch.Tensor:
+    def _attention(self, li: int, x: torch.Tensor, mask_bias: torch.Tensor,
+                   freqs: torch.Tensor) -> torch.Tensor:
         cfg, lw = self.cfg, self.layers[li]
-        B, nh = x.shape[0], cfg.num_heads
-        q = F.linear(x, lw["wq"]).view(B, nh, cfg.qk_nope + cfg.qk_rope)
-        q_nope, q_pe = q[..., :cfg.qk_nope], q[..., cfg.qk_nope:]
-        kv = F.linear(x, lw["wkva"])
-        c = _rms(kv[:, :cfg.kv_lora_rank], lw["kv_norm"], cfg.rms_eps)
-        cos, sin = self.rope_cos[self.pos], self.rope_sin[self.pos]
-        k_pe = _rope(kv[:, cfg.kv_lora_rank:], cos, sin)
-        q_pe = _rope(q_pe, cos, sin)
-        self.cache_c[li, self._rows, self.pos] = c
-        self.cache_pe[li, self._rows, self.pos] = k_pe
-        cc, cp = self.cache_c[li], self.cache_pe[li]
-        q_lat = torch.einsum("bhd,hdc->bhc", q_nope, lw["w_uk"])
-        s = torch.einsum("bhc,blc->bhl", q_lat, cc).float() + \
-            torch.einsum("bhr,blr->bhl", q_pe, cp).float()
-        s = s * self.scale
-        s = s.masked_fill((self._ar[None, :] > self.pos[:, None])[:, None, :], float("-inf"))
-        p = torch.softmax(s, dim=-1).to(x.dtype)
-        o_lat = torch.einsum("bhl,blc->bhc", p, cc)
-        o = torch.einsum("bhc,hdc->bhd", o_lat, lw["w_uv"]).reshape(B, nh * cfg.v_head)
-        return F.linear(o, lw["wo"])
+        B, nh, R = x.shape[0], cfg.num_heads, cfg.kv_lora_rank
+        dq = cfg.qk_nope + cfg.qk_rope
+        qkv = F.linear(x, lw["wqkv"])
+        q = qkv[:, :nh * dq].view(B, nh, dq)
+        kv = qkv[:, nh * dq:]
+        c = _rms(kv[:, :R], lw["kv_norm"], cfg.rms_eps)
+        k_pe = _rope(kv[:, R:], freqs)
+        self.cache[li, self._rows, self.pos] = torch.cat([c, k_pe], dim=-1)
+        # absorbed query: [q_nope W_uk | rope(q_pe)] against [c_kv | k_pe]
+        q_lat = torch.bmm(q[..., :cfg.qk_nope].transpose(0, 1), lw["w_uk_t"])  # [nh, B, R]
+        qf = torch.cat([q_lat.transpose(0, 1), _rope(q[..., cfg.qk_nope:], freqs)], dim=-1)
+        cl = self.cache[li]                                                   # [B, Lmax, R+r]
+        s = torch.baddbmm(mask_bias, qf, cl.transpose(1, 2), alpha=self.scale)
+        p = torch.softmax(s, dim=-1)
+        o_lat = torch.bmm(p, cl[..., :R])                                     # [B, nh, R]
+        o = torch.bmm(o_lat.transpose(0, 1), lw["w_uv_t"])                   # [nh, B, v]
+        return F.linear(o.transpose(0, 1).reshape(B, nh * cfg.v_head), lw["wo"])
 
     def _dense_ffn(self, li: int, x: torch.Tensor) -> torch.Tensor:
         lw = self.layers[li]
@@ -169,9 +171,15 @@ class DecoderHarness:
         the greedy next ids [batch]; the positions advance by one."""
         cfg = self.cfg
         h = self.embed[ids]
+        # per step: the positions' rotations and the causal mask as an additive
+        # bias over the cache (0 up to each sequence's position, -inf after)
+        freqs = self.freqs[self.pos]
+        mask_bias = torch.zeros(h.shape[0], 1, self.max_len, dtype=h.dtype, device=h.device)
+        mask_bias.masked_fill_((self._ar[None, :] > self.pos[:, None])[:, None, :],
+                               float("-inf"))
         for li in range(cfg.num_layers):
             lw = self.layers[li]
-            h = h + self._attention(li, _rms(h, lw["in_norm"], cfg.rms_eps))
+            h = h + self._attention(li, _rms(h, lw["in_norm"], cfg.rms_eps), mask_bias, freqs)
             x = _rms(h, lw["post_norm"], cfg.rms_eps)
             if li < cfg.first_dense:
                 h = h + self._dense_ffn(li, x)
@@ -243,13 +251,11 @@ class OffloadedDecoder:
     def save(self) -> dict:
         """The sequences' state (KV caches, positions, next input ids)."""
         m = self.model
-        return {"c": m.cache_c.clone(), "pe": m.cache_pe.clone(), "pos": m.pos.clone(),
-                "ids": self._ids.clone()}
+        return {"cache": m.cache.clone(), "pos": m.pos.clone(), "ids": self._ids.clone()}
 
     def restore(self, saved: dict) -> None:
         m = self.model
-        m.cache_c.copy_(saved["c"])
-        m.cache_pe.copy_(saved["pe"])
+        m.cache.copy_(saved["cache"])
         m.pos.copy_(saved["pos"])
         self._ids.copy_(saved["ids"])
 
