@@ -917,7 +917,19 @@ def run_sluice(a):
                       "traffic": None,
                       "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)",
                       "timing": "timed region, max over ranks"}
-    roof = roof_stream if roof_stream is not None else roof_fused
+    # the dominant kernel of the step: the expert streamer or the fused
+    # experts, whichever takes more device time per step
+    roof = roof_fused
+    if roof_stream is not None:
+        stream_ms_step = st_ms / K / (world if world > 1 else 1)
+        fused_ms_step = (roof_fused.get("per_launch_ms", {}).get("fused", 0.0) * layers
+                         if world == 1 else 0.0)
+        roof_stream["ms_per_step"] = stream_ms_step
+        if world == 1:
+            roof_fused["ms_per_step"] = fused_ms_step
+        if stream_ms_step >= fused_ms_step:
+            roof = roof_stream
+    roof_other = roof_stream if roof is roof_fused else roof_fused
 
     c1 = None
     if world == 1 and T != 1:
@@ -994,7 +1006,7 @@ def run_sluice(a):
                              "and slot contents)" if restored else
                              ", continuing from the cache state the timed window left")},
         "roofline": roof,
-        "roofline_fused_experts": roof_fused,
+        "roofline_other": roof_other,
         "step_roofline": step_roof,
         "stream": {"misses_per_step": misses / K, "fills_per_step": fills / K,
                    "bytes_per_step": fills / K * bpe, "probe": sprobe,
