@@ -60,13 +60,16 @@ def test_host_calls_reject_bad_arguments_without_a_gpu():
     assert L.sl_stream_experts_strided(None, 0, None, None, None, None, 0,
                                        None) == _lib.SL_ERR_INVALID
     # expert-parallel exchange: sizes, and world / rank / shape checks
-    assert L.sl_ep_dispatch_recv_bytes(2, 8, 2048, 6) == 2 * 2 * 8 * (2 * 2048 + 8 * 6)
+    # routed rows: hidden | weights | ids | token index, padded to 16 bytes,
+    # after a 128-byte header (the row counts) per half
+    row = (2 * 2048 + 8 * 6 + 4 + 15) // 16 * 16
+    assert L.sl_ep_dispatch_recv_bytes(2, 8, 2048, 6) == 2 * (128 + 2 * 8 * row)
     assert L.sl_ep_combine_recv_bytes(2, 8, 2048) == 2 * 2 * 8 * 2048 * 4
     assert L.sl_ep_dispatch_recv_bytes(0, 8, 2048, 6) == 0
-    assert L.sl_ep_dispatch(None, None, None, 8, 2048, 6, 0, 9, None, None, None, None,
-                            None, None, None, None) == _lib.SL_ERR_INVALID
-    assert L.sl_ep_combine(None, 8, 2048, 0, 0, None, None, None, None, None, None,
-                           None) == _lib.SL_ERR_INVALID
+    assert L.sl_ep_dispatch(None, None, None, 8, 2048, 6, 64, 0, 9, None, None, None, None,
+                            None, None, None, None, None) == _lib.SL_ERR_INVALID
+    assert L.sl_ep_combine(None, None, None, 8, 2048, 6, 64, 0, 0, None, None, None, None,
+                           None, None, None) == _lib.SL_ERR_INVALID
     # expert waves: layout and argument checks
     offs = (ctypes.c_size_t * (_lib.WAVE_NFIELDS + 1))()
     assert L.sl_wave_plan_offsets(48, 64, 7, offs) == 0
