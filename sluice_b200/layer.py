@@ -208,11 +208,6 @@ class SluiceMoELayer:
         thr = self.envelope
         if self.stream_timer is not None:
             self.stream_timer.reset()
-        if self._prefetched is not None:
-            # the previous layer's prefetch into this cache wrote its state,
-            # fill list and slots: plan and compute after it
-            torch.cuda.current_stream().wait_event(self._prefetched)
-            self._prefetched = None
         if hs.shape[0] > thr:
             if self.beyond_envelope == "waves":
                 return self._forward_waves(hs, decode_rows)
@@ -228,10 +223,19 @@ class SluiceMoELayer:
             return torch.cat(outs)
         return self._forward_step(hs)
 
+    def _await_prefetch(self) -> None:
+        """Order this layer's planner (and everything after it) after the
+        previous layer's prefetch into this cache, which wrote its state,
+        fill list and slots; the router runs before, unordered."""
+        if self._prefetched is not None:
+            torch.cuda.current_stream().wait_event(self._prefetched)
+            self._prefetched = None
+
     def _forward_waves(self, hs: torch.Tensor, decode_rows) -> torch.Tensor:
         hs = hs.contiguous()
         tw, ti, logits = self.router.route(hs)
         self.last_ids, self.last_logits = ti, logits
+        self._await_prefetch()
         acc = expert_waves(self.cache, self._side, hs, tw, ti, decode_rows,
                            self.shared_w13, self.shared_w2, 0, hs.shape[0],
                            self.cfg.routed_scaling_factor, self.shared_w13_scale,
@@ -241,6 +245,7 @@ class SluiceMoELayer:
     def _forward_step(self, hs: torch.Tensor) -> torch.Tensor:
         tw, ti, logits = self.router.route(hs)
         self.last_ids, self.last_logits = ti, logits
+        self._await_prefetch()
         if self.overlap:
             return self._forward_overlapped(hs, tw, ti)
         self.cache.gap(ti)
@@ -261,13 +266,28 @@ class SluiceMoELayer:
         on this layer's input) while this layer finishes."""
         c, cfg = self.cache, self.cfg
         main = torch.cuda.current_stream()
+        hs = hs.contiguous()
         c.plan(ti)
         self._side.wait_stream(main)
         streamed = torch.cuda.Event()
+        nxt = self.prefetch_next
+        prefetch = (nxt is not None and not nxt.cache.static_full and
+                    self.prefetch_max_fills > 0)
         with torch.cuda.stream(self._side):
             _timed(self.stream_timer, self._side, lambda: c.stream(self.stream_ctas))
             streamed.record(self._side)
-        hs = hs.contiguous()
+            if prefetch:
+                # on the copy stream, after this layer's own stream: predict the
+                # next layer's experts (its router on this layer's input), plan
+                # and stream them; the next layer plans after this
+                _, ti_next, _ = nxt.router.route(hs)
+                nc = nxt.cache
+                nc.prefetch(ti_next, self.prefetch_max_fills)
+                _timed(self.stream_timer, self._side, lambda: nc.stream(self.stream_ctas),
+                       other=nc)
+                done = torch.cuda.Event()
+                done.record(self._side)
+                nxt._prefetched = done
         T, H = hs.shape
         ws = ops.fused_experts_workspace(T, ti.shape[1], H, c.w13.shape[1] // 2,
                                          c.num_slots, 0 if self.shared_w13 is None
@@ -279,21 +299,6 @@ class SluiceMoELayer:
                   shared_w2_scale=self.shared_w2_scale,
                   routed_scaling_factor=cfg.routed_scaling_factor)
         ops.fused_experts_phase(*args, 0, ws, out, **kw)
-        nxt = self.prefetch_next
-        if nxt is not None and not nxt.cache.static_full and self.prefetch_max_fills > 0:
-            # predict the next layer's experts from this layer's input
-            _, ti_next, _ = nxt.router.route(hs)
-            predicted = torch.cuda.Event()
-            predicted.record(main)
-            nc = nxt.cache
-            with torch.cuda.stream(self._side):
-                self._side.wait_event(predicted)
-                nc.prefetch(ti_next, self.prefetch_max_fills)
-                _timed(self.stream_timer, self._side, lambda: nc.stream(self.stream_ctas),
-                       other=nc)
-                done = torch.cuda.Event()
-                done.record(self._side)
-            nxt._prefetched = done
         main.wait_event(streamed)
         return ops.fused_experts_phase(*args, 1, ws, out, **kw)
 
