@@ -188,6 +188,7 @@ class SluiceMoELayer:
         self.prefetch_next: "SluiceMoELayer | None" = None
         self.prefetch_max_fills = 0
         self._prefetched: torch.cuda.Event | None = None
+        self._prefetch_input: torch.Tensor | None = None
 
     @property
     def envelope(self) -> int:
@@ -230,6 +231,7 @@ class SluiceMoELayer:
         if self._prefetched is not None:
             torch.cuda.current_stream().wait_event(self._prefetched)
             self._prefetched = None
+            self._prefetch_input = None
 
     def _forward_waves(self, hs: torch.Tensor, decode_rows) -> torch.Tensor:
         hs = hs.contiguous()
@@ -288,6 +290,9 @@ class SluiceMoELayer:
                 done = torch.cuda.Event()
                 done.record(self._side)
                 nxt._prefetched = done
+                # the copy stream reads hs: keep it alive until the next layer
+                # has ordered its stream after that read
+                nxt._prefetch_input = hs
         T, H = hs.shape
         ws = ops.fused_experts_workspace(T, ti.shape[1], H, c.w13.shape[1] // 2,
                                          c.num_slots, 0 if self.shared_w13 is None
