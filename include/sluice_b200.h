@@ -396,6 +396,25 @@ int sl_ep_combine(const float* partial, const int32_t* src, const int32_t* topk_
                   void* const* peer_recv, void* const* peer_signal, void* book,
                   const void* residual, void* out, int32_t* status, sl_stream_t stream);
 
+/* ---------------------------------------------------- decoder harness
+ * Not part of the reference's MoE operator surface: the attention of the
+ * DeepSeek-V2-Lite-shaped decoder that wraps the MoE layers in this build's
+ * benchmark (the reference runs inside vLLM, whose attention this stands in
+ * for). One decode step of absorbed multi-head latent attention for B
+ * sequences: qkv bf16 [B, ld_qkv] rows [q (nh x (nope + rope)) | c_kv (rank)
+ * | k_pe (rope)]; c_kv RMSNormed (kv_norm bf16 [rank], eps) and k_pe / q_pe
+ * rotated by rope_cos_sin (f32 [max_len, rope/2, 2], adjacent pairs) at
+ * position pos[b] (int64 [B]); the position's [c_kv | k_pe] is written to
+ * cache bf16 [B, max_len, rank + rope]; scores of [q_nope W_uk | q_pe]
+ * (w_uk bf16 [nh, nope, rank]) against positions 0..pos[b], times scale,
+ * softmax; out bf16 [B, nh * vdim] = (sum_l p_l c_l) W_uv^T per head (w_uv
+ * bf16 [nh, vdim, rank]). */
+int sl_mla_decode(const void* qkv, int ld_qkv, const void* kv_norm, float eps,
+                  const void* w_uk, const void* w_uv, const float* rope_cos_sin,
+                  const int64_t* pos, void* cache, int B, int nh, int nope, int rope,
+                  int rank, int vdim, int max_len, float scale, void* out,
+                  sl_stream_t stream);
+
 /* sl_fused_experts without any device allocation. No counterpart in the
  * reference: it serves callers that cannot allocate device scratch memory for
  * a call -- a host program binding this C ABI directly (cgo, JNI, ctypes

@@ -83,7 +83,10 @@ class DecoderHarness:
     hidden states ``x`` [batch, H]."""
 
     def __init__(self, cfg: DecoderConfig, moe, batch: int, max_len: int, seed: int = 0,
-                 device="cuda", std: float = 0.02):
+                 device="cuda", std: float = 0.02, fused_attention: bool | None = None):
+        """``fused_attention`` (default: on a CUDA device) runs each layer's
+        attention core as the library's one-launch MLA decode kernel
+        (``sl_mla_decode``); otherwise, and on the host, as PyTorch ops."""
         self.cfg = cfg
         self.moe = moe
         self.batch = batch
@@ -128,6 +131,9 @@ class DecoderHarness:
         inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, cfg.qk_rope, 2).float() / cfg.qk_rope))
         ang = torch.arange(max_len).float()[:, None] * inv[None, :]
         self.freqs = torch.polar(torch.ones_like(ang), ang).to(dev)   # complex64
+        self.rope_cs = torch.view_as_real(self.freqs).contiguous()    # [max_len, r/2, 2]
+        self.fused_attention = (self.device.type == "cuda") if fused_attention is None \
+            else bool(fused_attention)
         self.pos = torch.zeros(batch, dtype=torch.long, device=dev)
         self.scale = 1.0 / math.sqrt(dq)
         self._ar = torch.arange(max_len, device=dev)
@@ -146,6 +152,16 @@ class DecoderHarness:
         B, nh, R = x.shape[0], cfg.num_heads, cfg.kv_lora_rank
         dq = cfg.qk_nope + cfg.qk_rope
         qkv = F.linear(x, lw["wqkv"])
+        if self.fused_attention:
+            from ._lib import check, lib, ptr
+            o = torch.empty(B, nh * cfg.v_head, dtype=x.dtype, device=x.device)
+            check(lib().sl_mla_decode(ptr(qkv), qkv.shape[1], ptr(lw["kv_norm"]), cfg.rms_eps,
+                                      ptr(lw["w_uk_t"]), ptr(lw["w_uv"]), ptr(self.rope_cs),
+                                      ptr(self.pos), ptr(self.cache[li]), B, nh, cfg.qk_nope,
+                                      cfg.qk_rope, R, cfg.v_head, self.max_len, self.scale,
+                                      ptr(o), torch.cuda.current_stream().cuda_stream),
+                  "sl_mla_decode")
+            return F.linear(o, lw["wo"])
         q = qkv[:, :nh * dq].view(B, nh, dq)
         kv = qkv[:, nh * dq:]
         c = _rms(kv[:, :R], lw["kv_norm"], cfg.rms_eps)

@@ -44,3 +44,37 @@ def test_captured_decode_step_replays_the_eager_step():
     assert a.stats() == b.stats()
     assert b.stats()["fills"] > 0
     assert int(b.model.pos[0]) == 20
+
+
+def test_fused_mla_decode_matches_the_pytorch_attention():
+    """sl_mla_decode (the harness's one-launch attention) against the same
+    attention in PyTorch ops, on caches filled by earlier steps: the layer's
+    output within bf16 tolerance and the written cache row equal."""
+    from sluice_b200.harness import DecoderHarness
+
+    dcfg = replace(V2_LITE_DECODER, num_layers=2, vocab=2048)
+    h = DecoderHarness(dcfg, lambda li, x: torch.zeros_like(x), batch=3, max_len=40, seed=4,
+                       fused_attention=False)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    ids = torch.randint(0, 2048, (3,), device="cuda", generator=g)
+    for _ in range(9):                      # fill positions 0..8 with the PyTorch path
+        ids = h.step(ids)
+    h.pos[1] = 3                            # ragged: sequences at different positions
+    x = torch.randn(3, dcfg.hidden, device="cuda", generator=g).to(torch.bfloat16)
+    freqs = h.freqs[h.pos]
+    mask = torch.zeros(3, 1, h.max_len, dtype=torch.bfloat16, device="cuda")
+    mask.masked_fill_((h._ar[None, :] > h.pos[:, None])[:, None, :], float("-inf"))
+    for li in range(dcfg.num_layers):
+        before = h.cache[li].clone()
+        h.fused_attention = False
+        ref = h._attention(li, x, mask, freqs)
+        ref_cache = h.cache[li].clone()
+        h.cache[li].copy_(before)
+        h.fused_attention = True
+        got = h._attention(li, x, mask, freqs)
+        torch.cuda.synchronize()
+        err = (got.float() - ref.float()).abs().max().item()
+        assert err <= 2e-2 * ref.float().abs().max().item() + 1e-3, (li, err)
+        rows = torch.arange(3, device="cuda")
+        new, old = h.cache[li][rows, h.pos].float(), ref_cache[rows, h.pos].float()
+        assert (new - old).abs().max().item() <= 1e-2 * old.abs().max().item(), li
