@@ -5,21 +5,30 @@
 // embedding, cache write, the absorbed query, scores, softmax, the weighted
 // latent sum and the value map) with one launch.
 //
-// One CTA per (head, sequence). Inputs per sequence: the fused projection row
-// [q (heads x (nope + rope)) | c_kv (rank) | k_pe (rope)] of this step, its
-// position P; the latent cache [B, max_len, rank + rope]. The CTA:
+// One CTA per (head, sequence), eight warps. Inputs per sequence: the fused
+// projection row [q (heads x (nope + rope)) | c_kv (rank) | k_pe (rope)] of
+// this step, its position P; the latent cache [B, max_len, rank + rope]. The
+// CTA:
 //   1. normalises c_kv (RMSNorm, fp32, one bf16 rounding) and rotates k_pe
 //      (RoPE on adjacent pairs) for position P; CTA head 0 writes them to the
 //      cache (the other heads use their own copy for position P);
 //   2. forms the absorbed query [q_nope W_uk | rope(q_pe)] (fp32 sums, bf16
 //      rounding, as the bf16 GEMM it replaces);
-//   3. scores every cached position 0..P (a warp per position), softmax;
+//   3. scores every cached position 0..P, softmax;
 //   4. sums the latents weighted by the probabilities, maps through W_uv.
+// Each lane owns 16 of the 512 latent columns (two 8-column chunks, so a
+// warp reads a whole 1 KB latent or weight row per step with 16-byte loads);
+// the warps split the rows of W_uk / W_uv and the cached positions, and every
+// loop keeps four rows' loads in flight. The rank is fixed at 512 (the
+// DeepSeek-V2 / V3 latent width); other shapes are refused by the host.
 #include "common.cuh"
 
 namespace {
 
 constexpr int kMlaThreads = 256;
+constexpr int kMlaWarps = kMlaThreads / 32;
+constexpr int kRank = 512;
+constexpr int kUnroll = 4;
 
 __device__ __forceinline__ float block_sum(float v, float* red) {
 #pragma unroll
@@ -45,21 +54,54 @@ __device__ __forceinline__ float block_max(float v, float* red) {
   return t;
 }
 
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// The lane's 16 columns of a 512-wide bf16 row: columns 8*lane.. and
+// 256 + 8*lane.., as two 16-byte loads.
+struct Row16 {
+  uint4 a, b;
+};
+__device__ __forceinline__ Row16 load_row16(const __nv_bfloat16* row, int lane) {
+  Row16 r;
+  r.a = *reinterpret_cast<const uint4*>(row + 8 * lane);
+  r.b = *reinterpret_cast<const uint4*>(row + 256 + 8 * lane);
+  return r;
+}
+__device__ __forceinline__ void unpack16(const Row16& r, float (&v)[16]) {
+  const __nv_bfloat162* a = reinterpret_cast<const __nv_bfloat162*>(&r.a);
+  const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&r.b);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 fa = __bfloat1622float2(a[i]), fb = __bfloat1622float2(b[i]);
+    v[2 * i] = fa.x;
+    v[2 * i + 1] = fa.y;
+    v[8 + 2 * i] = fb.x;
+    v[8 + 2 * i + 1] = fb.y;
+  }
+}
+__device__ __forceinline__ int col16(int lane, int i) {
+  return i < 8 ? 8 * lane + i : 256 + 8 * lane + (i - 8);
+}
+
 __global__ void __launch_bounds__(kMlaThreads) mla_decode_kernel(
     const __nv_bfloat16* __restrict__ qkv, int ld_qkv, const __nv_bfloat16* __restrict__ kv_norm,
     float eps, const __nv_bfloat16* __restrict__ w_uk, const __nv_bfloat16* __restrict__ w_uv,
     const float2* __restrict__ rope_cs, const int64_t* __restrict__ pos,
-    __nv_bfloat16* __restrict__ cache, int nh, int nope, int rope, int rank, int vdim,
-    int max_len, float scale, __nv_bfloat16* __restrict__ out) {
+    __nv_bfloat16* __restrict__ cache, int nh, int nope, int rope, int vdim, int max_len,
+    float scale, __nv_bfloat16* __restrict__ out) {
   extern __shared__ float sm[];
   const int h = blockIdx.x, b = blockIdx.y;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
-  const int dk = rank + rope;
-  float* q = sm;            // [dk] absorbed query
-  float* kv = q + dk;       // [dk] this position's latent | rotated k_pe
-  float* p = kv + dk;       // [max_len] scores, then probabilities
-  float* ol = p + max_len;  // [rank] probability-weighted latent
-  float* red = ol + rank;   // [32]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int dk = kRank + rope;
+  float* q = sm;                     // [dk] absorbed query
+  float* kv = q + dk;                // [dk] this position's latent | rotated k_pe
+  float* p = kv + dk;                // [max_len] scores, then probabilities
+  float* part = p + max_len;         // [warps][rank] per-warp partial sums
+  float* red = part + kMlaWarps * kRank;  // [32]
   sl::pdl_wait();
   sl::pdl_trigger();
   int P = static_cast<int>(pos[b]);
@@ -71,51 +113,111 @@ __global__ void __launch_bounds__(kMlaThreads) mla_decode_kernel(
 
   // 1. RMSNorm of c_kv and the rotated k_pe for position P
   float ss = 0.f;
-  for (int i = tid; i < rank; i += blockDim.x) {
+  for (int i = tid; i < kRank; i += blockDim.x) {
     const float v = __bfloat162float(ckv[i]);
     kv[i] = v;
     ss += v * v;
   }
-  const float r = rsqrtf(block_sum(ss, red) / rank + eps);
-  for (int i = tid; i < rank; i += blockDim.x)
+  const float r = rsqrtf(block_sum(ss, red) / kRank + eps);
+  for (int i = tid; i < kRank; i += blockDim.x)
     kv[i] = sl::bf16_round(kv[i] * r * __bfloat162float(kv_norm[i]));
   for (int j = tid; j < rope / 2; j += blockDim.x) {
-    const float x0 = __bfloat162float(ckv[rank + 2 * j]), x1 = __bfloat162float(ckv[rank + 2 * j + 1]);
+    const float x0 = __bfloat162float(ckv[kRank + 2 * j]);
+    const float x1 = __bfloat162float(ckv[kRank + 2 * j + 1]);
     const float2 c = cs[j];
-    kv[rank + 2 * j] = sl::bf16_round(x0 * c.x - x1 * c.y);
-    kv[rank + 2 * j + 1] = sl::bf16_round(x1 * c.x + x0 * c.y);
+    kv[kRank + 2 * j] = sl::bf16_round(x0 * c.x - x1 * c.y);
+    kv[kRank + 2 * j + 1] = sl::bf16_round(x1 * c.x + x0 * c.y);
     const float y0 = __bfloat162float(qh[nope + 2 * j]), y1 = __bfloat162float(qh[nope + 2 * j + 1]);
-    q[rank + 2 * j] = sl::bf16_round(y0 * c.x - y1 * c.y);
-    q[rank + 2 * j + 1] = sl::bf16_round(y1 * c.x + y0 * c.y);
+    q[kRank + 2 * j] = sl::bf16_round(y0 * c.x - y1 * c.y);
+    q[kRank + 2 * j + 1] = sl::bf16_round(y1 * c.x + y0 * c.y);
+  }
+  // 2. absorbed query: q_lat[c] = sum_d q_nope[d] W_uk[h][d][c]; warp w sums
+  // the rows d = w, w + 8, ...
+  {
+    const __nv_bfloat16* wk = w_uk + static_cast<size_t>(h) * nope * kRank;
+    float acc[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+    for (int d0 = warp; d0 < nope; d0 += kMlaWarps * kUnroll) {
+      Row16 rr[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int d = d0 + u * kMlaWarps;
+        if (d < nope) rr[u] = load_row16(wk + static_cast<size_t>(d) * kRank, lane);
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int d = d0 + u * kMlaWarps;
+        if (d < nope) {
+          const float qd = __bfloat162float(qh[d]);
+          float v[16];
+          unpack16(rr[u], v);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) acc[i] = fmaf(qd, v[i], acc[i]);
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) part[warp * kRank + col16(lane, i)] = acc[i];
   }
   __syncthreads();
+  for (int c = tid; c < kRank; c += blockDim.x) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < kMlaWarps; ++w) t += part[w * kRank + c];
+    q[c] = sl::bf16_round(t);
+  }
   if (h == 0) {
     __nv_bfloat16* dst = cache + (static_cast<size_t>(b) * max_len + P) * dk;
     for (int i = tid; i < dk; i += blockDim.x) dst[i] = __float2bfloat16(kv[i]);
   }
-  // 2. absorbed query: q_lat[c] = sum_d q_nope[d] W_uk[h][d][c]
-  const __nv_bfloat16* wk = w_uk + static_cast<size_t>(h) * nope * rank;
-  for (int c = tid; c < rank; c += blockDim.x) {
-    float acc = 0.f;
-    for (int d = 0; d < nope; ++d)
-      acc = fmaf(__bfloat162float(qh[d]), __bfloat162float(wk[static_cast<size_t>(d) * rank + c]),
-                 acc);
-    q[c] = sl::bf16_round(acc);
-  }
   __syncthreads();
-  // 3. scores over positions 0..P (a warp per position), softmax
+  // 3. scores over positions 0..P: warp w takes l = w, w + 8, ... (position
+  // P from this CTA's own copy of the new cache row)
   const __nv_bfloat16* cb = cache + static_cast<size_t>(b) * max_len * dk;
-  for (int l = warp; l <= P; l += nw) {
-    float acc = 0.f;
-    if (l == P) {
-      for (int i = lane; i < dk; i += 32) acc = fmaf(q[i], kv[i], acc);
-    } else {
-      const __nv_bfloat16* key = cb + static_cast<size_t>(l) * dk;
-      for (int i = lane; i < dk; i += 32) acc = fmaf(q[i], __bfloat162float(key[i]), acc);
-    }
+  {
+    float qr[16];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) p[l] = acc * scale;
+    for (int i = 0; i < 16; ++i) qr[i] = q[col16(lane, i)];
+    const int rp = rope / 32;  // rope columns per lane (rope <= 64)
+    float qp0 = rp > 0 ? q[kRank + lane * rp] : 0.f;
+    float qp1 = rp > 1 ? q[kRank + lane * rp + 1] : 0.f;
+    for (int l0 = warp; l0 <= P; l0 += kMlaWarps * kUnroll) {
+      Row16 rr[kUnroll];
+      float kp[kUnroll][2];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int l = l0 + u * kMlaWarps;
+        kp[u][0] = kp[u][1] = 0.f;
+        if (l < P) {
+          const __nv_bfloat16* key = cb + static_cast<size_t>(l) * dk;
+          rr[u] = load_row16(key, lane);
+          if (rp > 0) kp[u][0] = __bfloat162float(key[kRank + lane * rp]);
+          if (rp > 1) kp[u][1] = __bfloat162float(key[kRank + lane * rp + 1]);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int l = l0 + u * kMlaWarps;
+        if (l > P) continue;  // the same for the whole warp
+        float acc = 0.f;
+        if (l == P) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) acc = fmaf(qr[i], kv[col16(lane, i)], acc);
+          if (rp > 0) acc = fmaf(qp0, kv[kRank + lane * rp], acc);
+          if (rp > 1) acc = fmaf(qp1, kv[kRank + lane * rp + 1], acc);
+        } else {
+          float v[16];
+          unpack16(rr[u], v);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) acc = fmaf(qr[i], v[i], acc);
+          acc = fmaf(qp0, kp[u][0], acc);
+          acc = fmaf(qp1, kp[u][1], acc);
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) p[l] = acc * scale;
+      }
+    }
   }
   __syncthreads();
   float m = -INFINITY;
@@ -128,23 +230,71 @@ __global__ void __launch_bounds__(kMlaThreads) mla_decode_kernel(
     se += e;
   }
   const float inv = 1.f / block_sum(se, red);
-  // 4. probability-weighted latent, then the value map
-  for (int c = tid; c < rank; c += blockDim.x) {
-    float acc = 0.f;
-    for (int l = 0; l < P; ++l)
-      acc = fmaf(p[l], __bfloat162float(cb[static_cast<size_t>(l) * dk + c]), acc);
-    acc = fmaf(p[P], kv[c], acc);
-    ol[c] = sl::bf16_round(acc * inv);
+  // 4. probability-weighted latent (warp w: positions w, w + 8, ... < P),
+  // then the value map (warp w: rows d = w, w + 8, ...)
+  {
+    float acc[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+    for (int l0 = warp; l0 < P; l0 += kMlaWarps * kUnroll) {
+      Row16 rr[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int l = l0 + u * kMlaWarps;
+        if (l < P) rr[u] = load_row16(cb + static_cast<size_t>(l) * dk, lane);
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int l = l0 + u * kMlaWarps;
+        if (l < P) {
+          const float pl = p[l];
+          float v[16];
+          unpack16(rr[u], v);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) acc[i] = fmaf(pl, v[i], acc[i]);
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) part[warp * kRank + col16(lane, i)] = acc[i];
   }
   __syncthreads();
-  const __nv_bfloat16* wv = w_uv + static_cast<size_t>(h) * vdim * rank;
-  for (int d = warp; d < vdim; d += nw) {
-    float acc = 0.f;
-    for (int c = lane; c < rank; c += 32)
-      acc = fmaf(ol[c], __bfloat162float(wv[static_cast<size_t>(d) * rank + c]), acc);
+  float* ol = q;  // the query is no longer needed: [rank] weighted latent
+  for (int c = tid; c < kRank; c += blockDim.x) {
+    float t = 0.f;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) out[static_cast<size_t>(b) * nh * vdim + h * vdim + d] = __float2bfloat16(acc);
+    for (int w = 0; w < kMlaWarps; ++w) t += part[w * kRank + c];
+    t = fmaf(p[P], kv[c], t);
+    ol[c] = sl::bf16_round(t * inv);
+  }
+  __syncthreads();
+  {
+    float o16[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) o16[i] = ol[col16(lane, i)];
+    const __nv_bfloat16* wv = w_uv + static_cast<size_t>(h) * vdim * kRank;
+    __nv_bfloat16* dst = out + static_cast<size_t>(b) * nh * vdim + h * vdim;
+    for (int d0 = warp; d0 < vdim; d0 += kMlaWarps * kUnroll) {
+      Row16 rr[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int d = d0 + u * kMlaWarps;
+        if (d < vdim) rr[u] = load_row16(wv + static_cast<size_t>(d) * kRank, lane);
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int d = d0 + u * kMlaWarps;
+        if (d < vdim) {
+          float v[16];
+          unpack16(rr[u], v);
+          float acc = 0.f;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) acc = fmaf(o16[i], v[i], acc);
+          acc = warp_sum(acc);
+          if (lane == 0) dst[d] = __float2bfloat16(acc);
+        }
+      }
+    }
   }
 }
 
@@ -158,10 +308,18 @@ extern "C" int sl_mla_decode(const void* qkv, int ld_qkv, const void* kv_norm, f
   if (B < 0 || nh <= 0 || nope <= 0 || rope <= 0 || rope % 2 || rank <= 0 || vdim <= 0 ||
       max_len <= 0 || ld_qkv < nh * (nope + rope) + rank + rope)
     return SL_ERR_INVALID;
+  // the kernel's lane layout: a 512-wide latent, 16-byte aligned rows, at
+  // most two rope columns per lane
+  if (rank != kRank || rope > 64 || rope % 32 || nope % 8 || ld_qkv % 8)
+    return SL_ERR_UNSUPPORTED;
   if (B == 0) return SL_OK;
   if (!qkv || !kv_norm || !w_uk || !w_uv || !rope_cos_sin || !pos || !cache || !out)
     return SL_ERR_INVALID;
-  const size_t smem = sizeof(float) * (2 * static_cast<size_t>(rank + rope) + max_len + rank + 32);
+  if ((reinterpret_cast<uintptr_t>(w_uk) | reinterpret_cast<uintptr_t>(w_uv) |
+       reinterpret_cast<uintptr_t>(cache)) & 15)
+    return SL_ERR_INVALID;
+  const size_t smem =
+      sizeof(float) * (2 * static_cast<size_t>(rank + rope) + max_len + kMlaWarps * kRank + 32);
   if (smem > 200 * 1024 || B > 65535) return SL_ERR_UNSUPPORTED;
   static std::atomic<uint64_t> smem_set{0};
   if (smem > 48 * 1024) SL_CUDA_TRY(sl::ensure_smem_limit(mla_decode_kernel, static_cast<int>(smem), smem_set));
@@ -172,7 +330,7 @@ extern "C" int sl_mla_decode(const void* qkv, int ld_qkv, const void* kv_norm, f
                          static_cast<const __nv_bfloat16*>(w_uk),
                          static_cast<const __nv_bfloat16*>(w_uv),
                          reinterpret_cast<const float2*>(rope_cos_sin), pos,
-                         static_cast<__nv_bfloat16*>(cache), nh, nope, rope, rank, vdim, max_len,
-                         scale, static_cast<__nv_bfloat16*>(out)));
+                         static_cast<__nv_bfloat16*>(cache), nh, nope, rope, vdim, max_len, scale,
+                         static_cast<__nv_bfloat16*>(out)));
   return SL_OK;
 }

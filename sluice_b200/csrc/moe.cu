@@ -47,7 +47,7 @@ enum {
 };
 
 struct WsLayout {
-  size_t items, pair_pos, x, act, z, total;
+  size_t items, pair_pos, x, act, z, gu, total;
   int max_items, max_rows;
 };
 
@@ -56,19 +56,23 @@ __host__ __device__ inline size_t r256(size_t v) { return (v + 255) & ~size_t(25
 // Token-tile width from the average tokens per used slot: decode steps (a few
 // tokens per expert) use 16, prefill-sized steps 64 or 128 so each weight
 // tile is reused across more tokens.
-// fp8 stops at 64: its gate/up accumulators (128 token columns x gate and up)
-// would not fit the promotion warps' registers. fp8 keeps 16-token tiles up
-// to 32 tokens per expert on average: a 64-token tile would promote (and
-// multiply) four times the columns it uses, while a second 16-token item of
-// the same expert re-reads its weights mostly from L2.
+// fp8 keeps 16-token tiles up to 32 tokens per expert on average: a 64-token
+// tile would promote (and multiply) four times the columns it uses, while a
+// second 16-token item of the same expert re-reads its weights mostly from
+// L2. From kF8WideMinAvg tokens per expert on it runs the wide-tile GEMMs
+// (items of up to 192 tokens, gate/up as one GEMM over the 2I rows).
+constexpr int kF8WideBN = 192;
+constexpr long kF8WideMinAvg = 64;
 inline int choose_bn(int T, int topk, int S, bool fp8 = false) {
   const long P = static_cast<long>(T) * topk;
   const long used = P < S ? P : S;
   const long avg = used > 0 ? (P + used - 1) / used : 1;
-  if (fp8) return avg <= 32 ? 16 : 64;
+  if (fp8) return avg <= 32 ? 16 : avg < kF8WideMinAvg ? 64 : kF8WideBN;
   return avg <= 16 ? 16 : avg <= 64 ? 64 : 128;
 }
 
+// The wide fp8 path (BN = kF8WideBN) adds a bf16 buffer for the gate/up
+// output rows [max_rows, 2I] ahead of the SwiGLU quantisation.
 inline WsLayout ws_layout(int T, int topk, int H, int I, int S, int n_sh, int BN) {
   WsLayout w;
   const long P = static_cast<long>(T) * topk;
@@ -82,6 +86,8 @@ inline WsLayout ws_layout(int T, int topk, int H, int I, int S, int n_sh, int BN
   w.x = o; o += r256(sizeof(__nv_bfloat16) * size_t(w.max_rows) * H);
   w.act = o; o += r256(sizeof(__nv_bfloat16) * size_t(w.max_rows) * I);
   w.z = o; o += r256(sizeof(__nv_bfloat16) * size_t(w.max_rows) * H);
+  w.gu = o;
+  if (BN == kF8WideBN) o += r256(sizeof(__nv_bfloat16) * size_t(w.max_rows) * 2 * I);
   w.total = o;
   return w;
 }
@@ -1251,6 +1257,314 @@ __global__ void __launch_bounds__(F8Cfg<BN, GATED>::kThreads, 1) moe_gemm_f8_ker
 }
 
 
+// ------------------------------------------- fp8 GEMM, wide token tiles
+// Steps with many tokens per expert (prefill-sized) use items of up to 192
+// tokens: the MMA is M=128 weight rows x N=round16(item tokens) x K=32, so
+// each weight tile staged in shared memory feeds up to three times the
+// multiply-adds of a 64-token tile and the per-K-block promotion work per
+// multiply-add is amortised over 64 columns per warp. Gate/up is one plain
+// GEMM over the 2I rows of w13 (bf16 g and u rows written to a buffer, then
+// swiglu_quant_kernel applies vLLM's SiLU-and-mul chain and quantises per
+// 128-column group), so a tile keeps one accumulator per (row, token).
+// Roles: warp 0 TMA producer, warp 1 MMA issuer + TMEM owner, warps 2..13
+// promotion: four lane quadrants x three groups of 64 token columns; a warp
+// whose columns hold no token of the item only releases the buffers. 14
+// warps keep four per SM sub-partition, so a thread may hold 128 registers
+// (64 fp32 accumulators plus one 16-column TMEM load).
+// The token tile is loaded as 32-row boxes, only those that hold tokens.
+constexpr int F8W_BN = 192;
+static_assert(F8W_BN == kF8WideBN, "wide fp8 token tile");
+constexpr int F8W_CW = 64;                             // token columns per promotion warp
+constexpr int F8W_NP = 4 * (F8W_BN / F8W_CW);
+constexpr int F8W_THREADS = 64 + 32 * F8W_NP;
+constexpr int F8W_ABYTES = 128 * F8_BK;                // one 128x128 e4m3 weight tile
+constexpr int F8W_BBYTES = F8W_BN * F8_BK;             // up to 192 token rows
+constexpr int F8W_STAGE = F8W_ABYTES + F8W_BBYTES;     // multiple of 1024
+constexpr int F8W_STAGES = 5;
+constexpr int F8W_NB = 2;                              // TMEM accumulator buffers
+constexpr int F8W_TSTRIDE = 256;                       // TMEM columns per buffer
+constexpr int F8W_SMEM = 1024 /*align*/ + F8W_STAGES * (F8W_STAGE + F8W_BN * 4) +
+                         512 /*barriers*/;
+
+__global__ void __launch_bounds__(F8W_THREADS, 1) moe_gemm_f8w_kernel(
+    const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_wsh,
+    const __grid_constant__ CUtensorMap tm_b, const float* __restrict__ b_scale,
+    const float* __restrict__ w_scale, const float* __restrict__ wsh_scale,
+    const int32_t* __restrict__ ws_hdr, const int4* __restrict__ items,
+    __nv_bfloat16* __restrict__ out, int S, int K, int M_total, int max_rows,
+    int32_t* __restrict__ status, int phase) {
+  constexpr int ST = F8W_STAGES;
+  constexpr int NB = F8W_NB;
+  constexpr int CW = F8W_CW;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sAB = smem;                                                 // [ST][A | B]
+  float* sS = reinterpret_cast<float*>(sAB + ST * F8W_STAGE);          // [ST][BN]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sS + ST * F8W_BN);
+  uint64_t* empty = full + ST;
+  uint64_t* tfull = empty + ST;
+  uint64_t* tempty = tfull + NB;
+  uint64_t* mma_done = tempty + NB;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // both wide GEMMs read what the kernel just before them wrote (the
+  // quantised token rows, the quantised SwiGLU rows)
+  sl::pdl_wait();
+  sl::pdl_trigger();
+  const int m_tiles = M_total / 128;
+  const int num_items = ws_hdr[WS_NUM_ITEMS];
+  const int n_hit = ws_hdr[WS_NUM_HIT_ITEMS];
+  const int item_lo = phase == 1 ? n_hit : 0;
+  const int item_hi = phase == 0 ? n_hit : num_items;
+  const int num_tiles = (item_hi > item_lo ? item_hi - item_lo : 0) * m_tiles;
+  const int k_blocks = K / F8_BK;
+  const int kscale = K / 128;
+  if (static_cast<int>(blockIdx.x) >= num_tiles) return;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < ST; ++s) {
+      sl::mbar_init(&full[s], 1);
+      sl::mbar_init(&empty[s], 1 + F8W_NP);  // the MMAs' commit + every promotion warp
+    }
+    for (int b = 0; b < NB; ++b) {
+      sl::mbar_init(&tfull[b], 1);
+      sl::mbar_init(&tempty[b], F8W_NP);
+    }
+    sl::mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    sl::fence_barrier_init();
+    sl::tma_prefetch_desc(&tm_w);
+    sl::tma_prefetch_desc(&tm_wsh);
+    sl::tma_prefetch_desc(&tm_b);
+  }
+  if (warp == 1) sl::tmem_alloc(tmem_slot, NB * F8W_TSTRIDE);
+  sl::tc_fence_before();
+  __syncthreads();
+  sl::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------ TMA producer
+    if (sl::elect_one()) {
+      int s = 0;
+      uint32_t ph = 0;
+      uint32_t issued_mask = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int4 it = items[item_lo + tile / m_tiles];
+        const int mt = tile % m_tiles;
+        const bool sh = it.x >= S;
+        const CUtensorMap* tw = sh ? &tm_wsh : &tm_w;
+        const int e = sh ? it.x - S : it.x;
+        const int row0 = e * M_total + mt * 128;  // weight rows in the view [experts * rows, K]
+        const int nb32 = (it.z + 31) >> 5;        // 32-row boxes holding tokens
+        const uint32_t tx = F8W_ABYTES + nb32 * (32 * F8_BK + 32 * 4);
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (*abort_flag || !sl::mbar_wait(&empty[s], ph ^ 1)) {
+            ok = false;
+            break;
+          }
+          sl::mbar_arrive_expect_tx(&full[s], tx);
+          uint8_t* a0 = sAB + s * F8W_STAGE;
+          sl::tma_load_2d_nohint(a0, tw, &full[s], kb * F8_BK, row0);
+          for (int j = 0; j < nb32; ++j)
+            sl::tma_load_2d_nohint(a0 + F8W_ABYTES + j * 32 * F8_BK, &tm_b, &full[s], kb * F8_BK,
+                                   it.y + 32 * j);
+          sl::bulk_load(sS + s * F8W_BN, b_scale + static_cast<size_t>(kb) * max_rows + it.y,
+                        nb32 * 32 * 4, &full[s]);
+          issued_mask = (issued_mask & ~(1u << s)) | (ph << s);
+          if (++s == ST) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        atomicExch(status, SL_ERR_TIMEOUT);
+        *abort_flag = 1;
+        for (int i = 0; i < ST; ++i) (void)sl::mbar_wait(&full[i], (issued_mask >> i) & 1u);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------- MMA issuer
+    if (sl::elect_one()) {
+      int s = 0, b = 0;
+      uint32_t ph = 0, bph = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int n = items[item_lo + tile / m_tiles].z;
+        const uint32_t idesc = sl::umma_idesc_e4m3(128, (n + 15) & ~15);
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (*abort_flag || !sl::mbar_wait(&tempty[b], bph ^ 1) ||
+              !sl::mbar_wait(&full[s], ph)) {
+            ok = false;
+            break;
+          }
+          sl::tc_fence_after();
+          const uint32_t d0 = tmem_base + b * F8W_TSTRIDE;
+          const uint32_t a_addr = sl::smem_u32(sAB + s * F8W_STAGE);
+          const uint32_t b_addr = a_addr + F8W_ABYTES;
+#pragma unroll
+          for (int k = 0; k < F8_BK / 32; ++k)
+            sl::umma_e4m3(d0, sl::umma_desc_sw128(a_addr + k * 32),
+                          sl::umma_desc_sw128(b_addr + k * 32), idesc, k != 0);
+          sl::umma_commit(&empty[s]);
+          sl::umma_commit(&tfull[b]);
+          if (++s == ST) {
+            s = 0;
+            ph ^= 1;
+          }
+          if (++b == NB) {
+            b = 0;
+            bph ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        atomicExch(status, SL_ERR_TIMEOUT);
+        *abort_flag = 1;
+      }
+      sl::umma_commit(mma_done);
+      (void)sl::mbar_wait(mma_done, 0);
+    }
+  } else {
+    // ------------------------------------------- promotion and epilogue
+    const int q = warp & 3;               // TMEM lane quadrant of this warp
+    const int c0 = ((warp - 2) >> 2) * CW;  // first token column of this warp
+    const int row = q * 32 + lane;        // weight row within the 128-row tile
+    int s = 0, b = 0;
+    uint32_t ph = 0, bph = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      const int4 it = items[item_lo + tile / m_tiles];
+      const int mt = tile % m_tiles;
+      const bool sh = it.x >= S;
+      const int e = sh ? it.x - S : it.x;
+      const float* sc = (sh ? wsh_scale : w_scale) +
+                        (static_cast<size_t>(e) * m_tiles + mt) * kscale;
+      const int ncol = it.z - c0;  // token columns of this warp (<= 0: none)
+      float2 acc[CW / 2];
+#pragma unroll
+      for (int i = 0; i < CW / 2; ++i) acc[i] = make_float2(0.f, 0.f);
+      for (int kb = 0; kb < k_blocks; ++kb) {
+        const float wsk = __ldg(sc + kb);  // weight block scale of this K block
+        ok = ok && !*abort_flag && sl::mbar_wait(&tfull[b], bph) && sl::mbar_wait(&full[s], ph);
+        if (ok && ncol > 0) {
+          sl::tc_fence_after();
+          const uint32_t taddr = tmem_base + b * F8W_TSTRIDE +
+                                 (static_cast<uint32_t>(q * 32) << 16) + c0;
+          const float* ts = sS + s * F8W_BN + c0;
+#pragma unroll
+          for (int cc = 0; cc < CW; cc += 16) {
+            if (cc < ncol) {
+              uint32_t v[16];
+              sl::tmem_ld16_nowait(taddr + cc, v);
+              sl::tmem_wait_ld(v);
+              // acc += v x (weight block scale x token group scale), per column
+#pragma unroll
+              for (int i = 0; i < 8; i += 2) {
+                const float4 t4 = *reinterpret_cast<const float4*>(ts + cc + 2 * i);
+                const float2 c01 = __fmul2_rn(make_float2(wsk, wsk), make_float2(t4.x, t4.y));
+                const float2 c23 = __fmul2_rn(make_float2(wsk, wsk), make_float2(t4.z, t4.w));
+                acc[cc / 2 + i] = __ffma2_rn(
+                    make_float2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])), c01,
+                    acc[cc / 2 + i]);
+                acc[cc / 2 + i + 1] = __ffma2_rn(
+                    make_float2(__uint_as_float(v[2 * i + 2]), __uint_as_float(v[2 * i + 3])),
+                    c23, acc[cc / 2 + i + 1]);
+              }
+            }
+          }
+          sl::tc_fence_before();
+        }
+        __syncwarp();
+        if (ok && lane == 0) {
+          sl::mbar_arrive(&tempty[b]);
+          sl::mbar_arrive(&empty[s]);
+        }
+        if (++s == ST) {
+          s = 0;
+          ph ^= 1;
+        }
+        if (++b == NB) {
+          b = 0;
+          bph ^= 1;
+        }
+      }
+      if (!ok) {
+        atomicExch(status, SL_ERR_TIMEOUT);
+        *abort_flag = 1;
+      }
+      if (ok && ncol > 0) {
+        __nv_bfloat16* dst = out + static_cast<size_t>(it.y + c0) * M_total + mt * 128 + row;
+#pragma unroll
+        for (int i = 0; i < CW / 2; ++i) {
+          if (2 * i < ncol) dst[static_cast<size_t>(2 * i) * M_total] = __float2bfloat16(acc[i].x);
+          if (2 * i + 1 < ncol)
+            dst[static_cast<size_t>(2 * i + 1) * M_total] = __float2bfloat16(acc[i].y);
+        }
+      }
+    }
+  }
+  sl::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    sl::tc_fence_after();
+    sl::tmem_dealloc(tmem_base, NB * F8W_TSTRIDE);
+  }
+}
+
+// vLLM's SiLU-and-mul chain on the wide gate/up output (bf16 g and u rows of
+// 2I columns), then per-token 128-column quantisation for the down GEMM: the
+// same arithmetic as the narrow gate/up epilogue. One warp per (row, group).
+__global__ void __launch_bounds__(256) swiglu_quant_kernel(
+    const int32_t* __restrict__ ws_hdr, const int4* __restrict__ items, int BN,
+    const __nv_bfloat16* __restrict__ gu, int I, uint8_t* __restrict__ Aq,
+    float* __restrict__ As, int max_rows, int phase) {
+  sl::pdl_wait();
+  sl::pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int num_items = ws_hdr[WS_NUM_ITEMS];
+  const int n_hit = ws_hdr[WS_NUM_HIT_ITEMS];
+  const int item_lo = phase == 1 ? n_hit : 0;
+  const int item_hi = phase == 0 ? n_hit : num_items;
+  const int G = I / 128;
+  const long n_units = static_cast<long>(item_hi > item_lo ? item_hi - item_lo : 0) * BN * G;
+  const long nwarps = static_cast<long>(gridDim.x) * (blockDim.x >> 5);
+  for (long u = static_cast<long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+       u < n_units; u += nwarps) {
+    const int grp = static_cast<int>(u % G);
+    const long rr = u / G;
+    const int4 it = items[item_lo + static_cast<int>(rr / BN)];
+    const int r = static_cast<int>(rr % BN);
+    if (r >= it.z) continue;  // the same for the whole warp
+    const size_t row = static_cast<size_t>(it.y) + r;
+    const uint2 graw = *reinterpret_cast<const uint2*>(gu + row * 2 * I + grp * 128 + lane * 4);
+    const uint2 uraw =
+        *reinterpret_cast<const uint2*>(gu + row * 2 * I + I + grp * 128 + lane * 4);
+    const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&graw);
+    const __nv_bfloat162* u2 = reinterpret_cast<const __nv_bfloat162*>(&uraw);
+    float a[4];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float2 g = __bfloat1622float2(g2[h]);
+      const float2 uu = __bfloat1622float2(u2[h]);
+      a[2 * h] = sl::bf16_round(sl::bf16_round(g.x / (1.0f + expf(-g.x))) * uu.x);
+      a[2 * h + 1] = sl::bf16_round(sl::bf16_round(g.y / (1.0f + expf(-g.y))) * uu.y);
+    }
+    float m = fmaxf(fmaxf(fabsf(a[0]), fabsf(a[1])), fmaxf(fabsf(a[2]), fabsf(a[3])));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float scv = group_scale(m);
+    *reinterpret_cast<uint32_t*>(Aq + row * I + grp * 128 + lane * 4) =
+        e4m3x4(q_clamp(a[0], scv), q_clamp(a[1], scv), q_clamp(a[2], scv), q_clamp(a[3], scv));
+    if (lane == 0) As[static_cast<size_t>(grp) * max_rows + row] = scv;
+  }
+}
+
 // ---------------------------------------------------------------- combine
 // OUT_F32 = false: out = bf16(shared + bf16(scale * bf16(sum_j w z)))  (vLLM
 //   torch-native rounding chain, runner tail in bf16)
@@ -1394,6 +1708,23 @@ int launch_gemm_f8(const CUtensorMap& tw, const CUtensorMap& twsh, const CUtenso
   SL_CUDA_TRY(sl::launch(kern, dim3(grid), dim3(Cfg::kThreads), Cfg::kSmemBytes, st, tw, twsh,
                          tb, bscale, wscale, wshscale, hdr, items, out_q, out_s, out_z, S, K,
                          M_total, max_rows, status, phase));
+  return SL_OK;
+}
+
+int launch_gemm_f8w(const CUtensorMap& tw, const CUtensorMap& twsh, const CUtensorMap& tb,
+                    const float* bscale, const float* wscale, const float* wshscale,
+                    const int32_t* hdr, const int4* items, __nv_bfloat16* out, int S, int K,
+                    int M_total, int max_rows, int32_t* status, int max_items, cudaStream_t st,
+                    int phase) {
+  static std::atomic<uint64_t> smem_set{0};
+  SL_CUDA_TRY(sl::ensure_smem_limit(moe_gemm_f8w_kernel, F8W_SMEM, smem_set));
+  const long max_tiles = static_cast<long>(max_items) * (M_total / 128);
+  int grid = sl_device_sm_count();
+  if (grid <= 0) return SL_ERR_CUDA;
+  if (max_tiles < grid) grid = max_tiles > 0 ? static_cast<int>(max_tiles) : 1;
+  SL_CUDA_TRY(sl::launch(moe_gemm_f8w_kernel, dim3(grid), dim3(F8W_THREADS), F8W_SMEM, st, tw,
+                         twsh, tb, bscale, wscale, wshscale, hdr, items, out, S, K, M_total,
+                         max_rows, status, phase));
   return SL_OK;
 }
 
@@ -1565,7 +1896,31 @@ int run_fused(const void* hidden, int T, int H, int I, const sl_expert_weights& 
     rc = launch_gemm_f8<BNV, false>(m_w2, m_w2sh, m_a, As, w.w2_scale, w.shared_w2_scale, hdr,   \
                                     items, nullptr, nullptr, Z, num_slots, I, H, L.max_rows,    \
                                     hdr, L.max_items, st, phase);
-  if (fp8) {
+  if (fp8 && BN == kF8WideBN) {
+    // gate/up over the 2I rows into bf16 g | u rows, SwiGLU + quantisation,
+    // then down; the token tiles are read in 32-row boxes
+    CUtensorMap m_xw, m_aw;
+    if (!make_map(&m_xw, Xq, H, uint64_t(L.max_rows), 32, true) ||
+        !make_map(&m_aw, Aq, I, uint64_t(L.max_rows), 32, true))
+      return SL_ERR_INVALID;
+    __nv_bfloat16* GU = reinterpret_cast<__nv_bfloat16*>(ws + L.gu);
+    rc = launch_gemm_f8w(m_w13, m_w13sh, m_xw, Xs, w.w13_scale, w.shared_w13_scale, hdr, items,
+                         GU, num_slots, H, 2 * I, L.max_rows, hdr, L.max_items, st, phase);
+    if (rc == SL_OK) {
+      const long units = static_cast<long>(L.max_items) * BN * (I / 128);
+      long ctas = (units + 7) / 8;
+      const long cap = 8L * sl_device_sm_count();
+      if (ctas > cap) ctas = cap;
+      if (ctas < 1) ctas = 1;
+      SL_CUDA_TRY(sl::launch(swiglu_quant_kernel, dim3(static_cast<unsigned>(ctas)), dim3(256),
+                             0, st, static_cast<const int32_t*>(hdr),
+                             static_cast<const int4*>(items), BN,
+                             static_cast<const __nv_bfloat16*>(GU), I, Aq, As, L.max_rows,
+                             phase));
+      rc = launch_gemm_f8w(m_w2, m_w2sh, m_aw, As, w.w2_scale, w.shared_w2_scale, hdr, items, Z,
+                           num_slots, I, H, L.max_rows, hdr, L.max_items, st, phase);
+    }
+  } else if (fp8) {
     if (BN == 16) {
       SL_GEMMS_F8(16)
     } else {

@@ -130,6 +130,8 @@ def test_torch_op_registration():
     (8, 512, 256, 8, 16, 4, 1, 1.0),
     (8, 7168, 2048, 16, 256, 8, 1, 2.5),    # DeepSeek-V3 expert shape, decode
     (33, 1024, 512, 6, 12, 3, 0, 1.0),      # several items per expert
+    (400, 1024, 512, 8, 8, 2, 1, 2.5),      # ~100 tokens per expert: wide token tiles
+    (1000, 512, 256, 6, 6, 2, 0, 1.0),      # 333 per expert: two wide items each
 ])
 def test_fp8_block_scaled_cases(T, H, I, S, E, k, n_sh, scale):
     """fp8 e4m3 weights with 128x128 block scales: within 5e-2 of the oracle's
@@ -206,3 +208,52 @@ def test_empty_step_and_oversized_slot_count():
     with pytest.raises(_lib.SluiceError) as ei:
         ops.fused_experts(hs, w13b, w2b, tw, ti, global_num_experts=S)
     assert ei.value.status == _lib.SL_ERR_UNSUPPORTED
+
+
+def test_fp8_wide_tiles_split_around_the_stream():
+    """The wide-tile fp8 GEMMs (a prefill-sized step: ~100 tokens per expert)
+    split around the gap's expert stream: phase 0 over the resident experts
+    while the misses stream, phase 1 over the streamed ones and the combine,
+    against the oracle; then the whole call again on the now-resident experts,
+    bit-equal to the split one."""
+    from sluice_b200 import synth
+    from sluice_b200.offloader import ExpertStreamOffloader
+    T, H, I, E, S, k = 320, 1024, 512, 16, 8, 2
+    g = torch.Generator().manual_seed(5)
+    w13 = (torch.randn(E, 2 * I, H, generator=g) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn(E, H, I, generator=g) * 0.02).to(torch.bfloat16)
+    q13, s13 = synth.quantize_block_fp8(w13)
+    q2, s2 = synth.quantize_block_fp8(w2)
+    hs = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    # every token picks 2 distinct experts among 6: 3 pinned (resident), 3 streamed
+    choice = torch.stack([torch.randperm(6, generator=g)[:k] for _ in range(T)])
+    pool = torch.tensor([0, 1, 2, 9, 11, 14])
+    ti = pool[choice].to(torch.int32)
+    tw = torch.rand(T, k, generator=g)
+    tw = (tw / tw.sum(1, keepdim=True)).float()
+    off = ExpertStreamOffloader(S, protect_frac=0.5, fast_hit=True)
+    cache = off.install_layer(q13, q2, pins=[0, 1, 2], prefill_resident=False, device="cuda",
+                              w13_scale=s13, w2_scale=s2)
+    x, tic, twc = hs.cuda(), ti.cuda(), tw.cuda()
+    ws = ops.fused_experts_workspace(T, k, H, I, S, 0, torch.device("cuda"))
+    out = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+    kw = dict(w1_scale=cache.w13_scale, w2_scale=cache.w2_scale)
+    main, side = torch.cuda.current_stream(), torch.cuda.Stream()
+    cache.plan(tic)
+    side.wait_stream(main)
+    with torch.cuda.stream(side):
+        cache.stream()
+    args = (x, cache.w13, cache.w2, twc, tic, cache.expert_map, cache.state)
+    ops.fused_experts_phase(*args, 0, ws, out, **kw)
+    main.wait_stream(side)
+    ops.fused_experts_phase(*args, 1, ws, out, **kw)
+    torch.cuda.synchronize()
+    cache.check()
+    assert ops.workspace_status(ws) == 0
+    assert int((cache.expert_map >= 0).sum()) == 6
+    ref = omoe.fused_experts(hs, q13, q2, tw, ti, None, s13, s2)
+    assert_moe_close(out, ref, rtol=5e-2)
+    whole = ops.fused_experts(x, cache.w13, cache.w2, twc, tic, expert_map=cache.expert_map,
+                              **kw)
+    torch.cuda.synchronize()
+    assert torch.equal(whole, out)
