@@ -71,9 +71,10 @@ inline int choose_bn(int T, int topk, int S, bool fp8 = false) {
   return avg <= 16 ? 16 : avg <= 64 ? 64 : 128;
 }
 
-// The wide fp8 path (BN = kF8WideBN) adds a bf16 buffer for the gate/up
-// output rows [max_rows, 2I] ahead of the SwiGLU quantisation.
-inline WsLayout ws_layout(int T, int topk, int H, int I, int S, int n_sh, int BN) {
+// The wide fp8 path (`gu`) adds a bf16 buffer for the gate/up output rows
+// [max_rows, 2I] ahead of the SwiGLU quantisation.
+inline WsLayout ws_layout(int T, int topk, int H, int I, int S, int n_sh, int BN,
+                          bool gu = false) {
   WsLayout w;
   const long P = static_cast<long>(T) * topk;
   const long routed = P / BN + (P < S ? P : S);
@@ -87,7 +88,7 @@ inline WsLayout ws_layout(int T, int topk, int H, int I, int S, int n_sh, int BN
   w.act = o; o += r256(sizeof(__nv_bfloat16) * size_t(w.max_rows) * I);
   w.z = o; o += r256(sizeof(__nv_bfloat16) * size_t(w.max_rows) * H);
   w.gu = o;
-  if (BN == kF8WideBN) o += r256(sizeof(__nv_bfloat16) * size_t(w.max_rows) * 2 * I);
+  if (gu) o += r256(sizeof(__nv_bfloat16) * size_t(w.max_rows) * 2 * I);
   w.total = o;
   return w;
 }
@@ -850,56 +851,62 @@ __device__ __forceinline__ float q_clamp(float x, float scale) {
   return fminf(fmaxf(__fdiv_rn(x, scale), -kF8Max), kF8Max);
 }
 
-// Token rows for the fp8 GEMMs: row pair_pos[p] <- hidden row p / topk (and
-// the shared experts' rows <- their tokens), quantised per 128-column group:
-// Xq [max_rows, H] e4m3, Xs [H/128, max_rows] fp32. A warp takes four groups
-// of one row at a time (four independent 8-byte loads per lane in flight).
+// Token rows for the fp8 GEMMs, quantised per 128-column group once per token
+// and written to every row that token feeds: its routed pairs' rows
+// (pair_pos[t * topk + j]) and, for tokens in [sh_t0, sh_t0 + sh_nt), its
+// row of each shared expert. A warp takes four groups of one token at a time
+// (four independent 8-byte loads per lane in flight): Xq [max_rows, H] e4m3
+// codes, Xs [H/128, max_rows] fp32 scales.
 constexpr int kQuantGroups = 4;
 
 __global__ void __launch_bounds__(256) gather_quant_kernel(
-    const int32_t* __restrict__ ws_hdr, const int32_t* __restrict__ pair_pos, int P, int topk,
+    const int32_t* __restrict__ ws_hdr, const int32_t* __restrict__ pair_pos, int T, int topk,
     int n_sh, int sh_t0, int sh_nt, const __nv_bfloat16* __restrict__ hs, int H,
     uint8_t* __restrict__ Xq, float* __restrict__ Xs, int max_rows) {
   sl::pdl_wait();
   sl::pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int G = H / 128;
-  const int GU = (G + kQuantGroups - 1) / kQuantGroups;  // units per row
-  const long n_units = static_cast<long>(P + n_sh * sh_nt) * GU;
+  const int GU = (G + kQuantGroups - 1) / kQuantGroups;  // units per token
+  const long n_units = static_cast<long>(T) * GU;
   const long nwarps = static_cast<long>(gridDim.x) * (blockDim.x >> 5);
   for (long u = static_cast<long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
        u < n_units; u += nwarps) {
-    const int r = static_cast<int>(u / GU), kb0 = static_cast<int>(u % GU) * kQuantGroups;
-    int pos, tok;
-    if (r < P) {
-      pos = pair_pos[r];
-      tok = r / topk;
-    } else {
-      const int rr = r - P, i = rr / sh_nt, t = rr % sh_nt;
-      pos = ws_hdr[WS_SH_BASE + i] + t;
-      tok = sh_t0 + t;
-    }
-    if (pos < 0) continue;  // the same for the whole warp
+    const int tok = static_cast<int>(u / GU), kb0 = static_cast<int>(u % GU) * kQuantGroups;
     uint2 raw[kQuantGroups];
 #pragma unroll
     for (int g = 0; g < kQuantGroups; ++g)
       if (kb0 + g < G)
         raw[g] = *reinterpret_cast<const uint2*>(hs + static_cast<size_t>(tok) * H +
                                                  (kb0 + g) * 128 + lane * 4);
+    uint32_t code[kQuantGroups];
+    float scl[kQuantGroups];
 #pragma unroll
     for (int g = 0; g < kQuantGroups; ++g) {
-      const int kb = kb0 + g;
-      if (kb >= G) break;
+      if (kb0 + g >= G) break;
       const float2 f01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw[g].x));
       const float2 f23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw[g].y));
       float m = fmaxf(fmaxf(fabsf(f01.x), fabsf(f01.y)), fmaxf(fabsf(f23.x), fabsf(f23.y)));
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-      const float sc = group_scale(m);
-      *reinterpret_cast<uint32_t*>(Xq + static_cast<size_t>(pos) * H + kb * 128 + lane * 4) =
-          e4m3x4(q_clamp(f01.x, sc), q_clamp(f01.y, sc), q_clamp(f23.x, sc),
-                 q_clamp(f23.y, sc));
-      if (lane == 0) Xs[static_cast<size_t>(kb) * max_rows + pos] = sc;
+      scl[g] = group_scale(m);
+      code[g] = e4m3x4(q_clamp(f01.x, scl[g]), q_clamp(f01.y, scl[g]), q_clamp(f23.x, scl[g]),
+                       q_clamp(f23.y, scl[g]));
+    }
+    const bool shared_tok = n_sh > 0 && tok >= sh_t0 && tok < sh_t0 + sh_nt;
+    const int n_dst = topk + (shared_tok ? n_sh : 0);
+    for (int j = 0; j < n_dst; ++j) {
+      const int pos = j < topk ? pair_pos[static_cast<size_t>(tok) * topk + j]
+                               : ws_hdr[WS_SH_BASE + (j - topk)] + (tok - sh_t0);
+      if (pos < 0) continue;  // the same for the whole warp
+#pragma unroll
+      for (int g = 0; g < kQuantGroups; ++g) {
+        const int kb = kb0 + g;
+        if (kb >= G) break;
+        *reinterpret_cast<uint32_t*>(Xq + static_cast<size_t>(pos) * H + kb * 128 + lane * 4) =
+            code[g];
+        if (lane == 0) Xs[static_cast<size_t>(kb) * max_rows + pos] = scl[g];
+      }
     }
   }
 }
@@ -1519,7 +1526,8 @@ __global__ void __launch_bounds__(F8W_THREADS, 1) moe_gemm_f8w_kernel(
 
 // vLLM's SiLU-and-mul chain on the wide gate/up output (bf16 g and u rows of
 // 2I columns), then per-token 128-column quantisation for the down GEMM: the
-// same arithmetic as the narrow gate/up epilogue. One warp per (row, group).
+// same arithmetic as the narrow gate/up epilogue. A warp takes four groups of
+// one row (eight independent 8-byte loads per lane in flight).
 __global__ void __launch_bounds__(256) swiglu_quant_kernel(
     const int32_t* __restrict__ ws_hdr, const int4* __restrict__ items, int BN,
     const __nv_bfloat16* __restrict__ gu, int I, uint8_t* __restrict__ Aq,
@@ -1532,36 +1540,47 @@ __global__ void __launch_bounds__(256) swiglu_quant_kernel(
   const int item_lo = phase == 1 ? n_hit : 0;
   const int item_hi = phase == 0 ? n_hit : num_items;
   const int G = I / 128;
-  const long n_units = static_cast<long>(item_hi > item_lo ? item_hi - item_lo : 0) * BN * G;
+  const int GU = (G + kQuantGroups - 1) / kQuantGroups;
+  const long n_units = static_cast<long>(item_hi > item_lo ? item_hi - item_lo : 0) * BN * GU;
   const long nwarps = static_cast<long>(gridDim.x) * (blockDim.x >> 5);
   for (long u = static_cast<long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
        u < n_units; u += nwarps) {
-    const int grp = static_cast<int>(u % G);
-    const long rr = u / G;
+    const int g0 = static_cast<int>(u % GU) * kQuantGroups;
+    const long rr = u / GU;
     const int4 it = items[item_lo + static_cast<int>(rr / BN)];
     const int r = static_cast<int>(rr % BN);
     if (r >= it.z) continue;  // the same for the whole warp
     const size_t row = static_cast<size_t>(it.y) + r;
-    const uint2 graw = *reinterpret_cast<const uint2*>(gu + row * 2 * I + grp * 128 + lane * 4);
-    const uint2 uraw =
-        *reinterpret_cast<const uint2*>(gu + row * 2 * I + I + grp * 128 + lane * 4);
-    const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&graw);
-    const __nv_bfloat162* u2 = reinterpret_cast<const __nv_bfloat162*>(&uraw);
-    float a[4];
+    const __nv_bfloat16* gr = gu + row * 2 * I + lane * 4;
+    uint2 graw[kQuantGroups], uraw[kQuantGroups];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const float2 g = __bfloat1622float2(g2[h]);
-      const float2 uu = __bfloat1622float2(u2[h]);
-      a[2 * h] = sl::bf16_round(sl::bf16_round(g.x / (1.0f + expf(-g.x))) * uu.x);
-      a[2 * h + 1] = sl::bf16_round(sl::bf16_round(g.y / (1.0f + expf(-g.y))) * uu.y);
+    for (int g = 0; g < kQuantGroups; ++g)
+      if (g0 + g < G) {
+        graw[g] = *reinterpret_cast<const uint2*>(gr + (g0 + g) * 128);
+        uraw[g] = *reinterpret_cast<const uint2*>(gr + I + (g0 + g) * 128);
+      }
+#pragma unroll
+    for (int g = 0; g < kQuantGroups; ++g) {
+      const int grp = g0 + g;
+      if (grp >= G) break;
+      const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&graw[g]);
+      const __nv_bfloat162* u2 = reinterpret_cast<const __nv_bfloat162*>(&uraw[g]);
+      float a[4];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const float2 gg = __bfloat1622float2(g2[h]);
+        const float2 uu = __bfloat1622float2(u2[h]);
+        a[2 * h] = sl::bf16_round(sl::bf16_round(gg.x / (1.0f + expf(-gg.x))) * uu.x);
+        a[2 * h + 1] = sl::bf16_round(sl::bf16_round(gg.y / (1.0f + expf(-gg.y))) * uu.y);
+      }
+      float m = fmaxf(fmaxf(fabsf(a[0]), fabsf(a[1])), fmaxf(fabsf(a[2]), fabsf(a[3])));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      const float scv = group_scale(m);
+      *reinterpret_cast<uint32_t*>(Aq + row * I + grp * 128 + lane * 4) =
+          e4m3x4(q_clamp(a[0], scv), q_clamp(a[1], scv), q_clamp(a[2], scv), q_clamp(a[3], scv));
+      if (lane == 0) As[static_cast<size_t>(grp) * max_rows + row] = scv;
     }
-    float m = fmaxf(fmaxf(fabsf(a[0]), fabsf(a[1])), fmaxf(fabsf(a[2]), fabsf(a[3])));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    const float scv = group_scale(m);
-    *reinterpret_cast<uint32_t*>(Aq + row * I + grp * 128 + lane * 4) =
-        e4m3x4(q_clamp(a[0], scv), q_clamp(a[1], scv), q_clamp(a[2], scv), q_clamp(a[3], scv));
-    if (lane == 0) As[static_cast<size_t>(grp) * max_rows + row] = scv;
   }
 }
 
@@ -1753,8 +1772,8 @@ extern "C" size_t sl_fused_experts_workspace_bytes(int T, int topk, int H, int I
   if (T < 0 || topk <= 0 || H <= 0 || I <= 0 || num_slots <= 0 || n_shared < 0) return 0;
   // large enough for either weight dtype's token tiles
   const size_t a = ws_layout(T, topk, H, I, num_slots, n_shared, choose_bn(T, topk, num_slots)).total;
-  const size_t b = ws_layout(T, topk, H, I, num_slots, n_shared,
-                             choose_bn(T, topk, num_slots, true)).total;
+  const int bn8 = choose_bn(T, topk, num_slots, true);
+  const size_t b = ws_layout(T, topk, H, I, num_slots, n_shared, bn8, bn8 == kF8WideBN).total;
   return a > b ? a : b;
 }
 
@@ -1786,7 +1805,8 @@ int sl::fused_experts_check(const void* hidden, int T, int H, int I, const sl_ex
     return SL_ERR_INVALID;
   if (fp8 && (H / 128 > kF8MaxKBlocks || I / 128 > kF8MaxKBlocks)) return SL_ERR_UNSUPPORTED;
   const int BN = choose_bn(T, topk, num_slots, fp8);
-  if (workspace_bytes < ws_layout(T, topk, H, I, num_slots, n_shared, BN).total)
+  if (workspace_bytes < ws_layout(T, topk, H, I, num_slots, n_shared, BN,
+                                  fp8 && BN == kF8WideBN).total)
     return SL_ERR_INVALID;
   return SL_OK;
 }
@@ -1808,7 +1828,7 @@ int run_fused(const void* hidden, int T, int H, int I, const sl_expert_weights& 
   const int num_slots = w.num_slots, n_shared = w.n_shared;
   const bool fp8 = w.dtype == SL_WEIGHTS_FP8_BLOCK128;
   const int BN = choose_bn(T, topk, num_slots, fp8);
-  const WsLayout L = ws_layout(T, topk, H, I, num_slots, n_shared, BN);
+  const WsLayout L = ws_layout(T, topk, H, I, num_slots, n_shared, BN, fp8 && BN == kF8WideBN);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   int32_t* hdr = reinterpret_cast<int32_t*>(ws);
   int4* items = reinterpret_cast<int4*>(ws + L.items);
@@ -1868,15 +1888,17 @@ int run_fused(const void* hidden, int T, int H, int I, const sl_expert_weights& 
                                static_cast<const __nv_bfloat16*>(hidden), H, X));
     }
     if (fp8) {
-      const long units = static_cast<long>(P + nsh * (nsh ? sh_nt : 0)) *
-                         ((H / 128 + kQuantGroups - 1) / kQuantGroups);
+      // one unit = four 128-column groups of one token, quantised once and
+      // written to every row the token feeds
+      const long units = static_cast<long>(T) * ((H / 128 + kQuantGroups - 1) / kQuantGroups);
       long ctas = (units + 7) / 8;  // 8 warps per CTA, one unit each
       const long cap = 8L * sl_device_sm_count();
       if (ctas > cap) ctas = cap;
       if (ctas < 1) ctas = 1;
       SL_CUDA_TRY(sl::launch(gather_quant_kernel, dim3(static_cast<unsigned>(ctas)), dim3(256),
-                             0, st, static_cast<const int32_t*>(hdr),
-                             static_cast<const int32_t*>(pair_pos), P, topk, nsh,
+                             0, st,
+                             static_cast<const int32_t*>(hdr),
+                             static_cast<const int32_t*>(pair_pos), T, topk, nsh,
                              nsh ? sh_t0 : 0, nsh ? sh_nt : 0,
                              static_cast<const __nv_bfloat16*>(hidden), H, Xq, Xs, L.max_rows));
     }
@@ -1907,7 +1929,8 @@ int run_fused(const void* hidden, int T, int H, int I, const sl_expert_weights& 
     rc = launch_gemm_f8w(m_w13, m_w13sh, m_xw, Xs, w.w13_scale, w.shared_w13_scale, hdr, items,
                          GU, num_slots, H, 2 * I, L.max_rows, hdr, L.max_items, st, phase);
     if (rc == SL_OK) {
-      const long units = static_cast<long>(L.max_items) * BN * (I / 128);
+      const long units = static_cast<long>(L.max_items) * BN *
+                         ((I / 128 + kQuantGroups - 1) / kQuantGroups);
       long ctas = (units + 7) / 8;
       const long cap = 8L * sl_device_sm_count();
       if (ctas > cap) ctas = cap;
