@@ -430,7 +430,12 @@ def profile_layers(stack, x):
                                           out=out)
         fused_ms.append(_graph_time_ms(fused))
         route_ms.append(_graph_time_ms(lambda: layer.router.route(hs)))
-        u = len(set(ti.flatten().tolist()))
+        # the experts this cache serves (all of them on one GPU; this rank's
+        # under expert parallelism)
+        emap = layer.cache.expert_map.cpu()
+        ids = ti.flatten().cpu().long()
+        valid = (ids >= 0) & (ids < emap.numel())
+        u = len(set(ids[valid][emap[ids[valid]] >= 0].tolist()))
         fused_bytes.append((u + cfg.n_shared) * bpe)
         h = h + out
     torch.cuda.synchronize()
@@ -894,42 +899,37 @@ def run_sluice(a):
                       "replayed on the same inputs from the same restored cache state"
                       + (", summed over ranks" if world > 1 else "")}
 
-    roof_fused = None
     sprobe = None
-    if world == 1:
-        # fused_experts: each layer's call replayed as its own CUDA graph
-        hx = synth.TokenStream(cfg.hidden, T, seed=a.seed + 555).next().cuda()
-        route_ms, fused_ms, fbytes = profile_layers(stack, hx)
-        t_fused = statistics.mean(fused_ms)
-        fused_gbs = statistics.mean(fbytes) / (t_fused * 1e-3) / 1e9
-        roof_fused = {"bound": "hbm", "kernel": "fused_experts (align+gate/up+down+combine)",
-                      "achieved": fused_gbs, "peak": hbm_peak, "unit": "GB/s",
-                      "frac": fused_gbs / hbm_peak,
-                      "traffic": _traffic_per_launch(fbytes, cfg),
-                      "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)",
-                      "per_launch_ms": {"route": statistics.mean(route_ms), "fused": t_fused},
-                      "fused_bytes_per_launch": statistics.mean(fbytes),
-                      "timing": "each layer's fused_experts replayed as its own CUDA graph, "
-                                "CUDA events, mean over layers"}
-        if offloaded:
-            sprobe = stream_probe(stack)
-    else:
-        roof_fused = {"bound": "hbm", "kernel": "expert-parallel decode step (per rank)",
-                      "achieved": hbm_step / (ms / K * 1e-3) / 1e9, "peak": hbm_peak,
-                      "unit": "GB/s", "frac": hbm_step / (ms / K * 1e-3) / 1e9 / hbm_peak,
-                      "traffic": None,
-                      "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)",
-                      "timing": "timed region, max over ranks"}
+    # fused_experts: each layer's call replayed as its own CUDA graph (under
+    # expert parallelism: this rank's experts on its own tokens; the slowest
+    # rank's figures are reported)
+    hx = synth.TokenStream(cfg.hidden, T, seed=a.seed + 555 + rank).next().cuda()
+    route_ms, fused_ms, fbytes = profile_layers(stack, hx)
+    t_fused = _max_over_ranks(statistics.mean(fused_ms), dist)
+    t_route = _max_over_ranks(statistics.mean(route_ms), dist)
+    f_bytes = statistics.mean(fbytes)
+    fused_gbs = f_bytes / (t_fused * 1e-3) / 1e9
+    roof_fused = {"bound": "hbm", "kernel": "fused_experts (align+gate/up+down+combine)",
+                  "achieved": fused_gbs, "peak": hbm_peak, "unit": "GB/s",
+                  "frac": fused_gbs / hbm_peak,
+                  "traffic": _traffic_per_launch(fbytes, cfg),
+                  "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)",
+                  "per_launch_ms": {"route": t_route, "fused": t_fused},
+                  "fused_bytes_per_launch": f_bytes,
+                  "timing": "each layer's fused_experts replayed as its own CUDA graph, "
+                            "CUDA events, mean over layers"
+                            + ("; this rank's experts on its own tokens, slowest rank"
+                               if world > 1 else "")}
+    if world == 1 and offloaded:
+        sprobe = stream_probe(stack)
     # the dominant kernel of the step: the expert streamer or the fused
-    # experts, whichever takes more device time per step
+    # experts, whichever takes more device time per step (per rank)
     roof = roof_fused
+    fused_ms_step = t_fused * layers
+    roof_fused["ms_per_step"] = fused_ms_step
     if roof_stream is not None:
         stream_ms_step = st_ms / K / (world if world > 1 else 1)
-        fused_ms_step = (roof_fused.get("per_launch_ms", {}).get("fused", 0.0) * layers
-                         if world == 1 else 0.0)
         roof_stream["ms_per_step"] = stream_ms_step
-        if world == 1:
-            roof_fused["ms_per_step"] = fused_ms_step
         if stream_ms_step >= fused_ms_step:
             roof = roof_stream
     roof_other = roof_stream if roof is roof_fused else roof_fused

@@ -415,6 +415,16 @@ int sl_mla_decode(const void* qkv, int ld_qkv, const void* kv_norm, float eps,
                   int rank, int vdim, int max_len, float scale, void* out,
                   sl_stream_t stream);
 
+/* Not part of the reference's MoE operator surface: the residual add and
+ * RMSNorm between the decoder's sublayers in this build's benchmark harness
+ * (vLLM's fused add + RMSNorm, which the reference's model runs). For each of
+ * `rows` rows of width H (bf16): h = bf16(h + delta) in place (delta NULL:
+ * h unchanged), then out = bf16(h * rsqrt(mean(h^2) + eps) * w) (fp32
+ * arithmetic, w bf16 [H]). H a multiple of 8, at most 8192; rows 16-byte
+ * aligned. */
+int sl_add_rmsnorm(void* h, const void* delta, const void* w, float eps, void* out, int rows,
+                   int H, sl_stream_t stream);
+
 /* sl_fused_experts without any device allocation. No counterpart in the
  * reference: it serves callers that cannot allocate device scratch memory for
  * a call -- a host program binding this C ABI directly (cgo, JNI, ctypes

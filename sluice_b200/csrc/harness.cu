@@ -298,7 +298,83 @@ __global__ void __launch_bounds__(kMlaThreads) mla_decode_kernel(
   }
 }
 
+// Residual add + RMSNorm, one CTA per row: h = bf16(h + delta), then
+// out = bf16(h * rsqrt(mean(h^2) + eps) * w), fp32 arithmetic. Each thread
+// holds 8 consecutive columns (one 16-byte load of h, of delta and of w).
+constexpr int kNormThreads = 256;
+
+__global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(
+    __nv_bfloat16* __restrict__ h, const __nv_bfloat16* __restrict__ delta,
+    const __nv_bfloat16* __restrict__ w, float eps, __nv_bfloat16* __restrict__ out, int H) {
+  __shared__ float red[32];
+  sl::pdl_wait();
+  sl::pdl_trigger();
+  const size_t base = static_cast<size_t>(blockIdx.x) * H;
+  float v[4][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int nv = 0; nv < 4; ++nv) {
+    const int c = (threadIdx.x + nv * blockDim.x) * 8;
+    if (c >= H) break;
+    uint4 hv = *reinterpret_cast<const uint4*>(h + base + c);
+    const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&hv);
+    if (delta != nullptr) {
+      const uint4 dv = *reinterpret_cast<const uint4*>(delta + base + c);
+      const __nv_bfloat162* d2 = reinterpret_cast<const __nv_bfloat162*>(&dv);
+      uint4 sv;
+      __nv_bfloat162* s2 = reinterpret_cast<__nv_bfloat162*>(&sv);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 a = __bfloat1622float2(h2[i]), b = __bfloat1622float2(d2[i]);
+        s2[i] = __floats2bfloat162_rn(a.x + b.x, a.y + b.y);
+      }
+      *reinterpret_cast<uint4*>(h + base + c) = sv;
+      hv = sv;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 a = __bfloat1622float2(h2[i]);
+      v[nv][2 * i] = a.x;
+      v[nv][2 * i + 1] = a.y;
+      ss = fmaf(a.x, a.x, ss);
+      ss = fmaf(a.y, a.y, ss);
+    }
+  }
+  const float r = rsqrtf(block_sum(ss, red) / H + eps);
+#pragma unroll
+  for (int nv = 0; nv < 4; ++nv) {
+    const int c = (threadIdx.x + nv * blockDim.x) * 8;
+    if (c >= H) break;
+    const uint4 wv = *reinterpret_cast<const uint4*>(w + c);
+    const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wv);
+    uint4 ov;
+    __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&ov);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 g = __bfloat1622float2(w2[i]);
+      o2[i] = __floats2bfloat162_rn(v[nv][2 * i] * r * g.x, v[nv][2 * i + 1] * r * g.y);
+    }
+    *reinterpret_cast<uint4*>(out + base + c) = ov;
+  }
+}
+
 }  // namespace
+
+extern "C" int sl_add_rmsnorm(void* h, const void* delta, const void* w, float eps, void* out,
+                              int rows, int H, sl_stream_t stream) {
+  if (rows < 0 || H <= 0 || H % 8 || H > 8 * kNormThreads * 4) return SL_ERR_INVALID;
+  if (rows == 0) return SL_OK;
+  if (!h || !w || !out || rows > 65535 * 32) return SL_ERR_INVALID;
+  if ((reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(delta) |
+       reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(out)) & 15)
+    return SL_ERR_INVALID;
+  SL_CUDA_TRY(sl::launch(add_rmsnorm_kernel, dim3(rows), dim3(kNormThreads), 0,
+                         reinterpret_cast<cudaStream_t>(stream), static_cast<__nv_bfloat16*>(h),
+                         static_cast<const __nv_bfloat16*>(delta),
+                         static_cast<const __nv_bfloat16*>(w), eps,
+                         static_cast<__nv_bfloat16*>(out), H));
+  return SL_OK;
+}
 
 extern "C" int sl_mla_decode(const void* qkv, int ld_qkv, const void* kv_norm, float eps,
                              const void* w_uk, const void* w_uv, const float* rope_cos_sin,

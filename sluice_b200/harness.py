@@ -86,7 +86,9 @@ class DecoderHarness:
                  device="cuda", std: float = 0.02, fused_attention: bool | None = None):
         """``fused_attention`` (default: on a CUDA device) runs each layer's
         attention core as the library's one-launch MLA decode kernel
-        (``sl_mla_decode``); otherwise, and on the host, as PyTorch ops."""
+        (``sl_mla_decode``) and each residual add with the RMSNorm after it
+        as one launch (``sl_add_rmsnorm``); otherwise, and on the host, as
+        PyTorch ops."""
         self.cfg = cfg
         self.moe = moe
         self.batch = batch
@@ -177,6 +179,22 @@ class DecoderHarness:
         o = torch.bmm(o_lat.transpose(0, 1), lw["w_uv_t"])                   # [nh, B, v]
         return F.linear(o.transpose(0, 1).reshape(B, nh * cfg.v_head), lw["wo"])
 
+    def _add_norm(self, h: torch.Tensor, delta: torch.Tensor | None,
+                  w: torch.Tensor) -> torch.Tensor:
+        """h += delta (in place; None: no add), then RMSNorm(h) * w."""
+        eps = self.cfg.rms_eps
+        if self.fused_attention:
+            from ._lib import check, lib, ptr
+            out = torch.empty_like(h)
+            check(lib().sl_add_rmsnorm(ptr(h), ptr(delta) if delta is not None else None,
+                                       ptr(w), eps, ptr(out), h.shape[0], h.shape[1],
+                                       torch.cuda.current_stream().cuda_stream),
+                  "sl_add_rmsnorm")
+            return out
+        if delta is not None:
+            h.add_(delta)
+        return _rms(h, w, eps)
+
     def _dense_ffn(self, li: int, x: torch.Tensor) -> torch.Tensor:
         lw = self.layers[li]
         g, u = F.linear(x, lw["w13"]).chunk(2, dim=-1)
@@ -193,15 +211,15 @@ class DecoderHarness:
         mask_bias = torch.zeros(h.shape[0], 1, self.max_len, dtype=h.dtype, device=h.device)
         mask_bias.masked_fill_((self._ar[None, :] > self.pos[:, None])[:, None, :],
                                float("-inf"))
+        x = self._add_norm(h, None, self.layers[0]["in_norm"])
         for li in range(cfg.num_layers):
             lw = self.layers[li]
-            h = h + self._attention(li, _rms(h, lw["in_norm"], cfg.rms_eps), mask_bias, freqs)
-            x = _rms(h, lw["post_norm"], cfg.rms_eps)
-            if li < cfg.first_dense:
-                h = h + self._dense_ffn(li, x)
-            else:
-                h = h + self.moe(li - cfg.first_dense, x)
-        logits = F.linear(_rms(h, self.final_norm, cfg.rms_eps), self.head)
+            x = self._add_norm(h, self._attention(li, x, mask_bias, freqs), lw["post_norm"])
+            f = self._dense_ffn(li, x) if li < cfg.first_dense else \
+                self.moe(li - cfg.first_dense, x)
+            nxt = self.layers[li + 1]["in_norm"] if li + 1 < cfg.num_layers else self.final_norm
+            x = self._add_norm(h, f, nxt)
+        logits = F.linear(x, self.head)
         self.pos.add_(1)
         return logits.argmax(dim=-1)
 

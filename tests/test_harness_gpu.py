@@ -78,3 +78,32 @@ def test_fused_mla_decode_matches_the_pytorch_attention():
         rows = torch.arange(3, device="cuda")
         new, old = h.cache[li][rows, h.pos].float(), ref_cache[rows, h.pos].float()
         assert (new - old).abs().max().item() <= 1e-2 * old.abs().max().item(), li
+
+
+def test_fused_add_rmsnorm_matches_pytorch():
+    """sl_add_rmsnorm (the harness's residual add + RMSNorm) against the same
+    two PyTorch ops: the updated residual bit-equal, the normed rows within
+    one bf16 rounding; without a delta, the residual untouched."""
+    from sluice_b200._lib import check, lib, ptr
+
+    g = torch.Generator(device="cuda").manual_seed(11)
+    for rows, H in ((8, 2048), (3, 7168), (1, 512)):
+        h = torch.randn(rows, H, device="cuda", generator=g).to(torch.bfloat16)
+        d = torch.randn(rows, H, device="cuda", generator=g).to(torch.bfloat16)
+        w = (1 + 0.1 * torch.randn(H, device="cuda", generator=g)).to(torch.bfloat16)
+        ref_h = h + d
+        ref = torch.nn.functional.rms_norm(ref_h, (H,), w, 1e-6)
+        got_h, out = h.clone(), torch.empty_like(h)
+        stream = torch.cuda.current_stream().cuda_stream
+        check(lib().sl_add_rmsnorm(ptr(got_h), ptr(d), ptr(w), 1e-6, ptr(out), rows, H, stream),
+              "sl_add_rmsnorm")
+        torch.cuda.synchronize()
+        assert torch.equal(got_h, ref_h)
+        err = (out.float() - ref.float()).abs()
+        assert (err <= 1e-2 * ref.float().abs() + 1e-2).all(), err.max().item()
+        plain = torch.empty_like(h)
+        check(lib().sl_add_rmsnorm(ptr(h), None, ptr(w), 1e-6, ptr(plain), rows, H, stream),
+              "sl_add_rmsnorm")
+        torch.cuda.synchronize()
+        ref2 = torch.nn.functional.rms_norm(h, (H,), w, 1e-6)
+        assert ((plain.float() - ref2.float()).abs() <= 1e-2 * ref2.float().abs() + 1e-2).all()
