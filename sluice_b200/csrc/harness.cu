@@ -14,13 +14,18 @@
 //      cache (the other heads use their own copy for position P);
 //   2. forms the absorbed query [q_nope W_uk | rope(q_pe)] (fp32 sums, bf16
 //      rounding, as the bf16 GEMM it replaces);
-//   3. scores every cached position 0..P, softmax;
-//   4. sums the latents weighted by the probabilities, maps through W_uv.
-// Each lane owns 16 of the 512 latent columns (two 8-column chunks, so a
-// warp reads a whole 1 KB latent or weight row per step with 16-byte loads);
-// the warps split the rows of W_uk / W_uv and the cached positions, and every
-// loop keeps four rows' loads in flight. The rank is fixed at 512 (the
-// DeepSeek-V2 / V3 latent width); other shapes are refused by the host.
+//   3. scores every cached position 0..P and sums the latents weighted by
+//      their softmax probabilities in one pass (a running max and sum per
+//      warp, merged across the warps at the end);
+//   4. maps the weighted latent through W_uv.
+// Everything the CTA reads in bulk -- the head's W_uk rows, the sequence's
+// cached rows 0..P-1, the head's W_uv rows -- arrives in 32-row chunks by
+// 1-D bulk copies (cp.async.bulk) into a ring of four shared-memory slots,
+// issued up to four chunks ahead of the warps that consume them, so the
+// DRAM latency is paid about once per four chunks instead of once per row
+// batch. Each lane owns 16 of the 512 latent columns (two 8-column chunks);
+// the warps split a chunk's rows. The rank is fixed at 512 (the DeepSeek-V2 /
+// V3 latent width) and rope at most 64; other shapes are refused by the host.
 #include "common.cuh"
 
 namespace {
@@ -28,7 +33,10 @@ namespace {
 constexpr int kMlaThreads = 256;
 constexpr int kMlaWarps = kMlaThreads / 32;
 constexpr int kRank = 512;
-constexpr int kUnroll = 4;
+constexpr int kRingRows = 32;    // rows per bulk-copied chunk
+constexpr int kRingSlots = 4;    // chunks in flight
+constexpr int kMaxRowBytes = (512 + 64) * 2;
+constexpr int kSlotBytes = kRingRows * kMaxRowBytes;  // 36864, a multiple of 16
 
 __device__ __forceinline__ float block_sum(float v, float* red) {
 #pragma unroll
@@ -39,18 +47,6 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   __syncthreads();
   float t = 0.f;
   for (int i = 0; i < nw; ++i) t += red[i];
-  return t;
-}
-
-__device__ __forceinline__ float block_max(float v, float* red) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  __syncthreads();
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  float t = -INFINITY;
-  for (int i = 0; i < nw; ++i) t = fmaxf(t, red[i]);
   return t;
 }
 
@@ -93,31 +89,77 @@ __global__ void __launch_bounds__(kMlaThreads) mla_decode_kernel(
     const float2* __restrict__ rope_cs, const int64_t* __restrict__ pos,
     __nv_bfloat16* __restrict__ cache, int nh, int nope, int rope, int vdim, int max_len,
     float scale, __nv_bfloat16* __restrict__ out) {
-  extern __shared__ float sm[];
+  extern __shared__ __align__(16) uint8_t sm_raw[];
   const int h = blockIdx.x, b = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int dk = kRank + rope;
-  float* q = sm;                     // [dk] absorbed query
-  float* kv = q + dk;                // [dk] this position's latent | rotated k_pe
-  float* p = kv + dk;                // [max_len] scores, then probabilities
-  float* part = p + max_len;         // [warps][rank] per-warp partial sums
-  float* red = part + kMlaWarps * kRank;  // [32]
+  uint8_t* ring = sm_raw;                                            // [slots][kSlotBytes]
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + kRingSlots * kSlotBytes);
+  float* q = reinterpret_cast<float*>(full + kRingSlots);            // [dk] absorbed query
+  float* kv = q + dk;                      // [dk] this position's latent | rotated k_pe
+  float* part = kv + dk;                   // [warps][rank] per-warp partial sums
+  float* qn = part + kMlaWarps * kRank;    // [nope] q_nope of this head
+  float* wm = qn + nope;                   // [warps] running max per warp
+  float* wl = wm + kMlaWarps;              // [warps] running sum per warp
+  float* red = wl + kMlaWarps;             // [32]
+
+  // the chunk jobs, in consumption order: W_uk rows, cached rows 0..P-1,
+  // W_uv rows
+  const int nk = (nope + kRingRows - 1) / kRingRows;
+  const int nv = (vdim + kRingRows - 1) / kRingRows;
+  int P = 0, nc = 0;
+  auto issue = [&](int j) {
+    const __nv_bfloat16* src;
+    int rows;
+    size_t row_bytes;
+    if (j < nk) {
+      src = w_uk + (static_cast<size_t>(h) * nope + j * kRingRows) * kRank;
+      rows = min(kRingRows, nope - j * kRingRows);
+      row_bytes = kRank * 2;
+    } else if (j < nk + nc) {
+      const int c = j - nk;
+      src = cache + (static_cast<size_t>(b) * max_len + c * kRingRows) * dk;
+      rows = min(kRingRows, P - c * kRingRows);
+      row_bytes = static_cast<size_t>(dk) * 2;
+    } else {
+      const int v = j - nk - nc;
+      src = w_uv + (static_cast<size_t>(h) * vdim + v * kRingRows) * kRank;
+      rows = min(kRingRows, vdim - v * kRingRows);
+      row_bytes = kRank * 2;
+    }
+    const uint32_t bytes = static_cast<uint32_t>(rows * row_bytes);
+    uint64_t* bar = &full[j % kRingSlots];
+    sl::mbar_arrive_expect_tx(bar, bytes);
+    sl::bulk_load(ring + (j % kRingSlots) * kSlotBytes, src, bytes, bar);
+  };
+  if (tid == 0) {
+    for (int i = 0; i < kRingSlots; ++i) sl::mbar_init(&full[i], 1);
+    sl::fence_barrier_init();
+    // the weights are constants of the step: their chunks may be fetched
+    // before waiting on the kernel that wrote this step's projections
+    for (int j = 0; j < nk && j < kRingSlots; ++j) issue(j);
+  }
   sl::pdl_wait();
   sl::pdl_trigger();
-  int P = static_cast<int>(pos[b]);
+  P = static_cast<int>(pos[b]);
   P = P < 0 ? 0 : (P >= max_len ? max_len - 1 : P);
+  nc = (P + kRingRows - 1) / kRingRows;
+  const int J = nk + nc + nv;
+  if (tid == 0)  // the rest of the first ring's chunks (fewer weight chunks than slots)
+    for (int j = min(nk, kRingSlots); j < min(J, kRingSlots); ++j) issue(j);
   const __nv_bfloat16* row = qkv + static_cast<size_t>(b) * ld_qkv;
   const __nv_bfloat16* qh = row + h * (nope + rope);
   const __nv_bfloat16* ckv = row + nh * (nope + rope);
   const float2* cs = rope_cs + static_cast<size_t>(P) * (rope / 2);
 
-  // 1. RMSNorm of c_kv and the rotated k_pe for position P
+  // 1. RMSNorm of c_kv and the rotated k_pe for position P; q_nope to shared
   float ss = 0.f;
   for (int i = tid; i < kRank; i += blockDim.x) {
     const float v = __bfloat162float(ckv[i]);
     kv[i] = v;
     ss += v * v;
   }
+  for (int d = tid; d < nope; d += blockDim.x) qn[d] = __bfloat162float(qh[d]);
   const float r = rsqrtf(block_sum(ss, red) / kRank + eps);
   for (int i = tid; i < kRank; i += blockDim.x)
     kv[i] = sl::bf16_round(kv[i] * r * __bfloat162float(kv_norm[i]));
@@ -131,169 +173,146 @@ __global__ void __launch_bounds__(kMlaThreads) mla_decode_kernel(
     q[kRank + 2 * j] = sl::bf16_round(y0 * c.x - y1 * c.y);
     q[kRank + 2 * j + 1] = sl::bf16_round(y1 * c.x + y0 * c.y);
   }
-  // 2. absorbed query: q_lat[c] = sum_d q_nope[d] W_uk[h][d][c]; warp w sums
-  // the rows d = w, w + 8, ...
-  {
-    const __nv_bfloat16* wk = w_uk + static_cast<size_t>(h) * nope * kRank;
-    float acc[16];
+  __syncthreads();  // barriers initialised, kv / q rope / q_nope written
+
+  const int rp = rope / 32;  // rope columns per lane
+  float acc[16];              // absorbed query, then the weighted latent
 #pragma unroll
-    for (int i = 0; i < 16; ++i) acc[i] = 0.f;
-    for (int d0 = warp; d0 < nope; d0 += kMlaWarps * kUnroll) {
-      Row16 rr[kUnroll];
+  for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+  float qr[16], qp0 = 0.f, qp1 = 0.f;
+  float m_w = -INFINITY, l_w = 0.f;  // this warp's running max and sum
+  float o16[16];
+  // online softmax step of one row: score s, latent values v
+  auto absorb = [&](float s, const float (&v)[16]) {
+    if (s > m_w) {
+      const float corr = __expf(m_w - s);
+      l_w *= corr;
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int d = d0 + u * kMlaWarps;
-        if (d < nope) rr[u] = load_row16(wk + static_cast<size_t>(d) * kRank, lane);
+      for (int i = 0; i < 16; ++i) acc[i] *= corr;
+      m_w = s;
+    }
+    const float pe = __expf(s - m_w);
+    l_w += pe;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) acc[i] = fmaf(pe, v[i], acc[i]);
+  };
+
+  for (int j = 0; j < J; ++j) {
+    (void)sl::mbar_wait(&full[j % kRingSlots], (j / kRingSlots) & 1);
+    const uint8_t* slot = ring + (j % kRingSlots) * kSlotBytes;
+    if (j < nk) {
+      // 2. absorbed query: q_lat[c] += q_nope[d] W_uk[h][d][c] over this
+      // chunk's rows (warp w: rows w, w + 8, ...)
+      const int d0 = j * kRingRows;
+      const int rows = min(kRingRows, nope - d0);
+      for (int rr = warp; rr < rows; rr += kMlaWarps) {
+        float v[16];
+        unpack16(load_row16(reinterpret_cast<const __nv_bfloat16*>(slot) + rr * kRank, lane), v);
+        const float qd = qn[d0 + rr];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc[i] = fmaf(qd, v[i], acc[i]);
       }
+      if (j == nk - 1) {
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int d = d0 + u * kMlaWarps;
-        if (d < nope) {
-          const float qd = __bfloat162float(qh[d]);
-          float v[16];
-          unpack16(rr[u], v);
+        for (int i = 0; i < 16; ++i) part[warp * kRank + col16(lane, i)] = acc[i];
+        __syncthreads();
+        for (int c = tid; c < kRank; c += blockDim.x) {
+          float t = 0.f;
 #pragma unroll
-          for (int i = 0; i < 16; ++i) acc[i] = fmaf(qd, v[i], acc[i]);
+          for (int w = 0; w < kMlaWarps; ++w) t += part[w * kRank + c];
+          q[c] = sl::bf16_round(t);
         }
+        if (h == 0) {
+          __nv_bfloat16* dst = cache + (static_cast<size_t>(b) * max_len + P) * dk;
+          for (int i = tid; i < dk; i += blockDim.x) dst[i] = __float2bfloat16(kv[i]);
+        }
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          qr[i] = q[col16(lane, i)];
+          acc[i] = 0.f;
+        }
+        qp0 = rp > 0 ? q[kRank + lane * rp] : 0.f;
+        qp1 = rp > 1 ? q[kRank + lane * rp + 1] : 0.f;
+      }
+    } else if (j < nk + nc) {
+      // 3. scores and the weighted latent of this chunk's cached rows
+      const int l0 = (j - nk) * kRingRows;
+      const int rows = min(kRingRows, P - l0);
+      const __nv_bfloat16* base = reinterpret_cast<const __nv_bfloat16*>(slot);
+      for (int rr = warp; rr < rows; rr += kMlaWarps) {
+        const __nv_bfloat16* key = base + rr * dk;
+        float v[16];
+        unpack16(load_row16(key, lane), v);
+        float sdot = 0.f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) sdot = fmaf(qr[i], v[i], sdot);
+        if (rp > 0) sdot = fmaf(qp0, __bfloat162float(key[kRank + lane * rp]), sdot);
+        if (rp > 1) sdot = fmaf(qp1, __bfloat162float(key[kRank + lane * rp + 1]), sdot);
+        absorb(warp_sum(sdot) * scale, v);
       }
     }
+    if (j == nk + nc - 1 || (nc == 0 && j == nk - 1)) {
+      // position P from this CTA's own copy of the new row (warp 0), then
+      // the warps' running sums merged
+      if (warp == 0) {
+        float v[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) part[warp * kRank + col16(lane, i)] = acc[i];
-  }
-  __syncthreads();
-  for (int c = tid; c < kRank; c += blockDim.x) {
-    float t = 0.f;
+        for (int i = 0; i < 16; ++i) v[i] = kv[col16(lane, i)];
+        float sdot = 0.f;
 #pragma unroll
-    for (int w = 0; w < kMlaWarps; ++w) t += part[w * kRank + c];
-    q[c] = sl::bf16_round(t);
-  }
-  if (h == 0) {
-    __nv_bfloat16* dst = cache + (static_cast<size_t>(b) * max_len + P) * dk;
-    for (int i = tid; i < dk; i += blockDim.x) dst[i] = __float2bfloat16(kv[i]);
-  }
-  __syncthreads();
-  // 3. scores over positions 0..P: warp w takes l = w, w + 8, ... (position
-  // P from this CTA's own copy of the new cache row)
-  const __nv_bfloat16* cb = cache + static_cast<size_t>(b) * max_len * dk;
-  {
-    float qr[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) qr[i] = q[col16(lane, i)];
-    const int rp = rope / 32;  // rope columns per lane (rope <= 64)
-    float qp0 = rp > 0 ? q[kRank + lane * rp] : 0.f;
-    float qp1 = rp > 1 ? q[kRank + lane * rp + 1] : 0.f;
-    for (int l0 = warp; l0 <= P; l0 += kMlaWarps * kUnroll) {
-      Row16 rr[kUnroll];
-      float kp[kUnroll][2];
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int l = l0 + u * kMlaWarps;
-        kp[u][0] = kp[u][1] = 0.f;
-        if (l < P) {
-          const __nv_bfloat16* key = cb + static_cast<size_t>(l) * dk;
-          rr[u] = load_row16(key, lane);
-          if (rp > 0) kp[u][0] = __bfloat162float(key[kRank + lane * rp]);
-          if (rp > 1) kp[u][1] = __bfloat162float(key[kRank + lane * rp + 1]);
-        }
+        for (int i = 0; i < 16; ++i) sdot = fmaf(qr[i], v[i], sdot);
+        if (rp > 0) sdot = fmaf(qp0, kv[kRank + lane * rp], sdot);
+        if (rp > 1) sdot = fmaf(qp1, kv[kRank + lane * rp + 1], sdot);
+        absorb(warp_sum(sdot) * scale, v);
       }
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int l = l0 + u * kMlaWarps;
-        if (l > P) continue;  // the same for the whole warp
-        float acc = 0.f;
-        if (l == P) {
+      for (int i = 0; i < 16; ++i) part[warp * kRank + col16(lane, i)] = acc[i];
+      if (lane == 0) {
+        wm[warp] = m_w;
+        wl[warp] = l_w;
+      }
+      __syncthreads();
+      float M = -INFINITY;
 #pragma unroll
-          for (int i = 0; i < 16; ++i) acc = fmaf(qr[i], kv[col16(lane, i)], acc);
-          if (rp > 0) acc = fmaf(qp0, kv[kRank + lane * rp], acc);
-          if (rp > 1) acc = fmaf(qp1, kv[kRank + lane * rp + 1], acc);
-        } else {
-          float v[16];
-          unpack16(rr[u], v);
+      for (int w = 0; w < kMlaWarps; ++w) M = fmaxf(M, wm[w]);
+      float L = 0.f, f[kMlaWarps];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) acc = fmaf(qr[i], v[i], acc);
-          acc = fmaf(qp0, kp[u][0], acc);
-          acc = fmaf(qp1, kp[u][1], acc);
-        }
-        acc = warp_sum(acc);
-        if (lane == 0) p[l] = acc * scale;
+      for (int w = 0; w < kMlaWarps; ++w) {
+        f[w] = __expf(wm[w] - M);
+        L = fmaf(f[w], wl[w], L);
+      }
+      const float invL = 1.f / L;
+      for (int c = tid; c < kRank; c += blockDim.x) {
+        float t = 0.f;
+#pragma unroll
+        for (int w = 0; w < kMlaWarps; ++w) t = fmaf(f[w], part[w * kRank + c], t);
+        q[c] = sl::bf16_round(t * invL);  // the query is no longer needed
+      }
+      __syncthreads();
+#pragma unroll
+      for (int i = 0; i < 16; ++i) o16[i] = q[col16(lane, i)];
+    }
+    if (j >= nk + nc) {
+      // 4. value map: out[d] = sum_c o_lat[c] W_uv[h][d][c] (warp w: rows
+      // w, w + 8, ... of this chunk)
+      const int d0 = (j - nk - nc) * kRingRows;
+      const int rows = min(kRingRows, vdim - d0);
+      __nv_bfloat16* dst = out + static_cast<size_t>(b) * nh * vdim + h * vdim;
+      for (int rr = warp; rr < rows; rr += kMlaWarps) {
+        float v[16];
+        unpack16(load_row16(reinterpret_cast<const __nv_bfloat16*>(slot) + rr * kRank, lane), v);
+        float t = 0.f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) t = fmaf(o16[i], v[i], t);
+        t = warp_sum(t);
+        if (lane == 0) dst[d0 + rr] = __float2bfloat16(t);
       }
     }
-  }
-  __syncthreads();
-  float m = -INFINITY;
-  for (int l = tid; l <= P; l += blockDim.x) m = fmaxf(m, p[l]);
-  m = block_max(m, red);
-  float se = 0.f;
-  for (int l = tid; l <= P; l += blockDim.x) {
-    const float e = __expf(p[l] - m);
-    p[l] = e;
-    se += e;
-  }
-  const float inv = 1.f / block_sum(se, red);
-  // 4. probability-weighted latent (warp w: positions w, w + 8, ... < P),
-  // then the value map (warp w: rows d = w, w + 8, ...)
-  {
-    float acc[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) acc[i] = 0.f;
-    for (int l0 = warp; l0 < P; l0 += kMlaWarps * kUnroll) {
-      Row16 rr[kUnroll];
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int l = l0 + u * kMlaWarps;
-        if (l < P) rr[u] = load_row16(cb + static_cast<size_t>(l) * dk, lane);
-      }
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int l = l0 + u * kMlaWarps;
-        if (l < P) {
-          const float pl = p[l];
-          float v[16];
-          unpack16(rr[u], v);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) acc[i] = fmaf(pl, v[i], acc[i]);
-        }
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < 16; ++i) part[warp * kRank + col16(lane, i)] = acc[i];
-  }
-  __syncthreads();
-  float* ol = q;  // the query is no longer needed: [rank] weighted latent
-  for (int c = tid; c < kRank; c += blockDim.x) {
-    float t = 0.f;
-#pragma unroll
-    for (int w = 0; w < kMlaWarps; ++w) t += part[w * kRank + c];
-    t = fmaf(p[P], kv[c], t);
-    ol[c] = sl::bf16_round(t * inv);
-  }
-  __syncthreads();
-  {
-    float o16[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) o16[i] = ol[col16(lane, i)];
-    const __nv_bfloat16* wv = w_uv + static_cast<size_t>(h) * vdim * kRank;
-    __nv_bfloat16* dst = out + static_cast<size_t>(b) * nh * vdim + h * vdim;
-    for (int d0 = warp; d0 < vdim; d0 += kMlaWarps * kUnroll) {
-      Row16 rr[kUnroll];
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int d = d0 + u * kMlaWarps;
-        if (d < vdim) rr[u] = load_row16(wv + static_cast<size_t>(d) * kRank, lane);
-      }
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int d = d0 + u * kMlaWarps;
-        if (d < vdim) {
-          float v[16];
-          unpack16(rr[u], v);
-          float acc = 0.f;
-#pragma unroll
-          for (int i = 0; i < 16; ++i) acc = fmaf(o16[i], v[i], acc);
-          acc = warp_sum(acc);
-          if (lane == 0) dst[d] = __float2bfloat16(acc);
-        }
-      }
+    __syncthreads();  // every warp is done with the slot
+    if (tid == 0 && j + kRingSlots < J) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(j + kRingSlots);
     }
   }
 }
@@ -394,9 +413,10 @@ extern "C" int sl_mla_decode(const void* qkv, int ld_qkv, const void* kv_norm, f
   if ((reinterpret_cast<uintptr_t>(w_uk) | reinterpret_cast<uintptr_t>(w_uv) |
        reinterpret_cast<uintptr_t>(cache)) & 15)
     return SL_ERR_INVALID;
-  const size_t smem =
-      sizeof(float) * (2 * static_cast<size_t>(rank + rope) + max_len + kMlaWarps * kRank + 32);
-  if (smem > 200 * 1024 || B > 65535) return SL_ERR_UNSUPPORTED;
+  const size_t smem = static_cast<size_t>(kRingSlots) * kSlotBytes + kRingSlots * 8 +
+      sizeof(float) * (2 * static_cast<size_t>(rank + rope) + kMlaWarps * kRank + nope +
+                       2 * kMlaWarps + 32);
+  if (smem > 220 * 1024 || B > 65535) return SL_ERR_UNSUPPORTED;
   static std::atomic<uint64_t> smem_set{0};
   if (smem > 48 * 1024) SL_CUDA_TRY(sl::ensure_smem_limit(mla_decode_kernel, static_cast<int>(smem), smem_set));
   SL_CUDA_TRY(sl::launch(mla_decode_kernel, dim3(nh, B), dim3(kMlaThreads), smem,

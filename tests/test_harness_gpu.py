@@ -60,6 +60,7 @@ def test_fused_mla_decode_matches_the_pytorch_attention():
     for _ in range(9):                      # fill positions 0..8 with the PyTorch path
         ids = h.step(ids)
     h.pos[1] = 3                            # ragged: sequences at different positions
+    h.pos[2] = 0                            # a sequence at its first position
     x = torch.randn(3, dcfg.hidden, device="cuda", generator=g).to(torch.bfloat16)
     freqs = h.freqs[h.pos]
     mask = torch.zeros(3, 1, h.max_len, dtype=torch.bfloat16, device="cuda")
