@@ -5,7 +5,7 @@
 // embedding, cache write, the absorbed query, scores, softmax, the weighted
 // latent sum and the value map) with one launch.
 //
-// One CTA per (head, sequence), eight warps. Inputs per sequence: the fused
+// One CTA per (head, sequence), sixteen warps. Inputs per sequence: the fused
 // projection row [q (heads x (nope + rope)) | c_kv (rank) | k_pe (rope)] of
 // this step, its position P; the latent cache [B, max_len, rank + rope]. The
 // CTA:
@@ -30,7 +30,7 @@
 
 namespace {
 
-constexpr int kMlaThreads = 256;
+constexpr int kMlaThreads = 512;
 constexpr int kMlaWarps = kMlaThreads / 32;
 constexpr int kRank = 512;
 constexpr int kRingRows = 32;    // rows per bulk-copied chunk
@@ -67,16 +67,15 @@ __device__ __forceinline__ Row16 load_row16(const __nv_bfloat16* row, int lane) 
   r.b = *reinterpret_cast<const uint4*>(row + 256 + 8 * lane);
   return r;
 }
-__device__ __forceinline__ void unpack16(const Row16& r, float (&v)[16]) {
+// ... as eight column pairs: v[i] holds columns col16(lane, 2i), col16(lane, 2i + 1)
+// (the arithmetic on them is packed fp32x2, two columns per instruction)
+__device__ __forceinline__ void unpack16(const Row16& r, float2 (&v)[8]) {
   const __nv_bfloat162* a = reinterpret_cast<const __nv_bfloat162*>(&r.a);
   const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&r.b);
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const float2 fa = __bfloat1622float2(a[i]), fb = __bfloat1622float2(b[i]);
-    v[2 * i] = fa.x;
-    v[2 * i + 1] = fa.y;
-    v[8 + 2 * i] = fb.x;
-    v[8 + 2 * i + 1] = fb.y;
+    v[i] = __bfloat1622float2(a[i]);
+    v[4 + i] = __bfloat1622float2(b[i]);
   }
 }
 __device__ __forceinline__ int col16(int lane, int i) {
@@ -102,6 +101,7 @@ __global__ void __launch_bounds__(kMlaThreads) mla_decode_kernel(
   float* wm = qn + nope;                   // [warps] running max per warp
   float* wl = wm + kMlaWarps;              // [warps] running sum per warp
   float* red = wl + kMlaWarps;             // [32]
+  int* slot_done = reinterpret_cast<int*>(red + 32);  // [slots] warps done with a slot
 
   // the chunk jobs, in consumption order: W_uk rows, cached rows 0..P-1,
   // W_uv rows
@@ -133,7 +133,10 @@ __global__ void __launch_bounds__(kMlaThreads) mla_decode_kernel(
     sl::bulk_load(ring + (j % kRingSlots) * kSlotBytes, src, bytes, bar);
   };
   if (tid == 0) {
-    for (int i = 0; i < kRingSlots; ++i) sl::mbar_init(&full[i], 1);
+    for (int i = 0; i < kRingSlots; ++i) {
+      sl::mbar_init(&full[i], 1);
+      slot_done[i] = 0;
+    }
     sl::fence_barrier_init();
     // the weights are constants of the step: their chunks may be fetched
     // before waiting on the kernel that wrote this step's projections
@@ -145,8 +148,23 @@ __global__ void __launch_bounds__(kMlaThreads) mla_decode_kernel(
   P = P < 0 ? 0 : (P >= max_len ? max_len - 1 : P);
   nc = (P + kRingRows - 1) / kRingRows;
   const int J = nk + nc + nv;
-  if (tid == 0)  // the rest of the first ring's chunks (fewer weight chunks than slots)
+  if (tid == 0) {
+    // the rest of the first ring's chunks (fewer weight chunks than slots)
     for (int j = min(nk, kRingSlots); j < min(J, kRingSlots); ++j) issue(j);
+    // everything the ring will fetch later is asked into L2 now, so those
+    // chunks land at L2 rather than DRAM latency
+    auto prefetch = [&](const void* src, size_t bytes) {
+      for (size_t o = 0; o < bytes; o += 65536) {
+        const uint32_t n = static_cast<uint32_t>(bytes - o < 65536 ? bytes - o : 65536);
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(
+                         reinterpret_cast<const uint8_t*>(src) + o),
+                     "r"(n)
+                     : "memory");
+      }
+    };
+    prefetch(cache + static_cast<size_t>(b) * max_len * dk, static_cast<size_t>(P) * dk * 2);
+    prefetch(w_uv + static_cast<size_t>(h) * vdim * kRank, static_cast<size_t>(vdim) * kRank * 2);
+  }
   const __nv_bfloat16* row = qkv + static_cast<size_t>(b) * ld_qkv;
   const __nv_bfloat16* qh = row + h * (nope + rope);
   const __nv_bfloat16* ckv = row + nh * (nope + rope);
@@ -176,25 +194,43 @@ __global__ void __launch_bounds__(kMlaThreads) mla_decode_kernel(
   __syncthreads();  // barriers initialised, kv / q rope / q_nope written
 
   const int rp = rope / 32;  // rope columns per lane
-  float acc[16];              // absorbed query, then the weighted latent
+  float2 acc[8];              // absorbed query, then the weighted latent
 #pragma unroll
-  for (int i = 0; i < 16; ++i) acc[i] = 0.f;
-  float qr[16], qp0 = 0.f, qp1 = 0.f;
+  for (int i = 0; i < 8; ++i) acc[i] = make_float2(0.f, 0.f);
+  float2 qr[8];
+  float qp0 = 0.f, qp1 = 0.f;
   float m_w = -INFINITY, l_w = 0.f;  // this warp's running max and sum
-  float o16[16];
+  float2 o16[8];
+  auto store_part = [&]() {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      part[warp * kRank + col16(lane, 2 * i)] = acc[i].x;
+      part[warp * kRank + col16(lane, 2 * i + 1)] = acc[i].y;
+    }
+  };
+  auto load_pairs = [&](const float* src, float2 (&d)[8]) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) d[i] = make_float2(src[col16(lane, 2 * i)], src[col16(lane, 2 * i + 1)]);
+  };
   // online softmax step of one row: score s, latent values v
-  auto absorb = [&](float s, const float (&v)[16]) {
+  auto absorb = [&](float s, const float2 (&v)[8]) {
     if (s > m_w) {
       const float corr = __expf(m_w - s);
       l_w *= corr;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) acc[i] *= corr;
+      for (int i = 0; i < 8; ++i) acc[i] = __fmul2_rn(make_float2(corr, corr), acc[i]);
       m_w = s;
     }
     const float pe = __expf(s - m_w);
     l_w += pe;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) acc[i] = fmaf(pe, v[i], acc[i]);
+    for (int i = 0; i < 8; ++i) acc[i] = __ffma2_rn(make_float2(pe, pe), v[i], acc[i]);
+  };
+  auto dot = [&](const float2 (&v)[8]) {
+    float2 t = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t = __ffma2_rn(qr[i], v[i], t);
+    return t.x + t.y;
   };
 
   for (int j = 0; j < J; ++j) {
@@ -202,38 +238,15 @@ __global__ void __launch_bounds__(kMlaThreads) mla_decode_kernel(
     const uint8_t* slot = ring + (j % kRingSlots) * kSlotBytes;
     if (j < nk) {
       // 2. absorbed query: q_lat[c] += q_nope[d] W_uk[h][d][c] over this
-      // chunk's rows (warp w: rows w, w + 8, ...)
+      // chunk's rows (warp w: rows w, w + 16, ...)
       const int d0 = j * kRingRows;
       const int rows = min(kRingRows, nope - d0);
       for (int rr = warp; rr < rows; rr += kMlaWarps) {
-        float v[16];
+        float2 v[8];
         unpack16(load_row16(reinterpret_cast<const __nv_bfloat16*>(slot) + rr * kRank, lane), v);
         const float qd = qn[d0 + rr];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) acc[i] = fmaf(qd, v[i], acc[i]);
-      }
-      if (j == nk - 1) {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) part[warp * kRank + col16(lane, i)] = acc[i];
-        __syncthreads();
-        for (int c = tid; c < kRank; c += blockDim.x) {
-          float t = 0.f;
-#pragma unroll
-          for (int w = 0; w < kMlaWarps; ++w) t += part[w * kRank + c];
-          q[c] = sl::bf16_round(t);
-        }
-        if (h == 0) {
-          __nv_bfloat16* dst = cache + (static_cast<size_t>(b) * max_len + P) * dk;
-          for (int i = tid; i < dk; i += blockDim.x) dst[i] = __float2bfloat16(kv[i]);
-        }
-        __syncthreads();
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          qr[i] = q[col16(lane, i)];
-          acc[i] = 0.f;
-        }
-        qp0 = rp > 0 ? q[kRank + lane * rp] : 0.f;
-        qp1 = rp > 1 ? q[kRank + lane * rp + 1] : 0.f;
+        for (int i = 0; i < 8; ++i) acc[i] = __ffma2_rn(make_float2(qd, qd), v[i], acc[i]);
       }
     } else if (j < nk + nc) {
       // 3. scores and the weighted latent of this chunk's cached rows
@@ -242,32 +255,77 @@ __global__ void __launch_bounds__(kMlaThreads) mla_decode_kernel(
       const __nv_bfloat16* base = reinterpret_cast<const __nv_bfloat16*>(slot);
       for (int rr = warp; rr < rows; rr += kMlaWarps) {
         const __nv_bfloat16* key = base + rr * dk;
-        float v[16];
+        float2 v[8];
         unpack16(load_row16(key, lane), v);
-        float sdot = 0.f;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) sdot = fmaf(qr[i], v[i], sdot);
+        float sdot = dot(v);
         if (rp > 0) sdot = fmaf(qp0, __bfloat162float(key[kRank + lane * rp]), sdot);
         if (rp > 1) sdot = fmaf(qp1, __bfloat162float(key[kRank + lane * rp + 1]), sdot);
         absorb(warp_sum(sdot) * scale, v);
       }
+    } else {
+      // 4. value map: out[d] = sum_c o_lat[c] W_uv[h][d][c] (warp w: rows
+      // w, w + 16, ... of this chunk)
+      const int d0 = (j - nk - nc) * kRingRows;
+      const int rows = min(kRingRows, vdim - d0);
+      __nv_bfloat16* dst = out + static_cast<size_t>(b) * nh * vdim + h * vdim;
+      for (int rr = warp; rr < rows; rr += kMlaWarps) {
+        float2 v[8];
+        unpack16(load_row16(reinterpret_cast<const __nv_bfloat16*>(slot) + rr * kRank, lane), v);
+        float2 t2 = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) t2 = __ffma2_rn(o16[i], v[i], t2);
+        const float t = warp_sum(t2.x + t2.y);
+        if (lane == 0) dst[d0 + rr] = __float2bfloat16(t);
+      }
     }
-    if (j == nk + nc - 1 || (nc == 0 && j == nk - 1)) {
+    // this warp is done with the slot: the last warp to finish refills it,
+    // so the warps do not wait for one another between chunks
+    __syncwarp();
+    if (lane == 0) {
+      __threadfence_block();
+      const int si = j % kRingSlots;
+      if (atomicAdd(&slot_done[si], 1) == kMlaWarps - 1) {
+        slot_done[si] = 0;
+        if (j + kRingSlots < J) {
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          issue(j + kRingSlots);
+        }
+      }
+    }
+    if (j == nk - 1) {
+      // the absorbed query from the warps' partial sums; CTA head 0 writes
+      // position P's row to the cache
+      store_part();
+      __syncthreads();
+      for (int c = tid; c < kRank; c += blockDim.x) {
+        float t = 0.f;
+#pragma unroll
+        for (int w = 0; w < kMlaWarps; ++w) t += part[w * kRank + c];
+        q[c] = sl::bf16_round(t);
+      }
+      if (h == 0) {
+        __nv_bfloat16* dst = cache + (static_cast<size_t>(b) * max_len + P) * dk;
+        for (int i = tid; i < dk; i += blockDim.x) dst[i] = __float2bfloat16(kv[i]);
+      }
+      __syncthreads();
+      load_pairs(q, qr);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = make_float2(0.f, 0.f);
+      qp0 = rp > 0 ? q[kRank + lane * rp] : 0.f;
+      qp1 = rp > 1 ? q[kRank + lane * rp + 1] : 0.f;
+    }
+    if (j == nk + nc - 1) {
       // position P from this CTA's own copy of the new row (warp 0), then
-      // the warps' running sums merged
+      // the warps' running sums merged into the weighted latent
       if (warp == 0) {
-        float v[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = kv[col16(lane, i)];
-        float sdot = 0.f;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) sdot = fmaf(qr[i], v[i], sdot);
+        float2 v[8];
+        load_pairs(kv, v);
+        float sdot = dot(v);
         if (rp > 0) sdot = fmaf(qp0, kv[kRank + lane * rp], sdot);
         if (rp > 1) sdot = fmaf(qp1, kv[kRank + lane * rp + 1], sdot);
         absorb(warp_sum(sdot) * scale, v);
       }
-#pragma unroll
-      for (int i = 0; i < 16; ++i) part[warp * kRank + col16(lane, i)] = acc[i];
+      store_part();
       if (lane == 0) {
         wm[warp] = m_w;
         wl[warp] = l_w;
@@ -290,29 +348,7 @@ __global__ void __launch_bounds__(kMlaThreads) mla_decode_kernel(
         q[c] = sl::bf16_round(t * invL);  // the query is no longer needed
       }
       __syncthreads();
-#pragma unroll
-      for (int i = 0; i < 16; ++i) o16[i] = q[col16(lane, i)];
-    }
-    if (j >= nk + nc) {
-      // 4. value map: out[d] = sum_c o_lat[c] W_uv[h][d][c] (warp w: rows
-      // w, w + 8, ... of this chunk)
-      const int d0 = (j - nk - nc) * kRingRows;
-      const int rows = min(kRingRows, vdim - d0);
-      __nv_bfloat16* dst = out + static_cast<size_t>(b) * nh * vdim + h * vdim;
-      for (int rr = warp; rr < rows; rr += kMlaWarps) {
-        float v[16];
-        unpack16(load_row16(reinterpret_cast<const __nv_bfloat16*>(slot) + rr * kRank, lane), v);
-        float t = 0.f;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) t = fmaf(o16[i], v[i], t);
-        t = warp_sum(t);
-        if (lane == 0) dst[d0 + rr] = __float2bfloat16(t);
-      }
-    }
-    __syncthreads();  // every warp is done with the slot
-    if (tid == 0 && j + kRingSlots < J) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      issue(j + kRingSlots);
+      load_pairs(q, o16);
     }
   }
 }
@@ -415,7 +451,7 @@ extern "C" int sl_mla_decode(const void* qkv, int ld_qkv, const void* kv_norm, f
     return SL_ERR_INVALID;
   const size_t smem = static_cast<size_t>(kRingSlots) * kSlotBytes + kRingSlots * 8 +
       sizeof(float) * (2 * static_cast<size_t>(rank + rope) + kMlaWarps * kRank + nope +
-                       2 * kMlaWarps + 32);
+                       2 * kMlaWarps + 32) + sizeof(int) * kRingSlots;
   if (smem > 220 * 1024 || B > 65535) return SL_ERR_UNSUPPORTED;
   static std::atomic<uint64_t> smem_set{0};
   if (smem > 48 * 1024) SL_CUDA_TRY(sl::ensure_smem_limit(mla_decode_kernel, static_cast<int>(smem), smem_set));
