@@ -566,6 +566,14 @@ def layer_launches(cfg, tokens, world, slots, exchange="nvlink", no_overlap=Fals
     return 2 + 2 + (align + 3 if no_overlap else align + 5) + ex
 
 
+def harness_launches(num_layers, tokens) -> int:
+    """This build's kernels per decode step in the decoder harness around the
+    MoE layers: the first RMSNorm, then per layer the MLA attention kernel
+    and two residual add + RMSNorm kernels, and for one or two rows the q/kv
+    and output projections (cuBLAS, not counted, above that)."""
+    return 1 + num_layers * (3 + (2 if tokens <= 2 else 0))
+
+
 def _stack_save(stack):
     """Device copies of every offloaded layer's planner state, map and slots,
     or None when they would not fit in 80% of free HBM."""
@@ -986,6 +994,8 @@ def run_sluice(a):
                          f"reference arm"}
 
     launches = K * layers * layer_launches(cfg, T, world, slots, a.exchange, a.no_overlap)
+    if a.workload == "decoder":
+        launches += K * harness_launches(_decoder_cfg(a).num_layers, T)
     if a.prefetch and offloaded and world == 1 and not a.no_overlap:
         # each layer but the last: the next router (gate + select), the
         # prefetch planner and its stream

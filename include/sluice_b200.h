@@ -425,6 +425,14 @@ int sl_mla_decode(const void* qkv, int ld_qkv, const void* kv_norm, float eps,
 int sl_add_rmsnorm(void* h, const void* delta, const void* w, float eps, void* out, int rows,
                    int H, sl_stream_t stream);
 
+/* Not part of the reference's MoE operator surface: the projections of the
+ * decoder in this build's benchmark harness for single-sequence decode. y
+ * bf16 [T, N] = x bf16 [T, K] times w bf16 [N, K] transposed, fp32 sums; T <= 4,
+ * K a multiple of 8 with T * K * 2 bytes <= 200 KB; x and w 16-byte
+ * aligned. */
+int sl_linear_small(const void* x, int T, int K, const void* w, int N, void* y,
+                    sl_stream_t stream);
+
 /* sl_fused_experts without any device allocation. No counterpart in the
  * reference: it serves callers that cannot allocate device scratch memory for
  * a call -- a host program binding this C ABI directly (cgo, JNI, ctypes

@@ -100,6 +100,7 @@ _SIGNATURES = {
     "sl_fused_experts_noalloc": (_i, [_vp, _i, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _i,
                                       _vp, _i, _vp, _vp, _i, _f, _vp, _vp, _vp]),
     "sl_add_rmsnorm": (_i, [_vp, _vp, _vp, _f, _vp, _i, _i, _vp]),
+    "sl_linear_small": (_i, [_vp, _i, _i, _vp, _i, _vp, _vp]),
     "sl_mla_decode": (_i, [_vp, _i, _vp, _f, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i,
                            _i, _i, _f, _vp, _vp]),
 }

@@ -413,7 +413,94 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(
   }
 }
 
+// Skinny linear for single-sequence decode (T <= 4 rows): y[T, N] =
+// x[T, K] W[N, K]^T (bf16 in and out, fp32 sums). The token rows sit in
+// shared memory; each warp streams one weight row with 16-byte loads (eight
+// in flight per lane) and keeps its lane's T partial sums in registers. A
+// warp's first weight loads are issued before waiting on the kernel that
+// wrote x. (From about 8 rows on, cuBLAS's tensor-core kernels are faster.)
+constexpr int kLinThreads = 256;
+constexpr int kLinMaxT = 4;
+constexpr int kLinUnroll = 8;
+
+__global__ void __launch_bounds__(kLinThreads) linear_small_kernel(
+    const __nv_bfloat16* __restrict__ x, int T, int K, const __nv_bfloat16* __restrict__ w, int N,
+    __nv_bfloat16* __restrict__ y) {
+  extern __shared__ uint4 xs[];  // [T][K / 8]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int kv = K >> 3;
+  const int row = blockIdx.x * (kLinThreads / 32) + warp;
+  const uint4* wr = reinterpret_cast<const uint4*>(w) + static_cast<size_t>(row < N ? row : 0) * kv;
+  uint4 wb[kLinUnroll];
+#pragma unroll
+  for (int u = 0; u < kLinUnroll; ++u) {
+    const int v = lane + 32 * u;
+    if (row < N && v < kv) wb[u] = __ldg(wr + v);
+  }
+  sl::pdl_wait();
+  sl::pdl_trigger();
+  const uint4* xg = reinterpret_cast<const uint4*>(x);
+  for (int i = threadIdx.x; i < T * kv; i += blockDim.x) xs[i] = xg[i];
+  __syncthreads();
+  if (row >= N) return;
+  float2 acc[kLinMaxT];
+#pragma unroll
+  for (int t = 0; t < kLinMaxT; ++t) acc[t] = make_float2(0.f, 0.f);
+  for (int v0 = 0; v0 < kv; v0 += 32 * kLinUnroll) {
+    if (v0 > 0) {
+#pragma unroll
+      for (int u = 0; u < kLinUnroll; ++u) {
+        const int v = v0 + lane + 32 * u;
+        if (v < kv) wb[u] = __ldg(wr + v);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kLinUnroll; ++u) {
+      const int v = v0 + lane + 32 * u;
+      if (v >= kv) break;
+      const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wb[u]);
+      float2 wf[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) wf[i] = __bfloat1622float2(w2[i]);
+#pragma unroll
+      for (int t = 0; t < kLinMaxT; ++t) {
+        if (t >= T) break;
+        const uint4 xv = xs[t * kv + v];
+        const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&xv);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[t] = __ffma2_rn(wf[i], __bfloat1622float2(x2[i]), acc[t]);
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < kLinMaxT; ++t) {
+    if (t >= T) break;
+    const float sum = warp_sum(acc[t].x + acc[t].y);
+    if (lane == 0) y[static_cast<size_t>(t) * N + row] = __float2bfloat16(sum);
+  }
+}
+
 }  // namespace
+
+extern "C" int sl_linear_small(const void* x, int T, int K, const void* w, int N, void* y,
+                               sl_stream_t stream) {
+  if (T < 0 || T > kLinMaxT || K <= 0 || K % 8 || N <= 0) return SL_ERR_INVALID;
+  if (T == 0) return SL_OK;
+  if (!x || !w || !y) return SL_ERR_INVALID;
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15) return SL_ERR_INVALID;
+  const size_t smem = static_cast<size_t>(T) * K * 2;
+  if (smem > 200 * 1024) return SL_ERR_UNSUPPORTED;
+  static std::atomic<uint64_t> smem_set{0};
+  if (smem > 48 * 1024)
+    SL_CUDA_TRY(sl::ensure_smem_limit(linear_small_kernel, 200 * 1024, smem_set));
+  const int rows_per_cta = kLinThreads / 32;
+  SL_CUDA_TRY(sl::launch(linear_small_kernel, dim3((N + rows_per_cta - 1) / rows_per_cta),
+                         dim3(kLinThreads), smem, reinterpret_cast<cudaStream_t>(stream),
+                         static_cast<const __nv_bfloat16*>(x), T, K,
+                         static_cast<const __nv_bfloat16*>(w), N,
+                         static_cast<__nv_bfloat16*>(y)));
+  return SL_OK;
+}
 
 extern "C" int sl_add_rmsnorm(void* h, const void* delta, const void* w, float eps, void* out,
                               int rows, int H, sl_stream_t stream) {

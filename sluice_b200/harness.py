@@ -153,7 +153,7 @@ class DecoderHarness:
         cfg, lw = self.cfg, self.layers[li]
         B, nh, R = x.shape[0], cfg.num_heads, cfg.kv_lora_rank
         dq = cfg.qk_nope + cfg.qk_rope
-        qkv = F.linear(x, lw["wqkv"])
+        qkv = self._linear(x, lw["wqkv"])
         if self.fused_attention:
             from ._lib import check, lib, ptr
             o = torch.empty(B, nh * cfg.v_head, dtype=x.dtype, device=x.device)
@@ -163,7 +163,7 @@ class DecoderHarness:
                                       cfg.qk_rope, R, cfg.v_head, self.max_len, self.scale,
                                       ptr(o), torch.cuda.current_stream().cuda_stream),
                   "sl_mla_decode")
-            return F.linear(o, lw["wo"])
+            return self._linear(o, lw["wo"])
         q = qkv[:, :nh * dq].view(B, nh, dq)
         kv = qkv[:, nh * dq:]
         c = _rms(kv[:, :R], lw["kv_norm"], cfg.rms_eps)
@@ -178,6 +178,20 @@ class DecoderHarness:
         o_lat = torch.bmm(p, cl[..., :R])                                     # [B, nh, R]
         o = torch.bmm(o_lat.transpose(0, 1), lw["w_uv_t"])                   # [nh, B, v]
         return F.linear(o.transpose(0, 1).reshape(B, nh * cfg.v_head), lw["wo"])
+
+    def _linear(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        """x @ w.T: the library's skinny linear (``sl_linear_small``) for
+        one or two rows on the device (faster than cuBLAS there), else
+        PyTorch's (cuBLAS)."""
+        if self.fused_attention and x.shape[0] <= 2 and x.shape[1] * x.shape[0] * 2 <= 200 * 1024:
+            from ._lib import check, lib, ptr
+            x = x.contiguous()
+            y = torch.empty(x.shape[0], w.shape[0], dtype=x.dtype, device=x.device)
+            check(lib().sl_linear_small(ptr(x), x.shape[0], x.shape[1], ptr(w), w.shape[0],
+                                        ptr(y), torch.cuda.current_stream().cuda_stream),
+                  "sl_linear_small")
+            return y
+        return F.linear(x, w)
 
     def _add_norm(self, h: torch.Tensor, delta: torch.Tensor | None,
                   w: torch.Tensor) -> torch.Tensor:

@@ -108,3 +108,22 @@ def test_fused_add_rmsnorm_matches_pytorch():
         torch.cuda.synchronize()
         ref2 = torch.nn.functional.rms_norm(h, (H,), w, 1e-6)
         assert ((plain.float() - ref2.float()).abs() <= 1e-2 * ref2.float().abs() + 1e-2).all()
+
+
+def test_skinny_linear_matches_pytorch():
+    """sl_linear_small (the harness's decode-batch projections) against an
+    fp32 product of the same bf16 operands, within one bf16 rounding."""
+    from sluice_b200._lib import check, lib, ptr
+
+    g = torch.Generator(device="cuda").manual_seed(13)
+    for T, K, N in ((1, 2048, 3648), (2, 2048, 2048), (1, 2048, 100), (4, 4096, 301),
+                    (3, 10944, 64), (4, 520, 7)):
+        x = torch.randn(T, K, device="cuda", generator=g).to(torch.bfloat16)
+        w = (torch.randn(N, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+        y = torch.empty(T, N, dtype=torch.bfloat16, device="cuda")
+        check(lib().sl_linear_small(ptr(x), T, K, ptr(w), N, ptr(y),
+                                    torch.cuda.current_stream().cuda_stream), "sl_linear_small")
+        torch.cuda.synchronize()
+        ref = x.float() @ w.float().t()
+        err = (y.float() - ref).abs()
+        assert (err <= 1e-2 * ref.abs() + 1e-2 * ref.abs().max()).all(), (T, K, N, err.max().item())

@@ -230,6 +230,10 @@ def test_bench_launch_count_rule():
     assert bench.layer_launches(V2, 8, 1, 48, no_overlap=True) == 8
     assert bench.layer_launches(V2, 8, 2, 48) == 8
     assert bench.layer_launches(V2, 8, 2, 48, exchange="nccl") == 6
+    # the decoder harness's own kernels: first RMSNorm, per layer MLA + two
+    # add + RMSNorm, plus the two projections for one or two rows
+    assert bench.harness_launches(27, 8) == 1 + 27 * 3
+    assert bench.harness_launches(27, 1) == 1 + 27 * 5
     assert bench.layer_launches(V3, 8, 8, 128) == 9
     mw = max_waves_for(48, 64, 24, 0)
     assert bench.layer_launches(V2, 512, 1, 48, decode=False) == 2 + 1 + mw + 7 + \
