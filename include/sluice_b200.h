@@ -60,8 +60,8 @@ int sl_device_sm_count(void);
  * num_expert_group/topk_group group mask (1/1 = no grouping); top-k with
  * ties to the lower id; optional renormalisation; routed_scaling_factor.
  * Outputs are ordered by selection score descending, id ascending.
- * scoring: 0 = softmax, 1 = sigmoid. router_logits_out (bf16 [T,E]) may be
- * NULL. Limits: E % 32 == 0, E <= 512, H % 8 == 0, topk <= 32. */
+ * scoring: 0 = softmax, 1 = sigmoid. router_logits_out (bf16 [T,E]) receives
+ * the logits. Limits: E % 32 == 0, E <= 512, H % 8 == 0, topk <= 32. */
 int sl_route(const void* hidden, const void* gate_w, const float* logit_bias,
              int T, int H, int E, int topk, int scoring, int num_expert_group,
              int topk_group, int renormalize, float routed_scaling_factor,
