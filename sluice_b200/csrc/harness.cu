@@ -1,10 +1,12 @@
-// Decoder-harness kernel: the absorbed multi-head latent attention (MLA) of
-// one decode step, for the DeepSeek-V2-Lite-shaped decoder that wraps the MoE
-// layers in the benchmark. It is not part of the reference's MoE operator
-// surface; it replaces a dozen small PyTorch kernels per layer (norm, rotary
-// embedding, cache write, the absorbed query, scores, softmax, the weighted
-// latent sum and the value map) with one launch.
+// Decoder-harness kernels for the DeepSeek-V2-Lite-shaped decoder that wraps
+// the MoE layers in the benchmark (not part of the reference's MoE operator
+// surface): the absorbed multi-head latent attention (MLA) of one decode step
+// in one launch (it replaces a dozen small PyTorch kernels per layer: norm,
+// rotary embedding, cache write, the absorbed query, scores, softmax, the
+// weighted latent sum and the value map), the residual add + RMSNorm, and a
+// skinny linear for single-sequence projections.
 //
+// MLA:
 // One CTA per (head, sequence), sixteen warps. Inputs per sequence: the fused
 // projection row [q (heads x (nope + rope)) | c_kv (rank) | k_pe (rope)] of
 // this step, its position P; the latent cache [B, max_len, rank + rope]. The

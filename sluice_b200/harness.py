@@ -7,11 +7,15 @@ decoder layers of [RMSNorm -> multi-head latent attention -> residual ->
 RMSNorm -> FFN -> residual] with a dense SwiGLU FFN in layer 0 and an MoE
 layer elsewhere, final RMSNorm, the vocabulary head and greedy sampling.
 
-Only the MoE layers are this package's kernels (``SluiceMoELayer``: router,
-device slot planner, expert streamer, tcgen05 fused experts). Everything
-else is plain PyTorch (cuBLAS GEMMs): it is the harness around the hot path,
-not part of it. The same module runs on the host for the CPU baseline, with
-the MoE layers replaced by the oracle's torch-native MoE and slot policy.
+The MoE layers are this package's hot path (``SluiceMoELayer``: router,
+device slot planner, expert streamer, tcgen05 fused experts). Around them,
+on a CUDA device, the attention core, each residual add + RMSNorm and (for
+one or two sequences) the projections are also this package's kernels
+(``sl_mla_decode``, ``sl_add_rmsnorm``, ``sl_linear_small``); the rest is
+PyTorch (cuBLAS GEMMs): it is the harness around the hot path, not part of
+it. The same module runs on the host for the CPU baseline, with PyTorch ops
+throughout and the MoE layers replaced by the oracle's torch-native MoE and
+slot policy.
 
 Attention is decode-only MLA in its absorbed form over a compressed cache
 (kv_lora_rank 512 latent + 64 rotary dims per token and layer): per token
@@ -22,7 +26,8 @@ shapes, masked beyond the sequence's length, so a step captures in one CUDA
 graph); the output is ``softmax . c_kv`` projected through ``W_uv`` and the
 output projection. Prompt tokens are fed through the same decode step, one
 position per step. Rotary embedding: RoPE (theta 10000) on adjacent dim
-pairs. The causal mask is an additive bias folded into the score GEMM.
+pairs. In the PyTorch form the causal mask is an additive bias folded into
+the score GEMM; the fused kernel reads each sequence's positions 0..P.
 """
 
 from __future__ import annotations
