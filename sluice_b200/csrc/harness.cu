@@ -236,6 +236,8 @@ __global__ void __launch_bounds__(kMlaThreads) mla_decode_kernel(
   };
 
   for (int j = 0; j < J; ++j) {
+    // a chunk is a bulk copy of this GPU's own memory, which always lands;
+    // the wait is bounded (2 s) only so that no fault elsewhere can hang it
     (void)sl::mbar_wait(&full[j % kRingSlots], (j / kRingSlots) & 1);
     const uint8_t* slot = ring + (j % kRingSlots) * kSlotBytes;
     if (j < nk) {
