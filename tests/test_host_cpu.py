@@ -89,6 +89,20 @@ def test_host_calls_reject_bad_arguments_without_a_gpu():
     assert L.sl_fused_experts_ex(None, 4, 2048, 1408, ctypes.byref(w), None, None, 2, None, 0,
                                  1.0, 0, -1, None, -1, 0, None, None, 0, None) \
         == _lib.SL_ERR_INVALID
+    # the decoder harness's kernels: shapes outside their lane layouts and
+    # missing buffers are refused before any CUDA call
+    mla = lambda rank, rope: L.sl_mla_decode(None, 16 * 192 + rank + rope, None, 1e-6, None,
+                                             None, None, None, None, 8, 16, 128, rope, rank,
+                                             128, 384, 0.07, None, None)
+    assert mla(256, 64) == _lib.SL_ERR_UNSUPPORTED     # the latent width is fixed at 512
+    assert mla(512, 48) == _lib.SL_ERR_UNSUPPORTED     # rope a multiple of 32, at most 64
+    assert mla(512, 64) == _lib.SL_ERR_INVALID         # null buffers
+    assert L.sl_add_rmsnorm(None, None, None, 1e-6, None, 8, 2044, None) == _lib.SL_ERR_INVALID
+    assert L.sl_add_rmsnorm(None, None, None, 1e-6, None, 8, 16384, None) == _lib.SL_ERR_INVALID
+    assert L.sl_add_rmsnorm(None, None, None, 1e-6, None, 0, 2048, None) == _lib.SL_OK
+    assert L.sl_linear_small(None, 5, 2048, None, 64, None, None) == _lib.SL_ERR_INVALID
+    assert L.sl_linear_small(None, 1, 2044, None, 64, None, None) == _lib.SL_ERR_INVALID
+    assert L.sl_linear_small(None, 0, 2048, None, 64, None, None) == _lib.SL_OK
 
 
 @pytest.mark.parametrize("S,frac", [(48, 0.5), (48, 0.0), (48, 0.95), (1, 0.5), (96, 0.9)])
