@@ -1276,15 +1276,18 @@ __global__ void __launch_bounds__(F8Cfg<BN, GATED>::kThreads, 1) moe_gemm_f8_ker
 // swiglu_quant_kernel applies vLLM's SiLU-and-mul chain and quantises per
 // 128-column group), so a tile keeps one accumulator per (row, token).
 // Roles: warp 0 TMA producer, warp 1 MMA issuer + TMEM owner, warps 2..13
-// promotion: four lane quadrants x three groups of 64 token columns; a warp
-// whose columns hold no token of the item only releases the buffers. 14
+// promotion: four lane quadrants x three column groups; group g owns the
+// 16-column chunks g, g+3, g+6, g+9, so an item of n tokens costs each warp
+// at most ceil(n/48) TMEM round trips per K block (a warp whose chunks hold
+// no token of the item only releases the buffers). 14
 // warps keep four per SM sub-partition, so a thread may hold 128 registers
 // (64 fp32 accumulators plus one 16-column TMEM load).
 // The token tile is loaded as 32-row boxes, only those that hold tokens.
 constexpr int F8W_BN = 192;
 static_assert(F8W_BN == kF8WideBN, "wide fp8 token tile");
 constexpr int F8W_CW = 64;                             // token columns per promotion warp
-constexpr int F8W_NP = 4 * (F8W_BN / F8W_CW);
+constexpr int F8W_NG = F8W_BN / F8W_CW;                // column groups (chunk stride)
+constexpr int F8W_NP = 4 * F8W_NG;
 constexpr int F8W_THREADS = 64 + 32 * F8W_NP;
 constexpr int F8W_ABYTES = 128 * F8_BK;                // one 128x128 e4m3 weight tile
 constexpr int F8W_BBYTES = F8W_BN * F8_BK;             // up to 192 token rows
@@ -1441,7 +1444,7 @@ __global__ void __launch_bounds__(F8W_THREADS, 1) moe_gemm_f8w_kernel(
   } else {
     // ------------------------------------------- promotion and epilogue
     const int q = warp & 3;               // TMEM lane quadrant of this warp
-    const int c0 = ((warp - 2) >> 2) * CW;  // first token column of this warp
+    const int c0 = ((warp - 2) >> 2) * 16;  // first token column of this warp
     const int row = q * 32 + lane;        // weight row within the 128-row tile
     int s = 0, b = 0;
     uint32_t ph = 0, bph = 0;
@@ -1453,12 +1456,14 @@ __global__ void __launch_bounds__(F8W_THREADS, 1) moe_gemm_f8w_kernel(
       const int e = sh ? it.x - S : it.x;
       const float* sc = (sh ? wsh_scale : w_scale) +
                         (static_cast<size_t>(e) * m_tiles + mt) * kscale;
-      const int ncol = it.z - c0;  // token columns of this warp (<= 0: none)
+      const int ncol = it.z - c0;  // <= 0: no chunk of this warp holds a token
       float2 acc[CW / 2];
 #pragma unroll
       for (int i = 0; i < CW / 2; ++i) acc[i] = make_float2(0.f, 0.f);
+      float wsk_next = __ldg(sc);  // weight block scales, one K block ahead
       for (int kb = 0; kb < k_blocks; ++kb) {
-        const float wsk = __ldg(sc + kb);  // weight block scale of this K block
+        const float wsk = wsk_next;  // weight block scale of this K block
+        if (kb + 1 < k_blocks) wsk_next = __ldg(sc + kb + 1);
         ok = ok && !*abort_flag && sl::mbar_wait(&tfull[b], bph) && sl::mbar_wait(&full[s], ph);
         if (ok && ncol > 0) {
           sl::tc_fence_after();
@@ -1466,7 +1471,8 @@ __global__ void __launch_bounds__(F8W_THREADS, 1) moe_gemm_f8w_kernel(
                                  (static_cast<uint32_t>(q * 32) << 16) + c0;
           const float* ts = sS + s * F8W_BN + c0;
 #pragma unroll
-          for (int cc = 0; cc < CW; cc += 16) {
+          for (int j = 0; j < CW / 16; ++j) {
+            const int cc = j * 16 * F8W_NG;  // chunk j of this warp: columns c0 + cc ..
             if (cc < ncol) {
               uint32_t v[16];
               sl::tmem_ld16_nowait(taddr + cc, v);
@@ -1477,12 +1483,12 @@ __global__ void __launch_bounds__(F8W_THREADS, 1) moe_gemm_f8w_kernel(
                 const float4 t4 = *reinterpret_cast<const float4*>(ts + cc + 2 * i);
                 const float2 c01 = __fmul2_rn(make_float2(wsk, wsk), make_float2(t4.x, t4.y));
                 const float2 c23 = __fmul2_rn(make_float2(wsk, wsk), make_float2(t4.z, t4.w));
-                acc[cc / 2 + i] = __ffma2_rn(
+                acc[j * 8 + i] = __ffma2_rn(
                     make_float2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])), c01,
-                    acc[cc / 2 + i]);
-                acc[cc / 2 + i + 1] = __ffma2_rn(
+                    acc[j * 8 + i]);
+                acc[j * 8 + i + 1] = __ffma2_rn(
                     make_float2(__uint_as_float(v[2 * i + 2]), __uint_as_float(v[2 * i + 3])),
-                    c23, acc[cc / 2 + i + 1]);
+                    c23, acc[j * 8 + i + 1]);
               }
             }
           }
@@ -1510,9 +1516,10 @@ __global__ void __launch_bounds__(F8W_THREADS, 1) moe_gemm_f8w_kernel(
         __nv_bfloat16* dst = out + static_cast<size_t>(it.y + c0) * M_total + mt * 128 + row;
 #pragma unroll
         for (int i = 0; i < CW / 2; ++i) {
-          if (2 * i < ncol) dst[static_cast<size_t>(2 * i) * M_total] = __float2bfloat16(acc[i].x);
-          if (2 * i + 1 < ncol)
-            dst[static_cast<size_t>(2 * i + 1) * M_total] = __float2bfloat16(acc[i].y);
+          const int col = (i >> 3) * 16 * F8W_NG + 2 * (i & 7);  // column of acc[i].x - c0
+          if (col < ncol) dst[static_cast<size_t>(col) * M_total] = __float2bfloat16(acc[i].x);
+          if (col + 1 < ncol)
+            dst[static_cast<size_t>(col + 1) * M_total] = __float2bfloat16(acc[i].y);
         }
       }
     }
