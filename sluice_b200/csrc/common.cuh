@@ -231,6 +231,12 @@ __device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[16]) {
                : "memory");
 }
 
+// Ask L2 for `bytes` (a multiple of 16) of global memory from `src`
+// (16-byte aligned); no completion to wait for.
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // 1-D bulk copy global -> shared (no multicast), completing on `bar`:
 // both addresses 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint32_t bytes,

@@ -568,7 +568,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(
     const __grid_constant__ CUtensorMap tm_b, const int32_t* __restrict__ ws_hdr,
     const int4* __restrict__ items, __nv_bfloat16* __restrict__ out, int S, int K,
     int M_total /* rows of one expert's weight block in this GEMM's view */,
-    int out_ld, int32_t* __restrict__ status, int phase) {
+    int out_ld, int32_t* __restrict__ status, int phase,
+    const uint8_t* __restrict__ w_raw, const uint8_t* __restrict__ wsh_raw) {
   using Cfg = GemmCfg<BN, STAGES, GATED>;
   using TS = TileShape<BN, GATED>;
   extern __shared__ uint8_t smem_raw[];
@@ -648,6 +649,18 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(
       bool waited = GATED;
       int pend_n = 0;
       int pend_stage[STAGES], pend_kb[STAGES], pend_row[STAGES];
+      if constexpr (!GATED) {
+        // While the gate/up GEMM finishes, ask L2 for this CTA's first tile:
+        // its 128 weight rows over all of K are one contiguous range.
+        const int4 it = items[item_lo + blockIdx.x / m_tiles];
+        const int e = it.x >= S ? it.x - S : it.x;
+        const uint8_t* src = (it.x >= S ? wsh_raw : w_raw) +
+                             (static_cast<size_t>(e) * M_total + (blockIdx.x % m_tiles) * BM) *
+                                 static_cast<size_t>(K) * 2;
+        const size_t bytes = static_cast<size_t>(BM) * K * 2;
+        for (size_t o = 0; o < bytes; o += 65536)
+          sl::prefetch_l2(src + o, static_cast<uint32_t>(bytes - o < 65536 ? bytes - o : 65536));
+      }
       auto flush = [&]() {
         sl::pdl_wait();
         sl::pdl_trigger();
@@ -1760,7 +1773,7 @@ template <int BN, int STAGES, bool GATED>
 int launch_gemm(const CUtensorMap& tw, const CUtensorMap& twsh, const CUtensorMap& tb,
                 const int32_t* hdr, const int4* items, __nv_bfloat16* out, int S, int K,
                 int M_total, int out_ld, int32_t* status, int max_items, cudaStream_t st,
-                int phase) {
+                int phase, const void* w_raw, const void* wsh_raw) {
   using Cfg = GemmCfg<BN, STAGES, GATED>;
   auto kern = moe_gemm_kernel<BN, STAGES, GATED>;
   static std::atomic<uint64_t> smem_set{0};
@@ -1770,7 +1783,9 @@ int launch_gemm(const CUtensorMap& tw, const CUtensorMap& twsh, const CUtensorMa
   if (grid <= 0) return SL_ERR_CUDA;
   if (max_tiles < grid) grid = max_tiles > 0 ? max_tiles : 1;
   SL_CUDA_TRY(sl::launch(kern, dim3(grid), dim3(kThreads), Cfg::kSmemBytes, st, tw, twsh, tb,
-                         hdr, items, out, S, K, M_total, out_ld, status, phase));
+                         hdr, items, out, S, K, M_total, out_ld, status, phase,
+                         static_cast<const uint8_t*>(w_raw),
+                         static_cast<const uint8_t*>(wsh_raw ? wsh_raw : w_raw)));
   return SL_OK;
 }
 
@@ -1915,10 +1930,10 @@ int run_fused(const void* hidden, int T, int H, int I, const sl_expert_weights& 
   int rc = SL_OK;
 #define SL_GEMMS_BF16(BNV, S1, S2)                                                              \
   rc = launch_gemm<BNV, S1, true>(m_w13, m_w13sh, m_x, hdr, items, A, num_slots, H, I, I, hdr,   \
-                                  L.max_items, st, phase);                                       \
+                                  L.max_items, st, phase, w.w13, w.shared_w13);                  \
   if (rc == SL_OK)                                                                               \
     rc = launch_gemm<BNV, S2, false>(m_w2, m_w2sh, m_a, hdr, items, Z, num_slots, I, H, H, hdr,  \
-                                     L.max_items, st, phase);
+                                     L.max_items, st, phase, w.w2, w.shared_w2);
 #define SL_GEMMS_F8(BNV)                                                                         \
   rc = launch_gemm_f8<BNV, true>(m_w13, m_w13sh, m_x, Xs, w.w13_scale, w.shared_w13_scale, hdr,  \
                                  items, Aq, As, nullptr, num_slots, H, I, L.max_rows, hdr,      \
