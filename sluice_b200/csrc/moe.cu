@@ -933,7 +933,8 @@ __global__ void __launch_bounds__(F8Cfg<BN, GATED>::kThreads, 1) moe_gemm_f8_ker
     const float* __restrict__ w_scale, const float* __restrict__ wsh_scale,
     const int32_t* __restrict__ ws_hdr, const int4* __restrict__ items,
     uint8_t* __restrict__ out_q, float* __restrict__ out_s, __nv_bfloat16* __restrict__ out_z,
-    int S, int K, int M_total, int max_rows, int32_t* __restrict__ status, int phase) {
+    int S, int K, int M_total, int max_rows, int32_t* __restrict__ status, int phase,
+    const uint8_t* __restrict__ w_raw, const uint8_t* __restrict__ wsh_raw) {
   using Cfg = F8Cfg<BN, GATED>;
   constexpr int ST = Cfg::kStages;
   constexpr int NB = Cfg::kNB;
@@ -1009,6 +1010,18 @@ __global__ void __launch_bounds__(F8Cfg<BN, GATED>::kThreads, 1) moe_gemm_f8_ker
       bool waited = GATED;
       int pend_n = 0;
       int pend_s[ST], pend_kb[ST], pend_row[ST];
+      if constexpr (!GATED) {
+        // While the gate/up GEMM finishes, ask L2 for this CTA's first tile:
+        // its 128 e4m3 weight rows over all of K are one contiguous range.
+        const int4 it = items[item_lo + blockIdx.x / m_tiles];
+        const int e = it.x >= S ? it.x - S : it.x;
+        const uint8_t* src = (it.x >= S ? wsh_raw : w_raw) +
+                             (static_cast<size_t>(e) * M_total + (blockIdx.x % m_tiles) * 128) *
+                                 static_cast<size_t>(K);
+        const size_t bytes = static_cast<size_t>(128) * K;
+        for (size_t o = 0; o < bytes; o += 65536)
+          sl::prefetch_l2(src + o, static_cast<uint32_t>(bytes - o < 65536 ? bytes - o : 65536));
+      }
       auto load_b = [&](int st, int kb, int row) {
         sl::tma_load_2d(sAB + st * Cfg::kStageBytes + Cfg::kABytes, &tm_b, &full[st],
                         kb * F8_BK, row, pol_b);
@@ -1737,7 +1750,8 @@ int launch_gemm_f8(const CUtensorMap& tw, const CUtensorMap& twsh, const CUtenso
                    const float* bscale, const float* wscale, const float* wshscale,
                    const int32_t* hdr, const int4* items, uint8_t* out_q, float* out_s,
                    __nv_bfloat16* out_z, int S, int K, int M_total, int max_rows,
-                   int32_t* status, int max_items, cudaStream_t st, int phase) {
+                   int32_t* status, int max_items, cudaStream_t st, int phase,
+                   const void* w_raw, const void* wsh_raw) {
   using Cfg = F8Cfg<BN, GATED>;
   auto kern = moe_gemm_f8_kernel<BN, GATED>;
   static std::atomic<uint64_t> smem_set{0};
@@ -1748,7 +1762,8 @@ int launch_gemm_f8(const CUtensorMap& tw, const CUtensorMap& twsh, const CUtenso
   if (max_tiles < grid) grid = max_tiles > 0 ? max_tiles : 1;
   SL_CUDA_TRY(sl::launch(kern, dim3(grid), dim3(Cfg::kThreads), Cfg::kSmemBytes, st, tw, twsh,
                          tb, bscale, wscale, wshscale, hdr, items, out_q, out_s, out_z, S, K,
-                         M_total, max_rows, status, phase));
+                         M_total, max_rows, status, phase, static_cast<const uint8_t*>(w_raw),
+                         static_cast<const uint8_t*>(wsh_raw ? wsh_raw : w_raw)));
   return SL_OK;
 }
 
@@ -1937,11 +1952,11 @@ int run_fused(const void* hidden, int T, int H, int I, const sl_expert_weights& 
 #define SL_GEMMS_F8(BNV)                                                                         \
   rc = launch_gemm_f8<BNV, true>(m_w13, m_w13sh, m_x, Xs, w.w13_scale, w.shared_w13_scale, hdr,  \
                                  items, Aq, As, nullptr, num_slots, H, I, L.max_rows, hdr,      \
-                                 L.max_items, st, phase);                                        \
+                                 L.max_items, st, phase, w.w13, w.shared_w13);                   \
   if (rc == SL_OK)                                                                               \
     rc = launch_gemm_f8<BNV, false>(m_w2, m_w2sh, m_a, As, w.w2_scale, w.shared_w2_scale, hdr,   \
                                     items, nullptr, nullptr, Z, num_slots, I, H, L.max_rows,    \
-                                    hdr, L.max_items, st, phase);
+                                    hdr, L.max_items, st, phase, w.w2, w.shared_w2);
   if (fp8 && BN == kF8WideBN) {
     // gate/up over the 2I rows into bf16 g | u rows, SwiGLU + quantisation,
     // then down; the token tiles are read in 32-row boxes
