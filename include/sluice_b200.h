@@ -313,6 +313,15 @@ int sl_fused_experts_ex(const void* hidden, int T, int H, int I,
                         int out_f32, void* out, void* workspace,
                         size_t workspace_bytes, sl_stream_t stream);
 
+/* Parts of a phased fused-experts call (phase 0 = GROUP then
+ * RESIDENT_GEMMS, phase 1 = STREAMED_GEMMS then COMBINE). */
+enum {
+  SL_PHASE_GROUP = 2,           /* token grouping only */
+  SL_PHASE_RESIDENT_GEMMS = 3,  /* both GEMMs over the resident experts' items */
+  SL_PHASE_STREAMED_GEMMS = 4,  /* both GEMMs over the streamed experts' items */
+  SL_PHASE_COMBINE = 5          /* the combine only (output written here) */
+};
+
 /* sl_fused_experts in two phases, so the gap's expert stream can overlap
  * with the experts that were already resident (the reference serialises the
  * copy stream and the GEMM with events, offloader.py:2443-2464):
@@ -323,7 +332,10 @@ int sl_fused_experts_ex(const void* hidden, int T, int H, int I,
  *             combine (output written here).
  * Order sl_stream_experts (e.g. on a second stream) before phase 1 and after
  * sl_plan_slots; phase 0 only reads slots the streamer does not write. Both
- * calls take the same workspace. */
+ * calls take the same workspace. Phases 2..5 (SL_PHASE_*) run one part each,
+ * in that order, so the streamed experts' GEMMs can follow the stream on its
+ * own stream while the resident ones run: STREAMED_GEMMS after GROUP and
+ * after the stream, COMBINE after both GEMM parts. */
 int sl_fused_experts_phase(const void* hidden, int T, int H, int I,
                            const void* w13, const void* w2, int num_slots,
                            int weight_dtype, const float* topk_weights,

@@ -27,6 +27,8 @@ SL_ERR_NO_SCRATCH = 6
 SEG_FREE, SEG_PROBATION, SEG_PROTECTED, SEG_PINNED = 0, 1, 2, 3
 PLAN_FAST_HIT = 1
 PLAN_LFU = 2
+# parts of a phased fused-experts call (include/sluice_b200.h SL_PHASE_*)
+PHASE_GROUP, PHASE_RESIDENT_GEMMS, PHASE_STREAMED_GEMMS, PHASE_COMBINE = 2, 3, 4, 5
 
 # state header words / counters (include/sluice_b200.h)
 HDR = dict(num_slots=0, global_n=1, local_n=2, protected_cap=3, flags=4,

@@ -1830,7 +1830,8 @@ int sl::fused_experts_check(const void* hidden, int T, int H, int I, const sl_ex
   if (T < 0 || topk <= 0 || num_slots <= 0 || n_shared < 0) return SL_ERR_INVALID;
   if (H % BM || I % BM || H <= 0 || I <= 0) return SL_ERR_UNSUPPORTED;
   if (num_slots + n_shared > kMaxCode || n_shared > kMaxShared) return SL_ERR_UNSUPPORTED;
-  if (phase < -1 || phase > 1 || (phase >= 0 && !fill_state)) return SL_ERR_INVALID;
+  if (phase < -1 || phase > SL_PHASE_COMBINE || (phase >= 0 && !fill_state))
+    return SL_ERR_INVALID;
   if (T == 0) return SL_OK;
   if (!hidden || !w.w13 || !w.w2 || !topk_weights || !topk_ids || !out || !workspace)
     return SL_ERR_INVALID;
@@ -1905,7 +1906,15 @@ int run_fused(const void* hidden, int T, int H, int I, const sl_expert_weights& 
   // group in one CTA and gather with a grid-wide kernel
   const int P = T * topk;
   const bool small = P <= kSmallP && (num_slots + nsh) <= kMaxCode;
-  if (phase != 1) {
+  // phase -1: everything; 0 = grouping + resident experts' GEMMs; 1 =
+  // streamed experts' GEMMs + combine; 2..5: one of those four parts alone
+  const bool do_group = phase == -1 || phase == 0 || phase == SL_PHASE_GROUP;
+  const bool do_gemms = phase != SL_PHASE_GROUP && phase != SL_PHASE_COMBINE;
+  const bool do_combine = phase == -1 || phase == 1 || phase == SL_PHASE_COMBINE;
+  // the GEMM kernels' item range: -1 all, 0 resident experts, 1 streamed ones
+  const int gphase = phase == -1 ? -1
+                     : (phase == 0 || phase == SL_PHASE_RESIDENT_GEMMS) ? 0 : 1;
+  if (do_group) {
     if (small) {
       SL_CUDA_TRY(sl::launch(align_small_kernel, dim3(kAlignSmallCtas), dim3(kAlignSmallThreads),
                              0, st, topk_ids, T, topk, expert_map, global_n, num_slots, nsh,
@@ -1945,19 +1954,21 @@ int run_fused(const void* hidden, int T, int H, int I, const sl_expert_weights& 
   int rc = SL_OK;
 #define SL_GEMMS_BF16(BNV, S1, S2)                                                              \
   rc = launch_gemm<BNV, S1, true>(m_w13, m_w13sh, m_x, hdr, items, A, num_slots, H, I, I, hdr,   \
-                                  L.max_items, st, phase, w.w13, w.shared_w13);                  \
+                                  L.max_items, st, gphase, w.w13, w.shared_w13);                  \
   if (rc == SL_OK)                                                                               \
     rc = launch_gemm<BNV, S2, false>(m_w2, m_w2sh, m_a, hdr, items, Z, num_slots, I, H, H, hdr,  \
-                                     L.max_items, st, phase, w.w2, w.shared_w2);
+                                     L.max_items, st, gphase, w.w2, w.shared_w2);
 #define SL_GEMMS_F8(BNV)                                                                         \
   rc = launch_gemm_f8<BNV, true>(m_w13, m_w13sh, m_x, Xs, w.w13_scale, w.shared_w13_scale, hdr,  \
                                  items, Aq, As, nullptr, num_slots, H, I, L.max_rows, hdr,      \
-                                 L.max_items, st, phase, w.w13, w.shared_w13);                   \
+                                 L.max_items, st, gphase, w.w13, w.shared_w13);                   \
   if (rc == SL_OK)                                                                               \
     rc = launch_gemm_f8<BNV, false>(m_w2, m_w2sh, m_a, As, w.w2_scale, w.shared_w2_scale, hdr,   \
                                     items, nullptr, nullptr, Z, num_slots, I, H, L.max_rows,    \
-                                    hdr, L.max_items, st, phase, w.w2, w.shared_w2);
-  if (fp8 && BN == kF8WideBN) {
+                                    hdr, L.max_items, st, gphase, w.w2, w.shared_w2);
+  if (!do_gemms) {
+    // grouping or combine alone
+  } else if (fp8 && BN == kF8WideBN) {
     // gate/up over the 2I rows into bf16 g | u rows, SwiGLU + quantisation,
     // then down; the token tiles are read in 32-row boxes
     CUtensorMap m_xw, m_aw;
@@ -1966,7 +1977,7 @@ int run_fused(const void* hidden, int T, int H, int I, const sl_expert_weights& 
       return SL_ERR_INVALID;
     __nv_bfloat16* GU = reinterpret_cast<__nv_bfloat16*>(ws + L.gu);
     rc = launch_gemm_f8w(m_w13, m_w13sh, m_xw, Xs, w.w13_scale, w.shared_w13_scale, hdr, items,
-                         GU, num_slots, H, 2 * I, L.max_rows, hdr, L.max_items, st, phase);
+                         GU, num_slots, H, 2 * I, L.max_rows, hdr, L.max_items, st, gphase);
     if (rc == SL_OK) {
       const long units = static_cast<long>(L.max_items) * BN *
                          ((I / 128 + kQuantGroups - 1) / kQuantGroups);
@@ -1978,9 +1989,9 @@ int run_fused(const void* hidden, int T, int H, int I, const sl_expert_weights& 
                              0, st, static_cast<const int32_t*>(hdr),
                              static_cast<const int4*>(items), BN,
                              static_cast<const __nv_bfloat16*>(GU), I, Aq, As, L.max_rows,
-                             phase));
+                             gphase));
       rc = launch_gemm_f8w(m_w2, m_w2sh, m_aw, As, w.w2_scale, w.shared_w2_scale, hdr, items, Z,
-                           num_slots, I, H, L.max_rows, hdr, L.max_items, st, phase);
+                           num_slots, I, H, L.max_rows, hdr, L.max_items, st, gphase);
     }
   } else if (fp8) {
     SL_GEMMS_F8(16)
@@ -1994,7 +2005,7 @@ int run_fused(const void* hidden, int T, int H, int I, const sl_expert_weights& 
 #undef SL_GEMMS_BF16
 #undef SL_GEMMS_F8
   if (rc != SL_OK) return rc;
-  if (phase == 0) return SL_OK;
+  if (!do_combine) return SL_OK;
   dim3 cgrid((H / 8 + 255) / 256, T);
   SL_CUDA_TRY(sl::launch(accumulate ? combine_kernel<true, true>
                          : out_f32  ? combine_kernel<true>
@@ -2062,7 +2073,7 @@ extern "C" int sl_fused_experts_phase(const void* hidden, int T, int H, int I, c
                                       void* workspace, size_t workspace_bytes,
                                       sl_stream_t stream) {
   if (weight_dtype != SL_WEIGHTS_BF16) return SL_ERR_UNSUPPORTED;
-  if (phase != 0 && phase != 1) return SL_ERR_INVALID;
+  if (phase < 0 || phase > SL_PHASE_COMBINE) return SL_ERR_INVALID;
   const sl_expert_weights w = bf16_weights(w13, w2, num_slots, shared_w13, shared_w2, n_shared);
   return run_fused(hidden, T, H, I, w, topk_weights, topk_ids, topk, expert_map, global_n, 0,
                    T, routed_scaling_factor, out, 0, workspace, workspace_bytes,

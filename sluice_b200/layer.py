@@ -262,26 +262,47 @@ class SluiceMoELayer:
                                  routed_scaling_factor=self.cfg.routed_scaling_factor)
 
     def _forward_overlapped(self, hs, tw, ti):
-        """plan -> [stream on a side stream || resident experts' GEMMs] ->
-        streamed experts' GEMMs + combine. With prefetch on, the side stream
-        then plans and streams the next layer's predicted experts (its router
-        on this layer's input) while this layer finishes."""
+        """plan -> grouping -> [stream, then the streamed experts' GEMMs, on a
+        side stream || resident experts' GEMMs] -> combine. A layer without
+        misses thus puts no launch between its resident GEMMs and its
+        combine. With prefetch on, the side stream then plans and streams the
+        next layer's predicted experts (its router on this layer's input)
+        while this layer finishes."""
+        from ._lib import (PHASE_COMBINE, PHASE_GROUP, PHASE_RESIDENT_GEMMS,
+                           PHASE_STREAMED_GEMMS)
         c, cfg = self.cache, self.cfg
         main = torch.cuda.current_stream()
         hs = hs.contiguous()
         c.plan(ti)
         self._side.wait_stream(main)
+        T, H = hs.shape
+        ws = ops.fused_experts_workspace(T, ti.shape[1], H, c.w13.shape[1] // 2,
+                                         c.num_slots, 0 if self.shared_w13 is None
+                                         else self.shared_w13.shape[0], hs.device)
+        out = torch.empty_like(hs)
+        args = (hs, c.w13, c.w2, tw, ti, c.expert_map, c.state)
+        kw = dict(w1_scale=c.w13_scale, w2_scale=c.w2_scale, shared_w13=self.shared_w13,
+                  shared_w2=self.shared_w2, shared_w13_scale=self.shared_w13_scale,
+                  shared_w2_scale=self.shared_w2_scale,
+                  routed_scaling_factor=cfg.routed_scaling_factor)
+        with torch.cuda.stream(self._side):
+            _timed(self.stream_timer, self._side, lambda: c.stream(self.stream_ctas))
+        ops.fused_experts_phase(*args, PHASE_GROUP, ws, out, **kw)
+        grouped = torch.cuda.Event()
+        grouped.record(main)
         streamed = torch.cuda.Event()
         nxt = self.prefetch_next
         prefetch = (nxt is not None and not nxt.cache.static_full and
                     self.prefetch_max_fills > 0)
         with torch.cuda.stream(self._side):
-            _timed(self.stream_timer, self._side, lambda: c.stream(self.stream_ctas))
+            self._side.wait_event(grouped)
+            ops.fused_experts_phase(*args, PHASE_STREAMED_GEMMS, ws, out, **kw)
             streamed.record(self._side)
             if prefetch:
-                # on the copy stream, after this layer's own stream: predict the
-                # next layer's experts (its router on this layer's input), plan
-                # and stream them; the next layer plans after this
+                # on the copy stream, after this layer's own stream and its
+                # streamed experts' GEMMs: predict the next layer's experts (its
+                # router on this layer's input), plan and stream them; the next
+                # layer plans after this
                 _, ti_next, _ = nxt.router.route(hs)
                 nc = nxt.cache
                 nc.prefetch(ti_next, self.prefetch_max_fills)
@@ -293,19 +314,9 @@ class SluiceMoELayer:
                 # the copy stream reads hs: keep it alive until the next layer
                 # has ordered its stream after that read
                 nxt._prefetch_input = hs
-        T, H = hs.shape
-        ws = ops.fused_experts_workspace(T, ti.shape[1], H, c.w13.shape[1] // 2,
-                                         c.num_slots, 0 if self.shared_w13 is None
-                                         else self.shared_w13.shape[0], hs.device)
-        out = torch.empty_like(hs)
-        args = (hs, c.w13, c.w2, tw, ti, c.expert_map, c.state)
-        kw = dict(w1_scale=c.w13_scale, w2_scale=c.w2_scale, shared_w13=self.shared_w13,
-                  shared_w2=self.shared_w2, shared_w13_scale=self.shared_w13_scale,
-                  shared_w2_scale=self.shared_w2_scale,
-                  routed_scaling_factor=cfg.routed_scaling_factor)
-        ops.fused_experts_phase(*args, 0, ws, out, **kw)
+        ops.fused_experts_phase(*args, PHASE_RESIDENT_GEMMS, ws, out, **kw)
         main.wait_event(streamed)
-        return ops.fused_experts_phase(*args, 1, ws, out, **kw)
+        return ops.fused_experts_phase(*args, PHASE_COMBINE, ws, out, **kw)
 
     __call__ = forward
 

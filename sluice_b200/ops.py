@@ -224,7 +224,11 @@ def fused_experts_phase(hidden_states, w1, w2, topk_weights, topk_ids, expert_ma
                         routed_scaling_factor: float = 1.0) -> torch.Tensor:
     """One phase of ``fused_experts`` split around the expert stream: phase 0
     computes the already-resident experts, phase 1 the streamed ones and the
-    combine into ``out``. Both phases take the same ``workspace``."""
+    combine into ``out``. Both phases take the same ``workspace``. Phases
+    2..5 (``_lib.PHASE_*``: grouping, resident experts' GEMMs, streamed
+    experts' GEMMs, combine) run one part each, in that order, so the
+    streamed experts' GEMMs can be ordered after the stream on its own
+    stream."""
     return _fused_ex(hidden_states, w1, w2, topk_weights, topk_ids, expert_map,
                      expert_map.numel(), w1_scale=w1_scale, w2_scale=w2_scale,
                      shared_w13=shared_w13, shared_w2=shared_w2,

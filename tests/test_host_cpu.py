@@ -89,6 +89,15 @@ def test_host_calls_reject_bad_arguments_without_a_gpu():
     assert L.sl_fused_experts_ex(None, 4, 2048, 1408, ctypes.byref(w), None, None, 2, None, 0,
                                  1.0, 0, -1, None, -1, 0, None, None, 0, None) \
         == _lib.SL_ERR_INVALID
+    # phased calls: phases 0..5 only (-1, the whole call, is sl_fused_experts)
+    for bad in (-1, 6):
+        assert L.sl_fused_experts_phase(None, 4, 2048, 1408, None, None, 8, 0, None, None, 2,
+                                        None, 0, None, None, 0, 1.0, None, bad, None, None, 0,
+                                        None) == _lib.SL_ERR_INVALID
+    w.dtype = 0
+    assert L.sl_fused_experts_ex(None, 4, 2048, 1408, ctypes.byref(w), None, None, 2, None, 0,
+                                 1.0, 0, -1, None, _lib.PHASE_COMBINE + 1, 0, None, None, 0,
+                                 None) == _lib.SL_ERR_INVALID
     # the decoder harness's kernels: shapes outside their lane layouts and
     # missing buffers are refused before any CUDA call
     mla = lambda rank, rope: L.sl_mla_decode(None, 16 * 192 + rank + rope, None, 1e-6, None,

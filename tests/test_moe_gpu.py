@@ -257,3 +257,66 @@ def test_fp8_wide_tiles_split_around_the_stream():
                               **kw)
     torch.cuda.synchronize()
     assert torch.equal(whole, out)
+
+
+@pytest.mark.parametrize("fp8,T", [(False, 8), (True, 8), (False, 320), (True, 320)])
+def test_four_part_split_on_two_streams(fp8, T):
+    """The phased call in its four parts as the offloaded layer issues them:
+    grouping and the resident experts' GEMMs on the main stream; the stream,
+    then (after the grouping) the streamed experts' GEMMs on a side stream;
+    the combine on the main stream after both. Against the oracle, and bit-
+    equal to the whole call on the now-resident experts (decode- and
+    prefill-sized steps, bf16 and fp8)."""
+    from sluice_b200 import _lib, synth
+    from sluice_b200.offloader import ExpertStreamOffloader
+    H, I, E, S, k = 1024, 512, 16, 8, 2
+    g = torch.Generator().manual_seed(11 + T)
+    w13 = (torch.randn(E, 2 * I, H, generator=g) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn(E, H, I, generator=g) * 0.02).to(torch.bfloat16)
+    hs = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    # every token picks 2 distinct experts among 6: 3 pinned (resident), 3 streamed
+    choice = torch.stack([torch.randperm(6, generator=g)[:k] for _ in range(T)])
+    ti = torch.tensor([0, 1, 2, 9, 11, 14])[choice].to(torch.int32)
+    tw = torch.rand(T, k, generator=g)
+    tw = (tw / tw.sum(1, keepdim=True)).float()
+    off = ExpertStreamOffloader(S, protect_frac=0.5, fast_hit=True)
+    if fp8:
+        q13, s13 = synth.quantize_block_fp8(w13)
+        q2, s2 = synth.quantize_block_fp8(w2)
+        cache = off.install_layer(q13, q2, pins=[0, 1, 2], prefill_resident=False,
+                                  device="cuda", w13_scale=s13, w2_scale=s2)
+        ref = omoe.fused_experts(hs, q13, q2, tw, ti, None, s13, s2)
+        rtol = 5e-2
+    else:
+        cache = off.install_layer(w13, w2, pins=[0, 1, 2], prefill_resident=False,
+                                  device="cuda")
+        ref = omoe.fused_experts(hs, w13, w2, tw, ti)
+        rtol = RTOL
+    x, tic, twc = hs.cuda(), ti.cuda(), tw.cuda()
+    ws = ops.fused_experts_workspace(T, k, H, I, S, 0, torch.device("cuda"))
+    out = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+    kw = dict(w1_scale=cache.w13_scale, w2_scale=cache.w2_scale)
+    args = (x, cache.w13, cache.w2, twc, tic, cache.expert_map, cache.state)
+    main, side = torch.cuda.current_stream(), torch.cuda.Stream()
+    cache.plan(tic)
+    side.wait_stream(main)
+    with torch.cuda.stream(side):
+        cache.stream()
+    ops.fused_experts_phase(*args, _lib.PHASE_GROUP, ws, out, **kw)
+    grouped = torch.cuda.Event()
+    grouped.record(main)
+    with torch.cuda.stream(side):
+        side.wait_event(grouped)
+        ops.fused_experts_phase(*args, _lib.PHASE_STREAMED_GEMMS, ws, out, **kw)
+    ops.fused_experts_phase(*args, _lib.PHASE_RESIDENT_GEMMS, ws, out, **kw)
+    main.wait_stream(side)
+    ops.fused_experts_phase(*args, _lib.PHASE_COMBINE, ws, out, **kw)
+    torch.cuda.synchronize()
+    cache.check()
+    assert ops.workspace_status(ws) == 0
+    assert int((cache.expert_map >= 0).sum()) == 6
+    assert_moe_close(out, ref, rtol=rtol)
+    whole = ops.fused_experts(x, cache.w13, cache.w2, twc, tic, expert_map=cache.expert_map,
+                              **kw)
+    torch.cuda.synchronize()
+    assert torch.equal(whole, out)
