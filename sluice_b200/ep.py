@@ -268,7 +268,10 @@ class EPMoELayer:
                                 self.cfg.routed_scaling_factor, self.shared_w13_scale,
                                 self.shared_w2_scale, self.stream_ctas, self.stream_timer)
         elif self.overlap:
-            # plan -> [stream on a side stream || resident experts] -> streamed experts
+            # plan -> grouping -> [stream, then the streamed experts, on a side
+            # stream || resident experts] -> combine
+            from ._lib import (PHASE_COMBINE, PHASE_GROUP, PHASE_RESIDENT_GEMMS,
+                               PHASE_STREAMED_GEMMS)
             main = torch.cuda.current_stream()
             c.plan(tig)
             self._side.wait_stream(main)
@@ -278,11 +281,19 @@ class EPMoELayer:
             ws = ops.fused_experts_workspace(xg.shape[0], tig.shape[1], xg.shape[1],
                                              c.w13.shape[1] // 2, c.num_slots, n_sh, xg.device)
             part = torch.empty(xg.shape, dtype=torch.float32, device=xg.device)
-            ops.fused_experts_partial(*args, out=part, slot_state=c.state, phase=0,
-                                      workspace=ws, **kw)
+
+            def run(phase):
+                ops.fused_experts_partial(*args, out=part, slot_state=c.state, phase=phase,
+                                          workspace=ws, **kw)
+            run(PHASE_GROUP)
+            grouped = torch.cuda.Event()
+            grouped.record(main)
+            with torch.cuda.stream(self._side):
+                self._side.wait_event(grouped)
+                run(PHASE_STREAMED_GEMMS)
+            run(PHASE_RESIDENT_GEMMS)
             main.wait_stream(self._side)
-            ops.fused_experts_partial(*args, out=part, slot_state=c.state, phase=1,
-                                      workspace=ws, **kw)
+            run(PHASE_COMBINE)
         else:
             c.gap(tig)
             part = ops.fused_experts_partial(*args, **kw)

@@ -246,8 +246,9 @@ def fused_experts_partial(hidden_states, w1, w2, topk_weights, topk_ids, expert_
     """Expert-parallel partial output [T, H] fp32: this rank's experts (the
     ones ``expert_map`` maps) scaled by ``routed_scaling_factor``, plus the
     shared experts on rows [shared_t0, shared_t0 + shared_nt). ``phase`` 0 / 1
-    split the call around the gap's expert stream as ``fused_experts_phase``
-    does (both phases: the same ``slot_state``, ``workspace`` and ``out``)."""
+    (or its four parts 2..5) split the call around the gap's expert stream as
+    ``fused_experts_phase`` does (every part: the same ``slot_state``,
+    ``workspace`` and ``out``)."""
     return _fused_ex(hidden_states, w1, w2, topk_weights, topk_ids, expert_map,
                      expert_map.numel(), w1_scale=w1_scale, w2_scale=w2_scale,
                      shared_w13=shared_w13, shared_w2=shared_w2,
