@@ -543,8 +543,10 @@ def layer_launches(cfg, tokens, world, slots, exchange="nvlink", no_overlap=Fals
     launch rules of the host code: gate + select; a fused-experts call is its
     token grouping (one kernel for up to 1024 bf16 pairs, else grouping +
     gather; fp8: grouping + quantising gather), the gate/up and down GEMMs and
-    the combine (a phase-0 call stops before the combine; its phase 1 runs
-    the GEMMs again and the combine); an offloaded gap adds plan + stream; a
+    the combine (an offloaded layer issues it in parts: grouping, the
+    resident experts' GEMMs, the streamed experts' GEMMs on the stream's side
+    stream, the combine: the GEMMs twice); an offloaded gap adds plan +
+    stream; a
     step beyond the envelope runs max_waves waves (one plan, a stream per
     wave, wave 0 split in two phases, the rest whole calls; decode steps,
     every expert decode-class, take the tighter wave count); the NVLink
