@@ -29,6 +29,10 @@ int main(void) {
   EXPECT(sl_plan_waves(NULL, NULL, 8, 6, 0, NULL, NULL, NULL) == SL_ERR_INVALID);
   EXPECT(sl_stream_wave(NULL, 0, 2, NULL, NULL, NULL, NULL, 0, NULL) == SL_ERR_INVALID);
   EXPECT(sl_wave_plan_init(NULL, 48, 64, 5, NULL) == SL_ERR_INVALID);
+  /* phased fused experts: parts 0..SL_PHASE_COMBINE only */
+  EXPECT(sl_fused_experts_phase(NULL, 4, 2048, 1408, NULL, NULL, 8, SL_WEIGHTS_BF16, NULL, NULL,
+                                2, NULL, 0, NULL, NULL, 0, 1.0f, NULL, SL_PHASE_COMBINE + 1,
+                                NULL, NULL, 0, NULL) == SL_ERR_INVALID);
   printf("c host ok: library version %d\n", sl_version());
   return 0;
 }
