@@ -300,8 +300,9 @@ typedef struct sl_expert_weights {
  * scales (dequantised per tile into bf16 for the tensor cores; activations
  * stay bf16), shared experts on tokens [shared_t0, shared_t0 + shared_nt)
  * (shared_nt < 0: every token), optional phase split around the expert
- * stream (phase -1: whole call; 0 / 1 as sl_fused_experts_phase, slot_state
- * required), and out_f32 = 1 for the expert-parallel fp32 partial (as
+ * stream (phase -1: whole call; 0 / 1 or the parts SL_PHASE_* as
+ * sl_fused_experts_phase, slot_state required), and out_f32 = 1 for the
+ * expert-parallel fp32 partial (as
  * sl_fused_experts_partial), 2 for the same partial added to the fp32 `out`
  * (the expert waves of one step, sl_plan_waves). */
 int sl_fused_experts_ex(const void* hidden, int T, int H, int I,
